@@ -1,0 +1,276 @@
+/* SPDX-License-Identifier: Apache-2.0 */
+/*
+ * k3_cuda.h -- device context and B200-native decode entry points of libk3cuda.so.
+ *
+ * Two groups of symbols live here.
+ *
+ *  1. The device context (k3d_init ... k3d_graph_*). The CPU engine has no context
+ *     object; its entry points in k3.h run on the context this header manages: one
+ *     CUDA device, one stream, one sticky error status per process.
+ *
+ *  2. Decode-path operators at the shapes of the synthetic K3 benchmark, which the CPU
+ *     engine's API cannot express: SwiGLU experts without the latent projection, a bf16
+ *     shared expert, RoPE'd MLA over a bf16 latent cache with absorbed weights, batched
+ *     KDA decode, the 8-layer decode stack and expert parallelism over NCCL. Each cites
+ *     the CPU routine whose arithmetic it follows. These take DEVICE pointers only, are
+ *     asynchronous on the library stream and can be captured into a CUDA graph.
+ *
+ * All functions return K3D_OK (0) or a K3D_E* code; the first non-zero code is also kept
+ * in the sticky status read by k3d_status().
+ */
+#ifndef K3_CUDA_H
+#define K3_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include "k3.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------------- status ---- */
+enum {
+    K3D_OK = 0,
+    K3D_ENODEV = 1,        /* no usable CUDA device */
+    K3D_EINVAL = 2,        /* bad argument: null pointer, size, alignment, host pointer */
+    K3D_ENOMEM = 3,        /* device allocation failed */
+    K3D_ECUDA = 4,         /* a CUDA runtime call failed */
+    K3D_EDEVICE = 5,       /* a kernel raised the device error flag */
+    K3D_EUNSUPPORTED = 6,  /* outside this library's scope (e.g. K3_WI8) */
+    K3D_ENCCL = 7,         /* an NCCL call failed */
+    K3D_EBOUND = 8,        /* a capacity bound was exceeded (cache position, top-k) */
+    K3D_ETIMEOUT = 9       /* a bounded device-side wait gave up */
+};
+
+/* Select the CUDA device and create the library stream. Idempotent for the same
+ * device; the k3.h entry points call k3d_init(0) on first use if nobody did. */
+int         k3d_init(int device);
+int         k3d_device(void);
+/* The first error since the last k3d_clear_status(); also folds in the device error
+ * flag as of the last k3d_sync(). */
+int         k3d_status(void);
+void        k3d_clear_status(void);
+const char *k3d_strerror(int code);
+const char *k3d_last_message(void);
+/* 1: a recorded error prints and calls abort(), the CPU engine's fatal policy. */
+void        k3d_set_abort_on_error(int on);
+/* Device-side error detail: the code a kernel stored and the site id that stored it. */
+int         k3d_device_error(int *code, int *site);
+
+/* Memory. k3d_alloc returns 256-byte aligned device memory or NULL. */
+void  *k3d_alloc(size_t bytes);
+void   k3d_free(void *p);
+int    k3d_upload(void *dst_dev, const void *src_host, size_t bytes);
+int    k3d_download(void *dst_host, const void *src_dev, size_t bytes);
+int    k3d_memset(void *dst_dev, int value, size_t bytes);
+int    k3d_copy(void *dst_dev, const void *src_dev, size_t bytes);
+/* Page-locked host memory, for host<->device copies at full PCIe speed. */
+void  *k3d_host_alloc(size_t bytes);
+void   k3d_host_free(void *p);
+/* Host weight residency for the k3.h entry points. Off (the default): a host weight is
+ * copied to the device on every call, which is always correct. On: the first call that
+ * sees a host weight address uploads it once and later calls reuse the HBM copy; the
+ * caller promises not to rewrite those bytes (or to call k3d_forget) -- a ring buffer of
+ * streamed layers, as the CPU engine's trunk reader keeps, must leave this off. */
+void   k3d_set_weight_cache(int on);
+/* Forget the HBM copy made for a host weight pointer passed to a k3.h entry point. */
+void   k3d_forget(const void *host_ptr);
+void   k3d_forget_all(void);
+size_t k3d_weight_cache_bytes(void);
+
+/* Stream, events, graphs. */
+int    k3d_sync(void);
+void  *k3d_stream(void);
+int    k3d_set_stream(void *cuda_stream);
+void  *k3d_event_create(void);
+int    k3d_event_record(void *ev);
+float  k3d_event_elapsed_ms(void *start, void *stop);
+void   k3d_event_destroy(void *ev);
+int    k3d_graph_begin(void);
+void  *k3d_graph_end(void);
+int    k3d_graph_launch(void *graph_exec);
+void   k3d_graph_destroy(void *graph_exec);
+/* Section timers. When enabled, the library records CUDA events on its stream around its
+ * main kernel groups ("moe.experts", "moe.router", "moe.shared", "moe.combine", ...);
+ * k3d_prof_ms() synchronises and returns the accumulated device time of one section and
+ * the number of times it ran. Recording is skipped while a graph is being captured. */
+void   k3d_prof_enable(int on);
+void   k3d_prof_reset(void);
+double k3d_prof_ms(const char *section, long *count);
+/* Number of kernels this library launched since the last reset (host-side count). */
+long   k3d_launch_count(void);
+void   k3d_launch_count_reset(void);
+int    k3d_sm_count(void);
+
+/* -------------------------------------------------------- synthetic fill ---- */
+/* Deterministic device-side fills for the synthetic benchmark inputs. The value of
+ * element i depends only on (seed, i). Normal values are an Irwin-Hall sum of four
+ * 16-bit uniforms scaled to the requested standard deviation. */
+int k3d_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float stddev);
+int k3d_fill_f32_normal(float *dst, size_t n, uint64_t seed, float stddev);
+int k3d_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi);
+/* E2M1 codes uniform over all 16 values; E8M0 bytes uniform in [s_lo, s_hi]. */
+int k3d_fill_mxfp4(unsigned char *packed, size_t packed_bytes,
+                   unsigned char *scales, size_t scale_bytes,
+                   uint64_t seed, int s_lo, int s_hi);
+int k3d_fill_i32_uniform(int *dst, size_t n, uint64_t seed, int lo, int hi);
+
+/* ------------------------------------------------------------------ MXFP4 ---- */
+/* Config 0: y = W_down . (silu(W_gate . x) * (W_up . x)), one MXFP4 expert. x [hidden],
+ * y [hidden], fp32. Follows k3_moe's per-expert body (k3_ops.c:628-631) with SiLU in
+ * place of SiTU. `e` is a HOST struct holding device pointers. ws: k3d_expert_ws_bytes. */
+size_t k3d_expert_ws_bytes(int hidden, int inter);
+int    k3d_expert_swiglu(float *y, const float *x, const K3ExpertQ *e,
+                         int hidden, int inter, void *ws, size_t ws_bytes);
+
+/* ------------------------------------------------------------------- MoE ---- */
+/* One MoE layer without the latent projection: router (k3_router semantics, bf16 W),
+ * routed MXFP4 SwiGLU experts combined in top-k order, plus an optional unweighted
+ * bf16 SwiGLU shared expert. Follows k3_moe / moe_prefill_chunk
+ * (k3_ops.c:556-656, 717-825) with SwiGLU and no latent step. */
+typedef struct {
+    int   hidden;          /* 7168 */
+    int   inter;           /* routed expert intermediate, 2048 */
+    int   n_experts;       /* 384 */
+    int   topk;            /* 8, at most K3_MAX_TOPK */
+    int   renorm;          /* 1 */
+    float routed_scale;    /* 2.5 */
+    int   shared_inter;    /* 2048; 0 = no shared expert */
+    int   expert_lo;       /* experts [expert_lo, expert_hi) are computed here */
+    int   expert_hi;
+    int   add_shared;      /* 1: this rank adds the shared expert (one rank under EP) */
+} K3dMoeShape;
+
+typedef struct {
+    const uint16_t  *router_w;      /* [n_experts][hidden] bf16 */
+    const float     *router_bias;   /* [n_experts] */
+    const K3ExpertQ *experts;       /* DEVICE array [n_experts] */
+    const uint16_t  *sh_gate;       /* [shared_inter][hidden] bf16 */
+    const uint16_t  *sh_up;         /* [shared_inter][hidden] bf16 */
+    const uint16_t  *sh_down;       /* [hidden][shared_inter] bf16 */
+} K3dMoeW;
+
+size_t k3d_moe_ws_bytes(const K3dMoeShape *s, int T);
+/* out[T][hidden] (+)= moe(x[T][hidden]). accumulate = 1 adds into out (residual).
+ * idx/wts (device, [T][topk]) receive the routing; either may be NULL. */
+int    k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s,
+                      int T, int accumulate, int *idx, float *wts,
+                      void *ws, size_t ws_bytes);
+/* The router alone on a bf16 W: idx/w [T][topk], device. */
+int    k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W,
+                       const float *bias, int T, int hidden, int n_experts, int topk,
+                       int renorm, float routed_scale);
+/* Number of distinct experts routed to by the last k3d_moe_swiglu call (host copy made
+ * on k3d_sync(); -1 if unknown). Used for the algorithmic-bytes numerator. */
+int    k3d_moe_last_unique(void);
+
+/* --------------------------------------------------------------- GEMV ---- */
+/* y[T][out] = x[T][in] . W^T for bf16 W; accumulate = 1 adds into y. */
+int k3d_gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int T,
+                  int accumulate);
+
+/* ------------------------------------------------------------------- KDA ---- */
+/* Batched KDA decode step: per (sequence b, head h) exactly k3_kda_step
+ * (k3_ops.c:186-243) on S[b][h] ([dk][dv] fp32, updated in place). q, k, alpha
+ * [B][H][dk], v and o [B][H][dv], beta [B][H]; q arrives pre-scaled as in k3.h. */
+int k3d_kda_decode(float *S, float *o, const float *q, const float *k, const float *v,
+                   const float *alpha, const float *beta, int B, int H, int dk, int dv);
+/* T-step recurrence for one sequence, all heads: the same result as T sequential
+ * k3d_kda_decode calls. q,k,alpha [T][H][dk]; v,o [T][H][dv]; beta [T][H].
+ * chunk = 0 runs the sequential recurrence; chunk = 64 runs the chunked (WY) form. */
+int k3d_kda_prefill(float *S, float *o, const float *q, const float *k, const float *v,
+                    const float *alpha, const float *beta, int T, int H, int dk, int dv,
+                    int chunk);
+
+/* ------------------------------------------------------------------- MLA ---- */
+typedef struct {
+    int   hidden, n_heads, q_lora, kv_lora, qk_nope, qk_rope, v_head;
+    float rope_theta;      /* 50000; 0 disables the rotation (NoPE) */
+    float eps;
+    int   out_gate;        /* 1: sigmoid(g x) gates the heads before o_proj */
+} K3dMlaShape;
+
+typedef struct {
+    const uint16_t *q_a;       /* [q_lora][hidden] */
+    const uint16_t *q_b;       /* [H*(nope+rope)][q_lora] */
+    const uint16_t *kv_a;      /* [kv_lora+rope][hidden] */
+    const uint16_t *kv_b;      /* [H*(nope+v)][kv_lora] */
+    const uint16_t *o;         /* [hidden][H*v] */
+    const uint16_t *g;         /* [H*v][hidden], NULL when out_gate == 0 */
+    const float    *q_a_norm;  /* [q_lora] */
+    const float    *kv_a_norm; /* [kv_lora] */
+} K3dMlaW;
+
+size_t k3d_mla_ws_bytes(const K3dMlaShape *s, int B, int cap);
+/* One decode token per sequence. cache [B][cap][kv_lora+rope] bf16 holds the normalised
+ * latent and the rotated rope key of every earlier position; *pos (device int) is the
+ * number of cached positions, the new token is written at index *pos and attends over
+ * *pos + 1 positions. Follows k3_mla_cached (k3_ops.c:321-410) in absorbed form. */
+int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *s,
+                   int B, uint16_t *cache, int cap, const int *pos, int accumulate,
+                   void *ws, size_t ws_bytes);
+
+/* ------------------------------------------------------------- small ops ---- */
+int k3d_rmsnorm(float *y, const float *x, const float *w, int n, int rows, float eps);
+int k3d_silu_mul(float *y, const float *gu, int n, int rows); /* gu = [gate | up] per row */
+
+/* --------------------------------------------------------------- EP/NCCL ---- */
+/* Expert parallelism over NCCL: one process per GPU. rank 0 calls
+ * k3d_ep_unique_id, ships the 128 bytes to the other ranks, and every rank calls
+ * k3d_ep_init. */
+int k3d_ep_unique_id(unsigned char id[128]);
+int k3d_ep_init(int rank, int nranks, const unsigned char id[128]);
+int k3d_ep_finalize(void);
+int k3d_ep_rank(void);
+int k3d_ep_size(void);
+/* In-place sum of a float buffer over all ranks (the MoE combine). */
+int k3d_ep_allreduce_f32(float *buf, size_t n);
+
+/* ----------------------------------------------------------- decode stack ---- */
+typedef struct {
+    int   hidden, vocab, n_layers;
+    float eps;
+    /* KDA */
+    int   kda_heads, kda_head_dim, conv_k;
+    float gate_lb;
+    /* MLA */
+    K3dMlaShape mla;
+    /* MoE: shape of layers >= first_dense */
+    K3dMoeShape moe;
+    int   first_dense, dense_inter;
+    /* zero-based MLA layers, -1 terminated list */
+    int   mla_layers[16];
+    /* batch and cache */
+    int   batch;
+    int   ctx_cap;
+} K3dStackCfg;
+
+typedef struct K3dModel K3dModel;
+
+/* Random-init weights on the device (synthetic benchmark), MLA cache and KDA state
+ * allocated for cfg->batch sequences of up to ctx_cap positions. Under EP each rank
+ * allocates only its own experts. */
+K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed);
+void      k3d_model_destroy(K3dModel *m);
+/* Fill the MLA latent caches and KDA states as after `len` tokens of context with
+ * seeded synthetic values (latent ~N(0,1), state ~N(0,0.01), conv history ~N(0,1)). */
+int       k3d_model_fill_context(K3dModel *m, int len, uint64_t seed);
+/* One decode step for the batch: ids (device [B]) in, next ids (device [B], argmax of
+ * the logits) out, logits (device [B][vocab]) optional. Captures into a graph. */
+int       k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits);
+/* The same through host buffers: copies ids in, runs the step, copies next ids out. */
+int       k3d_model_step_host(K3dModel *m, const int *ids_host, int *next_host);
+/* Use a CUDA graph for k3d_model_step_* (default 1). */
+int       k3d_model_use_graph(K3dModel *m, int on);
+/* Device pointers to model internals for tests: name = "embed", "lm_head",
+ * "final_norm", "pos", "layer<i>.<tensor>". Returns NULL if unknown. */
+void     *k3d_model_tensor(K3dModel *m, const char *name, size_t *bytes);
+/* Algorithmic bytes the last step read or wrote in HBM (weights + caches + states). */
+double    k3d_model_last_step_bytes(K3dModel *m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* K3_CUDA_H */

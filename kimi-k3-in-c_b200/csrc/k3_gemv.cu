@@ -1,0 +1,286 @@
+// k3_gemv.cu -- fp32 and bf16 GEMVs: k3_matmul and k3_matmul_bf16 (include/k3/k3.h,
+// following k3_ops.c:265-291 and 1108-1213) and k3d_gemv_bf16, plus the fused
+// gate|up -> SiLU*mul GEMV used by the shared and dense SwiGLU MLPs.
+#include "k3_gemv.cuh"
+#include "k3_ops.cuh"
+
+namespace k3 {
+
+enum { EPI_STORE = 0, EPI_ACCUM = 1 };
+
+// y[t][r] (+)= W[r] . x[t] for up to NT tokens, bf16 W, in % 8 == 0, 16-byte rows.
+template <int R, int SEG, int NT>
+__global__ void __launch_bounds__(256) k_gemv_bf16(float *y, const float *x, const uint16_t *W,
+                                                   int in, int out, int T, int accumulate)
+{
+    extern __shared__ float4 xs[];
+    const int nf4 = in >> 2;
+    for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
+    __syncthreads();
+    const int nch = in >> 3;
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int r0 = warp * R; r0 < out; r0 += nwarps * R) {
+        const uint16_t *pr[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) pr[r] = W + (size_t)min(r0 + r, out - 1) * in;
+        if (NT == 1) {
+            float acc[R];
+            bf16_rows_partial<R, SEG>(acc, pr, xs, nch);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const float v = warp_sum(acc[r]);
+                if (lane == 0 && r0 + r < out) {
+                    float *dst = y + (r0 + r);
+                    *dst = accumulate ? *dst + v : v;
+                }
+            }
+        } else {
+            for (int t = 0; t < T; t++) {
+                float acc[R];
+                bf16_rows_partial<R, SEG>(acc, pr, xs + (size_t)t * nf4, nch);
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const float v = warp_sum(acc[r]);
+                    if (lane == 0 && r0 + r < out) {
+                        float *dst = y + (size_t)t * out + (r0 + r);
+                        *dst = accumulate ? *dst + v : v;
+                    }
+                }
+            }
+        }
+    }
+}
+
+// act[t][i] = silu(Wg[i] . x[t]) * (Wu[i] . x[t]) for bf16 gate/up matrices.
+template <int SEG>
+__global__ void __launch_bounds__(256) k_gemv_bf16_swiglu(float *act, const float *x,
+                                                          const uint16_t *Wg, const uint16_t *Wu,
+                                                          int in, int inter, int T)
+{
+    extern __shared__ float4 xs[];
+    const int nf4 = in >> 2;
+    for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
+    __syncthreads();
+    const int nch = in >> 3;
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int i = warp; i < inter; i += nwarps) {
+        const uint16_t *pr[2] = {Wg + (size_t)i * in, Wu + (size_t)i * in};
+        for (int t = 0; t < T; t++) {
+            float acc[2];
+            bf16_rows_partial<2, SEG>(acc, pr, xs + (size_t)t * nf4, nch);
+            const float g = warp_sum(acc[0]);
+            const float u = warp_sum(acc[1]);
+            if (lane == 0) act[(size_t)t * inter + i] = silu_f(g) * u;
+        }
+    }
+}
+
+// fp32 W, in % 4 == 0, 16-byte rows: chunk = 4 elements = one float4 of x (no swizzle
+// needed, consecutive lanes read consecutive float4s).
+template <int R, int SEG>
+__global__ void __launch_bounds__(256) k_gemv_f32(float *y, const float *x, const float *W,
+                                                  int in, int out)
+{
+    extern __shared__ float4 xs[];
+    const int nf4 = in >> 2;
+    for (int f = threadIdx.x; f < nf4; f += blockDim.x)
+        xs[f] = make_float4(x[4 * f], x[4 * f + 1], x[4 * f + 2], x[4 * f + 3]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int r0 = warp * R; r0 < out; r0 += nwarps * R) {
+        float2 a2[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) a2[r] = make_float2(0.f, 0.f);
+        for (int base = 0; base < nf4; base += 32 * SEG) {
+            uint4 w[R][SEG];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const float *pr = W + (size_t)min(r0 + r, out - 1) * in;
+#pragma unroll
+                for (int j = 0; j < SEG; j++) {
+                    const int c = base + lane + 32 * j;
+                    w[r][j] = (c < nf4) ? ldg_nc_v4(pr + 4 * (size_t)c) : make_uint4(0, 0, 0, 0);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < SEG; j++) {
+                const int c = base + lane + 32 * j;
+                if (c < nf4) {
+                    const float4 xv = xs[c];
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        a2[r] = ffma2(make_float2(__uint_as_float(w[r][j].x), __uint_as_float(w[r][j].y)),
+                                      make_float2(xv.x, xv.y), a2[r]);
+                        a2[r] = ffma2(make_float2(__uint_as_float(w[r][j].z), __uint_as_float(w[r][j].w)),
+                                      make_float2(xv.z, xv.w), a2[r]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const float v = warp_sum(a2[r].x + a2[r].y);
+            if (lane == 0 && r0 + r < out) y[r0 + r] = v;
+        }
+    }
+}
+
+// Any shape / alignment: one warp per row, lanes over elements.
+template <typename WT>
+__global__ void k_gemv_generic(float *y, const float *x, const WT *W, int in, int out,
+                               int accumulate)
+{
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int r = warp; r < out; r += nwarps) {
+        const WT *row = W + (size_t)r * in;
+        float acc = 0.f;
+        for (int i = lane; i < in; i += 32) {
+            float w;
+            if (sizeof(WT) == 2) w = bf16_to_f32((uint16_t)row[i]);
+            else w = (float)row[i];
+            acc = fmaf(w, x[i], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) y[r] = accumulate ? y[r] + acc : acc;
+    }
+}
+
+static bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+static int grid_for(int rows, int rows_per_cta)
+{
+    int grid = (rows + rows_per_cta - 1) / rows_per_cta;
+    const int cap = sm_count() * 4;
+    if (grid > cap) grid = cap;
+    return grid < 1 ? 1 : grid;
+}
+
+template <typename K>
+static void allow_smem(K kern)
+{
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int T,
+              int accumulate, cudaStream_t s)
+{
+    if (out <= 0 || T <= 0) return K3D_OK;
+    const bool fast = (in % 8) == 0 && al16(W) && (size_t)in * 4 * 4 <= 200 * 1024;
+    if (!fast) {
+        for (int t = 0; t < T; t++) {
+            k_gemv_generic<uint16_t><<<grid_for(out, 8), 256, 0, s>>>(
+                y + (size_t)t * out, x + (size_t)t * in, W, in, out, accumulate);
+            note_launch();
+        }
+        return check_launch("gemv bf16 generic");
+    }
+    static bool init = false;
+    if (!init) {
+        allow_smem(k_gemv_bf16<2, 7, 1>);
+        allow_smem(k_gemv_bf16<2, 7, 4>);
+        init = true;
+    }
+    for (int t0 = 0; t0 < T; t0 += 4) {
+        const int nt = min(4, T - t0);
+        const size_t smem = (size_t)nt * in * sizeof(float);
+        if (nt == 1)
+            k_gemv_bf16<2, 7, 1><<<grid_for(out, 64), 256, smem, s>>>(
+                y + (size_t)t0 * out, x + (size_t)t0 * in, W, in, out, 1, accumulate);
+        else
+            k_gemv_bf16<2, 7, 4><<<grid_for(out, 64), 256, smem, s>>>(
+                y + (size_t)t0 * out, x + (size_t)t0 * in, W, in, out, nt, accumulate);
+        note_launch();
+    }
+    return check_launch("gemv bf16");
+}
+
+int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint16_t *Wu,
+                     int in, int inter, int T, cudaStream_t s)
+{
+    if (inter <= 0 || T <= 0) return K3D_OK;
+    if ((in % 8) != 0 || !al16(Wg) || !al16(Wu) || (size_t)in * 4 * 4 > 200 * 1024)
+        return fail(K3D_EINVAL, "swiglu gemv needs in %% 8 == 0 and aligned rows (in=%d)", in);
+    static bool init = false;
+    if (!init) { allow_smem(k_gemv_bf16_swiglu<7>); init = true; }
+    for (int t0 = 0; t0 < T; t0 += 4) {
+        const int nt = min(4, T - t0);
+        const size_t smem = (size_t)nt * in * sizeof(float);
+        k_gemv_bf16_swiglu<7><<<grid_for(inter, 32), 256, smem, s>>>(
+            act + (size_t)t0 * inter, x + (size_t)t0 * in, Wg, Wu, in, inter, nt);
+        note_launch();
+    }
+    return check_launch("gemv bf16 swiglu");
+}
+
+int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStream_t s)
+{
+    if (out <= 0) return K3D_OK;
+    const bool fast = (in % 4) == 0 && al16(W) && (size_t)in * 4 <= 200 * 1024;
+    if (!fast) {
+        k_gemv_generic<float><<<grid_for(out, 8), 256, 0, s>>>(y, x, W, in, out, 0);
+        note_launch();
+        return check_launch("gemv f32 generic");
+    }
+    static bool init = false;
+    if (!init) { allow_smem(k_gemv_f32<2, 4>); init = true; }
+    k_gemv_f32<2, 4><<<grid_for(out, 64), 256, (size_t)in * sizeof(float), s>>>(y, x, W, in, out);
+    note_launch();
+    return check_launch("gemv f32");
+}
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" {
+
+void k3_matmul(float *y, const float *x, const float *W, int in, int out)
+{
+    if (ensure_ctx()) return;
+    if (in <= 0 || out <= 0) return;
+    Stage st;
+    const float *Wd = (const float *)st.weight(W, (size_t)in * out * sizeof(float));
+    const float *X = (const float *)st.in(x, (size_t)in * sizeof(float));
+    float *Y = (float *)st.out(y, (size_t)out * sizeof(float));
+    if (st.err) return;
+    if (gemv_f32(Y, X, Wd, in, out, stream())) return;
+    st.finish();
+}
+
+void k3_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out)
+{
+    if (ensure_ctx()) return;
+    if (in <= 0 || out <= 0) return;
+    Stage st;
+    const uint16_t *Wd = (const uint16_t *)st.weight(W, (size_t)in * out * sizeof(uint16_t));
+    const float *X = (const float *)st.in(x, (size_t)in * sizeof(float));
+    float *Y = (float *)st.out(y, (size_t)out * sizeof(float));
+    if (st.err) return;
+    if (gemv_bf16(Y, X, Wd, in, out, 1, 0, stream())) return;
+    st.finish();
+}
+
+void k3_matmul_q8(float *y, const float *x, const void *W, int in, int out)
+{
+    (void)y; (void)x; (void)W; (void)in; (void)out;
+    if (ensure_ctx()) return;
+    fail(K3D_EUNSUPPORTED, "k3_matmul_q8: the int8 draft-model format is not served here");
+}
+
+int k3d_gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int T,
+                  int accumulate)
+{
+    K3_TRY(ensure_ctx());
+    if (!y || !x || !W) return fail(K3D_EINVAL, "k3d_gemv_bf16 null pointer");
+    return gemv_bf16(y, x, W, in, out, T, accumulate, stream());
+}
+
+}  // extern "C"

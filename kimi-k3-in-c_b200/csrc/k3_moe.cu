@@ -1,0 +1,451 @@
+// k3_moe.cu -- MXFP4 routed experts (SwiGLU) and the MoE layer at the benchmark shapes:
+// k3d_expert_swiglu (config 0) and k3d_moe_swiglu (config 1).
+//
+// Follows k3_moe / moe_prefill_chunk (k3_ops.c:556-656, 717-825):
+//   1. route every token (k3_router semantics, bit-identical indices and weights);
+//   2. group the (token, slot) assignments by expert, so each selected expert's bytes
+//      are read from HBM once per step however many tokens chose it (the CPU's
+//      "fetch each unique expert once" of moe_prefill_chunk);
+//   3. gate/up GEMVs with SiLU(g)*u fused into the epilogue, per expert;
+//   4. down GEMV per expert into a per-assignment contribution buffer;
+//   5. per token, sum contributions in the ORIGINAL top-k order (acc += w_j * edn_j
+//      with separate multiply and add, k3_ops.c:641-642 / 806-810), then add the
+//      unweighted shared expert.
+// BASELINE shapes have no latent projection and use SiLU where the released model uses
+// SiTU; the CPU reference-semantics path (k3_moe in k3_refops.cu) keeps SiTU and the
+// latent MoE.
+//
+// Expert parallelism: only experts in [expert_lo, expert_hi) are computed here; the
+// combine treats the others as zero and the caller sums the partial outputs over ranks.
+#include "k3_mxfp4.cuh"
+#include "k3_ops.cuh"
+
+namespace k3 {
+
+struct MoeWork {
+    const K3ExpertQ *table;     // device table, indexed by expert id (MoE mode)
+    K3ExpertQ single;           // the one expert (single mode)
+    const int *n_active;        // device: number of active (local, selected) experts
+    const int *act_expert;      // device [n_active]
+    const int *act_off;         // device [n_active + 1] into assign
+    const int *assign;          // device: assignment ids a = t*K + j, grouped by expert
+    int single_mode;
+    int ntok_single;            // single mode: assignments a = 0..ntok-1, token t = a
+    int K;                      // top-k (token t = a / K)
+};
+
+__device__ __forceinline__ void work_item(const MoeWork &w, int u, K3ExpertQ &q, int &beg,
+                                          int &end, bool &ok)
+{
+    if (w.single_mode) {
+        q = w.single; beg = 0; end = w.ntok_single; ok = (u == 0);
+        return;
+    }
+    const int na = __ldg(w.n_active);
+    ok = u < na;
+    if (!ok) return;
+    const int e = __ldg(w.act_expert + u);
+    q = w.table[e];
+    beg = __ldg(w.act_off + u);
+    end = __ldg(w.act_off + u + 1);
+}
+
+__device__ __forceinline__ int work_assign(const MoeWork &w, int p)
+{
+    return w.single_mode ? p : __ldg(w.assign + p);
+}
+
+__device__ __forceinline__ bool bad_align(const void *a, const void *b)
+{
+    return (((uintptr_t)a | (uintptr_t)b) & 15u) != 0;
+}
+
+// ---- prep: group assignments by expert (one CTA) --------------------------------
+__global__ void __launch_bounds__(1024) k_moe_prep(const int *idx, int TK, int n_experts,
+                                                   int lo, int hi, int *n_active,
+                                                   int *act_expert, int *act_off, int *assign)
+{
+    extern __shared__ int sm[];
+    int *cnt = sm;                 // [n_experts]
+    int *cur = sm + n_experts;     // [n_experts]
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int a = threadIdx.x; a < TK; a += blockDim.x) {
+        const int e = idx[a];
+        if (e >= lo && e < hi && e < n_experts && e >= 0) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int per = (n_experts + 31) / 32;
+        const int e0 = min(n_experts, lane * per), e1 = min(n_experts, e0 + per);
+        int sc = 0, sf = 0;
+        for (int e = e0; e < e1; e++) { sc += cnt[e]; sf += cnt[e] > 0; }
+        int ic = sc, iff = sf;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int vc = __shfl_up_sync(0xffffffffu, ic, o);
+            const int vf = __shfl_up_sync(0xffffffffu, iff, o);
+            if (lane >= o) { ic += vc; iff += vf; }
+        }
+        int off = ic - sc, u = iff - sf;
+        for (int e = e0; e < e1; e++) {
+            cur[e] = off;
+            if (cnt[e] > 0) { act_expert[u] = e; act_off[u] = off; u++; }
+            off += cnt[e];
+        }
+        if (lane == 31) { *n_active = iff; act_off[iff] = ic; }
+    }
+    __syncthreads();
+    for (int a = threadIdx.x; a < TK; a += blockDim.x) {
+        const int e = idx[a];
+        if (e >= lo && e < hi && e < n_experts && e >= 0) {
+            const int p = atomicAdd(&cur[e], 1);
+            assign[p] = a;
+        }
+    }
+}
+
+// ---- gate/up + SiLU*mul -------------------------------------------------------------
+// Work item = (active expert u, block of IPC intermediate indices). Persistent grid.
+template <int NCHMAX>
+__global__ void __launch_bounds__(256, 2) k_moe_gate_up(float *act, const float *x, MoeWork w,
+                                                        int hidden, int inter, int nblk,
+                                                        int n_items, int ipc)
+{
+    extern __shared__ float4 xs[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nch = hidden >> 5;
+    const int pcols = hidden >> 1, ngrp = hidden >> 5;
+    int staged_tok = -1;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int u = item / nblk, blk = item % nblk;
+        K3ExpertQ q; int beg = 0, end = 0; bool ok;
+        work_item(w, u, q, beg, end, ok);
+        if (!ok) continue;
+        if (bad_align(q.p1, q.p3)) { if (threadIdx.x == 0) k3_raise(K3D_EINVAL, K3_SITE_MOE); continue; }
+        for (int p = beg; p < end; p++) {
+            const int a = work_assign(w, p);
+            const int t = a / w.K;
+            if (t != staged_tok) {
+                __syncthreads();
+                stage_x_mxfp4(xs, x + (size_t)t * hidden, hidden);
+                __syncthreads();
+                staged_tok = t;
+            }
+            for (int i = blk * ipc + warp; i < min(inter, (blk + 1) * ipc); i += 8) {
+                const unsigned char *pr[2] = {q.p1 + (size_t)i * pcols, q.p3 + (size_t)i * pcols};
+                const unsigned char *sr[2] = {q.s1 + (size_t)i * ngrp, q.s3 + (size_t)i * ngrp};
+                float acc[2];
+                mxfp4_rows_partial<2, NCHMAX>(acc, pr, sr, xs, nch);
+                const float g = warp_sum(acc[0]);
+                const float uu = warp_sum(acc[1]);
+                if (lane == 0) act[(size_t)a * inter + i] = silu_f(g) * uu;
+            }
+        }
+    }
+}
+
+// ---- down ---------------------------------------------------------------------------
+// Work item = (active expert u, block of RPC output rows). contrib[a][r] = W_down[r] . act[a]
+template <int R, int NCHMAX>
+__global__ void __launch_bounds__(256, 2) k_moe_down(float *contrib, const float *act, MoeWork w,
+                                                     int hidden, int inter, int nblk,
+                                                     int n_items, int rpc)
+{
+    extern __shared__ float4 xs[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nch = inter >> 5;
+    const int pcols = inter >> 1, ngrp = inter >> 5;
+    int staged_a = -1;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int u = item / nblk, blk = item % nblk;
+        K3ExpertQ q; int beg = 0, end = 0; bool ok;
+        work_item(w, u, q, beg, end, ok);
+        if (!ok) continue;
+        if (bad_align(q.p2, q.p2)) { if (threadIdx.x == 0) k3_raise(K3D_EINVAL, K3_SITE_MOE); continue; }
+        for (int p = beg; p < end; p++) {
+            const int a = work_assign(w, p);
+            if (a != staged_a) {
+                __syncthreads();
+                stage_x_mxfp4(xs, act + (size_t)a * inter, inter);
+                __syncthreads();
+                staged_a = a;
+            }
+            const int r_end = min(hidden, (blk + 1) * rpc);
+            for (int r0 = blk * rpc + warp * R; r0 < r_end; r0 += 8 * R) {
+                const unsigned char *pr[R];
+                const unsigned char *sr[R];
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const int rr = min(r0 + r, hidden - 1);
+                    pr[r] = q.p2 + (size_t)rr * pcols;
+                    sr[r] = q.s2 + (size_t)rr * ngrp;
+                }
+                float acc[R];
+                mxfp4_rows_partial<R, NCHMAX>(acc, pr, sr, xs, nch);
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const float v = warp_sum(acc[r]);
+                    if (lane == 0 && r0 + r < r_end) contrib[(size_t)a * hidden + r0 + r] = v;
+                }
+            }
+        }
+    }
+}
+
+// ---- ordered combine ------------------------------------------------------------------
+__global__ void k_moe_combine(float *out, const float *contrib, const int *idx, const float *wts,
+                              const float *sh_out, int hidden, int K, int lo, int hi,
+                              int accumulate)
+{
+    const int t = blockIdx.y;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= hidden) return;
+    float acc = 0.0f;
+    for (int j = 0; j < K; j++) {
+        const int a = t * K + j;
+        const int e = __ldg(idx + a);
+        if (e < lo || e >= hi) continue;
+        acc = __fadd_rn(acc, __fmul_rn(__ldg(wts + a), contrib[(size_t)a * hidden + r]));
+    }
+    if (sh_out) acc = __fadd_rn(acc, sh_out[(size_t)t * hidden + r]);
+    float *o = out + (size_t)t * hidden + r;
+    *o = accumulate ? __fadd_rn(*o, acc) : acc;
+}
+
+// ---- host side -------------------------------------------------------------------------
+template <typename K>
+static void allow_smem(K kern)
+{
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+static int nchmax_for(int n)
+{
+    const int per = (n / 32 + 31) / 32;
+    if (per <= 1) return 1;
+    if (per <= 2) return 2;
+    if (per <= 4) return 4;
+    if (per <= 7) return 7;
+    if (per <= 8) return 8;
+    return -1;
+}
+
+static int persistent_grid(int items)
+{
+    int g = sm_count() * 2;
+    if (items < g) g = items;
+    return g < 1 ? 1 : g;
+}
+
+static const int kIPC = 32;   // intermediate indices per gate/up work item
+static const int kRPC = 64;   // down rows per work item
+
+static int launch_gate_up(float *act, const float *x, const MoeWork &w, int hidden, int inter,
+                          int umax, cudaStream_t s)
+{
+    const int nblk = (inter + kIPC - 1) / kIPC;
+    const int items = umax * nblk;
+    const size_t smem = (size_t)hidden * sizeof(float);
+    const int g = persistent_grid(items);
+    switch (nchmax_for(hidden)) {
+#define K3_GU(N) case N: { static bool i = false; if (!i) { allow_smem(k_moe_gate_up<N>); i = true; } \
+        k_moe_gate_up<N><<<g, 256, smem, s>>>(act, x, w, hidden, inter, nblk, items, kIPC); break; }
+        K3_GU(1) K3_GU(2) K3_GU(4) K3_GU(7) K3_GU(8)
+#undef K3_GU
+    default: return fail(K3D_EINVAL, "expert hidden=%d exceeds 8192", hidden);
+    }
+    note_launch();
+    return check_launch("moe gate/up");
+}
+
+static int launch_down(float *contrib, const float *act, const MoeWork &w, int hidden, int inter,
+                       int umax, cudaStream_t s)
+{
+    const int nblk = (hidden + kRPC - 1) / kRPC;
+    const int items = umax * nblk;
+    const size_t smem = (size_t)inter * sizeof(float);
+    const int g = persistent_grid(items);
+    switch (nchmax_for(inter)) {
+#define K3_DN(N) case N: { static bool i = false; if (!i) { allow_smem(k_moe_down<4, N>); i = true; } \
+        k_moe_down<4, N><<<g, 256, smem, s>>>(contrib, act, w, hidden, inter, nblk, items, kRPC); break; }
+        K3_DN(1) K3_DN(2) K3_DN(4) K3_DN(7) K3_DN(8)
+#undef K3_DN
+    default: return fail(K3D_EINVAL, "expert inter=%d exceeds 8192", inter);
+    }
+    note_launch();
+    return check_launch("moe down");
+}
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// Workspace carve-up for k3d_moe_swiglu.
+struct MoeWs {
+    int *idx; float *wts; void *router; int *n_active; int *act_expert; int *act_off;
+    int *assign; float *act; float *contrib; float *sh_act; float *sh_out;
+    size_t total;
+};
+
+static MoeWs moe_ws_layout(const K3dMoeShape *s, int T, void *base)
+{
+    MoeWs L;
+    const size_t TK = (size_t)T * s->topk;
+    size_t off = 0;
+    char *b = (char *)base;
+    auto take = [&](size_t bytes) { char *p = b + off; off += align256(bytes); return (void *)p; };
+    L.idx = (int *)take(TK * sizeof(int));
+    L.wts = (float *)take(TK * sizeof(float));
+    L.router = take(router_ws_bytes(T, s->n_experts));
+    L.n_active = (int *)take(4 * sizeof(int));
+    L.act_expert = (int *)take((size_t)s->n_experts * sizeof(int));
+    L.act_off = (int *)take(((size_t)s->n_experts + 1) * sizeof(int));
+    L.assign = (int *)take(TK * sizeof(int));
+    L.act = (float *)take(TK * s->inter * sizeof(float));
+    L.contrib = (float *)take(TK * s->hidden * sizeof(float));
+    L.sh_act = (float *)take((size_t)T * (s->shared_inter > 0 ? s->shared_inter : 1) * sizeof(float));
+    L.sh_out = (float *)take((size_t)T * s->hidden * sizeof(float));
+    L.total = off;
+    return L;
+}
+
+static int check_shape(const K3dMoeShape *s, int T)
+{
+    if (!s) return fail(K3D_EINVAL, "null MoE shape");
+    if (T < 1) return fail(K3D_EINVAL, "MoE T=%d", T);
+    if (s->hidden % 32 || s->inter % 32 || s->hidden > 8192 || s->inter > 8192)
+        return fail(K3D_EINVAL, "MoE hidden=%d inter=%d must be multiples of 32 up to 8192",
+                    s->hidden, s->inter);
+    if (s->topk < 1 || s->topk > K3_MAX_TOPK || s->topk > s->n_experts)
+        return fail(K3D_EBOUND, "MoE topk=%d (n_experts=%d, max %d)", s->topk, s->n_experts,
+                    K3_MAX_TOPK);
+    if (s->expert_lo < 0 || s->expert_hi > s->n_experts || s->expert_lo > s->expert_hi)
+        return fail(K3D_EINVAL, "MoE expert range [%d, %d)", s->expert_lo, s->expert_hi);
+    if (s->n_experts > 8192) return fail(K3D_EINVAL, "MoE n_experts=%d > 8192", s->n_experts);
+    if (s->shared_inter > 0 && (s->shared_inter % 8))
+        return fail(K3D_EINVAL, "shared_inter=%d must be a multiple of 8", s->shared_inter);
+    return K3D_OK;
+}
+
+static int g_last_unique_host = -1;
+static int *g_last_unique_dev = nullptr;
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" {
+
+size_t k3d_expert_ws_bytes(int hidden, int inter)
+{
+    (void)hidden;
+    return align256((size_t)inter * sizeof(float)) + 256;
+}
+
+int k3d_expert_swiglu(float *y, const float *x, const K3ExpertQ *e, int hidden, int inter,
+                      void *ws, size_t ws_bytes)
+{
+    K3_TRY(ensure_ctx());
+    if (!y || !x || !e || !ws) return fail(K3D_EINVAL, "k3d_expert_swiglu null pointer");
+    if (hidden % 32 || inter % 32 || hidden > 8192 || inter > 8192)
+        return fail(K3D_EINVAL, "k3d_expert_swiglu hidden=%d inter=%d", hidden, inter);
+    if (ws_bytes < k3d_expert_ws_bytes(hidden, inter))
+        return fail(K3D_EINVAL, "k3d_expert_swiglu workspace too small");
+    const uintptr_t al = (uintptr_t)e->p1 | (uintptr_t)e->p3 | (uintptr_t)e->p2 | (uintptr_t)x |
+                         (uintptr_t)ws;
+    if (al & 15u) return fail(K3D_EINVAL, "k3d_expert_swiglu pointers must be 16-byte aligned");
+    MoeWork w{};
+    w.single = *e;
+    w.single_mode = 1;
+    w.ntok_single = 1;
+    w.K = 1;
+    float *act = (float *)ws;
+    cudaStream_t s = stream();
+    prof_begin("expert.swiglu");
+    K3_TRY(launch_gate_up(act, x, w, hidden, inter, 1, s));
+    // contrib of the single assignment is y itself
+    K3_TRY(launch_down(y, act, w, hidden, inter, 1, s));
+    prof_end("expert.swiglu");
+    return K3D_OK;
+}
+
+size_t k3d_moe_ws_bytes(const K3dMoeShape *s, int T)
+{
+    if (!s || T < 1) return 0;
+    return moe_ws_layout(s, T, nullptr).total + 256;
+}
+
+int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s, int T,
+                   int accumulate, int *idx, float *wts, void *ws, size_t ws_bytes)
+{
+    K3_TRY(ensure_ctx());
+    K3_TRY(check_shape(s, T));
+    if (!out || !x || !w || !ws || !w->router_w || !w->experts)
+        return fail(K3D_EINVAL, "k3d_moe_swiglu null pointer");
+    if (s->shared_inter > 0 && s->add_shared && (!w->sh_gate || !w->sh_up || !w->sh_down))
+        return fail(K3D_EINVAL, "k3d_moe_swiglu shared expert weights missing");
+    if (ws_bytes < k3d_moe_ws_bytes(s, T)) return fail(K3D_EINVAL, "k3d_moe_swiglu workspace too small");
+    if (((uintptr_t)x | (uintptr_t)ws) & 15u) return fail(K3D_EINVAL, "k3d_moe_swiglu alignment");
+    MoeWs L = moe_ws_layout(s, T, ws);
+    cudaStream_t st = stream();
+    int *I = idx ? idx : L.idx;
+    float *Wt = wts ? wts : L.wts;
+    const int K = s->topk;
+    const int TK = T * K;
+
+    // shared expert first: it does not depend on the router
+    const bool shared = s->shared_inter > 0 && s->add_shared;
+    if (shared) {
+        prof_begin("moe.shared");
+        K3_TRY(gemv_bf16_swiglu(L.sh_act, x, w->sh_gate, w->sh_up, s->hidden, s->shared_inter, T, st));
+        K3_TRY(gemv_bf16(L.sh_out, L.sh_act, w->sh_down, s->shared_inter, s->hidden, T, 0, st));
+        prof_end("moe.shared");
+    }
+    prof_begin("moe.router");
+    K3_TRY(router_bf16(I, Wt, x, w->router_w, w->router_bias, T, s->hidden, s->n_experts, K,
+                       s->renorm, s->routed_scale, L.router, st));
+    prof_end("moe.router");
+    {
+        const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
+        k_moe_prep<<<1, 1024, smem, st>>>(I, TK, s->n_experts, s->expert_lo, s->expert_hi,
+                                          L.n_active, L.act_expert, L.act_off, L.assign);
+        note_launch();
+        K3_TRY(check_launch("moe prep"));
+    }
+    MoeWork mw{};
+    mw.table = w->experts;
+    mw.n_active = L.n_active;
+    mw.act_expert = L.act_expert;
+    mw.act_off = L.act_off;
+    mw.assign = L.assign;
+    mw.K = K;
+    int umax = TK < (s->expert_hi - s->expert_lo) ? TK : (s->expert_hi - s->expert_lo);
+    if (umax > 0) {
+        prof_begin("moe.experts");
+        K3_TRY(launch_gate_up(L.act, x, mw, s->hidden, s->inter, umax, st));
+        K3_TRY(launch_down(L.contrib, L.act, mw, s->hidden, s->inter, umax, st));
+        prof_end("moe.experts");
+    }
+    dim3 grid((s->hidden + 255) / 256, T);
+    k_moe_combine<<<grid, 256, 0, st>>>(out, L.contrib, I, Wt, shared ? L.sh_out : nullptr,
+                                        s->hidden, K, s->expert_lo, s->expert_hi, accumulate);
+    note_launch();
+    K3_TRY(check_launch("moe combine"));
+    g_last_unique_dev = L.n_active;
+    g_last_unique_host = -1;
+    return K3D_OK;
+}
+
+int k3d_moe_last_unique(void)
+{
+    if (g_last_unique_dev && g_last_unique_host < 0) {
+        int v = -1;
+        if (cudaMemcpy(&v, g_last_unique_dev, sizeof v, cudaMemcpyDeviceToHost) == cudaSuccess)
+            g_last_unique_host = v;
+        else
+            cudaGetLastError();
+    }
+    return g_last_unique_host;
+}
+
+}  // extern "C"
