@@ -61,10 +61,13 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0:   # first sample before timing
+                time.sleep(0.02)
         except OSError:
             self.proc = None
 
@@ -73,6 +76,10 @@ class ClockSampler:
             self.rows.append([c.strip() for c in line.split(",")])
 
     def stop(self):
+        t0 = time.time()
+        n0 = len(self.rows)
+        while self.proc and len(self.rows) < n0 + 2 and time.time() - t0 < 2.0:
+            time.sleep(0.02)                                     # a sample after the region
         if self.proc:
             self.proc.terminate()
             try:
@@ -151,19 +158,116 @@ def cpu_moe_sample(seconds=12.0, max_tokens=2000):
                       f"bf16 shared expert) in {dt:.1f} s; AVX2 k3_ops.c, OpenMP"}
 
 
+def cpu_stack_sample(seconds=20.0):
+    """The reference's k3_ops.c (oracle/_ref) on the pieces of one config-4 decode token,
+    each timed on the host's cores and composed: 6 x k3_kda_layer (timed at 16 of the 64
+    heads, x4: every term but the 128-row f_a scales with heads) + 2 x k3_mla_cached with
+    its own fp32 expanded cache at 4096 cached positions + 7 x the config-1 MoE token
+    (cpu_moe_sample) + the dense SwiGLU layer and the LM head through k3_matmul_bf16
+    (timed on 1/4 and 1/10 of the rows and scaled). Returns tok/s."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as orc
+    import synth
+    if orc.Reference.available():
+        impl, kind = orc.Reference(), "reference"
+    else:
+        impl, kind = orc.Oracle(), "port"
+    lib = impl.lib
+    pre = "k3_" if kind == "reference" else "orc_"
+    g = synth.rng(909)
+    E = HIDDEN
+
+    def timeit(fn, reps=2):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    # KDA at 16 heads, bf16 weights (wdt = 1)
+    H, D = 16, 128
+    P = H * D
+    kw = {k: synth.bf16_normal(g, shp, 0.02) for k, shp in
+          (("q", (P, E)), ("k", (P, E)), ("v", (P, E)), ("g", (P, E)), ("b", (H, E)), ("f_a", (D, E)),
+           ("f_b", (P, D)), ("o", (E, P)))}
+    for k in ("q_conv", "k_conv", "v_conv"):
+        kw[k] = g.standard_normal(P * 4, dtype=np.float32) * np.float32(0.5)
+    kw["A_log"] = g.uniform(0, 1.5, H).astype(np.float32)
+    kw["dt_bias"] = g.standard_normal(P, dtype=np.float32) * np.float32(0.5)
+    kw["o_norm"] = np.ones(D, np.float32)
+    cfg = orc.K3Cfg(hidden=E, kda_heads=H, kda_head_dim=D, conv_k=4, gate_lb=-5.0, rms_eps=1e-6)
+    KW = orc.K3KdaW(*(kw[k].ctypes.data for k in ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a",
+                                                    "f_b", "A_log", "dt_bias", "b", "g", "o_norm", "o")), 1)
+    fn = getattr(lib, pre + "kda_layer")
+    fn.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(orc.K3KdaW), C.POINTER(orc.K3Cfg), C.c_int,
+                   C.c_void_p, C.c_void_p]
+    fn.restype = None
+    sfn = getattr(lib, pre + "kda_scratch")
+    sfn.argtypes = [C.POINTER(orc.K3Cfg), C.c_int]
+    sfn.restype = C.c_size_t
+    scratch = np.empty(sfn(C.byref(cfg), 1) + 1024, np.float32)
+    state = (g.standard_normal(H * D * D + 3 * P * 3, dtype=np.float32) * np.float32(0.01))
+    x = g.standard_normal(E, dtype=np.float32)
+    out = np.empty(E, np.float32)
+    t_kda = 4.0 * timeit(lambda: fn(out.ctypes.data, x.ctypes.data, C.byref(KW), C.byref(cfg), 1,
+                                    state.ctypes.data, scratch.ctypes.data))
+    del kw
+    # MLA with the reference's fp32 expanded cache, 4096 cached positions
+    Hm, ql, kvl, qn, qr, vh = 64, 1536, 512, 128, 64, 128
+    mw = {"q_a": synth.bf16_normal(g, (ql, E), 0.02), "q_b": synth.bf16_normal(g, (Hm * (qn + qr), ql), 0.02),
+          "kv_a": synth.bf16_normal(g, (kvl + qr, E), 0.02),
+          "kv_b": synth.bf16_normal(g, (Hm * (qn + vh), kvl), 0.02),
+          "o": synth.bf16_normal(g, (E, Hm * vh), 0.02), "g": synth.bf16_normal(g, (Hm * vh, E), 0.02),
+          "q_a_norm": np.ones(ql, np.float32), "kv_a_norm": np.ones(kvl, np.float32)}
+    MW = orc.K3MlaW(*(mw[k].ctypes.data for k in ("q_a", "q_b", "kv_a", "kv_b", "o", "g",
+                                                    "q_a_norm", "kv_a_norm")), 1)
+    mcfg = orc.K3Cfg(hidden=E, n_heads=Hm, q_lora=ql, kv_lora=kvl, qk_nope=qn, qk_rope=qr, v_head=vh,
+                     mla_out_gate=1, rms_eps=1e-6)
+    cached, cap = 4096, 4097
+    kvc = g.standard_normal(cap * Hm * (qn + vh), dtype=np.float32)
+    ropec = g.standard_normal(cap * qr, dtype=np.float32)
+    mf = getattr(lib, pre + "mla_cached")
+    mf.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(orc.K3MlaW), C.POINTER(orc.K3Cfg), C.c_int,
+                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+    mf.restype = None
+    msf = getattr(lib, pre + "mla_scratch_cached")
+    msf.argtypes = [C.POINTER(orc.K3Cfg), C.c_int, C.c_int, C.c_int]
+    msf.restype = C.c_size_t
+    mscratch = np.empty(msf(C.byref(mcfg), 1, cap, 1) + 1024, np.float32)
+    t_mla = timeit(lambda: mf(out.ctypes.data, x.ctypes.data, C.byref(MW), C.byref(mcfg), 1,
+                              mscratch.ctypes.data, kvc.ctypes.data, ropec.ctypes.data, cached, cap), 1)
+    del mw, kvc
+    # dense SwiGLU (1/4 of the rows) and the LM head (1/10 of the rows), bf16
+    Wd = synth.bf16_normal(g, (18432 // 4, E), 0.02)
+    t_dense = 4.0 * 3.0 * timeit(lambda: impl.matmul_bf16(x, Wd))
+    Wl = synth.bf16_normal(g, (16384, E), 0.02)
+    t_lm = 10.0 * timeit(lambda: impl.matmul_bf16(x, Wl))
+    del Wd, Wl
+    moe = cpu_moe_sample(seconds=max(3.0, seconds / 4))
+    t_moe = 1.0 / moe["value"]
+    t_tok = 6 * t_kda + 2 * t_mla + 7 * t_moe + t_dense + t_lm
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
+    return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"one config-4 token composed from timed pieces: KDA layer {t_kda * 1e3:.1f} ms x6, "
+                      f"MLA layer (4096 cached, fp32 expanded cache) {t_mla * 1e3:.1f} ms x2, MoE layer "
+                      f"{t_moe * 1e3:.1f} ms x7, dense {t_dense * 1e3:.1f} ms, LM head {t_lm * 1e3:.1f} ms; "
+                      "AVX2 k3_ops.c, OpenMP"}
+
+
 # --------------------------------------------------------------------- GPU arm ----
 def bench_moe(args, rank, world):
     import k3cuda
     lib = k3cuda.init(0)
-    per = N_EXPERTS // world
+    n_exp = args.n_experts
+    per = n_exp // world
     lo, hi = rank * per, (rank + 1) * per
     import synth
     g = synth.rng(4242)
-    W = synth.bf16_normal(g, (N_EXPERTS, HIDDEN), 0.02)
-    bias = g.uniform(-0.1, 0.1, N_EXPERTS).astype(np.float32)
+    W = synth.bf16_normal(g, (n_exp, HIDDEN), 0.02)
+    bias = g.uniform(-0.1, 0.1, n_exp).astype(np.float32)
     sh = (synth.bf16_normal(g, (SHARED, HIDDEN), 0.02), synth.bf16_normal(g, (SHARED, HIDDEN), 0.02),
           synth.bf16_normal(g, (HIDDEN, SHARED), 0.02))
-    mw = k3cuda.MoeWeights(HIDDEN, INTER, N_EXPERTS, TOPK, W, bias, shared=sh, seed=7, lo=lo, hi=hi,
+    mw = k3cuda.MoeWeights(HIDDEN, INTER, n_exp, TOPK, W, bias, shared=sh, seed=7, lo=lo, hi=hi,
                            add_shared=1 if rank == 0 else 0, lib=lib)
     P = 64
     xs = synth.bf16_to_f32(synth.bf16_normal(g, (P, HIDDEN), 1.0))
@@ -201,13 +305,13 @@ def bench_moe(args, rank, world):
     launches = lib.k3d_launch_count() - args.steps        # minus the flush memsets
     cnt = C.c_long()
     exp_ms = lib.k3d_prof_ms(b"moe.experts", C.byref(cnt))
-    n_exp = cnt.value
+    n_prof = cnt.value
     lib.k3d_prof_enable(0)
     clk = clocks.stop()
     barrier()
     tot_ms = sum(step_ms)
     tot_ms = reduce_max(tot_ms)
-    exp_ms_avg = exp_ms / max(1, n_exp)
+    exp_ms_avg = exp_ms / max(1, n_prof)
     u_avg = float(np.mean(uniq))
     alg_bytes = u_avg * (EXPERT_BYTES + INTER * 8 + HIDDEN * 4) + HIDDEN * 4
     hbm, peak_kind = measured_peaks()
@@ -235,7 +339,7 @@ def bench_moe(args, rank, world):
         "data": "synthetic (seeded MXFP4 experts, E8M0 117..121; bf16 ~N(0,0.02) router and "
                 "shared expert; bf16 ~N(0,1) tokens)",
         "config": {"workload": "config1 MoE layer decode, T=1", "hidden": HIDDEN,
-                   "n_experts": N_EXPERTS, "topk": TOPK, "inter": INTER, "shared_inter": SHARED,
+                   "n_experts": n_exp, "topk": TOPK, "inter": INTER, "shared_inter": SHARED,
                    "parallelism": f"ep{world}", "l2": "flushed between steps (256 MB write)"},
         "roofline": {"kernel": "MXFP4 expert GEMV (k_moe_gate_up + k_moe_down)", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -247,6 +351,129 @@ def bench_moe(args, rank, world):
                 "d2h_bytes_per_step": HIDDEN * 4},
         "gpu_launches": int(launches),
         "clocks": clk,
+    }
+    return res
+
+
+# ----------------------------------------------------------------- stack (config 4) ----
+def stack_cfg(world, rank, batch, cap):
+    import k3cuda
+    sc = k3cuda.K3dStackCfg()
+    sc.hidden, sc.vocab, sc.n_layers, sc.eps = HIDDEN, 163840, 8, 1e-6
+    sc.kda_heads, sc.kda_head_dim, sc.conv_k, sc.gate_lb = 64, 128, 4, -5.0
+    sc.mla = k3cuda.K3dMlaShape(HIDDEN, 64, 1536, 512, 128, 64, 128, 50000.0, 1e-6, 1)
+    per = N_EXPERTS // world
+    sc.moe = k3cuda.K3dMoeShape(HIDDEN, INTER, N_EXPERTS, TOPK, 1, 2.5, SHARED, rank * per,
+                                (rank + 1) * per, 1 if rank == 0 else 0)
+    sc.first_dense, sc.dense_inter = 1, 18432
+    for i in range(16):
+        sc.mla_layers[i] = (3, 7)[i] if i < 2 else -1
+    sc.batch, sc.ctx_cap = batch, cap
+    return sc
+
+
+def bench_stack(args, rank, world):
+    import k3cuda
+    lib = k3cuda.init(0)
+    ctx = args.context
+    cap = ctx + args.steps * 2 + args.warmup * 2 + 16
+    cfg = stack_cfg(world, rank, args.batch, cap)
+    t0 = time.time()
+    model = lib.k3d_model_create(C.byref(cfg), 2024)
+    if not model:
+        raise k3cuda.K3Error("k3d_model_create failed: " + lib.k3d_last_message().decode())
+    k3cuda.check(lib.k3d_model_fill_context(model, ctx, 77))
+    k3cuda.check(lib.k3d_sync())
+    init_s = time.time() - t0
+    B = args.batch
+    ids = k3cuda.DevBuf(B * 4, lib)
+    nxt = k3cuda.DevBuf(B * 4, lib)
+    k3cuda.check(lib.k3d_fill_i32_uniform(ids.ptr, B, 5, 0, 163839))
+    logits_p = lib.k3d_model_tensor(model, b"logits", None)
+    ev = [lib.k3d_event_create() for _ in range(2)]
+    # warm-up: the first step runs eagerly, the second captures the graph
+    for i in range(args.warmup):
+        k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "warmup step")
+        k3cuda.check(lib.k3d_copy(ids.ptr, nxt.ptr, B * 4))
+    k3cuda.check(lib.k3d_sync())
+    barrier()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0)))
+    clocks.start()
+    lib.k3d_launch_count_reset()
+    step_ms = []
+    for i in range(args.steps):
+        lib.k3d_event_record(ev[0])
+        k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "step")
+        lib.k3d_event_record(ev[1])
+        step_ms.append(lib.k3d_event_elapsed_ms(ev[0], ev[1]))
+        k3cuda.check(lib.k3d_copy(ids.ptr, nxt.ptr, B * 4))   # greedy: next token in
+    k3cuda.check(lib.k3d_sync())
+    clk = clocks.stop()
+    barrier()
+    tot_ms = reduce_max(sum(step_ms))
+    step_bytes = lib.k3d_model_last_step_bytes(model)
+    hbm, peak_kind = measured_peaks()
+    # per-kernel device times from an eager pass with the section timers on (graph
+    # replays carry no per-kernel events); same kernels, same inputs
+    k3cuda.check(lib.k3d_model_use_graph(model, 0))
+    lib.k3d_prof_reset()
+    lib.k3d_prof_enable(1)
+    lib.k3d_launch_count_reset()
+    n_prof = max(3, min(args.steps, 10))
+    for i in range(n_prof):
+        k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "profiled step")
+    k3cuda.check(lib.k3d_sync())
+    launches_per_step = lib.k3d_launch_count() / n_prof
+    sections = {}
+    for name in ("moe.experts", "moe.shared", "moe.router", "kda.proj_in", "kda.core",
+                 "kda.proj_out", "mla.proj_in", "mla.core", "mla.proj_out", "dense.mlp", "lm_head",
+                 "ep.combine"):
+        cnt = C.c_long()
+        ms = lib.k3d_prof_ms(name.encode(), C.byref(cnt))
+        if cnt.value:
+            sections[name] = {"ms_per_call": ms / cnt.value, "calls_per_step": cnt.value / n_prof}
+    lib.k3d_prof_enable(0)
+    k3cuda.check(lib.k3d_model_use_graph(model, 1))
+    exp_ms = sections.get("moe.experts", {}).get("ms_per_call", float("nan"))
+    alg_exp = (TOPK * B) * (EXPERT_BYTES + INTER * 8 + HIDDEN * 4) + HIDDEN * 4 * B
+    if world > 1:
+        alg_exp /= world
+    achieved = alg_exp / (exp_ms * 1e-3) / 1e9
+    # end to end through the public API with host buffers: token ids in, next ids out
+    hid = np.zeros(B, np.int32)
+    hnx = np.zeros(B, np.int32)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        k3cuda.check(lib.k3d_model_step_host(model, hid.ctypes.data, hnx.ctypes.data), "e2e step")
+        hid[:] = hnx
+    e2e_s = reduce_max(time.perf_counter() - t0)
+    lib.k3d_model_destroy(model)
+    ms = tot_ms / args.steps
+    res = {
+        "metric": METRIC, "value": B * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic random-init weights (bf16 ~N(0,0.02), MXFP4 experts E8M0 117..121); "
+                f"MLA latent caches ~N(0,1) and KDA states ~N(0,0.01) filled as after {ctx} tokens",
+        "config": {"workload": "config4 8-layer K3 stack decode", "batch": B, "context": ctx,
+                   "hidden": HIDDEN, "layers": "KDA x6 + MLA x2 (one-based 4, 8); layer 0 dense 18432, "
+                   "layers 1-7 MoE 384x top-8 + shared", "vocab": 163840,
+                   "parallelism": f"ep{world}", "graph": True,
+                   "l2": f"per-step working set {step_bytes / 1e9:.2f} GB >> 126 MB L2"},
+        "roofline": {"kernel": "MXFP4 expert GEMV (k_mxfp4_mma gate/up + down)", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": peak_kind, "traffic": load_traffic("moe_experts_traffic.json"),
+                     "alg_bytes_per_launch": alg_exp, "kernel_ms": exp_ms},
+        "roofline_step": {"bound": "hbm", "alg_bytes_per_step": step_bytes,
+                          "achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                          "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm},
+        "sections_ms": sections,
+        "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": clk,
+        "init_s": init_s,
     }
     return res
 
@@ -300,31 +527,44 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="moe", choices=["moe"])
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", default="stack", choices=["stack", "moe"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="bounded CPU-baseline sample length; 0 skips it")
+    ap.add_argument("--n-experts", type=int, default=N_EXPERTS,
+                    help="routed experts resident per layer (384 = config 1; fewer only for "
+                         "profiling captures that must stay small)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_env()
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_moe_sample(seconds=args.cpu_seconds)
+        if args.workload == "stack":
+            cb = cpu_stack_sample(args.cpu_seconds)
+            wl = {"workload": "config4 8-layer K3 stack decode", "batch": 1, "context": args.context,
+                  "hidden": HIDDEN, "vocab": 163840, "parallelism": "cpu"}
+        else:
+            cb = cpu_moe_sample(seconds=args.cpu_seconds)
+            wl = {"workload": "config1 MoE layer decode, T=1", "hidden": HIDDEN,
+                  "n_experts": N_EXPERTS, "topk": TOPK, "parallelism": "cpu"}
         res = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cb["value"],
                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                "dtype": "fp64-accumulate/fp32", "data": "synthetic",
-               "config": {"workload": "config1 MoE layer decode, T=1", "hidden": HIDDEN,
-                          "n_experts": N_EXPERTS, "topk": TOPK, "parallelism": "cpu"},
+               "config": wl,
                "impl": "reference", "cpu_baseline": cb,
                "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                        "d2h_bytes_per_step": 0}}
         print(json.dumps(res), flush=True)
         return
     setup_dist(world, rank, local)
-    res = bench_moe(args, rank, world)
+    res = bench_stack(args, rank, world) if args.workload == "stack" else bench_moe(args, rank, world)
     if rank == 0:
-        if world == 1:
-            res["cpu_baseline"] = cpu_moe_sample(seconds=args.cpu_seconds)
+        if world == 1 and args.cpu_seconds > 0:
+            res["cpu_baseline"] = (cpu_stack_sample(args.cpu_seconds) if args.workload == "stack"
+                                   else cpu_moe_sample(seconds=args.cpu_seconds))
         print(json.dumps(res), flush=True)
     if world > 1:
         import k3cuda

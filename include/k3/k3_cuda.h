@@ -183,6 +183,32 @@ int k3d_kda_prefill(float *S, float *o, const float *q, const float *k, const fl
                     const float *alpha, const float *beta, int T, int H, int dk, int dv,
                     int chunk);
 
+/* Full KDA decode layer (one token per sequence) at bf16 weights: k3_kda_layer
+ * (k3_ops.c:850-937) at T = 1. h (+)= o_proj(...) of the normed input xn; state is the
+ * CPU engine's per-sequence layout (H*D*D recurrent floats, then 3*H*D*(conv_k-1) conv
+ * history floats), k3d_kda_state_floats() per sequence, updated in place. */
+typedef struct {
+    int   hidden, heads, head_dim, conv_k;
+    float gate_lb, eps;
+} K3dKdaShape;
+
+typedef struct {
+    const uint16_t *q, *k, *v, *g;     /* [H*D][hidden] */
+    const uint16_t *b;                 /* [H][hidden] */
+    const uint16_t *f_a;               /* [D][hidden] */
+    const uint16_t *f_b;               /* [H*D][D] */
+    const uint16_t *o;                 /* [hidden][H*D] */
+    const float *q_conv, *k_conv, *v_conv;   /* [H*D][conv_k] */
+    const float *A_log;                /* [H] */
+    const float *dt_bias;              /* [H*D] */
+    const float *o_norm;               /* [D] */
+} K3dKdaW;
+
+size_t k3d_kda_layer_ws_bytes(const K3dKdaShape *s, int B);
+size_t k3d_kda_state_floats(const K3dKdaShape *s);
+int    k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dKdaShape *s,
+                            int B, float *state, void *ws, size_t ws_bytes);
+
 /* ------------------------------------------------------------------- MLA ---- */
 typedef struct {
     int   hidden, n_heads, q_lora, kv_lora, qk_nope, qk_rope, v_head;
@@ -214,6 +240,21 @@ int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaSha
 /* ------------------------------------------------------------- small ops ---- */
 int k3d_rmsnorm(float *y, const float *x, const float *w, int n, int rows, float eps);
 int k3d_silu_mul(float *y, const float *gu, int n, int rows); /* gu = [gate | up] per row */
+/* h[b] = bf16 table row ids[b], widened (the CPU's k3_embed_row, k3_bind.h:148-157) */
+int k3d_embed_bf16(float *h, const int *ids, const uint16_t *table, int B, int hidden, int vocab);
+/* dense SwiGLU MLP: h[b] (+)= down(silu(gate x) * (up x)), bf16 weights; ws holds
+ * B*inter floats */
+int k3d_swiglu_mlp_bf16(float *h, const float *x, const uint16_t *gate, const uint16_t *up,
+                        const uint16_t *down, int hidden, int inter, int B, int accumulate,
+                        float *ws);
+/* logits = W x (bf16 W [vocab][hidden]) and next[b] = first index of the maximum logit
+ * (argmax_ of k3_run.c:134-135); logits may be NULL; key_ws holds B 8-byte keys. */
+int k3d_lm_head_argmax(int *next, float *logits, const float *x, const uint16_t *W, int vocab,
+                       int hidden, int B, void *key_ws);
+/* y[i] += x[i] for i < n (device floats) */
+int k3d_add_f32(float *y, const float *x, size_t n);
+/* p[i] += delta for i < n (device ints; advances cache positions inside a graph) */
+int k3d_add_i32(int *p, int n, int delta);
 
 /* --------------------------------------------------------------- EP/NCCL ---- */
 /* Expert parallelism over NCCL: one process per GPU. rank 0 calls

@@ -25,6 +25,11 @@ void note_launch(int n = 1);
 // Checks cudaGetLastError() after a launch; records K3D_ECUDA on failure.
 int check_launch(const char *what);
 
+// Raises a kernel's dynamic shared memory limit to the device's opt-in maximum minus
+// the kernel's static shared memory (cudaFuncSetAttribute rejects anything above that).
+void allow_dyn_smem(const void *func);
+template <typename F> inline void allow_smem_max(F *f) { allow_dyn_smem((const void *)f); }
+
 // Section timers (k3d_prof_*): begin/end record events on the library stream when
 // profiling is on and no capture is in progress.
 void prof_begin(const char *section);

@@ -96,6 +96,19 @@ void prof_collect(Ctx::Sec &sec)
 
 }  // namespace
 
+void allow_dyn_smem(const void *func)
+{
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, g.device < 0 ? 0 : g.device);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, func) != cudaSuccess) { cudaGetLastError(); return; }
+    const int want = optin - (int)fa.sharedSizeBytes;
+    if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, want) != cudaSuccess) {
+        cudaGetLastError();
+        fail(K3D_ECUDA, "cannot raise dynamic shared memory to %d bytes", want);
+    }
+}
+
 void prof_begin(const char *section)
 {
     if (!g.prof || capturing_now()) return;

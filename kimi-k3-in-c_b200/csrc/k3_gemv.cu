@@ -153,20 +153,123 @@ __global__ void k_gemv_generic(float *y, const float *x, const WT *W, int in, in
     }
 }
 
+// Up to 8 weight matrices sharing the input x (q|k|v|g|b|f_a of a KDA layer, q_a|kv_a|g
+// of an MLA layer): one launch over the concatenated row space.
+template <typename K>
+static void allow_smem(K kern)
+{
+    allow_smem_max(kern);
+}
+int grid_for(int rows, int rows_per_cta);
+
+struct Segs {
+    const uint16_t *W[8];
+    float *y[8];
+    int rows[8];
+    int start[9];      // prefix of rows
+    int n;
+};
+
+template <int R, int SEG>
+__global__ void __launch_bounds__(256) k_gemv_bf16_multi(Segs S, const float *x, int in, int T)
+{
+    extern __shared__ float4 xs[];
+    const int nf4 = in >> 2;
+    for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
+    __syncthreads();
+    const int nch = in >> 3;
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int total = S.start[S.n];
+    for (int r0 = warp * R; r0 < total; r0 += nwarps * R) {
+        const uint16_t *pr[R];
+        float *dst[R];
+        int seg_rows[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int gr = min(r0 + r, total - 1);
+            int sgi = 0;
+            while (sgi + 1 < S.n && gr >= S.start[sgi + 1]) sgi++;
+            const int lr = gr - S.start[sgi];
+            pr[r] = S.W[sgi] + (size_t)lr * in;
+            dst[r] = S.y[sgi] + lr;
+            seg_rows[r] = S.rows[sgi];
+        }
+        for (int t = 0; t < T; t++) {
+            float acc[R];
+            bf16_rows_partial<R, SEG>(acc, pr, xs + (size_t)t * nf4, nch);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const float v = warp_sum(acc[r]);
+                if (lane == 0 && r0 + r < total) dst[r][(size_t)t * seg_rows[r]] = v;
+            }
+        }
+    }
+}
+
+// Logits with a fused argmax: key[t] = max over rows of (ordered float bits << 32 |
+// ~row), so the largest logit wins and, among equal logits, the lowest row (the first
+// maximum, as the CPU's argmax scan returns).
+__device__ __forceinline__ unsigned long long argmax_pack(float v, int row)
+{
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)row);
+}
+
+template <int R, int SEG>
+__global__ void __launch_bounds__(256) k_gemv_bf16_argmax(float *y, unsigned long long *key,
+                                                          const float *x, const uint16_t *W,
+                                                          int in, int out, int T)
+{
+    extern __shared__ float4 xs[];
+    const int nf4 = in >> 2;
+    for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
+    __syncthreads();
+    const int nch = in >> 3;
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    unsigned long long best[4] = {0, 0, 0, 0};
+    for (int r0 = warp * R; r0 < out; r0 += nwarps * R) {
+        const uint16_t *pr[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) pr[r] = W + (size_t)min(r0 + r, out - 1) * in;
+        for (int t = 0; t < T; t++) {
+            float acc[R];
+            bf16_rows_partial<R, SEG>(acc, pr, xs + (size_t)t * nf4, nch);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const float v = warp_sum(acc[r]);
+                if (lane == 0 && r0 + r < out) {
+                    if (y) y[(size_t)t * out + r0 + r] = v;
+                    const unsigned long long k = argmax_pack(v, r0 + r);
+                    if (v == v && k > best[t]) best[t] = k;
+                }
+            }
+        }
+    }
+    if (lane == 0)
+        for (int t = 0; t < T; t++)
+            if (best[t]) atomicMax(key + t, best[t]);
+}
+
+__global__ void k_argmax_finish(int *next, const unsigned long long *key, int T)
+{
+    const int t = threadIdx.x;
+    if (t < T) next[t] = (int)(0xffffffffu - (uint32_t)(key[t] & 0xffffffffu));
+}
+
 static bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
-static int grid_for(int rows, int rows_per_cta)
+int grid_for(int rows, int rows_per_cta);
+int grid_for(int rows, int rows_per_cta)
 {
     int grid = (rows + rows_per_cta - 1) / rows_per_cta;
     const int cap = sm_count() * 4;
     if (grid > cap) grid = cap;
     return grid < 1 ? 1 : grid;
-}
-
-template <typename K>
-static void allow_smem(K kern)
-{
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
 int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int T,
@@ -218,6 +321,45 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
         note_launch();
     }
     return check_launch("gemv bf16 swiglu");
+}
+
+int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
+                    const float *x, int in, int T, cudaStream_t s)
+{
+    if (nseg < 1 || nseg > 8 || T < 1 || T > 4)
+        return fail(K3D_EINVAL, "multi-segment GEMV: %d segments, T=%d", nseg, T);
+    Segs S;
+    S.n = nseg;
+    S.start[0] = 0;
+    for (int i = 0; i < nseg; i++) {
+        if (!al16(W[i])) return fail(K3D_EINVAL, "multi-segment GEMV: unaligned matrix");
+        S.W[i] = W[i];
+        S.y[i] = y[i];
+        S.rows[i] = rows[i];
+        S.start[i + 1] = S.start[i] + rows[i];
+    }
+    if ((in % 8) != 0 || (size_t)in * 4 * T > 200 * 1024)
+        return fail(K3D_EINVAL, "multi-segment GEMV: in=%d", in);
+    static bool init = false;
+    if (!init) { allow_smem(k_gemv_bf16_multi<2, 7>); init = true; }
+    k_gemv_bf16_multi<2, 7><<<grid_for(S.start[nseg], 64), 256, (size_t)T * in * 4, s>>>(S, x, in, T);
+    note_launch();
+    return check_launch("gemv bf16 multi");
+}
+
+int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
+                     const uint16_t *W, int in, int out, int T, cudaStream_t s)
+{
+    if (T < 1 || T > 4 || (in % 8) != 0 || !al16(W))
+        return fail(K3D_EINVAL, "lm head: T=%d in=%d", T, in);
+    static bool init = false;
+    if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
+    K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
+               ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
+    k_gemv_bf16_argmax<2, 7><<<grid_for(out, 64), 256, (size_t)T * in * 4, s>>>(y, key, x, W, in, out, T);
+    k_argmax_finish<<<1, 32, 0, s>>>(next, key, T);
+    note_launch(2);
+    return check_launch("lm head argmax");
 }
 
 int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStream_t s)

@@ -115,8 +115,8 @@ static void kda_attrs()
 {
     static bool init = false;
     if (!init) {
-        cudaFuncSetAttribute(k_kda_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(k_kda_seq, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        allow_smem_max(k_kda_decode);
+        allow_smem_max(k_kda_seq);
         init = true;
     }
 }

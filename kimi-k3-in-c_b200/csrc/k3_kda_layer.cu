@@ -1,0 +1,203 @@
+// k3_kda_layer.cu -- one KDA decode layer for B sequences (one token each), following
+// k3_kda_layer (k3_ops.c:850-937) at T = 1, with bf16 projection weights:
+//
+//   1. one multi-segment GEMV of the normed input: q, k, v, g [P], b [H], f_a [D]
+//   2. f_b GEMV: z = f_b(f_a x)                                               [P]
+//   3. k_kda_head, one CTA per (sequence, head), thread j = channel:
+//        ShortConv + SiLU on q, k, v (conv history updated in place)  k3_ops.c:875-878
+//        L2Norm q and k over the head (sum of squares, eps 1e-6)      k3_ops.c:881-885
+//        beta = sigmoid(b);  g = lb*sigmoid(exp(A_log[h])*(z+dt_bias)); alpha = exp(g)
+//        q *= D^-0.5; the delta-rule step on the head's state tile, staged in shared
+//        memory, one column per thread in the CPU's order       k3_ops.c:186-243, 916-924
+//        head RMSNorm with o_norm, THEN times sigmoid(g)         k3_ops.c:927-933
+//   4. o_proj GEMV accumulated into the residual stream.
+//
+// State per sequence: S [H][D][D] fp32 followed by the conv history [3][P][conv_k-1]
+// (q, k, v channels), the CPU engine's layout (k3.h:464-466).
+#include "k3_common.cuh"
+#include "k3_ops.cuh"
+
+namespace k3 {
+
+__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ double block_sum_dd(double v, double *red, int nwarps)
+{
+    v = warp_sum_d(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double s = 0.0;
+    for (int i = 0; i < nwarps; i++) s += red[i];
+    return s;
+}
+
+struct KdaHeadArgs {
+    const float *qp, *kp, *vp, *gp, *bp, *z;   // projections [B][P] / [B][H]
+    const float *q_conv, *k_conv, *v_conv;     // [P][K]
+    const float *A_log, *dt_bias, *o_norm;     // [H], [P], [D]
+    float *state;                              // [B][state floats]
+    float *heads;                              // [B][P]
+    int H, D, K;
+    float lb, eps;
+    size_t state_stride;                       // floats per sequence
+};
+
+__device__ __forceinline__ float conv_silu(const float *w, float *hist, float cur, int K)
+{
+    const int hst = K - 1;
+    float acc = __fmul_rn(w[hst], cur);
+    for (int j = 0; j < hst; j++) acc = __fadd_rn(acc, __fmul_rn(w[j], hist[j]));
+    for (int j = 0; j + 1 < hst; j++) hist[j] = hist[j + 1];
+    if (hst > 0) hist[hst - 1] = cur;
+    return __fmul_rn(acc, sigm(acc));
+}
+
+// grid (H, B), blockDim = D (<= 128, multiple of 32). Shared: D*D state + 3*D vectors.
+__global__ void k_kda_head(KdaHeadArgs A)
+{
+    extern __shared__ float sh[];
+    __shared__ double red[8];
+    const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
+    const int D = A.D, H = A.H, K = A.K, P = H * D, hst = K - 1;
+    float *St = sh;
+    float *qs = St + D * D, *ks = qs + D, *as = ks + D;
+    float *S = A.state + (size_t)b * A.state_stride + (size_t)h * D * D;
+    float *conv = A.state + (size_t)b * A.state_stride + (size_t)H * D * D;
+    const int nw = blockDim.x >> 5;
+    // stage the state tile
+    {
+        const float4 *S4 = reinterpret_cast<const float4 *>(S);
+        float4 *T4 = reinterpret_cast<float4 *>(St);
+        for (int f = j; f < D * D / 4; f += blockDim.x) T4[f] = S4[f];
+    }
+    const int c = h * D + j;
+    const size_t bp = (size_t)b * P + c;
+    // ShortConv + SiLU (history in place)
+    float hist[15];
+    float qv, kv, vv;
+    {
+        float *hq = conv + (size_t)c * hst;
+        for (int t = 0; t < hst; t++) hist[t] = hq[t];
+        qv = conv_silu(A.q_conv + (size_t)c * K, hist, A.qp[bp], K);
+        for (int t = 0; t < hst; t++) hq[t] = hist[t];
+        float *hk = conv + (size_t)P * hst + (size_t)c * hst;
+        for (int t = 0; t < hst; t++) hist[t] = hk[t];
+        kv = conv_silu(A.k_conv + (size_t)c * K, hist, A.kp[bp], K);
+        for (int t = 0; t < hst; t++) hk[t] = hist[t];
+        float *hv = conv + (size_t)2 * P * hst + (size_t)c * hst;
+        for (int t = 0; t < hst; t++) hist[t] = hv[t];
+        vv = conv_silu(A.v_conv + (size_t)c * K, hist, A.vp[bp], K);
+        for (int t = 0; t < hst; t++) hv[t] = hist[t];
+    }
+    // L2Norm q and k over the head
+    const double sq = block_sum_dd((double)qv * (double)qv, red, nw);
+    const double sk = block_sum_dd((double)kv * (double)kv, red, nw);
+    qv = __fmul_rn(qv, (float)(1.0 / sqrt(sq + (double)1e-6f)));
+    kv = __fmul_rn(kv, (float)(1.0 / sqrt(sk + (double)1e-6f)));
+    qv = __fmul_rn(qv, 1.0f / sqrtf((float)D));
+    // beta and the decay chain
+    const float beta = sigm(A.bp[(size_t)b * H + h]);
+    const float a = expf(A.A_log[h]);
+    const float gdec = __fmul_rn(A.lb, sigm(__fmul_rn(a, __fadd_rn(A.z[bp], A.dt_bias[c]))));
+    qs[j] = qv;
+    ks[j] = kv;
+    as[j] = expf(gdec);
+    __syncthreads();
+    // delta-rule step, column j (the CPU's order and roundings)
+    float u = 0.0f;
+    for (int i = 0; i < D; i++) {
+        const float si = __fmul_rn(St[i * D + j], as[i]);
+        St[i * D + j] = si;
+        if (ks[i] != 0.0f) u = __fadd_rn(u, __fmul_rn(ks[i], si));
+    }
+    const float d = __fsub_rn(vv, u);
+    float o = 0.0f;
+    for (int i = 0; i < D; i++) {
+        float si = St[i * D + j];
+        if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(__fmul_rn(ks[i], beta), d));
+        if (qs[i] != 0.0f) o = __fadd_rn(o, __fmul_rn(qs[i], si));
+        S[(size_t)i * D + j] = si;
+    }
+    // head RMSNorm, then the output gate
+    const double so = block_sum_dd((double)o * (double)o, red, nw);
+    const float inv = (float)(1.0 / sqrt(so / (double)D + (double)A.eps));
+    o = __fmul_rn(__fmul_rn(A.o_norm[j], o), inv);
+    o = __fmul_rn(o, sigm(A.gp[bp]));
+    A.heads[bp] = o;
+}
+
+static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" {
+
+size_t k3d_kda_layer_ws_bytes(const K3dKdaShape *s, int B)
+{
+    if (!s || B < 1) return 0;
+    const size_t P = (size_t)s->heads * s->head_dim;
+    return 6 * al256((size_t)B * P * 4) + al256((size_t)B * s->heads * 4) +
+           al256((size_t)B * s->head_dim * 4) + 256;
+}
+
+size_t k3d_kda_state_floats(const K3dKdaShape *s)
+{
+    const size_t P = (size_t)s->heads * s->head_dim;
+    return (size_t)s->heads * s->head_dim * s->head_dim + 3 * P * (size_t)(s->conv_k - 1);
+}
+
+int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dKdaShape *s,
+                         int B, float *state, void *ws, size_t ws_bytes)
+{
+    K3_TRY(ensure_ctx());
+    if (!h || !xn || !w || !s || !state || !ws) return fail(K3D_EINVAL, "kda layer null pointer");
+    if (!w->q || !w->k || !w->v || !w->g || !w->b || !w->f_a || !w->f_b || !w->o ||
+        !w->q_conv || !w->k_conv || !w->v_conv || !w->A_log || !w->dt_bias || !w->o_norm)
+        return fail(K3D_EINVAL, "kda layer weight missing");
+    const int H = s->heads, D = s->head_dim, P = H * D;
+    if (D < 32 || D > 128 || D % 32 || s->conv_k < 1 || s->conv_k > 16 || B < 1 || B > 4)
+        return fail(K3D_EINVAL, "kda layer: head_dim %d (32..128, multiple of 32), conv_k %d, B %d (1..4)",
+                    D, s->conv_k, B);
+    if (ws_bytes < k3d_kda_layer_ws_bytes(s, B)) return fail(K3D_EINVAL, "kda layer workspace");
+    char *p = (char *)ws;
+    auto take = [&](size_t bytes) { char *r = p; p += al256(bytes); return (float *)r; };
+    float *qp = take((size_t)B * P * 4), *kp = take((size_t)B * P * 4), *vp = take((size_t)B * P * 4);
+    float *gp = take((size_t)B * P * 4), *z = take((size_t)B * P * 4), *heads = take((size_t)B * P * 4);
+    float *bp = take((size_t)B * H * 4), *fa = take((size_t)B * D * 4);
+    cudaStream_t st = stream();
+    prof_begin("kda.proj_in");
+    const uint16_t *Ws[6] = {w->q, w->k, w->v, w->g, w->b, w->f_a};
+    float *Ys[6] = {qp, kp, vp, gp, bp, fa};
+    const int rows[6] = {P, P, P, P, H, D};
+    K3_TRY(gemv_bf16_multi(6, Ws, Ys, rows, xn, s->hidden, B, st));
+    K3_TRY(gemv_bf16(z, fa, w->f_b, D, P, B, 0, st));
+    prof_end("kda.proj_in");
+    prof_begin("kda.core");
+    KdaHeadArgs A;
+    A.qp = qp; A.kp = kp; A.vp = vp; A.gp = gp; A.bp = bp; A.z = z;
+    A.q_conv = w->q_conv; A.k_conv = w->k_conv; A.v_conv = w->v_conv;
+    A.A_log = w->A_log; A.dt_bias = w->dt_bias; A.o_norm = w->o_norm;
+    A.state = state; A.heads = heads;
+    A.H = H; A.D = D; A.K = s->conv_k; A.lb = s->gate_lb; A.eps = s->eps;
+    A.state_stride = k3d_kda_state_floats(s);
+    const size_t smem = ((size_t)D * D + 3 * (size_t)D) * 4;
+    static bool init = false;
+    if (!init) {
+        allow_smem_max(k_kda_head);
+        init = true;
+    }
+    k_kda_head<<<dim3(H, B), D, smem, st>>>(A);
+    note_launch();
+    K3_TRY(check_launch("kda head"));
+    prof_end("kda.core");
+    prof_begin("kda.proj_out");
+    K3_TRY(gemv_bf16(h, heads, w->o, P, s->hidden, B, 1, st));
+    prof_end("kda.proj_out");
+    return K3D_OK;
+}
+
+}  // extern "C"

@@ -18,47 +18,10 @@
 // Expert parallelism: only experts in [expert_lo, expert_hi) are computed here; the
 // combine treats the others as zero and the caller sums the partial outputs over ranks.
 #include "k3_mxfp4.cuh"
+#include "k3_moe.cuh"
 #include "k3_ops.cuh"
 
 namespace k3 {
-
-struct MoeWork {
-    const K3ExpertQ *table;     // device table, indexed by expert id (MoE mode)
-    K3ExpertQ single;           // the one expert (single mode)
-    const int *n_active;        // device: number of active (local, selected) experts
-    const int *act_expert;      // device [n_active]
-    const int *act_off;         // device [n_active + 1] into assign
-    const int *assign;          // device: assignment ids a = t*K + j, grouped by expert
-    int single_mode;
-    int ntok_single;            // single mode: assignments a = 0..ntok-1, token t = a
-    int K;                      // top-k (token t = a / K)
-};
-
-__device__ __forceinline__ void work_item(const MoeWork &w, int u, K3ExpertQ &q, int &beg,
-                                          int &end, bool &ok)
-{
-    if (w.single_mode) {
-        q = w.single; beg = 0; end = w.ntok_single; ok = (u == 0);
-        return;
-    }
-    const int na = __ldg(w.n_active);
-    ok = u < na;
-    if (!ok) return;
-    const int e = __ldg(w.act_expert + u);
-    q = w.table[e];
-    beg = __ldg(w.act_off + u);
-    end = __ldg(w.act_off + u + 1);
-}
-
-__device__ __forceinline__ int work_assign(const MoeWork &w, int p)
-{
-    return w.single_mode ? p : __ldg(w.assign + p);
-}
-
-__device__ __forceinline__ bool bad_align(const void *a, const void *b)
-{
-    return (((uintptr_t)a | (uintptr_t)b) & 15u) != 0;
-}
 
 // ---- prep: group assignments by expert (one CTA) --------------------------------
 __global__ void __launch_bounds__(1024) k_moe_prep(const int *idx, int TK, int n_experts,
@@ -218,7 +181,7 @@ __global__ void k_moe_combine(float *out, const float *contrib, const int *idx, 
 template <typename K>
 static void allow_smem(K kern)
 {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    allow_smem_max(kern);
 }
 
 static int nchmax_for(int n)
@@ -280,10 +243,27 @@ static int launch_down(float *contrib, const float *act, const MoeWork &w, int h
 
 static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
+// gate/up -> act -> down -> contrib for a work list, on tensor cores when the shapes
+// allow (hidden, inter multiples of 512) and on the CUDA-core kernels otherwise.
+static int run_experts(const MoeWork &mw, int umax, const float *x, int T, int TK, int hidden,
+                       int inter, float *act, float *contrib, __half *xb_x, float *xs_x,
+                       __half *xb_a, float *xs_a, cudaStream_t st)
+{
+    if (mma_supported(hidden, inter, 0) && mma_supported(inter, hidden, 1) && xb_x && xb_a) {
+        K3_TRY(xsplit(xb_x, xs_x, x, hidden, T, hidden, st));
+        K3_TRY(mxfp4_mma_launch(0, mw, umax, hidden, inter, xb_x, xs_x, 0, act, st));
+        K3_TRY(xsplit(xb_a, xs_a, act, inter, TK, inter, st));
+        return mxfp4_mma_launch(1, mw, umax, inter, hidden, xb_a, xs_a, 1, contrib, st);
+    }
+    K3_TRY(launch_gate_up(act, x, mw, hidden, inter, umax, st));
+    return launch_down(contrib, act, mw, hidden, inter, umax, st);
+}
+
 // Workspace carve-up for k3d_moe_swiglu.
 struct MoeWs {
     int *idx; float *wts; void *router; int *n_active; int *act_expert; int *act_off;
     int *assign; float *act; float *contrib; float *sh_act; float *sh_out;
+    __half *xb_x; float *xs_x; __half *xb_a; float *xs_a;
     size_t total;
 };
 
@@ -305,6 +285,10 @@ static MoeWs moe_ws_layout(const K3dMoeShape *s, int T, void *base)
     L.contrib = (float *)take(TK * s->hidden * sizeof(float));
     L.sh_act = (float *)take((size_t)T * (s->shared_inter > 0 ? s->shared_inter : 1) * sizeof(float));
     L.sh_out = (float *)take((size_t)T * s->hidden * sizeof(float));
+    L.xb_x = (__half *)take((size_t)T * 2 * s->hidden * sizeof(__half));
+    L.xs_x = (float *)take((size_t)T * sizeof(float));
+    L.xb_a = (__half *)take(TK * 2 * s->inter * sizeof(__half));
+    L.xs_a = (float *)take(TK * sizeof(float));
     L.total = off;
     return L;
 }
@@ -327,8 +311,10 @@ static int check_shape(const K3dMoeShape *s, int T)
     return K3D_OK;
 }
 
-static int g_last_unique_host = -1;
-static int *g_last_unique_dev = nullptr;
+// pinned host copy of the last call's active-expert count (copied asynchronously, so the
+// value survives the caller freeing its workspace)
+static int *g_last_unique_pinned = nullptr;
+static bool g_last_unique_valid = false;
 
 }  // namespace k3
 
@@ -338,8 +324,9 @@ extern "C" {
 
 size_t k3d_expert_ws_bytes(int hidden, int inter)
 {
-    (void)hidden;
-    return align256((size_t)inter * sizeof(float)) + 256;
+    return align256((size_t)inter * sizeof(float)) + align256((size_t)2 * hidden * sizeof(__half)) +
+           align256(sizeof(float)) + align256((size_t)2 * inter * sizeof(__half)) +
+           align256(sizeof(float)) + 256;
 }
 
 int k3d_expert_swiglu(float *y, const float *x, const K3ExpertQ *e, int hidden, int inter,
@@ -359,12 +346,20 @@ int k3d_expert_swiglu(float *y, const float *x, const K3ExpertQ *e, int hidden, 
     w.single_mode = 1;
     w.ntok_single = 1;
     w.K = 1;
-    float *act = (float *)ws;
+    char *b = (char *)ws;
+    float *act = (float *)b;
+    b += align256((size_t)inter * sizeof(float));
+    __half *xb_x = (__half *)b;
+    b += align256((size_t)2 * hidden * sizeof(__half));
+    float *xs_x = (float *)b;
+    b += align256(sizeof(float));
+    __half *xb_a = (__half *)b;
+    b += align256((size_t)2 * inter * sizeof(__half));
+    float *xs_a = (float *)b;
     cudaStream_t s = stream();
     prof_begin("expert.swiglu");
-    K3_TRY(launch_gate_up(act, x, w, hidden, inter, 1, s));
-    // contrib of the single assignment is y itself
-    K3_TRY(launch_down(y, act, w, hidden, inter, 1, s));
+    // the contribution of the single assignment is y itself
+    K3_TRY(run_experts(w, 1, x, 1, 1, hidden, inter, act, y, xb_x, xs_x, xb_a, xs_a, s));
     prof_end("expert.swiglu");
     return K3D_OK;
 }
@@ -422,8 +417,8 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     int umax = TK < (s->expert_hi - s->expert_lo) ? TK : (s->expert_hi - s->expert_lo);
     if (umax > 0) {
         prof_begin("moe.experts");
-        K3_TRY(launch_gate_up(L.act, x, mw, s->hidden, s->inter, umax, st));
-        K3_TRY(launch_down(L.contrib, L.act, mw, s->hidden, s->inter, umax, st));
+        K3_TRY(run_experts(mw, umax, x, T, TK, s->hidden, s->inter, L.act, L.contrib, L.xb_x,
+                           L.xs_x, L.xb_a, L.xs_a, st));
         prof_end("moe.experts");
     }
     dim3 grid((s->hidden + 255) / 256, T);
@@ -431,21 +426,26 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
                                         s->hidden, K, s->expert_lo, s->expert_hi, accumulate);
     note_launch();
     K3_TRY(check_launch("moe combine"));
-    g_last_unique_dev = L.n_active;
-    g_last_unique_host = -1;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs == cudaStreamCaptureStatusNone) {
+        if (!g_last_unique_pinned && cudaMallocHost(&g_last_unique_pinned, sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            g_last_unique_pinned = nullptr;
+        }
+        if (g_last_unique_pinned) {
+            cudaMemcpyAsync(g_last_unique_pinned, L.n_active, sizeof(int), cudaMemcpyDeviceToHost, st);
+            g_last_unique_valid = true;
+        }
+    }
     return K3D_OK;
 }
 
 int k3d_moe_last_unique(void)
 {
-    if (g_last_unique_dev && g_last_unique_host < 0) {
-        int v = -1;
-        if (cudaMemcpy(&v, g_last_unique_dev, sizeof v, cudaMemcpyDeviceToHost) == cudaSuccess)
-            g_last_unique_host = v;
-        else
-            cudaGetLastError();
-    }
-    return g_last_unique_host;
+    if (!g_last_unique_valid || !g_last_unique_pinned) return -1;
+    cudaStreamSynchronize(stream());
+    return *g_last_unique_pinned;
 }
 
 }  // extern "C"

@@ -5,6 +5,8 @@
 //   k3_matmul_mxfp4   follows k3_ops.c:1380-1785 (y = W x straight out of MXFP4,
 //                     scale 255 contributes nothing, odd `in` and group > 64 rejected).
 #include "k3_mxfp4.cuh"
+#include "k3_moe.cuh"
+#include "k3_ops.cuh"
 
 namespace k3 {
 
@@ -116,6 +118,21 @@ int mxfp4_gemv(float *y, const float *x, const unsigned char *packed,
                const unsigned char *scales, int in, int rows, int group, cudaStream_t s)
 {
     if (rows <= 0 || in <= 0) return K3D_OK;
+    // tensor-core path: 16-row tiles streamed by bulk copies (k3_mxfp4_mma.cu)
+    if (group == 32 && mma_supported(in, rows, 1) && aligned16(packed) && aligned16(scales)) {
+        char *ws = (char *)scratch((size_t)2 * in * sizeof(__half) + 256, 2);
+        if (!ws) return k3d_status();
+        __half *xb = (__half *)ws;
+        float *xs = (float *)(ws + (size_t)2 * in * sizeof(__half));
+        MoeWork w{};
+        w.single.p2 = packed;
+        w.single.s2 = scales;
+        w.single_mode = 1;
+        w.ntok_single = 1;
+        w.K = 1;
+        K3_TRY(xsplit(xb, xs, x, in, 1, in, s));
+        return mxfp4_mma_launch(1, w, 1, in, rows, xb, xs, 1, y, s);
+    }
     const bool fast = group == 32 && (in % 32) == 0 && aligned16(packed) && in <= 32 * 32 * 8;
     if (fast) {
         const int nch = in / 32;
@@ -130,28 +147,28 @@ int mxfp4_gemv(float *y, const float *x, const unsigned char *packed,
         if (nch <= 32) {
             static bool attr = false;
             if (!attr) {
-                cudaFuncSetAttribute(k_mxfp4_gemv_fast<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                allow_smem_max(k_mxfp4_gemv_fast<2, 1>);
                 attr = true;
             }
             k_mxfp4_gemv_fast<2, 1><<<grid, threads, smem, s>>>(y, x, packed, scales, in, rows, xa);
         } else if (nch <= 64) {
             static bool attr = false;
             if (!attr) {
-                cudaFuncSetAttribute(k_mxfp4_gemv_fast<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                allow_smem_max(k_mxfp4_gemv_fast<2, 2>);
                 attr = true;
             }
             k_mxfp4_gemv_fast<2, 2><<<grid, threads, smem, s>>>(y, x, packed, scales, in, rows, xa);
         } else if (nch <= 128) {
             static bool attr = false;
             if (!attr) {
-                cudaFuncSetAttribute(k_mxfp4_gemv_fast<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                allow_smem_max(k_mxfp4_gemv_fast<2, 4>);
                 attr = true;
             }
             k_mxfp4_gemv_fast<2, 4><<<grid, threads, smem, s>>>(y, x, packed, scales, in, rows, xa);
         } else {
             static bool attr = false;
             if (!attr) {
-                cudaFuncSetAttribute(k_mxfp4_gemv_fast<2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                allow_smem_max(k_mxfp4_gemv_fast<2, 8>);
                 attr = true;
             }
             k_mxfp4_gemv_fast<2, 8><<<grid, threads, smem, s>>>(y, x, packed, scales, in, rows, xa);

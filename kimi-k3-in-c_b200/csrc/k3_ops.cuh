@@ -16,9 +16,20 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
 int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint16_t *Wu,
                      int in, int inter, int T, cudaStream_t s);
 int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStream_t s);
+int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
+                    const float *x, int in, int T, cudaStream_t s);
+int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
+                     const uint16_t *W, int in, int out, int T, cudaStream_t s);
 // tagged weight: wdt 0 fp32, 1 bf16
 int gemv_tagged(float *y, const float *x, const void *W, int wdt, int in, int out,
                 cudaStream_t s);
+
+// k3_mxfp4_mma.cu
+struct MoeWork;
+bool mma_supported(int in, int rows, int mode);
+int xsplit(__half *xb, float *xsc, const float *x, int n, int nvec, size_t ld, cudaStream_t s);
+int mxfp4_mma_launch(int mode, const MoeWork &w, int umax, int in, int rows, const __half *xb,
+                     const float *xsc, int x_by_assign, float *out, cudaStream_t st);
 
 // k3_router.cu
 size_t router_ws_bytes(int T, int n_experts);

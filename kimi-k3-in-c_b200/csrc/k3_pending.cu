@@ -32,15 +32,5 @@ size_t k3_layer_scratch(const K3Cfg *c, int T) { PENDING("k3_layer_scratch"); re
 void k3_decoder_layer(float *h, float *br, int *nb, const K3LayerW *w, const K3Cfg *c, int li, int T, float *state, float *scratch) { PENDING("k3_decoder_layer"); }
 void k3_decoder_layer_inc(float *h, float *br, int *nb, const K3LayerW *w, const K3Cfg *c, int li, int T, float *state, float *scratch, float *kvc, float *ropec, int cached, int cap) { PENDING("k3_decoder_layer_inc"); }
 
-size_t k3d_mla_ws_bytes(const K3dMlaShape *s, int B, int cap) { PENDING("k3d_mla_ws_bytes"); return 0; }
-int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *s, int B, uint16_t *cache, int cap, const int *pos, int accumulate, void *ws, size_t ws_bytes) { return PENDING("k3d_mla_decode"); }
-K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed) { PENDING("k3d_model_create"); return nullptr; }
-void k3d_model_destroy(K3dModel *m) {}
-int k3d_model_fill_context(K3dModel *m, int len, uint64_t seed) { return PENDING("k3d_model_fill_context"); }
-int k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits) { return PENDING("k3d_model_step_dev"); }
-int k3d_model_step_host(K3dModel *m, const int *ids_host, int *next_host) { return PENDING("k3d_model_step_host"); }
-int k3d_model_use_graph(K3dModel *m, int on) { return PENDING("k3d_model_use_graph"); }
-void *k3d_model_tensor(K3dModel *m, const char *name, size_t *bytes) { return nullptr; }
-double k3d_model_last_step_bytes(K3dModel *m) { return 0.0; }
 
 }

@@ -1,0 +1,451 @@
+/* k3_stack.c -- the synthetic K3 decode stack (config 4), host side in C99.
+ *
+ * This is the B200 counterpart of the CPU engine's forward() (src/cli/k3_run.c:561-679):
+ * embed the token, run every decoder layer, final RMSNorm, LM head, argmax. Each layer is
+ * pre-norm residual (the benchmark lists no AttnRes weights): h += attention(norm(h));
+ * h += mlp(norm(h)), with KDA or MLA attention by the layer map and a dense SwiGLU MLP on
+ * the first_dense layers, the routed MoE elsewhere. All device work goes through the
+ * public C ABI of k3_cuda.h; the whole step is captured once into a CUDA graph and
+ * replayed, so a decode step is one graph launch.
+ *
+ * Weights are random-initialised on the device from a seed (the benchmark's synthetic
+ * random-init data). Under expert parallelism (k3d_ep_init with more than one rank) each
+ * rank allocates only the experts in cfg->moe.[expert_lo, expert_hi) and the step sums
+ * the per-rank MoE partials with one NCCL all-reduce per MoE layer.
+ */
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "k3_cuda.h"
+
+#define K3S_MAX_LAYERS 16
+#define K3S_MAX_TENSORS 4096
+
+typedef struct {
+    char name[64];
+    void *ptr;
+    size_t bytes;
+} K3sTensor;
+
+typedef struct {
+    int is_mla, is_dense;
+    float *in_norm, *post_norm;
+    /* KDA */
+    K3dKdaW kda;
+    K3dKdaShape kshape;
+    float *kda_state;              /* [B][state floats] */
+    /* MLA */
+    K3dMlaW mla;
+    uint16_t *cache;               /* [B][cap][kv_lora + rope] */
+    /* dense */
+    uint16_t *dg, *du, *dd;
+    /* MoE */
+    K3dMoeW moe;
+    K3ExpertQ *table;              /* device [n_experts] */
+    unsigned char *pool;           /* experts [lo, hi), 6 tensors each */
+} K3sLayer;
+
+struct K3dModel {
+    K3dStackCfg c;
+    K3sLayer L[K3S_MAX_LAYERS];
+    uint16_t *embed, *lm_head;
+    float *final_norm;
+    float *h, *xn, *mo;            /* [B][hidden] */
+    float *logits;                 /* [B][vocab] */
+    int *ids, *next, *pos;         /* device */
+    int *ids_host, *next_host;     /* pinned */
+    void *key;                     /* argmax keys */
+    float *mlp_ws;
+    void *ws;
+    size_t ws_bytes;
+    void *graph;
+    const int *g_ids;
+    int *g_next;
+    float *g_logits;
+    int use_graph, warmed;
+    uint64_t seed, counter;
+    double step_bytes;
+    K3sTensor t[K3S_MAX_TENSORS];
+    int nt;
+};
+
+static int is_mla_layer(const K3dStackCfg *c, int l)
+{
+    for (int i = 0; i < 16 && c->mla_layers[i] >= 0; i++)
+        if (c->mla_layers[i] == l) return 1;
+    return 0;
+}
+
+static void *reg(K3dModel *m, const char *name, void *p, size_t bytes)
+{
+    if (p && m->nt < K3S_MAX_TENSORS) {
+        K3sTensor *t = &m->t[m->nt++];
+        snprintf(t->name, sizeof t->name, "%s", name);
+        t->ptr = p;
+        t->bytes = bytes;
+    }
+    return p;
+}
+
+static void *dalloc(K3dModel *m, const char *name, size_t bytes)
+{
+    void *p = k3d_alloc(bytes);
+    return reg(m, name, p, bytes);
+}
+
+static uint64_t next_seed(K3dModel *m) { return m->seed * 1000003ull + (++m->counter) * 7919ull; }
+
+static uint16_t *bf16_param(K3dModel *m, const char *name, size_t n, float sd, int *err)
+{
+    uint16_t *p = (uint16_t *)dalloc(m, name, n * 2);
+    if (!p || k3d_fill_bf16_normal(p, n, next_seed(m), sd)) { *err = 1; return NULL; }
+    m->step_bytes += 0.0;  /* weights are counted when a step reads them */
+    return p;
+}
+
+static float *f32_uniform(K3dModel *m, const char *name, size_t n, float lo, float hi, int *err)
+{
+    float *p = (float *)dalloc(m, name, n * 4);
+    if (!p || k3d_fill_f32_uniform(p, n, next_seed(m), lo, hi)) { *err = 1; return NULL; }
+    return p;
+}
+
+static float *f32_normal(K3dModel *m, const char *name, size_t n, float sd, int *err)
+{
+    float *p = (float *)dalloc(m, name, n * 4);
+    if (!p || k3d_fill_f32_normal(p, n, next_seed(m), sd)) { *err = 1; return NULL; }
+    return p;
+}
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
+{
+    if (!cfg || cfg->n_layers < 1 || cfg->n_layers > K3S_MAX_LAYERS || cfg->batch < 1 ||
+        cfg->batch > 4 || cfg->ctx_cap < 1 || cfg->hidden < 1 || cfg->vocab < 1)
+        return NULL;
+    if (k3d_init(k3d_device() < 0 ? 0 : k3d_device())) return NULL;
+    K3dModel *m = (K3dModel *)calloc(1, sizeof(K3dModel));
+    if (!m) return NULL;
+    m->c = *cfg;
+    m->seed = seed;
+    m->use_graph = 1;
+    const K3dStackCfg *c = &m->c;
+    const int E = c->hidden, B = c->batch;
+    const size_t P = (size_t)c->kda_heads * c->kda_head_dim;
+    const int D = c->kda_head_dim, H = c->kda_heads;
+    int err = 0;
+    char nm[64];
+    size_t ws = 0;
+
+    m->embed = bf16_param(m, "embed", (size_t)c->vocab * E, 0.02f, &err);
+    m->lm_head = bf16_param(m, "lm_head", (size_t)c->vocab * E, 0.02f, &err);
+    m->final_norm = f32_uniform(m, "final_norm", E, 0.9f, 1.1f, &err);
+
+    for (int l = 0; l < c->n_layers && !err; l++) {
+        K3sLayer *L = &m->L[l];
+        L->is_mla = is_mla_layer(c, l);
+        L->is_dense = l < c->first_dense;
+        snprintf(nm, sizeof nm, "layer%d.in_norm", l);
+        L->in_norm = f32_uniform(m, nm, E, 0.9f, 1.1f, &err);
+        snprintf(nm, sizeof nm, "layer%d.post_norm", l);
+        L->post_norm = f32_uniform(m, nm, E, 0.9f, 1.1f, &err);
+        if (L->is_mla) {
+            const K3dMlaShape *s = &c->mla;
+            const int qh = s->qk_nope + s->qk_rope, kvw = s->kv_lora + s->qk_rope;
+            const int kvd = s->qk_nope + s->v_head;
+#define MLA_W(field, rows, cols) do { snprintf(nm, sizeof nm, "layer%d.mla." #field, l); \
+            L->mla.field = bf16_param(m, nm, (size_t)(rows) * (cols), 0.02f, &err); } while (0)
+            MLA_W(q_a, s->q_lora, E);
+            MLA_W(q_b, (size_t)s->n_heads * qh, s->q_lora);
+            MLA_W(kv_a, kvw, E);
+            MLA_W(kv_b, (size_t)s->n_heads * kvd, s->kv_lora);
+            MLA_W(o, E, (size_t)s->n_heads * s->v_head);
+            if (s->out_gate) MLA_W(g, (size_t)s->n_heads * s->v_head, E);
+#undef MLA_W
+            snprintf(nm, sizeof nm, "layer%d.mla.q_a_norm", l);
+            L->mla.q_a_norm = f32_uniform(m, nm, s->q_lora, 0.9f, 1.1f, &err);
+            snprintf(nm, sizeof nm, "layer%d.mla.kv_a_norm", l);
+            L->mla.kv_a_norm = f32_uniform(m, nm, s->kv_lora, 0.9f, 1.1f, &err);
+            snprintf(nm, sizeof nm, "layer%d.mla.cache", l);
+            L->cache = (uint16_t *)dalloc(m, nm, (size_t)B * c->ctx_cap * kvw * 2);
+            if (!L->cache || k3d_memset(L->cache, 0, (size_t)B * c->ctx_cap * kvw * 2)) err = 1;
+            const size_t w = k3d_mla_ws_bytes(&c->mla, B, c->ctx_cap);
+            if (w > ws) ws = w;
+        } else {
+            K3dKdaShape *ks = &L->kshape;
+            ks->hidden = E; ks->heads = H; ks->head_dim = D; ks->conv_k = c->conv_k;
+            ks->gate_lb = c->gate_lb; ks->eps = c->eps;
+#define KDA_W(field, rows, cols) do { snprintf(nm, sizeof nm, "layer%d.kda." #field, l); \
+            L->kda.field = bf16_param(m, nm, (size_t)(rows) * (cols), 0.02f, &err); } while (0)
+            KDA_W(q, P, E); KDA_W(k, P, E); KDA_W(v, P, E); KDA_W(g, P, E);
+            KDA_W(b, H, E); KDA_W(f_a, D, E); KDA_W(f_b, P, D); KDA_W(o, E, P);
+#undef KDA_W
+            snprintf(nm, sizeof nm, "layer%d.kda.q_conv", l);
+            L->kda.q_conv = f32_normal(m, nm, P * c->conv_k, 0.5f, &err);
+            snprintf(nm, sizeof nm, "layer%d.kda.k_conv", l);
+            L->kda.k_conv = f32_normal(m, nm, P * c->conv_k, 0.5f, &err);
+            snprintf(nm, sizeof nm, "layer%d.kda.v_conv", l);
+            L->kda.v_conv = f32_normal(m, nm, P * c->conv_k, 0.5f, &err);
+            snprintf(nm, sizeof nm, "layer%d.kda.A_log", l);
+            L->kda.A_log = f32_uniform(m, nm, H, 0.0f, 1.5f, &err);
+            snprintf(nm, sizeof nm, "layer%d.kda.dt_bias", l);
+            L->kda.dt_bias = f32_normal(m, nm, P, 0.5f, &err);
+            snprintf(nm, sizeof nm, "layer%d.kda.o_norm", l);
+            L->kda.o_norm = f32_uniform(m, nm, D, 0.9f, 1.1f, &err);
+            const size_t sf = k3d_kda_state_floats(ks);
+            snprintf(nm, sizeof nm, "layer%d.kda.state", l);
+            L->kda_state = (float *)dalloc(m, nm, (size_t)B * sf * 4);
+            if (!L->kda_state || k3d_memset(L->kda_state, 0, (size_t)B * sf * 4)) err = 1;
+            const size_t w = k3d_kda_layer_ws_bytes(ks, B);
+            if (w > ws) ws = w;
+        }
+        if (L->is_dense) {
+            snprintf(nm, sizeof nm, "layer%d.dense.gate", l);
+            L->dg = bf16_param(m, nm, (size_t)c->dense_inter * E, 0.02f, &err);
+            snprintf(nm, sizeof nm, "layer%d.dense.up", l);
+            L->du = bf16_param(m, nm, (size_t)c->dense_inter * E, 0.02f, &err);
+            snprintf(nm, sizeof nm, "layer%d.dense.down", l);
+            L->dd = bf16_param(m, nm, (size_t)E * c->dense_inter, 0.02f, &err);
+        } else {
+            const K3dMoeShape *s = &c->moe;
+            const size_t gu = (size_t)s->inter * E / 2, gus = (size_t)s->inter * E / 32;
+            const size_t sz[6] = {gu, gus, gu, gus, gu, gus};
+            size_t off[6], per = 0;
+            for (int i = 0; i < 6; i++) { off[i] = per; per += align256(sz[i]); }
+            const int nloc = s->expert_hi - s->expert_lo;
+            snprintf(nm, sizeof nm, "layer%d.moe.pool", l);
+            L->pool = (unsigned char *)dalloc(m, nm, (size_t)(nloc > 0 ? nloc : 1) * per);
+            K3ExpertQ *tab = (K3ExpertQ *)calloc((size_t)s->n_experts, sizeof(K3ExpertQ));
+            if (!L->pool || !tab) { err = 1; free(tab); break; }
+            for (int e = s->expert_lo; e < s->expert_hi && !err; e++) {
+                unsigned char *base = L->pool + (size_t)(e - s->expert_lo) * per;
+                tab[e].p1 = base + off[0]; tab[e].s1 = base + off[1];
+                tab[e].p3 = base + off[2]; tab[e].s3 = base + off[3];
+                tab[e].p2 = base + off[4]; tab[e].s2 = base + off[5];
+                for (int j = 0; j < 3; j++)
+                    if (k3d_fill_mxfp4(base + off[2 * j], sz[2 * j], base + off[2 * j + 1],
+                                       sz[2 * j + 1], next_seed(m) + (uint64_t)e, 117, 121))
+                        err = 1;
+            }
+            snprintf(nm, sizeof nm, "layer%d.moe.table", l);
+            L->table = (K3ExpertQ *)dalloc(m, nm, (size_t)s->n_experts * sizeof(K3ExpertQ));
+            if (!L->table || k3d_upload(L->table, tab, (size_t)s->n_experts * sizeof(K3ExpertQ)))
+                err = 1;
+            free(tab);
+            L->moe.experts = L->table;
+            snprintf(nm, sizeof nm, "layer%d.moe.router_w", l);
+            L->moe.router_w = bf16_param(m, nm, (size_t)s->n_experts * E, 0.02f, &err);
+            snprintf(nm, sizeof nm, "layer%d.moe.router_bias", l);
+            L->moe.router_bias = f32_uniform(m, nm, s->n_experts, -0.1f, 0.1f, &err);
+            if (s->shared_inter > 0) {
+                snprintf(nm, sizeof nm, "layer%d.moe.sh_gate", l);
+                L->moe.sh_gate = bf16_param(m, nm, (size_t)s->shared_inter * E, 0.02f, &err);
+                snprintf(nm, sizeof nm, "layer%d.moe.sh_up", l);
+                L->moe.sh_up = bf16_param(m, nm, (size_t)s->shared_inter * E, 0.02f, &err);
+                snprintf(nm, sizeof nm, "layer%d.moe.sh_down", l);
+                L->moe.sh_down = bf16_param(m, nm, (size_t)E * s->shared_inter, 0.02f, &err);
+            }
+            const size_t w = k3d_moe_ws_bytes(&c->moe, B);
+            if (w > ws) ws = w;
+        }
+    }
+    if (!err) {
+        m->h = (float *)dalloc(m, "h", (size_t)B * E * 4);
+        m->xn = (float *)dalloc(m, "xn", (size_t)B * E * 4);
+        m->mo = (float *)dalloc(m, "mo", (size_t)B * E * 4);
+        m->logits = (float *)dalloc(m, "logits", (size_t)B * c->vocab * 4);
+        m->ids = (int *)dalloc(m, "ids", (size_t)B * 4);
+        m->next = (int *)dalloc(m, "next", (size_t)B * 4);
+        m->pos = (int *)dalloc(m, "pos", 16);
+        m->key = dalloc(m, "argmax_key", (size_t)B * 8);
+        m->mlp_ws = (float *)dalloc(m, "mlp_ws", (size_t)B * (c->dense_inter > 0 ? c->dense_inter : 1) * 4);
+        m->ws_bytes = ws;
+        m->ws = dalloc(m, "ws", ws);
+        m->ids_host = (int *)k3d_host_alloc((size_t)B * 4);
+        m->next_host = (int *)k3d_host_alloc((size_t)B * 4);
+        if (!m->h || !m->xn || !m->mo || !m->logits || !m->ids || !m->next || !m->pos ||
+            !m->key || !m->mlp_ws || !m->ws || !m->ids_host || !m->next_host)
+            err = 1;
+        if (!err && k3d_memset(m->pos, 0, 16)) err = 1;
+        if (!err && k3d_sync()) err = 1;
+    }
+    if (err) {
+        k3d_model_destroy(m);
+        return NULL;
+    }
+    return m;
+}
+
+void k3d_model_destroy(K3dModel *m)
+{
+    if (!m) return;
+    if (m->graph) k3d_graph_destroy(m->graph);
+    for (int i = 0; i < m->nt; i++) k3d_free(m->t[i].ptr);
+    k3d_host_free(m->ids_host);
+    k3d_host_free(m->next_host);
+    free(m);
+}
+
+int k3d_model_fill_context(K3dModel *m, int len, uint64_t seed)
+{
+    if (!m || len < 0 || len >= m->c.ctx_cap) return K3D_EINVAL;
+    const K3dStackCfg *c = &m->c;
+    const int B = c->batch;
+    for (int l = 0; l < c->n_layers; l++) {
+        K3sLayer *L = &m->L[l];
+        if (L->is_mla) {
+            const int kvw = c->mla.kv_lora + c->mla.qk_rope;
+            for (int b = 0; b < B && len > 0; b++) {
+                int r = k3d_fill_bf16_normal(L->cache + (size_t)b * c->ctx_cap * kvw,
+                                             (size_t)len * kvw, seed * 131 + l * 17 + b, 1.0f);
+                if (r) return r;
+            }
+        } else {
+            const size_t sf = k3d_kda_state_floats(&L->kshape);
+            const size_t ns = (size_t)L->kshape.heads * L->kshape.head_dim * L->kshape.head_dim;
+            for (int b = 0; b < B; b++) {
+                int r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf, ns, seed * 137 + l * 19 + b, 0.01f);
+                if (!r) r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf + ns, sf - ns,
+                                                seed * 139 + l * 23 + b, 1.0f);
+                if (r) return r;
+            }
+        }
+    }
+    int p[4] = {len, len, len, len};
+    return k3d_upload(m->pos, p, sizeof p);
+}
+
+/* One decode step, launched eagerly on the library stream. */
+static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
+{
+    const K3dStackCfg *c = &m->c;
+    const int B = c->batch, E = c->hidden;
+    const int ep = k3d_ep_size() > 1;
+    int r;
+#define TRY(x) do { if ((r = (x)) != 0) return r; } while (0)
+    TRY(k3d_embed_bf16(m->h, ids, m->embed, B, E, c->vocab));
+    for (int l = 0; l < c->n_layers; l++) {
+        K3sLayer *L = &m->L[l];
+        TRY(k3d_rmsnorm(m->xn, m->h, L->in_norm, E, B, c->eps));
+        if (L->is_mla)
+            TRY(k3d_mla_decode(m->h, m->xn, &L->mla, &c->mla, B, L->cache, c->ctx_cap, m->pos, 1,
+                               m->ws, m->ws_bytes));
+        else
+            TRY(k3d_kda_layer_decode(m->h, m->xn, &L->kda, &L->kshape, B, L->kda_state, m->ws,
+                                     m->ws_bytes));
+        TRY(k3d_rmsnorm(m->xn, m->h, L->post_norm, E, B, c->eps));
+        if (L->is_dense) {
+            TRY(k3d_swiglu_mlp_bf16(m->h, m->xn, L->dg, L->du, L->dd, E, c->dense_inter, B, 1,
+                                    m->mlp_ws));
+        } else if (ep) {
+            TRY(k3d_moe_swiglu(m->mo, m->xn, &L->moe, &c->moe, B, 0, NULL, NULL, m->ws, m->ws_bytes));
+            TRY(k3d_ep_allreduce_f32(m->mo, (size_t)B * E));
+            TRY(k3d_add_f32(m->h, m->mo, (size_t)B * E));
+        } else {
+            TRY(k3d_moe_swiglu(m->h, m->xn, &L->moe, &c->moe, B, 1, NULL, NULL, m->ws, m->ws_bytes));
+        }
+    }
+    TRY(k3d_rmsnorm(m->xn, m->h, m->final_norm, E, B, c->eps));
+    TRY(k3d_lm_head_argmax(next, logits, m->xn, m->lm_head, c->vocab, E, B, m->key));
+    TRY(k3d_add_i32(m->pos, 1, 1));
+#undef TRY
+    return K3D_OK;
+}
+
+int k3d_model_use_graph(K3dModel *m, int on)
+{
+    if (!m) return K3D_EINVAL;
+    m->use_graph = on;
+    return K3D_OK;
+}
+
+int k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits)
+{
+    if (!m || !ids || !next_ids) return K3D_EINVAL;
+    if (!m->use_graph || !m->warmed) {
+        /* the first step runs eagerly: it initialises every kernel's attributes and
+         * lazily created buffers before anything is captured */
+        int r = step_eager(m, ids, next_ids, logits);
+        if (!r) m->warmed = 1;
+        return r;
+    }
+    if (!m->graph || m->g_ids != ids || m->g_next != next_ids || m->g_logits != logits) {
+        if (m->graph) { k3d_graph_destroy(m->graph); m->graph = NULL; }
+        int r = k3d_graph_begin();
+        if (r) return r;
+        r = step_eager(m, ids, next_ids, logits);
+        void *g = k3d_graph_end();
+        if (r) { k3d_graph_destroy(g); return r; }
+        if (!g) return k3d_status() ? k3d_status() : K3D_ECUDA;
+        m->graph = g;
+        m->g_ids = ids;
+        m->g_next = next_ids;
+        m->g_logits = logits;
+    }
+    return k3d_graph_launch(m->graph);
+}
+
+int k3d_model_step_host(K3dModel *m, const int *ids_host, int *next_host)
+{
+    if (!m || !ids_host || !next_host) return K3D_EINVAL;
+    const size_t n = (size_t)m->c.batch * sizeof(int);
+    memcpy(m->ids_host, ids_host, n);
+    int r = k3d_upload(m->ids, m->ids_host, n);
+    if (!r) r = k3d_model_step_dev(m, m->ids, m->next, m->logits);
+    if (!r) r = k3d_download(m->next_host, m->next, n);
+    if (!r) memcpy(next_host, m->next_host, n);
+    return r;
+}
+
+void *k3d_model_tensor(K3dModel *m, const char *name, size_t *bytes)
+{
+    if (!m || !name) return NULL;
+    for (int i = 0; i < m->nt; i++)
+        if (!strcmp(m->t[i].name, name)) {
+            if (bytes) *bytes = m->t[i].bytes;
+            return m->t[i].ptr;
+        }
+    return NULL;
+}
+
+/* Algorithmic HBM bytes of one step: every weight a token reads (routed experts counted
+ * for the unique experts of the last MoE call, shared expert, router), KDA states read
+ * and written, the MLA cache read over pos + 1 positions and one entry written. */
+double k3d_model_last_step_bytes(K3dModel *m)
+{
+    if (!m) return 0.0;
+    const K3dStackCfg *c = &m->c;
+    const double E = c->hidden, B = c->batch;
+    double bytes = 2.0 * c->vocab * E + 2.0 * B * E * 4;    /* lm_head + embed rows */
+    int pos = 0;
+    k3d_download(&pos, m->pos, sizeof pos);
+    const int U = k3d_moe_last_unique();
+    for (int l = 0; l < c->n_layers; l++) {
+        const K3sLayer *L = &m->L[l];
+        bytes += 2.0 * E * 4;                                /* norms */
+        if (L->is_mla) {
+            const K3dMlaShape *s = &c->mla;
+            const double qh = s->qk_nope + s->qk_rope, kvw = s->kv_lora + s->qk_rope;
+            bytes += 2.0 * (s->q_lora * E + s->n_heads * qh * s->q_lora + kvw * E +
+                            s->n_heads * (double)(s->qk_nope + s->v_head) * s->kv_lora +
+                            E * s->n_heads * s->v_head +
+                            (s->out_gate ? s->n_heads * (double)s->v_head * E : 0.0));
+            bytes += B * 2.0 * kvw * pos;                    /* cache read (pos positions) */
+        } else {
+            const double P = (double)c->kda_heads * c->kda_head_dim, D = c->kda_head_dim;
+            bytes += 2.0 * (4 * P * E + c->kda_heads * E + D * E + P * D + E * P);
+            bytes += B * 2.0 * 4.0 * k3d_kda_state_floats(&L->kshape);   /* read + write */
+        }
+        if (L->is_dense) {
+            bytes += 2.0 * 3.0 * c->dense_inter * E;
+        } else {
+            const K3dMoeShape *s = &c->moe;
+            const double per = 3.0 * (s->inter * E / 2.0 + s->inter * E / 32.0);
+            bytes += (U > 0 ? U : s->topk) * per;
+            bytes += 2.0 * s->n_experts * E + 2.0 * 3.0 * s->shared_inter * E;
+        }
+    }
+    return bytes;
+}

@@ -88,6 +88,17 @@ class K3dMlaW(C.Structure):
                 ("q_a_norm", vp), ("kv_a_norm", vp)]
 
 
+class K3dKdaShape(C.Structure):
+    _fields_ = [("hidden", i32), ("heads", i32), ("head_dim", i32), ("conv_k", i32),
+                ("gate_lb", f32), ("eps", f32)]
+
+
+class K3dKdaW(C.Structure):
+    _fields_ = [("q", vp), ("k", vp), ("v", vp), ("g", vp), ("b", vp), ("f_a", vp), ("f_b", vp),
+                ("o", vp), ("q_conv", vp), ("k_conv", vp), ("v_conv", vp), ("A_log", vp),
+                ("dt_bias", vp), ("o_norm", vp)]
+
+
 class K3dStackCfg(C.Structure):
     _fields_ = [("hidden", i32), ("vocab", i32), ("n_layers", i32), ("eps", f32),
                 ("kda_heads", i32), ("kda_head_dim", i32), ("conv_k", i32), ("gate_lb", f32),
@@ -187,6 +198,14 @@ _PROTOS = {
     "k3d_mla_decode": (i32, [vp, vp, C.POINTER(K3dMlaW), C.POINTER(K3dMlaShape), i32, vp, i32, vp,
                              i32, vp, sz]),
     "k3d_rmsnorm": (i32, [vp, vp, vp, i32, i32, f32]),
+    "k3d_embed_bf16": (i32, [vp, vp, vp, i32, i32, i32]),
+    "k3d_swiglu_mlp_bf16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "k3d_lm_head_argmax": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
+    "k3d_add_f32": (i32, [vp, vp, sz]),
+    "k3d_add_i32": (i32, [vp, i32, i32]),
+    "k3d_kda_layer_ws_bytes": (sz, [C.POINTER(K3dKdaShape), i32]),
+    "k3d_kda_state_floats": (sz, [C.POINTER(K3dKdaShape)]),
+    "k3d_kda_layer_decode": (i32, [vp, vp, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32, vp, vp, sz]),
     "k3d_silu_mul": (i32, [vp, vp, i32, i32]),
     # EP
     "k3d_ep_unique_id": (i32, [vp]),

@@ -652,3 +652,90 @@ void orc_kda_decode(float *S, float *o, const float *q, const float *k, const fl
                          alpha + bh * dk, beta[bh], dk, dv);
         }
 }
+
+/* RoPE on interleaved pairs (x[2i], x[2i+1]) with frequency theta^(-2i/d): the convention
+ * chosen for the benchmark (the reference is NoPE, k3.h:43-48). Angle in double. */
+void orc_rope(float *x, int d, int pos, float theta)
+{
+    if (!(theta > 0.0f)) return;   /* theta 0: NoPE, the reference's behaviour */
+    for (int i = 0; i < d / 2; i++) {
+        const double f = pow((double)theta, -2.0 * (double)i / (double)d);
+        const double a = (double)pos * f;
+        const float c = (float)cos(a), s = (float)sin(a);
+        const float x0 = x[2 * i], x1 = x[2 * i + 1];
+        x[2 * i] = x0 * c - x1 * s;
+        x[2 * i + 1] = x0 * s + x1 * c;
+    }
+}
+
+/* config 2: one decode token per sequence over a bf16 latent cache, k3_mla_cached's
+ * arithmetic (k3_ops.c:321-410) in the EXPANDED form: every cached latent is widened and
+ * re-projected through kv_b to per-head keys and values, then scored exactly as the
+ * reference scores its fp32 expanded cache. Differences from the reference: the rope slot
+ * is rotated (q per head, k at write time) and the cache holds bf16 latents. The new
+ * token's latent and rotated rope key are rounded to bf16 when written, and attention
+ * reads them back from the cache. cache [B][cap][kv_lora + rope]; positions [0, pos) are
+ * filled and the new token is written at pos. */
+void orc_mla_decode(float *out, const float *x, int B, int hidden, int H, int q_lora,
+                    int kv_lora, int qn, int qr, int vh, float theta, float eps,
+                    const uint16_t *q_a, const uint16_t *q_b, const uint16_t *kv_a,
+                    const uint16_t *kv_b, const uint16_t *o, const uint16_t *g,
+                    const float *q_a_norm, const float *kv_a_norm, uint16_t *cache, int cap,
+                    int pos)
+{
+    const int qh = qn + qr, kvw = kv_lora + qr, kvd = qn + vh;
+    const float scale = 1.0f / sqrtf((float)qh);
+    float *ql = (float *)xmalloc((size_t)q_lora * sizeof(float));
+    float *q = (float *)xmalloc((size_t)H * qh * sizeof(float));
+    float *c = (float *)xmalloc((size_t)kvw * sizeof(float));
+    float *cl = (float *)xmalloc((size_t)kv_lora * sizeof(float));
+    float *kv = (float *)xmalloc((size_t)(pos + 1) * H * kvd * sizeof(float));
+    float *kr = (float *)xmalloc((size_t)(pos + 1) * qr * sizeof(float));
+    float *sc = (float *)xmalloc((size_t)(pos + 1) * sizeof(float));
+    float *acc = (float *)xmalloc((size_t)H * vh * sizeof(float));
+    float *gb = (float *)xmalloc((size_t)H * vh * sizeof(float));
+    for (int b = 0; b < B; b++) {
+        const float *xb = x + (size_t)b * hidden;
+        uint16_t *cb = cache + (size_t)b * cap * kvw;
+        orc_matmul_bf16(ql, xb, q_a, hidden, q_lora);
+        orc_rmsnorm(ql, ql, q_a_norm, q_lora, eps);
+        orc_matmul_bf16(q, ql, q_b, q_lora, H * qh);
+        for (int h = 0; h < H; h++) orc_rope(q + (size_t)h * qh + qn, qr, pos, theta);
+        orc_matmul_bf16(c, xb, kv_a, hidden, kvw);
+        orc_rmsnorm(c, c, kv_a_norm, kv_lora, eps);
+        orc_rope(c + kv_lora, qr, pos, theta);
+        for (int i = 0; i < kvw; i++) cb[(size_t)pos * kvw + i] = orc_f2bf(c[i]);
+        for (int s = 0; s <= pos; s++) {
+            for (int i = 0; i < kv_lora; i++) cl[i] = orc_bf16f(cb[(size_t)s * kvw + i]);
+            for (int i = 0; i < qr; i++) kr[(size_t)s * qr + i] = orc_bf16f(cb[(size_t)s * kvw + kv_lora + i]);
+            orc_matmul_bf16(kv + (size_t)s * H * kvd, cl, kv_b, kv_lora, H * kvd);
+        }
+        for (int h = 0; h < H; h++) {
+            const float *qt = q + (size_t)h * qh;
+            float m = -INFINITY;
+            for (int s = 0; s <= pos; s++) {
+                const float *ks = kv + ((size_t)s * H + h) * kvd;
+                double d = 0.0;
+                for (int i = 0; i < qn; i++) d += (double)qt[i] * (double)ks[i];
+                for (int i = 0; i < qr; i++) d += (double)qt[qn + i] * (double)kr[(size_t)s * qr + i];
+                sc[s] = (float)d * scale;
+                if (sc[s] > m) m = sc[s];
+            }
+            double z = 0.0;
+            for (int s = 0; s <= pos; s++) { sc[s] = expf(sc[s] - m); z += sc[s]; }
+            float *oh = acc + (size_t)h * vh;
+            for (int j = 0; j < vh; j++) oh[j] = 0.0f;
+            for (int s = 0; s <= pos; s++) {
+                const float pr = (float)(sc[s] / z);
+                const float *vs = kv + ((size_t)s * H + h) * kvd + qn;
+                for (int j = 0; j < vh; j++) oh[j] += pr * vs[j];
+            }
+        }
+        if (g) {
+            orc_matmul_bf16(gb, xb, g, hidden, H * vh);
+            for (int i = 0; i < H * vh; i++) acc[i] *= 1.0f / (1.0f + expf(-gb[i]));
+        }
+        orc_matmul_bf16(out + (size_t)b * hidden, acc, o, H * vh, hidden);
+    }
+    free(ql); free(q); free(c); free(cl); free(kv); free(kr); free(sc); free(acc); free(gb);
+}

@@ -82,6 +82,15 @@ void  orc_moe_swiglu(float *out, const float *x, int T, int hidden, int inter,
                      const uint16_t *sh_up, const uint16_t *sh_down,
                      int expert_lo, int expert_hi, int add_shared, int *idx_out,
                      float *w_out);
+/* RoPE on interleaved pairs, frequency theta^(-2i/d) */
+void  orc_rope(float *x, int d, int pos, float theta);
+/* config 2: MLA decode over a bf16 latent cache, expanded form (see the .c file) */
+void  orc_mla_decode(float *out, const float *x, int B, int hidden, int H, int q_lora,
+                     int kv_lora, int qn, int qr, int vh, float theta, float eps,
+                     const uint16_t *q_a, const uint16_t *q_b, const uint16_t *kv_a,
+                     const uint16_t *kv_b, const uint16_t *o, const uint16_t *g,
+                     const float *q_a_norm, const float *kv_a_norm, uint16_t *cache, int cap,
+                     int pos);
 /* config 3: B*H heads of k3_kda_step */
 void  orc_kda_decode(float *S, float *o, const float *q, const float *k, const float *v,
                      const float *alpha, const float *beta, int B, int H, int dk, int dv);

@@ -162,6 +162,9 @@ class Oracle(_Common):
         L.orc_moe_swiglu.restype = None
         L.orc_kda_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]
         L.orc_kda_decode.restype = None
+        L.orc_mla_decode.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, f32,
+                                     vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32]
+        L.orc_mla_decode.restype = None
 
     def expert_swiglu(self, x, e, hidden, inter):
         """e: dict with numpy arrays p1,s1,p3,s3,p2,s2."""
@@ -219,3 +222,116 @@ class Reference(_Common):
             raise FileNotFoundError(REF_SO)
         self.lib = C.CDLL(REF_SO)
         _declare(self.lib, "k3_")
+
+
+def mla_decode(orc, x, dims, w, cache, pos):
+    """config-2 oracle: x [B][hidden]; dims dict; w dict of numpy weights (bf16 as uint16,
+    norms fp32); cache [B][cap][kvw] uint16, updated in place at `pos`."""
+    B = x.shape[0]
+    out = np.empty((B, dims["hidden"]), np.float32)
+    orc.lib.orc_mla_decode(ptr(out), ptr(np.ascontiguousarray(x, np.float32)), B, dims["hidden"],
+                           dims["H"], dims["q_lora"], dims["kv_lora"], dims["qn"], dims["qr"],
+                           dims["vh"], dims["theta"], dims["eps"], ptr(w["q_a"]), ptr(w["q_b"]),
+                           ptr(w["kv_a"]), ptr(w["kv_b"]), ptr(w["o"]), ptr(w.get("g")),
+                           ptr(w["q_a_norm"]), ptr(w["kv_a_norm"]), ptr(cache), cache.shape[1], pos)
+    return out
+
+
+# ------------------------------------------------------------- decode stack (config 4)
+class K3Cfg(C.Structure):
+    _fields_ = [
+        ("hidden", i32), ("n_layers", i32), ("vocab", i32), ("rms_eps", f32),
+        ("kda_heads", i32), ("kda_head_dim", i32), ("conv_k", i32), ("gate_lb", f32),
+        ("n_heads", i32), ("q_lora", i32), ("kv_lora", i32), ("qk_nope", i32),
+        ("qk_rope", i32), ("v_head", i32), ("mla_out_gate", i32),
+        ("n_experts", i32), ("topk", i32), ("n_shared", i32), ("latent", i32),
+        ("moe_inter", i32), ("routed_scale", f32), ("moe_renorm", i32), ("latent_norm", i32),
+        ("first_dense", i32), ("dense_inter", i32), ("attn_res_block", i32),
+        ("situ_b1", f32), ("situ_b2", f32), ("n_full_attn", i32), ("full_attn", C.POINTER(i32)),
+    ]
+
+
+class K3KdaW(C.Structure):
+    _fields_ = [("q", vp), ("k", vp), ("v", vp), ("q_conv", vp), ("k_conv", vp),
+                ("v_conv", vp), ("f_a", vp), ("f_b", vp), ("A_log", vp), ("dt_bias", vp),
+                ("b", vp), ("g", vp), ("o_norm", vp), ("o", vp), ("wdt", i32)]
+
+
+def kda_layer(orc, x, w, hidden, H, D, conv_k, gate_lb, eps, state):
+    """k3_kda_layer (T = 1) with bf16 weights on host copies; state updated in place."""
+    L = orc.lib
+    L.orc_kda_layer.argtypes = [vp, vp, C.POINTER(K3KdaW), C.POINTER(K3Cfg), i32, vp, vp]
+    L.orc_kda_layer.restype = None
+    L.orc_kda_scratch.argtypes = [C.POINTER(K3Cfg), i32]
+    L.orc_kda_scratch.restype = C.c_size_t
+    cfg = K3Cfg(hidden=hidden, kda_heads=H, kda_head_dim=D, conv_k=conv_k, gate_lb=gate_lb,
+                rms_eps=eps)
+    kw = K3KdaW(*(w[k].ctypes.data for k in ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a",
+                                               "f_b", "A_log", "dt_bias", "b", "g", "o_norm", "o")),
+                1)
+    scratch = np.empty(L.orc_kda_scratch(C.byref(cfg), 1), np.float32)
+    out = np.empty(hidden, np.float32)
+    L.orc_kda_layer(ptr(out), ptr(np.ascontiguousarray(x, np.float32)), C.byref(kw), C.byref(cfg), 1,
+                    ptr(state), ptr(scratch))
+    return out
+
+
+def silu_mul(g, u):
+    g = g.astype(np.float32)
+    return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32) * u.astype(np.float32)
+
+
+def stack_step(orc, cfg, W, S, token):
+    """One decode step of the synthetic stack on host copies. cfg: dict; W: weights by
+    name (numpy); S: mutable state {"pos", "layer<l>.kda.state", "layer<l>.mla.cache"}.
+    Returns logits (float32 [vocab])."""
+    E = cfg["hidden"]
+    h = (W["embed"].reshape(cfg["vocab"], E)[token].astype(np.uint32) << 16).view(np.float32).copy()
+    for l in range(cfg["n_layers"]):
+        p = f"layer{l}."
+        xn = orc.rmsnorm(h, W[p + "in_norm"], cfg["eps"])
+        if l in cfg["mla_layers"]:
+            m = cfg["mla"]
+            w = {k: W[p + "mla." + k] for k in ("q_a", "q_b", "kv_a", "kv_b", "o", "g",
+                                                 "q_a_norm", "kv_a_norm")}
+            cache = S[p + "mla.cache"]
+            out = mla_decode(orc, xn[None], m, w, cache, S["pos"])[0]
+        else:
+            w = {k: W[p + "kda." + k] for k in ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a",
+                                                 "f_b", "A_log", "dt_bias", "b", "g", "o_norm", "o")}
+            out = kda_layer(orc, xn, w, E, cfg["kda_heads"], cfg["kda_head_dim"], cfg["conv_k"],
+                            cfg["gate_lb"], cfg["eps"], S[p + "kda.state"])
+        h = (h + out).astype(np.float32)
+        xn = orc.rmsnorm(h, W[p + "post_norm"], cfg["eps"])
+        if l < cfg["first_dense"]:
+            a = silu_mul(orc.matmul_bf16(xn, W[p + "dense.gate"]), orc.matmul_bf16(xn, W[p + "dense.up"]))
+            out = orc.matmul_bf16(a, W[p + "dense.down"])
+        else:
+            mo = cfg["moe"]
+            out, _, _ = orc.moe_swiglu(xn[None], 1, E, mo["inter"], mo["n_experts"], mo["topk"], 1,
+                                       mo["routed_scale"], W[p + "moe.router_w"],
+                                       W[p + "moe.router_bias"], W[p + "moe.experts"],
+                                       mo["shared_inter"], W[p + "moe.sh_gate"], W[p + "moe.sh_up"],
+                                       W[p + "moe.sh_down"])
+            out = out[0]
+        h = (h + out).astype(np.float32)
+    xn = orc.rmsnorm(h, W["final_norm"], cfg["eps"])
+    logits = orc.matmul_bf16(xn, W["lm_head"])
+    S["pos"] += 1
+    return logits
+
+
+class K3MlaW(C.Structure):
+    _fields_ = [("q_a", vp), ("q_b", vp), ("kv_a", vp), ("kv_b", vp), ("o", vp), ("g", vp),
+                ("q_a_norm", vp), ("kv_a_norm", vp), ("wdt", i32)]
+
+
+def ref_kda_layer_fn(lib):
+    lib.k3_kda_layer.argtypes = [vp, vp, C.POINTER(K3KdaW), C.POINTER(K3Cfg), i32, vp, vp]
+    lib.k3_kda_layer.restype = None
+    lib.k3_kda_scratch.argtypes = [C.POINTER(K3Cfg), i32]
+    lib.k3_kda_scratch.restype = C.c_size_t
+    lib.k3_mla_cached.argtypes = [vp, vp, C.POINTER(K3MlaW), C.POINTER(K3Cfg), i32, vp, vp, vp, i32, i32]
+    lib.k3_mla_cached.restype = None
+    lib.k3_mla_scratch_cached.argtypes = [C.POINTER(K3Cfg), i32, i32, i32]
+    lib.k3_mla_scratch_cached.restype = C.c_size_t

@@ -10,7 +10,7 @@ import synth
 pytestmark = pytest.mark.gpu
 
 
-def small_layer(seed, hidden=1024, inter=256, E=64, topk=8, shared_inter=256):
+def small_layer(seed, hidden=1024, inter=512, E=64, topk=8, shared_inter=256):
     g = synth.rng(seed)
     experts = [synth.mxfp4_expert(g, hidden, inter) for _ in range(E)]
     W = synth.bf16_normal(g, (E, hidden), 0.02)
@@ -37,10 +37,11 @@ def run_layer(k3, mw, x, T, accumulate_into=None):
             Wt.download(np.float32, (T, mw.shape.topk)))
 
 
-@pytest.mark.parametrize("T", [1, 8, 64, 512])
-def test_moe_layer_matches_oracle(k3, oracle, T):
-    g, experts, W, bias, sh = small_layer(100 + T)
-    hidden, inter, E = 1024, 256, 64
+@pytest.mark.parametrize("T,inter", [(1, 512), (8, 512), (64, 512), (512, 512), (8, 256)])
+def test_moe_layer_matches_oracle(k3, oracle, T, inter):
+    """inter 512 runs the tensor-core expert kernels, inter 256 the CUDA-core ones."""
+    g, experts, W, bias, sh = small_layer(100 + T, inter=inter)
+    hidden, E = 1024, 64
     mw = k3cuda.MoeWeights(hidden, inter, E, 8, W, bias, shared=sh, experts=experts)
     x = synth.bf16_to_f32(synth.bf16_normal(g, (T, hidden), 1.0))
     y, idx, wts = run_layer(k3, mw, x, T)
@@ -56,7 +57,7 @@ def test_moe_residual_accumulate_and_expert_parallel_partials(k3, oracle):
     whole layer, and accumulate=1 adds onto the residual."""
     T = 8
     g, experts, W, bias, sh = small_layer(7)
-    hidden, inter, E = 1024, 256, 64
+    hidden, inter, E = 1024, 512, 64
     x = synth.bf16_to_f32(synth.bf16_normal(g, (T, hidden), 1.0))
     resid = g.standard_normal((T, hidden), dtype=np.float32)
     parts = []

@@ -39,7 +39,8 @@ def test_dequant_bit_exact_device_pointers_all_scale_bytes(k3, oracle):
 
 
 @pytest.mark.parametrize("rows,cols,group", [(64, 3584, 32), (2048, 7168, 32), (7168, 2048, 32),
-                                             (33, 96, 32), (17, 50, 25), (9, 64, 64), (5, 30, 7)])
+                                             (40, 1024, 32), (33, 96, 32), (17, 50, 25),
+                                             (9, 64, 64), (5, 30, 7)])
 def test_matmul_mxfp4_matches_oracle(k3, oracle, rows, cols, group):
     g = synth.rng(rows * 7 + cols)
     packed = g.integers(0, 256, (rows, cols // 2), dtype=np.uint8)

@@ -1,0 +1,131 @@
+"""Config 4 at reduced width: the 8-layer decode stack (KDA x6, MLA x2 at one-based layers 4
+and 8, dense layer 0, MoE layers 1-7), graph-captured, against the oracle composed from the
+reference routines, step by step from the same synthetic weights and context."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import k3cuda
+from conftest import max_rel_err
+import oracle as orc_mod
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(hidden=512, vocab=1024, n_layers=8, eps=1e-6, kda_heads=4, kda_head_dim=64, conv_k=4,
+           gate_lb=-5.0, first_dense=1, dense_inter=1024, mla_layers=[3, 7],
+           mla=dict(hidden=512, H=8, q_lora=128, kv_lora=64, qn=32, qr=16, vh=32, theta=50000.0,
+                    eps=1e-6),
+           moe=dict(inter=512, n_experts=16, topk=4, routed_scale=2.5, shared_inter=256))
+
+
+def make_cfg(c, batch=1, cap=64):
+    m, mo = c["mla"], c["moe"]
+    sc = k3cuda.K3dStackCfg()
+    sc.hidden, sc.vocab, sc.n_layers, sc.eps = c["hidden"], c["vocab"], c["n_layers"], c["eps"]
+    sc.kda_heads, sc.kda_head_dim, sc.conv_k, sc.gate_lb = (c["kda_heads"], c["kda_head_dim"],
+                                                            c["conv_k"], c["gate_lb"])
+    sc.mla = k3cuda.K3dMlaShape(m["hidden"], m["H"], m["q_lora"], m["kv_lora"], m["qn"], m["qr"],
+                                m["vh"], m["theta"], m["eps"], 1)
+    sc.moe = k3cuda.K3dMoeShape(c["hidden"], mo["inter"], mo["n_experts"], mo["topk"], 1,
+                                mo["routed_scale"], mo["shared_inter"], 0, mo["n_experts"], 1)
+    sc.first_dense, sc.dense_inter = c["first_dense"], c["dense_inter"]
+    for i in range(16):
+        sc.mla_layers[i] = c["mla_layers"][i] if i < len(c["mla_layers"]) else -1
+    sc.batch, sc.ctx_cap = batch, cap
+    return sc
+
+
+def download(k3, model, name, dtype, shape=None):
+    n = ctypes.c_size_t()
+    p = k3.k3d_model_tensor(model, name.encode(), ctypes.byref(n))
+    assert p, name
+    a = np.empty(n.value // np.dtype(dtype).itemsize, dtype)
+    k3cuda.check(k3.k3d_download(a.ctypes.data, p, a.nbytes))
+    return a.reshape(shape) if shape else a
+
+
+def host_copy(k3, model, c):
+    E, P, D, H = c["hidden"], c["kda_heads"] * c["kda_head_dim"], c["kda_head_dim"], c["kda_heads"]
+    m, mo = c["mla"], c["moe"]
+    W, S = {}, {}
+    W["embed"] = download(k3, model, "embed", np.uint16)
+    W["lm_head"] = download(k3, model, "lm_head", np.uint16, (c["vocab"], E))
+    W["final_norm"] = download(k3, model, "final_norm", np.float32)
+    for l in range(c["n_layers"]):
+        p = f"layer{l}."
+        W[p + "in_norm"] = download(k3, model, p + "in_norm", np.float32)
+        W[p + "post_norm"] = download(k3, model, p + "post_norm", np.float32)
+        if l in c["mla_layers"]:
+            qh, kvw, kvd = m["qn"] + m["qr"], m["kv_lora"] + m["qr"], m["qn"] + m["vh"]
+            shapes = {"q_a": (m["q_lora"], E), "q_b": (m["H"] * qh, m["q_lora"]), "kv_a": (kvw, E),
+                      "kv_b": (m["H"] * kvd, m["kv_lora"]), "o": (E, m["H"] * m["vh"]),
+                      "g": (m["H"] * m["vh"], E)}
+            for k, shp in shapes.items():
+                W[p + "mla." + k] = download(k3, model, p + "mla." + k, np.uint16, shp)
+            for k in ("q_a_norm", "kv_a_norm"):
+                W[p + "mla." + k] = download(k3, model, p + "mla." + k, np.float32)
+            S[p + "mla.cache"] = download(k3, model, p + "mla.cache", np.uint16, (1, 64, kvw))
+        else:
+            shapes = {"q": (P, E), "k": (P, E), "v": (P, E), "g": (P, E), "b": (H, E), "f_a": (D, E),
+                      "f_b": (P, D), "o": (E, P)}
+            for k, shp in shapes.items():
+                W[p + "kda." + k] = download(k3, model, p + "kda." + k, np.uint16, shp)
+            for k in ("q_conv", "k_conv", "v_conv", "A_log", "dt_bias", "o_norm"):
+                W[p + "kda." + k] = download(k3, model, p + "kda." + k, np.float32)
+            S[p + "kda.state"] = download(k3, model, p + "kda.state", np.float32)
+        if l < c["first_dense"]:
+            W[p + "dense.gate"] = download(k3, model, p + "dense.gate", np.uint16, (c["dense_inter"], E))
+            W[p + "dense.up"] = download(k3, model, p + "dense.up", np.uint16, (c["dense_inter"], E))
+            W[p + "dense.down"] = download(k3, model, p + "dense.down", np.uint16, (E, c["dense_inter"]))
+        else:
+            W[p + "moe.router_w"] = download(k3, model, p + "moe.router_w", np.uint16,
+                                             (mo["n_experts"], E))
+            W[p + "moe.router_bias"] = download(k3, model, p + "moe.router_bias", np.float32)
+            for k, shp in (("sh_gate", (mo["shared_inter"], E)), ("sh_up", (mo["shared_inter"], E)),
+                           ("sh_down", (E, mo["shared_inter"]))):
+                W[p + "moe." + k] = download(k3, model, p + "moe." + k, np.uint16, shp)
+            pool = download(k3, model, p + "moe.pool", np.uint8)
+            gu, gus = mo["inter"] * E // 2, mo["inter"] * E // 32
+            sizes = [gu, gus, gu, gus, gu, gus]
+            offs, o = [], 0
+            for s_ in sizes:
+                offs.append(o)
+                o += (s_ + 255) // 256 * 256
+            experts = []
+            for e in range(mo["n_experts"]):
+                base = e * o
+                d = {}
+                for key, off, s_ in zip(("p1", "s1", "p3", "s3", "p2", "s2"), offs, sizes):
+                    d[key] = np.ascontiguousarray(pool[base + off: base + off + s_])
+                experts.append(d)
+            W[p + "moe.experts"] = experts
+    S["pos"] = int(download(k3, model, "pos", np.int32)[0])
+    return W, S
+
+
+def test_stack_decode_matches_oracle_eager_and_graph(k3, oracle):
+    c = CFG
+    model = k3.k3d_model_create(ctypes.byref(make_cfg(c)), 1234)
+    assert model, k3.k3d_last_message()
+    try:
+        k3cuda.check(k3.k3d_model_fill_context(model, 5, 99))
+        k3cuda.check(k3.k3d_sync())
+        W, S = host_copy(k3, model, c)
+        assert S["pos"] == 5
+        tok = 17
+        for step in range(4):          # step 0 eager, step 1 captures the graph, 2-3 replay
+            ids = np.array([tok], np.int32)
+            nxt = np.zeros(1, np.int32)
+            k3cuda.check(k3.k3d_model_step_host(model, ids.ctypes.data, nxt.ctypes.data), f"step {step}")
+            got = download(k3, model, "logits", np.float32)
+            want = orc_mod.stack_step(oracle, c, W, S, tok)
+            err = max_rel_err(got, want)
+            assert err <= 1e-3, (step, err)
+            top2 = np.sort(want)[-2:]
+            if top2[1] - top2[0] > 1e-3 * np.abs(want).max():
+                assert nxt[0] == int(np.argmax(want)), step
+            tok = int(nxt[0])
+        assert int(download(k3, model, "pos", np.int32)[0]) == 9
+    finally:
+        k3.k3d_model_destroy(model)
