@@ -161,8 +161,12 @@ int    k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoe
 int    k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W,
                        const float *bias, int T, int hidden, int n_experts, int topk,
                        int renorm, float routed_scale);
-/* Number of distinct experts routed to by the last k3d_moe_swiglu call (host copy made
- * on k3d_sync(); -1 if unknown). Used for the algorithmic-bytes numerator. */
+/* Experts (summed over all router calls in this process) whose fp32 logit could not be
+ * settled from the exact dot product and its error bound, and were recomputed with the
+ * CPU engine's sequential double loop. Diagnostic; results are bit-exact either way. */
+long long k3d_router_fallbacks(void);
+/* Number of distinct experts routed to by the last eagerly launched k3d_moe_swiglu call
+ * (synchronises the stream; -1 before the first call). Used for the bytes numerator. */
 int    k3d_moe_last_unique(void);
 
 /* --------------------------------------------------------------- GEMV ---- */

@@ -46,7 +46,12 @@ struct Stage {
     int n_out = 0;
     bool any_host = false;
     int err = 0;
-    size_t arena_used = 0;
+    // Stages nest (an operator may stage per-call expert bytes while its caller's
+    // arguments are staged): each takes arena space above the enclosing one and gives it
+    // back when it goes out of scope.
+    size_t base = 0;
+    Stage();
+    ~Stage();
     // device pointer usable by kernels for a read-only model tensor
     const void *weight(const void *p, size_t bytes);
     // input activations / state read by the call

@@ -38,6 +38,7 @@ struct Ctx {
     size_t scratch_bytes[4] = {0, 0, 0, 0};
     void *arena = nullptr;
     size_t arena_bytes = 0;
+    size_t arena_top = 0;
     cudaGraph_t capturing = nullptr;
     bool prof = false;
     struct Sec { std::vector<std::pair<cudaEvent_t, cudaEvent_t>> done; cudaEvent_t open = nullptr;
@@ -189,14 +190,16 @@ void *scratch(size_t bytes, int slot)
 }
 
 // ------------------------------------------------------------------- staging ----
+Stage::Stage() { base = g.arena_top; }
+Stage::~Stage() { g.arena_top = base; }
+
 void *Stage::arena(size_t bytes)
 {
-    size_t off = (arena_used + 255) & ~(size_t)255;
+    size_t off = (g.arena_top + 255) & ~(size_t)255;
     size_t need = off + bytes;
     if (need > g.arena_bytes) {
-        // Grow only when nothing staged is live in this call; earlier pointers of the
-        // same call must stay valid, so grow to a generous size up front.
-        if (arena_used != 0) {
+        // Grow only when nothing staged is live; earlier pointers must stay valid.
+        if (g.arena_top != 0) {
             err = fail(K3D_ENOMEM, "staging arena exhausted mid-call (%zu bytes)", need);
             return nullptr;
         }
@@ -210,7 +213,7 @@ void *Stage::arena(size_t bytes)
         }
         g.arena_bytes = want;
     }
-    arena_used = need;
+    g.arena_top = need;
     return (char *)g.arena + off;
 }
 

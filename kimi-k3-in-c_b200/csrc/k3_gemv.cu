@@ -264,10 +264,12 @@ __global__ void k_argmax_finish(int *next, const unsigned long long *key, int T)
 static bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 int grid_for(int rows, int rows_per_cta);
-int grid_for(int rows, int rows_per_cta)
+// CTAs for `rows` rows when one pass of a CTA covers rows_per_pass rows: one pass per CTA
+// up to 8 CTAs per SM, grid-striding beyond that.
+int grid_for(int rows, int rows_per_pass)
 {
-    int grid = (rows + rows_per_cta - 1) / rows_per_cta;
-    const int cap = sm_count() * 4;
+    int grid = (rows + rows_per_pass - 1) / rows_per_pass;
+    const int cap = sm_count() * 8;
     if (grid > cap) grid = cap;
     return grid < 1 ? 1 : grid;
 }
@@ -295,10 +297,10 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
         const int nt = min(4, T - t0);
         const size_t smem = (size_t)nt * in * sizeof(float);
         if (nt == 1)
-            k_gemv_bf16<2, 7, 1><<<grid_for(out, 64), 256, smem, s>>>(
+            k_gemv_bf16<2, 7, 1><<<grid_for(out, 16), 256, smem, s>>>(
                 y + (size_t)t0 * out, x + (size_t)t0 * in, W, in, out, 1, accumulate);
         else
-            k_gemv_bf16<2, 7, 4><<<grid_for(out, 64), 256, smem, s>>>(
+            k_gemv_bf16<2, 7, 4><<<grid_for(out, 16), 256, smem, s>>>(
                 y + (size_t)t0 * out, x + (size_t)t0 * in, W, in, out, nt, accumulate);
         note_launch();
     }
@@ -316,7 +318,7 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
     for (int t0 = 0; t0 < T; t0 += 4) {
         const int nt = min(4, T - t0);
         const size_t smem = (size_t)nt * in * sizeof(float);
-        k_gemv_bf16_swiglu<7><<<grid_for(inter, 32), 256, smem, s>>>(
+        k_gemv_bf16_swiglu<7><<<grid_for(inter, 8), 256, smem, s>>>(
             act + (size_t)t0 * inter, x + (size_t)t0 * in, Wg, Wu, in, inter, nt);
         note_launch();
     }
@@ -342,7 +344,7 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
         return fail(K3D_EINVAL, "multi-segment GEMV: in=%d", in);
     static bool init = false;
     if (!init) { allow_smem(k_gemv_bf16_multi<2, 7>); init = true; }
-    k_gemv_bf16_multi<2, 7><<<grid_for(S.start[nseg], 64), 256, (size_t)T * in * 4, s>>>(S, x, in, T);
+    k_gemv_bf16_multi<2, 7><<<grid_for(S.start[nseg], 16), 256, (size_t)T * in * 4, s>>>(S, x, in, T);
     note_launch();
     return check_launch("gemv bf16 multi");
 }
@@ -356,10 +358,17 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
     if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
                ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
-    k_gemv_bf16_argmax<2, 7><<<grid_for(out, 64), 256, (size_t)T * in * 4, s>>>(y, key, x, W, in, out, T);
+    k_gemv_bf16_argmax<2, 7><<<grid_for(out, 16), 256, (size_t)T * in * 4, s>>>(y, key, x, W, in, out, T);
     k_argmax_finish<<<1, 32, 0, s>>>(next, key, T);
     note_launch(2);
     return check_launch("lm head argmax");
+}
+
+int gemv_tagged(float *y, const float *x, const void *W, int wdt, int in, int out, cudaStream_t s)
+{
+    if (wdt == K3_WBF16) return gemv_bf16(y, x, (const uint16_t *)W, in, out, 1, 0, s);
+    if (wdt == K3_WF32) return gemv_f32(y, x, (const float *)W, in, out, s);
+    return fail(K3D_EUNSUPPORTED, "weight tag %d (the int8 draft format is not served here)", wdt);
 }
 
 int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStream_t s)
@@ -373,7 +382,7 @@ int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStre
     }
     static bool init = false;
     if (!init) { allow_smem(k_gemv_f32<2, 4>); init = true; }
-    k_gemv_f32<2, 4><<<grid_for(out, 64), 256, (size_t)in * sizeof(float), s>>>(y, x, W, in, out);
+    k_gemv_f32<2, 4><<<grid_for(out, 16), 256, (size_t)in * sizeof(float), s>>>(y, x, W, in, out);
     note_launch();
     return check_launch("gemv f32");
 }

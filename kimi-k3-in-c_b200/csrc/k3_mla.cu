@@ -90,30 +90,56 @@ __global__ void k_mla_prep(float *ql, float *c, uint16_t *cache, const float *q_
     for (int i = threadIdx.x; i < d.kvw; i += blockDim.x) dst[i] = f32_to_bf16_bits(cb[i]);
 }
 
-// grid (H, B): q_lat = W_uk_h^T q_nope_h, RoPE(q_rope_h); output qa [B][H][kvw]
+// grid (H, kv_lora / 128, B), block (16, 8): q_lat[j] = sum_i W_uk[h][i][j] q_nope[i] for a
+// 128-wide block of j, 8 j per thread (16-byte loads), the 8 thread rows splitting i;
+// then RoPE(q_rope_h). Output qa [B][H][kvw].
 __global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, const int *pos_p,
                              MlaDims d)
 {
-    extern __shared__ float qs[];    // [qh]
-    const int h = blockIdx.x, b = blockIdx.y;
+    __shared__ float qs[256];
+    __shared__ float part[8][128 + 4];
+    const int h = blockIdx.x, jb = blockIdx.y, b = blockIdx.z;
+    const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * 16 + tx;
     const float *qh = q + ((size_t)b * d.H + h) * d.qh;
-    for (int i = threadIdx.x; i < d.qh; i += blockDim.x) qs[i] = qh[i];
+    for (int i = tid; i < d.qh; i += 128) qs[i] = qh[i];
+    __syncthreads();
+    const size_t kvd = (size_t)(d.qn + d.vh);
+    const uint16_t *wuk = kv_b + (size_t)h * kvd * d.kv_lora + jb * 128 + tx * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int per = (d.qn + 7) / 8;
+#pragma unroll 4
+    for (int ii = 0; ii < per; ii++) {
+        const int i = ty * per + ii;
+        if (i < d.qn) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4 *>(wuk + (size_t)i * d.kv_lora));
+            const float qi = qs[i];
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                acc[2 * k] = fmaf(__uint_as_float(u[k] << 16), qi, acc[2 * k]);
+                acc[2 * k + 1] = fmaf(__uint_as_float(u[k] & 0xffff0000u), qi, acc[2 * k + 1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) part[ty][tx * 8 + k] = acc[k];
     __syncthreads();
     float *out = qa + ((size_t)b * d.H + h) * d.kvw;
-    const size_t kvd = (size_t)(d.qn + d.vh);
-    const uint16_t *wuk = kv_b + (size_t)h * kvd * d.kv_lora;   // rows h*kvd + i, i < qn
-    for (int j = threadIdx.x; j < d.kv_lora; j += blockDim.x) {
-        float acc = 0.f;
-        for (int i = 0; i < d.qn; i++)
-            acc = fmaf(bf16_to_f32(wuk[(size_t)i * d.kv_lora + j]), qs[i], acc);
-        out[j] = acc;
+    {
+        const int j = tid;   // 0..127
+        float v = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; r++) v += part[r][j];
+        out[jb * 128 + j] = v;
     }
-    if (d.theta > 0.f) {
-        __syncthreads();
-        rope_pairs(qs + d.qn, d.qr, *pos_p, d.theta, threadIdx.x, blockDim.x);
-        __syncthreads();
+    if (jb == 0) {
+        if (d.theta > 0.f) {
+            __syncthreads();
+            rope_pairs(qs + d.qn, d.qr, *pos_p, d.theta, tid, 128);
+            __syncthreads();
+        }
+        for (int i = tid; i < d.qr; i += 128) out[d.kv_lora + i] = qs[d.qn + i];
     }
-    for (int i = threadIdx.x; i < d.qr; i += blockDim.x) out[d.kv_lora + i] = qs[d.qn + i];
 }
 
 // grid (nsplit, H / kHG, B), 256 threads. Partials: part [B][H][nsplit][kv_lora + 2]
@@ -298,16 +324,25 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
     d.nsplit = mla_nsplit(B, s->n_heads, cap);
     d.theta = s->rope_theta; d.eps = s->eps; d.scale = 1.0f / sqrtf((float)d.qh);
     prof_begin("mla.proj_in");
-    K3_TRY(gemv_bf16(L.ql, x, w->q_a, s->hidden, s->q_lora, B, 0, st));
-    K3_TRY(gemv_bf16(L.c, x, w->kv_a, s->hidden, d.kvw, B, 0, st));
-    if (s->out_gate) K3_TRY(gemv_bf16(L.gate, x, w->g, s->hidden, d.H * d.vh, B, 0, st));
+    {
+        const uint16_t *Ws[3] = {w->q_a, w->kv_a, w->g};
+        float *Ys[3] = {L.ql, L.c, L.gate};
+        const int rows[3] = {s->q_lora, d.kvw, d.H * d.vh};
+        if (B <= 4) {
+            K3_TRY(gemv_bf16_multi(s->out_gate ? 3 : 2, Ws, Ys, rows, x, s->hidden, B, st));
+        } else {
+            K3_TRY(gemv_bf16(L.ql, x, w->q_a, s->hidden, s->q_lora, B, 0, st));
+            K3_TRY(gemv_bf16(L.c, x, w->kv_a, s->hidden, d.kvw, B, 0, st));
+            if (s->out_gate) K3_TRY(gemv_bf16(L.gate, x, w->g, s->hidden, d.H * d.vh, B, 0, st));
+        }
+    }
     prof_end("mla.proj_in");
     prof_begin("mla.core");
     k_mla_prep<<<B, 256, 0, st>>>(L.ql, L.c, cache, w->q_a_norm, w->kv_a_norm, pos, d, cap);
     note_launch();
     K3_TRY(check_launch("mla prep"));
     K3_TRY(gemv_bf16(L.q, L.ql, w->q_b, s->q_lora, d.H * d.qh, B, 0, st));
-    k_mla_absorb<<<dim3(d.H, B), 256, (size_t)d.qh * 4, st>>>(L.qa, L.q, w->kv_b, pos, d);
+    k_mla_absorb<<<dim3(d.H, d.kv_lora / 128, B), dim3(16, 8), 0, st>>>(L.qa, L.q, w->kv_b, pos, d);
     note_launch();
     K3_TRY(check_launch("mla absorb"));
     const size_t smem = ((size_t)kHG * d.kvw + kHG * kTP) * 4 + (size_t)kTP * (d.kvw + 2) * 2;
@@ -352,10 +387,10 @@ int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaSha
     if (!w->q_a || !w->q_b || !w->kv_a || !w->kv_b || !w->o || !w->q_a_norm || !w->kv_a_norm ||
         (s->out_gate && !w->g))
         return fail(K3D_EINVAL, "k3d_mla_decode weight missing");
-    if (s->n_heads % kHG || s->kv_lora > 512 || s->kv_lora % 2 || s->qk_rope % 2 ||
-        ((s->kv_lora + s->qk_rope) % 8))
-        return fail(K3D_EINVAL, "k3d_mla_decode: n_heads %% 8, kv_lora <= 512, even rope, "
-                                "(kv_lora + rope) %% 8 required");
+    if (s->n_heads % kHG || s->kv_lora > 512 || s->kv_lora % 128 || s->qk_rope % 2 ||
+        ((s->kv_lora + s->qk_rope) % 8) || s->qk_nope + s->qk_rope > 256 || s->hidden % 8)
+        return fail(K3D_EINVAL, "k3d_mla_decode: n_heads %% 8, kv_lora a multiple of 128 up to "
+                                "512, even rope, (kv_lora + rope) %% 8, nope + rope <= 256");
     if (ws_bytes < k3d_mla_ws_bytes(s, B, cap)) return fail(K3D_EINVAL, "k3d_mla_decode workspace");
     return mla_decode(out, x, w, s, B, cache, cap, pos, accumulate, ws, stream());
 }

@@ -42,8 +42,9 @@ struct MmaJob {
     int mode;
     int in;            // K: elements per row
     int rows;          // gate/up: intermediate size (pairs); down: output rows
-    int nblk;          // tiles per expert
+    int nblk;          // items (stages) per expert
     int n_items;       // (max active experts) * nblk
+    int rt;            // 16-row tiles per stage
     const __half *xb;  // split activations [nvec][2][in]
     const float *xsc;  // per-vector scale 2^e [nvec]
     int x_by_assign;   // 0: vector = token (a / K); 1: vector = assignment a
@@ -52,6 +53,9 @@ struct MmaJob {
     int stage_bytes;
     int pitch;         // bytes per code row in shared memory
 };
+
+static const int kCW = 16;          // consumer warps
+static const int kThreads = (kCW + 1) * 32;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
 {
@@ -101,25 +105,52 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(b)) : "memory");
 }
 
+// volatile + memory clobber: must not move above the mbarrier wait that publishes the
+// stage it reads
 __device__ __forceinline__ void ldsm_x4(uint32_t r[4], uint32_t addr)
 {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
 }
 
+// register-only: free for the compiler to schedule across loop iterations
 __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
                                           const float c[4])
 {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
-                 : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
-                   "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
+          "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+__device__ __forceinline__ void cvt8(uint32_t w, uint32_t out[4])
+{
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3]) : "r"(w));
 }
 
 __device__ __forceinline__ void named_sync(int id, int n)
 {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory");
+}
+
+// Two E8M0 bytes (low byte = first group) -> two fp32 scales. Bytes 1..254 are the
+// normal power of two s << 23; 0 (2^-127) and 255 (NaN -> 0) take the exact slow path.
+__device__ __forceinline__ void e8m0x2(uint32_t v, float &s0, float &s1)
+{
+    const uint32_t b0 = v & 0xffu, b1 = (v >> 8) & 0xffu;
+    s0 = __uint_as_float(b0 << 23);
+    s1 = __uint_as_float(b1 << 23);
+    if (((b0 - 1u) > 253u) | ((b1 - 1u) > 253u)) {
+        s0 = e8m0_to_f32(b0);
+        s1 = e8m0_to_f32(b1);
+    }
 }
 
 // Resolves a work item; identical in producer and consumers so both walk the same
@@ -134,34 +165,48 @@ __device__ __forceinline__ bool job_item(const MmaJob &J, int item, K3ExpertQ &q
     return ok;
 }
 
-__global__ void __launch_bounds__(288, 1) k_mxfp4_mma(MmaJob J)
+// Items are dealt in contiguous runs, so one CTA mostly stays on one expert (its
+// activation fragments stay in registers and its reads stay sequential).
+__device__ __forceinline__ void item_range(const MmaJob &J, int &i0, int &i1)
+{
+    const int per = (J.n_items + gridDim.x - 1) / gridDim.x;
+    i0 = blockIdx.x * per;
+    i1 = min(J.n_items, i0 + per);
+}
+
+template <int GPW>
+__global__ void __launch_bounds__(kThreads, 1) k_mxfp4_mma(MmaJob J)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const int S = J.stages;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + S;
-    float *red = reinterpret_cast<float *>(smem + 256);          // [8 warps][32 lanes][4]
-    unsigned char *stage0 = smem + 256 + 8 * 32 * 4 * 4;          // 128-aligned
+    float *red = reinterpret_cast<float *>(smem + 256);          // [kCW warps][32 lanes][4]
+    unsigned char *stage0 = smem + 256 + kCW * 32 * 4 * 4;        // 128-aligned
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rowbytes = J.in >> 1;
     const int ngrp = J.in >> 5;
     const int pitch = J.pitch;
-    const int codes_bytes = 16 * pitch;
+    const int rt = J.rt;
+    const int tile_rows = 16 * rt;
+    const int codes_bytes = tile_rows * pitch;
+    int i_beg, i_end;
+    item_range(J, i_beg, i_end);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 8); }
+        for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], kCW); }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
-    if (warp == 8) {
+    if (warp == kCW) {
         // ------------------------------------------------------------- producer ----
         if (lane == 0) {
             int it = 0;
-            for (int item = blockIdx.x; item < J.n_items; item += gridDim.x) {
+            for (int item = i_beg; item < i_end; item++) {
                 K3ExpertQ q; int beg, end, blk;
                 if (!job_item(J, item, q, beg, end, blk)) continue;
                 const int s = it % S;
@@ -171,10 +216,10 @@ __global__ void __launch_bounds__(288, 1) k_mxfp4_mma(MmaJob J)
                     break;
                 }
                 unsigned char *st = stage0 + (size_t)s * J.stage_bytes;
-                const uint32_t tx = 16u * rowbytes + 16u * ngrp;
+                const uint32_t tx = (uint32_t)tile_rows * (rowbytes + ngrp);
                 mbar_expect_tx(&full[s], tx);
                 if (J.mode == MODE_GATEUP) {
-                    const int i0 = blk * 8;
+                    const int i0 = blk * 8;               // rt == 1
                     for (int r = 0; r < 8; r++) {
                         bulk_g2s(st + r * pitch, q.p1 + (size_t)(i0 + r) * rowbytes, rowbytes, &full[s]);
                         bulk_g2s(st + (r + 8) * pitch, q.p3 + (size_t)(i0 + r) * rowbytes, rowbytes, &full[s]);
@@ -182,10 +227,10 @@ __global__ void __launch_bounds__(288, 1) k_mxfp4_mma(MmaJob J)
                     bulk_g2s(st + codes_bytes, q.s1 + (size_t)i0 * ngrp, 8u * ngrp, &full[s]);
                     bulk_g2s(st + codes_bytes + 8 * ngrp, q.s3 + (size_t)i0 * ngrp, 8u * ngrp, &full[s]);
                 } else {
-                    const int r0 = blk * 16;
-                    for (int r = 0; r < 16; r++)
+                    const int r0 = blk * tile_rows;
+                    for (int r = 0; r < tile_rows; r++)
                         bulk_g2s(st + r * pitch, q.p2 + (size_t)(r0 + r) * rowbytes, rowbytes, &full[s]);
-                    bulk_g2s(st + codes_bytes, q.s2 + (size_t)r0 * ngrp, 16u * ngrp, &full[s]);
+                    bulk_g2s(st + codes_bytes, q.s2 + (size_t)r0 * ngrp, (uint32_t)tile_rows * ngrp, &full[s]);
                 }
                 it++;
             }
@@ -195,32 +240,35 @@ __global__ void __launch_bounds__(288, 1) k_mxfp4_mma(MmaJob J)
 
     // ---------------------------------------------------------------- consumers ----
     const int qrow = lane >> 2, c = lane & 3;
-    const int gpw = ngrp / 8;                 // groups per warp (even)
-    const int g0 = warp * gpw;
-    // ldmatrix source row for this lane: matrix m = lane / 8 covers rows (m&1)*8 .. +7
-    // at group g + (m >> 1)
-    const int lm_row = ((lane >> 3) & 1) * 8 + (lane & 7);
+    const int wpt = kCW / rt;                 // warps per 16-row tile
+    const int tile = warp / wpt;              // this warp's tile within the stage
+    const int wk = warp % wpt;                // this warp's K slice
+    const int gpw = ngrp / wpt;               // == GPW when specialised
+    const int g0 = wk * gpw;
+    const int lm_row = tile * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
     const int lm_goff = (lane >> 4);
+    // B fragments of the current quad for this warp's K slice, kept across items
+    uint4 breg[GPW > 0 ? GPW : 1];
+    int cached_v0 = -2, cached_v1 = -2, cached_v2 = -2, cached_v3 = -2;
     int it = 0;
-    for (int item = blockIdx.x; item < J.n_items; item += gridDim.x) {
+    for (int item = i_beg; item < i_end; item++) {
         K3ExpertQ q; int beg, end, blk;
         if (!job_item(J, item, q, beg, end, blk)) continue;
         const int s = it % S;
         // the wait is bounded; its outcome is made collective (a named barrier over the
-        // eight consumer warps, which every one of them reaches in bounded time) so that
-        // no warp can be left waiting at a later barrier for a warp that gave up
+        // consumer warps, which every one of them reaches in bounded time) so that no
+        // warp can be left waiting at a later barrier for a warp that gave up
         if (!mbar_wait(&full[s], (it / S) & 1)) {
             if (lane == 0) k3_raise(K3D_ETIMEOUT, K3_SITE_MXFP4);
             atomicExch(&abort_flag, 1);
         }
-        named_sync(1, 256);
+        named_sync(1, kCW * 32);
         if (*(volatile int *)&abort_flag) return;
         const unsigned char *st = stage0 + (size_t)s * J.stage_bytes;
-        const unsigned char *sc = st + codes_bytes;   // scales [16][ngrp]
+        const unsigned char *sc = st + codes_bytes + (size_t)tile * 16 * ngrp;
         const uint32_t lm_base = smem_u32(st + lm_row * pitch + lm_goff * 16);
 
         for (int p0 = beg; p0 < end; p0 += 4) {
-            // the four vectors of this quad (assignment ids; -1 = empty slot)
             int a_of[4], v_of[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -228,47 +276,61 @@ __global__ void __launch_bounds__(288, 1) k_mxfp4_mma(MmaJob J)
                 a_of[k] = a;
                 v_of[k] = a < 0 ? -1 : (J.x_by_assign ? a : a / J.w.K);
             }
-            // B operand source for this lane: column n = qrow -> vector n/2, piece n%2
             const int bv = v_of[qrow >> 1];
             const __half *bsrc = bv < 0 ? nullptr
                                         : J.xb + ((size_t)bv * 2 + (qrow & 1)) * J.in + 8 * c;
+            if (GPW > 0) {
+                if (v_of[0] != cached_v0 || v_of[1] != cached_v1 || v_of[2] != cached_v2 ||
+                    v_of[3] != cached_v3) {
+#pragma unroll
+                    for (int j = 0; j < (GPW > 0 ? GPW : 1); j++)
+                        breg[j] = bsrc ? *reinterpret_cast<const uint4 *>(bsrc + 32 * (g0 + j))
+                                       : make_uint4(0, 0, 0, 0);
+                    cached_v0 = v_of[0]; cached_v1 = v_of[1]; cached_v2 = v_of[2]; cached_v3 = v_of[3];
+                }
+            }
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
             const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int g = g0; g < g0 + gpw; g += 2) {
+            const int jmax = GPW > 0 ? GPW : gpw;
+#pragma unroll
+            for (int j = 0; j < jmax; j += 2) {
+                const int g = g0 + j;
                 uint32_t w4[4];
                 ldsm_x4(w4, lm_base + g * 16);
+                float sq[2], sq8[2];
+                e8m0x2(*reinterpret_cast<const uint16_t *>(sc + qrow * ngrp + g), sq[0], sq[1]);
+                e8m0x2(*reinterpret_cast<const uint16_t *>(sc + (qrow + 8) * ngrp + g), sq8[0], sq8[1]);
 #pragma unroll
                 for (int gg = 0; gg < 2; gg++) {
                     uint32_t hq[4], hq8[4];
-                    e2m1x8_to_f16x8(w4[2 * gg], hq);       // row qrow, codes 8c..8c+7
-                    e2m1x8_to_f16x8(w4[2 * gg + 1], hq8);  // row qrow + 8
-                    uint4 bb = make_uint4(0, 0, 0, 0);
-                    if (bsrc) bb = *reinterpret_cast<const uint4 *>(bsrc + 32 * (g + gg));
+                    cvt8(w4[2 * gg], hq);
+                    cvt8(w4[2 * gg + 1], hq8);
+                    uint4 bb;
+                    if (GPW > 0) bb = breg[(j + gg) % (GPW > 0 ? GPW : 1)];
+                    else bb = bsrc ? *reinterpret_cast<const uint4 *>(bsrc + 32 * (g + gg))
+                                   : make_uint4(0, 0, 0, 0);
                     const uint32_t a0[4] = {hq[0], hq8[0], hq[1], hq8[1]};
                     const uint32_t a1[4] = {hq[2], hq8[2], hq[3], hq8[3]};
                     float d0[4], d1[4];
                     mma_16816(d0, a0, bb.x, bb.y, zero);
                     mma_16816(d1, a1, bb.z, bb.w, d0);
-                    const float sq = e8m0_to_f32(sc[qrow * ngrp + g + gg]);
-                    const float sq8 = e8m0_to_f32(sc[(qrow + 8) * ngrp + g + gg]);
-                    acc[0] = fmaf(d1[0], sq, acc[0]);
-                    acc[1] = fmaf(d1[1], sq, acc[1]);
-                    acc[2] = fmaf(d1[2], sq8, acc[2]);
-                    acc[3] = fmaf(d1[3], sq8, acc[3]);
+                    acc[0] = fmaf(d1[0], sq[gg], acc[0]);
+                    acc[1] = fmaf(d1[1], sq[gg], acc[1]);
+                    acc[2] = fmaf(d1[2], sq8[gg], acc[2]);
+                    acc[3] = fmaf(d1[3], sq8[gg], acc[3]);
                 }
             }
-            // cross-warp reduction of the K slices, then the epilogue on warp 0
+            // reduction of the K slices of each tile, then the epilogue on the tile's
+            // first warp
             float4 *rw = reinterpret_cast<float4 *>(red) + warp * 32 + lane;
             *rw = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            named_sync(1, 256);
-            if (warp == 0) {
+            named_sync(1, kCW * 32);
+            if (wk == 0) {
                 float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    const float4 v = reinterpret_cast<const float4 *>(red)[w * 32 + lane];
+                for (int w = 0; w < wpt; w++) {
+                    const float4 v = reinterpret_cast<const float4 *>(red)[(tile * wpt + w) * 32 + lane];
                     t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
                 }
-                // lane (qrow, c): vector c, rows qrow and qrow + 8, pieces hi + lo
                 const int a = a_of[c];
                 if (a >= 0) {
                     const float xs = J.xsc[v_of[c]];
@@ -277,13 +339,13 @@ __global__ void __launch_bounds__(288, 1) k_mxfp4_mma(MmaJob J)
                     if (J.mode == MODE_GATEUP) {
                         J.out[(size_t)a * J.rows + blk * 8 + qrow] = silu_f(r0v) * r8v;
                     } else {
-                        float *o = J.out + (size_t)a * J.rows + blk * 16;
+                        float *o = J.out + (size_t)a * J.rows + (size_t)blk * tile_rows + tile * 16;
                         o[qrow] = r0v;
                         o[qrow + 8] = r8v;
                     }
                 }
             }
-            named_sync(1, 256);
+            named_sync(1, kCW * 32);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -324,13 +386,39 @@ __global__ void k_xsplit(__half *xb, float *xsc, const float *x, int n, size_t l
     if (threadIdx.x == 0) xsc[blockIdx.x] = ldexpf(1.0f, e);
 }
 
-bool mma_supported(int in, int rows, int mode)
+// Shared memory: a head (barriers + the B-fragment exchange) then S stages of rt
+// 16-row tiles, each row in/2 packed bytes padded by 16, then the tiles' scales.
+static constexpr int kHead = 256 + kCW * 32 * 4 * 4;
+static constexpr int kBudget = 220 * 1024 - kHead;
+static int stage_bytes_for(int in, int rt)
 {
-    if (in % 512 != 0 || in > 16384) return false;
-    if (mode == MODE_GATEUP && rows % 8 != 0) return false;
-    if (mode == MODE_DOWN && rows % 16 != 0) return false;
-    return true;
+    return ((16 * rt * (in / 2 + 16) + 16 * rt * (in / 32)) + 127) & ~127;
 }
+
+// Tiles per stage for a shape, or 0 when the tensor-core kernel cannot run it: every
+// consumer warp takes an even number of 32-element groups of one 16-row tile, and the
+// ring holds at least two stages (three when a smaller tile allows it).
+static int mma_plan(int in, int rows, int mode)
+{
+    if (in % 32 != 0 || in > 16384 || in < 64) return 0;
+    const int ngrp = in / 32;
+    if (mode == MODE_GATEUP) {
+        if (rows % 8 != 0) return 0;
+        if (kBudget / stage_bytes_for(in, 1) < 2) return 0;
+        return (ngrp % kCW == 0 && (ngrp / kCW) % 2 == 0) ? 1 : 0;
+    }
+    int fallback = 0;
+    for (int rt = 4; rt >= 1; rt /= 2) {
+        const int wpt = kCW / rt;
+        if (rows % (16 * rt) != 0 || ngrp % wpt != 0 || (ngrp / wpt) % 2 != 0) continue;
+        const int S = kBudget / stage_bytes_for(in, rt);
+        if (S >= 3) return rt;
+        if (S >= 2 && fallback == 0) fallback = rt;
+    }
+    return fallback;
+}
+
+bool mma_supported(int in, int rows, int mode) { return mma_plan(in, rows, mode) > 0; }
 
 int xsplit(__half *xb, float *xsc, const float *x, int n, int nvec, size_t ld, cudaStream_t s)
 {
@@ -349,31 +437,41 @@ int mxfp4_mma_launch(int mode, const MoeWork &w, int umax, int in, int rows, con
     J.mode = mode;
     J.in = in;
     J.rows = rows;
-    J.nblk = mode == MODE_GATEUP ? rows / 8 : rows / 16;
+    const int ngrp = in / 32;
+    // gate/up: one 16-row tile (8 gate + 8 up rows) per stage; down: up to 4 tiles so a
+    // stage carries ~64 KB whatever the row length
+    const int rt = mma_plan(in, rows, mode);
+    if (rt == 0) return fail(K3D_EINVAL, "mxfp4 mma: unsupported shape in=%d rows=%d", in, rows);
+    const int wpt = kCW / rt;
+    J.rt = rt;
+    J.nblk = mode == MODE_GATEUP ? rows / 8 : rows / (16 * rt);
     J.n_items = umax * J.nblk;
     J.xb = xb;
     J.xsc = xsc;
     J.x_by_assign = x_by_assign;
     J.out = out;
     J.pitch = in / 2 + 16;
-    const int ngrp = in / 32;
-    J.stage_bytes = ((16 * J.pitch + 16 * ngrp) + 127) & ~127;
-    const int head = 256 + 8 * 32 * 4 * 4;
-    const int budget = 220 * 1024 - head;
-    int S = budget / J.stage_bytes;
+    J.stage_bytes = stage_bytes_for(in, rt);
+    const int head = kHead;
+    int S = kBudget / J.stage_bytes;
     if (S > 8) S = 8;
     if (S < 2) return fail(K3D_EINVAL, "mxfp4 mma: stage of %d bytes does not fit", J.stage_bytes);
     J.stages = S;
     const size_t smem = (size_t)head + (size_t)S * J.stage_bytes;
     static bool init = false;
     if (!init) {
-        allow_smem_max(k_mxfp4_mma);
+        allow_smem_max(k_mxfp4_mma<14>);
+        allow_smem_max(k_mxfp4_mma<16>);
+        allow_smem_max(k_mxfp4_mma<0>);
         init = true;
     }
     int grid = sm_count();
     if (grid > J.n_items) grid = J.n_items;
     if (grid < 1) return K3D_OK;
-    k_mxfp4_mma<<<grid, 288, smem, st>>>(J);
+    const int gpw = ngrp / wpt;
+    if (gpw == 14) k_mxfp4_mma<14><<<grid, kThreads, smem, st>>>(J);
+    else if (gpw == 16) k_mxfp4_mma<16><<<grid, kThreads, smem, st>>>(J);
+    else k_mxfp4_mma<0><<<grid, kThreads, smem, st>>>(J);
     note_launch();
     return check_launch("mxfp4 mma");
 }

@@ -12,11 +12,13 @@
 //   rounding in the CPU sum is in its additions. Let s_k be the exact prefix sums and
 //   A = sum |p_i|. The sequential double sum differs from the exact sum by at most
 //   u * sum_k |s^_k| <= u * (sum_k |s_k| + n * gamma_n * A), u = 2^-53.
-//   A warp computes (1) the exact sum to ~2^-100 relative with compensated lane sums
-//   and a TwoSum tree, and (2) sum_k |s_k| from a second pass over prefix sums. If the
-//   whole interval [S - bound, S + bound] rounds to one float, that float IS
-//   (float)acc of the CPU. Otherwise (about one expert in 10^5 at the benchmark shapes)
-//   lane 0 runs the CPU's exact sequential loop for that expert.
+//   A warp computes, in one coalesced pass over the row, (1) the exact sum to ~2^-100
+//   relative (TwoSum accumulation per lane, then a TwoSum tree) and (2) sum_k |s_k| from
+//   the prefix sums in the CPU's element order (a warp scan per round of 32 chunks gives
+//   each chunk's starting prefix). If the whole interval [S - bound, S + bound] rounds
+//   to one float, that float IS (float)acc of the CPU. Otherwise (about one expert in
+//   10^5 at the benchmark shapes; k3d_router_fallbacks counts them) lane 0 runs the
+//   CPU's exact sequential loop for that expert.
 //   The sigmoid uses k3_expf (glibc's expf restated, bit-identical), and all float
 //   operations use explicit round-to-nearest intrinsics so nothing is contracted.
 #include "k3_common.cuh"
@@ -42,7 +44,36 @@ __device__ __forceinline__ void two_sum(double a, double b, double &s, double &e
     e = __dadd_rn(__dsub_rn(a, __dsub_rn(s, bb)), __dsub_rn(b, bb));
 }
 
-// One warp per (token, expert): writes score and choice.
+// Counts experts whose logit needed the sequential fallback (read by k3d_router_fallbacks).
+__device__ unsigned long long k3_router_fallbacks;
+
+template <typename WT> struct Chunk;
+template <> struct Chunk<uint16_t> {   // 8 bf16 = 16 bytes
+    __device__ static void load(const uint16_t *row, int c, double w[8])
+    {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row) + c);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[2 * i] = (double)__uint_as_float(u[i] << 16);
+            w[2 * i + 1] = (double)__uint_as_float(u[i] & 0xffff0000u);
+        }
+    }
+};
+template <> struct Chunk<float> {      // 8 fp32 = 32 bytes
+    __device__ static void load(const float *row, int c, double w[8])
+    {
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(row) + 2 * c);
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(row) + 2 * c + 1);
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    }
+};
+
+// One warp per (token, expert): writes score and choice. Lane l owns 8-element chunks
+// l, l+32, ...; one pass computes (1) the exact total with TwoSum accumulation, (2)
+// sum |p|, and (3) sum over k of |prefix sum k| in the CPU's element order, using a warp
+// scan per round of 32 chunks for the prefix at each chunk start.
+// Requires hidden % 8 == 0 and 16-byte aligned rows and x.
 template <typename WT>
 __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choice,
                                                        const float *x, const WT *W,
@@ -55,11 +86,111 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
     if (e >= n_experts) return;
     const float *xt = x + (size_t)t * hidden;
     const WT *row = W + (size_t)e * hidden;
+    const int nchunk = hidden >> 3;
+    double hs = 0.0, ls = 0.0, A = 0.0, absum = 0.0, run = 0.0;
+    for (int base = 0; base < nchunk; base += 32) {
+        const int c = base + lane;
+        double p[8];
+        if (c < nchunk) {
+            double w[8];
+            Chunk<WT>::load(row, c, w);
+            const float4 xa = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c);
+            const float4 xb = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c + 1);
+            const double xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) p[i] = __dmul_rn(w[i], xv[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) p[i] = 0.0;
+        }
+        double cs = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            // exact accumulation of the lane's products
+            const double s1 = __dadd_rn(hs, p[i]);
+            const double bb = __dsub_rn(s1, hs);
+            ls = __dadd_rn(ls, __dadd_rn(__dsub_rn(hs, __dsub_rn(s1, bb)), __dsub_rn(p[i], bb)));
+            hs = s1;
+            A = __dadd_rn(A, fabs(p[i]));
+            cs = __dadd_rn(cs, p[i]);
+        }
+        // prefix at this chunk's start: run + exclusive scan of chunk sums
+        double incl = cs;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl = __dadd_rn(incl, v);
+        }
+        double pre = __dadd_rn(run, __dsub_rn(incl, cs));
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            pre = __dadd_rn(pre, p[i]);
+            absum = __dadd_rn(absum, fabs(pre));
+        }
+        run = __dadd_rn(run, __shfl_sync(0xffffffffu, incl, 31));
+    }
+    // TwoSum tree over the lanes' (hs, ls)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const double oh = __shfl_xor_sync(0xffffffffu, hs, o);
+        const double ol = __shfl_xor_sync(0xffffffffu, ls, o);
+        double sum, err;
+        two_sum(hs, oh, sum, err);
+        const double low = __dadd_rn(__dadd_rn(ls, ol), err);
+        double s2, e2;
+        two_sum(sum, low, s2, e2);
+        hs = s2;
+        ls = e2;
+    }
+    const double total = hs;
+    A = warp_sum_d(A);
+    const double R = warp_sum_d(absum);
+
+    if (lane == 0) {
+        const double u = 0x1p-53;
+        const double n = (double)hidden;
+        const double gam = n * u / (1.0 - n * u);
+        const double bound = (u * (R + 4.0 * n * gam * A) + 8.0 * u * fabs(total) +
+                              64.0 * n * n * u * u * A) * (1.0 + 0x1p-20) + 0x1p-1074;
+        const float flo = (float)(total - bound);
+        const float fhi = (float)(total + bound);
+        float logit;
+        if (flo == fhi) {
+            logit = flo;
+        } else {
+            // ambiguous: the CPU's exact sequential loop (k3_ops.c:449-450)
+            double acc = 0.0;
+            for (int i = 0; i < hidden; i++) {
+                const double wv = (sizeof(WT) == 2)
+                    ? (double)__uint_as_float((uint32_t)__ldg((const uint16_t *)row + i) << 16)
+                    : (double)__ldg((const float *)row + i);
+                acc = __dadd_rn(acc, __dmul_rn(wv, (double)__ldg(xt + i)));
+            }
+            logit = (float)acc;
+            atomicAdd(&k3_router_fallbacks, 1ull);
+        }
+        const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-logit)));
+        score[(size_t)t * n_experts + e] = sc;
+        choice[(size_t)t * n_experts + e] = bias ? __fadd_rn(sc, __ldg(bias + e)) : sc;
+    }
+}
+
+// Any shape: one warp per (token, expert), lanes over contiguous segments.
+template <typename WT>
+__global__ void __launch_bounds__(256) k_router_scores_generic(float *score, float *choice,
+                                                               const float *x, const WT *W,
+                                                               const float *bias, int hidden,
+                                                               int n_experts)
+{
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int t = blockIdx.y;
+    if (e >= n_experts) return;
+    const float *xt = x + (size_t)t * hidden;
+    const WT *row = W + (size_t)e * hidden;
     const int seg = (hidden + 31) >> 5;
     const int lo = min(hidden, lane * seg);
     const int hi = min(hidden, lo + seg);
-
-    // pass 1: compensated lane sum (Neumaier) and sum of |p|
     double s = 0.0, c = 0.0, a = 0.0;
     for (int i = lo; i < hi; i++) {
         const double p = __dmul_rn(wval<WT>(row, i), (double)__ldg(xt + i));
@@ -69,9 +200,7 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         s = tt;
         a = __dadd_rn(a, fabs(p));
     }
-    // lane total for the prefix pass
     const double lane_tot = __dadd_rn(s, c);
-    // exclusive prefix of lane totals
     double incl = lane_tot;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -79,8 +208,6 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         if (lane >= o) incl = __dadd_rn(incl, v);
     }
     const double excl = __dsub_rn(incl, lane_tot);
-
-    // exact-ish total: TwoSum tree over (s, c) pairs
     double hs = s, ls = c;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -94,10 +221,8 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         hs = s2;
         ls = e2;
     }
-    const double total = hs;  // |ls| <= u |hs|
+    const double total = hs;
     const double A = warp_sum_d(a);
-
-    // pass 2: sum over k of |prefix sum|
     double run = excl, absum = 0.0;
     for (int i = lo; i < hi; i++) {
         const double p = __dmul_rn(wval<WT>(row, i), (double)__ldg(xt + i));
@@ -105,25 +230,23 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         absum = __dadd_rn(absum, fabs(run));
     }
     const double R = warp_sum_d(absum);
-
-    float logit = 0.f;
     if (lane == 0) {
         const double u = 0x1p-53;
         const double n = (double)hidden;
         const double gam = n * u / (1.0 - n * u);
-        // sequential-sum bound + error of our own total + slack for the arithmetic here
         const double bound = (u * (R + 4.0 * n * gam * A) + 8.0 * u * fabs(total) +
                               64.0 * n * n * u * u * A) * (1.0 + 0x1p-20) + 0x1p-1074;
         const float flo = (float)(total - bound);
         const float fhi = (float)(total + bound);
+        float logit;
         if (flo == fhi) {
             logit = flo;
         } else {
-            // ambiguous: reproduce the CPU loop exactly
             double acc = 0.0;
             for (int i = 0; i < hidden; i++)
                 acc = __dadd_rn(acc, __dmul_rn(wval<WT>(row, i), (double)__ldg(xt + i)));
             logit = (float)acc;
+            atomicAdd(&k3_router_fallbacks, 1ull);
         }
         const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-logit)));
         score[(size_t)t * n_experts + e] = sc;
@@ -195,7 +318,9 @@ static int router_launch(int *idx, float *w, const float *x, const WT *W, const 
     float *score = (float *)ws;
     float *choice = score + (size_t)T * n_experts;
     dim3 grid((n_experts + 7) / 8, T);
-    k_router_scores<WT><<<grid, 256, 0, s>>>(score, choice, x, W, bias, hidden, n_experts);
+    const bool vec = (hidden % 8) == 0 && (((uintptr_t)W | (uintptr_t)x) & 15u) == 0;
+    if (vec) k_router_scores<WT><<<grid, 256, 0, s>>>(score, choice, x, W, bias, hidden, n_experts);
+    else k_router_scores_generic<WT><<<grid, 256, 0, s>>>(score, choice, x, W, bias, hidden, n_experts);
     k_router_topk<<<T, 32, 0, s>>>(idx, w, choice, score, n_experts, topk, renorm,
                                    routed_scale, topk);
     note_launch(2);
@@ -246,6 +371,14 @@ void k3_router(int *idx, float *w, const float *x, const float *W, const float *
                    stream()))
         return;
     st.finish();
+}
+
+long long k3d_router_fallbacks(void)
+{
+    if (ensure_ctx()) return -1;
+    unsigned long long v = 0;
+    cudaMemcpyFromSymbol(&v, k3_router_fallbacks, sizeof v);
+    return (long long)v;
 }
 
 int k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W, const float *bias,

@@ -190,6 +190,7 @@ _PROTOS = {
                              vp, sz]),
     "k3d_router_bf16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32]),
     "k3d_moe_last_unique": (i32, []),
+    "k3d_router_fallbacks": (C.c_longlong, []),
     "k3d_gemv_bf16": (i32, [vp, vp, vp, i32, i32, i32, i32]),
     # KDA / MLA / small
     "k3d_kda_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),

@@ -71,7 +71,7 @@ def test_mla_decode_matches_oracle(k3, oracle, B, L):
 
 
 def test_mla_decode_nope_small_dims_and_accumulate(k3, oracle):
-    d = dict(hidden=256, H=8, q_lora=64, kv_lora=64, qn=32, qr=16, vh=32, theta=0.0, eps=1e-5)
+    d = dict(hidden=256, H=8, q_lora=64, kv_lora=128, qn=32, qr=16, vh=32, theta=0.0, eps=1e-5)
     cap, L = 96, 70
     w, cache, x = make(3, d, 1, cap, L)
     resid = synth.rng(4).standard_normal((1, d["hidden"]), dtype=np.float32)
@@ -81,7 +81,7 @@ def test_mla_decode_nope_small_dims_and_accumulate(k3, oracle):
 
 
 def test_mla_decode_rejects_position_beyond_capacity(k3):
-    d = dict(hidden=256, H=8, q_lora=64, kv_lora=64, qn=32, qr=16, vh=32, theta=0.0, eps=1e-5)
+    d = dict(hidden=256, H=8, q_lora=64, kv_lora=128, qn=32, qr=16, vh=32, theta=0.0, eps=1e-5)
     cap = 16
     w, cache, x = make(5, d, 1, cap, 8)
     try:

@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 CFG = dict(hidden=512, vocab=1024, n_layers=8, eps=1e-6, kda_heads=4, kda_head_dim=64, conv_k=4,
            gate_lb=-5.0, first_dense=1, dense_inter=1024, mla_layers=[3, 7],
-           mla=dict(hidden=512, H=8, q_lora=128, kv_lora=64, qn=32, qr=16, vh=32, theta=50000.0,
+           mla=dict(hidden=512, H=8, q_lora=128, kv_lora=128, qn=32, qr=16, vh=32, theta=50000.0,
                     eps=1e-6),
            moe=dict(inter=512, n_experts=16, topk=4, routed_scale=2.5, shared_inter=256))
 
