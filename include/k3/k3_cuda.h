@@ -161,6 +161,23 @@ int    k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoe
 int    k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W,
                        const float *bias, int T, int hidden, int n_experts, int topk,
                        int renorm, float routed_scale);
+/* k3d_router_bf16 without device allocation. No reference counterpart: the CPU engine
+ * never allocates device memory. k3d_router_bf16 takes its score buffer from the
+ * library workspace, which grows with cudaMalloc (a device-wide synchronisation) the
+ * first time a larger T * n_experts arrives. This variant instead uses one fixed
+ * scratch array compiled into the library (2 * K3D_ROUTER_NOALLOC_MAX floats, 256 KB),
+ * for callers that must not allocate once running: a serving loop whose device memory
+ * is fixed at start-up, or a host whose allocator owns all device memory.
+ *   - T * n_experts above K3D_ROUTER_NOALLOC_MAX returns K3D_EBOUND and launches nothing.
+ *   - The first call on a device does set-up (it looks up the scratch array's address);
+ *     make that first call before any stream capture.
+ *   - The scratch array is shared: calls that overlap (other threads, other streams)
+ *     race on it. Serialise them.
+ * Results are bit-identical to k3d_router_bf16. */
+#define K3D_ROUTER_NOALLOC_MAX 32768
+int    k3d_router_bf16_noalloc(int *idx, float *w, const float *x, const uint16_t *W,
+                               const float *bias, int T, int hidden, int n_experts,
+                               int topk, int renorm, float routed_scale);
 /* Experts (summed over all router calls in this process) whose fp32 logit could not be
  * settled from the exact dot product and its error bound, and were recomputed with the
  * CPU engine's sequential double loop. Diagnostic; results are bit-exact either way. */

@@ -343,6 +343,12 @@ int router_bf16(int *idx, float *w, const float *x, const uint16_t *W, const flo
                                    routed_scale, ws, s);
 }
 
+// Fixed scratch of k3d_router_bf16_noalloc: scores then choice keys, each up to
+// K3D_ROUTER_NOALLOC_MAX floats. Every element a call reads it has first written, so
+// nothing needs clearing between calls.
+static __device__ __align__(256) float g_router_noalloc_ws[2 * K3D_ROUTER_NOALLOC_MAX];
+static const int kMaxDevices = 64;
+
 }  // namespace k3
 
 using namespace k3;
@@ -390,6 +396,33 @@ int k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W, const
     if (!ws) return k3d_status();
     return router_bf16(idx, w, x, W, bias, T, hidden, n_experts, topk, renorm, routed_scale,
                        ws, stream());
+}
+
+int k3d_router_bf16_noalloc(int *idx, float *w, const float *x, const uint16_t *W,
+                            const float *bias, int T, int hidden, int n_experts, int topk,
+                            int renorm, float routed_scale)
+{
+    K3_TRY(ensure_ctx());
+    if (!idx || !w || !x || !W) return fail(K3D_EINVAL, "k3d_router_bf16_noalloc null pointer");
+    if (T < 1 || n_experts < 1 || (long long)T * n_experts > K3D_ROUTER_NOALLOC_MAX)
+        return fail(K3D_EBOUND, "k3d_router_bf16_noalloc: T=%d x n_experts=%d scores exceed "
+                    "the fixed scratch of %d", T, n_experts, K3D_ROUTER_NOALLOC_MAX);
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return fail(K3D_ECUDA, "k3d_router_bf16_noalloc: device %d: %s", dev, cudaGetErrorString(e));
+    // set-up once per device: the address of the scratch array in this device's module
+    static void *ws_of[kMaxDevices];
+    if (!ws_of[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_router_noalloc_ws);
+        if (e != cudaSuccess || !p)
+            return fail(K3D_ECUDA, "k3d_router_bf16_noalloc: scratch address: %s",
+                        cudaGetErrorString(e));
+        ws_of[dev] = p;
+    }
+    return router_bf16(idx, w, x, W, bias, T, hidden, n_experts, topk, renorm, routed_scale,
+                       ws_of[dev], stream());
 }
 
 }  // extern "C"

@@ -189,6 +189,7 @@ _PROTOS = {
     "k3d_moe_swiglu": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, vp, vp,
                              vp, sz]),
     "k3d_router_bf16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32]),
+    "k3d_router_bf16_noalloc": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32]),
     "k3d_moe_last_unique": (i32, []),
     "k3d_router_fallbacks": (C.c_longlong, []),
     "k3d_gemv_bf16": (i32, [vp, vp, vp, i32, i32, i32, i32]),
