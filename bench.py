@@ -31,6 +31,9 @@ sys.path.insert(0, os.path.join(REPO, "tests", "golden"))
 HIDDEN, INTER, N_EXPERTS, TOPK, SHARED = 7168, 2048, 384, 8, 2048
 EXPERT_BYTES = 3 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)   # 23,396,352
 METRIC = "decode tok/s at 1/2/4/8 B200; MXFP4 expert GEMV HBM GB/s vs peak"
+EXPERT_KERNEL = {0: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA (k_mxfp4_umma gate/up + down)",
+                 1: "MXFP4 expert GEMV, mma.sync m16n8k16 (k_mxfp4_mma gate/up + down)",
+                 2: "MXFP4 expert GEMV, CUDA cores (k_moe_gate_up + k_moe_down)"}
 
 
 def dist_env():
@@ -258,6 +261,7 @@ def cpu_stack_sample(seconds=20.0):
 def bench_moe(args, rank, world):
     import k3cuda
     lib = k3cuda.init(0)
+    k3cuda.check(lib.k3d_set_expert_kernel(args.expert_kernel))
     n_exp = args.n_experts
     per = n_exp // world
     lo, hi = rank * per, (rank + 1) * per
@@ -268,7 +272,8 @@ def bench_moe(args, rank, world):
     sh = (synth.bf16_normal(g, (SHARED, HIDDEN), 0.02), synth.bf16_normal(g, (SHARED, HIDDEN), 0.02),
           synth.bf16_normal(g, (HIDDEN, SHARED), 0.02))
     mw = k3cuda.MoeWeights(HIDDEN, INTER, n_exp, TOPK, W, bias, shared=sh, seed=7, lo=lo, hi=hi,
-                           add_shared=1 if rank == 0 else 0, lib=lib)
+                           add_shared=1 if rank == 0 else 0, tiled=args.expert_kernel == 0,
+                           lib=lib)
     P = 64
     xs = synth.bf16_to_f32(synth.bf16_normal(g, (P, HIDDEN), 1.0))
     X = k3cuda.DevBuf.from_array(xs, lib)
@@ -306,6 +311,10 @@ def bench_moe(args, rank, world):
     cnt = C.c_long()
     exp_ms = lib.k3d_prof_ms(b"moe.experts", C.byref(cnt))
     n_prof = cnt.value
+    kern_ms = 0.0
+    for name in (b"experts.gateup", b"experts.down"):
+        c2 = C.c_long()
+        kern_ms += lib.k3d_prof_ms(name, C.byref(c2)) / max(1, c2.value)
     lib.k3d_prof_enable(0)
     clk = clocks.stop()
     barrier()
@@ -315,7 +324,7 @@ def bench_moe(args, rank, world):
     u_avg = float(np.mean(uniq))
     alg_bytes = u_avg * (EXPERT_BYTES + INTER * 8 + HIDDEN * 4) + HIDDEN * 4
     hbm, peak_kind = measured_peaks()
-    achieved = alg_bytes / (exp_ms_avg * 1e-3) / 1e9
+    achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
     # end to end through the public API with host buffers
     hx = lib.k3d_host_alloc(HIDDEN * 4)
     hy = lib.k3d_host_alloc(HIDDEN * 4)
@@ -341,12 +350,12 @@ def bench_moe(args, rank, world):
         "config": {"workload": "config1 MoE layer decode, T=1", "hidden": HIDDEN,
                    "n_experts": n_exp, "topk": TOPK, "inter": INTER, "shared_inter": SHARED,
                    "parallelism": f"ep{world}", "l2": "flushed between steps (256 MB write)"},
-        "roofline": {"kernel": "MXFP4 expert GEMV (k_moe_gate_up + k_moe_down)", "bound": "hbm",
+        "roofline": {"kernel": EXPERT_KERNEL[args.expert_kernel], "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_kind": peak_kind,
                      "traffic": load_traffic("moe_experts_traffic.json"),
                      "alg_bytes_per_launch": alg_bytes, "unique_experts": u_avg,
-                     "kernel_ms": exp_ms_avg},
+                     "kernel_ms": kern_ms, "expert_section_ms": exp_ms_avg},
         "e2e": {"value": args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
                 "d2h_bytes_per_step": HIDDEN * 4},
         "gpu_launches": int(launches),
@@ -356,7 +365,7 @@ def bench_moe(args, rank, world):
 
 
 # ----------------------------------------------------------------- stack (config 4) ----
-def stack_cfg(world, rank, batch, cap):
+def stack_cfg(world, rank, batch, cap, layout=1):
     import k3cuda
     sc = k3cuda.K3dStackCfg()
     sc.hidden, sc.vocab, sc.n_layers, sc.eps = HIDDEN, 163840, 8, 1e-6
@@ -364,7 +373,7 @@ def stack_cfg(world, rank, batch, cap):
     sc.mla = k3cuda.K3dMlaShape(HIDDEN, 64, 1536, 512, 128, 64, 128, 50000.0, 1e-6, 1)
     per = N_EXPERTS // world
     sc.moe = k3cuda.K3dMoeShape(HIDDEN, INTER, N_EXPERTS, TOPK, 1, 2.5, SHARED, rank * per,
-                                (rank + 1) * per, 1 if rank == 0 else 0)
+                                (rank + 1) * per, 1 if rank == 0 else 0, layout)
     sc.first_dense, sc.dense_inter = 1, 18432
     for i in range(16):
         sc.mla_layers[i] = (3, 7)[i] if i < 2 else -1
@@ -375,9 +384,12 @@ def stack_cfg(world, rank, batch, cap):
 def bench_stack(args, rank, world):
     import k3cuda
     lib = k3cuda.init(0)
+    k3cuda.check(lib.k3d_set_expert_kernel(args.expert_kernel))
     ctx = args.context
     cap = ctx + args.steps * 2 + args.warmup * 2 + 16
-    cfg = stack_cfg(world, rank, args.batch, cap)
+    # the tcgen05 kernel streams experts stored in the tiled layout; the other two
+    # kernels read the checkpoint layout
+    cfg = stack_cfg(world, rank, args.batch, cap, 1 if args.expert_kernel == 0 else 0)
     t0 = time.time()
     model = lib.k3d_model_create(C.byref(cfg), 2024)
     if not model:
@@ -425,7 +437,7 @@ def bench_stack(args, rank, world):
     k3cuda.check(lib.k3d_sync())
     launches_per_step = lib.k3d_launch_count() / n_prof
     sections = {}
-    for name in ("moe.experts", "moe.shared", "moe.router", "kda.proj_in", "kda.core",
+    for name in ("moe.experts", "experts.gateup", "experts.down", "moe.shared", "moe.router", "kda.proj_in", "kda.core",
                  "kda.proj_out", "mla.proj_in", "mla.core", "mla.proj_out", "dense.mlp", "lm_head",
                  "ep.combine"):
         cnt = C.c_long()
@@ -434,7 +446,8 @@ def bench_stack(args, rank, world):
             sections[name] = {"ms_per_call": ms / cnt.value, "calls_per_step": cnt.value / n_prof}
     lib.k3d_prof_enable(0)
     k3cuda.check(lib.k3d_model_use_graph(model, 1))
-    exp_ms = sections.get("moe.experts", {}).get("ms_per_call", float("nan"))
+    exp_ms = sum(sections.get(k, {}).get("ms_per_call", float("nan"))
+                 for k in ("experts.gateup", "experts.down"))
     alg_exp = (TOPK * B) * (EXPERT_BYTES + INTER * 8 + HIDDEN * 4) + HIDDEN * 4 * B
     if world > 1:
         alg_exp /= world
@@ -461,7 +474,7 @@ def bench_stack(args, rank, world):
                    "layers 1-7 MoE 384x top-8 + shared", "vocab": 163840,
                    "parallelism": f"ep{world}", "graph": True,
                    "l2": f"per-step working set {step_bytes / 1e9:.2f} GB >> 126 MB L2"},
-        "roofline": {"kernel": "MXFP4 expert GEMV (k_mxfp4_mma gate/up + down)", "bound": "hbm",
+        "roofline": {"kernel": EXPERT_KERNEL[args.expert_kernel], "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": load_traffic("moe_experts_traffic.json"),
                      "alg_bytes_per_launch": alg_exp, "kernel_ms": exp_ms},
@@ -532,6 +545,8 @@ def main():
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bounded CPU-baseline sample length; 0 skips it")
+    ap.add_argument("--expert-kernel", type=int, default=0, choices=[0, 1, 2],
+                    help="0 tcgen05 block-scaled (default), 1 mma.sync, 2 CUDA cores")
     ap.add_argument("--n-experts", type=int, default=N_EXPERTS,
                     help="routed experts resident per layer (384 = config 1; fewer only for "
                          "profiling captures that must stay small)")

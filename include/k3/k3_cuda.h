@@ -140,6 +140,8 @@ typedef struct {
     int   expert_lo;       /* experts [expert_lo, expert_hi) are computed here */
     int   expert_hi;
     int   add_shared;      /* 1: this rank adds the shared expert (one rank under EP) */
+    int   expert_layout;   /* 0: checkpoint layout (p1,s1,p3,s3,p2,s2 as in the model
+                            *    files); 1: tiled (k3d_expert_pretile), tcgen05 kernel only */
 } K3dMoeShape;
 
 typedef struct {
@@ -157,6 +159,21 @@ size_t k3d_moe_ws_bytes(const K3dMoeShape *s, int T);
 int    k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s,
                       int T, int accumulate, int *idx, float *wts,
                       void *ws, size_t ws_bytes);
+/* Rewrites one expert into the tiled layout: the stage-ordered image of the tcgen05
+ * kernel's shared-memory tiles, so each pipeline stage is a few large bulk copies.
+ * dst->p1 / dst->s1 receive gate and up together (2*inter*hidden/2 and 2*inter*hidden/32
+ * bytes), dst->p2 / dst->s2 the down matrix (same sizes as src->p2 / src->s2); dst->p3
+ * and dst->s3 are unused. E8M0 255 becomes 0 (the CPU engine reads 255 as zero). hidden
+ * and inter must be multiples of 512. Device pointers; asynchronous on the library
+ * stream. Use with K3dMoeShape.expert_layout = 1. */
+int    k3d_expert_pretile(const K3ExpertQ *dst, const K3ExpertQ *src, int hidden, int inter);
+/* Which MXFP4 expert kernel k3d_expert_swiglu / k3d_moe_swiglu run: 0 (default) the
+ * tcgen05 block-scaled tensor-core kernel whenever the shapes allow it (hidden and inter
+ * multiples of 512, T * topk <= 64), 1 the mma.sync kernel, 2 the CUDA-core kernels.
+ * Experts in the tiled layout always run on the tcgen05 kernel.
+ * All three give the same results within the expert tolerance; the switch exists to
+ * measure and test each. */
+int    k3d_set_expert_kernel(int kind);
 /* The router alone on a bf16 W: idx/w [T][topk], device. */
 int    k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W,
                        const float *bias, int T, int hidden, int n_experts, int topk,

@@ -17,6 +17,8 @@
 //
 // Expert parallelism: only experts in [expert_lo, expert_hi) are computed here; the
 // combine treats the others as zero and the caller sums the partial outputs over ranks.
+#include <algorithm>
+
 #include "k3_mxfp4.cuh"
 #include "k3_moe.cuh"
 #include "k3_ops.cuh"
@@ -57,7 +59,7 @@ __global__ void __launch_bounds__(1024) k_moe_prep(const int *idx, int TK, int n
             if (cnt[e] > 0) { act_expert[u] = e; act_off[u] = off; u++; }
             off += cnt[e];
         }
-        if (lane == 31) { *n_active = iff; act_off[iff] = ic; }
+        if (lane == 31) { n_active[0] = iff; n_active[1] = ic; act_off[iff] = ic; }
     }
     __syncthreads();
     for (int a = threadIdx.x; a < TK; a += blockDim.x) {
@@ -158,9 +160,9 @@ __global__ void __launch_bounds__(256, 2) k_moe_down(float *contrib, const float
 }
 
 // ---- ordered combine ------------------------------------------------------------------
-__global__ void k_moe_combine(float *out, const float *contrib, const int *idx, const float *wts,
-                              const float *sh_out, int hidden, int K, int lo, int hi,
-                              int accumulate)
+__global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t slice_stride,
+                              const int *idx, const float *wts, const float *sh_out, int hidden,
+                              int K, int lo, int hi, int accumulate)
 {
     const int t = blockIdx.y;
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -170,7 +172,11 @@ __global__ void k_moe_combine(float *out, const float *contrib, const int *idx, 
         const int a = t * K + j;
         const int e = __ldg(idx + a);
         if (e < lo || e >= hi) continue;
-        acc = __fadd_rn(acc, __fmul_rn(__ldg(wts + a), contrib[(size_t)a * hidden + r]));
+        // the contribution, summed over the K slices of the down pass in slice order
+        const float *c = contrib + (size_t)a * hidden + r;
+        float v = c[0];
+        for (int s = 1; s < ks; s++) v += c[(size_t)s * slice_stride];
+        acc = __fadd_rn(acc, __fmul_rn(__ldg(wts + a), v));
     }
     if (sh_out) acc = __fadd_rn(acc, sh_out[(size_t)t * hidden + r]);
     float *o = out + (size_t)t * hidden + r;
@@ -243,27 +249,106 @@ static int launch_down(float *contrib, const float *act, const MoeWork &w, int h
 
 static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-// gate/up -> act -> down -> contrib for a work list, on tensor cores when the shapes
-// allow (hidden, inter multiples of 512) and on the CUDA-core kernels otherwise.
-static int run_experts(const MoeWork &mw, int umax, const float *x, int T, int TK, int hidden,
-                       int inter, float *act, float *contrib, __half *xb_x, float *xs_x,
-                       __half *xb_a, float *xs_a, cudaStream_t st)
+// Which expert kernel runs (k3d_set_expert_kernel): 0 chooses the tcgen05 block-scaled
+// kernel whenever the shapes allow, 1 forces the mma.sync kernel, 2 the CUDA-core kernels.
+static int g_expert_kernel = 0;
+static const int kUmmaMaxTK = 64;     // assignments per call for the tcgen05 path
+
+// Buffers of one run_experts call; the tcgen05 ones are null when the workspace has none.
+struct ExpertBufs {
+    float *act, *contrib;                  // CUDA-core / mma.sync: [TK][inter], [TK][hidden]
+    __half *xb_x; float *xs_x; __half *xb_a; float *xs_a;   // mma.sync activation splits
+    uint8_t *bq_x, *bs_x, *bq_a, *bs_a;    // tcgen05: E2M1 pieces of x and of act
+    float *part_gu, *part_d;               // tcgen05: K-slice partials
+};
+
+// Where the per-assignment contributions ended up: contrib[s * slice + a * hidden + r].
+struct ExpertOut {
+    const float *contrib;
+    int ks;
+    size_t slice;
+};
+
+static bool umma_shapes(int hidden, int inter)
 {
-    if (mma_supported(hidden, inter, 0) && mma_supported(inter, hidden, 1) && xb_x && xb_a) {
-        K3_TRY(xsplit(xb_x, xs_x, x, hidden, T, hidden, st));
-        K3_TRY(mxfp4_mma_launch(0, mw, umax, hidden, inter, xb_x, xs_x, 0, act, st));
-        K3_TRY(xsplit(xb_a, xs_a, act, inter, TK, inter, st));
-        return mxfp4_mma_launch(1, mw, umax, inter, hidden, xb_a, xs_a, 1, contrib, st);
+    return umma_supported(hidden, inter, 0) && umma_supported(inter, hidden, 1);
+}
+
+// The tcgen05 buffers exist in a workspace when the kernel can run: checkpoint-layout
+// experts up to kUmmaMaxTK assignments (beyond that the grouped mma.sync kernel reads each
+// expert once for all its tokens), tiled experts always.
+static bool umma_eligible(int hidden, int inter, int TK, int layout)
+{
+    return umma_shapes(hidden, inter) && (layout == 1 || TK <= kUmmaMaxTK);
+}
+
+// K slices the partial buffers are sized for: every stage up to kUmmaMaxTK assignments,
+// one slice beyond (there are enough items to fill the GPU without splitting K).
+static int umma_ks_cap(int K, int TK)
+{
+    return TK <= kUmmaMaxTK ? K / 512 : 1;
+}
+
+// gate/up -> act -> down -> contributions for a work list. tcgen05 block-scaled MMA
+// (k3_mxfp4_umma.cu) when the workspace carries its buffers and the kernel choice allows,
+// else the mma.sync kernel (k3_mxfp4_mma.cu), else the CUDA-core kernels. `count` is the
+// device count of local assignments (MoE) or null (single expert, one assignment).
+static int run_experts(const MoeWork &mw, const int *idx, const int *count, int umax,
+                       const float *x, int T, int TK, int hidden, int inter, int layout,
+                       const ExpertBufs &B, ExpertOut &O, cudaStream_t st)
+{
+    O.contrib = B.contrib;
+    O.ks = 1;
+    O.slice = 0;
+    const int topk = mw.single_mode ? 1 : mw.K;
+    if (layout == 1 && (!B.bq_x || !umma_eligible(hidden, inter, TK, 1)))
+        return fail(K3D_EINVAL, "tiled experts need hidden and inter multiples of 512");
+    if ((layout == 1 || g_expert_kernel == 0) && B.bq_x && umma_eligible(hidden, inter, TK, layout)) {
+        const int ks_gu = std::min(umma_slices(TK, hidden, inter, 0), umma_ks_cap(hidden, TK));
+        const int ks_d = std::min(umma_slices(TK, inter, hidden, 1), umma_ks_cap(inter, TK));
+        const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
+        K3_TRY(umma_bsplit(B.bq_x, B.bs_x, x, hidden, T, hidden, st));
+        prof_begin("experts.gateup");
+        K3_TRY(umma_launch(0, layout, mw, idx, count, TK, hidden, inter, ks_gu, B.bq_x, B.bs_x, topk,
+                           B.part_gu, 2 * inter, sl_gu, st));
+        prof_end("experts.gateup");
+        K3_TRY(umma_bsplit_swiglu(B.bq_a, B.bs_a, B.part_gu, ks_gu, sl_gu, inter,
+                                  mw.single_mode ? nullptr : mw.assign, count, TK, st));
+        prof_begin("experts.down");
+        K3_TRY(umma_launch(1, layout, mw, idx, count, TK, inter, hidden, ks_d, B.bq_a, B.bs_a, 1,
+                           B.part_d, hidden, sl_d, st));
+        prof_end("experts.down");
+        O.contrib = B.part_d;
+        O.ks = ks_d;
+        O.slice = sl_d;
+        return K3D_OK;
     }
-    K3_TRY(launch_gate_up(act, x, mw, hidden, inter, umax, st));
-    return launch_down(contrib, act, mw, hidden, inter, umax, st);
+    if (g_expert_kernel <= 1 && mma_supported(hidden, inter, 0) && mma_supported(inter, hidden, 1) &&
+        B.xb_x && B.xb_a) {
+        K3_TRY(xsplit(B.xb_x, B.xs_x, x, hidden, T, hidden, st));
+        prof_begin("experts.gateup");
+        K3_TRY(mxfp4_mma_launch(0, mw, umax, hidden, inter, B.xb_x, B.xs_x, 0, B.act, st));
+        prof_end("experts.gateup");
+        K3_TRY(xsplit(B.xb_a, B.xs_a, B.act, inter, TK, inter, st));
+        prof_begin("experts.down");
+        K3_TRY(mxfp4_mma_launch(1, mw, umax, inter, hidden, B.xb_a, B.xs_a, 1, B.contrib, st));
+        prof_end("experts.down");
+        return K3D_OK;
+    }
+    prof_begin("experts.gateup");
+    K3_TRY(launch_gate_up(B.act, x, mw, hidden, inter, umax, st));
+    prof_end("experts.gateup");
+    prof_begin("experts.down");
+    K3_TRY(launch_down(B.contrib, B.act, mw, hidden, inter, umax, st));
+    prof_end("experts.down");
+    return K3D_OK;
 }
 
 // Workspace carve-up for k3d_moe_swiglu.
 struct MoeWs {
     int *idx; float *wts; void *router; int *n_active; int *act_expert; int *act_off;
-    int *assign; float *act; float *contrib; float *sh_act; float *sh_out;
-    __half *xb_x; float *xs_x; __half *xb_a; float *xs_a;
+    int *assign; float *sh_act; float *sh_out;
+    ExpertBufs eb;
     size_t total;
 };
 
@@ -281,14 +366,27 @@ static MoeWs moe_ws_layout(const K3dMoeShape *s, int T, void *base)
     L.act_expert = (int *)take((size_t)s->n_experts * sizeof(int));
     L.act_off = (int *)take(((size_t)s->n_experts + 1) * sizeof(int));
     L.assign = (int *)take(TK * sizeof(int));
-    L.act = (float *)take(TK * s->inter * sizeof(float));
-    L.contrib = (float *)take(TK * s->hidden * sizeof(float));
+    L.eb.act = (float *)take(TK * s->inter * sizeof(float));
+    L.eb.contrib = (float *)take(TK * s->hidden * sizeof(float));
     L.sh_act = (float *)take((size_t)T * (s->shared_inter > 0 ? s->shared_inter : 1) * sizeof(float));
     L.sh_out = (float *)take((size_t)T * s->hidden * sizeof(float));
-    L.xb_x = (__half *)take((size_t)T * 2 * s->hidden * sizeof(__half));
-    L.xs_x = (float *)take((size_t)T * sizeof(float));
-    L.xb_a = (__half *)take(TK * 2 * s->inter * sizeof(__half));
-    L.xs_a = (float *)take(TK * sizeof(float));
+    L.eb.xb_x = (__half *)take((size_t)T * 2 * s->hidden * sizeof(__half));
+    L.eb.xs_x = (float *)take((size_t)T * sizeof(float));
+    L.eb.xb_a = (__half *)take(TK * 2 * s->inter * sizeof(__half));
+    L.eb.xs_a = (float *)take(TK * sizeof(float));
+    if (umma_eligible(s->hidden, s->inter, (int)TK, s->expert_layout)) {
+        L.eb.bq_x = (uint8_t *)take((size_t)T * umma_bq_bytes(s->hidden));
+        L.eb.bs_x = (uint8_t *)take((size_t)T * umma_bs_bytes(s->hidden));
+        L.eb.bq_a = (uint8_t *)take(TK * umma_bq_bytes(s->inter));
+        L.eb.bs_a = (uint8_t *)take(TK * umma_bs_bytes(s->inter));
+        L.eb.part_gu = (float *)take((size_t)umma_ks_cap(s->hidden, (int)TK) * TK * 2 * s->inter *
+                                     sizeof(float));
+        L.eb.part_d = (float *)take((size_t)umma_ks_cap(s->inter, (int)TK) * TK * s->hidden *
+                                    sizeof(float));
+    } else {
+        L.eb.bq_x = L.eb.bs_x = L.eb.bq_a = L.eb.bs_a = nullptr;
+        L.eb.part_gu = L.eb.part_d = nullptr;
+    }
     L.total = off;
     return L;
 }
@@ -308,6 +406,11 @@ static int check_shape(const K3dMoeShape *s, int T)
     if (s->n_experts > 8192) return fail(K3D_EINVAL, "MoE n_experts=%d > 8192", s->n_experts);
     if (s->shared_inter > 0 && (s->shared_inter % 8))
         return fail(K3D_EINVAL, "shared_inter=%d must be a multiple of 8", s->shared_inter);
+    if (s->expert_layout != 0 && s->expert_layout != 1)
+        return fail(K3D_EINVAL, "expert_layout=%d (0 checkpoint, 1 tiled)", s->expert_layout);
+    if (s->expert_layout == 1 && !umma_shapes(s->hidden, s->inter))
+        return fail(K3D_EINVAL, "tiled experts need hidden=%d and inter=%d multiples of 512",
+                    s->hidden, s->inter);
     return K3D_OK;
 }
 
@@ -315,6 +418,39 @@ static int check_shape(const K3dMoeShape *s, int T)
 // value survives the caller freeing its workspace)
 static int *g_last_unique_pinned = nullptr;
 static bool g_last_unique_valid = false;
+
+// Single-expert workspace: the mma.sync / CUDA-core buffers, then the tcgen05 ones.
+struct ExpertWs {
+    ExpertBufs eb;
+    size_t total;
+};
+
+static ExpertWs expert_ws_layout(int hidden, int inter, void *base)
+{
+    ExpertWs L;
+    size_t off = 0;
+    char *b = (char *)base;
+    auto take = [&](size_t bytes) { char *p = b + off; off += align256(bytes); return (void *)p; };
+    L.eb.act = (float *)take((size_t)inter * sizeof(float));
+    L.eb.contrib = nullptr;
+    L.eb.xb_x = (__half *)take((size_t)2 * hidden * sizeof(__half));
+    L.eb.xs_x = (float *)take(sizeof(float));
+    L.eb.xb_a = (__half *)take((size_t)2 * inter * sizeof(__half));
+    L.eb.xs_a = (float *)take(sizeof(float));
+    if (umma_eligible(hidden, inter, 1, 0)) {
+        L.eb.bq_x = (uint8_t *)take(umma_bq_bytes(hidden));
+        L.eb.bs_x = (uint8_t *)take(umma_bs_bytes(hidden));
+        L.eb.bq_a = (uint8_t *)take(umma_bq_bytes(inter));
+        L.eb.bs_a = (uint8_t *)take(umma_bs_bytes(inter));
+        L.eb.part_gu = (float *)take((size_t)(hidden / 512) * 2 * inter * sizeof(float));
+        L.eb.part_d = (float *)take((size_t)(inter / 512) * hidden * sizeof(float));
+    } else {
+        L.eb.bq_x = L.eb.bs_x = L.eb.bq_a = L.eb.bs_a = nullptr;
+        L.eb.part_gu = L.eb.part_d = nullptr;
+    }
+    L.total = off;
+    return L;
+}
 
 }  // namespace k3
 
@@ -324,9 +460,14 @@ extern "C" {
 
 size_t k3d_expert_ws_bytes(int hidden, int inter)
 {
-    return align256((size_t)inter * sizeof(float)) + align256((size_t)2 * hidden * sizeof(__half)) +
-           align256(sizeof(float)) + align256((size_t)2 * inter * sizeof(__half)) +
-           align256(sizeof(float)) + 256;
+    return expert_ws_layout(hidden, inter, nullptr).total + 256;
+}
+
+int k3d_set_expert_kernel(int kind)
+{
+    if (kind < 0 || kind > 2) return fail(K3D_EINVAL, "k3d_set_expert_kernel(%d): 0, 1 or 2", kind);
+    g_expert_kernel = kind;
+    return K3D_OK;
 }
 
 int k3d_expert_swiglu(float *y, const float *x, const K3ExpertQ *e, int hidden, int inter,
@@ -338,28 +479,21 @@ int k3d_expert_swiglu(float *y, const float *x, const K3ExpertQ *e, int hidden, 
         return fail(K3D_EINVAL, "k3d_expert_swiglu hidden=%d inter=%d", hidden, inter);
     if (ws_bytes < k3d_expert_ws_bytes(hidden, inter))
         return fail(K3D_EINVAL, "k3d_expert_swiglu workspace too small");
-    const uintptr_t al = (uintptr_t)e->p1 | (uintptr_t)e->p3 | (uintptr_t)e->p2 | (uintptr_t)x |
-                         (uintptr_t)ws;
+    const uintptr_t al = (uintptr_t)e->p1 | (uintptr_t)e->p3 | (uintptr_t)e->p2 | (uintptr_t)e->s1 |
+                         (uintptr_t)e->s3 | (uintptr_t)e->s2 | (uintptr_t)x | (uintptr_t)ws;
     if (al & 15u) return fail(K3D_EINVAL, "k3d_expert_swiglu pointers must be 16-byte aligned");
     MoeWork w{};
     w.single = *e;
     w.single_mode = 1;
     w.ntok_single = 1;
     w.K = 1;
-    char *b = (char *)ws;
-    float *act = (float *)b;
-    b += align256((size_t)inter * sizeof(float));
-    __half *xb_x = (__half *)b;
-    b += align256((size_t)2 * hidden * sizeof(__half));
-    float *xs_x = (float *)b;
-    b += align256(sizeof(float));
-    __half *xb_a = (__half *)b;
-    b += align256((size_t)2 * inter * sizeof(__half));
-    float *xs_a = (float *)b;
+    ExpertWs L = expert_ws_layout(hidden, inter, ws);
+    L.eb.contrib = y;      // the contribution of the single assignment is y itself
     cudaStream_t s = stream();
     prof_begin("expert.swiglu");
-    // the contribution of the single assignment is y itself
-    K3_TRY(run_experts(w, 1, x, 1, 1, hidden, inter, act, y, xb_x, xs_x, xb_a, xs_a, s));
+    ExpertOut O;
+    K3_TRY(run_experts(w, nullptr, nullptr, 1, x, 1, 1, hidden, inter, 0, L.eb, O, s));
+    if (O.contrib != y) K3_TRY(umma_slice_sum(y, O.contrib, O.ks, O.slice, hidden, s));
     prof_end("expert.swiglu");
     return K3D_OK;
 }
@@ -414,15 +548,16 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     mw.act_off = L.act_off;
     mw.assign = L.assign;
     mw.K = K;
+    ExpertOut O{L.eb.contrib, 1, 0};
     int umax = TK < (s->expert_hi - s->expert_lo) ? TK : (s->expert_hi - s->expert_lo);
     if (umax > 0) {
         prof_begin("moe.experts");
-        K3_TRY(run_experts(mw, umax, x, T, TK, s->hidden, s->inter, L.act, L.contrib, L.xb_x,
-                           L.xs_x, L.xb_a, L.xs_a, st));
+        K3_TRY(run_experts(mw, I, L.n_active + 1, umax, x, T, TK, s->hidden, s->inter,
+                           s->expert_layout, L.eb, O, st));
         prof_end("moe.experts");
     }
     dim3 grid((s->hidden + 255) / 256, T);
-    k_moe_combine<<<grid, 256, 0, st>>>(out, L.contrib, I, Wt, shared ? L.sh_out : nullptr,
+    k_moe_combine<<<grid, 256, 0, st>>>(out, O.contrib, O.ks, O.slice, I, Wt, shared ? L.sh_out : nullptr,
                                         s->hidden, K, s->expert_lo, s->expert_hi, accumulate);
     note_launch();
     K3_TRY(check_launch("moe combine"));

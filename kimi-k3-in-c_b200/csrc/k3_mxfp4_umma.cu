@@ -1,0 +1,799 @@
+// k3_mxfp4_umma.cu -- the MXFP4 expert GEMV on the fifth-generation tensor cores:
+// tcgen05.mma.kind::mxf4.block_scale.block32 (E2M1 x E2M1 with one UE8M0 scale per 32
+// elements on each operand, fp32 accumulation in tensor memory).
+//
+// WHAT IT COMPUTES: for each routed (token, expert) assignment, the gate/up rows of the
+// expert against the token's activation (k3_ops.c:1380-1785 for the MXFP4 dot, 628-630
+// for SwiGLU), then the down rows against silu(gate) * up. Weights are read in the
+// checkpoint layout (codes [rows][in/2], low nibble = even element; scales [rows][in/32]),
+// so no repacking step exists.
+//
+// THE ACTIVATION OPERAND. The tensor core takes B in E2M1 too, so each fp32 activation
+// vector is written as a sum of 16 E2M1 "pieces" with their own per-32 E8M0 scales:
+//   r_0 = x;  piece p = round_to_E2M1(r_p / 2^s_p) with s_p the smallest exponent that
+//   fits the block maximum of |r_p| into [0, 6];  r_{p+1} = r_p - piece_p * 2^s_p.
+// Every step is exact in fp32 (a power-of-two scaling, and a subtraction of the nearest
+// grid point, which Sterbenz's lemma makes exact), and each piece shrinks the block
+// maximum by at least 3x, so 16 pieces leave a residual below 3^-16 ~ 2e-8 of the block
+// maximum. The 16 pieces are the 16 columns of B (N = 16): one MMA produces the 16
+// partial dot products of a 128-row tile, and the epilogue adds them. E8M0 code 255 in the
+// weights (NaN to the hardware) is replaced by 0 (2^-127) on its way to tensor memory; the
+// CPU engine treats 255 as zero, and 2^-127 * 6 * |piece| is below any fp32 output ulp.
+//
+// DATA MOVEMENT AND ROLES (one CTA per SM, 9 warps):
+//   warps 0-3  producers: cp.async 16-byte copies of the weight tile (128 rows x 512
+//              K-elements per stage) and of the B tile into the SWIZZLE_128B K-major
+//              layout the MMA descriptors describe, and of the scale rows. Nothing in
+//              the loop waits on memory: a thread publishes a stage three stages later,
+//              once its copies for it have landed (cp.async.wait_group), after moving its
+//              scale row, cleaned of 255, into the 32x16-byte atom tcgen05.cp reads and
+//              fencing the stage for the tensor core's proxy.
+//   warp 4     allocates 128 tensor-memory columns; one thread issues tcgen05.cp (scales)
+//              and tcgen05.mma (8 MMAs of K = 64 per stage) and commits stage release and
+//              accumulator completion to mbarriers.
+//   warps 5-8  epilogue: tcgen05.ld of the 128 x 16 accumulator (two buffers, so the
+//              epilogue of one item overlaps the MMAs of the next), the piece sum, and the
+//              store of the partial result.
+// Work items are (assignment, 128-row tile, K slice); K slices are summed in a fixed order
+// by the consumer (no atomics, results are deterministic). Every mbarrier wait is bounded:
+// on timeout the kernel stores K3D_ETIMEOUT in the device error flag, all roles leave
+// their loops, outstanding copies and MMAs are drained, and tensor memory is freed.
+#include "k3_moe.cuh"
+#include "k3_ops.cuh"
+
+namespace k3 {
+namespace umma {
+
+constexpr int kStageK = 512;                 // K elements per stage
+constexpr int kRowBytes = kStageK / 2;       // packed bytes of one row per stage
+constexpr int kN = 16;                       // B columns (pieces)
+constexpr int kOffB = 128 * kRowBytes;       // 32768: A is 2 SW128 blocks of 128 x 128 B
+constexpr int kOffSFA = kOffB + kN * kRowBytes;  // 36864
+constexpr int kOffSFB = kOffSFA + 4 * 512;       // 38912
+constexpr int kOffRawA = kOffSFB + 4 * 512;      // 40960: scale rows as loaded, 128 x 16 B
+constexpr int kStageBytes = kOffRawA + 128 * 16;  // 43008 (multiple of 1024)
+constexpr int kTileA = 32768, kTileSF = 2048, kTileB = 4096;   // tiled-layout units per stage
+constexpr uint32_t kStageTx = kTileA + kTileSF + kTileB + kTileSF;
+constexpr int kStages = 5;
+constexpr int kLag = 3;                      // producer publishes a stage kLag stages later
+constexpr int kProducers = 128;
+constexpr int kThreads = 288;
+constexpr int kTmemCols = 128;               // acc 4 x 16 @0, SFA 2 x 16 @64, SFB 2 x 16 @96
+constexpr uint32_t kSfaCol = 64, kSfbCol = 96;
+constexpr long long kSpinLimit = 4000000000LL;   // ~2 s at 1.9 GHz
+
+enum { GATEUP = 0, DOWN = 1 };
+
+struct Job {
+    const K3ExpertQ *table;
+    K3ExpertQ single;
+    int single_mode;
+    const int *assign;       // grouped position -> assignment id (MoE mode)
+    const int *idx;          // [assignments] expert id
+    const int *count;        // device count of local assignments (MoE), else null
+    int count_host;          // count when `count` is null
+    int mode;
+    int K;                   // reduction length
+    int ntiles;              // gate/up: inter / 64; down: rows / 128
+    int ks;                  // K slices per tile
+    int cps;                 // stages per slice
+    int nch;                 // stages along the whole K (K / 512)
+    int tiled;               // 1: experts in the tiled layout (k3d_expert_pretile)
+    const uint8_t *bq;       // B pieces [vec][16][K/2]
+    const uint8_t *bs;       // B scales [vec][16][K/32]
+    int vec_div;             // vector of assignment a = a / vec_div
+    float *part;             // [ks][cap][out_w]
+    int out_w;               // gate/up: 2 * inter (gate rows then up rows); down: rows
+    size_t slice_stride;     // floats per K slice
+};
+
+__device__ __forceinline__ uint32_t saddr(const void *p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t b, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(b), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(b) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(b), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false when it gave up (time limit, or another role already aborted).
+__device__ __forceinline__ bool mbar_wait(uint32_t b, uint32_t parity, volatile int *abort)
+{
+    if (mbar_try(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(b, parity)) {
+        if (*abort) return false;
+        if (clock64() - t0 > kSpinLimit) {
+            k3_raise(K3D_ETIMEOUT, K3_SITE_MXFP4);
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(b), "r"(bytes) : "memory");
+}
+
+// 1-D bulk copy global -> shared, completing on an mbarrier (no multicast)
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+// Bounded wait that ignores the abort flag: used to drain in-flight tensor-core work
+// before tensor memory is freed.
+__device__ __forceinline__ void mbar_drain(uint32_t b, uint32_t parity)
+{
+    const long long t0 = clock64();
+    while (!mbar_try(b, parity)) {
+        if (clock64() - t0 > kSpinLimit) { k3_raise(K3D_ETIMEOUT, K3_SITE_MXFP4); return; }
+    }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major SWIZZLE_128B: 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t a)
+{
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Descriptor of one 32-row x 16-byte scale atom (no swizzle; 8-row groups 128 B apart).
+__device__ __forceinline__ uint64_t desc_sf(uint32_t a)
+{
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+}
+
+// Instruction descriptor: kind::mxf4, A and B E2M1 (format 1), UE8M0 scales, K-major
+// operands, M = 128, N = 16, scale-factor byte ids for A and B.
+__device__ __forceinline__ uint32_t idesc_mxf4(uint32_t sf_id)
+{
+    return (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) | (1u << 23) |
+           ((uint32_t)(128 >> 4) << 24) | (sf_id << 29) | (sf_id << 4);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accum, uint32_t sfa, uint32_t sfb)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+                 :: "r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum), "r"(sfa), "r"(sfb)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc)
+{
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" :: "r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16])
+{
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                   "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 0xFF bytes (E8M0 NaN) -> 0x00, bytewise on a 32-bit word
+__device__ __forceinline__ uint32_t clean_e8m0(uint32_t w)
+{
+    const uint32_t lo7 = w & 0x7F7F7F7Fu;
+    const uint32_t ff = ((lo7 + 0x01010101u) & w) & 0x80808080u;   // high bit set iff byte == 0xFF
+    const uint32_t mask = (ff >> 7) * 0xFFu;
+    return w & ~mask;
+}
+
+// Once this thread's copies for a stage have landed (checkpoint layout only): move its
+// scale row into the 32x16-byte atom tcgen05.cp reads (row m of the 128-row operand at
+// byte 16*(m%32) + 4*(m/32), blocks 4a..4a+3 in atom a), cleaned of 255, then make the
+// stage's shared-memory writes visible to the tensor core.
+__device__ __forceinline__ void publish(unsigned char *st, int tid)
+{
+    const uint4 v = *reinterpret_cast<const uint4 *>(st + kOffRawA + 16 * tid);
+    uint32_t *atom = reinterpret_cast<uint32_t *>(st + kOffSFA + 16 * (tid & 31) + 4 * (tid >> 5));
+    atom[0] = clean_e8m0(v.x);
+    atom[128] = clean_e8m0(v.y);
+    atom[256] = clean_e8m0(v.z);
+    atom[384] = clean_e8m0(v.w);
+    fence_async_smem();
+}
+
+// One work item as the roles need it, resolved once per round into shared memory so
+// that no role's loop waits on a dependent chain of global loads (assignment -> expert id
+// -> expert table entry).
+struct ItemEnt {
+    const uint8_t *c0, *c1, *s0, *s1;   // weight codes / scales (gate and up, or down twice)
+    int a;                              // assignment
+    int tile, s;                        // 128-row tile, K slice
+    int vec;                            // B operand vector
+};
+static_assert(sizeof(ItemEnt) == 48, "item entry size");
+constexpr int kMaxItems = 128;          // table entries per round
+constexpr int kOffItems = 1024;         // after the barrier header
+constexpr int kStage0 = kOffItems + kMaxItems * 48;   // 7168, 1024-aligned
+constexpr int kAccBufs = 4;             // accumulator ring depth
+constexpr size_t kSmemTotal = 1024 + kStage0 + (size_t)kStages * kStageBytes;
+
+__device__ __forceinline__ ItemEnt decode(const Job &J, int item)
+{
+    ItemEnt it;
+    it.s = item % J.ks;
+    const int rest = item / J.ks;
+    it.tile = rest % J.ntiles;
+    const int p = rest / J.ntiles;
+    K3ExpertQ q;
+    if (J.single_mode) {
+        it.a = p;
+        q = J.single;
+    } else {
+        it.a = __ldg(J.assign + p);
+        q = J.table[__ldg(J.idx + it.a)];
+    }
+    if (J.mode == GATEUP) { it.c0 = q.p1; it.c1 = q.p3; it.s0 = q.s1; it.s1 = q.s3; }
+    else { it.c0 = it.c1 = q.p2; it.s0 = it.s1 = q.s2; }
+    it.vec = it.a / J.vec_div;
+    return it;
+}
+
+__device__ __forceinline__ int item_count(const Job &J)
+{
+    const int n = J.count ? *(volatile const int *)J.count : J.count_host;
+    return n * J.ntiles * J.ks;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
+{
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-aligned base (the SWIZZLE_128B pattern is a function of the absolute address)
+    const uint32_t raw = saddr(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char *gbase = smem_raw + (base - raw);
+    // header: barriers, abort flag, tensor-memory address slot
+    const uint32_t b_full = base;                       // [kStages] x 8
+    const uint32_t b_empty = base + 8 * kStages;        // [kStages] x 8
+    const uint32_t b_accf = base + 16 * kStages;        // [kAccBufs] x 8
+    const uint32_t b_acce = b_accf + 8 * kAccBufs;      // [kAccBufs] x 8
+    const uint32_t b_drain = b_acce + 8 * kAccBufs;
+    volatile int *abort = reinterpret_cast<volatile int *>(gbase + 512);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + 520);
+    ItemEnt *items = reinterpret_cast<ItemEnt *>(gbase + kOffItems);
+    const uint32_t stage0 = base + kStage0;
+    unsigned char *gstage0 = gbase + kStage0;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(b_full + 8 * s, J.tiled ? 1 : kProducers);
+            mbar_init(b_empty + 8 * s, 1);
+        }
+        for (int i = 0; i < kAccBufs; i++) { mbar_init(b_accf + 8 * i, 1); mbar_init(b_acce + 8 * i, 4); }
+        mbar_init(b_drain, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(saddr(tmem_slot)), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int total = item_count(J);
+    const int i_beg = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int i_end = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    const int rowbytes = J.K >> 1;
+    const int sfrow = J.K >> 5;
+
+    // pipeline positions, carried across rounds
+    int g_prod = 0;      // stages issued by this producer thread
+    int g_mma = 0;       // stages consumed by the MMA thread
+    int n_mma = 0;       // items issued by the MMA thread
+    int n_epi = 0;       // items finished by this epilogue warp
+    bool stop = false;
+
+    for (int r0 = i_beg; r0 < i_end; r0 += kMaxItems) {
+        const int r1 = min(i_end, r0 + kMaxItems);
+        for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) items[i - r0] = decode(J, i);
+        __syncthreads();
+        const int nr = r1 - r0;
+
+        if (warp < 4 && J.tiled) {
+            // ------------------------------------------ producer, tiled layout: one thread
+            // streams each stage as four bulk copies (weight tile, its scale atoms, the B
+            // tile and its scale atoms), all completing on the stage's mbarrier
+            if (threadIdx.x == 0) {
+                for (int k = 0; k < nr && !stop; k++) {
+                    const ItemEnt &it = items[k];
+                    const bool aligned = ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) == 0);
+                    if (!aligned) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
+                    const size_t vbase = (size_t)it.vec * J.nch;
+                    for (int c = 0; c < J.cps; c++) {
+                        const int chunk = it.s * J.cps + c;
+                        const int st = g_prod % kStages;
+                        if (g_prod >= kStages &&
+                            !mbar_wait(b_empty + 8 * st, ((g_prod / kStages) - 1) & 1, abort)) {
+                            stop = true;
+                            break;
+                        }
+                        const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
+                        const uint32_t fb = b_full + 8 * st;
+                        const size_t tix = (size_t)it.tile * J.nch + chunk;
+                        if (aligned) {
+                            mbar_expect_tx(fb, kStageTx);
+                            bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
+                            bulk_g2s(sb + kOffSFA, it.s0 + tix * kTileSF, kTileSF, fb);
+                            bulk_g2s(sb + kOffB, J.bq + (vbase + chunk) * kTileB, kTileB, fb);
+                            bulk_g2s(sb + kOffSFB, J.bs + (vbase + chunk) * kTileSF, kTileSF, fb);
+                        } else {
+                            mbar_arrive(fb);
+                        }
+                        g_prod++;
+                    }
+                }
+            }
+        } else if (warp < 4) {
+            // -------------------------- producers, checkpoint layout: 128 threads, cp.async
+            const int tid = threadIdx.x;
+            const int g_round = g_prod;          // stages of this round are published here
+            for (int k = 0; k < nr && !stop; k++) {
+                const ItemEnt &it = items[k];
+                const int r0w = J.mode == GATEUP ? it.tile * 64 : it.tile * 128;
+                const bool aligned = ((((uintptr_t)it.c0 | (uintptr_t)it.c1 | (uintptr_t)it.s0 |
+                                        (uintptr_t)it.s1) & 15u) == 0);
+                if (!aligned && tid == 0) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
+                const size_t vbase = (size_t)it.vec * J.nch;
+                for (int c = 0; c < J.cps; c++) {
+                    const int chunk = it.s * J.cps + c;
+                    const int st = g_prod % kStages;
+                    if (g_prod >= kStages &&
+                        !mbar_wait(b_empty + 8 * st, ((g_prod / kStages) - 1) & 1, abort)) {
+                        stop = true;
+                        break;
+                    }
+                    const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
+                    if (aligned) {
+                        // A: 128 rows x 16 chunks of 16 B into the SWIZZLE_128B layout; a
+                        // warp reads 2 full row segments
+#pragma unroll 4
+                        for (int i = 0; i < 16; i++) {
+                            const int qd = tid + kProducers * i;
+                            const int r = qd >> 4, j = qd & 15;
+                            const uint8_t *src_row = (J.mode == GATEUP && r >= 64)
+                                ? it.c1 + (size_t)(r0w + r - 64) * rowbytes
+                                : it.c0 + (size_t)(r0w + r) * rowbytes;
+                            const uint32_t dst = sb + (uint32_t)((j >> 3) * 16384 + (r >> 3) * 1024 +
+                                                                 (r & 7) * 128 + (((j & 7) ^ (r & 7)) << 4));
+                            cp_async16(dst, src_row + (size_t)chunk * kRowBytes + j * 16);
+                        }
+                        // B tile and its scale atoms are stored ready-made: straight copies
+                        const uint8_t *btile = J.bq + (vbase + chunk) * kTileB;
+                        const uint8_t *bsf = J.bs + (vbase + chunk) * kTileSF;
+                        cp_async16(sb + kOffB + 16 * tid, btile + 16 * tid);
+                        cp_async16(sb + kOffB + 16 * (tid + kProducers), btile + 16 * (tid + kProducers));
+                        cp_async16(sb + kOffSFB + 16 * tid, bsf + 16 * tid);
+                        // the scale row as it is in memory; rearranged when the stage is
+                        // published (below), so no load blocks this loop
+                        const uint8_t *srow = (J.mode == GATEUP && tid >= 64)
+                            ? it.s1 + (size_t)(r0w + tid - 64) * sfrow
+                            : it.s0 + (size_t)(r0w + tid) * sfrow;
+                        cp_async16(sb + kOffRawA + 16 * tid, srow + (size_t)chunk * 16);
+                    }
+                    cp_commit();
+                    if (g_prod - g_round >= kLag) {
+                        cp_wait<kLag>();
+                        publish(gstage0 + (size_t)((g_prod - kLag) % kStages) * kStageBytes, tid);
+                        mbar_arrive(b_full + 8 * ((g_prod - kLag) % kStages));
+                    }
+                    g_prod++;
+                }
+            }
+            // publish the round's last stages before the round barrier
+            cp_wait_all();
+            const int h0 = max(g_round, g_prod - kLag);
+            for (int h = h0; h < g_prod; h++) {
+                publish(gstage0 + (size_t)(h % kStages) * kStageBytes, tid);
+                mbar_arrive(b_full + 8 * (h % kStages));
+            }
+        } else if (warp == 4) {
+            // ----------------------------------------------------------- MMA issuer
+            if (lane == 0) {
+                for (int k = 0; k < nr && !stop; k++, n_mma++) {
+                    const int buf = n_mma % kAccBufs;
+                    if (n_mma >= kAccBufs &&
+                        !mbar_wait(b_acce + 8 * buf, ((n_mma / kAccBufs) - 1) & 1, abort)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t dcol = tmem + (uint32_t)(buf * kN);
+                    for (int c = 0; c < J.cps; c++) {
+                        const int st = g_mma % kStages;
+                        if (!mbar_wait(b_full + 8 * st, (g_mma / kStages) & 1, abort)) { stop = true; break; }
+                        tc_fence_after();
+                        const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
+                        const uint32_t sfa = tmem + kSfaCol + (uint32_t)((g_mma & 1) * 16);
+                        const uint32_t sfb = tmem + kSfbCol + (uint32_t)((g_mma & 1) * 16);
+#pragma unroll
+                        for (int a4 = 0; a4 < 4; a4++) {
+                            tc_cp_sf(sfa + 4 * a4, desc_sf(sb + kOffSFA + 512 * a4));
+                            tc_cp_sf(sfb + 4 * a4, desc_sf(sb + kOffSFB + 512 * a4));
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
+                            const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
+                            const uint64_t bd = desc_sw128(sb + kOffB + kb * 2048u + off);
+                            const uint32_t id = (uint32_t)((j & 1) * 2);
+                            const uint32_t atom = (uint32_t)(4 * (j >> 1));
+                            tc_mma(dcol, ad, bd, idesc_mxf4(id), (c > 0 || j > 0) ? 1u : 0u,
+                                   (sfa + atom) | (id << 30), (sfb + atom) | (id << 30));
+                        }
+                        tc_commit(b_empty + 8 * st);
+                        g_mma++;
+                    }
+                    if (!stop) tc_commit(b_accf + 8 * buf);
+                }
+            }
+            __syncwarp();
+        } else {
+            // ------------------------------------------------------------- epilogue
+            const int q = warp & 3;                 // tensor-memory lane quadrant of this warp
+            const int m = q * 32 + lane;            // tile row
+            for (int k = 0; k < nr; k++, n_epi++) {
+                const ItemEnt &it = items[k];
+                int row;
+                if (J.mode == GATEUP) row = m < 64 ? it.tile * 64 + m : (J.out_w >> 1) + it.tile * 64 + (m - 64);
+                else row = it.tile * 128 + m;
+                float *dst = J.part + (size_t)it.s * J.slice_stride + (size_t)it.a * J.out_w + row;
+                const int buf = n_epi % kAccBufs;
+                if (!mbar_wait(b_accf + 8 * buf, (n_epi / kAccBufs) & 1, abort)) break;
+                tc_fence_after();
+                float v[16];
+                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kN), v);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b_acce + 8 * buf);
+                float sum = v[15];
+#pragma unroll
+                for (int i = 14; i >= 0; i--) sum += v[i];
+                *dst = sum;
+            }
+        }
+        __syncthreads();          // every role is done with this round's table
+    }
+    if (warp == 4 && lane == 0) {
+        // every MMA and copy issued above has completed once this barrier flips
+        tc_commit(b_drain);
+        mbar_drain(b_drain, 0);
+    }
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                     :: "r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- activation split
+// The B operand of one vector, stored ready for the kernel's stages: for each 512-element
+// chunk c, a 4 KB tile (16 piece rows x 256 bytes in the SWIZZLE_128B K-major layout) at
+// bq + 4096 c, and 4 scale atoms at bs + 2048 c (piece p's scale for block 4a+i at byte
+// 512 a + 16 p + i; every other byte of an atom is zero).
+__device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, int blk, int lane)
+{
+    const float grid[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const int c = blk >> 4, j = blk & 15;
+    uint8_t *tile = bq + (size_t)c * kTileB + (j >> 3) * 2048;
+    uint8_t *atom = bs + (size_t)c * kTileSF + ((j & 15) >> 2) * 512;
+    if ((j & 3) == 0) {
+        // the zero bytes of this atom (its data bytes are written below by 4 blocks)
+        if (lane < 16) {
+            uint32_t *z = reinterpret_cast<uint32_t *>(atom + 16 * lane + 4);
+            z[0] = 0u; z[1] = 0u; z[2] = 0u;
+        } else {
+            *reinterpret_cast<uint4 *>(atom + 256 + 16 * (lane - 16)) = make_uint4(0, 0, 0, 0);
+        }
+    }
+    for (int p = 0; p < kN; p++) {
+        const bool bad = __any_sync(0xffffffffu, !isfinite(r));
+        const float m = warp_max(fabsf(r));
+        int code;
+        if (bad) code = 255;
+        else if (m == 0.0f) code = 127;
+        else {
+            const int e = ilogbf(m);
+            int sx = (m <= ldexpf(1.5f, e)) ? e - 2 : e - 1;
+            sx = max(-127, min(127, sx));
+            code = sx + 127;
+        }
+        uint32_t nib = 0;
+        if (code != 255) {
+            const float inv = ldexpf(1.0f, 127 - code);
+            const float a = fabsf(r) * inv;
+            const uint32_t q3 = a < 0.25f ? 0u : a < 0.75f ? 1u : a < 1.25f ? 2u : a < 1.75f ? 3u
+                              : a < 2.5f ? 4u : a < 3.5f ? 5u : a < 5.0f ? 6u : 7u;
+            const float val = ldexpf(grid[q3], code - 127);
+            nib = q3 | (signbit(r) && q3 ? 8u : 0u);
+            r = signbit(r) ? r + val : r - val;
+        }
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 1);
+        if ((lane & 1) == 0)
+            tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] =
+                (uint8_t)(nib | (hi << 4));
+        if (lane == 0) atom[16 * p + (j & 3)] = (uint8_t)code;
+    }
+}
+
+// B operands of fp32 vectors: grid (ceil(K/32 / 8), nvec), 256 threads, a warp per block.
+__global__ void k_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, size_t ld)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int blk = blockIdx.x * 8 + warp;
+    if (blk >= K / 32) return;
+    const int v = blockIdx.y;
+    const int nch = K / kStageK;
+    const float r = x[(size_t)v * ld + blk * 32 + lane];
+    split_block(bq + (size_t)v * nch * kTileB, bs + (size_t)v * nch * kTileSF, r, blk, lane);
+}
+
+// B operands of act = silu(gate) * up, gate/up summed over the K slices of the gate/up
+// pass in slice order. grid (ceil(inter/32 / 8), assignment positions).
+__global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks,
+                                size_t slice_stride, int inter, const int *assign,
+                                const int *count, int count_host)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int blk = blockIdx.x * 8 + warp;
+    const int p = blockIdx.y;
+    const int n = count ? *count : count_host;
+    if (blk >= inter / 32 || p >= n) return;
+    const int a = assign ? __ldg(assign + p) : p;
+    const float *pa = part + (size_t)a * 2 * inter;
+    const int i = blk * 32 + lane;
+    float g = 0.0f, u = 0.0f;
+    for (int s = 0; s < ks; s++) {
+        g += pa[(size_t)s * slice_stride + i];
+        u += pa[(size_t)s * slice_stride + inter + i];
+    }
+    const float act = silu_f(g) * u;
+    const int nch = inter / kStageK;
+    split_block(bq + (size_t)a * nch * kTileB, bs + (size_t)a * nch * kTileSF, act, blk, lane);
+}
+
+// ------------------------------------------------------------- weight tiling
+// Rewrites MXFP4 weights from the checkpoint layout into the stage-ordered tiled layout:
+// for 128-row tile t and 512-element chunk c, a 32 KB block at codes + 32768 (t * nch + c)
+// holding the tile's codes exactly as the kernel's shared-memory stage (SWIZZLE_128B
+// K-major), and a 2 KB block at sf + 2048 (t * nch + c) holding its scales as the four
+// tcgen05.cp atoms, with E8M0 255 replaced by 0. Gate/up tiles interleave 64 gate rows and
+// the same 64 up rows (c1/s1 given); down tiles are 128 rows of one matrix (c1 null).
+// grid (ntiles * nch), 256 threads.
+__global__ void k_pretile(uint8_t *dc, uint8_t *ds, const uint8_t *c0, const uint8_t *s0,
+                          const uint8_t *c1, const uint8_t *s1, int K)
+{
+    const int nch = K / kStageK;
+    const int t = blockIdx.x / nch, c = blockIdx.x % nch;
+    const int rowbytes = K >> 1, sfrow = K >> 5;
+    const bool gu = c1 != nullptr;
+    uint8_t *dtile = dc + (size_t)blockIdx.x * kTileA;
+    for (int q = threadIdx.x; q < 2048; q += blockDim.x) {
+        const int r = q >> 4, j = q & 15;
+        const uint8_t *row = gu ? (r < 64 ? c0 + (size_t)(t * 64 + r) * rowbytes
+                                          : c1 + (size_t)(t * 64 + r - 64) * rowbytes)
+                                : c0 + (size_t)(t * 128 + r) * rowbytes;
+        const uint4 v = *reinterpret_cast<const uint4 *>(row + (size_t)c * kRowBytes + 16 * j);
+        *reinterpret_cast<uint4 *>(dtile + (j >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 +
+                                   (((j & 7) ^ (r & 7)) << 4)) = v;
+    }
+    if (threadIdx.x < 128) {
+        const int r = threadIdx.x;
+        const uint8_t *srow = gu ? (r < 64 ? s0 + (size_t)(t * 64 + r) * sfrow
+                                           : s1 + (size_t)(t * 64 + r - 64) * sfrow)
+                                 : s0 + (size_t)(t * 128 + r) * sfrow;
+        const uint4 v = *reinterpret_cast<const uint4 *>(srow + (size_t)c * 16);
+        uint32_t *atom = reinterpret_cast<uint32_t *>(ds + (size_t)blockIdx.x * kTileSF +
+                                                      16 * (r & 31) + 4 * (r >> 5));
+        atom[0] = clean_e8m0(v.x);
+        atom[128] = clean_e8m0(v.y);
+        atom[256] = clean_e8m0(v.z);
+        atom[384] = clean_e8m0(v.w);
+    }
+}
+
+// y[r] = sum over K slices of part[s][r] (single-expert mode)
+__global__ void k_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n)
+{
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    float acc = 0.0f;
+    for (int s = 0; s < ks; s++) acc += part[(size_t)s * slice_stride + r];
+    y[r] = acc;
+}
+
+}  // namespace umma
+
+using namespace umma;
+
+bool umma_supported(int K, int rows, int mode)
+{
+    if (K % kStageK != 0 || K < kStageK || K > 16384) return false;
+    return mode == GATEUP ? (rows % 64 == 0) : (rows % 128 == 0);
+}
+
+// K slices for `units` assignments: the divisor of the stage count that minimises the
+// estimated time (rounds of items over the SMs x bytes per item, plus a fixed per-item
+// cost for the accumulator hand-off and the partial-sum write and read).
+int umma_slices(int units, int K, int rows, int mode)
+{
+    const int chunks = K / kStageK;
+    const int ntiles = mode == GATEUP ? rows / 64 : rows / 128;
+    const int G = sm_count();
+    int best = 1;
+    double best_cost = 1e30;
+    for (int d = 1; d <= chunks; d++) {
+        if (chunks % d) continue;
+        const long long items = (long long)units * ntiles * d;
+        const long long rounds = (items + G - 1) / G;
+        const double item_bytes = 128.0 * (K / d) * 0.53125 + 2048.0;
+        const double cost = (double)rounds * item_bytes;
+        if (cost < best_cost * 0.999) { best_cost = cost; best = d; }
+    }
+    return best;
+}
+
+size_t umma_bq_bytes(int K) { return (size_t)(K / kStageK) * kTileB; }
+size_t umma_bs_bytes(int K) { return (size_t)(K / kStageK) * kTileSF; }
+
+int umma_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, int nvec, size_t ld,
+                cudaStream_t st)
+{
+    if (nvec <= 0) return K3D_OK;
+    dim3 grid((K / 32 + 7) / 8, nvec);
+    k_bsplit<<<grid, 256, 0, st>>>(bq, bs, x, K, ld);
+    note_launch();
+    return check_launch("umma bsplit");
+}
+
+int umma_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride,
+                       int inter, const int *assign, const int *count, int npos, cudaStream_t st)
+{
+    if (npos <= 0) return K3D_OK;
+    dim3 grid((inter / 32 + 7) / 8, npos);
+    k_bsplit_swiglu<<<grid, 256, 0, st>>>(bq, bs, part, ks, slice_stride, inter, assign, count, npos);
+    note_launch();
+    return check_launch("umma bsplit swiglu");
+}
+
+int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n, cudaStream_t st)
+{
+    k_slice_sum<<<(n + 255) / 256, 256, 0, st>>>(y, part, ks, slice_stride, n);
+    note_launch();
+    return check_launch("umma slice sum");
+}
+
+// Launch over `npos_max` assignment positions (the device count, when given, may be
+// smaller). MoE mode: w.table/assign/idx; single mode: w.single_mode with positions 0..n-1.
+int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
+                int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
+                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st)
+{
+    if (!umma_supported(K, rows, mode)) return fail(K3D_EINVAL, "umma: unsupported K=%d rows=%d", K, rows);
+    const int chunks = K / kStageK;
+    if (ks < 1 || chunks % ks) return fail(K3D_EINVAL, "umma: %d slices of %d stages", ks, chunks);
+    Job J;
+    J.table = w.table;
+    J.single = w.single;
+    J.single_mode = w.single_mode;
+    J.assign = w.assign;
+    J.idx = idx;
+    J.count = count;
+    J.count_host = npos_max;
+    J.mode = mode;
+    J.K = K;
+    J.ntiles = mode == GATEUP ? rows / 64 : rows / 128;
+    J.ks = ks;
+    J.cps = chunks / ks;
+    J.nch = chunks;
+    J.tiled = tiled;
+
+    J.bq = bq;
+    J.bs = bs;
+    J.vec_div = vec_div;
+    J.part = part;
+    J.out_w = out_w;
+    J.slice_stride = slice_stride;
+    static bool init = false;
+    if (!init) {
+        cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kSmemTotal);
+        if (e != cudaSuccess) return fail(K3D_ECUDA, "umma smem attribute: %s", cudaGetErrorString(e));
+        init = true;
+    }
+    const long long items = (long long)npos_max * J.ntiles * ks;
+    if (items <= 0) return K3D_OK;
+    const int grid = (int)(items < sm_count() ? items : sm_count());
+    k_mxfp4_umma<<<grid, kThreads, kSmemTotal, st>>>(J);
+    note_launch();
+    return check_launch("mxfp4 umma");
+}
+
+}  // namespace k3
+
+using namespace k3;
+
+extern "C" {
+
+int k3d_expert_pretile(const K3ExpertQ *dst, const K3ExpertQ *src, int hidden, int inter)
+{
+    K3_TRY(ensure_ctx());
+    if (!dst || !src) return fail(K3D_EINVAL, "k3d_expert_pretile null pointer");
+    if (!umma_supported(hidden, inter, GATEUP) || !umma_supported(inter, hidden, DOWN))
+        return fail(K3D_EINVAL, "k3d_expert_pretile: hidden=%d and inter=%d must be multiples of 512",
+                    hidden, inter);
+    const uintptr_t al = (uintptr_t)dst->p1 | (uintptr_t)dst->s1 | (uintptr_t)dst->p2 |
+                         (uintptr_t)dst->s2 | (uintptr_t)src->p1 | (uintptr_t)src->s1 |
+                         (uintptr_t)src->p3 | (uintptr_t)src->s3 | (uintptr_t)src->p2 |
+                         (uintptr_t)src->s2;
+    if (al & 15u) return fail(K3D_EINVAL, "k3d_expert_pretile pointers must be 16-byte aligned");
+    cudaStream_t st = stream();
+    k_pretile<<<(inter / 64) * (hidden / kStageK), 256, 0, st>>>(
+        (uint8_t *)dst->p1, (uint8_t *)dst->s1, src->p1, src->s1, src->p3, src->s3, hidden);
+    k_pretile<<<(hidden / 128) * (inter / kStageK), 256, 0, st>>>(
+        (uint8_t *)dst->p2, (uint8_t *)dst->s2, src->p2, src->s2, nullptr, nullptr, inter);
+    note_launch(2);
+    return check_launch("expert pretile");
+}
+
+}  // extern "C"

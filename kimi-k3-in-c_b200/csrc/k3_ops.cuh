@@ -31,6 +31,21 @@ int xsplit(__half *xb, float *xsc, const float *x, int n, int nvec, size_t ld, c
 int mxfp4_mma_launch(int mode, const MoeWork &w, int umax, int in, int rows, const __half *xb,
                      const float *xsc, int x_by_assign, float *out, cudaStream_t st);
 
+// k3_mxfp4_umma.cu (tcgen05 block-scaled MXFP4; mode 0 gate/up, 1 down)
+bool umma_supported(int K, int rows, int mode);
+int umma_slices(int units, int K, int rows, int mode);
+size_t umma_bq_bytes(int K);
+size_t umma_bs_bytes(int K);
+int umma_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, int nvec, size_t ld,
+                cudaStream_t st);
+int umma_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride,
+                       int inter, const int *assign, const int *count, int npos, cudaStream_t st);
+int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n,
+                   cudaStream_t st);
+int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
+                int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
+                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st);
+
 // k3_router.cu
 size_t router_ws_bytes(int T, int n_experts);
 int router_f32(int *idx, float *w, const float *x, const float *W, const float *bias,

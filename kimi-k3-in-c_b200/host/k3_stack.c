@@ -68,6 +68,7 @@ struct K3dModel {
     double step_bytes;
     K3sTensor t[K3S_MAX_TENSORS];
     int nt;
+    unsigned char *stage_expert;   /* creation only: checkpoint-layout expert before tiling */
 };
 
 static int is_mla_layer(const K3dStackCfg *c, int l)
@@ -214,20 +215,44 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             const size_t sz[6] = {gu, gus, gu, gus, gu, gus};
             size_t off[6], per = 0;
             for (int i = 0; i < 6; i++) { off[i] = per; per += align256(sz[i]); }
+            /* tiled layout: [gate/up codes][gate/up scales][down codes][down scales] */
+            const size_t tsz[4] = {2 * gu, 2 * gus, gu, gus};
+            size_t toff[4], tper = 0;
+            for (int i = 0; i < 4; i++) { toff[i] = tper; tper += align256(tsz[i]); }
+            const int tiled = s->expert_layout == 1;
             const int nloc = s->expert_hi - s->expert_lo;
             snprintf(nm, sizeof nm, "layer%d.moe.pool", l);
             L->pool = (unsigned char *)dalloc(m, nm, (size_t)(nloc > 0 ? nloc : 1) * per);
             K3ExpertQ *tab = (K3ExpertQ *)calloc((size_t)s->n_experts, sizeof(K3ExpertQ));
             if (!L->pool || !tab) { err = 1; free(tab); break; }
+            if (tiled && !m->stage_expert) {
+                /* one checkpoint-layout expert the fills land in before tiling; freed at
+                 * the end of model creation (all on the library stream, so reuse is
+                 * ordered) */
+                m->stage_expert = (unsigned char *)k3d_alloc(per);
+                if (!m->stage_expert) { err = 1; free(tab); break; }
+            }
             for (int e = s->expert_lo; e < s->expert_hi && !err; e++) {
                 unsigned char *base = L->pool + (size_t)(e - s->expert_lo) * per;
-                tab[e].p1 = base + off[0]; tab[e].s1 = base + off[1];
-                tab[e].p3 = base + off[2]; tab[e].s3 = base + off[3];
-                tab[e].p2 = base + off[4]; tab[e].s2 = base + off[5];
+                unsigned char *src = tiled ? m->stage_expert : base;
+                K3ExpertQ q;
+                q.p1 = src + off[0]; q.s1 = src + off[1];
+                q.p3 = src + off[2]; q.s3 = src + off[3];
+                q.p2 = src + off[4]; q.s2 = src + off[5];
                 for (int j = 0; j < 3; j++)
-                    if (k3d_fill_mxfp4(base + off[2 * j], sz[2 * j], base + off[2 * j + 1],
+                    if (k3d_fill_mxfp4(src + off[2 * j], sz[2 * j], src + off[2 * j + 1],
                                        sz[2 * j + 1], next_seed(m) + (uint64_t)e, 117, 121))
                         err = 1;
+                if (tiled) {
+                    K3ExpertQ t;
+                    t.p1 = base + toff[0]; t.s1 = base + toff[1];
+                    t.p3 = NULL; t.s3 = NULL;
+                    t.p2 = base + toff[2]; t.s2 = base + toff[3];
+                    if (k3d_expert_pretile(&t, &q, E, s->inter)) err = 1;
+                    tab[e] = t;
+                } else {
+                    tab[e] = q;
+                }
             }
             snprintf(nm, sizeof nm, "layer%d.moe.table", l);
             L->table = (K3ExpertQ *)dalloc(m, nm, (size_t)s->n_experts * sizeof(K3ExpertQ));
@@ -270,6 +295,11 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             err = 1;
         if (!err && k3d_memset(m->pos, 0, 16)) err = 1;
         if (!err && k3d_sync()) err = 1;
+    }
+    if (m->stage_expert) {
+        if (k3d_sync()) err = 1;
+        k3d_free(m->stage_expert);
+        m->stage_expert = NULL;
     }
     if (err) {
         k3d_model_destroy(m);

@@ -69,7 +69,8 @@ class K3LayerW(C.Structure):
 class K3dMoeShape(C.Structure):
     _fields_ = [("hidden", i32), ("inter", i32), ("n_experts", i32), ("topk", i32),
                 ("renorm", i32), ("routed_scale", f32), ("shared_inter", i32),
-                ("expert_lo", i32), ("expert_hi", i32), ("add_shared", i32)]
+                ("expert_lo", i32), ("expert_hi", i32), ("add_shared", i32),
+                ("expert_layout", i32)]
 
 
 class K3dMoeW(C.Structure):
@@ -189,6 +190,8 @@ _PROTOS = {
     "k3d_moe_swiglu": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, vp, vp,
                              vp, sz]),
     "k3d_router_bf16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32]),
+    "k3d_set_expert_kernel": (i32, [i32]),
+    "k3d_expert_pretile": (i32, [C.POINTER(K3ExpertQ), C.POINTER(K3ExpertQ), i32, i32]),
     "k3d_router_bf16_noalloc": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32]),
     "k3d_moe_last_unique": (i32, []),
     "k3d_router_fallbacks": (C.c_longlong, []),
@@ -333,12 +336,12 @@ class MoeWeights:
 
     def __init__(self, hidden, inter, n_experts, topk, router_w, router_bias, shared=None,
                  experts=None, seed=None, lo=0, hi=None, s_lo=117, s_hi=121, renorm=1,
-                 routed_scale=2.5, add_shared=1, lib=None):
+                 routed_scale=2.5, add_shared=1, tiled=False, lib=None):
         self.lib = lib or load()
         hi = n_experts if hi is None else hi
         self.shape = K3dMoeShape(hidden, inter, n_experts, topk, renorm, routed_scale,
                                  shared[0].shape[0] if shared is not None else 0, lo, hi,
-                                 add_shared)
+                                 add_shared, 1 if tiled else 0)
         gu = inter * hidden // 2
         gus = inter * hidden // 32
         sizes = [gu, gus, gu, gus, gu, gus]
@@ -350,11 +353,21 @@ class MoeWeights:
         self.per_expert = o
         n_local = hi - lo
         self.pool = DevBuf(max(1, n_local) * o, self.lib)
+        # tiled: the checkpoint bytes go to a staging expert and k3d_expert_pretile writes
+        # the pool slot as [gate/up codes 2*gu][gate/up scales 2*gus][down codes][down scales]
+        tsizes = [2 * gu, 2 * gus, gu, gus]
+        toffs = []
+        o2 = 0
+        for s_ in tsizes:
+            toffs.append(o2)
+            o2 += _align(s_)
+        assert o2 <= o
+        stage = DevBuf(o, self.lib) if tiled else None
         table = (K3ExpertQ * n_experts)()
         for e in range(lo, hi):
             base = self.pool.ptr + (e - lo) * o
-            ptrs = [base + off for off in offs]
-            table[e] = K3ExpertQ(*ptrs)
+            src_base = stage.ptr if tiled else base
+            ptrs = [src_base + off for off in offs]
             if experts is not None:
                 for key, p in zip(("p1", "s1", "p3", "s3", "p2", "s2"), ptrs):
                     a = np.ascontiguousarray(experts[e][key])
@@ -364,6 +377,16 @@ class MoeWeights:
                     check(self.lib.k3d_fill_mxfp4(ptrs[2 * j], sizes[2 * j], ptrs[2 * j + 1],
                                                   sizes[2 * j + 1], seed * 7919 + e * 3 + j,
                                                   s_lo, s_hi), "expert fill")
+            if tiled:
+                tp = [base + off for off in toffs]
+                dst = K3ExpertQ(tp[0], tp[1], None, None, tp[2], tp[3])
+                check(self.lib.k3d_expert_pretile(C.byref(dst), C.byref(K3ExpertQ(*ptrs)),
+                                                  hidden, inter), "expert pretile")
+                check(self.lib.k3d_sync(), "pretile")     # the staging expert is reused
+                table[e] = dst
+            else:
+                table[e] = K3ExpertQ(*ptrs)
+        self.tiled = tiled
         self.table_host = table
         self.offs = offs
         self.sizes = sizes
@@ -380,6 +403,7 @@ class MoeWeights:
         return sum(self.sizes)
 
     def download_expert(self, e):
+        assert not self.tiled, "tiled experts hold no checkpoint-layout copy"
         q = self.table_host[e]
         out = {}
         for key, size in zip(("p1", "s1", "p3", "s3", "p2", "s2"), self.sizes):

@@ -19,7 +19,7 @@ CFG = dict(hidden=512, vocab=1024, n_layers=8, eps=1e-6, kda_heads=4, kda_head_d
            moe=dict(inter=512, n_experts=16, topk=4, routed_scale=2.5, shared_inter=256))
 
 
-def make_cfg(c, batch=1, cap=64):
+def make_cfg(c, batch=1, cap=64, layout=0):
     m, mo = c["mla"], c["moe"]
     sc = k3cuda.K3dStackCfg()
     sc.hidden, sc.vocab, sc.n_layers, sc.eps = c["hidden"], c["vocab"], c["n_layers"], c["eps"]
@@ -28,7 +28,8 @@ def make_cfg(c, batch=1, cap=64):
     sc.mla = k3cuda.K3dMlaShape(m["hidden"], m["H"], m["q_lora"], m["kv_lora"], m["qn"], m["qr"],
                                 m["vh"], m["theta"], m["eps"], 1)
     sc.moe = k3cuda.K3dMoeShape(c["hidden"], mo["inter"], mo["n_experts"], mo["topk"], 1,
-                                mo["routed_scale"], mo["shared_inter"], 0, mo["n_experts"], 1)
+                                mo["routed_scale"], mo["shared_inter"], 0, mo["n_experts"], 1,
+                                layout)
     sc.first_dense, sc.dense_inter = c["first_dense"], c["dense_inter"]
     for i in range(16):
         sc.mla_layers[i] = c["mla_layers"][i] if i < len(c["mla_layers"]) else -1
@@ -45,7 +46,52 @@ def download(k3, model, name, dtype, shape=None):
     return a.reshape(shape) if shape else a
 
 
-def host_copy(k3, model, c):
+def _untile(codes, sf, K, rows, gu):
+    """Inverse of k3d_expert_pretile for one matrix pair: tiles of 128 rows x 512 elements
+    (codes in the SWIZZLE_128B K-major image, scales as four 32x16-byte atoms)."""
+    nch = K // 512
+    ntiles = rows // 64 if gu else rows // 128
+    r = np.arange(128)[:, None]
+    j = np.arange(16)[None, :]
+    chunk_off = (j >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((j & 7) ^ (r & 7)) << 4)
+    byte_idx = (chunk_off[:, :, None] + np.arange(16)[None, None, :]).reshape(128, 256)
+    rr = np.arange(128)[:, None]
+    w = np.arange(4)[None, :]
+    sf_off = (512 * w + 16 * (rr & 31) + 4 * (rr >> 5))[:, :, None] + np.arange(4)[None, None, :]
+    sf_idx = sf_off.reshape(128, 16)
+    out_c = np.zeros((ntiles * 128, K // 2), np.uint8)
+    out_s = np.zeros((ntiles * 128, K // 32), np.uint8)
+    for t in range(ntiles):
+        for c in range(nch):
+            blk = (t * nch + c)
+            tile = codes[blk * 32768:(blk + 1) * 32768]
+            out_c[t * 128:(t + 1) * 128, c * 256:(c + 1) * 256] = tile[byte_idx]
+            atoms = sf[blk * 2048:(blk + 1) * 2048]
+            out_s[t * 128:(t + 1) * 128, c * 16:(c + 1) * 16] = atoms[sf_idx]
+    if not gu:
+        return out_c, out_s
+    # gate/up tiles hold 64 gate rows then the same 64 up rows
+    oc = out_c.reshape(ntiles, 2, 64, K // 2)
+    os_ = out_s.reshape(ntiles, 2, 64, K // 32)
+    return (oc[:, 0].reshape(rows, K // 2), os_[:, 0].reshape(rows, K // 32),
+            oc[:, 1].reshape(rows, K // 2), os_[:, 1].reshape(rows, K // 32))
+
+
+def untile_expert(slot, hidden, inter):
+    gu, gus = inter * hidden // 2, inter * hidden // 32
+    sizes = [2 * gu, 2 * gus, gu, gus]
+    offs, o = [], 0
+    for s_ in sizes:
+        offs.append(o)
+        o += (s_ + 255) // 256 * 256
+    parts = [slot[off:off + s_] for off, s_ in zip(offs, sizes)]
+    p1, s1, p3, s3 = _untile(parts[0], parts[1], hidden, inter, True)
+    p2, s2 = _untile(parts[2], parts[3], inter, hidden, False)
+    return {k: np.ascontiguousarray(v).reshape(-1) for k, v in
+            (("p1", p1), ("s1", s1), ("p3", p3), ("s3", s3), ("p2", p2), ("s2", s2))}
+
+
+def host_copy(k3, model, c, layout=0):
     E, P, D, H = c["hidden"], c["kda_heads"] * c["kda_head_dim"], c["kda_head_dim"], c["kda_heads"]
     m, mo = c["mla"], c["moe"]
     W, S = {}, {}
@@ -95,6 +141,9 @@ def host_copy(k3, model, c):
             experts = []
             for e in range(mo["n_experts"]):
                 base = e * o
+                if layout == 1:
+                    experts.append(untile_expert(pool[base:base + o], E, mo["inter"]))
+                    continue
                 d = {}
                 for key, off, s_ in zip(("p1", "s1", "p3", "s3", "p2", "s2"), offs, sizes):
                     d[key] = np.ascontiguousarray(pool[base + off: base + off + s_])
@@ -104,14 +153,17 @@ def host_copy(k3, model, c):
     return W, S
 
 
-def test_stack_decode_matches_oracle_eager_and_graph(k3, oracle):
+@pytest.mark.parametrize("layout", [0, 1])
+def test_stack_decode_matches_oracle_eager_and_graph(k3, oracle, layout):
+    """layout 0: checkpoint-layout experts (mma.sync / tcgen05 cp.async path); layout 1:
+    tiled experts on the tcgen05 bulk-copy path (the oracle gets the un-tiled bytes)."""
     c = CFG
-    model = k3.k3d_model_create(ctypes.byref(make_cfg(c)), 1234)
+    model = k3.k3d_model_create(ctypes.byref(make_cfg(c, layout=layout)), 1234)
     assert model, k3.k3d_last_message()
     try:
         k3cuda.check(k3.k3d_model_fill_context(model, 5, 99))
         k3cuda.check(k3.k3d_sync())
-        W, S = host_copy(k3, model, c)
+        W, S = host_copy(k3, model, c, layout)
         assert S["pos"] == 5
         tok = 17
         for step in range(4):          # step 0 eager, step 1 captures the graph, 2-3 replay
