@@ -18,6 +18,9 @@ int fail(int code, const char *fmt, ...);
 // Ensures the context exists on the current device; returns K3D_OK or an error.
 int ensure_ctx();
 cudaStream_t stream();
+cudaStream_t side_stream();          // null if it could not be created
+cudaEvent_t side_event(int i);       // fork/join events of the side stream (i = 0..3)
+bool profiling();                    // section timers on (k3d_prof_enable)
 int sm_count();
 // Host-side launch accounting: every kernel launch of this library goes through
 // note_launch() so that tests and the bench can count them.

@@ -45,6 +45,8 @@ struct Ctx {
                  double ms = 0.0; long count = 0; };
     std::map<std::string, Sec> secs;
     std::vector<cudaEvent_t> pool;
+    cudaStream_t side = nullptr;          // second stream for independent work in a layer
+    cudaEvent_t side_ev[4] = {nullptr, nullptr, nullptr, nullptr};
 };
 
 Ctx g;
@@ -154,6 +156,29 @@ int ensure_ctx()
 }
 
 cudaStream_t stream() { return g.stream; }
+
+// The side stream and its fork/join events, created on first use. Work forked onto it is
+// always joined back into the main stream before the call returns, so synchronising the
+// main stream (or capturing it into a graph) covers it.
+cudaStream_t side_stream()
+{
+    if (!g.side) {
+        if (cudaStreamCreateWithFlags(&g.side, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            g.side = nullptr;
+        }
+        for (int i = 0; i < 4 && g.side; i++)
+            if (cudaEventCreateWithFlags(&g.side_ev[i], cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                g.side = nullptr;
+            }
+    }
+    return g.side;
+}
+
+cudaEvent_t side_event(int i) { return g.side_ev[i & 3]; }
+
+bool profiling() { return g.prof; }
 int sm_count() { return g.sms; }
 void note_launch(int n) { g.launches += n; }
 

@@ -278,7 +278,7 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
               int accumulate, cudaStream_t s)
 {
     if (out <= 0 || T <= 0) return K3D_OK;
-    const bool fast = (in % 8) == 0 && al16(W) && (size_t)in * 4 * 4 <= 200 * 1024;
+    const bool fast = (in % 8) == 0 && al16(W) && (size_t)in * 4 * min(T, 4) <= 200 * 1024;
     if (!fast) {
         for (int t = 0; t < T; t++) {
             k_gemv_generic<uint16_t><<<grid_for(out, 8), 256, 0, s>>>(

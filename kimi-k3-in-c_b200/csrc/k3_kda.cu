@@ -63,9 +63,12 @@ __global__ void k_kda_decode(float *S, float *o, const float *q, const float *k,
     if ((n & 3) == 0 && (((uintptr_t)Sh) & 15u) == 0) {
         const float4 *S4 = reinterpret_cast<const float4 *>(Sh);
         float4 *T4 = reinterpret_cast<float4 *>(St);
+        #pragma unroll 8
         for (int f = threadIdx.x; f < n / 4; f += blockDim.x) T4[f] = S4[f];
     } else {
-        for (int f = threadIdx.x; f < n; f += blockDim.x) St[f] = Sh[f];
+        #pragma unroll 8
+        #pragma unroll 8
+    for (int f = threadIdx.x; f < n; f += blockDim.x) St[f] = Sh[f];
     }
     for (int i = threadIdx.x; i < dk; i += blockDim.x) {
         qs[i] = q[bh * dk + i];

@@ -55,41 +55,84 @@ __device__ __forceinline__ float conv_silu(const float *w, float *hist, float cu
 }
 
 // grid (H, B), blockDim = D (<= 128, multiple of 32). Shared: D*D state + 3*D vectors.
-__global__ void k_kda_head(KdaHeadArgs A)
+// KC = conv_k when it is a compile-time constant (4 for the K3 model): every global load
+// of the thread (projections, gates, conv weights and histories) is then issued before any
+// arithmetic; KC = 0 handles any conv_k.
+template <int KC>
+__global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
 {
     extern __shared__ float sh[];
     __shared__ double red[8];
     const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
-    const int D = A.D, H = A.H, K = A.K, P = H * D, hst = K - 1;
+    const int D = A.D, H = A.H, K = KC > 0 ? KC : A.K, P = H * D, hst = K - 1;
     float *St = sh;
     float *qs = St + D * D, *ks = qs + D, *as = ks + D;
     float *S = A.state + (size_t)b * A.state_stride + (size_t)h * D * D;
     float *conv = A.state + (size_t)b * A.state_stride + (size_t)H * D * D;
     const int nw = blockDim.x >> 5;
-    // stage the state tile
-    {
-        const float4 *S4 = reinterpret_cast<const float4 *>(S);
-        float4 *T4 = reinterpret_cast<float4 *>(St);
-        for (int f = j; f < D * D / 4; f += blockDim.x) T4[f] = S4[f];
-    }
     const int c = h * D + j;
     const size_t bp = (size_t)b * P + c;
-    // ShortConv + SiLU (history in place)
-    float hist[15];
-    float qv, kv, vv;
-    {
-        float *hq = conv + (size_t)c * hst;
+    float qv, kv, vv, gpv, zv, dtb, bpv, alog, onw;
+    float *hq = conv + (size_t)c * hst;
+    float *hk = conv + (size_t)P * hst + (size_t)c * hst;
+    float *hv = conv + (size_t)2 * P * hst + (size_t)c * hst;
+    if constexpr (KC > 0) {
+        // all loads first
+        float wq[KC], wk[KC], wv[KC], xq[KC], xk[KC], xv[KC];
+#pragma unroll
+        for (int t = 0; t < KC; t++) {
+            wq[t] = A.q_conv[(size_t)c * KC + t];
+            wk[t] = A.k_conv[(size_t)c * KC + t];
+            wv[t] = A.v_conv[(size_t)c * KC + t];
+        }
+#pragma unroll
+        for (int t = 0; t < KC - 1; t++) { xq[t] = hq[t]; xk[t] = hk[t]; xv[t] = hv[t]; }
+        xq[KC - 1] = A.qp[bp]; xk[KC - 1] = A.kp[bp]; xv[KC - 1] = A.vp[bp];
+        gpv = A.gp[bp]; zv = A.z[bp]; dtb = A.dt_bias[c];
+        bpv = A.bp[(size_t)b * H + h]; alog = A.A_log[h]; onw = A.o_norm[j];
+        {
+            const float4 *S4 = reinterpret_cast<const float4 *>(S);
+            float4 *T4 = reinterpret_cast<float4 *>(St);
+#pragma unroll 8
+            for (int f = j; f < D * D / 4; f += blockDim.x) T4[f] = S4[f];
+        }
+        // ShortConv + SiLU in the CPU's order: the newest input times the last tap, then the
+        // history oldest first (k3_ops.c:875-878); the history shifts in place
+        float aq = __fmul_rn(wq[KC - 1], xq[KC - 1]);
+        float ak = __fmul_rn(wk[KC - 1], xk[KC - 1]);
+        float av = __fmul_rn(wv[KC - 1], xv[KC - 1]);
+#pragma unroll
+        for (int t = 0; t < KC - 1; t++) {
+            aq = __fadd_rn(aq, __fmul_rn(wq[t], xq[t]));
+            ak = __fadd_rn(ak, __fmul_rn(wk[t], xk[t]));
+            av = __fadd_rn(av, __fmul_rn(wv[t], xv[t]));
+        }
+#pragma unroll
+        for (int t = 0; t < KC - 1; t++) { hq[t] = xq[t + 1]; hk[t] = xk[t + 1]; hv[t] = xv[t + 1]; }
+        qv = __fmul_rn(aq, sigm(aq));
+        kv = __fmul_rn(ak, sigm(ak));
+        vv = __fmul_rn(av, sigm(av));
+    } else {
+        // stage the state tile
+        {
+            const float4 *S4 = reinterpret_cast<const float4 *>(S);
+            float4 *T4 = reinterpret_cast<float4 *>(St);
+#pragma unroll 8
+            for (int f = j; f < D * D / 4; f += blockDim.x) T4[f] = S4[f];
+        }
+        // ShortConv + SiLU (history in place)
+        float hist[15];
         for (int t = 0; t < hst; t++) hist[t] = hq[t];
         qv = conv_silu(A.q_conv + (size_t)c * K, hist, A.qp[bp], K);
         for (int t = 0; t < hst; t++) hq[t] = hist[t];
-        float *hk = conv + (size_t)P * hst + (size_t)c * hst;
         for (int t = 0; t < hst; t++) hist[t] = hk[t];
         kv = conv_silu(A.k_conv + (size_t)c * K, hist, A.kp[bp], K);
         for (int t = 0; t < hst; t++) hk[t] = hist[t];
-        float *hv = conv + (size_t)2 * P * hst + (size_t)c * hst;
         for (int t = 0; t < hst; t++) hist[t] = hv[t];
         vv = conv_silu(A.v_conv + (size_t)c * K, hist, A.vp[bp], K);
         for (int t = 0; t < hst; t++) hv[t] = hist[t];
+        gpv = A.gp[bp]; zv = A.z[bp]; dtb = A.dt_bias[c];
+        bpv = A.bp[(size_t)b * H + h]; alog = A.A_log[h]; onw = A.o_norm[j];
     }
     // L2Norm q and k over the head
     const double sq = block_sum_dd((double)qv * (double)qv, red, nw);
@@ -98,9 +141,9 @@ __global__ void k_kda_head(KdaHeadArgs A)
     kv = __fmul_rn(kv, (float)(1.0 / sqrt(sk + (double)1e-6f)));
     qv = __fmul_rn(qv, 1.0f / sqrtf((float)D));
     // beta and the decay chain
-    const float beta = sigm(A.bp[(size_t)b * H + h]);
-    const float a = expf(A.A_log[h]);
-    const float gdec = __fmul_rn(A.lb, sigm(__fmul_rn(a, __fadd_rn(A.z[bp], A.dt_bias[c]))));
+    const float beta = sigm(bpv);
+    const float a = expf(alog);
+    const float gdec = __fmul_rn(A.lb, sigm(__fmul_rn(a, __fadd_rn(zv, dtb))));
     qs[j] = qv;
     ks[j] = kv;
     as[j] = expf(gdec);
@@ -123,8 +166,8 @@ __global__ void k_kda_head(KdaHeadArgs A)
     // head RMSNorm, then the output gate
     const double so = block_sum_dd((double)o * (double)o, red, nw);
     const float inv = (float)(1.0 / sqrt(so / (double)D + (double)A.eps));
-    o = __fmul_rn(__fmul_rn(A.o_norm[j], o), inv);
-    o = __fmul_rn(o, sigm(A.gp[bp]));
+    o = __fmul_rn(__fmul_rn(onw, o), inv);
+    o = __fmul_rn(o, sigm(gpv));
     A.heads[bp] = o;
 }
 
@@ -187,10 +230,12 @@ int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dK
     const size_t smem = ((size_t)D * D + 3 * (size_t)D) * 4;
     static bool init = false;
     if (!init) {
-        allow_smem_max(k_kda_head);
+        allow_smem_max(k_kda_head<4>);
+        allow_smem_max(k_kda_head<0>);
         init = true;
     }
-    k_kda_head<<<dim3(H, B), D, smem, st>>>(A);
+    if (s->conv_k == 4) k_kda_head<4><<<dim3(H, B), D, smem, st>>>(A);
+    else k_kda_head<0><<<dim3(H, B), D, smem, st>>>(A);
     note_launch();
     K3_TRY(check_launch("kda head"));
     prof_end("kda.core");

@@ -168,15 +168,31 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= hidden) return;
     float acc = 0.0f;
-    for (int j = 0; j < K; j++) {
-        const int a = t * K + j;
-        const int e = __ldg(idx + a);
-        if (e < lo || e >= hi) continue;
-        // the contribution, summed over the K slices of the down pass in slice order
-        const float *c = contrib + (size_t)a * hidden + r;
-        float v = c[0];
-        for (int s = 1; s < ks; s++) v += c[(size_t)s * slice_stride];
-        acc = __fadd_rn(acc, __fmul_rn(__ldg(wts + a), v));
+    // top-k slots in groups of 8: the group's expert ids, weights and contributions are all
+    // loaded before the ordered sum, so the loads overlap instead of chaining
+    for (int j0 = 0; j0 < K; j0 += 8) {
+        int e[8];
+        float w[8], v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int a = t * K + min(j0 + k, K - 1);
+            e[k] = __ldg(idx + a);
+            w[k] = __ldg(wts + a);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int a = t * K + min(j0 + k, K - 1);
+            const float *c = contrib + (size_t)a * hidden + r;
+            float sum = c[0];
+#pragma unroll 4
+            for (int s = 1; s < ks; s++) sum += c[(size_t)s * slice_stride];
+            v[k] = sum;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (j0 + k >= K || e[k] < lo || e[k] >= hi) continue;
+            acc = __fadd_rn(acc, __fmul_rn(w[k], v[k]));
+        }
     }
     if (sh_out) acc = __fadd_rn(acc, sh_out[(size_t)t * hidden + r]);
     float *o = out + (size_t)t * hidden + r;
@@ -522,13 +538,24 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     const int K = s->topk;
     const int TK = T * K;
 
-    // shared expert first: it does not depend on the router
+    // The shared expert does not depend on the router: it runs on the side stream, in
+    // parallel with routing and the routed experts (a parallel branch when the stream is
+    // captured into a graph), and is joined before the combine. With the section timers
+    // on it runs in line so that its time is measured on its own.
     const bool shared = s->shared_inter > 0 && s->add_shared;
+    cudaStream_t sst = (!profiling() && side_stream()) ? side_stream() : st;
     if (shared) {
+        if (sst != st) {
+            if (cudaEventRecord(side_event(0), st) != cudaSuccess ||
+                cudaStreamWaitEvent(sst, side_event(0), 0) != cudaSuccess)
+                return fail(K3D_ECUDA, "moe: fork to the side stream");
+        }
         prof_begin("moe.shared");
-        K3_TRY(gemv_bf16_swiglu(L.sh_act, x, w->sh_gate, w->sh_up, s->hidden, s->shared_inter, T, st));
-        K3_TRY(gemv_bf16(L.sh_out, L.sh_act, w->sh_down, s->shared_inter, s->hidden, T, 0, st));
+        K3_TRY(gemv_bf16_swiglu(L.sh_act, x, w->sh_gate, w->sh_up, s->hidden, s->shared_inter, T, sst));
+        K3_TRY(gemv_bf16(L.sh_out, L.sh_act, w->sh_down, s->shared_inter, s->hidden, T, 0, sst));
         prof_end("moe.shared");
+        if (sst != st && cudaEventRecord(side_event(1), sst) != cudaSuccess)
+            return fail(K3D_ECUDA, "moe: side stream join event");
     }
     prof_begin("moe.router");
     K3_TRY(router_bf16(I, Wt, x, w->router_w, w->router_bias, T, s->hidden, s->n_experts, K,
@@ -556,6 +583,8 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
                            s->expert_layout, L.eb, O, st));
         prof_end("moe.experts");
     }
+    if (shared && sst != st && cudaStreamWaitEvent(st, side_event(1), 0) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe: join from the side stream");
     dim3 grid((s->hidden + 255) / 256, T);
     k_moe_combine<<<grid, 256, 0, st>>>(out, O.contrib, O.ks, O.slice, I, Wt, shared ? L.sh_out : nullptr,
                                         s->hidden, K, s->expert_lo, s->expert_hi, accumulate);

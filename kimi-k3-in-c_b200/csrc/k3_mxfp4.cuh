@@ -31,6 +31,7 @@ __device__ __forceinline__ void stage_x_mxfp4(float4 *xs, const float *x, int in
 {
     const int nf4 = in >> 2;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
+#pragma unroll 8
     for (int f = threadIdx.x; f < nf4; f += blockDim.x) {
         const int c = f >> 3, k = f & 7;
         xs[xs_idx(c, k)] = x4[f];
@@ -41,6 +42,7 @@ __device__ __forceinline__ void stage_x_mxfp4(float4 *xs, const float *x, int in
 __device__ __forceinline__ void stage_x_mxfp4_scalar(float4 *xs, const float *x, int in)
 {
     const int nf4 = in >> 2;
+#pragma unroll 8
     for (int f = threadIdx.x; f < nf4; f += blockDim.x) {
         const int c = f >> 3, k = f & 7;
         xs[xs_idx(c, k)] = make_float4(x[4 * f], x[4 * f + 1], x[4 * f + 2], x[4 * f + 3]);

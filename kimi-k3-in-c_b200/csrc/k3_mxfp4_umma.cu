@@ -531,12 +531,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 // chunk c, a 4 KB tile (16 piece rows x 256 bytes in the SWIZZLE_128B K-major layout) at
 // bq + 4096 c, and 4 scale atoms at bs + 2048 c (piece p's scale for block 4a+i at byte
 // 512 a + 16 p + i; every other byte of an atom is zero).
+//
+// One lane per element of a 32-element block; per piece: the block maximum (five
+// shuffles), the E8M0 scale, the E2M1 rounding and the exact residual. Powers of two are
+// built from their bits (exact; 2^-127 is the one subnormal an E8M0 scale can be).
+__device__ __forceinline__ float pow2f(int k)
+{
+    return k >= -126 ? __int_as_float((k + 127) << 23) : __int_as_float(0x00400000 >> (-127 - k));
+}
+
 __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, int blk, int lane)
 {
-    const float grid[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
     const int c = blk >> 4, j = blk & 15;
     uint8_t *tile = bq + (size_t)c * kTileB + (j >> 3) * 2048;
-    uint8_t *atom = bs + (size_t)c * kTileSF + ((j & 15) >> 2) * 512;
+    uint8_t *atom = bs + (size_t)c * kTileSF + (j >> 2) * 512;
     if ((j & 3) == 0) {
         // the zero bytes of this atom (its data bytes are written below by 4 blocks)
         if (lane < 16) {
@@ -546,25 +554,28 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
             *reinterpret_cast<uint4 *>(atom + 256 + 16 * (lane - 16)) = make_uint4(0, 0, 0, 0);
         }
     }
+    const bool bad = __any_sync(0xffffffffu, !isfinite(r));
     for (int p = 0; p < kN; p++) {
-        const bool bad = __any_sync(0xffffffffu, !isfinite(r));
         const float m = warp_max(fabsf(r));
         int code;
         if (bad) code = 255;
         else if (m == 0.0f) code = 127;
         else {
-            const int e = ilogbf(m);
-            int sx = (m <= ldexpf(1.5f, e)) ? e - 2 : e - 1;
+            // e = floor(log2 m) from the bits (m may be subnormal)
+            const int bits = __float_as_int(m);
+            const int e = (bits >> 23) ? (bits >> 23) - 127 : -127 - (__clz(bits) - 9);
+            int sx = (m <= 1.5f * pow2f(max(e, -126)) * (e < -126 ? pow2f(e + 126) : 1.0f)) ? e - 2 : e - 1;
             sx = max(-127, min(127, sx));
             code = sx + 127;
         }
         uint32_t nib = 0;
         if (code != 255) {
-            const float inv = ldexpf(1.0f, 127 - code);
-            const float a = fabsf(r) * inv;
+            const float a = fabsf(r) * pow2f(127 - code);
             const uint32_t q3 = a < 0.25f ? 0u : a < 0.75f ? 1u : a < 1.25f ? 2u : a < 1.75f ? 3u
                               : a < 2.5f ? 4u : a < 3.5f ? 5u : a < 5.0f ? 6u : 7u;
-            const float val = ldexpf(grid[q3], code - 127);
+            // E2M1 value of q3 (0, .5, 1, 1.5, 2, 3, 4, 6) times the scale, exactly
+            const float g = q3 < 4u ? 0.5f * (float)q3 : (float)(q3 & 1u ? 3u : 2u) * pow2f((int)(q3 >> 1) - 2);
+            const float val = g * pow2f(code - 127);
             nib = q3 | (signbit(r) && q3 ? 8u : 0u);
             r = signbit(r) ? r + val : r - val;
         }
@@ -600,12 +611,12 @@ __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int
     const int n = count ? *count : count_host;
     if (blk >= inter / 32 || p >= n) return;
     const int a = assign ? __ldg(assign + p) : p;
-    const float *pa = part + (size_t)a * 2 * inter;
-    const int i = blk * 32 + lane;
+    const float *pa = part + (size_t)a * 2 * inter + blk * 32 + lane;
     float g = 0.0f, u = 0.0f;
-    for (int s = 0; s < ks; s++) {
-        g += pa[(size_t)s * slice_stride + i];
-        u += pa[(size_t)s * slice_stride + inter + i];
+#pragma unroll 16
+    for (int s = 0; s < ks; s++) {       // unrolled: the slices' loads are all in flight
+        g += pa[(size_t)s * slice_stride];
+        u += pa[(size_t)s * slice_stride + inter];
     }
     const float act = silu_f(g) * u;
     const int nch = inter / kStageK;
@@ -658,6 +669,7 @@ __global__ void k_slice_sum(float *y, const float *part, int ks, size_t slice_st
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n) return;
     float acc = 0.0f;
+#pragma unroll 16
     for (int s = 0; s < ks; s++) acc += part[(size_t)s * slice_stride + r];
     y[r] = acc;
 }

@@ -37,12 +37,14 @@ __global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float
     const float *xr = x + (size_t)blockIdx.x * n;
     float *yr = y + (size_t)blockIdx.x * n;
     double ss = 0.0;
+#pragma unroll 8
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const double v = (double)xr[i];
         ss = fma(v, v, ss);
     }
     ss = block_sum_d(ss, red);
     const float inv = (float)(1.0 / sqrt(ss / (double)n + (double)eps));
+#pragma unroll 8
     for (int i = threadIdx.x; i < n; i += blockDim.x)
         yr[i] = __fmul_rn(__fmul_rn(w[i], xr[i]), inv);
 }
