@@ -182,7 +182,7 @@ int    k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W,
  * never allocates device memory. k3d_router_bf16 takes its score buffer from the
  * library workspace, which grows with cudaMalloc (a device-wide synchronisation) the
  * first time a larger T * n_experts arrives. This variant instead uses one fixed
- * scratch array compiled into the library (2 * K3D_ROUTER_NOALLOC_MAX floats, 256 KB),
+ * scratch array compiled into the library (3 * K3D_ROUTER_NOALLOC_MAX floats, 384 KB),
  * for callers that must not allocate once running: a serving loop whose device memory
  * is fixed at start-up, or a host whose allocator owns all device memory.
  *   - T * n_experts above K3D_ROUTER_NOALLOC_MAX returns K3D_EBOUND and launches nothing.

@@ -31,44 +31,7 @@ __global__ void __launch_bounds__(1024) k_moe_prep(const int *idx, int TK, int n
                                                    int *act_expert, int *act_off, int *assign)
 {
     extern __shared__ int sm[];
-    int *cnt = sm;                 // [n_experts]
-    int *cur = sm + n_experts;     // [n_experts]
-    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
-    __syncthreads();
-    for (int a = threadIdx.x; a < TK; a += blockDim.x) {
-        const int e = idx[a];
-        if (e >= lo && e < hi && e < n_experts && e >= 0) atomicAdd(&cnt[e], 1);
-    }
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        const int per = (n_experts + 31) / 32;
-        const int e0 = min(n_experts, lane * per), e1 = min(n_experts, e0 + per);
-        int sc = 0, sf = 0;
-        for (int e = e0; e < e1; e++) { sc += cnt[e]; sf += cnt[e] > 0; }
-        int ic = sc, iff = sf;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int vc = __shfl_up_sync(0xffffffffu, ic, o);
-            const int vf = __shfl_up_sync(0xffffffffu, iff, o);
-            if (lane >= o) { ic += vc; iff += vf; }
-        }
-        int off = ic - sc, u = iff - sf;
-        for (int e = e0; e < e1; e++) {
-            cur[e] = off;
-            if (cnt[e] > 0) { act_expert[u] = e; act_off[u] = off; u++; }
-            off += cnt[e];
-        }
-        if (lane == 31) { n_active[0] = iff; n_active[1] = ic; act_off[iff] = ic; }
-    }
-    __syncthreads();
-    for (int a = threadIdx.x; a < TK; a += blockDim.x) {
-        const int e = idx[a];
-        if (e >= lo && e < hi && e < n_experts && e >= 0) {
-            const int p = atomicAdd(&cur[e], 1);
-            assign[p] = a;
-        }
-    }
+    group_assignments(idx, TK, n_experts, lo, hi, n_active, act_expert, act_off, assign, sm);
 }
 
 // ---- gate/up + SiLU*mul -------------------------------------------------------------
@@ -167,26 +130,30 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
     const int t = blockIdx.y;
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= hidden) return;
+    float *o = out + (size_t)t * hidden + r;
+    const float sh = sh_out ? sh_out[(size_t)t * hidden + r] : 0.0f;
+    const float prev = accumulate ? *o : 0.0f;
     float acc = 0.0f;
     // top-k slots in groups of 8: the group's expert ids, weights and contributions are all
-    // loaded before the ordered sum, so the loads overlap instead of chaining
+    // loaded before the ordered sum, so the loads overlap instead of chaining. The slice
+    // loop is outermost with the 8 slots inside it, so every slice's 8 loads are independent
+    // and the unrolled loop keeps 8 x 4 loads in flight.
     for (int j0 = 0; j0 < K; j0 += 8) {
         int e[8];
         float w[8], v[8];
+        const float *c[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
             const int a = t * K + min(j0 + k, K - 1);
             e[k] = __ldg(idx + a);
             w[k] = __ldg(wts + a);
+            c[k] = contrib + (size_t)a * hidden + r;
+            v[k] = c[k][0];
         }
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int a = t * K + min(j0 + k, K - 1);
-            const float *c = contrib + (size_t)a * hidden + r;
-            float sum = c[0];
 #pragma unroll 4
-            for (int s = 1; s < ks; s++) sum += c[(size_t)s * slice_stride];
-            v[k] = sum;
+        for (int s = 1; s < ks; s++) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[k] += c[k][(size_t)s * slice_stride];
         }
 #pragma unroll
         for (int k = 0; k < 8; k++) {
@@ -194,9 +161,8 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
             acc = __fadd_rn(acc, __fmul_rn(w[k], v[k]));
         }
     }
-    if (sh_out) acc = __fadd_rn(acc, sh_out[(size_t)t * hidden + r]);
-    float *o = out + (size_t)t * hidden + r;
-    *o = accumulate ? __fadd_rn(*o, acc) : acc;
+    if (sh_out) acc = __fadd_rn(acc, sh);
+    *o = accumulate ? __fadd_rn(prev, acc) : acc;
 }
 
 // ---- host side -------------------------------------------------------------------------
@@ -305,13 +271,20 @@ static int umma_ks_cap(int K, int TK)
     return TK <= kUmmaMaxTK ? K / 512 : 1;
 }
 
+// True when run_experts takes the tcgen05 path.
+static bool use_umma(const ExpertBufs &B, int hidden, int inter, int TK, int layout)
+{
+    return (layout == 1 || g_expert_kernel == 0) && B.bq_x && umma_eligible(hidden, inter, TK, layout);
+}
+
 // gate/up -> act -> down -> contributions for a work list. tcgen05 block-scaled MMA
 // (k3_mxfp4_umma.cu) when the workspace carries its buffers and the kernel choice allows,
 // else the mma.sync kernel (k3_mxfp4_mma.cu), else the CUDA-core kernels. `count` is the
 // device count of local assignments (MoE) or null (single expert, one assignment).
+// x_split: the caller already wrote x's tcgen05 B operand (umma_bsplit into B.bq_x/bs_x).
 static int run_experts(const MoeWork &mw, const int *idx, const int *count, int umax,
                        const float *x, int T, int TK, int hidden, int inter, int layout,
-                       const ExpertBufs &B, ExpertOut &O, cudaStream_t st)
+                       const ExpertBufs &B, ExpertOut &O, cudaStream_t st, bool x_split = false)
 {
     O.contrib = B.contrib;
     O.ks = 1;
@@ -319,17 +292,16 @@ static int run_experts(const MoeWork &mw, const int *idx, const int *count, int 
     const int topk = mw.single_mode ? 1 : mw.K;
     if (layout == 1 && (!B.bq_x || !umma_eligible(hidden, inter, TK, 1)))
         return fail(K3D_EINVAL, "tiled experts need hidden and inter multiples of 512");
-    if ((layout == 1 || g_expert_kernel == 0) && B.bq_x && umma_eligible(hidden, inter, TK, layout)) {
+    if (use_umma(B, hidden, inter, TK, layout)) {
         const int ks_gu = std::min(umma_slices(TK, hidden, inter, 0), umma_ks_cap(hidden, TK));
         const int ks_d = std::min(umma_slices(TK, inter, hidden, 1), umma_ks_cap(inter, TK));
         const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
-        K3_TRY(umma_bsplit(B.bq_x, B.bs_x, x, hidden, T, hidden, st));
+        if (!x_split) K3_TRY(umma_bsplit(B.bq_x, B.bs_x, x, hidden, T, hidden, st));
         prof_begin("experts.gateup");
         K3_TRY(umma_launch(0, layout, mw, idx, count, TK, hidden, inter, ks_gu, B.bq_x, B.bs_x, topk,
                            B.part_gu, 2 * inter, sl_gu, st));
         prof_end("experts.gateup");
-        K3_TRY(umma_bsplit_swiglu(B.bq_a, B.bs_a, B.part_gu, ks_gu, sl_gu, inter,
-                                  mw.single_mode ? nullptr : mw.assign, count, TK, st));
+        K3_TRY(umma_bsplit_swiglu(B.bq_a, B.bs_a, B.part_gu, ks_gu, sl_gu, inter, count, TK, st));
         prof_begin("experts.down");
         K3_TRY(umma_launch(1, layout, mw, idx, count, TK, inter, hidden, ks_d, B.bq_a, B.bs_a, 1,
                            B.part_d, hidden, sl_d, st));
@@ -538,18 +510,26 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     const int K = s->topk;
     const int TK = T * K;
 
-    // The shared expert does not depend on the router: it runs on the side stream, in
-    // parallel with routing and the routed experts (a parallel branch when the stream is
-    // captured into a graph), and is joined before the combine. With the section timers
-    // on it runs in line so that its time is measured on its own.
+    // Neither the tcgen05 B operand of x nor the shared expert depends on the router: both
+    // run on the side stream, in parallel with routing (a parallel branch when the stream
+    // is captured into a graph); the routed experts wait for the split, the combine for the
+    // shared expert. With the section timers on they run in line, so that each section's
+    // time is measured on its own.
     const bool shared = s->shared_inter > 0 && s->add_shared;
+    const int umax = TK < (s->expert_hi - s->expert_lo) ? TK : (s->expert_hi - s->expert_lo);
+    const bool early_split = umax > 0 && use_umma(L.eb, s->hidden, s->inter, TK, s->expert_layout);
     cudaStream_t sst = (!profiling() && side_stream()) ? side_stream() : st;
+    if ((shared || early_split) && sst != st) {
+        if (cudaEventRecord(side_event(0), st) != cudaSuccess ||
+            cudaStreamWaitEvent(sst, side_event(0), 0) != cudaSuccess)
+            return fail(K3D_ECUDA, "moe: fork to the side stream");
+    }
+    if (early_split) {
+        K3_TRY(umma_bsplit(L.eb.bq_x, L.eb.bs_x, x, s->hidden, T, s->hidden, sst));
+        if (sst != st && cudaEventRecord(side_event(2), sst) != cudaSuccess)
+            return fail(K3D_ECUDA, "moe: side stream split event");
+    }
     if (shared) {
-        if (sst != st) {
-            if (cudaEventRecord(side_event(0), st) != cudaSuccess ||
-                cudaStreamWaitEvent(sst, side_event(0), 0) != cudaSuccess)
-                return fail(K3D_ECUDA, "moe: fork to the side stream");
-        }
         prof_begin("moe.shared");
         K3_TRY(gemv_bf16_swiglu(L.sh_act, x, w->sh_gate, w->sh_up, s->hidden, s->shared_inter, T, sst));
         K3_TRY(gemv_bf16(L.sh_out, L.sh_act, w->sh_down, s->shared_inter, s->hidden, T, 0, sst));
@@ -558,10 +538,11 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
             return fail(K3D_ECUDA, "moe: side stream join event");
     }
     prof_begin("moe.router");
+    RouterGroup grp{L.n_active, L.act_expert, L.act_off, L.assign, s->expert_lo, s->expert_hi, 0};
     K3_TRY(router_bf16(I, Wt, x, w->router_w, w->router_bias, T, s->hidden, s->n_experts, K,
-                       s->renorm, s->routed_scale, L.router, st));
+                       s->renorm, s->routed_scale, L.router, st, &grp));
     prof_end("moe.router");
-    {
+    if (!grp.done) {
         const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
         k_moe_prep<<<1, 1024, smem, st>>>(I, TK, s->n_experts, s->expert_lo, s->expert_hi,
                                           L.n_active, L.act_expert, L.act_off, L.assign);
@@ -576,11 +557,12 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     mw.assign = L.assign;
     mw.K = K;
     ExpertOut O{L.eb.contrib, 1, 0};
-    int umax = TK < (s->expert_hi - s->expert_lo) ? TK : (s->expert_hi - s->expert_lo);
+    if (early_split && sst != st && cudaStreamWaitEvent(st, side_event(2), 0) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe: join of the split from the side stream");
     if (umax > 0) {
         prof_begin("moe.experts");
         K3_TRY(run_experts(mw, I, L.n_active + 1, umax, x, T, TK, s->hidden, s->inter,
-                           s->expert_layout, L.eb, O, st));
+                           s->expert_layout, L.eb, O, st, early_split));
         prof_end("moe.experts");
     }
     if (shared && sst != st && cudaStreamWaitEvent(st, side_event(1), 0) != cudaSuccess)

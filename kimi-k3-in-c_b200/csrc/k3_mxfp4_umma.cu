@@ -81,7 +81,9 @@ struct Job {
     int tiled;               // 1: experts in the tiled layout (k3d_expert_pretile)
     const uint8_t *bq;       // B pieces [vec][16][K/2]
     const uint8_t *bs;       // B scales [vec][16][K/32]
-    int vec_div;             // vector of assignment a = a / vec_div
+    int vec_div;             // vector of assignment a = a / vec_div (unless vec_pos)
+    int vec_pos;             // 1: B vector = grouped position p (down: act pieces by position)
+    int out_pos;             // 1: partial row block = p (gate/up), else the assignment a
     float *part;             // [ks][cap][out_w]
     int out_w;               // gate/up: 2 * inter (gate rows then up rows); down: rows
     size_t slice_stride;     // floats per K slice
@@ -251,7 +253,7 @@ __device__ __forceinline__ void publish(unsigned char *st, int tid)
 // -> expert table entry).
 struct ItemEnt {
     const uint8_t *c0, *c1, *s0, *s1;   // weight codes / scales (gate and up, or down twice)
-    int a;                              // assignment
+    int out;                            // partial row block (position or assignment)
     int tile, s;                        // 128-row tile, K slice
     int vec;                            // B operand vector
 };
@@ -269,17 +271,19 @@ __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
     const int rest = item / J.ks;
     it.tile = rest % J.ntiles;
     const int p = rest / J.ntiles;
+    int a;
     K3ExpertQ q;
     if (J.single_mode) {
-        it.a = p;
+        a = p;
         q = J.single;
     } else {
-        it.a = __ldg(J.assign + p);
-        q = J.table[__ldg(J.idx + it.a)];
+        a = __ldg(J.assign + p);
+        q = J.table[__ldg(J.idx + a)];
     }
     if (J.mode == GATEUP) { it.c0 = q.p1; it.c1 = q.p3; it.s0 = q.s1; it.s1 = q.s3; }
     else { it.c0 = it.c1 = q.p2; it.s0 = it.s1 = q.s2; }
-    it.vec = it.a / J.vec_div;
+    it.out = J.out_pos ? p : a;
+    it.vec = J.vec_pos ? p : a / J.vec_div;
     return it;
 }
 
@@ -496,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                 int row;
                 if (J.mode == GATEUP) row = m < 64 ? it.tile * 64 + m : (J.out_w >> 1) + it.tile * 64 + (m - 64);
                 else row = it.tile * 128 + m;
-                float *dst = J.part + (size_t)it.s * J.slice_stride + (size_t)it.a * J.out_w + row;
+                float *dst = J.part + (size_t)it.s * J.slice_stride + (size_t)it.out * J.out_w + row;
                 const int buf = n_epi % kAccBufs;
                 if (!mbar_wait(b_accf + 8 * buf, (n_epi / kAccBufs) & 1, abort)) break;
                 tc_fence_after();
@@ -532,8 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 // bq + 4096 c, and 4 scale atoms at bs + 2048 c (piece p's scale for block 4a+i at byte
 // 512 a + 16 p + i; every other byte of an atom is zero).
 //
-// One lane per element of a 32-element block; per piece: the block maximum (five
-// shuffles), the E8M0 scale, the E2M1 rounding and the exact residual. Powers of two are
+// One lane per element of a 32-element block; per piece: the block maximum (one redux),
+// the E8M0 scale, the E2M1 rounding and the exact residual. Powers of two are
 // built from their bits (exact; 2^-127 is the one subnormal an E8M0 scale can be).
 __device__ __forceinline__ float pow2f(int k)
 {
@@ -556,7 +560,8 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
     }
     const bool bad = __any_sync(0xffffffffu, !isfinite(r));
     for (int p = 0; p < kN; p++) {
-        const float m = warp_max(fabsf(r));
+        // block maximum in one warp reduction: non-negative floats order like their bits
+        const float m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
         int code;
         if (bad) code = 255;
         else if (m == 0.0f) code = 127;
@@ -600,27 +605,28 @@ __global__ void k_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, size_t
 }
 
 // B operands of act = silu(gate) * up, gate/up summed over the K slices of the gate/up
-// pass in slice order. grid (ceil(inter/32 / 8), assignment positions).
+// pass in slice order; both indexed by grouped position p. grid (ceil(inter/32 / 8),
+// positions). The count and the partials are loaded together (the partial rows of every
+// position exist), so the block pays one memory latency.
 __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks,
-                                size_t slice_stride, int inter, const int *assign,
-                                const int *count, int count_host)
+                                size_t slice_stride, int inter, const int *count, int count_host)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int blk = blockIdx.x * 8 + warp;
     const int p = blockIdx.y;
+    if (blk >= inter / 32) return;
+    const float *pa = part + (size_t)p * 2 * inter + blk * 32 + lane;
     const int n = count ? *count : count_host;
-    if (blk >= inter / 32 || p >= n) return;
-    const int a = assign ? __ldg(assign + p) : p;
-    const float *pa = part + (size_t)a * 2 * inter + blk * 32 + lane;
     float g = 0.0f, u = 0.0f;
 #pragma unroll 16
     for (int s = 0; s < ks; s++) {       // unrolled: the slices' loads are all in flight
         g += pa[(size_t)s * slice_stride];
         u += pa[(size_t)s * slice_stride + inter];
     }
+    if (p >= n) return;
     const float act = silu_f(g) * u;
     const int nch = inter / kStageK;
-    split_block(bq + (size_t)a * nch * kTileB, bs + (size_t)a * nch * kTileSF, act, blk, lane);
+    split_block(bq + (size_t)p * nch * kTileB, bs + (size_t)p * nch * kTileSF, act, blk, lane);
 }
 
 // ------------------------------------------------------------- weight tiling
@@ -719,11 +725,11 @@ int umma_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, int nvec, size_
 }
 
 int umma_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride,
-                       int inter, const int *assign, const int *count, int npos, cudaStream_t st)
+                       int inter, const int *count, int npos, cudaStream_t st)
 {
     if (npos <= 0) return K3D_OK;
     dim3 grid((inter / 32 + 7) / 8, npos);
-    k_bsplit_swiglu<<<grid, 256, 0, st>>>(bq, bs, part, ks, slice_stride, inter, assign, count, npos);
+    k_bsplit_swiglu<<<grid, 256, 0, st>>>(bq, bs, part, ks, slice_stride, inter, count, npos);
     note_launch();
     return check_launch("umma bsplit swiglu");
 }
@@ -763,6 +769,11 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     J.bq = bq;
     J.bs = bs;
     J.vec_div = vec_div;
+    // gate/up partials and the act pieces built from them are indexed by grouped position
+    // (no assignment lookup between the two passes); down partials by assignment, for the
+    // combine
+    J.out_pos = mode == GATEUP;
+    J.vec_pos = mode == DOWN;
     J.part = part;
     J.out_w = out_w;
     J.slice_stride = slice_stride;

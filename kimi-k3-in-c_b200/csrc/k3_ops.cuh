@@ -39,7 +39,7 @@ size_t umma_bs_bytes(int K);
 int umma_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, int nvec, size_t ld,
                 cudaStream_t st);
 int umma_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride,
-                       int inter, const int *assign, const int *count, int npos, cudaStream_t st);
+                       int inter, const int *count, int npos, cudaStream_t st);
 int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n,
                    cudaStream_t st);
 int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
@@ -51,9 +51,16 @@ size_t router_ws_bytes(int T, int n_experts);
 int router_f32(int *idx, float *w, const float *x, const float *W, const float *bias,
                int T, int hidden, int n_experts, int topk, int renorm, float routed_scale,
                void *ws, cudaStream_t s);
+// Optional grouping of the routed assignments by expert (the MoE's prep step), done by the
+// router's own launch when its fused kernel runs (done = 1), else left to the caller.
+struct RouterGroup {
+    int *n_active, *act_expert, *act_off, *assign;
+    int lo, hi;
+    int done;
+};
 int router_bf16(int *idx, float *w, const float *x, const uint16_t *W, const float *bias,
                 int T, int hidden, int n_experts, int topk, int renorm, float routed_scale,
-                void *ws, cudaStream_t s);
+                void *ws, cudaStream_t s, RouterGroup *grp = nullptr);
 
 // k3_small.cu
 int rmsnorm(float *y, const float *x, const float *w, int n, int rows, float eps,

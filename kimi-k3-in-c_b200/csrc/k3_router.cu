@@ -25,6 +25,7 @@
 //   operations use explicit round-to-nearest intrinsics so nothing is contracted.
 #include "k3_common.cuh"
 #include "k3_expf.h"
+#include "k3_moe.cuh"
 #include "k3_ops.cuh"
 
 namespace k3 {
@@ -153,21 +154,19 @@ __device__ __forceinline__ int val_f32(float f)
     return (be ? be : 1) - 150 + (__ffs((int)m) - 1);
 }
 
-// ------------------------------------------------------------------ scores kernel
-// CTA = 2 experts x 4 warps (256 threads); warp w takes expert slot w/4 and quarter w%4
-// of the row. The row is cut into 128 contiguous segments of se = hidden/128 elements in
-// the CPU's order; lane l of quarter q owns segment 32q + l. x and both rows are staged in
-// shared memory first (independent cp.async copies: the memory latency is paid once),
-// each segment padded so that the lanes' 16-byte reads hit distinct banks.
+// ---------------------------------------------------------------- the exact path
+// For the rare expert whose logit the fast pass cannot settle and that can change the
+// selection. x and the expert's row are staged in shared memory as 128 contiguous segments
+// of se = hidden/128 elements in the CPU's order (segment g at g * pitch, padded so that
+// the lanes' 16-byte reads hit distinct banks). All 128 threads of the CTA call
+// exact_logit; lane l of warp q owns segment 32q + l.
 //
-// Fast pass (every expert): the exact sum S of the products (TwoSum accumulation per lane,
-// then exact combination of lanes and quarters) and A = sum |p|. Any summation order of n
-// terms is within gamma_n * A of S (gamma_n = n u / (1 - n u)), so if
-// [S - gamma_n A, S + gamma_n A] rounds to one float, that float is the CPU's logit
-// (about 99.4% of experts at the benchmark shapes).
+// Exact pass: the exact sum S of the products (TwoSum accumulation per lane, then exact
+// combination of lanes and quarters) and A = sum |p|. Any summation order of n terms is
+// within gamma_n * A of S (gamma_n = n u / (1 - n u)), so if [S - gamma_n A, S + gamma_n A]
+// rounds to one float, that float is the CPU's logit.
 //
-// Tight pass (the rest; the expert's 4 warps, synchronised by a named barrier): a
-// rigorous bound that counts only additions that can round. Step k computes
+// Tight pass: a rigorous bound that counts only additions that can round. Step k computes
 // fl(s^_{k-1} + p_k), exact when the result is a multiple of U = ulp of the largest
 // |s^_{k-1} + p_k| possible. Two sufficient tests:
 //   granularity: every CPU prefix s^_k is a multiple of 2^G_k, G_k = the lowest 2-adic
@@ -178,74 +177,67 @@ __device__ __forceinline__ int val_f32(float f)
 // `run` tracks the prefix to within M = 4 n u A of both the exact prefix and the CPU's.
 // Each step that may round adds U/2. If the bound is zero and S is a double, the CPU sum
 // is S; otherwise the interval test is repeated with the tight bound, and if that still
-// straddles a float rounding boundary lane 0 runs the CPU's sequential loop.
+// straddles a float rounding boundary thread 0 runs the CPU's sequential loop
+// (k3d_router_fallbacks counts these).
+struct ExactShared {
+    double th[4], tl[4], A[4], bt[4];
+    int q[4];
+    float logit;
+};
+
+__host__ __device__ __forceinline__ int seg_xpitch(int hidden) { return (hidden >> 10) * 32 + 16; }
 template <typename WT>
-__global__ void __launch_bounds__(256) k_router_scores(float *score, float *choice,
-                                                       const float *x, const WT *W,
-                                                       const float *bias, int hidden,
-                                                       int n_experts)
+__host__ __device__ __forceinline__ int seg_wpitch(int hidden)
 {
-    extern __shared__ __align__(16) unsigned char rsm[];
-    __shared__ double s_th[2][4], s_tl[2][4], s_A[2][4], s_bt[2][4];
-    __shared__ int s_q[2][4];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int es = warp >> 2, q = warp & 3;
-    const int e = blockIdx.x * 2 + es;
-    const int t = blockIdx.y;
-    const float *xt = x + (size_t)t * hidden;
+    return (hidden >> 10) * 8 * (int)sizeof(WT) + (sizeof(WT) == 2 ? 32 : 16);
+}
+
+// Copies hidden elements of elem_bytes each as 128 segments, segment g at dst + g * pitch.
+__device__ __forceinline__ void stage_segments(unsigned char *dst, const void *src, int hidden,
+                                               int elem_bytes, int pitch)
+{
+    const int per = (hidden >> 7) * elem_bytes / 16;      // 16-byte pieces per segment
+    const int n16 = hidden * elem_bytes / 16;
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    const unsigned char *s = static_cast<const unsigned char *>(src);
+    for (int c = threadIdx.x; c < n16; c += blockDim.x)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                     :: "r"(d + (uint32_t)((c / per) * pitch + (c % per) * 16)), "l"(s + 16 * (size_t)c)
+                     : "memory");
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+}
+
+template <typename WT>
+__device__ float exact_logit(const unsigned char *xs, const unsigned char *wr, int hidden,
+                             ExactShared &X)
+{
+    const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
     const int se = hidden >> 7;               // elements per segment
     const int nc = se >> 3;                   // 8-element chunks per segment
-    const int xpitch = nc * 32 + 16;
-    const int wpitch = nc * 8 * (int)sizeof(WT) + (sizeof(WT) == 2 ? 32 : 16);
-    unsigned char *xs = rsm;
-    unsigned char *wrow0 = rsm + 128 * xpitch;
-    {
-        const uint32_t xs_s = (uint32_t)__cvta_generic_to_shared(xs);
-        const int x4 = se / 4;                // float4 chunks per segment
-        for (int f = threadIdx.x; f < hidden / 4; f += blockDim.x)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                         :: "r"(xs_s + (uint32_t)((f / x4) * xpitch + (f % x4) * 16)), "l"(xt + 4 * f)
-                         : "memory");
-        const int per_seg = nc * (int)sizeof(WT) / 2;      // 16-byte chunks per segment
-        const int wq = hidden * (int)sizeof(WT) / 16;
-        for (int k = 0; k < 2; k++) {
-            const int ek = blockIdx.x * 2 + k;
-            if (ek >= n_experts) break;
-            const unsigned char *row = reinterpret_cast<const unsigned char *>(W + (size_t)ek * hidden);
-            const uint32_t w_s = (uint32_t)__cvta_generic_to_shared(wrow0 + k * 128 * wpitch);
-            for (int c = threadIdx.x; c < wq; c += blockDim.x)
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                             :: "r"(w_s + (uint32_t)((c / per_seg) * wpitch + (c % per_seg) * 16)),
-                                "l"(row + 16 * (size_t)c) : "memory");
-        }
-        asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
-    }
-    __syncthreads();
-    const bool active = e < n_experts;
+    const int xpitch = seg_xpitch(hidden);
+    const int wpitch = seg_wpitch<WT>(hidden);
     const int seg = q * 32 + lane;
     const unsigned char *xl = xs + seg * xpitch;
-    const unsigned char *wl = wrow0 + es * 128 * wpitch + seg * wpitch;
+    const unsigned char *wl = wr + seg * wpitch;
 
-    // ---- fast pass: exact segment total, sum |p|
+    // ---- exact pass: exact segment total, sum |p|
     double hs[4] = {0.0, 0.0, 0.0, 0.0}, ls[4] = {0.0, 0.0, 0.0, 0.0};
     double A0 = 0.0, A1 = 0.0;
-    if (active) {
-        for (int c = 0; c < nc; c++) {
-            double w[8];
-            Chunk<WT>::load_smem(wl, c, w);
-            const float4 xa = *reinterpret_cast<const float4 *>(xl + 32 * c);
-            const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 * c + 16);
-            const double xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    for (int c = 0; c < nc; c++) {
+        double w[8];
+        Chunk<WT>::load_smem(wl, c, w);
+        const float4 xa = *reinterpret_cast<const float4 *>(xl + 32 * c);
+        const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 * c + 16);
+        const double xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const double pi = __dmul_rn(w[i], xv[i]);
-                const int k = i & 3;
-                const double s1 = __dadd_rn(hs[k], pi);
-                const double bb = __dsub_rn(s1, hs[k]);
-                ls[k] = __dadd_rn(ls[k], __dadd_rn(__dsub_rn(hs[k], __dsub_rn(s1, bb)), __dsub_rn(pi, bb)));
-                hs[k] = s1;
-                if (i & 1) A1 = __dadd_rn(A1, fabs(pi)); else A0 = __dadd_rn(A0, fabs(pi));
-            }
+        for (int i = 0; i < 8; i++) {
+            const double pi = __dmul_rn(w[i], xv[i]);
+            const int k = i & 3;
+            const double s1 = __dadd_rn(hs[k], pi);
+            const double bb = __dsub_rn(s1, hs[k]);
+            ls[k] = __dadd_rn(ls[k], __dadd_rn(__dsub_rn(hs[k], __dsub_rn(s1, bb)), __dsub_rn(pi, bb)));
+            hs[k] = s1;
+            if (i & 1) A1 = __dadd_rn(A1, fabs(pi)); else A0 = __dadd_rn(A0, fabs(pi));
         }
     }
     // the lane's exact total as a double-double
@@ -269,18 +261,17 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         two_sum(sum, low, h, l);
     }
     const double Aq = warp_sum_d(__dadd_rn(A0, A1));
-    if (lane == 0) { s_th[es][q] = h; s_tl[es][q] = l; s_A[es][q] = Aq; }
+    if (lane == 0) { X.th[q] = h; X.tl[q] = l; X.A[q] = Aq; }
     __syncthreads();
-    if (!active) return;
-    // the row's exact total and sum |p| (same arithmetic in all four warps)
-    double Sh = s_th[es][0], Sl = s_tl[es][0];
-    double A = s_A[es][0];
+    // the row's exact total and sum |p| (same arithmetic in every thread)
+    double Sh = X.th[0], Sl = X.tl[0];
+    double A = X.A[0];
     for (int k = 1; k < 4; k++) {
         double sum, err;
-        two_sum(Sh, s_th[es][k], sum, err);
-        const double low = __dadd_rn(__dadd_rn(Sl, s_tl[es][k]), err);
+        two_sum(Sh, X.th[k], sum, err);
+        const double low = __dadd_rn(__dadd_rn(Sl, X.tl[k]), err);
         two_sum(sum, low, Sh, Sl);
-        A = __dadd_rn(A, s_A[es][k]);
+        A = __dadd_rn(A, X.A[k]);
     }
     const double u = 0x1p-53;
     const double n = (double)hidden;
@@ -289,16 +280,9 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         const double gam = n * u / (1.0 - n * u);
         const double bound = (gam * A * (1.0 + 0x1p-20) + slack) * (1.0 + 0x1p-20) + 0x1p-1074;
         const float flo = (float)__dsub_rn(Sh, bound), fhi = (float)__dadd_rn(Sh, bound);
-        if (flo == fhi) {
-            if (q == 0 && lane == 0) {
-                const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-flo)));
-                score[(size_t)t * n_experts + e] = sc;
-                choice[(size_t)t * n_experts + e] = bias ? __fadd_rn(sc, __ldg(bias + e)) : sc;
-            }
-            return;
-        }
+        if (flo == fhi) return flo;          // uniform: every thread computed the same values
     }
-    // ---- tight pass (this expert's four warps; named barrier 1 + es, 128 threads)
+    // ---- tight pass
     const double M = 4.0 * n * u * A + 0x1p-1000;
     // the lane's lowest product valuation (integer work on the raw bits only)
     int qmin = 4096;
@@ -314,12 +298,12 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
     int wq = qmin;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) wq = min(wq, __shfl_xor_sync(0xffffffffu, wq, o));
-    if (lane == 0) s_q[es][q] = wq;
-    asm volatile("bar.sync %0, 128;" :: "r"(1 + es) : "memory");
+    if (lane == 0) X.q[q] = wq;
+    __syncthreads();
     // offsets: previous quarters' totals + the exclusive prefix of this warp's lane totals
     double off = 0.0;
     int G = 4096;
-    for (int k = 0; k < q; k++) { off = __dadd_rn(off, __dadd_rn(s_th[es][k], s_tl[es][k])); G = min(G, s_q[es][k]); }
+    for (int k = 0; k < q; k++) { off = __dadd_rn(off, __dadd_rn(X.th[k], X.tl[k])); G = min(G, X.q[k]); }
     const double lt = __dadd_rn(lh, ll);
     double incl = lt;
     int gq = qmin;
@@ -354,37 +338,37 @@ __global__ void __launch_bounds__(256) k_router_scores(float *score, float *choi
         }
     }
     bt = warp_sum_d(bt);
-    if (lane == 0) s_bt[es][q] = bt;
-    asm volatile("bar.sync %0, 128;" :: "r"(1 + es) : "memory");
-    if (q != 0 || lane != 0) return;
-    const double B = __dadd_rn(__dadd_rn(s_bt[es][0], s_bt[es][1]), __dadd_rn(s_bt[es][2], s_bt[es][3]));
-    float flo, fhi;
-    if (B == 0.0 && Sl == 0.0) {
-        flo = fhi = (float)Sh;       // no addition can have rounded: the CPU sum is S
-    } else {
-        const double bound = (B + slack) * (1.0 + 0x1p-20) + 0x1p-1074;
-        flo = (float)__dsub_rn(Sh, bound);
-        fhi = (float)__dadd_rn(Sh, bound);
-    }
-    float logit = flo;
-    if (flo != fhi) {
-        // still ambiguous: the CPU's sequential loop (k3_ops.c:449-450), from shared memory
-        const unsigned char *wr = wrow0 + es * 128 * wpitch;
-        double acc = 0.0;
-        for (int i = 0; i < hidden; i++) {
-            const int sg = i / se, k = i % se;
-            const double wv = (sizeof(WT) == 2)
-                ? (double)__uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(wr + sg * wpitch)[k] << 16)
-                : (double)reinterpret_cast<const float *>(wr + sg * wpitch)[k];
-            const double xv = (double)reinterpret_cast<const float *>(xs + sg * xpitch)[k];
-            acc = __dadd_rn(acc, __dmul_rn(wv, xv));
+    if (lane == 0) X.bt[q] = bt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const double B = __dadd_rn(__dadd_rn(X.bt[0], X.bt[1]), __dadd_rn(X.bt[2], X.bt[3]));
+        float flo, fhi;
+        if (B == 0.0 && Sl == 0.0) {
+            flo = fhi = (float)Sh;       // no addition can have rounded: the CPU sum is S
+        } else {
+            const double bound = (B + slack) * (1.0 + 0x1p-20) + 0x1p-1074;
+            flo = (float)__dsub_rn(Sh, bound);
+            fhi = (float)__dadd_rn(Sh, bound);
         }
-        atomicAdd(&k3_router_fallbacks, 1ull);
-        logit = (float)acc;
+        float logit = flo;
+        if (flo != fhi) {
+            // still ambiguous: the CPU's sequential loop (k3_ops.c:449-450), from shared memory
+            double acc = 0.0;
+            for (int i = 0; i < hidden; i++) {
+                const int sg = i / se, k = i % se;
+                const double wv = (sizeof(WT) == 2)
+                    ? (double)__uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(wr + sg * wpitch)[k] << 16)
+                    : (double)reinterpret_cast<const float *>(wr + sg * wpitch)[k];
+                const double xv = (double)reinterpret_cast<const float *>(xs + sg * xpitch)[k];
+                acc = __dadd_rn(acc, __dmul_rn(wv, xv));
+            }
+            atomicAdd(&k3_router_fallbacks, 1ull);
+            logit = (float)acc;
+        }
+        X.logit = logit;
     }
-    const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-logit)));
-    score[(size_t)t * n_experts + e] = sc;
-    choice[(size_t)t * n_experts + e] = bias ? __fadd_rn(sc, __ldg(bias + e)) : sc;
+    __syncthreads();
+    return X.logit;
 }
 
 // Any shape: one warp per (token, expert), lanes over contiguous segments.
@@ -551,40 +535,365 @@ __global__ void k_router_topk(int *idx, float *wout, float *choice, const float 
                     topk, renorm, routed_scale);
 }
 
+// ------------------------------------------------------------------ fused router
+// One launch for scores, top-k and (MoE) the grouping of assignments by expert.
+//
+// Phase 1, CTA = 2 experts x 128 threads; quarter q (a warp) takes a contiguous quarter of
+// the row, lane l its 8-element chunks l, l+32, ... (coalesced). Per expert, in fp64, the
+// sum s~ of the exact products in this order (summation depth d <= 128 for hidden <= 16384)
+// and, in fp32, A~ = sum |w||x| (an upper bound after a relative 2^-15 and an absolute
+// 2^-100 margin). The CPU's sequential sum is within gamma_{n-1} A of the exact sum S and
+// s~ within gamma_d A, so [s~ - B, s~ + B] with B = gamma_{n+128} A~ (+ 4u|s~| for the
+// rounding of the endpoints) holds the CPU's double; if both ends round to one float, that
+// float is the CPU's logit ("settled", about 99% of experts). Otherwise the expert carries
+// an interval [lo, hi] of its choice value (sigmoid + bias at both ends, widened by two
+// float ulps for the last-bit behaviour of expf).
+//
+// Phase 2, the last CTA of token t (completion counter): top-k by repeated strict-greater
+// max over keys = the exact choice of settled experts and lo of the others. If every
+// selected expert is settled and every unsettled one has hi below the k-th selected key,
+// the selection is the CPU's (each unsettled expert is below k settled ones). Otherwise
+// the offending experts are settled exactly (the exact path above) and the selection is
+// repeated. Then the weights (renorm in double) and, for the MoE, once the last token is
+// done, the grouping by expert.
+constexpr int kRouterMaxT = 4096;          // tokens per fused call
+constexpr int kNeedMax = 16;               // exact settlements per selection round
+// Completion counters: [t] counts the CTAs of token t that wrote their experts,
+// [kRouterMaxT] the tokens whose top-k is written. The last CTA to arrive resets its
+// counter, so every call starts from zero; calls are ordered on the library stream.
+__device__ unsigned int g_router_ctr[kRouterMaxT + 1] = {0};
+
+struct RouterJob {
+    const float *x;
+    const void *W;
+    const float *bias;
+    float *lo, *hi, *score;        // [T][n_experts] scratch
+    int *idx;
+    float *wts;
+    int T, hidden, n_experts, topk, renorm;
+    float routed_scale;
+    // grouping of the assignments by expert (MoE), when n_active is set
+    int *n_active, *act_expert, *act_off, *assign;
+    int e_lo, e_hi;
+};
+
+template <typename WT> struct WChunk;       // 8 weights held in registers
+template <> struct WChunk<uint16_t> {
+    uint4 v;
+    __device__ __forceinline__ void load(const uint16_t *row, int c) { v = ldg_nc_v4(row + 8 * (size_t)c); }
+    __device__ __forceinline__ void get(float w[8]) const
+    {
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[2 * i] = __uint_as_float(u[i] << 16);
+            w[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+        }
+    }
+};
+template <> struct WChunk<float> {
+    uint4 a, b;
+    __device__ __forceinline__ void load(const float *row, int c)
+    {
+        a = ldg_nc_v4(row + 8 * (size_t)c);
+        b = ldg_nc_v4(row + 8 * (size_t)c + 4);
+    }
+    __device__ __forceinline__ void get(float w[8]) const
+    {
+        w[0] = __uint_as_float(a.x); w[1] = __uint_as_float(a.y);
+        w[2] = __uint_as_float(a.z); w[3] = __uint_as_float(a.w);
+        w[4] = __uint_as_float(b.x); w[5] = __uint_as_float(b.y);
+        w[6] = __uint_as_float(b.z); w[7] = __uint_as_float(b.w);
+    }
+};
+
+__device__ __forceinline__ float sigmoid_k(float v)
+{
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-v)));
+}
+
+template <typename WT>
+__host__ __device__ inline size_t fused_smem_bytes(int hidden, int n_experts)
+{
+    return (size_t)128 * seg_xpitch(hidden) + (size_t)128 * seg_wpitch<WT>(hidden) +
+           (size_t)n_experts * (3 * sizeof(float) + 2 * sizeof(int) + 1) + 16;
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
+{
+    extern __shared__ __align__(16) unsigned char rsm[];
+    __shared__ double p_s[2][4];
+    __shared__ float p_a[2][4];
+    __shared__ ExactShared X;
+    __shared__ int s_last, s_nneed;
+    __shared__ int s_need[kNeedMax];
+    __shared__ int s_isel[K3_MAX_TOPK];
+    __shared__ float s_m;
+    const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
+    const int t = blockIdx.y;
+    const int E = J.n_experts, hidden = J.hidden;
+    const int e0 = blockIdx.x * 2;
+    const float *xt = J.x + (size_t)t * hidden;
+    const WT *W = static_cast<const WT *>(J.W);
+    const size_t tE = (size_t)t * E;
+
+    // ---------------------------------------------------------------- phase 1
+    {
+        const int nj = hidden >> 10;                     // chunks per lane
+        const int cbase = q * (hidden >> 5) + lane;
+        const bool act0 = e0 < E, act1 = e0 + 1 < E;
+        const WT *row0 = W + (size_t)e0 * hidden;
+        const WT *row1 = W + (size_t)(e0 + 1) * hidden;
+        double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
+        float a[2] = {0.0f, 0.0f};
+        for (int j0 = 0; j0 < nj; j0 += 8) {
+            float4 xv[8][2];
+            WChunk<WT> wv[2][8];
+            // every load of the batch is issued before any arithmetic
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j0 + j < nj) {
+                    const int c = cbase + 32 * (j0 + j);
+                    xv[j][0] = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c);
+                    xv[j][1] = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c + 1);
+                    if (act0) wv[0][j].load(row0, c);
+                    if (act1) wv[1][j].load(row1, c);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j0 + j < nj) {
+                    const float xf[8] = {xv[j][0].x, xv[j][0].y, xv[j][0].z, xv[j][0].w,
+                                         xv[j][1].x, xv[j][1].y, xv[j][1].z, xv[j][1].w};
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        if (!(k == 0 ? act0 : act1)) continue;
+                        float wf[8];
+                        wv[k][j].get(wf);
+#pragma unroll
+                        for (int i = 0; i < 8; i += 2) {
+                            // products are exact in double, so the fma rounds only the sum
+                            s0[k] = __fma_rn((double)wf[i], (double)xf[i], s0[k]);
+                            s1[k] = __fma_rn((double)wf[i + 1], (double)xf[i + 1], s1[k]);
+                            a[k] = __fmaf_rn(fabsf(wf[i]), fabsf(xf[i]), a[k]);
+                            a[k] = __fmaf_rn(fabsf(wf[i + 1]), fabsf(xf[i + 1]), a[k]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const double sk = warp_sum_d(__dadd_rn(s0[k], s1[k]));
+            const float ak = warp_sum(a[k]);
+            if (lane == 0) { p_s[k][q] = sk; p_a[k][q] = ak; }
+        }
+        __syncthreads();
+        if (threadIdx.x < 2 && e0 + (int)threadIdx.x < E) {
+            const int k = threadIdx.x, e = e0 + k;
+            const double S = __dadd_rn(__dadd_rn(__dadd_rn(p_s[k][0], p_s[k][1]), p_s[k][2]), p_s[k][3]);
+            const float A32 = __fadd_rn(__fadd_rn(__fadd_rn(p_a[k][0], p_a[k][1]), p_a[k][2]), p_a[k][3]);
+            const double u = 0x1p-53, n = (double)hidden + 128.0;
+            const double Aup = __fma_rn((double)A32, 1.0 + 0x1p-15, 0x1p-100);   // +inf stays +inf
+            const double gam = n * u / (1.0 - n * u) * (1.0 + 0x1p-20);
+            const double bound = __fma_rn(gam, Aup, 4.0 * u * fabs(S)) * (1.0 + 0x1p-20) + 0x1p-1074;
+            const float flo = (float)__dsub_rn(S, bound), fhi = (float)__dadd_rn(S, bound);
+            const float b = J.bias ? __ldg(J.bias + e) : 0.0f;
+            float lo, hi, sc = 0.0f;
+            if (flo == fhi) {
+                sc = sigmoid_k(flo);
+                lo = hi = J.bias ? __fadd_rn(sc, b) : sc;
+            } else if (isnan(flo) || isnan(fhi)) {
+                lo = hi = __int_as_float(0x7fc00000);
+            } else {
+                const float c1 = sigmoid_k(flo), c2 = sigmoid_k(fhi);
+                lo = J.bias ? __fadd_rd(fminf(c1, c2), b) : fminf(c1, c2);
+                hi = J.bias ? __fadd_ru(fmaxf(c1, c2), b) : fmaxf(c1, c2);
+                lo = __fsub_rd(lo, __fmaf_ru(fabsf(lo), 0x1p-21f, 0x1p-120f));
+                hi = __fadd_ru(hi, __fmaf_ru(fabsf(hi), 0x1p-21f, 0x1p-120f));
+            }
+            J.lo[tE + e] = lo;
+            J.hi[tE + e] = hi;
+            J.score[tE + e] = sc;
+            __threadfence();
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const unsigned prev = atomicAdd(&g_router_ctr[t], 1u);
+            s_last = (prev == gridDim.x - 1);
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        if (threadIdx.x == 0) g_router_ctr[t] = 0;
+    }
+
+    // ---------------------------------------------------------------- phase 2
+    unsigned char *xs = rsm;
+    unsigned char *wr = xs + 128 * seg_xpitch(hidden);
+    float *key = reinterpret_cast<float *>(wr + 128 * seg_wpitch<WT>(hidden));
+    float *hv = key + E;
+    float *sv = hv + E;
+    int *gsm = reinterpret_cast<int *>(sv + E);                 // 2 * E ints for the grouping
+    unsigned char *settled = reinterpret_cast<unsigned char *>(gsm + 2 * E);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const float l = __ldcg(J.lo + tE + e), h = __ldcg(J.hi + tE + e);
+        key[e] = l;
+        hv[e] = h;
+        sv[e] = __ldcg(J.score + tE + e);
+        settled[e] = (l == h);
+    }
+    __syncthreads();
+    const int K = J.topk;
+    bool x_staged = false;
+    for (int iter = 0; iter <= E; iter++) {
+        if (q == 0) {
+            // the register scan of k_router_topk_reg over the keys (lane l: experts l + 32k)
+            float v[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int e = lane + 32 * k;
+                v[k] = e < E ? key[e] : -INFINITY;
+            }
+            for (int j = 0; j < K; j++) {
+                float bv = -INFINITY;
+                int best = -1;
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    if (v[k] > bv) { bv = v[k]; best = lane + 32 * k; }
+                warp_best(bv, best);
+                if (best >= 0 && (best & 31) == lane) {
+#pragma unroll
+                    for (int k = 0; k < 16; k++)
+                        if (lane + 32 * k == best) v[k] = -INFINITY;
+                }
+                if (lane == 0) {
+                    s_isel[j] = best;
+                    s_m = best >= 0 ? bv : -INFINITY;
+                }
+            }
+            if (lane == 0) s_nneed = 0;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            if (settled[e]) continue;
+            bool need = !(hv[e] < s_m);
+            for (int j = 0; j < K; j++) need |= (s_isel[j] == e);
+            if (need) {
+                const int slot = atomicAdd(&s_nneed, 1);
+                if (slot < kNeedMax) s_need[slot] = e;
+            }
+        }
+        __syncthreads();
+        const int nn = min(s_nneed, kNeedMax);
+        if (nn == 0) break;
+        if (!x_staged) {
+            stage_segments(xs, xt, hidden, 4, seg_xpitch(hidden));
+            x_staged = true;
+        }
+        for (int i = 0; i < nn; i++) {
+            const int e = s_need[i];
+            stage_segments(wr, W + (size_t)e * hidden, hidden, (int)sizeof(WT), seg_wpitch<WT>(hidden));
+            __syncthreads();
+            const float logit = exact_logit<WT>(xs, wr, hidden, X);
+            if (threadIdx.x == 0) {
+                const float sc = sigmoid_k(logit);
+                const float c = J.bias ? __fadd_rn(sc, __ldg(J.bias + e)) : sc;
+                key[e] = c;
+                hv[e] = c;
+                sv[e] = sc;
+                settled[e] = 1;
+            }
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0) {
+        int isel[K3_MAX_TOPK];
+        float wsel[K3_MAX_TOPK];
+        for (int j = 0; j < K; j++) {
+            const int b = s_isel[j];
+            isel[j] = b >= 0 ? b : 0;
+            wsel[j] = b >= 0 ? sv[b] : 0.0f;
+        }
+        topk_finish(J.idx + (size_t)t * K, J.wts + (size_t)t * K, isel, wsel, K, J.renorm,
+                    J.routed_scale);
+    }
+    if (!J.n_active) return;
+    // ---------------------------------------------------------------- grouping
+    if (J.T > 1) {
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const unsigned prev = atomicAdd(&g_router_ctr[kRouterMaxT], 1u);
+            s_last = (prev == (unsigned)J.T - 1);
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        if (threadIdx.x == 0) g_router_ctr[kRouterMaxT] = 0;
+    } else {
+        __syncthreads();
+    }
+    group_assignments(J.idx, J.T * K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
+                      J.assign, gsm);
+}
+
 size_t router_ws_bytes(int T, int n_experts)
 {
-    return 2 * (size_t)T * n_experts * sizeof(float) + 256;
+    return 3 * (size_t)T * n_experts * sizeof(float) + 256;
 }
 
 template <typename WT>
 static int router_launch(int *idx, float *w, const float *x, const WT *W, const float *bias,
                          int T, int hidden, int n_experts, int topk, int renorm,
-                         float routed_scale, void *ws, cudaStream_t s)
+                         float routed_scale, void *ws, cudaStream_t s, RouterGroup *grp)
 {
     if (topk < 1 || topk > K3_MAX_TOPK)
         return fail(K3D_EBOUND, "router topk=%d outside 1..%d", topk, K3_MAX_TOPK);
     if (n_experts < 1 || hidden < 1 || T < 1)
         return fail(K3D_EINVAL, "router hidden=%d n_experts=%d T=%d", hidden, n_experts, T);
+    if (grp) grp->done = 0;
     float *score = (float *)ws;
     float *choice = score + (size_t)T * n_experts;
-    // the staged kernel needs hidden % 1024 == 0, 16-byte aligned rows and x, and its
-    // shared-memory image (x plus two rows, padded) within the opt-in limit
-    const size_t need = (size_t)hidden * 4 + (size_t)2 * hidden * sizeof(WT) + 128 * 16 * 3;
-    const bool vec = (hidden % 1024) == 0 && (((uintptr_t)W | (uintptr_t)x) & 15u) == 0 &&
-                     need <= 200 * 1024;
-    if (vec) {
-        // four warps (experts) per CTA: 96 CTAs for 384 experts, one wave over the SMs
-        dim3 grid((n_experts + 1) / 2, T);
-        const int nc = hidden >> 10;
-        const size_t smem = (size_t)128 * (nc * 32 + 16) +
-                            (size_t)2 * 128 * (nc * 8 * sizeof(WT) + (sizeof(WT) == 2 ? 32 : 16));
+    // the fused kernel needs hidden % 1024 == 0 (<= 16384), 16-byte aligned rows and x,
+    // at most 512 experts (the register scan) and kRouterMaxT tokens
+    const bool fused = (hidden % 1024) == 0 && hidden <= 16384 &&
+                       (((uintptr_t)W | (uintptr_t)x) & 15u) == 0 && n_experts <= 512 &&
+                       T <= kRouterMaxT;
+    if (fused) {
+        RouterJob J;
+        J.x = x;
+        J.W = W;
+        J.bias = bias;
+        J.lo = score;
+        J.hi = score + (size_t)T * n_experts;
+        J.score = score + 2 * (size_t)T * n_experts;
+        J.idx = idx;
+        J.wts = w;
+        J.T = T;
+        J.hidden = hidden;
+        J.n_experts = n_experts;
+        J.topk = topk;
+        J.renorm = renorm;
+        J.routed_scale = routed_scale;
+        J.n_active = grp ? grp->n_active : nullptr;
+        J.act_expert = grp ? grp->act_expert : nullptr;
+        J.act_off = grp ? grp->act_off : nullptr;
+        J.assign = grp ? grp->assign : nullptr;
+        J.e_lo = grp ? grp->lo : 0;
+        J.e_hi = grp ? grp->hi : n_experts;
+        const size_t smem = fused_smem_bytes<WT>(hidden, n_experts);
         static bool init = false;
-        if (!init) { allow_smem_max(k_router_scores<WT>); init = true; }
-        k_router_scores<WT><<<grid, 256, smem, s>>>(score, choice, x, W, bias, hidden, n_experts);
-    } else {
-        dim3 grid((n_experts + 7) / 8, T);
-        k_router_scores_generic<WT><<<grid, 256, 0, s>>>(score, choice, x, W, bias, hidden, n_experts);
+        if (!init) { allow_smem_max(k_router_fused<WT>); init = true; }
+        dim3 grid((n_experts + 1) / 2, T);
+        k_router_fused<WT><<<grid, 128, smem, s>>>(J);
+        note_launch();
+        if (grp) grp->done = 1;
+        return check_launch("router");
     }
+    dim3 grid((n_experts + 7) / 8, T);
+    k_router_scores_generic<WT><<<grid, 256, 0, s>>>(score, choice, x, W, bias, hidden, n_experts);
     if (n_experts <= 512)
         k_router_topk_reg<16><<<T, 32, 0, s>>>(idx, w, choice, score, n_experts, topk, renorm,
                                                routed_scale, topk);
@@ -600,21 +909,21 @@ int router_f32(int *idx, float *w, const float *x, const float *W, const float *
                void *ws, cudaStream_t s)
 {
     return router_launch<float>(idx, w, x, W, bias, T, hidden, n_experts, topk, renorm,
-                                routed_scale, ws, s);
+                                routed_scale, ws, s, nullptr);
 }
 
 int router_bf16(int *idx, float *w, const float *x, const uint16_t *W, const float *bias,
                 int T, int hidden, int n_experts, int topk, int renorm, float routed_scale,
-                void *ws, cudaStream_t s)
+                void *ws, cudaStream_t s, RouterGroup *grp)
 {
     return router_launch<uint16_t>(idx, w, x, W, bias, T, hidden, n_experts, topk, renorm,
-                                   routed_scale, ws, s);
+                                   routed_scale, ws, s, grp);
 }
 
-// Fixed scratch of k3d_router_bf16_noalloc: scores then choice keys, each up to
+// Fixed scratch of k3d_router_bf16_noalloc: three score arrays, each up to
 // K3D_ROUTER_NOALLOC_MAX floats. Every element a call reads it has first written, so
 // nothing needs clearing between calls.
-static __device__ __align__(256) float g_router_noalloc_ws[2 * K3D_ROUTER_NOALLOC_MAX];
+static __device__ __align__(256) float g_router_noalloc_ws[3 * K3D_ROUTER_NOALLOC_MAX];
 static const int kMaxDevices = 64;
 
 }  // namespace k3

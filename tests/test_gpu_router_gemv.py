@@ -59,6 +59,66 @@ def test_router_many_tokens_and_ties_bit_exact(k3, oracle):
         assert np.array_equal(gw[t].view(np.uint32), ow.view(np.uint32)), t
 
 
+def _midpoint_row(hidden, sign):
+    """bf16 row whose dot with x = ones is exactly sign * (1 + 2^-24), a float rounding
+    midpoint, reached through two cancelling 2^-60 terms: the fast pass cannot settle it,
+    and the tight pass cannot either (the tiny terms may round), so only the sequential
+    loop decides it."""
+    r = np.zeros(hidden, np.float32)
+    r[0], r[1], r[2], r[3] = 1.0, 2.0 ** -24, 2.0 ** -60, -(2.0 ** -60)
+    return synth.f32_to_bf16(sign * r)
+
+
+def _route(k3, x, W, bias, T, hidden, E):
+    X, Wd, B = (k3cuda.DevBuf.from_array(a) for a in (x, W, bias))
+    I = k3cuda.DevBuf(T * 8 * 4)
+    Wt = k3cuda.DevBuf(T * 8 * 4)
+    k3cuda.check(k3.k3d_router_bf16(I.ptr, Wt.ptr, X.ptr, Wd.ptr, B.ptr, T, hidden, E, 8, 1, 2.5))
+    k3cuda.check(k3.k3d_sync())
+    return I.download(np.int32, (T, 8)), Wt.download(np.float32, (T, 8))
+
+
+def test_router_unsettled_experts_only_where_they_matter(k3, oracle):
+    """Expert 7 (large bias) is selected and sits on a rounding midpoint: it must be settled
+    by the exact path. Expert 9 is as ambiguous but far below the top 8: the selection is
+    proven without it, so it costs no sequential loop. Bit-exact against the CPU either way."""
+    T, hidden, E = 4, 7168, 384
+    _, W, bias = synth.router_inputs(seed=91, T=T, hidden=hidden, n_experts=E)
+    x = np.ones((T, hidden), np.float32)
+    W[7] = _midpoint_row(hidden, 1.0)
+    W[9] = _midpoint_row(hidden, -1.0)
+    bias[7], bias[9] = 1.0, -1.0
+    f0 = k3.k3d_router_fallbacks()
+    gi, gw = _route(k3, x, W, bias, T, hidden, E)
+    nfb = k3.k3d_router_fallbacks() - f0
+    for t in range(T):
+        oi, ow = oracle.router_bf16(x[t], W, bias, 8, 1, 2.5)
+        assert np.array_equal(gi[t], oi), t
+        assert np.array_equal(gw[t].view(np.uint32), ow.view(np.uint32)), t
+        assert 7 in gi[t] and 9 not in gi[t]
+    assert nfb == T, f"{nfb} sequential loops for {T} tokens: expert 9 should not need one"
+
+
+def test_router_nine_tied_unsettled_experts(k3, oracle):
+    """Nine identical ambiguous experts dominate the choice: the first selection round picks
+    eight of them by their lower bounds, the ninth overlaps the eighth, so all nine are
+    settled exactly, then the ties go to the lowest indices."""
+    T, hidden, E = 2, 7168, 384
+    _, W, bias = synth.router_inputs(seed=92, T=T, hidden=hidden, n_experts=E)
+    x = np.ones((T, hidden), np.float32)
+    for e in range(100, 109):
+        W[e] = _midpoint_row(hidden, 1.0)
+        bias[e] = 2.0
+    f0 = k3.k3d_router_fallbacks()
+    gi, gw = _route(k3, x, W, bias, T, hidden, E)
+    assert k3.k3d_router_fallbacks() - f0 == 9 * T
+    for t in range(T):
+        oi, ow = oracle.router_bf16(x[t], W, bias, 8, 1, 2.5)
+        assert np.array_equal(gi[t], oi), t
+        assert np.array_equal(gw[t].view(np.uint32), ow.view(np.uint32)), t
+        assert list(gi[t]) == list(range(100, 108))
+
+
 @pytest.mark.parametrize("inp,out", [(7168, 4096), (2048, 7168), (100, 33), (7, 5)])
 def test_gemv_bf16_and_f32(k3, oracle, inp, out):
     g = synth.rng(inp + out)
