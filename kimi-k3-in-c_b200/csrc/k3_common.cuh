@@ -33,6 +33,31 @@ int check_launch(const char *what);
 void allow_dyn_smem(const void *func);
 template <typename F> inline void allow_smem_max(F *f) { allow_dyn_smem((const void *)f); }
 
+// Programmatic dependent launch: kernels of the decode path are launched with
+// launch_pdl, so that a kernel's launch and prologue overlap the end of the kernel before
+// it in the stream. Such a kernel must execute pdl_wait() before its first access to
+// memory that earlier work in the stream writes or reads (after which everything earlier
+// in the stream has completed and is visible), and calls pdl_trigger() to let the next
+// kernel launch. Off when the environment sets K3_PDL=0.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Section timers (k3d_prof_*): begin/end record events on the library stream when
 // profiling is on and no capture is in progress.
 void prof_begin(const char *section);
@@ -83,6 +108,12 @@ __device__ __forceinline__ void k3_raise(int code, int site)
 {
     if (atomicCAS(&k3_dev_err[0], 0, code) == 0) k3_dev_err[1] = site;
 }
+
+// Waits until every earlier kernel of the stream has completed and its memory operations
+// are visible (a no-op for a kernel launched without the PDL attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the stream launch (its CTAs then wait in their own pdl_wait).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t h)
 {

@@ -179,6 +179,15 @@ cudaStream_t side_stream()
 cudaEvent_t side_event(int i) { return g.side_ev[i & 3]; }
 
 bool profiling() { return g.prof; }
+
+bool pdl_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("K3_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 int sm_count() { return g.sms; }
 void note_launch(int n) { g.launches += n; }
 

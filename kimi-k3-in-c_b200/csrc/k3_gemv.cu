@@ -13,6 +13,8 @@ template <int R, int SEG, int NT>
 __global__ void __launch_bounds__(256) k_gemv_bf16(float *y, const float *x, const uint16_t *W,
                                                    int in, int out, int T, int accumulate)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 xs[];
     const int nf4 = in >> 2;
     for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
@@ -59,6 +61,8 @@ __global__ void __launch_bounds__(256) k_gemv_bf16_swiglu(float *act, const floa
                                                           const uint16_t *Wg, const uint16_t *Wu,
                                                           int in, int inter, int T)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 xs[];
     const int nf4 = in >> 2;
     for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
@@ -173,6 +177,8 @@ struct Segs {
 template <int R, int SEG>
 __global__ void __launch_bounds__(256) k_gemv_bf16_multi(Segs S, const float *x, int in, int T)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 xs[];
     const int nf4 = in >> 2;
     for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
@@ -223,6 +229,8 @@ __global__ void __launch_bounds__(256) k_gemv_bf16_argmax(float *y, unsigned lon
                                                           const float *x, const uint16_t *W,
                                                           int in, int out, int T)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 xs[];
     const int nf4 = in >> 2;
     for (int t = 0; t < T; t++) stage_x_bf16(xs + (size_t)t * nf4, x + (size_t)t * in, in);
@@ -257,6 +265,8 @@ __global__ void __launch_bounds__(256) k_gemv_bf16_argmax(float *y, unsigned lon
 
 __global__ void k_argmax_finish(int *next, const unsigned long long *key, int T)
 {
+    pdl_wait();
+    pdl_trigger();
     const int t = threadIdx.x;
     if (t < T) next[t] = (int)(0xffffffffu - (uint32_t)(key[t] & 0xffffffffu));
 }
@@ -297,10 +307,10 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
         const int nt = min(4, T - t0);
         const size_t smem = (size_t)nt * in * sizeof(float);
         if (nt == 1)
-            k_gemv_bf16<2, 7, 1><<<grid_for(out, 16), 256, smem, s>>>(
+            launch_pdl(k_gemv_bf16<2, 7, 1>, dim3(grid_for(out, 16)), dim3(256), smem, s, 
                 y + (size_t)t0 * out, x + (size_t)t0 * in, W, in, out, 1, accumulate);
         else
-            k_gemv_bf16<2, 7, 4><<<grid_for(out, 16), 256, smem, s>>>(
+            launch_pdl(k_gemv_bf16<2, 7, 4>, dim3(grid_for(out, 16)), dim3(256), smem, s, 
                 y + (size_t)t0 * out, x + (size_t)t0 * in, W, in, out, nt, accumulate);
         note_launch();
     }
@@ -318,7 +328,7 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
     for (int t0 = 0; t0 < T; t0 += 4) {
         const int nt = min(4, T - t0);
         const size_t smem = (size_t)nt * in * sizeof(float);
-        k_gemv_bf16_swiglu<7><<<grid_for(inter, 8), 256, smem, s>>>(
+        launch_pdl(k_gemv_bf16_swiglu<7>, dim3(grid_for(inter, 8)), dim3(256), smem, s, 
             act + (size_t)t0 * inter, x + (size_t)t0 * in, Wg, Wu, in, inter, nt);
         note_launch();
     }
@@ -344,7 +354,7 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
         return fail(K3D_EINVAL, "multi-segment GEMV: in=%d", in);
     static bool init = false;
     if (!init) { allow_smem(k_gemv_bf16_multi<2, 7>); init = true; }
-    k_gemv_bf16_multi<2, 7><<<grid_for(S.start[nseg], 16), 256, (size_t)T * in * 4, s>>>(S, x, in, T);
+    launch_pdl(k_gemv_bf16_multi<2, 7>, dim3(grid_for(S.start[nseg], 16)), dim3(256), (size_t)T * in * 4, s, S, x, in, T);
     note_launch();
     return check_launch("gemv bf16 multi");
 }
@@ -358,8 +368,8 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
     if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
                ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
-    k_gemv_bf16_argmax<2, 7><<<grid_for(out, 16), 256, (size_t)T * in * 4, s>>>(y, key, x, W, in, out, T);
-    k_argmax_finish<<<1, 32, 0, s>>>(next, key, T);
+    launch_pdl(k_gemv_bf16_argmax<2, 7>, dim3(grid_for(out, 16)), dim3(256), (size_t)T * in * 4, s, y, key, x, W, in, out, T);
+    launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);
     note_launch(2);
     return check_launch("lm head argmax");
 }

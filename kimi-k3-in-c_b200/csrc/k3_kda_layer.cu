@@ -61,6 +61,8 @@ __device__ __forceinline__ float conv_silu(const float *w, float *hist, float cu
 template <int KC>
 __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float sh[];
     __shared__ double red[8];
     const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
@@ -234,8 +236,8 @@ int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dK
         allow_smem_max(k_kda_head<0>);
         init = true;
     }
-    if (s->conv_k == 4) k_kda_head<4><<<dim3(H, B), D, smem, st>>>(A);
-    else k_kda_head<0><<<dim3(H, B), D, smem, st>>>(A);
+    if (s->conv_k == 4) launch_pdl(k_kda_head<4>, dim3(H, B), dim3(D), smem, st, A);
+    else launch_pdl(k_kda_head<0>, dim3(H, B), dim3(D), smem, st, A);
     note_launch();
     K3_TRY(check_launch("kda head"));
     prof_end("kda.core");

@@ -94,6 +94,8 @@ __global__ void __launch_bounds__(256) k_mla_prep(float *ql, float *c, uint16_t 
                                                   const float *kv_a_norm, const int *pos_p,
                                                   MlaDims d, int cap)
 {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double red[32];
     __shared__ float crope[256];
     const int b = blockIdx.x, tid = threadIdx.x;
@@ -167,6 +169,8 @@ __global__ void __launch_bounds__(256) k_mla_prep(float *ql, float *c, uint16_t 
 __global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, const float2 *rope_tab,
                              const int *pos_p, MlaDims d, int cap)
 {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float qs[256];
     __shared__ float part[8][128 + 4];
     const int h = blockIdx.x, jb = blockIdx.y, b = blockIdx.z;
@@ -296,6 +300,8 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
                                                      const uint16_t *cache, const int *pos_p,
                                                      MlaDims d, int cap)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     const int split = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
     const int pos = *pos_p;
@@ -530,6 +536,8 @@ __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *pa
                                                    const uint16_t *kv_b, const float *gate,
                                                    const int *pos_p, MlaDims d, int cap)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float cx[];   // [kv_lora]
     __shared__ float wsc[256 + 2 * 256];   // split weights, then partial column sums
     __shared__ float red[8];
@@ -740,11 +748,11 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
         rope_tab = rope_table(d.theta, d.qr, cap, st);
         if (!rope_tab) return k3d_status();
     }
-    k_mla_prep<<<B, 256, 0, st>>>(L.ql, L.c, cache, rope_tab, w->q_a_norm, w->kv_a_norm, pos, d, cap);
+    launch_pdl(k_mla_prep, dim3(B), dim3(256), 0, st, L.ql, L.c, cache, rope_tab, w->q_a_norm, w->kv_a_norm, pos, d, cap);
     note_launch();
     K3_TRY(check_launch("mla prep"));
     K3_TRY(gemv_bf16(L.q, L.ql, w->q_b, s->q_lora, d.H * d.qh, B, 0, st));
-    k_mla_absorb<<<dim3(d.H, d.kv_lora / 128, B), dim3(16, 8), 0, st>>>(L.qa, L.q, w->kv_b, rope_tab,
+    launch_pdl(k_mla_absorb, dim3(d.H, d.kv_lora / 128, B), dim3(16, 8), 0, st, L.qa, L.q, w->kv_b, rope_tab,
                                                                        pos, d, cap);
     note_launch();
     K3_TRY(check_launch("mla absorb"));
@@ -760,15 +768,15 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
         const size_t smem = mla_attn_smem(d.kvw);
         const dim3 grid(d.nsplit, (d.H + kAHG - 1) / kAHG, B);
         switch (d.kv_lora / 32) {
-        case 4: k_mla_attn_tc<4><<<grid, 128, smem, st>>>(L.part, L.qa, cache, pos, d, cap); break;
-        case 8: k_mla_attn_tc<8><<<grid, 128, smem, st>>>(L.part, L.qa, cache, pos, d, cap); break;
-        case 12: k_mla_attn_tc<12><<<grid, 128, smem, st>>>(L.part, L.qa, cache, pos, d, cap); break;
-        default: k_mla_attn_tc<16><<<grid, 128, smem, st>>>(L.part, L.qa, cache, pos, d, cap); break;
+        case 4: launch_pdl(k_mla_attn_tc<4>, dim3(grid), dim3(128), smem, st, L.part, L.qa, cache, pos, d, cap); break;
+        case 8: launch_pdl(k_mla_attn_tc<8>, dim3(grid), dim3(128), smem, st, L.part, L.qa, cache, pos, d, cap); break;
+        case 12: launch_pdl(k_mla_attn_tc<12>, dim3(grid), dim3(128), smem, st, L.part, L.qa, cache, pos, d, cap); break;
+        default: launch_pdl(k_mla_attn_tc<16>, dim3(grid), dim3(128), smem, st, L.part, L.qa, cache, pos, d, cap); break;
         }
         note_launch();
         K3_TRY(check_launch("mla attn"));
     }
-    k_mla_merge<<<dim3(d.H, d.vh / 32, B), 256, (size_t)d.kv_lora * 4, st>>>(
+    launch_pdl(k_mla_merge, dim3(d.H, d.vh / 32, B), dim3(256), (size_t)d.kv_lora * 4, st, 
         L.heads, L.part, w->kv_b, s->out_gate ? L.gate : nullptr, pos, d, cap);
     note_launch();
     K3_TRY(check_launch("mla merge"));

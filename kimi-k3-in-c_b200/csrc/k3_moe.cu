@@ -30,6 +30,8 @@ __global__ void __launch_bounds__(1024) k_moe_prep(const int *idx, int TK, int n
                                                    int lo, int hi, int *n_active,
                                                    int *act_expert, int *act_off, int *assign)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ int sm[];
     group_assignments(idx, TK, n_experts, lo, hi, n_active, act_expert, act_off, assign, sm);
 }
@@ -127,6 +129,8 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
                               const int *idx, const float *wts, const float *sh_out, int hidden,
                               int K, int lo, int hi, int accumulate)
 {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.y;
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= hidden) return;
@@ -544,7 +548,7 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     prof_end("moe.router");
     if (!grp.done) {
         const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
-        k_moe_prep<<<1, 1024, smem, st>>>(I, TK, s->n_experts, s->expert_lo, s->expert_hi,
+        launch_pdl(k_moe_prep, dim3(1), dim3(1024), smem, st, I, TK, s->n_experts, s->expert_lo, s->expert_hi,
                                           L.n_active, L.act_expert, L.act_off, L.assign);
         note_launch();
         K3_TRY(check_launch("moe prep"));
@@ -568,7 +572,7 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     if (shared && sst != st && cudaStreamWaitEvent(st, side_event(1), 0) != cudaSuccess)
         return fail(K3D_ECUDA, "moe: join from the side stream");
     dim3 grid((s->hidden + 255) / 256, T);
-    k_moe_combine<<<grid, 256, 0, st>>>(out, O.contrib, O.ks, O.slice, I, Wt, shared ? L.sh_out : nullptr,
+    launch_pdl(k_moe_combine, dim3(grid), dim3(256), 0, st, out, O.contrib, O.ks, O.slice, I, Wt, shared ? L.sh_out : nullptr,
                                         s->hidden, K, s->expert_lo, s->expert_hi, accumulate);
     note_launch();
     K3_TRY(check_launch("moe combine"));

@@ -295,6 +295,8 @@ __device__ __forceinline__ int item_count(const Job &J)
 
 __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
     // 1024-aligned base (the SWIZZLE_128B pattern is a function of the absolute address)
     const uint32_t raw = saddr(smem_raw);
@@ -536,12 +538,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 // bq + 4096 c, and 4 scale atoms at bs + 2048 c (piece p's scale for block 4a+i at byte
 // 512 a + 16 p + i; every other byte of an atom is zero).
 //
-// One lane per element of a 32-element block; per piece: the block maximum (one redux),
-// the E8M0 scale, the E2M1 rounding and the exact residual. Powers of two are
-// built from their bits (exact; 2^-127 is the one subnormal an E8M0 scale can be).
-__device__ __forceinline__ float pow2f(int k)
+// One lane per element of a 32-element block. Per piece, with m the block maximum of |r|
+// (one redux on the bits: non-negative floats order like their bits):
+//   scale 2^s, s = e - 2 if m <= 1.5 * 2^e else e - 1 (e = floor(log2 m)), so m / 2^s
+//   lies in (3, 6]; from the bits, the E8M0 code is s + 127 = E - 2 + (mantissa >
+//   0x400000), at least 0 (blocks below 2^-124 share the smallest scale, 2^-127);
+//   the E2M1 code of r / 2^s by the hardware conversion (round to nearest even; the
+//   scaled value never exceeds 6, so saturation never acts), and its value q;
+//   the residual (r / 2^s - q) * 2^s, exact: q is a neighbour of r / 2^s on the E2M1 grid,
+//   so the difference is a multiple of ulp(r / 2^s) no larger than it, and the result
+//   r - q 2^s is representable.
+// A block holding an inf or NaN gets scale code 255 (NaN) on every piece, zero codes.
+__device__ __forceinline__ uint32_t e2m1_code(float v)
 {
-    return k >= -126 ? __int_as_float((k + 127) << 23) : __int_as_float(0x00400000 >> (-127 - k));
+    uint32_t r;
+    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %1;\n\tcvt.u32.u8 %0, t;\n\t}"
+        : "=r"(r) : "f"(v));
+    return r & 0xFu;          // both halves hold v's code
 }
 
 __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, int blk, int lane)
@@ -558,43 +571,38 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
             *reinterpret_cast<uint4 *>(atom + 256 + 16 * (lane - 16)) = make_uint4(0, 0, 0, 0);
         }
     }
-    const bool bad = __any_sync(0xffffffffu, !isfinite(r));
-    for (int p = 0; p < kN; p++) {
-        // block maximum in one warp reduction: non-negative floats order like their bits
-        const float m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
-        int code;
-        if (bad) code = 255;
-        else if (m == 0.0f) code = 127;
-        else {
-            // e = floor(log2 m) from the bits (m may be subnormal)
-            const int bits = __float_as_int(m);
-            const int e = (bits >> 23) ? (bits >> 23) - 127 : -127 - (__clz(bits) - 9);
-            int sx = (m <= 1.5f * pow2f(max(e, -126)) * (e < -126 ? pow2f(e + 126) : 1.0f)) ? e - 2 : e - 1;
-            sx = max(-127, min(127, sx));
-            code = sx + 127;
+    int my_code = 255;                       // lane p < 16 keeps piece p's scale code
+    if (__any_sync(0xffffffffu, !isfinite(r))) {
+#pragma unroll
+        for (int p = 0; p < kN; p++)
+            if ((lane & 1) == 0)
+                tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] = 0;
+    } else {
+#pragma unroll
+        for (int p = 0; p < kN; p++) {
+            const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r)));
+            const int code = max(0, (int)(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0));
+            const float rs = __fmul_rn(r, __int_as_float((254 - code) << 23));   // r / 2^s, exact
+            uint32_t nib = e2m1_code(rs);
+            if ((nib & 7u) == 0u) nib = 0u;                                     // no -0 codes
+            const float q = __half2float(__ushort_as_half((unsigned short)(e2m1x2_to_f16x2(nib) & 0xffffu)));
+            const float sc = code ? __int_as_float(code << 23) : __int_as_float(0x00400000);
+            r = __fmul_rn(__fsub_rn(rs, q), sc);
+            if (lane == p) my_code = code;
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 1);
+            if ((lane & 1) == 0)
+                tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] =
+                    (uint8_t)(nib | (hi << 4));
         }
-        uint32_t nib = 0;
-        if (code != 255) {
-            const float a = fabsf(r) * pow2f(127 - code);
-            const uint32_t q3 = a < 0.25f ? 0u : a < 0.75f ? 1u : a < 1.25f ? 2u : a < 1.75f ? 3u
-                              : a < 2.5f ? 4u : a < 3.5f ? 5u : a < 5.0f ? 6u : 7u;
-            // E2M1 value of q3 (0, .5, 1, 1.5, 2, 3, 4, 6) times the scale, exactly
-            const float g = q3 < 4u ? 0.5f * (float)q3 : (float)(q3 & 1u ? 3u : 2u) * pow2f((int)(q3 >> 1) - 2);
-            const float val = g * pow2f(code - 127);
-            nib = q3 | (signbit(r) && q3 ? 8u : 0u);
-            r = signbit(r) ? r + val : r - val;
-        }
-        const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 1);
-        if ((lane & 1) == 0)
-            tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] =
-                (uint8_t)(nib | (hi << 4));
-        if (lane == 0) atom[16 * p + (j & 3)] = (uint8_t)code;
     }
+    if (lane < kN) atom[16 * lane + (j & 3)] = (uint8_t)my_code;
 }
 
 // B operands of fp32 vectors: grid (ceil(K/32 / 8), nvec), 256 threads, a warp per block.
 __global__ void k_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, size_t ld)
 {
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int blk = blockIdx.x * 8 + warp;
     if (blk >= K / 32) return;
@@ -611,6 +619,8 @@ __global__ void k_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, size_t
 __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks,
                                 size_t slice_stride, int inter, const int *count, int count_host)
 {
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int blk = blockIdx.x * 8 + warp;
     const int p = blockIdx.y;
@@ -672,6 +682,8 @@ __global__ void k_pretile(uint8_t *dc, uint8_t *ds, const uint8_t *c0, const uin
 // y[r] = sum over K slices of part[s][r] (single-expert mode)
 __global__ void k_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n)
 {
+    pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n) return;
     float acc = 0.0f;
@@ -719,7 +731,7 @@ int umma_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, int nvec, size_
 {
     if (nvec <= 0) return K3D_OK;
     dim3 grid((K / 32 + 7) / 8, nvec);
-    k_bsplit<<<grid, 256, 0, st>>>(bq, bs, x, K, ld);
+    launch_pdl(k_bsplit, dim3(grid), dim3(256), 0, st, bq, bs, x, K, ld);
     note_launch();
     return check_launch("umma bsplit");
 }
@@ -729,14 +741,14 @@ int umma_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks, size
 {
     if (npos <= 0) return K3D_OK;
     dim3 grid((inter / 32 + 7) / 8, npos);
-    k_bsplit_swiglu<<<grid, 256, 0, st>>>(bq, bs, part, ks, slice_stride, inter, count, npos);
+    launch_pdl(k_bsplit_swiglu, dim3(grid), dim3(256), 0, st, bq, bs, part, ks, slice_stride, inter, count, npos);
     note_launch();
     return check_launch("umma bsplit swiglu");
 }
 
 int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n, cudaStream_t st)
 {
-    k_slice_sum<<<(n + 255) / 256, 256, 0, st>>>(y, part, ks, slice_stride, n);
+    launch_pdl(k_slice_sum, dim3((n + 255) / 256), dim3(256), 0, st, y, part, ks, slice_stride, n);
     note_launch();
     return check_launch("umma slice sum");
 }
@@ -787,7 +799,7 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     const long long items = (long long)npos_max * J.ntiles * ks;
     if (items <= 0) return K3D_OK;
     const int grid = (int)(items < sm_count() ? items : sm_count());
-    k_mxfp4_umma<<<grid, kThreads, kSmemTotal, st>>>(J);
+    launch_pdl(k_mxfp4_umma, dim3(grid), dim3(kThreads), kSmemTotal, st, J);
     note_launch();
     return check_launch("mxfp4 umma");
 }

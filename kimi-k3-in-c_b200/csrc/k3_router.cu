@@ -607,6 +607,38 @@ template <> struct WChunk<float> {
     }
 };
 
+// atomic add with acquire-release semantics at GPU scope: it releases this thread's earlier
+// stores and, for the CTA that arrives last, acquires the stores the others released
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v)
+{
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Order-preserving code of a selection key: a larger float gives a larger code, -0 and +0
+// the same; -inf and NaN give 0, which the top-k never selects (the CPU's strict-greater
+// scan from -inf never selects them either).
+__device__ __forceinline__ uint32_t order_code(float v)
+{
+    if (!(v > -INFINITY)) return 0u;
+    const uint32_t u = __float_as_uint(__fadd_rn(v, 0.0f));
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// The largest of a lane's 16 codes (a max tree).
+__device__ __forceinline__ uint32_t umax16(const uint32_t c[16])
+{
+    uint32_t v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = max(c[i], c[i + 8]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = max(v[i], v[i + 4]);
+    v[0] = max(v[0], v[2]);
+    v[1] = max(v[1], v[3]);
+    return max(v[0], v[1]);
+}
+
 __device__ __forceinline__ float sigmoid_k(float v)
 {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-v)));
@@ -622,6 +654,8 @@ __host__ __device__ inline size_t fused_smem_bytes(int hidden, int n_experts)
 template <typename WT>
 __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
 {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char rsm[];
     __shared__ double p_s[2][4];
     __shared__ float p_a[2][4];
@@ -637,6 +671,12 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
     const float *xt = J.x + (size_t)t * hidden;
     const WT *W = static_cast<const WT *>(J.W);
     const size_t tE = (size_t)t * E;
+    if (threadIdx.x == 0) s_last = 0;
+    // loads whose latency would otherwise sit on the tail of phase 1: the writers' biases,
+    // and the expf table (constant memory) into this SM's constant cache
+    const int ew = e0 + (int)threadIdx.x;
+    const float bias_w = (threadIdx.x < 2 && ew < E && J.bias) ? __ldg(J.bias + ew) : 0.0f;
+    if (q == 3 && k3_exp2_tab_d[lane] == 0ull) s_last = 0;   // never true: keeps the load
 
     // ---------------------------------------------------------------- phase 1
     {
@@ -699,7 +739,7 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
             const double gam = n * u / (1.0 - n * u) * (1.0 + 0x1p-20);
             const double bound = __fma_rn(gam, Aup, 4.0 * u * fabs(S)) * (1.0 + 0x1p-20) + 0x1p-1074;
             const float flo = (float)__dsub_rn(S, bound), fhi = (float)__dadd_rn(S, bound);
-            const float b = J.bias ? __ldg(J.bias + e) : 0.0f;
+            const float b = bias_w;
             float lo, hi, sc = 0.0f;
             if (flo == fhi) {
                 sc = sigmoid_k(flo);
@@ -716,18 +756,15 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
             J.lo[tE + e] = lo;
             J.hi[tE + e] = hi;
             J.score[tE + e] = sc;
-            __threadfence();
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned prev = atomicAdd(&g_router_ctr[t], 1u);
-            s_last = (prev == gridDim.x - 1);
+            // one arrival per expert; the release publishes this thread's stores, and the
+            // thread that completes the count acquires everyone's
+            if (atom_add_acq_rel(&g_router_ctr[t], 1u) == (unsigned)E - 1) {
+                g_router_ctr[t] = 0;
+                s_last = 1;
+            }
         }
         __syncthreads();
         if (!s_last) return;
-        __threadfence();
-        if (threadIdx.x == 0) g_router_ctr[t] = 0;
     }
 
     // ---------------------------------------------------------------- phase 2
@@ -738,43 +775,68 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
     float *sv = hv + E;
     int *gsm = reinterpret_cast<int *>(sv + E);                 // 2 * E ints for the grouping
     unsigned char *settled = reinterpret_cast<unsigned char *>(gsm + 2 * E);
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const float l = __ldcg(J.lo + tE + e), h = __ldcg(J.hi + tE + e);
-        key[e] = l;
-        hv[e] = h;
-        sv[e] = __ldcg(J.score + tE + e);
-        settled[e] = (l == h);
+    {
+        // every value in flight at once (E <= 512, 128 threads)
+        float l4[4], h4[4], s4[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int e = threadIdx.x + 128 * k;
+            if (e < E) {
+                l4[k] = __ldcg(J.lo + tE + e);
+                h4[k] = __ldcg(J.hi + tE + e);
+                s4[k] = __ldcg(J.score + tE + e);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int e = threadIdx.x + 128 * k;
+            if (e < E) {
+                key[e] = l4[k];
+                hv[e] = h4[k];
+                sv[e] = s4[k];
+                settled[e] = (l4[k] == h4[k]);
+            }
+        }
     }
     __syncthreads();
     const int K = J.topk;
     bool x_staged = false;
     for (int iter = 0; iter <= E; iter++) {
         if (q == 0) {
-            // the register scan of k_router_topk_reg over the keys (lane l: experts l + 32k)
-            float v[16];
+            // top-k by repeated strict-greater max over the keys, lowest index on ties
+            // (k3_ops.c:459-466): per round one redux for the largest key and one for the
+            // lowest index holding it; lane l holds experts l + 32k, its lowest k holding
+            // the round's maximum found from a bit mask
+            uint32_t c[16];
 #pragma unroll
             for (int k = 0; k < 16; k++) {
                 const int e = lane + 32 * k;
-                v[k] = e < E ? key[e] : -INFINITY;
+                c[k] = e < E ? order_code(key[e]) : 0u;
             }
+            uint32_t bc = umax16(c);
             for (int j = 0; j < K; j++) {
-                float bv = -INFINITY;
+                const uint32_t m = __reduce_max_sync(0xffffffffu, bc);
                 int best = -1;
+                if (m != 0u) {
+                    uint32_t mask = 0u;
 #pragma unroll
-                for (int k = 0; k < 16; k++)
-                    if (v[k] > bv) { bv = v[k]; best = lane + 32 * k; }
-                warp_best(bv, best);
+                    for (int k = 0; k < 16; k++) mask |= (c[k] == m ? 1u : 0u) << k;
+                    const uint32_t cand = mask ? (uint32_t)(lane + 32 * (__ffs(mask) - 1)) : 0xffffffffu;
+                    best = (int)__reduce_min_sync(0xffffffffu, cand);
+                }
                 if (best >= 0 && (best & 31) == lane) {
+                    // the owning lane takes the entry out
 #pragma unroll
-                    for (int k = 0; k < 16; k++)
-                        if (lane + 32 * k == best) v[k] = -INFINITY;
+                    for (int k = 0; k < 16; k++) c[k] = (k == (best >> 5)) ? 0u : c[k];
+                    bc = umax16(c);
                 }
-                if (lane == 0) {
-                    s_isel[j] = best;
-                    s_m = best >= 0 ? bv : -INFINITY;
-                }
+                if (lane == 0) s_isel[j] = best;
             }
-            if (lane == 0) s_nneed = 0;
+            if (lane == 0) {
+                const int b = s_isel[K - 1];
+                s_m = b >= 0 ? key[b] : -INFINITY;
+                s_nneed = 0;
+            }
         }
         __syncthreads();
         for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -809,31 +871,47 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
             __syncthreads();
         }
     }
-    if (threadIdx.x == 0) {
-        int isel[K3_MAX_TOPK];
-        float wsel[K3_MAX_TOPK];
-        for (int j = 0; j < K; j++) {
-            const int b = s_isel[j];
-            isel[j] = b >= 0 ? b : 0;
-            wsel[j] = b >= 0 ? sv[b] : 0.0f;
+    if (q == 0) {
+        // weights (k3_ops.c:468-475): lane j < K fetches slot j; lane 0 forms the double
+        // sum in slot order and the reciprocal; lanes scale and store their slots
+        const bool rn = J.renorm && K > 1;
+        const int b0 = lane < K ? s_isel[lane] : -1;
+        const int b1 = lane + 32 < K ? s_isel[lane + 32] : -1;
+        float w0 = b0 >= 0 ? sv[b0] : 0.0f;
+        float w1 = b1 >= 0 ? sv[b1] : 0.0f;
+        float inv = 1.0f;
+        if (rn) {
+            double sum = 0.0;
+            for (int j = 0; j < K; j++) {
+                const float wj = __shfl_sync(0xffffffffu, j < 32 ? w0 : w1, j & 31);
+                sum = __dadd_rn(sum, (double)wj);
+            }
+            if (lane == 0) inv = (float)__ddiv_rn(1.0, __dadd_rn(sum, 1e-20));
+            inv = __shfl_sync(0xffffffffu, inv, 0);
+            w0 = __fmul_rn(w0, inv);
+            w1 = __fmul_rn(w1, inv);
         }
-        topk_finish(J.idx + (size_t)t * K, J.wts + (size_t)t * K, isel, wsel, K, J.renorm,
-                    J.routed_scale);
+        if (lane < K) {
+            J.idx[(size_t)t * K + lane] = b0 >= 0 ? b0 : 0;
+            J.wts[(size_t)t * K + lane] = __fmul_rn(w0, J.routed_scale);
+        }
+        if (lane + 32 < K) {
+            J.idx[(size_t)t * K + lane + 32] = b1 >= 0 ? b1 : 0;
+            J.wts[(size_t)t * K + lane + 32] = __fmul_rn(w1, J.routed_scale);
+        }
+        if (J.T > 1) __threadfence();
     }
     if (!J.n_active) return;
     // ---------------------------------------------------------------- grouping
+    __syncthreads();
     if (J.T > 1) {
         if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned prev = atomicAdd(&g_router_ctr[kRouterMaxT], 1u);
+            const unsigned prev = atom_add_acq_rel(&g_router_ctr[kRouterMaxT], 1u);
             s_last = (prev == (unsigned)J.T - 1);
+            if (s_last) g_router_ctr[kRouterMaxT] = 0;
         }
         __syncthreads();
         if (!s_last) return;
-        __threadfence();
-        if (threadIdx.x == 0) g_router_ctr[kRouterMaxT] = 0;
-    } else {
-        __syncthreads();
     }
     group_assignments(J.idx, J.T * K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
                       J.assign, gsm);
@@ -887,7 +965,7 @@ static int router_launch(int *idx, float *w, const float *x, const WT *W, const 
         static bool init = false;
         if (!init) { allow_smem_max(k_router_fused<WT>); init = true; }
         dim3 grid((n_experts + 1) / 2, T);
-        k_router_fused<WT><<<grid, 128, smem, s>>>(J);
+        launch_pdl(k_router_fused<WT>, dim3(grid), dim3(128), smem, s, J);
         note_launch();
         if (grp) grp->done = 1;
         return check_launch("router");

@@ -30,9 +30,44 @@ __device__ __forceinline__ double block_sum_d(double v, double *red)
     return red[0];
 }
 
-// one CTA per row
+// one CTA per row, the row and the weights held in registers: x and w are loaded together
+// up front (one memory round trip), the same per-thread order as k_rmsnorm below.
+template <int PER>
+__global__ void __launch_bounds__(1024) k_rmsnorm_reg(float *y, const float *x, const float *w,
+                                                      int n, float eps)
+{
+    pdl_wait();
+    pdl_trigger();
+    __shared__ double red[32];
+    const float *xr = x + (size_t)blockIdx.x * n;
+    float *yr = y + (size_t)blockIdx.x * n;
+    float xv[PER], wv[PER];
+#pragma unroll
+    for (int k = 0; k < PER; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        xv[k] = i < n ? xr[i] : 0.0f;
+        wv[k] = i < n ? __ldg(w + i) : 0.0f;
+    }
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < PER; k++) {
+        const double v = (double)xv[k];
+        ss = fma(v, v, ss);
+    }
+    ss = block_sum_d(ss, red);
+    const float inv = (float)(1.0 / sqrt(ss / (double)n + (double)eps));
+#pragma unroll
+    for (int k = 0; k < PER; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < n) yr[i] = __fmul_rn(__fmul_rn(wv[k], xv[k]), inv);
+    }
+}
+
+// one CTA per row (any n)
 __global__ void k_rmsnorm(float *y, const float *x, const float *w, int n, float eps)
 {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double red[32];
     const float *xr = x + (size_t)blockIdx.x * n;
     float *yr = y + (size_t)blockIdx.x * n;
@@ -154,7 +189,10 @@ static int blocks_for(size_t n, int threads)
 int rmsnorm(float *y, const float *x, const float *w, int n, int rows, float eps, cudaStream_t s)
 {
     if (rows <= 0 || n <= 0) return K3D_OK;
-    k_rmsnorm<<<rows, n >= 1024 ? 1024 : 256, 0, s>>>(y, x, w, n, eps);
+    if (n > 4096 && n <= 8192)
+        launch_pdl(k_rmsnorm_reg<8>, dim3(rows), dim3(1024), 0, s, y, x, w, n, eps);
+    else
+        launch_pdl(k_rmsnorm, dim3(rows), dim3(n >= 1024 ? 1024 : 256), 0, s, y, x, w, n, eps);
     note_launch();
     return check_launch("rmsnorm");
 }

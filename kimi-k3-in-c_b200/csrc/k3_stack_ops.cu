@@ -7,6 +7,8 @@ namespace k3 {
 
 __global__ void k_embed(float *h, const int *ids, const uint16_t *table, int hidden, int vocab)
 {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     int id = ids[b];
     if (id < 0 || id >= vocab) {
@@ -20,12 +22,16 @@ __global__ void k_embed(float *h, const int *ids, const uint16_t *table, int hid
 
 __global__ void k_add_f32(float *y, const float *x, size_t n)
 {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         y[i] = __fadd_rn(y[i], x[i]);
 }
 
 __global__ void k_add_i32(int *p, int n, int delta)
 {
+    pdl_wait();
+    pdl_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] += delta;
 }
@@ -40,7 +46,7 @@ int k3d_embed_bf16(float *h, const int *ids, const uint16_t *table, int B, int h
 {
     K3_TRY(ensure_ctx());
     if (!h || !ids || !table || B < 1 || hidden < 1) return fail(K3D_EINVAL, "k3d_embed_bf16");
-    k_embed<<<dim3((hidden + 1023) / 1024, B), 256, 0, stream()>>>(h, ids, table, hidden, vocab);
+    launch_pdl(k_embed, dim3((hidden + 1023) / 1024, B), dim3(256), 0, stream(), h, ids, table, hidden, vocab);
     note_launch();
     return check_launch("embed");
 }
@@ -77,7 +83,7 @@ int k3d_add_f32(float *y, const float *x, size_t n)
     if (!n) return K3D_OK;
     size_t g = (n + 255) / 256;
     if (g > (size_t)sm_count() * 8) g = (size_t)sm_count() * 8;
-    k_add_f32<<<(int)g, 256, 0, stream()>>>(y, x, n);
+    launch_pdl(k_add_f32, dim3((int)g), dim3(256), 0, stream(), y, x, n);
     note_launch();
     return check_launch("add_f32");
 }
@@ -86,7 +92,7 @@ int k3d_add_i32(int *p, int n, int delta)
 {
     K3_TRY(ensure_ctx());
     if (!p || n < 1) return fail(K3D_EINVAL, "k3d_add_i32");
-    k_add_i32<<<(n + 255) / 256, 256, 0, stream()>>>(p, n, delta);
+    launch_pdl(k_add_i32, dim3((n + 255) / 256), dim3(256), 0, stream(), p, n, delta);
     note_launch();
     return check_launch("add_i32");
 }
