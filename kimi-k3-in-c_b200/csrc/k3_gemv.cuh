@@ -17,23 +17,38 @@ namespace k3 {
 // their chunks hit eight distinct bank groups.
 __device__ __forceinline__ int xb_idx(int c, int k) { return 2 * c + (k ^ ((c >> 2) & 1)); }
 
-// Loads are unrolled so a thread has several in flight (a loop with one load per
-// iteration would pay the memory latency once per iteration).
+// Each thread issues up to 8 loads before its first store (a loop with a run-time count
+// and one load per iteration would pay the memory latency once per iteration).
 __device__ __forceinline__ void stage_x_bf16(float4 *xs, const float *x, int in)
 {
     const int nf4 = in >> 2;
+    const int nb = blockDim.x;
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
         const float4 *x4 = reinterpret_cast<const float4 *>(x);
-#pragma unroll 8
-        for (int f = threadIdx.x; f < nf4; f += blockDim.x) {
-            const int c = f >> 1, k = f & 1;
-            xs[xb_idx(c, k)] = __ldg(x4 + f);
+        for (int f0 = threadIdx.x; f0 < nf4; f0 += 8 * nb) {
+            float4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (f0 + i * nb < nf4) v[i] = __ldg(x4 + f0 + i * nb);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int f = f0 + i * nb;
+                if (f < nf4) xs[xb_idx(f >> 1, f & 1)] = v[i];
+            }
         }
     } else {
-#pragma unroll 8
-        for (int f = threadIdx.x; f < nf4; f += blockDim.x) {
-            const int c = f >> 1, k = f & 1;
-            xs[xb_idx(c, k)] = make_float4(x[4 * f], x[4 * f + 1], x[4 * f + 2], x[4 * f + 3]);
+        for (int f0 = threadIdx.x; f0 < nf4; f0 += 8 * nb) {
+            float4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int f = f0 + i * nb;
+                if (f < nf4) v[i] = make_float4(x[4 * f], x[4 * f + 1], x[4 * f + 2], x[4 * f + 3]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int f = f0 + i * nb;
+                if (f < nf4) xs[xb_idx(f >> 1, f & 1)] = v[i];
+            }
         }
     }
 }

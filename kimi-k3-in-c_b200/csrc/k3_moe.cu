@@ -139,9 +139,8 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
     const float prev = accumulate ? *o : 0.0f;
     float acc = 0.0f;
     // top-k slots in groups of 8: the group's expert ids, weights and contributions are all
-    // loaded before the ordered sum, so the loads overlap instead of chaining. The slice
-    // loop is outermost with the 8 slots inside it, so every slice's 8 loads are independent
-    // and the unrolled loop keeps 8 x 4 loads in flight.
+    // loaded before the ordered sum, so the loads overlap instead of chaining; the slices
+    // go in groups of 4 whose 8 x 4 loads are all issued before they are added.
     for (int j0 = 0; j0 < K; j0 += 8) {
         int e[8];
         float w[8], v[8];
@@ -154,10 +153,20 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
             c[k] = contrib + (size_t)a * hidden + r;
             v[k] = c[k][0];
         }
-#pragma unroll 4
-        for (int s = 1; s < ks; s++) {
+        for (int s0 = 1; s0 < ks; s0 += 4) {
+            float t4[4][8];
 #pragma unroll
-            for (int k = 0; k < 8; k++) v[k] += c[k][(size_t)s * slice_stride];
+            for (int i = 0; i < 4; i++)
+                if (s0 + i < ks) {
+#pragma unroll
+                    for (int k = 0; k < 8; k++) t4[i][k] = c[k][(size_t)(s0 + i) * slice_stride];
+                }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (s0 + i < ks) {
+#pragma unroll
+                    for (int k = 0; k < 8; k++) v[k] += t4[i][k];
+                }
         }
 #pragma unroll
         for (int k = 0; k < 8; k++) {
@@ -302,13 +311,15 @@ static int run_experts(const MoeWork &mw, const int *idx, const int *count, int 
         const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
         if (!x_split) K3_TRY(umma_bsplit(B.bq_x, B.bs_x, x, hidden, T, hidden, st));
         prof_begin("experts.gateup");
+        // the gate/up work list comes from the router just before (MoE); the down pass's
+        // does not depend on the split just before it, nor does a single expert's
         K3_TRY(umma_launch(0, layout, mw, idx, count, TK, hidden, inter, ks_gu, B.bq_x, B.bs_x, topk,
-                           B.part_gu, 2 * inter, sl_gu, st));
+                           B.part_gu, 2 * inter, sl_gu, st, mw.single_mode ? 1 : 0));
         prof_end("experts.gateup");
         K3_TRY(umma_bsplit_swiglu(B.bq_a, B.bs_a, B.part_gu, ks_gu, sl_gu, inter, count, TK, st));
         prof_begin("experts.down");
         K3_TRY(umma_launch(1, layout, mw, idx, count, TK, inter, hidden, ks_d, B.bq_a, B.bs_a, 1,
-                           B.part_d, hidden, sl_d, st));
+                           B.part_d, hidden, sl_d, st, 1));
         prof_end("experts.down");
         O.contrib = B.part_d;
         O.ks = ks_d;

@@ -30,11 +30,19 @@ __device__ __forceinline__ int xs_idx(int c, int k) { return (c << 3) + (k ^ (c 
 __device__ __forceinline__ void stage_x_mxfp4(float4 *xs, const float *x, int in)
 {
     const int nf4 = in >> 2;
+    const int nb = blockDim.x;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
-#pragma unroll 8
-    for (int f = threadIdx.x; f < nf4; f += blockDim.x) {
-        const int c = f >> 3, k = f & 7;
-        xs[xs_idx(c, k)] = x4[f];
+    // up to 8 loads in flight per thread before the stores
+    for (int f0 = threadIdx.x; f0 < nf4; f0 += 8 * nb) {
+        float4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            if (f0 + i * nb < nf4) v[i] = x4[f0 + i * nb];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int f = f0 + i * nb;
+            if (f < nf4) xs[xs_idx(f >> 3, f & 7)] = v[i];
+        }
     }
 }
 

@@ -84,6 +84,10 @@ struct Job {
     int vec_div;             // vector of assignment a = a / vec_div (unless vec_pos)
     int vec_pos;             // 1: B vector = grouped position p (down: act pieces by position)
     int out_pos;             // 1: partial row block = p (gate/up), else the assignment a
+    int early;               // 1: the work list and the weights do not depend on the kernel
+                             //    launched just before (only the B operand does): the work
+                             //    list is read and the first stages' weights are requested
+                             //    before waiting for that kernel
     float *part;             // [ks][cap][out_w]
     int out_w;               // gate/up: 2 * inter (gate rows then up rows); down: rows
     size_t slice_stride;     // floats per K slice
@@ -277,8 +281,8 @@ __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
         a = p;
         q = J.single;
     } else {
-        a = __ldg(J.assign + p);
-        q = J.table[__ldg(J.idx + a)];
+        a = __ldcg(J.assign + p);
+        q = J.table[__ldcg(J.idx + a)];
     }
     if (J.mode == GATEUP) { it.c0 = q.p1; it.c1 = q.p3; it.s0 = q.s1; it.s1 = q.s3; }
     else { it.c0 = it.c1 = q.p2; it.s0 = it.s1 = q.s2; }
@@ -295,8 +299,6 @@ __device__ __forceinline__ int item_count(const Job &J)
 
 __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 {
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
     // 1024-aligned base (the SWIZZLE_128B pattern is a function of the absolute address)
     const uint32_t raw = saddr(smem_raw);
@@ -335,6 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // programmatic dependent launch: the set-up above overlapped the kernel before this
+    // one; unless the work list is independent of it, wait for it before reading the list
+    if (!J.early) pdl_wait();
 
     const int total = item_count(J);
     const int i_beg = (int)((long long)blockIdx.x * total / gridDim.x);
@@ -354,18 +359,59 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
         for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) items[i - r0] = decode(J, i);
         __syncthreads();
         const int nr = r1 - r0;
+        const bool prefetch = J.early && J.tiled && r0 == i_beg;
+        if (r0 == i_beg) {
+            // early: everyone but the tiled producer (which first requests the weights of
+            // its first stages) waits for the kernel before this one here
+            if (J.early && !(prefetch && threadIdx.x == 0)) pdl_wait();
+            pdl_trigger();
+        }
 
         if (warp < 4 && J.tiled) {
             // ------------------------------------------ producer, tiled layout: one thread
             // streams each stage as four bulk copies (weight tile, its scale atoms, the B
             // tile and its scale atoms), all completing on the stage's mbarrier
             if (threadIdx.x == 0) {
+                // early launch: the weight tiles and scale atoms of the first stages are
+                // requested before waiting for the kernel that writes the B operand
+                int pre = 0;
+                if (prefetch) {
+                    pre = min(kStages, nr * J.cps);
+                    for (int h = 0; h < pre; h++) {
+                        const ItemEnt &it = items[h / J.cps];
+                        if ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) continue;
+                        const int chunk = it.s * J.cps + h % J.cps;
+                        const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
+                        const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
+                        const size_t tix = (size_t)it.tile * J.nch + chunk;
+                        mbar_expect_tx(fb, kStageTx);
+                        bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
+                        bulk_g2s(sb + kOffSFA, it.s0 + tix * kTileSF, kTileSF, fb);
+                    }
+                    pdl_wait();
+                    for (int h = 0; h < pre; h++) {
+                        const ItemEnt &it = items[h / J.cps];
+                        const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
+                        if ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) {
+                            k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
+                            mbar_arrive(fb);
+                            continue;
+                        }
+                        const int chunk = it.s * J.cps + h % J.cps;
+                        const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
+                        const size_t vbase = (size_t)it.vec * J.nch;
+                        bulk_g2s(sb + kOffB, J.bq + (vbase + chunk) * kTileB, kTileB, fb);
+                        bulk_g2s(sb + kOffSFB, J.bs + (vbase + chunk) * kTileSF, kTileSF, fb);
+                    }
+                }
+                int h = 0;       // stage index within this round
                 for (int k = 0; k < nr && !stop; k++) {
                     const ItemEnt &it = items[k];
                     const bool aligned = ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) == 0);
                     if (!aligned) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
                     const size_t vbase = (size_t)it.vec * J.nch;
-                    for (int c = 0; c < J.cps; c++) {
+                    for (int c = 0; c < J.cps; c++, h++) {
+                        if (h < pre) { g_prod++; continue; }     // issued above
                         const int chunk = it.s * J.cps + c;
                         const int st = g_prod % kStages;
                         if (g_prod >= kStages &&
@@ -628,10 +674,24 @@ __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int
     const float *pa = part + (size_t)p * 2 * inter + blk * 32 + lane;
     const int n = count ? *count : count_host;
     float g = 0.0f, u = 0.0f;
-#pragma unroll 16
-    for (int s = 0; s < ks; s++) {       // unrolled: the slices' loads are all in flight
-        g += pa[(size_t)s * slice_stride];
-        u += pa[(size_t)s * slice_stride + inter];
+    // slices in groups of 16, every load of a group issued before the ordered sums (a loop
+    // with a run-time count and one load per iteration would pay the latency per slice)
+    for (int s0 = 0; s0 < ks; s0 += 16) {
+        float gv[16], uv[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (s0 + i < ks) {
+                gv[i] = pa[(size_t)(s0 + i) * slice_stride];
+                uv[i] = pa[(size_t)(s0 + i) * slice_stride + inter];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (s0 + i < ks) {
+                g += gv[i];
+                u += uv[i];
+            }
+        }
     }
     if (p >= n) return;
     const float act = silu_f(g) * u;
@@ -687,8 +747,15 @@ __global__ void k_slice_sum(float *y, const float *part, int ks, size_t slice_st
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n) return;
     float acc = 0.0f;
-#pragma unroll 16
-    for (int s = 0; s < ks; s++) acc += part[(size_t)s * slice_stride + r];
+    for (int s0 = 0; s0 < ks; s0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (s0 + i < ks) v[i] = part[(size_t)(s0 + i) * slice_stride + r];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (s0 + i < ks) acc += v[i];
+    }
     y[r] = acc;
 }
 
@@ -757,7 +824,8 @@ int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int
 // smaller). MoE mode: w.table/assign/idx; single mode: w.single_mode with positions 0..n-1.
 int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
                 int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
-                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st)
+                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
+                int early)
 {
     if (!umma_supported(K, rows, mode)) return fail(K3D_EINVAL, "umma: unsupported K=%d rows=%d", K, rows);
     const int chunks = K / kStageK;
@@ -786,6 +854,7 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     // combine
     J.out_pos = mode == GATEUP;
     J.vec_pos = mode == DOWN;
+    J.early = early;
     J.part = part;
     J.out_w = out_w;
     J.slice_stride = slice_stride;

@@ -44,7 +44,8 @@ int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int
                    cudaStream_t st);
 int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
                 int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
-                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st);
+                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
+                int early);
 
 // k3_router.cu
 size_t router_ws_bytes(int T, int n_experts);
