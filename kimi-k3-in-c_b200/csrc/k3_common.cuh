@@ -27,6 +27,9 @@ int sm_count();
 void note_launch(int n = 1);
 // Checks cudaGetLastError() after a launch; records K3D_ECUDA on failure.
 int check_launch(const char *what);
+// Reads the device error flag (call after a synchronisation): K3D_OK, or K3D_EDEVICE
+// recorded with the kernel's site and location details.
+int device_flag_status();
 
 // Raises a kernel's dynamic shared memory limit to the device's opt-in maximum minus
 // the kernel's static shared memory (cudaFuncSetAttribute rejects anything above that).
@@ -103,10 +106,23 @@ bool is_device_ptr(const void *p);
 // ---------------------------------------------------------------- device side ----
 // Device error flag: first (code, site) pair wins. Read back by k3d_sync().
 extern __device__ int k3_dev_err[2];
+// Where the first error happened, when its kernel says (three integers and a valid flag).
+extern __device__ int k3_dev_diag[4];
 
 __device__ __forceinline__ void k3_raise(int code, int site)
 {
     if (atomicCAS(&k3_dev_err[0], 0, code) == 0) k3_dev_err[1] = site;
+}
+
+__device__ __forceinline__ void k3_raise_at(int code, int site, int a, int b, int c)
+{
+    if (atomicCAS(&k3_dev_err[0], 0, code) == 0) {
+        k3_dev_err[1] = site;
+        k3_dev_diag[0] = a;
+        k3_dev_diag[1] = b;
+        k3_dev_diag[2] = c;
+        k3_dev_diag[3] = 1;
+    }
 }
 
 // Waits until every earlier kernel of the stream has completed and its memory operations

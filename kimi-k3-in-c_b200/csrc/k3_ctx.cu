@@ -14,6 +14,7 @@
 #include "k3_common.cuh"
 
 __device__ int k3_dev_err[2];
+__device__ int k3_dev_diag[4];
 
 namespace k3 {
 
@@ -337,11 +338,24 @@ int Stage::finish()
     if (any_host) {
         cudaError_t e = cudaStreamSynchronize(g.stream);
         if (e != cudaSuccess) return fail(K3D_ECUDA, "stream sync: %s", cudaGetErrorString(e));
-        int flag[2] = {0, 0};
-        cudaMemcpyFromSymbol(flag, k3_dev_err, sizeof flag);
-        if (flag[0]) return fail(K3D_EDEVICE, "device error %d at site %d", flag[0], flag[1]);
+        return device_flag_status();
     }
     return K3D_OK;
+}
+
+// The device error flag (after a synchronisation), as a status with the kernel's location
+// details when it gave any.
+int device_flag_status()
+{
+    int flag[2] = {0, 0};
+    cudaMemcpyFromSymbol(flag, k3_dev_err, sizeof flag);
+    if (!flag[0]) return K3D_OK;
+    int diag[4] = {0, 0, 0, 0};
+    cudaMemcpyFromSymbol(diag, k3_dev_diag, sizeof diag);
+    if (diag[3])
+        return fail(K3D_EDEVICE, "device error %d at site %d (%d, %d, %d)", flag[0], flag[1], diag[0],
+                    diag[1], diag[2]);
+    return fail(K3D_EDEVICE, "device error %d at site %d", flag[0], flag[1]);
 }
 
 }  // namespace k3
@@ -375,8 +389,9 @@ int k3d_init(int device)
     g.stream = s;
     g.own_stream = true;
     g.sms = p.multiProcessorCount;
-    int zero[2] = {0, 0};
-    cudaMemcpyToSymbol(k3_dev_err, zero, sizeof zero);
+    int zero[4] = {0, 0, 0, 0};
+    cudaMemcpyToSymbol(k3_dev_err, zero, 2 * sizeof(int));
+    cudaMemcpyToSymbol(k3_dev_diag, zero, sizeof zero);
     g.ready = true;
     return K3D_OK;
 }
@@ -390,8 +405,9 @@ void k3d_clear_status(void)
     g.status = 0;
     g.msg[0] = 0;
     if (g.ready) {
-        int zero[2] = {0, 0};
-        cudaMemcpyToSymbol(k3_dev_err, zero, sizeof zero);
+        int zero[4] = {0, 0, 0, 0};
+        cudaMemcpyToSymbol(k3_dev_err, zero, 2 * sizeof(int));
+        cudaMemcpyToSymbol(k3_dev_diag, zero, sizeof zero);
     }
 }
 
@@ -515,10 +531,7 @@ int k3d_sync(void)
     K3_TRY(ensure_ctx());
     cudaError_t e = cudaStreamSynchronize(g.stream);
     if (e != cudaSuccess) return fail(K3D_ECUDA, "k3d_sync: %s", cudaGetErrorString(e));
-    int flag[2] = {0, 0};
-    cudaMemcpyFromSymbol(flag, k3_dev_err, sizeof flag);
-    if (flag[0]) return fail(K3D_EDEVICE, "device error %d at site %d", flag[0], flag[1]);
-    return K3D_OK;
+    return device_flag_status();
 }
 
 void *k3d_stream(void) { ensure_ctx(); return (void *)g.stream; }

@@ -1,6 +1,8 @@
 // k3_gemv.cu -- fp32 and bf16 GEMVs: k3_matmul and k3_matmul_bf16 (include/k3/k3.h,
 // following k3_ops.c:265-291 and 1108-1213) and k3d_gemv_bf16, plus the fused
 // gate|up -> SiLU*mul GEMV used by the shared and dense SwiGLU MLPs.
+#include <cstdlib>
+
 #include "k3_gemv.cuh"
 #include "k3_ops.cuh"
 
@@ -273,6 +275,15 @@ __global__ void k_argmax_finish(int *next, const unsigned long long *key, int T)
 
 static bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+// The streamed GEMVs (k3_gemv_stream.cu) where the shape allows, on the library stream
+// (work on the side stream, which runs beside the main stream's one-CTA-per-SM kernels,
+// keeps the register-staged kernels); K3_GEMV_STREAM=0 in the environment selects the
+// register-staged kernels everywhere.
+static const bool g_gemv_stream = [] {
+    const char *v = getenv("K3_GEMV_STREAM");
+    return !(v && v[0] == '0');
+}();
+
 int grid_for(int rows, int rows_per_cta);
 // CTAs for `rows` rows when one pass of a CTA covers rows_per_pass rows: one pass per CTA
 // up to 8 CTAs per SM, grid-striding beyond that.
@@ -288,6 +299,11 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
               int accumulate, cudaStream_t s)
 {
     if (out <= 0 || T <= 0) return K3D_OK;
+    if (T <= 4 && g_gemv_stream && s == stream()) {
+        float *ys[1] = {y};
+        const int rows[1] = {out};
+        if (gemv_stream_multi(1, &W, ys, rows, x, in, T, accumulate, s)) return check_launch("gemv bf16 stream");
+    }
     const bool fast = (in % 8) == 0 && al16(W) && (size_t)in * 4 * min(T, 4) <= 200 * 1024;
     if (!fast) {
         for (int t = 0; t < T; t++) {
@@ -321,6 +337,8 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
                      int in, int inter, int T, cudaStream_t s)
 {
     if (inter <= 0 || T <= 0) return K3D_OK;
+    if (T <= 4 && g_gemv_stream && s == stream() && gemv_stream_swiglu(act, x, Wg, Wu, in, inter, T, s))
+        return check_launch("gemv bf16 swiglu stream");
     if ((in % 8) != 0 || !al16(Wg) || !al16(Wu) || (size_t)in * 4 * 4 > 200 * 1024)
         return fail(K3D_EINVAL, "swiglu gemv needs in %% 8 == 0 and aligned rows (in=%d)", in);
     static bool init = false;
@@ -340,6 +358,8 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
 {
     if (nseg < 1 || nseg > 8 || T < 1 || T > 4)
         return fail(K3D_EINVAL, "multi-segment GEMV: %d segments, T=%d", nseg, T);
+    if (g_gemv_stream && s == stream() && gemv_stream_multi(nseg, W, y, rows, x, in, T, 0, s))
+        return check_launch("gemv bf16 multi stream");
     Segs S;
     S.n = nseg;
     S.start[0] = 0;
@@ -368,6 +388,11 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
     if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
                ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
+    if (g_gemv_stream && s == stream() && gemv_stream_argmax(y, key, x, W, in, out, T, s)) {
+        launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);
+        note_launch();
+        return check_launch("lm head argmax stream");
+    }
     launch_pdl(k_gemv_bf16_argmax<2, 7>, dim3(grid_for(out, 16)), dim3(256), (size_t)T * in * 4, s, y, key, x, W, in, out, T);
     launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);
     note_launch(2);

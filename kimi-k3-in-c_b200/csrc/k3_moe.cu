@@ -571,6 +571,7 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     mw.act_off = L.act_off;
     mw.assign = L.assign;
     mw.K = K;
+    mw.n_experts = s->n_experts;
     ExpertOut O{L.eb.contrib, 1, 0};
     if (early_split && sst != st && cudaStreamWaitEvent(st, side_event(2), 0) != cudaSuccess)
         return fail(K3D_ECUDA, "moe: join of the split from the side stream");

@@ -15,6 +15,7 @@ struct MoeWork {
     int single_mode;
     int ntok_single;            // single mode: assignments a = 0..ntok-1, token t = a
     int K;                      // top-k (token t = a / K)
+    int n_experts;              // MoE mode: size of the expert table
 };
 
 __device__ __forceinline__ void work_item(const MoeWork &w, int u, K3ExpertQ &q, int &beg,

@@ -84,6 +84,7 @@ struct Job {
     int vec_div;             // vector of assignment a = a / vec_div (unless vec_pos)
     int vec_pos;             // 1: B vector = grouped position p (down: act pieces by position)
     int out_pos;             // 1: partial row block = p (gate/up), else the assignment a
+    int n_experts;           // MoE mode: expert ids must lie in [0, n_experts)
     int early;               // 1: the work list and the weights do not depend on the kernel
                              //    launched just before (only the B operand does): the work
                              //    list is read and the first stages' weights are requested
@@ -282,7 +283,17 @@ __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
         q = J.single;
     } else {
         a = __ldcg(J.assign + p);
-        q = J.table[__ldcg(J.idx + a)];
+        const int e = (a >= 0 && a < J.count_host) ? __ldcg(J.idx + a) : -1;
+        if (e < 0 || e >= J.n_experts) {
+            // a corrupt work list: the item is skipped (no copies), the error recorded
+            k3_raise(K3D_EBOUND, K3_SITE_MXFP4);
+            it.c0 = it.c1 = it.s0 = it.s1 = nullptr;
+            it.out = 0;
+            it.tile = it.s = 0;
+            it.vec = 0;
+            return it;
+        }
+        q = J.table[e];
     }
     if (J.mode == GATEUP) { it.c0 = q.p1; it.c1 = q.p3; it.s0 = q.s1; it.s1 = q.s3; }
     else { it.c0 = it.c1 = q.p2; it.s0 = it.s1 = q.s2; }
@@ -379,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                     pre = min(kStages, nr * J.cps);
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h / J.cps];
-                        if ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) continue;
+                        if (!it.c0 || (((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) continue;
                         const int chunk = it.s * J.cps + h % J.cps;
                         const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
                         const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
@@ -392,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h / J.cps];
                         const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
-                        if ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) {
+                        if (!it.c0 || (((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) {
                             k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
                             mbar_arrive(fb);
                             continue;
@@ -407,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                 int h = 0;       // stage index within this round
                 for (int k = 0; k < nr && !stop; k++) {
                     const ItemEnt &it = items[k];
-                    const bool aligned = ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) == 0);
+                    const bool aligned = it.c0 && ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) == 0);
                     if (!aligned) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
                     const size_t vbase = (size_t)it.vec * J.nch;
                     for (int c = 0; c < J.cps; c++, h++) {
@@ -442,7 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             for (int k = 0; k < nr && !stop; k++) {
                 const ItemEnt &it = items[k];
                 const int r0w = J.mode == GATEUP ? it.tile * 64 : it.tile * 128;
-                const bool aligned = ((((uintptr_t)it.c0 | (uintptr_t)it.c1 | (uintptr_t)it.s0 |
+                const bool aligned = it.c0 && it.c1 &&
+                                     ((((uintptr_t)it.c0 | (uintptr_t)it.c1 | (uintptr_t)it.s0 |
                                         (uintptr_t)it.s1) & 15u) == 0);
                 if (!aligned && tid == 0) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
                 const size_t vbase = (size_t)it.vec * J.nch;
@@ -855,6 +867,7 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     J.out_pos = mode == GATEUP;
     J.vec_pos = mode == DOWN;
     J.early = early;
+    J.n_experts = w.n_experts;
     J.part = part;
     J.out_w = out_w;
     J.slice_stride = slice_stride;

@@ -16,6 +16,14 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
 int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint16_t *Wu,
                      int in, int inter, int T, cudaStream_t s);
 int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStream_t s);
+// k3_gemv_stream.cu: the streamed forms; each returns 1 when it launched, 0 when the shape
+// needs the register-staged kernels instead
+int gemv_stream_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
+                      const float *x, int in, int T, int accumulate, cudaStream_t st);
+int gemv_stream_swiglu(float *act, const float *x, const uint16_t *Wg, const uint16_t *Wu,
+                       int in, int inter, int T, cudaStream_t st);
+int gemv_stream_argmax(float *y, unsigned long long *key, const float *x, const uint16_t *W,
+                       int in, int out, int T, cudaStream_t st);
 int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
                     const float *x, int in, int T, cudaStream_t s);
 int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
