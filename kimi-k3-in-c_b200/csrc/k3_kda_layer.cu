@@ -61,10 +61,9 @@ __device__ __forceinline__ float conv_silu(const float *w, float *hist, float cu
 template <int KC>
 __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
 {
-    pdl_wait();
-    pdl_trigger();
-    extern __shared__ float sh[];
+    extern __shared__ __align__(16) float sh[];
     __shared__ double red[8];
+    __shared__ __align__(8) unsigned long long st_bar;
     const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
     const int D = A.D, H = A.H, K = KC > 0 ? KC : A.K, P = H * D, hst = K - 1;
     float *St = sh;
@@ -78,8 +77,21 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
     float *hq = conv + (size_t)c * hst;
     float *hk = conv + (size_t)P * hst + (size_t)c * hst;
     float *hv = conv + (size_t)2 * P * hst + (size_t)c * hst;
+    // The state tile (written by this layer's previous step, never by the kernels just
+    // before) streams in as one bulk copy, requested before the programmatic wait.
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&st_bar);
+    const bool bulk_ok = (((uintptr_t)S) & 15u) == 0;
+    if (j == 0 && bulk_ok) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(bar));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const uint32_t bytes = (uint32_t)(D * D * 4);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     :: "r"((uint32_t)__cvta_generic_to_shared(St)), "l"(S), "r"(bytes), "r"(bar) : "memory");
+    }
     if constexpr (KC > 0) {
-        // all loads first
+        // every load of the thread is issued before any arithmetic; the weights, the conv
+        // history and the per-head constants before the programmatic wait as well
         float wq[KC], wk[KC], wv[KC], xq[KC], xk[KC], xv[KC];
 #pragma unroll
         for (int t = 0; t < KC; t++) {
@@ -89,10 +101,15 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
         }
 #pragma unroll
         for (int t = 0; t < KC - 1; t++) { xq[t] = hq[t]; xk[t] = hk[t]; xv[t] = hv[t]; }
+        dtb = A.dt_bias[c];
+        alog = A.A_log[h];
+        onw = A.o_norm[j];
+        pdl_wait();
+        pdl_trigger();
         xq[KC - 1] = A.qp[bp]; xk[KC - 1] = A.kp[bp]; xv[KC - 1] = A.vp[bp];
-        gpv = A.gp[bp]; zv = A.z[bp]; dtb = A.dt_bias[c];
-        bpv = A.bp[(size_t)b * H + h]; alog = A.A_log[h]; onw = A.o_norm[j];
-        {
+        gpv = A.gp[bp]; zv = A.z[bp];
+        bpv = A.bp[(size_t)b * H + h];
+        if (!bulk_ok) {
             const float4 *S4 = reinterpret_cast<const float4 *>(S);
             float4 *T4 = reinterpret_cast<float4 *>(St);
 #pragma unroll 8
@@ -115,8 +132,9 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
         kv = __fmul_rn(ak, sigm(ak));
         vv = __fmul_rn(av, sigm(av));
     } else {
-        // stage the state tile
-        {
+        pdl_wait();
+        pdl_trigger();
+        if (!bulk_ok) {
             const float4 *S4 = reinterpret_cast<const float4 *>(S);
             float4 *T4 = reinterpret_cast<float4 *>(St);
 #pragma unroll 8
@@ -149,6 +167,17 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
     qs[j] = qv;
     ks[j] = kv;
     as[j] = expf(gdec);
+    if (bulk_ok) {
+        // the state tile has landed (bounded wait: on a time-out the device error flag is
+        // raised and the tile is read as it is)
+        uint32_t ok = 0;
+        const long long t0 = clock64();
+        do {
+            asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+                         "selp.b32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(bar) : "memory");
+            if (!ok && clock64() - t0 > 4000000000LL) { k3_raise(K3D_ETIMEOUT, K3_SITE_KDA); break; }
+        } while (!ok);
+    }
     __syncthreads();
     // delta-rule step, column j (the CPU's order and roundings)
     float u = 0.0f;
