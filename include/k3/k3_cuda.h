@@ -246,6 +246,13 @@ size_t k3d_kda_layer_ws_bytes(const K3dKdaShape *s, int B);
 size_t k3d_kda_state_floats(const K3dKdaShape *s);
 int    k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dKdaShape *s,
                             int B, float *state, void *ws, size_t ws_bytes);
+/* The same layer taking the raw residual h as its input: it applies the layer's input
+ * RMSNorm (weights norm_w [hidden], eps; k3_rmsnorm's arithmetic, k3_ops.c:94-102) itself,
+ * inside the projection GEMV's load where that kernel runs, saving the separate norm
+ * launch and its output buffer. No reference counterpart (the CPU engine norms first). */
+int    k3d_kda_layer_decode_normed(float *h, const float *norm_w, float eps, const K3dKdaW *w,
+                                   const K3dKdaShape *s, int B, float *state, void *ws,
+                                   size_t ws_bytes);
 
 /* ------------------------------------------------------------------- MLA ---- */
 typedef struct {
@@ -274,6 +281,11 @@ size_t k3d_mla_ws_bytes(const K3dMlaShape *s, int B, int cap);
 int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *s,
                    int B, uint16_t *cache, int cap, const int *pos, int accumulate,
                    void *ws, size_t ws_bytes);
+/* k3d_mla_decode with x the raw residual, RMS-normalised by the layer itself (norm_w
+ * [hidden], eps), as k3d_kda_layer_decode_normed. No reference counterpart. */
+int k3d_mla_decode_normed(float *out, const float *x, const float *norm_w, float eps,
+                          const K3dMlaW *w, const K3dMlaShape *s, int B, uint16_t *cache,
+                          int cap, const int *pos, int accumulate, void *ws, size_t ws_bytes);
 
 /* ------------------------------------------------------------- small ops ---- */
 int k3d_rmsnorm(float *y, const float *x, const float *w, int n, int rows, float eps);
@@ -289,6 +301,11 @@ int k3d_swiglu_mlp_bf16(float *h, const float *x, const uint16_t *gate, const ui
  * (argmax_ of k3_run.c:134-135); logits may be NULL; key_ws holds B 8-byte keys. */
 int k3d_lm_head_argmax(int *next, float *logits, const float *x, const uint16_t *W, int vocab,
                        int hidden, int B, void *key_ws);
+/* The LM head on the raw residual, with the final RMSNorm (norm_w, eps) applied on load.
+ * No reference counterpart. */
+int k3d_lm_head_argmax_normed(int *next, float *logits, const float *x, const float *norm_w,
+                              float eps, const uint16_t *W, int vocab, int hidden, int B,
+                              void *key_ws);
 /* y[i] += x[i] for i < n (device floats) */
 int k3d_add_f32(float *y, const float *x, size_t n);
 /* p[i] += delta for i < n (device ints; advances cache positions inside a graph) */

@@ -353,13 +353,25 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
     return check_launch("gemv bf16 swiglu");
 }
 
+const float *norm_to_scratch(const float *x, const NormIn &ni, int n, int rows, cudaStream_t s)
+{
+    float *xn = (float *)scratch((size_t)n * rows * sizeof(float), 0);
+    if (!xn) return nullptr;
+    if (rmsnorm(xn, x, ni.w, n, rows, ni.eps, s)) return nullptr;
+    return xn;
+}
+
 int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
-                    const float *x, int in, int T, cudaStream_t s)
+                    const float *x, int in, int T, cudaStream_t s, const NormIn *ni)
 {
     if (nseg < 1 || nseg > 8 || T < 1 || T > 4)
         return fail(K3D_EINVAL, "multi-segment GEMV: %d segments, T=%d", nseg, T);
-    if (g_gemv_stream && s == stream() && gemv_stream_multi(nseg, W, y, rows, x, in, T, 0, s))
+    if (g_gemv_stream && s == stream() && gemv_stream_multi(nseg, W, y, rows, x, in, T, 0, s, ni))
         return check_launch("gemv bf16 multi stream");
+    if (ni) {
+        x = norm_to_scratch(x, *ni, in, T, s);
+        if (!x) return k3d_status();
+    }
     Segs S;
     S.n = nseg;
     S.start[0] = 0;
@@ -380,7 +392,7 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
 }
 
 int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
-                     const uint16_t *W, int in, int out, int T, cudaStream_t s)
+                     const uint16_t *W, int in, int out, int T, cudaStream_t s, const NormIn *ni)
 {
     if (T < 1 || T > 4 || (in % 8) != 0 || !al16(W))
         return fail(K3D_EINVAL, "lm head: T=%d in=%d", T, in);
@@ -388,10 +400,14 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
     if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
                ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
-    if (g_gemv_stream && s == stream() && gemv_stream_argmax(y, key, x, W, in, out, T, s)) {
+    if (g_gemv_stream && s == stream() && gemv_stream_argmax(y, key, x, W, in, out, T, s, ni)) {
         launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);
         note_launch();
         return check_launch("lm head argmax stream");
+    }
+    if (ni) {
+        x = norm_to_scratch(x, *ni, in, T, s);
+        if (!x) return k3d_status();
     }
     launch_pdl(k_gemv_bf16_argmax<2, 7>, dim3(grid_for(out, 16)), dim3(256), (size_t)T * in * 4, s, y, key, x, W, in, out, T);
     launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);

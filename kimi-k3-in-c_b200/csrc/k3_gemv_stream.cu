@@ -46,6 +46,8 @@ struct Args {
     int in, T;
     int accumulate;           // PLAIN: y += W x
     unsigned long long *key;  // ARGMAX: [T]
+    const float *norm_w;      // non-null: x is a raw residual, normalised on load (RMSNorm
+    float norm_eps;           //   with these weights, k3_rmsnorm's arithmetic; in <= 8192)
     int stages;               // ring depth
     int R;                    // units per stage
     int stage_bytes;          // R * rows-per-unit * in * 2
@@ -169,11 +171,63 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_stream(Args A)
     }
 
     // -------------------------------------------------------------------- consumers
+    const int nf4 = in >> 2;
+    constexpr int nt = kWarps * 32;
+    // RMSNorm on load: this thread's norm weights (float4 f = tid + k * nt) are constants,
+    // loaded before the programmatic wait
+    float4 wn[8];
+    if (A.norm_w) {
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if ((int)threadIdx.x + k * nt < nf4)
+                wn[k] = __ldg(reinterpret_cast<const float4 *>(A.norm_w) + threadIdx.x + k * nt);
+    }
     pdl_wait();
     pdl_trigger();
-    const int nf4 = in >> 2;
     for (int t = 0; t < NT; t++)
-        if (t < A.T) stage_x_part(xs + (size_t)t * nf4, A.x + (size_t)t * in, in, threadIdx.x, kWarps * 32);
+        if (t < A.T) stage_x_part(xs + (size_t)t * nf4, A.x + (size_t)t * in, in, threadIdx.x, nt);
+    if (A.norm_w) {
+        // x = (w * x) * inv_rms(x) per token, with the sum of squares in double as k3_rmsnorm
+        // does; each thread rescales the float4s it staged
+        __shared__ double red[kWarps][4];
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            if (t >= A.T) break;
+            double ss = 0.0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int f = threadIdx.x + k * nt;
+                if (f < nf4) {
+                    const float4 v = xs[(size_t)t * nf4 + xb_idx(f >> 1, f & 1)];
+                    ss = fma((double)v.x, (double)v.x, ss);
+                    ss = fma((double)v.y, (double)v.y, ss);
+                    ss = fma((double)v.z, (double)v.z, ss);
+                    ss = fma((double)v.w, (double)v.w, ss);
+                }
+            }
+            ss = warp_sum_d(ss);
+            if (lane == 0) red[warp][t] = ss;
+        }
+        asm volatile("bar.sync 1, %0;" :: "n"(nt) : "memory");
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            if (t >= A.T) break;
+            double tot = 0.0;
+            for (int w = 0; w < kWarps; w++) tot += red[w][t];
+            const float inv = (float)(1.0 / sqrt(tot / (double)in + (double)A.norm_eps));
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int f = threadIdx.x + k * nt;
+                if (f < nf4) {
+                    float4 &v = xs[(size_t)t * nf4 + xb_idx(f >> 1, f & 1)];
+                    v.x = __fmul_rn(__fmul_rn(wn[k].x, v.x), inv);
+                    v.y = __fmul_rn(__fmul_rn(wn[k].y, v.y), inv);
+                    v.z = __fmul_rn(__fmul_rn(wn[k].z, v.z), inv);
+                    v.w = __fmul_rn(__fmul_rn(wn[k].w, v.w), inv);
+                }
+            }
+        }
+    }
     asm volatile("bar.sync 1, %0;" :: "n"(kWarps * 32) : "memory");
 
     const int nch = in >> 3;                        // 8-element chunks of a row
@@ -261,12 +315,13 @@ template <int MODE>
 static int stream_launch(Args &A, cudaStream_t st)
 {
     if (A.T < 1 || A.T > 4 || (A.in % 8) != 0 || A.in < 512) return 0;
+    if (A.norm_w && (A.in > 8 * 4 * kWarps * 32 || ((uintptr_t)A.norm_w & 15u) != 0)) return 0;
     if (((uintptr_t)A.x & 15u) != 0) return 0;
     const int nw = MODE == SWIGLU ? 2 : A.nseg;
     for (int i = 0; i < nw; i++)
         if (((uintptr_t)A.W[i] & 15u) != 0) return 0;
     const size_t xbytes = (size_t)A.T * A.in * sizeof(float);
-    const size_t limit = 227 * 1024;
+    const size_t limit = 226 * 1024;    // the opt-in maximum less room for static shared memory
     const size_t unitb = (size_t)(MODE == SWIGLU ? 2 : 1) * A.in * 2;
     A.R = (int)std::max<size_t>(1, kStageTarget / unitb);
     A.stage_bytes = (int)((size_t)A.R * unitb);
@@ -293,7 +348,8 @@ static int stream_launch(Args &A, cudaStream_t st)
 }
 
 int gemv_stream_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
-                      const float *x, int in, int T, int accumulate, cudaStream_t st)
+                      const float *x, int in, int T, int accumulate, cudaStream_t st,
+                      const NormIn *ni)
 {
     if (nseg < 1 || nseg > 8) return 0;
     Args A{};
@@ -308,6 +364,8 @@ int gemv_stream_multi(int nseg, const uint16_t *const *W, float *const *y, const
     A.in = in;
     A.T = T;
     A.accumulate = accumulate;
+    A.norm_w = ni ? ni->w : nullptr;
+    A.norm_eps = ni ? ni->eps : 0.0f;
     return stream_launch<PLAIN>(A, st);
 }
 
@@ -328,7 +386,7 @@ int gemv_stream_swiglu(float *act, const float *x, const uint16_t *Wg, const uin
 }
 
 int gemv_stream_argmax(float *y, unsigned long long *key, const float *x, const uint16_t *W,
-                       int in, int out, int T, cudaStream_t st)
+                       int in, int out, int T, cudaStream_t st, const NormIn *ni)
 {
     Args A{};
     A.nseg = 1;
@@ -340,6 +398,8 @@ int gemv_stream_argmax(float *y, unsigned long long *key, const float *x, const 
     A.in = in;
     A.T = T;
     A.key = key;
+    A.norm_w = ni ? ni->w : nullptr;
+    A.norm_eps = ni ? ni->eps : 0.0f;
     return stream_launch<ARGMAX>(A, st);
 }
 

@@ -224,8 +224,11 @@ size_t k3d_kda_state_floats(const K3dKdaShape *s)
     return (size_t)s->heads * s->head_dim * s->head_dim + 3 * P * (size_t)(s->conv_k - 1);
 }
 
-int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dKdaShape *s,
-                         int B, float *state, void *ws, size_t ws_bytes)
+}  // extern "C"
+
+// The layer; with ni, xn is the raw residual and the projection GEMV normalises it.
+static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K3dKdaW *w,
+                            const K3dKdaShape *s, int B, float *state, void *ws, size_t ws_bytes)
 {
     K3_TRY(ensure_ctx());
     if (!h || !xn || !w || !s || !state || !ws) return fail(K3D_EINVAL, "kda layer null pointer");
@@ -247,7 +250,7 @@ int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dK
     const uint16_t *Ws[6] = {w->q, w->k, w->v, w->g, w->b, w->f_a};
     float *Ys[6] = {qp, kp, vp, gp, bp, fa};
     const int rows[6] = {P, P, P, P, H, D};
-    K3_TRY(gemv_bf16_multi(6, Ws, Ys, rows, xn, s->hidden, B, st));
+    K3_TRY(gemv_bf16_multi(6, Ws, Ys, rows, xn, s->hidden, B, st, ni));
     K3_TRY(gemv_bf16(z, fa, w->f_b, D, P, B, 0, st));
     prof_end("kda.proj_in");
     prof_begin("kda.core");
@@ -274,6 +277,23 @@ int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dK
     K3_TRY(gemv_bf16(h, heads, w->o, P, s->hidden, B, 1, st));
     prof_end("kda.proj_out");
     return K3D_OK;
+}
+
+extern "C" {
+
+int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dKdaShape *s,
+                         int B, float *state, void *ws, size_t ws_bytes)
+{
+    return kda_layer_decode(h, xn, nullptr, w, s, B, state, ws, ws_bytes);
+}
+
+int k3d_kda_layer_decode_normed(float *h, const float *norm_w, float eps, const K3dKdaW *w,
+                                const K3dKdaShape *s, int B, float *state, void *ws,
+                                size_t ws_bytes)
+{
+    if (!norm_w) return fail(K3D_EINVAL, "kda layer: null norm weights");
+    const NormIn ni{norm_w, eps};
+    return kda_layer_decode(h, h, &ni, w, s, B, state, ws, ws_bytes);
 }
 
 }  // extern "C"

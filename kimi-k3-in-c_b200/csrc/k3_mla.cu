@@ -719,7 +719,7 @@ static const float2 *rope_table(float theta, int qr, int cap, cudaStream_t st)
 
 int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *s, int B,
                uint16_t *cache, int cap, const int *pos, int accumulate, void *ws,
-               cudaStream_t st)
+               cudaStream_t st, const NormIn *ni = nullptr)
 {
     MlaWs L = mla_layout(s, B, cap, ws);
     MlaDims d;
@@ -734,8 +734,12 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
         float *Ys[3] = {L.ql, L.c, L.gate};
         const int rows[3] = {s->q_lora, d.kvw, d.H * d.vh};
         if (B <= 4) {
-            K3_TRY(gemv_bf16_multi(s->out_gate ? 3 : 2, Ws, Ys, rows, x, s->hidden, B, st));
+            K3_TRY(gemv_bf16_multi(s->out_gate ? 3 : 2, Ws, Ys, rows, x, s->hidden, B, st, ni));
         } else {
+            if (ni) {
+                x = norm_to_scratch(x, *ni, s->hidden, B, st);
+                if (!x) return k3d_status();
+            }
             K3_TRY(gemv_bf16(L.ql, x, w->q_a, s->hidden, s->q_lora, B, 0, st));
             K3_TRY(gemv_bf16(L.c, x, w->kv_a, s->hidden, d.kvw, B, 0, st));
             if (s->out_gate) K3_TRY(gemv_bf16(L.gate, x, w->g, s->hidden, d.H * d.vh, B, 0, st));
@@ -799,9 +803,9 @@ size_t k3d_mla_ws_bytes(const K3dMlaShape *s, int B, int cap)
     return mla_layout(s, B, cap, nullptr).total + 256;
 }
 
-int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *s, int B,
-                   uint16_t *cache, int cap, const int *pos, int accumulate, void *ws,
-                   size_t ws_bytes)
+static int mla_decode_checked(float *out, const float *x, const NormIn *ni, const K3dMlaW *w,
+                              const K3dMlaShape *s, int B, uint16_t *cache, int cap,
+                              const int *pos, int accumulate, void *ws, size_t ws_bytes)
 {
     K3_TRY(ensure_ctx());
     if (!out || !x || !w || !s || !cache || !pos || !ws)
@@ -817,7 +821,23 @@ int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaSha
                                 "512, even rope, (kv_lora + rope) %% 16, nope + rope <= 256, "
                                 "v_head %% 32, q_lora <= 2048");
     if (ws_bytes < k3d_mla_ws_bytes(s, B, cap)) return fail(K3D_EINVAL, "k3d_mla_decode workspace");
-    return mla_decode(out, x, w, s, B, cache, cap, pos, accumulate, ws, stream());
+    return mla_decode(out, x, w, s, B, cache, cap, pos, accumulate, ws, stream(), ni);
+}
+
+int k3d_mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *s, int B,
+                   uint16_t *cache, int cap, const int *pos, int accumulate, void *ws,
+                   size_t ws_bytes)
+{
+    return mla_decode_checked(out, x, nullptr, w, s, B, cache, cap, pos, accumulate, ws, ws_bytes);
+}
+
+int k3d_mla_decode_normed(float *out, const float *x, const float *norm_w, float eps,
+                          const K3dMlaW *w, const K3dMlaShape *s, int B, uint16_t *cache,
+                          int cap, const int *pos, int accumulate, void *ws, size_t ws_bytes)
+{
+    if (!norm_w) return fail(K3D_EINVAL, "k3d_mla_decode_normed: null norm weights");
+    const NormIn ni{norm_w, eps};
+    return mla_decode_checked(out, x, &ni, w, s, B, cache, cap, pos, accumulate, ws, ws_bytes);
 }
 
 }  // extern "C"

@@ -16,18 +16,30 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
 int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint16_t *Wu,
                      int in, int inter, int T, cudaStream_t s);
 int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStream_t s);
+// RMSNorm of the input done by the consuming GEMV (x is then the raw residual stream).
+struct NormIn {
+    const float *w;
+    float eps;
+};
 // k3_gemv_stream.cu: the streamed forms; each returns 1 when it launched, 0 when the shape
 // needs the register-staged kernels instead
 int gemv_stream_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
-                      const float *x, int in, int T, int accumulate, cudaStream_t st);
+                      const float *x, int in, int T, int accumulate, cudaStream_t st,
+                      const NormIn *ni = nullptr);
 int gemv_stream_swiglu(float *act, const float *x, const uint16_t *Wg, const uint16_t *Wu,
                        int in, int inter, int T, cudaStream_t st);
 int gemv_stream_argmax(float *y, unsigned long long *key, const float *x, const uint16_t *W,
-                       int in, int out, int T, cudaStream_t st);
+                       int in, int out, int T, cudaStream_t st, const NormIn *ni = nullptr);
+// With ni, x is the raw residual stream and is RMS-normalised first (in the streamed
+// kernel's load when it runs, else by a separate rmsnorm into the library scratch).
 int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
-                    const float *x, int in, int T, cudaStream_t s);
+                    const float *x, int in, int T, cudaStream_t s, const NormIn *ni = nullptr);
 int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
-                     const uint16_t *W, int in, int out, int T, cudaStream_t s);
+                     const uint16_t *W, int in, int out, int T, cudaStream_t s,
+                     const NormIn *ni = nullptr);
+// x RMS-normalised into the library scratch (slot 0) for consumers that cannot normalise on
+// load; returns the normalised copy, or null with the error recorded.
+const float *norm_to_scratch(const float *x, const NormIn &ni, int n, int rows, cudaStream_t s);
 // tagged weight: wdt 0 fp32, 1 bf16
 int gemv_tagged(float *y, const float *x, const void *W, int wdt, int in, int out,
                 cudaStream_t s);

@@ -76,6 +76,20 @@ int k3d_lm_head_argmax(int *next, float *logits, const float *x, const uint16_t 
     return r;
 }
 
+int k3d_lm_head_argmax_normed(int *next, float *logits, const float *x, const float *norm_w,
+                              float eps, const uint16_t *W, int vocab, int hidden, int B,
+                              void *key_ws)
+{
+    K3_TRY(ensure_ctx());
+    if (!next || !x || !norm_w || !W || !key_ws) return fail(K3D_EINVAL, "k3d_lm_head_argmax_normed");
+    const NormIn ni{norm_w, eps};
+    prof_begin("lm_head");
+    const int r = gemv_bf16_argmax(logits, (unsigned long long *)key_ws, next, x, W, hidden, vocab, B,
+                                   stream(), &ni);
+    prof_end("lm_head");
+    return r;
+}
+
 int k3d_add_f32(float *y, const float *x, size_t n)
 {
     K3_TRY(ensure_ctx());

@@ -358,13 +358,13 @@ static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
     TRY(k3d_embed_bf16(m->h, ids, m->embed, B, E, c->vocab));
     for (int l = 0; l < c->n_layers; l++) {
         K3sLayer *L = &m->L[l];
-        TRY(k3d_rmsnorm(m->xn, m->h, L->in_norm, E, B, c->eps));
+        /* the layer applies its input RMSNorm itself (inside its projection GEMV) */
         if (L->is_mla)
-            TRY(k3d_mla_decode(m->h, m->xn, &L->mla, &c->mla, B, L->cache, c->ctx_cap, m->pos, 1,
-                               m->ws, m->ws_bytes));
+            TRY(k3d_mla_decode_normed(m->h, m->h, L->in_norm, c->eps, &L->mla, &c->mla, B, L->cache,
+                                      c->ctx_cap, m->pos, 1, m->ws, m->ws_bytes));
         else
-            TRY(k3d_kda_layer_decode(m->h, m->xn, &L->kda, &L->kshape, B, L->kda_state, m->ws,
-                                     m->ws_bytes));
+            TRY(k3d_kda_layer_decode_normed(m->h, L->in_norm, c->eps, &L->kda, &L->kshape, B,
+                                            L->kda_state, m->ws, m->ws_bytes));
         TRY(k3d_rmsnorm(m->xn, m->h, L->post_norm, E, B, c->eps));
         if (L->is_dense) {
             TRY(k3d_swiglu_mlp_bf16(m->h, m->xn, L->dg, L->du, L->dd, E, c->dense_inter, B, 1,
@@ -377,8 +377,8 @@ static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
             TRY(k3d_moe_swiglu(m->h, m->xn, &L->moe, &c->moe, B, 1, NULL, NULL, m->ws, m->ws_bytes));
         }
     }
-    TRY(k3d_rmsnorm(m->xn, m->h, m->final_norm, E, B, c->eps));
-    TRY(k3d_lm_head_argmax(next, logits, m->xn, m->lm_head, c->vocab, E, B, m->key));
+    TRY(k3d_lm_head_argmax_normed(next, logits, m->h, m->final_norm, c->eps, m->lm_head, c->vocab,
+                                  E, B, m->key));
     TRY(k3d_add_i32(m->pos, 1, 1));
 #undef TRY
     return K3D_OK;

@@ -202,15 +202,20 @@ _PROTOS = {
     "k3d_mla_ws_bytes": (sz, [C.POINTER(K3dMlaShape), i32, i32]),
     "k3d_mla_decode": (i32, [vp, vp, C.POINTER(K3dMlaW), C.POINTER(K3dMlaShape), i32, vp, i32, vp,
                              i32, vp, sz]),
+    "k3d_mla_decode_normed": (i32, [vp, vp, vp, f32, C.POINTER(K3dMlaW), C.POINTER(K3dMlaShape), i32, vp,
+                                    i32, vp, i32, vp, sz]),
     "k3d_rmsnorm": (i32, [vp, vp, vp, i32, i32, f32]),
     "k3d_embed_bf16": (i32, [vp, vp, vp, i32, i32, i32]),
     "k3d_swiglu_mlp_bf16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "k3d_lm_head_argmax": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
+    "k3d_lm_head_argmax_normed": (i32, [vp, vp, vp, vp, f32, vp, i32, i32, i32, vp]),
     "k3d_add_f32": (i32, [vp, vp, sz]),
     "k3d_add_i32": (i32, [vp, i32, i32]),
     "k3d_kda_layer_ws_bytes": (sz, [C.POINTER(K3dKdaShape), i32]),
     "k3d_kda_state_floats": (sz, [C.POINTER(K3dKdaShape)]),
     "k3d_kda_layer_decode": (i32, [vp, vp, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32, vp, vp, sz]),
+    "k3d_kda_layer_decode_normed": (i32, [vp, vp, f32, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32,
+                                          vp, vp, sz]),
     "k3d_silu_mul": (i32, [vp, vp, i32, i32]),
     # EP
     "k3d_ep_unique_id": (i32, [vp]),

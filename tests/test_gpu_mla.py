@@ -92,3 +92,60 @@ def test_mla_decode_rejects_position_beyond_capacity(k3):
     k3.k3d_device_error(ctypes.byref(code), ctypes.byref(site))
     assert code.value == k3cuda.K3D_EBOUND
     k3.k3d_clear_status()
+
+
+def test_mla_decode_normed_matches_separate_norm(k3):
+    """k3d_mla_decode_normed on the raw residual (the input RMSNorm applied inside the
+    projection GEMV's load) equals k3d_rmsnorm followed by k3d_mla_decode, to within the
+    rounding of the sum of squares (a different reduction order)."""
+    d, B, cap, L = DIMS, 1, 256, 100
+    w, cache, _ = make(7, d, B, cap, L)
+    g = synth.rng(8)
+    h = (g.standard_normal((B, d["hidden"])) * 3.0).astype(np.float32)
+    nw = (1.0 + 0.1 * g.standard_normal(d["hidden"])).astype(np.float32)
+    eps = 1e-6
+    H, NW = k3cuda.DevBuf.from_array(h), k3cuda.DevBuf.from_array(nw)
+    XN = k3cuda.DevBuf(h.nbytes)
+    k3cuda.check(k3.k3d_rmsnorm(XN.ptr, H.ptr, NW.ptr, d["hidden"], B, eps))
+    k3cuda.check(k3.k3d_sync())
+    xn = XN.download(np.float32, (B, d["hidden"]))
+    want, want_cache = run_gpu(k3, d, w, cache, xn, L, cap)
+
+    shape = k3cuda.K3dMlaShape(d["hidden"], d["H"], d["q_lora"], d["kv_lora"], d["qn"], d["qr"],
+                               d["vh"], d["theta"], d["eps"], 1)
+    bufs = {k: k3cuda.DevBuf.from_array(v) for k, v in w.items()}
+    mw = k3cuda.K3dMlaW(*(bufs[k].ptr for k in ("q_a", "q_b", "kv_a", "kv_b", "o", "g",
+                                                 "q_a_norm", "kv_a_norm")))
+    C = k3cuda.DevBuf.from_array(cache)
+    O = k3cuda.DevBuf.from_array(np.zeros((B, d["hidden"]), np.float32))
+    P = k3cuda.DevBuf.from_array(np.array([L], np.int32))
+    n = k3.k3d_mla_ws_bytes(ctypes.byref(shape), B, cap)
+    WS = k3cuda.DevBuf(n)
+    k3cuda.check(k3.k3d_mla_decode_normed(O.ptr, H.ptr, NW.ptr, eps, ctypes.byref(mw),
+                                          ctypes.byref(shape), B, C.ptr, cap, P.ptr, 0, WS.ptr, n))
+    k3cuda.check(k3.k3d_sync())
+    got = O.download(np.float32, (B, d["hidden"]))
+    assert max_rel_err(got, want) <= 1e-5
+    got_cache = C.download(np.uint16, cache.shape)
+    assert np.array_equal(got_cache[:, :L], want_cache[:, :L])
+
+
+def test_lm_head_normed_matches_separate_norm(k3):
+    g = synth.rng(9)
+    hidden, vocab = 7168, 16384
+    W = synth.bf16_normal(g, (vocab, hidden), 0.02)
+    h = (g.standard_normal((1, hidden)) * 2.0).astype(np.float32)
+    nw = (1.0 + 0.1 * g.standard_normal(hidden)).astype(np.float32)
+    Wd, H, NW = (k3cuda.DevBuf.from_array(a) for a in (W, h, nw))
+    XN = k3cuda.DevBuf(h.nbytes)
+    key = k3cuda.DevBuf(64)
+    L1, L2 = k3cuda.DevBuf(vocab * 4), k3cuda.DevBuf(vocab * 4)
+    n1, n2 = k3cuda.DevBuf(16), k3cuda.DevBuf(16)
+    k3cuda.check(k3.k3d_rmsnorm(XN.ptr, H.ptr, NW.ptr, hidden, 1, 1e-6))
+    k3cuda.check(k3.k3d_lm_head_argmax(n1.ptr, L1.ptr, XN.ptr, Wd.ptr, vocab, hidden, 1, key.ptr))
+    k3cuda.check(k3.k3d_lm_head_argmax_normed(n2.ptr, L2.ptr, H.ptr, NW.ptr, 1e-6, Wd.ptr, vocab,
+                                              hidden, 1, key.ptr))
+    k3cuda.check(k3.k3d_sync())
+    a, b = L1.download(np.float32, vocab), L2.download(np.float32, vocab)
+    assert max_rel_err(b, a) <= 1e-5
+    assert int(n2.download(np.int32, 1)[0]) == int(np.argmax(b))
