@@ -10,13 +10,17 @@
 //
 // THE ACTIVATION OPERAND. The tensor core takes B in E2M1 too, so each fp32 activation
 // vector is written as a sum of 16 E2M1 "pieces" with their own per-32 E8M0 scales:
-//   r_0 = x;  piece p = round_to_E2M1(r_p / 2^s_p) with s_p the smallest exponent that
-//   fits the block maximum of |r_p| into [0, 6];  r_{p+1} = r_p - piece_p * 2^s_p.
-// Every step is exact in fp32 (a power-of-two scaling, and a subtraction of the nearest
-// grid point, which Sterbenz's lemma makes exact), and each piece shrinks the block
-// maximum by at least 3x, so 16 pieces leave a residual below 3^-16 ~ 2e-8 of the block
-// maximum. The 16 pieces are the 16 columns of B (N = 16): one MMA produces the 16
-// partial dot products of a 128-row tile, and the epilogue adds them. E8M0 code 255 in the
+//   r_0 = x;  piece p = round_to_E2M1(r_p / 2^s_p);  r_{p+1} = r_p - piece_p * 2^s_p,
+// with s_0 the smallest exponent that fits the block maximum of |r_0| into [0, 6], then
+// s_1 = s_0 - 2 and s_{p+1} = s_p - 3: rounding to the E2M1 grid {0, .5, 1, 1.5, 2, 3, 4, 6}
+// leaves |r_1| <= 2^s_0 (grid spacing 2 in [4, 6]) and, once |r_p / 2^s_p| <= 4,
+// |r_{p+1}| <= 2^(s_p - 1) (spacing at most 1), so every scaled residual stays within
+// [-4, 4] and 16 pieces leave a residual below 2^-46 of the block maximum (in practice 0:
+// the ~9 pieces that hold a float's 24 bits take all of it). Every step is exact in fp32
+// (a power-of-two scaling, and a subtraction of the nearest grid point, a multiple of
+// ulp(r / 2^s) no larger than r / 2^s). The schedule needs one block maximum per block,
+// not one per piece. The 16 pieces are the 16 columns of B (N = 16): one MMA produces the
+// 16 partial dot products of a 128-row tile, and the epilogue adds them. E8M0 code 255 in the
 // weights (NaN to the hardware) is replaced by 0 (2^-127) on its way to tensor memory; the
 // CPU engine treats 255 as zero, and 2^-127 * 6 * |piece| is below any fp32 output ulp.
 //
@@ -308,6 +312,104 @@ __device__ __forceinline__ int item_count(const Job &J)
     return n * J.ntiles * J.ks;
 }
 
+__device__ __forceinline__ bool item_ok(const ItemEnt &it)
+{
+    return it.c0 && ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) == 0);
+}
+
+// Tiled layout: the weight tile of one stage and its scale atoms, completing on `fb`.
+__device__ __forceinline__ void issue_weights(uint32_t sb, uint32_t fb, const Job &J, const ItemEnt &it,
+                                              int chunk)
+{
+    const size_t tix = (size_t)it.tile * J.nch + chunk;
+    bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
+    bulk_g2s(sb + kOffSFA, it.s0 + tix * kTileSF, kTileSF, fb);
+}
+
+// The B tile of one stage and its scale atoms, completing on `fb`.
+__device__ __forceinline__ void issue_operand(uint32_t sb, uint32_t fb, const Job &J, const ItemEnt &it,
+                                              int chunk)
+{
+    const size_t vix = (size_t)it.vec * J.nch + chunk;
+    bulk_g2s(sb + kOffB, J.bq + vix * kTileB, kTileB, fb);
+    bulk_g2s(sb + kOffSFB, J.bs + vix * kTileSF, kTileSF, fb);
+}
+
+// MMA issuer (one thread): the J.cps stages of each of `nr` items into the accumulator
+// buffer of the item, releasing each stage and publishing each accumulator on its
+// mbarrier. The stage and item positions carry across calls. False when a wait gave up.
+__device__ __forceinline__ bool mma_items(const Job &J, int nr, int &g_mma, int &n_mma, uint32_t tmem,
+                                          uint32_t stage0, uint32_t b_full, uint32_t b_empty,
+                                          uint32_t b_accf, uint32_t b_acce, volatile int *abort)
+{
+    for (int k = 0; k < nr; k++, n_mma++) {
+        const int buf = n_mma % kAccBufs;
+        if (n_mma >= kAccBufs && !mbar_wait(b_acce + 8 * buf, ((n_mma / kAccBufs) - 1) & 1, abort))
+            return false;
+        tc_fence_after();
+        const uint32_t dcol = tmem + (uint32_t)(buf * kN);
+        for (int c = 0; c < J.cps; c++) {
+            const int st = g_mma % kStages;
+            if (!mbar_wait(b_full + 8 * st, (g_mma / kStages) & 1, abort)) return false;
+            tc_fence_after();
+            const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
+            const uint32_t sfa = tmem + kSfaCol + (uint32_t)((g_mma & 1) * 16);
+            const uint32_t sfb = tmem + kSfbCol + (uint32_t)((g_mma & 1) * 16);
+#pragma unroll
+            for (int a4 = 0; a4 < 4; a4++) {
+                tc_cp_sf(sfa + 4 * a4, desc_sf(sb + kOffSFA + 512 * a4));
+                tc_cp_sf(sfb + 4 * a4, desc_sf(sb + kOffSFB + 512 * a4));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
+                const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
+                const uint64_t bd = desc_sw128(sb + kOffB + kb * 2048u + off);
+                const uint32_t id = (uint32_t)((j & 1) * 2);
+                // blocks 2j, 2j+1: the scales in atom j/2 (a scale address is a 4-column
+                // group); the byte id picks the pair
+                const uint32_t atom = (uint32_t)(4 * (j >> 1));
+                tc_mma(dcol, ad, bd, idesc_mxf4(id), (c > 0 || j > 0) ? 1u : 0u,
+                       (sfa + atom) | (id << 30), (sfb + atom) | (id << 30));
+            }
+            tc_commit(b_empty + 8 * st);
+            g_mma++;
+        }
+        tc_commit(b_accf + 8 * buf);
+    }
+    return true;
+}
+
+// Epilogue warp of tensor-memory lane quadrant q: for each of `nr` items, its 32 rows of
+// the 128 x 16 accumulator, summed over the 16 pieces and stored as the item's partial.
+// False when a wait gave up.
+__device__ __forceinline__ bool epilogue_items(const Job &J, const ItemEnt *items, int nr, int &n_epi,
+                                               uint32_t tmem, uint32_t b_accf, uint32_t b_acce,
+                                               volatile int *abort, int q, int lane)
+{
+    const int m = q * 32 + lane;            // tile row
+    for (int k = 0; k < nr; k++, n_epi++) {
+        const ItemEnt &it = items[k];
+        int row;
+        if (J.mode == GATEUP) row = m < 64 ? it.tile * 64 + m : (J.out_w >> 1) + it.tile * 64 + (m - 64);
+        else row = it.tile * 128 + m;
+        float *dst = J.part + (size_t)it.s * J.slice_stride + (size_t)it.out * J.out_w + row;
+        const int buf = n_epi % kAccBufs;
+        if (!mbar_wait(b_accf + 8 * buf, (n_epi / kAccBufs) & 1, abort)) return false;
+        tc_fence_after();
+        float v[16];
+        tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kN), v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_acce + 8 * buf);
+        float sum = v[15];
+#pragma unroll
+        for (int i = 14; i >= 0; i--) sum += v[i];
+        *dst = sum;
+    }
+    return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 {
     extern __shared__ unsigned char smem_raw[];
@@ -390,37 +492,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                     pre = min(kStages, nr * J.cps);
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h / J.cps];
-                        if (!it.c0 || (((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) continue;
-                        const int chunk = it.s * J.cps + h % J.cps;
+                        if (!item_ok(it)) continue;
                         const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
                         const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
-                        const size_t tix = (size_t)it.tile * J.nch + chunk;
                         mbar_expect_tx(fb, kStageTx);
-                        bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
-                        bulk_g2s(sb + kOffSFA, it.s0 + tix * kTileSF, kTileSF, fb);
+                        issue_weights(sb, fb, J, it, it.s * J.cps + h % J.cps);
                     }
                     pdl_wait();
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h / J.cps];
                         const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
-                        if (!it.c0 || (((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) != 0) {
+                        if (!item_ok(it)) {
                             k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
                             mbar_arrive(fb);
                             continue;
                         }
-                        const int chunk = it.s * J.cps + h % J.cps;
                         const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
-                        const size_t vbase = (size_t)it.vec * J.nch;
-                        bulk_g2s(sb + kOffB, J.bq + (vbase + chunk) * kTileB, kTileB, fb);
-                        bulk_g2s(sb + kOffSFB, J.bs + (vbase + chunk) * kTileSF, kTileSF, fb);
+                        issue_operand(sb, fb, J, it, it.s * J.cps + h % J.cps);
                     }
                 }
                 int h = 0;       // stage index within this round
                 for (int k = 0; k < nr && !stop; k++) {
                     const ItemEnt &it = items[k];
-                    const bool aligned = it.c0 && ((((uintptr_t)it.c0 | (uintptr_t)it.s0) & 15u) == 0);
+                    const bool aligned = item_ok(it);
                     if (!aligned) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
-                    const size_t vbase = (size_t)it.vec * J.nch;
                     for (int c = 0; c < J.cps; c++, h++) {
                         if (h < pre) { g_prod++; continue; }     // issued above
                         const int chunk = it.s * J.cps + c;
@@ -432,13 +527,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                         }
                         const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
                         const uint32_t fb = b_full + 8 * st;
-                        const size_t tix = (size_t)it.tile * J.nch + chunk;
                         if (aligned) {
                             mbar_expect_tx(fb, kStageTx);
-                            bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
-                            bulk_g2s(sb + kOffSFA, it.s0 + tix * kTileSF, kTileSF, fb);
-                            bulk_g2s(sb + kOffB, J.bq + (vbase + chunk) * kTileB, kTileB, fb);
-                            bulk_g2s(sb + kOffSFB, J.bs + (vbase + chunk) * kTileSF, kTileSF, fb);
+                            issue_weights(sb, fb, J, it, chunk);
+                            issue_operand(sb, fb, J, it, chunk);
                         } else {
                             mbar_arrive(fb);
                         }
@@ -512,68 +604,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             }
         } else if (warp == 4) {
             // ----------------------------------------------------------- MMA issuer
-            if (lane == 0) {
-                for (int k = 0; k < nr && !stop; k++, n_mma++) {
-                    const int buf = n_mma % kAccBufs;
-                    if (n_mma >= kAccBufs &&
-                        !mbar_wait(b_acce + 8 * buf, ((n_mma / kAccBufs) - 1) & 1, abort)) {
-                        stop = true;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t dcol = tmem + (uint32_t)(buf * kN);
-                    for (int c = 0; c < J.cps; c++) {
-                        const int st = g_mma % kStages;
-                        if (!mbar_wait(b_full + 8 * st, (g_mma / kStages) & 1, abort)) { stop = true; break; }
-                        tc_fence_after();
-                        const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
-                        const uint32_t sfa = tmem + kSfaCol + (uint32_t)((g_mma & 1) * 16);
-                        const uint32_t sfb = tmem + kSfbCol + (uint32_t)((g_mma & 1) * 16);
-#pragma unroll
-                        for (int a4 = 0; a4 < 4; a4++) {
-                            tc_cp_sf(sfa + 4 * a4, desc_sf(sb + kOffSFA + 512 * a4));
-                            tc_cp_sf(sfb + 4 * a4, desc_sf(sb + kOffSFB + 512 * a4));
-                        }
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
-                            const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
-                            const uint64_t bd = desc_sw128(sb + kOffB + kb * 2048u + off);
-                            const uint32_t id = (uint32_t)((j & 1) * 2);
-                            const uint32_t atom = (uint32_t)(4 * (j >> 1));
-                            tc_mma(dcol, ad, bd, idesc_mxf4(id), (c > 0 || j > 0) ? 1u : 0u,
-                                   (sfa + atom) | (id << 30), (sfb + atom) | (id << 30));
-                        }
-                        tc_commit(b_empty + 8 * st);
-                        g_mma++;
-                    }
-                    if (!stop) tc_commit(b_accf + 8 * buf);
-                }
-            }
+            if (lane == 0 && !stop &&
+                !mma_items(J, nr, g_mma, n_mma, tmem, stage0, b_full, b_empty, b_accf, b_acce, abort))
+                stop = true;
             __syncwarp();
         } else {
             // ------------------------------------------------------------- epilogue
-            const int q = warp & 3;                 // tensor-memory lane quadrant of this warp
-            const int m = q * 32 + lane;            // tile row
-            for (int k = 0; k < nr; k++, n_epi++) {
-                const ItemEnt &it = items[k];
-                int row;
-                if (J.mode == GATEUP) row = m < 64 ? it.tile * 64 + m : (J.out_w >> 1) + it.tile * 64 + (m - 64);
-                else row = it.tile * 128 + m;
-                float *dst = J.part + (size_t)it.s * J.slice_stride + (size_t)it.out * J.out_w + row;
-                const int buf = n_epi % kAccBufs;
-                if (!mbar_wait(b_accf + 8 * buf, (n_epi / kAccBufs) & 1, abort)) break;
-                tc_fence_after();
-                float v[16];
-                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kN), v);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(b_acce + 8 * buf);
-                float sum = v[15];
-#pragma unroll
-                for (int i = 14; i >= 0; i--) sum += v[i];
-                *dst = sum;
-            }
+            epilogue_items(J, items, nr, n_epi, tmem, b_accf, b_acce, abort, warp & 3, lane);
         }
         __syncthreads();          // every role is done with this round's table
     }
@@ -596,16 +633,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 // bq + 4096 c, and 4 scale atoms at bs + 2048 c (piece p's scale for block 4a+i at byte
 // 512 a + 16 p + i; every other byte of an atom is zero).
 //
-// One lane per element of a 32-element block. Per piece, with m the block maximum of |r|
-// (one redux on the bits: non-negative floats order like their bits):
-//   scale 2^s, s = e - 2 if m <= 1.5 * 2^e else e - 1 (e = floor(log2 m)), so m / 2^s
-//   lies in (3, 6]; from the bits, the E8M0 code is s + 127 = E - 2 + (mantissa >
-//   0x400000), at least 0 (blocks below 2^-124 share the smallest scale, 2^-127);
-//   the E2M1 code of r / 2^s by the hardware conversion (round to nearest even; the
-//   scaled value never exceeds 6, so saturation never acts), and its value q;
-//   the residual (r / 2^s - q) * 2^s, exact: q is a neighbour of r / 2^s on the E2M1 grid,
-//   so the difference is a multiple of ulp(r / 2^s) no larger than it, and the result
-//   r - q 2^s is representable.
+// One lane per element of a 32-element block. From the block maximum m of |x| (one redux
+// on the bits: non-negative floats order like their bits):
+//   s_0 = e - 2 if m <= 1.5 * 2^e else e - 1 (e = floor(log2 m)), so m / 2^s_0 lies in
+//   (3, 6]; from the bits, the E8M0 code is s_0 + 127 = E - 2 + (mantissa > 0x400000);
+//   the later codes follow the schedule s_1 = s_0 - 2, s_{p+1} = s_p - 3; every code is
+//   clamped at 0 (blocks below 2^-80 or so share the smallest scale, 2^-127, which only
+//   makes their scaled residuals smaller);
+//   per piece, the E2M1 code of r / 2^s by the hardware conversion (round to nearest even;
+//   the scaled value never exceeds 6, so saturation never acts), its value q, and the
+//   residual (r / 2^s - q) * 2^s.
 // A block holding an inf or NaN gets scale code 255 (NaN) on every piece, zero codes.
 __device__ __forceinline__ uint32_t e2m1_code(float v)
 {
@@ -636,10 +673,11 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
             if ((lane & 1) == 0)
                 tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] = 0;
     } else {
+        const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r)));
+        const int code0 = (int)(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
 #pragma unroll
         for (int p = 0; p < kN; p++) {
-            const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r)));
-            const int code = max(0, (int)(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0));
+            const int code = max(0, p == 0 ? code0 : code0 + 1 - 3 * p);
             const float rs = __fmul_rn(r, __int_as_float((254 - code) << 23));   // r / 2^s, exact
             uint32_t nib = e2m1_code(rs);
             if ((nib & 7u) == 0u) nib = 0u;                                     // no -0 codes
@@ -670,6 +708,33 @@ __global__ void k_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, size_t
     split_block(bq + (size_t)v * nch * kTileB, bs + (size_t)v * nch * kTileSF, r, blk, lane);
 }
 
+// silu(gate) * up of one element, gate and up summed over the K slices in slice order from
+// the partials at pa[s * slice_stride] (gate) and pa[s * slice_stride + inter] (up). Loads
+// go to L2 (the partials may have been written by other CTAs of the same launch) in groups
+// of 16 slices, every load of a group issued before the ordered sums.
+__device__ __forceinline__ float act_value(const float *pa, int ks, size_t slice_stride, int inter)
+{
+    float g = 0.0f, u = 0.0f;
+    for (int s0 = 0; s0 < ks; s0 += 16) {
+        float gv[16], uv[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (s0 + i < ks) {
+                gv[i] = __ldcg(pa + (size_t)(s0 + i) * slice_stride);
+                uv[i] = __ldcg(pa + (size_t)(s0 + i) * slice_stride + inter);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (s0 + i < ks) {
+                g += gv[i];
+                u += uv[i];
+            }
+        }
+    }
+    return silu_f(g) * u;
+}
+
 // B operands of act = silu(gate) * up, gate/up summed over the K slices of the gate/up
 // pass in slice order; both indexed by grouped position p. grid (ceil(inter/32 / 8),
 // positions). The count and the partials are loaded together (the partial rows of every
@@ -683,30 +748,9 @@ __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int
     const int blk = blockIdx.x * 8 + warp;
     const int p = blockIdx.y;
     if (blk >= inter / 32) return;
-    const float *pa = part + (size_t)p * 2 * inter + blk * 32 + lane;
     const int n = count ? *count : count_host;
-    float g = 0.0f, u = 0.0f;
-    // slices in groups of 16, every load of a group issued before the ordered sums (a loop
-    // with a run-time count and one load per iteration would pay the latency per slice)
-    for (int s0 = 0; s0 < ks; s0 += 16) {
-        float gv[16], uv[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            if (s0 + i < ks) {
-                gv[i] = pa[(size_t)(s0 + i) * slice_stride];
-                uv[i] = pa[(size_t)(s0 + i) * slice_stride + inter];
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            if (s0 + i < ks) {
-                g += gv[i];
-                u += uv[i];
-            }
-        }
-    }
+    const float act = act_value(part + (size_t)p * 2 * inter + blk * 32 + lane, ks, slice_stride, inter);
     if (p >= n) return;
-    const float act = silu_f(g) * u;
     const int nch = inter / kStageK;
     split_block(bq + (size_t)p * nch * kTileB, bs + (size_t)p * nch * kTileSF, act, blk, lane);
 }
@@ -832,17 +876,16 @@ int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int
     return check_launch("umma slice sum");
 }
 
-// Launch over `npos_max` assignment positions (the device count, when given, may be
-// smaller). MoE mode: w.table/assign/idx; single mode: w.single_mode with positions 0..n-1.
-int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
-                int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
-                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
-                int early)
+// The work description of one pass over `npos_max` assignment positions (the device count,
+// when given, may be smaller). MoE mode: w.table/assign/idx; single mode: w.single_mode
+// with positions 0..n-1.
+static int make_job(Job &J, int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
+                    int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
+                    int vec_div, float *part, int out_w, size_t slice_stride, int early)
 {
     if (!umma_supported(K, rows, mode)) return fail(K3D_EINVAL, "umma: unsupported K=%d rows=%d", K, rows);
     const int chunks = K / kStageK;
     if (ks < 1 || chunks % ks) return fail(K3D_EINVAL, "umma: %d slices of %d stages", ks, chunks);
-    Job J;
     J.table = w.table;
     J.single = w.single;
     J.single_mode = w.single_mode;
@@ -857,7 +900,6 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     J.cps = chunks / ks;
     J.nch = chunks;
     J.tiled = tiled;
-
     J.bq = bq;
     J.bs = bs;
     J.vec_div = vec_div;
@@ -871,6 +913,17 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     J.part = part;
     J.out_w = out_w;
     J.slice_stride = slice_stride;
+    return K3D_OK;
+}
+
+int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
+                int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
+                int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
+                int early)
+{
+    Job J;
+    K3_TRY(make_job(J, mode, tiled, w, idx, count, npos_max, K, rows, ks, bq, bs, vec_div, part, out_w,
+                    slice_stride, early));
     static bool init = false;
     if (!init) {
         cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma, cudaFuncAttributeMaxDynamicSharedMemorySize,
