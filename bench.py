@@ -370,6 +370,88 @@ def bench_moe(args, rank, world):
     return res
 
 
+# -------------------------------------------------- MoE layer, Mode A (all-to-all EP) ----
+def bench_moe_a2a(args, rank, world):
+    """Config 1 MoE layer for a batch of args.batch tokens split over the ranks
+    (data-parallel tokens): each rank routes its own tokens and k3d_moe_swiglu_a2a sends
+    every (token, slot) row to its expert's rank and back (grouped NCCL send/recv). A step
+    is one layer call on every rank; the step time is the max over ranks."""
+    import k3cuda
+    import synth
+    lib = k3cuda.init(0)
+    n_exp = args.n_experts
+    per = n_exp // world
+    T = max(1, args.batch // world)
+    g = synth.rng(4242)
+    W = synth.bf16_normal(g, (n_exp, HIDDEN), 0.02)
+    bias = g.uniform(-0.1, 0.1, n_exp).astype(np.float32)
+    sh = (synth.bf16_normal(g, (SHARED, HIDDEN), 0.02), synth.bf16_normal(g, (SHARED, HIDDEN), 0.02),
+          synth.bf16_normal(g, (HIDDEN, SHARED), 0.02))
+    mw = k3cuda.MoeWeights(HIDDEN, INTER, n_exp, TOPK, W, bias, shared=sh, seed=7, lo=rank * per,
+                           hi=(rank + 1) * per, add_shared=1, tiled=True, lib=lib)
+    P = 16
+    xs = synth.bf16_to_f32(synth.bf16_normal(synth.rng(5000 + rank), (P * T, HIDDEN), 1.0))
+    X = k3cuda.DevBuf.from_array(xs, lib)
+    Y = k3cuda.DevBuf(T * HIDDEN * 4, lib)
+    nws = mw.a2a_ws_bytes(T, world)
+    WS = k3cuda.DevBuf(nws, lib)
+    FL = k3cuda.DevBuf(256 << 20, lib)
+    ev = [lib.k3d_event_create() for _ in range(2)]
+
+    def step(i):
+        k3cuda.check(mw.run_a2a(Y.ptr, X.ptr + (i % P) * T * HIDDEN * 4, T, T, WS.ptr, nws), "moe a2a step")
+
+    for i in range(args.warmup):
+        step(i)
+    k3cuda.check(lib.k3d_sync())
+    barrier()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0)))
+    clocks.start()
+    lib.k3d_launch_count_reset()
+    step_ms = []
+    for i in range(args.steps):
+        lib.k3d_memset(FL.ptr, i & 0xff, FL.nbytes)      # L2 flush, outside the events
+        barrier()
+        lib.k3d_event_record(ev[0])
+        step(args.warmup + i)
+        lib.k3d_event_record(ev[1])
+        step_ms.append(lib.k3d_event_elapsed_ms(ev[0], ev[1]))
+    k3cuda.check(lib.k3d_sync())
+    launches = lib.k3d_launch_count() - args.steps
+    clk = clocks.stop()
+    tot_ms = reduce_max(sum(step_ms))
+    # end to end through the public API with host buffers (this rank's tokens in and out)
+    hx = lib.k3d_host_alloc(T * HIDDEN * 4)
+    hy = lib.k3d_host_alloc(T * HIDDEN * 4)
+    C.memmove(hx, xs[:T].ctypes.data, T * HIDDEN * 4)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        k3cuda.check(lib.k3d_upload(X.ptr, hx, T * HIDDEN * 4))
+        step(0)
+        k3cuda.check(lib.k3d_download(hy, Y.ptr, T * HIDDEN * 4))
+    e2e_s = reduce_max(time.perf_counter() - t0)
+    lib.k3d_host_free(hx)
+    lib.k3d_host_free(hy)
+    B = T * world
+    return {
+        "metric": METRIC, "value": B * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded MXFP4 experts, E8M0 117..121; bf16 ~N(0,0.02) router and "
+                "shared expert; bf16 ~N(0,1) tokens, different on every rank)",
+        "config": {"workload": f"config1 MoE layer, Mode A all-to-all EP, batch {B} "
+                               f"({T} tokens per rank)", "hidden": HIDDEN, "n_experts": n_exp,
+                   "topk": TOPK, "inter": INTER, "shared_inter": SHARED, "parallelism": f"ep{world}-a2a",
+                   "l2": "flushed between steps (256 MB write)"},
+        "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s",
+                "h2d_bytes_per_step": T * HIDDEN * 4, "d2h_bytes_per_step": T * HIDDEN * 4},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+
+
 # ----------------------------------------------------------------- stack (config 4) ----
 def stack_cfg(world, rank, batch, cap, layout=1):
     import k3cuda
@@ -546,7 +628,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack", "moe"])
+    ap.add_argument("--workload", default="stack", choices=["stack", "moe", "moe_a2a"],
+                    help="moe_a2a: the MoE layer for a --batch split over the ranks (Mode A)")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -580,10 +663,17 @@ def main():
                        "d2h_bytes_per_step": 0}}
         print(json.dumps(res), flush=True)
         return
+    if args.workload == "moe_a2a" and args.batch == 1:
+        args.batch = 64
     setup_dist(world, rank, local)
-    res = bench_stack(args, rank, world) if args.workload == "stack" else bench_moe(args, rank, world)
+    if args.workload == "stack":
+        res = bench_stack(args, rank, world)
+    elif args.workload == "moe":
+        res = bench_moe(args, rank, world)
+    else:
+        res = bench_moe_a2a(args, rank, world)
     if rank == 0:
-        if world == 1 and args.cpu_seconds > 0:
+        if world == 1 and args.cpu_seconds > 0 and args.workload != "moe_a2a":
             res["cpu_baseline"] = (cpu_stack_sample(args.cpu_seconds) if args.workload == "stack"
                                    else cpu_moe_sample(seconds=args.cpu_seconds))
         print(json.dumps(res), flush=True)

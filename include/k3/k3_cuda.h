@@ -323,6 +323,29 @@ int k3d_ep_size(void);
 /* In-place sum of a float buffer over all ranks (the MoE combine). */
 int k3d_ep_allreduce_f32(float *buf, size_t n);
 
+/* Mode A expert parallelism: all-to-all dispatch and combine for data-parallel tokens (a
+ * batch split over the ranks, e.g. B = 64). Every rank passes ITS OWN tokens x[T][hidden]
+ * (T may differ between ranks; at most t_max on every rank) and holds the experts
+ * [expert_lo, expert_hi) = [rank * E / nranks, (rank + 1) * E / nranks) in w->experts
+ * (entries indexed by global expert id). Each rank routes its tokens; the fp32 row of each
+ * (token, slot) goes to the rank of its expert with grouped NCCL send/recv, is run through
+ * that rank's experts and comes back the same way; the tokens' rank sums the rows in top-k
+ * order, adds the shared expert (s->add_shared: set it on every rank) and writes
+ * out[T][hidden] (+= with accumulate). Routing and the receive counts decide the transfer
+ * sizes, so the call synchronises the host twice and cannot be captured into a graph.
+ * nranks = k3d_ep_size() (1 without k3d_ep_init: all experts local, same result).
+ * No reference counterpart: the CPU engine is single-process. */
+size_t k3d_moe_a2a_ws_bytes(const K3dMoeShape *s, int t_max, int nranks);
+int    k3d_moe_swiglu_a2a(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s,
+                          int T, int t_max, int accumulate, int *idx, float *wts,
+                          void *ws, size_t ws_bytes);
+/* The Mode A dispatch plan, on HOST arrays (no device work): for assignments idx[TK]
+ * (expert ids), cnt[r] rows go to rank r (expert e on rank e / (n_experts / nranks)),
+ * rank r's rows start at row off[r] of the send buffer, each rank's rows in assignment
+ * order, and pos[a] is the row of assignment a. n_experts must be a multiple of nranks. */
+int    k3d_a2a_plan(const int *idx, int TK, int n_experts, int nranks, int *cnt, int *off,
+                    int *pos);
+
 /* ----------------------------------------------------------- decode stack ---- */
 typedef struct {
     int   hidden, vocab, n_layers;

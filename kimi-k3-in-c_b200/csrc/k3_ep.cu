@@ -2,7 +2,8 @@
 // [n*E/G, (n+1)*E/G) on rank n. The combine of a replicated-activation decode step is an
 // in-place sum of the per-rank partial MoE outputs (ncclAllReduce on the library stream,
 // so it orders after the expert kernels and can be captured into a CUDA graph).
-// The CPU engine is single-process and has no counterpart.
+// Mode A (all-to-all dispatch and combine of data-parallel tokens) exchanges rows with
+// grouped send/recv (ep_exchange). The CPU engine is single-process and has no counterpart.
 #include <nccl.h>
 
 #include "k3_common.cuh"
@@ -12,6 +13,36 @@ namespace {
 ncclComm_t g_comm = nullptr;
 int g_rank = 0, g_size = 1;
 }  // namespace
+}  // namespace k3
+
+namespace k3 {
+
+// Grouped point-to-point exchange on the library stream: to each rank r, scnt[r] bytes of
+// `send` from byte soff[r]; from it, rcnt[r] bytes into `recv` at byte roff[r]. Both sides
+// of a pair agree on the size (the receive counts come from an earlier exchange of the
+// send counts), so zero-byte pairs are skipped on both. One rank: a device copy.
+int ep_exchange(const void *send, const size_t *scnt, const size_t *soff, void *recv,
+                const size_t *rcnt, const size_t *roff, cudaStream_t st)
+{
+    if (g_size == 1) {
+        if (scnt[0] != rcnt[0]) return fail(K3D_EINVAL, "ep exchange: %zu bytes sent, %zu expected", scnt[0], rcnt[0]);
+        if (scnt[0] && cudaMemcpyAsync((char *)recv + roff[0], (const char *)send + soff[0], scnt[0],
+                                       cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return fail(K3D_ECUDA, "ep exchange copy");
+        return K3D_OK;
+    }
+    if (!g_comm) return fail(K3D_ENCCL, "ep exchange before k3d_ep_init");
+    ncclResult_t r = ncclGroupStart();
+    for (int p = 0; p < g_size && r == ncclSuccess; p++) {
+        if (scnt[p]) r = ncclSend((const char *)send + soff[p], scnt[p], ncclInt8, p, g_comm, st);
+        if (r == ncclSuccess && rcnt[p]) r = ncclRecv((char *)recv + roff[p], rcnt[p], ncclInt8, p, g_comm, st);
+    }
+    const ncclResult_t e = ncclGroupEnd();
+    if (r == ncclSuccess) r = e;
+    if (r != ncclSuccess) return fail(K3D_ENCCL, "ep exchange: %s", ncclGetErrorString(r));
+    return K3D_OK;
+}
+
 }  // namespace k3
 
 using namespace k3;

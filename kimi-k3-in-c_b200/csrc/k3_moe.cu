@@ -18,6 +18,7 @@
 // Expert parallelism: only experts in [expert_lo, expert_hi) are computed here; the
 // combine treats the others as zero and the caller sums the partial outputs over ranks.
 #include <algorithm>
+#include <vector>
 
 #include "k3_mxfp4.cuh"
 #include "k3_moe.cuh"
@@ -355,6 +356,29 @@ struct MoeWs {
     size_t total;
 };
 
+// The expert buffers of run_experts for T token vectors and TK assignments.
+template <class Take>
+static void expert_bufs_layout(ExpertBufs &eb, const K3dMoeShape *s, size_t T, size_t TK, Take &take)
+{
+    eb.act = (float *)take(TK * s->inter * sizeof(float));
+    eb.contrib = (float *)take(TK * s->hidden * sizeof(float));
+    eb.xb_x = (__half *)take(T * 2 * s->hidden * sizeof(__half));
+    eb.xs_x = (float *)take(T * sizeof(float));
+    eb.xb_a = (__half *)take(TK * 2 * s->inter * sizeof(__half));
+    eb.xs_a = (float *)take(TK * sizeof(float));
+    if (umma_eligible(s->hidden, s->inter, (int)TK, s->expert_layout)) {
+        eb.bq_x = (uint8_t *)take(T * umma_bq_bytes(s->hidden));
+        eb.bs_x = (uint8_t *)take(T * umma_bs_bytes(s->hidden));
+        eb.bq_a = (uint8_t *)take(TK * umma_bq_bytes(s->inter));
+        eb.bs_a = (uint8_t *)take(TK * umma_bs_bytes(s->inter));
+        eb.part_gu = (float *)take((size_t)umma_ks_cap(s->hidden, (int)TK) * TK * 2 * s->inter * sizeof(float));
+        eb.part_d = (float *)take((size_t)umma_ks_cap(s->inter, (int)TK) * TK * s->hidden * sizeof(float));
+    } else {
+        eb.bq_x = eb.bs_x = eb.bq_a = eb.bs_a = nullptr;
+        eb.part_gu = eb.part_d = nullptr;
+    }
+}
+
 static MoeWs moe_ws_layout(const K3dMoeShape *s, int T, void *base)
 {
     MoeWs L;
@@ -369,27 +393,9 @@ static MoeWs moe_ws_layout(const K3dMoeShape *s, int T, void *base)
     L.act_expert = (int *)take((size_t)s->n_experts * sizeof(int));
     L.act_off = (int *)take(((size_t)s->n_experts + 1) * sizeof(int));
     L.assign = (int *)take(TK * sizeof(int));
-    L.eb.act = (float *)take(TK * s->inter * sizeof(float));
-    L.eb.contrib = (float *)take(TK * s->hidden * sizeof(float));
     L.sh_act = (float *)take((size_t)T * (s->shared_inter > 0 ? s->shared_inter : 1) * sizeof(float));
     L.sh_out = (float *)take((size_t)T * s->hidden * sizeof(float));
-    L.eb.xb_x = (__half *)take((size_t)T * 2 * s->hidden * sizeof(__half));
-    L.eb.xs_x = (float *)take((size_t)T * sizeof(float));
-    L.eb.xb_a = (__half *)take(TK * 2 * s->inter * sizeof(__half));
-    L.eb.xs_a = (float *)take(TK * sizeof(float));
-    if (umma_eligible(s->hidden, s->inter, (int)TK, s->expert_layout)) {
-        L.eb.bq_x = (uint8_t *)take((size_t)T * umma_bq_bytes(s->hidden));
-        L.eb.bs_x = (uint8_t *)take((size_t)T * umma_bs_bytes(s->hidden));
-        L.eb.bq_a = (uint8_t *)take(TK * umma_bq_bytes(s->inter));
-        L.eb.bs_a = (uint8_t *)take(TK * umma_bs_bytes(s->inter));
-        L.eb.part_gu = (float *)take((size_t)umma_ks_cap(s->hidden, (int)TK) * TK * 2 * s->inter *
-                                     sizeof(float));
-        L.eb.part_d = (float *)take((size_t)umma_ks_cap(s->inter, (int)TK) * TK * s->hidden *
-                                    sizeof(float));
-    } else {
-        L.eb.bq_x = L.eb.bs_x = L.eb.bq_a = L.eb.bs_a = nullptr;
-        L.eb.part_gu = L.eb.part_d = nullptr;
-    }
+    expert_bufs_layout(L.eb, s, (size_t)T, TK, take);
     L.total = off;
     return L;
 }
@@ -455,11 +461,281 @@ static ExpertWs expert_ws_layout(int hidden, int inter, void *base)
     return L;
 }
 
+// ---- Mode A: all-to-all expert parallelism ------------------------------------------
+// Every rank routes ITS OWN tokens; the row of each (token, slot) assignment goes to the
+// rank of its expert (expert e on rank e / (n_experts / nranks)), which runs its local
+// experts over everything it received, one assignment per row, and sends the results
+// back; the tokens' rank sums them in top-k order with the shared expert. Rows travel as
+// fp32, so a token's result does not depend on where its experts ran.
+
+// Host dispatch plan: cnt[r] rows for rank r, its rows from off[r] on in the send buffer,
+// each rank's rows in assignment order; pos[a] = row of assignment a. -1 on a bad id.
+static int a2a_plan_host(const int *idx, int TK, int n_experts, int nranks, int *cnt, int *off, int *pos)
+{
+    if (nranks < 1 || n_experts < nranks || n_experts % nranks) return -1;
+    const int per = n_experts / nranks;
+    for (int r = 0; r < nranks; r++) cnt[r] = 0;
+    for (int a = 0; a < TK; a++) {
+        if (idx[a] < 0 || idx[a] >= n_experts) return -1;
+        cnt[idx[a] / per]++;
+    }
+    for (int r = 0, o = 0; r < nranks; r++) { off[r] = o; o += cnt[r]; }
+    std::vector<int> cur(off, off + nranks);
+    for (int a = 0; a < TK; a++) pos[a] = cur[idx[a] / per]++;
+    return 0;
+}
+
+// Send rows: row pos[a] = x[a / K], and its expert id. grid TK, 256 threads.
+__global__ void k_a2a_pack(float *sendbuf, int *send_ids, const float *x, const int *idx, const int *pos,
+                           int K, int hidden)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int a = blockIdx.x;
+    const int row = pos[a];
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(a / K) * hidden);
+    float4 *dst = reinterpret_cast<float4 *>(sendbuf + (size_t)row * hidden);
+    for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) dst[i] = src[i];
+    if (threadIdx.x == 0) send_ids[row] = idx[a];
+}
+
+// out[t] (+)= sum over slots k, in top-k order, of w[t][k] * back[pos[t K + k]], then the
+// shared expert: the arithmetic of k_moe_combine. grid (ceil(hidden / 256), T).
+__global__ void k_a2a_combine(float *out, const float *back, const int *pos, const float *wts,
+                              const float *sh_out, int hidden, int K, int accumulate)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.y;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= hidden) return;
+    float acc = 0.0f;
+    for (int k = 0; k < K; k++) {
+        const int a = t * K + k;
+        acc = __fadd_rn(acc, __fmul_rn(wts[a], back[(size_t)pos[a] * hidden + r]));
+    }
+    if (sh_out) acc = __fadd_rn(acc, sh_out[(size_t)t * hidden + r]);
+    float *o = out + (size_t)t * hidden + r;
+    *o = accumulate ? __fadd_rn(*o, acc) : acc;
+}
+
+// Workspace of k3d_moe_swiglu_a2a: at most t_max tokens on any rank, so a rank receives at
+// most nranks * t_max * topk rows.
+struct A2aWs {
+    int *idx; float *wts; void *router; float *sh_act, *sh_out;
+    int *pos, *cnt_s, *cnt_r;
+    float *sendbuf, *recvbuf, *back;
+    int *send_ids, *recv_ids;
+    int *n_active, *act_expert, *act_off, *assign;
+    ExpertBufs eb;
+    size_t total;
+};
+
+static A2aWs a2a_ws_layout(const K3dMoeShape *s, int t_max, int nranks, void *base)
+{
+    A2aWs L;
+    const size_t TK = (size_t)t_max * s->topk, R = (size_t)nranks * TK;
+    size_t off = 0;
+    char *b = (char *)base;
+    auto take = [&](size_t bytes) { char *p = b + off; off += align256(bytes); return (void *)p; };
+    L.idx = (int *)take(TK * sizeof(int));
+    L.wts = (float *)take(TK * sizeof(float));
+    L.router = take(router_ws_bytes(t_max, s->n_experts));
+    L.sh_act = (float *)take((size_t)t_max * (s->shared_inter > 0 ? s->shared_inter : 1) * sizeof(float));
+    L.sh_out = (float *)take((size_t)t_max * s->hidden * sizeof(float));
+    L.pos = (int *)take(TK * sizeof(int));
+    L.cnt_s = (int *)take((size_t)nranks * sizeof(int));
+    L.cnt_r = (int *)take((size_t)nranks * sizeof(int));
+    L.sendbuf = (float *)take(TK * s->hidden * sizeof(float));
+    L.send_ids = (int *)take(TK * sizeof(int));
+    L.recvbuf = (float *)take(R * s->hidden * sizeof(float));
+    L.recv_ids = (int *)take(R * sizeof(int));
+    L.back = (float *)take(TK * s->hidden * sizeof(float));
+    L.n_active = (int *)take(4 * sizeof(int));
+    L.act_expert = (int *)take((size_t)s->n_experts * sizeof(int));
+    L.act_off = (int *)take(((size_t)s->n_experts + 1) * sizeof(int));
+    L.assign = (int *)take(R * sizeof(int));
+    expert_bufs_layout(L.eb, s, R, R, take);
+    L.total = off;
+    return L;
+}
+
+// Pinned host scratch of the plan (grows; Mode A synchronises the host anyway).
+static int *a2a_host_ints(size_t n)
+{
+    static int *buf = nullptr;
+    static size_t cap = 0;
+    if (n <= cap) return buf;
+    if (buf) cudaFreeHost(buf);
+    buf = nullptr;
+    cap = 0;
+    if (cudaMallocHost(&buf, n * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        fail(K3D_ENOMEM, "moe a2a: %zu pinned host ints", n);
+        return nullptr;
+    }
+    cap = n;
+    return buf;
+}
+
 }  // namespace k3
 
 using namespace k3;
 
 extern "C" {
+
+int k3d_a2a_plan(const int *idx, int TK, int n_experts, int nranks, int *cnt, int *off, int *pos)
+{
+    if (!idx || !cnt || !off || !pos || TK < 0) return fail(K3D_EINVAL, "k3d_a2a_plan null pointer");
+    if (a2a_plan_host(idx, TK, n_experts, nranks, cnt, off, pos))
+        return fail(K3D_EINVAL, "k3d_a2a_plan: %d experts over %d ranks, or an expert id out of range",
+                    n_experts, nranks);
+    return K3D_OK;
+}
+
+size_t k3d_moe_a2a_ws_bytes(const K3dMoeShape *s, int t_max, int nranks)
+{
+    if (!s || t_max < 1 || nranks < 1) return 0;
+    return a2a_ws_layout(s, t_max, nranks, nullptr).total + 256;
+}
+
+int k3d_moe_swiglu_a2a(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s, int T,
+                       int t_max, int accumulate, int *idx, float *wts, void *ws, size_t ws_bytes)
+{
+    K3_TRY(ensure_ctx());
+    K3_TRY(check_shape(s, T));
+    const int G = k3d_ep_size(), rank = k3d_ep_rank();
+    if (!out || !x || !w || !ws || !w->router_w || !w->experts)
+        return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a null pointer");
+    if (T > t_max) return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a: T=%d above t_max=%d", T, t_max);
+    if (s->n_experts % G) return fail(K3D_EINVAL, "moe a2a: %d experts over %d ranks", s->n_experts, G);
+    const int per = s->n_experts / G;
+    if (s->expert_lo != rank * per || s->expert_hi != (rank + 1) * per)
+        return fail(K3D_EINVAL, "moe a2a: rank %d owns experts [%d, %d), not [%d, %d)", rank, rank * per,
+                    (rank + 1) * per, s->expert_lo, s->expert_hi);
+    if (s->shared_inter > 0 && s->add_shared && (!w->sh_gate || !w->sh_up || !w->sh_down))
+        return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a shared expert weights missing");
+    if (ws_bytes < k3d_moe_a2a_ws_bytes(s, t_max, G)) return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a workspace too small");
+    if (((uintptr_t)x | (uintptr_t)ws) & 15u) return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a alignment");
+    cudaStream_t st = stream();
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs != cudaStreamCaptureStatusNone)
+        return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a synchronises the host and cannot be captured");
+    A2aWs L = a2a_ws_layout(s, t_max, G, ws);
+    const int K = s->topk, TK = T * K;
+    int *I = idx ? idx : L.idx;
+    float *Wt = wts ? wts : L.wts;
+    int *h = a2a_host_ints((size_t)2 * TK + 4 * (size_t)G + 4);
+    if (!h) return k3d_status();
+    int *h_idx = h, *h_pos = h + TK, *h_cnt = h + 2 * TK, *h_off = h_cnt + G, *h_rcnt = h_off + G,
+        *h_roff = h_rcnt + G;
+
+    // the shared expert of this rank's tokens, on the side stream (joined before the combine)
+    const bool shared = s->shared_inter > 0 && s->add_shared;
+    cudaStream_t sst = (!profiling() && side_stream()) ? side_stream() : st;
+    if (shared) {
+        if (sst != st && (cudaEventRecord(side_event(0), st) != cudaSuccess ||
+                          cudaStreamWaitEvent(sst, side_event(0), 0) != cudaSuccess))
+            return fail(K3D_ECUDA, "moe a2a: fork to the side stream");
+        prof_begin("moe.shared");
+        K3_TRY(gemv_bf16_swiglu(L.sh_act, x, w->sh_gate, w->sh_up, s->hidden, s->shared_inter, T, sst));
+        K3_TRY(gemv_bf16(L.sh_out, L.sh_act, w->sh_down, s->shared_inter, s->hidden, T, 0, sst));
+        prof_end("moe.shared");
+        if (sst != st && cudaEventRecord(side_event(1), sst) != cudaSuccess)
+            return fail(K3D_ECUDA, "moe a2a: side stream join event");
+    }
+    prof_begin("moe.router");
+    K3_TRY(router_bf16(I, Wt, x, w->router_w, w->router_bias, T, s->hidden, s->n_experts, K, s->renorm,
+                       s->routed_scale, L.router, st));
+    prof_end("moe.router");
+
+    // plan on the host: the routing decides how many rows go to each rank
+    prof_begin("ep.dispatch");
+    if (cudaMemcpyAsync(h_idx, I, (size_t)TK * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe a2a: routing to the host");
+    K3_TRY(device_flag_status());
+    if (a2a_plan_host(h_idx, TK, s->n_experts, G, h_cnt, h_off, h_pos))
+        return fail(K3D_EBOUND, "moe a2a: expert id out of range");
+    if (cudaMemcpyAsync(L.pos, h_pos, (size_t)TK * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(L.cnt_s, h_cnt, (size_t)G * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe a2a: plan to the device");
+    // the row counts every rank sends here
+    {
+        std::vector<size_t> c4(G, sizeof(int)), o4(G);
+        for (int r = 0; r < G; r++) o4[r] = (size_t)r * sizeof(int);
+        K3_TRY(ep_exchange(L.cnt_s, c4.data(), o4.data(), L.cnt_r, c4.data(), o4.data(), st));
+    }
+    if (cudaMemcpyAsync(h_rcnt, L.cnt_r, (size_t)G * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe a2a: receive counts to the host");
+    long long R = 0;
+    for (int r = 0; r < G; r++) {
+        if (h_rcnt[r] < 0) return fail(K3D_EBOUND, "moe a2a: rank %d sends %d rows", r, h_rcnt[r]);
+        h_roff[r] = (int)R;
+        R += h_rcnt[r];
+    }
+    if (R > (long long)G * t_max * K)
+        return fail(K3D_EBOUND, "moe a2a: %lld rows received, room for %lld", R, (long long)G * t_max * K);
+    if (TK > 0) {
+        launch_pdl(k_a2a_pack, dim3(TK), dim3(256), 0, st, L.sendbuf, L.send_ids, x, (const int *)I,
+                   (const int *)L.pos, K, s->hidden);
+        note_launch();
+        K3_TRY(check_launch("moe a2a pack"));
+    }
+    const size_t rowb = (size_t)s->hidden * sizeof(float);
+    std::vector<size_t> sb(G), so(G), rb(G), ro(G), si(G), soi(G), ri(G), roi(G);
+    for (int r = 0; r < G; r++) {
+        sb[r] = (size_t)h_cnt[r] * rowb;   so[r] = (size_t)h_off[r] * rowb;
+        rb[r] = (size_t)h_rcnt[r] * rowb;  ro[r] = (size_t)h_roff[r] * rowb;
+        si[r] = (size_t)h_cnt[r] * 4;      soi[r] = (size_t)h_off[r] * 4;
+        ri[r] = (size_t)h_rcnt[r] * 4;     roi[r] = (size_t)h_roff[r] * 4;
+    }
+    K3_TRY(ep_exchange(L.send_ids, si.data(), soi.data(), L.recv_ids, ri.data(), roi.data(), st));
+    K3_TRY(ep_exchange(L.sendbuf, sb.data(), so.data(), L.recvbuf, rb.data(), ro.data(), st));
+    prof_end("ep.dispatch");
+
+    // this rank's experts over the rows it received: one assignment per row
+    const float *ybuf = L.recvbuf;    // unused when R = 0
+    if (R > 0) {
+        const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
+        launch_pdl(k_moe_prep, dim3(1), dim3(1024), smem, st, (const int *)L.recv_ids, (int)R, s->n_experts,
+                   s->expert_lo, s->expert_hi, L.n_active, L.act_expert, L.act_off, L.assign);
+        note_launch();
+        K3_TRY(check_launch("moe a2a prep"));
+        MoeWork mw{};
+        mw.table = w->experts;
+        mw.n_active = L.n_active;
+        mw.act_expert = L.act_expert;
+        mw.act_off = L.act_off;
+        mw.assign = L.assign;
+        mw.K = 1;
+        mw.n_experts = s->n_experts;
+        ExpertOut O{L.eb.contrib, 1, 0};
+        const int umax = (int)std::min<long long>(R, per);
+        prof_begin("moe.experts");
+        K3_TRY(run_experts(mw, L.recv_ids, L.n_active + 1, umax, L.recvbuf, (int)R, (int)R, s->hidden,
+                           s->inter, s->expert_layout, L.eb, O, st));
+        prof_end("moe.experts");
+        ybuf = O.contrib;
+        if (O.ks > 1) {
+            K3_TRY(umma_slice_sum(L.eb.contrib, O.contrib, O.ks, O.slice, (int)(R * s->hidden), st));
+            ybuf = L.eb.contrib;
+        }
+    }
+    // results back to the tokens' ranks, into the rows they were sent from
+    prof_begin("ep.combine");
+    K3_TRY(ep_exchange(ybuf, rb.data(), ro.data(), L.back, sb.data(), so.data(), st));
+    prof_end("ep.combine");
+    if (shared && sst != st && cudaStreamWaitEvent(st, side_event(1), 0) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe a2a: join from the side stream");
+    dim3 grid((s->hidden + 255) / 256, T);
+    launch_pdl(k_a2a_combine, dim3(grid), dim3(256), 0, st, out, (const float *)L.back, (const int *)L.pos,
+               (const float *)Wt, shared ? (const float *)L.sh_out : nullptr, s->hidden, K, accumulate);
+    note_launch();
+    return check_launch("moe a2a combine");
+}
 
 size_t k3d_expert_ws_bytes(int hidden, int inter)
 {

@@ -67,6 +67,10 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
                 int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
                 int early);
 
+// k3_ep.cu: grouped byte exchange with every rank (a device copy on one rank)
+int ep_exchange(const void *send, const size_t *scnt, const size_t *soff, void *recv,
+                const size_t *rcnt, const size_t *roff, cudaStream_t st);
+
 // k3_router.cu
 size_t router_ws_bytes(int T, int n_experts);
 int router_f32(int *idx, float *w, const float *x, const float *W, const float *bias,

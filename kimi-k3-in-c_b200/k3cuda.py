@@ -224,6 +224,10 @@ _PROTOS = {
     "k3d_ep_rank": (i32, []),
     "k3d_ep_size": (i32, []),
     "k3d_ep_allreduce_f32": (i32, [vp, sz]),
+    "k3d_moe_a2a_ws_bytes": (sz, [C.POINTER(K3dMoeShape), i32, i32]),
+    "k3d_moe_swiglu_a2a": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, i32, vp,
+                                 vp, vp, sz]),
+    "k3d_a2a_plan": (i32, [vp, i32, i32, i32, vp, vp, vp]),
     # stack
     "k3d_model_create": (vp, [C.POINTER(K3dStackCfg), u64]),
     "k3d_model_destroy": (None, [vp]),
@@ -423,3 +427,23 @@ class MoeWeights:
     def run(self, out, x, T, ws, ws_bytes, accumulate=0, idx=None, wts=None):
         return self.lib.k3d_moe_swiglu(out, x, C.byref(self.w), C.byref(self.shape), T,
                                        accumulate, idx, wts, ws, ws_bytes)
+
+    def a2a_ws_bytes(self, t_max, nranks):
+        return self.lib.k3d_moe_a2a_ws_bytes(C.byref(self.shape), t_max, nranks)
+
+    def run_a2a(self, out, x, T, t_max, ws, ws_bytes, accumulate=0, idx=None, wts=None):
+        """Mode A: this rank's own T tokens, experts dispatched to their ranks."""
+        return self.lib.k3d_moe_swiglu_a2a(out, x, C.byref(self.w), C.byref(self.shape), T, t_max,
+                                           accumulate, idx, wts, ws, ws_bytes)
+
+
+def a2a_plan(idx, n_experts, nranks, lib=None):
+    """k3d_a2a_plan on host arrays: (cnt[nranks], off[nranks], pos[len(idx)])."""
+    lib = lib or load()
+    idx = np.ascontiguousarray(idx, np.int32).reshape(-1)
+    cnt = np.zeros(nranks, np.int32)
+    off = np.zeros(nranks, np.int32)
+    pos = np.zeros(idx.size, np.int32)
+    check(lib.k3d_a2a_plan(idx.ctypes.data, idx.size, n_experts, nranks, cnt.ctypes.data,
+                           off.ctypes.data, pos.ctypes.data), "k3d_a2a_plan")
+    return cnt, off, pos
