@@ -67,7 +67,8 @@ void prof_begin(const char *section);
 void prof_end(const char *section);
 
 // Growable device workspace owned by the context (used by the k3.h entry points,
-// which have no workspace argument of their own).
+// which have no workspace argument of their own). Slots 0-5: 0 normalised inputs, 1 and 4
+// the tensor-core GEMM on the library and the side stream, 2 and 3 other callers.
 void *scratch(size_t bytes, int slot = 0);
 
 // Argument staging for the k3.h entry points (see the POINTERS note in k3.h).

@@ -35,8 +35,8 @@ struct Ctx {
     long launches = 0;
     std::unordered_map<const void *, WeightCopy> wcache;
     size_t wcache_bytes = 0;
-    void *scratch[4] = {nullptr, nullptr, nullptr, nullptr};
-    size_t scratch_bytes[4] = {0, 0, 0, 0};
+    void *scratch[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t scratch_bytes[6] = {0, 0, 0, 0, 0, 0};
     void *arena = nullptr;
     size_t arena_bytes = 0;
     size_t arena_top = 0;
@@ -209,10 +209,14 @@ bool is_device_ptr(const void *p)
 
 void *scratch(size_t bytes, int slot)
 {
-    if (slot < 0 || slot > 3) return nullptr;
+    if (slot < 0 || slot > 5) return nullptr;
     if (bytes == 0) bytes = 256;
     if (g.scratch_bytes[slot] >= bytes) return g.scratch[slot];
-    if (g.scratch[slot]) { cudaStreamSynchronize(g.stream); cudaFree(g.scratch[slot]); }
+    if (g.scratch[slot]) {
+        cudaStreamSynchronize(g.stream);
+        if (g.side) cudaStreamSynchronize(g.side);
+        cudaFree(g.scratch[slot]);
+    }
     g.scratch[slot] = nullptr; g.scratch_bytes[slot] = 0;
     size_t want = bytes + bytes / 4;
     if (cudaMalloc(&g.scratch[slot], want) != cudaSuccess) {

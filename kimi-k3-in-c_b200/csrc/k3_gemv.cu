@@ -275,6 +275,45 @@ __global__ void k_argmax_finish(int *next, const unsigned long long *key, int T)
 
 static bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+// Batches of more than four tokens go to the tensor-core GEMM (k3_gemm_tc.cu), which reads
+// each weight once per 128 tokens, on the two streams it keeps workspace for.
+static bool use_gemm_tc(int in, int T, const float *x, cudaStream_t s)
+{
+    return T > 4 && in % 64 == 0 && al16(x) && (s == stream() || s == side_stream());
+}
+
+// next[t] = the first maximum of logits row t (lowest index among equal values; NaN never
+// wins), by the packing of argmax_pack. grid T, 1024 threads.
+__global__ void k_rows_argmax(int *next, const float *y, int out)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    unsigned long long best = 0;
+    for (int r = threadIdx.x; r < out; r += blockDim.x) {
+        const float v = y[(size_t)t * out + r];
+        const unsigned long long k = argmax_pack(v, r);
+        if (v == v && k > best) best = k;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+    }
+    __shared__ unsigned long long red[32];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            best = v > best ? v : best;
+        }
+        if (threadIdx.x == 0) next[t] = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
+    }
+}
+
 // The streamed GEMVs (k3_gemv_stream.cu) where the shape allows, on the library stream
 // (work on the side stream, which runs beside the main stream's one-CTA-per-SM kernels,
 // keeps the register-staged kernels); K3_GEMV_STREAM=0 in the environment selects the
@@ -304,6 +343,7 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
         const int rows[1] = {out};
         if (gemv_stream_multi(1, &W, ys, rows, x, in, T, accumulate, s)) return check_launch("gemv bf16 stream");
     }
+    if (use_gemm_tc(in, T, x, s) && al16(W)) return gemm_bf16_tc(1, &W, &y, &out, x, in, T, accumulate, 0, s);
     const bool fast = (in % 8) == 0 && al16(W) && (size_t)in * 4 * min(T, 4) <= 200 * 1024;
     if (!fast) {
         for (int t = 0; t < T; t++) {
@@ -339,6 +379,12 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
     if (inter <= 0 || T <= 0) return K3D_OK;
     if (T <= 4 && g_gemv_stream && s == stream() && gemv_stream_swiglu(act, x, Wg, Wu, in, inter, T, s))
         return check_launch("gemv bf16 swiglu stream");
+    if (use_gemm_tc(in, T, x, s) && al16(Wg) && al16(Wu)) {
+        const uint16_t *Ws[2] = {Wg, Wu};
+        float *Ys[2] = {act, act};
+        const int rows[2] = {inter, inter};
+        return gemm_bf16_tc(2, Ws, Ys, rows, x, in, T, 0, 1, s);
+    }
     if ((in % 8) != 0 || !al16(Wg) || !al16(Wu) || (size_t)in * 4 * 4 > 200 * 1024)
         return fail(K3D_EINVAL, "swiglu gemv needs in %% 8 == 0 and aligned rows (in=%d)", in);
     static bool init = false;
@@ -364,8 +410,16 @@ const float *norm_to_scratch(const float *x, const NormIn &ni, int n, int rows, 
 int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const int *rows,
                     const float *x, int in, int T, cudaStream_t s, const NormIn *ni)
 {
-    if (nseg < 1 || nseg > 8 || T < 1 || T > 4)
+    if (nseg < 1 || nseg > 8 || T < 1)
         return fail(K3D_EINVAL, "multi-segment GEMV: %d segments, T=%d", nseg, T);
+    if (T > 4) {
+        if (ni) {
+            x = norm_to_scratch(x, *ni, in, T, s);
+            if (!x) return k3d_status();
+        }
+        if (!use_gemm_tc(in, T, x, s)) return fail(K3D_EINVAL, "multi-segment GEMV: T=%d needs in %% 64 == 0", T);
+        return gemm_bf16_tc(nseg, W, y, rows, x, in, T, 0, 0, s);
+    }
     if (g_gemv_stream && s == stream() && gemv_stream_multi(nseg, W, y, rows, x, in, T, 0, s, ni))
         return check_launch("gemv bf16 multi stream");
     if (ni) {
@@ -394,8 +448,24 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
 int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
                      const uint16_t *W, int in, int out, int T, cudaStream_t s, const NormIn *ni)
 {
-    if (T < 1 || T > 4 || (in % 8) != 0 || !al16(W))
+    if (T < 1 || (in % 8) != 0 || !al16(W))
         return fail(K3D_EINVAL, "lm head: T=%d in=%d", T, in);
+    if (T > 4) {
+        // a batch: logits by the tensor-core GEMM, then one argmax per row
+        if (ni) {
+            x = norm_to_scratch(x, *ni, in, T, s);
+            if (!x) return k3d_status();
+        }
+        if (!use_gemm_tc(in, T, x, s)) return fail(K3D_EINVAL, "lm head: T=%d needs in %% 64 == 0", T);
+        if (!y) {
+            y = (float *)scratch((size_t)T * out * sizeof(float), 5);
+            if (!y) return k3d_status();
+        }
+        K3_TRY(gemm_bf16_tc(1, &W, &y, &out, x, in, T, 0, 0, s));
+        launch_pdl(k_rows_argmax, dim3(T), dim3(1024), 0, s, next, (const float *)y, out);
+        note_launch();
+        return check_launch("lm head rows argmax");
+    }
     static bool init = false;
     if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess

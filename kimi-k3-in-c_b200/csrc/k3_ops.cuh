@@ -67,6 +67,11 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
                 int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
                 int early);
 
+// k3_gemm_tc.cu: Y[j][T][rows[j]] (+)= x[T][in] . W[j]^T on the tensor cores (more than four
+// tokens); swiglu: two matrices (gate, up), Y[0] = silu(gate) * up
+int gemm_bf16_tc(int nmat, const uint16_t *const *W, float *const *Y, const int *rows, const float *x,
+                 int in, int T, int accumulate, int swiglu, cudaStream_t st);
+
 // k3_ep.cu: grouped byte exchange with every rank (a device copy on one rank)
 int ep_exchange(const void *send, const size_t *scnt, const size_t *soff, void *recv,
                 const size_t *rcnt, const size_t *roff, cudaStream_t st);
