@@ -536,7 +536,12 @@ def bench_stack(args, rank, world):
     k3cuda.check(lib.k3d_model_use_graph(model, 1))
     exp_ms = sum(sections.get(k, {}).get("ms_per_call", float("nan"))
                  for k in ("experts.gateup", "experts.down"))
-    alg_exp = (TOPK * B) * (EXPERT_BYTES + INTER * 8 + HIDDEN * 4) + HIDDEN * 4 * B
+    # algorithmic bytes: the weights of the distinct experts the step routed to (measured:
+    # the last MoE layer's count), read once, plus the activation and output rows
+    uniq = lib.k3d_moe_last_unique()
+    if uniq <= 0:
+        uniq = TOPK * B
+    alg_exp = uniq * EXPERT_BYTES + TOPK * B * (INTER * 8 + HIDDEN * 4) + HIDDEN * 4 * B
     if world > 1:
         alg_exp /= world
     achieved = alg_exp / (exp_ms * 1e-3) / 1e9
@@ -565,7 +570,7 @@ def bench_stack(args, rank, world):
         "roofline": {"kernel": EXPERT_KERNEL[args.expert_kernel], "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": load_traffic("moe_experts_traffic.json"),
-                     "alg_bytes_per_launch": alg_exp, "kernel_ms": exp_ms},
+                     "alg_bytes_per_launch": alg_exp, "unique_experts": uniq, "kernel_ms": exp_ms},
         "roofline_step": {"bound": "hbm", "alg_bytes_per_step": step_bytes,
                           "achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm},

@@ -360,7 +360,8 @@ typedef struct {
     int   first_dense, dense_inter;
     /* zero-based MLA layers, -1 terminated list */
     int   mla_layers[16];
-    /* batch and cache */
+    /* batch (1..64: up to 4 tokens stream the weights through GEMVs, more run the
+     * tensor-core GEMM) and cache */
     int   batch;
     int   ctx_cap;
 } K3dStackCfg;

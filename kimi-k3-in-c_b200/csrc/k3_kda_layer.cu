@@ -236,8 +236,8 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
         !w->q_conv || !w->k_conv || !w->v_conv || !w->A_log || !w->dt_bias || !w->o_norm)
         return fail(K3D_EINVAL, "kda layer weight missing");
     const int H = s->heads, D = s->head_dim, P = H * D;
-    if (D < 32 || D > 128 || D % 32 || s->conv_k < 1 || s->conv_k > 16 || B < 1 || B > 4)
-        return fail(K3D_EINVAL, "kda layer: head_dim %d (32..128, multiple of 32), conv_k %d, B %d (1..4)",
+    if (D < 32 || D > 128 || D % 32 || s->conv_k < 1 || s->conv_k > 16 || B < 1 || B > 256)
+        return fail(K3D_EINVAL, "kda layer: head_dim %d (32..128, multiple of 32), conv_k %d, B %d (1..256)",
                     D, s->conv_k, B);
     if (ws_bytes < k3d_kda_layer_ws_bytes(s, B)) return fail(K3D_EINVAL, "kda layer workspace");
     char *p = (char *)ws;

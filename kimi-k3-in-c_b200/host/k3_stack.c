@@ -20,6 +20,7 @@
 #include "k3_cuda.h"
 
 #define K3S_MAX_LAYERS 16
+#define K3S_MAX_BATCH 64
 #define K3S_MAX_TENSORS 4096
 
 typedef struct {
@@ -124,7 +125,7 @@ static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
 {
     if (!cfg || cfg->n_layers < 1 || cfg->n_layers > K3S_MAX_LAYERS || cfg->batch < 1 ||
-        cfg->batch > 4 || cfg->ctx_cap < 1 || cfg->hidden < 1 || cfg->vocab < 1)
+        cfg->batch > K3S_MAX_BATCH || cfg->ctx_cap < 1 || cfg->hidden < 1 || cfg->vocab < 1)
         return NULL;
     if (k3d_init(k3d_device() < 0 ? 0 : k3d_device())) return NULL;
     K3dModel *m = (K3dModel *)calloc(1, sizeof(K3dModel));

@@ -91,7 +91,7 @@ def untile_expert(slot, hidden, inter):
             (("p1", p1), ("s1", s1), ("p3", p3), ("s3", s3), ("p2", p2), ("s2", s2))}
 
 
-def host_copy(k3, model, c, layout=0):
+def host_copy(k3, model, c, layout=0, batch=1, cap=64):
     E, P, D, H = c["hidden"], c["kda_heads"] * c["kda_head_dim"], c["kda_head_dim"], c["kda_heads"]
     m, mo = c["mla"], c["moe"]
     W, S = {}, {}
@@ -111,7 +111,7 @@ def host_copy(k3, model, c, layout=0):
                 W[p + "mla." + k] = download(k3, model, p + "mla." + k, np.uint16, shp)
             for k in ("q_a_norm", "kv_a_norm"):
                 W[p + "mla." + k] = download(k3, model, p + "mla." + k, np.float32)
-            S[p + "mla.cache"] = download(k3, model, p + "mla.cache", np.uint16, (1, 64, kvw))
+            S[p + "mla.cache"] = download(k3, model, p + "mla.cache", np.uint16, (batch, cap, kvw))
         else:
             shapes = {"q": (P, E), "k": (P, E), "v": (P, E), "g": (P, E), "b": (H, E), "f_a": (D, E),
                       "f_b": (P, D), "o": (E, P)}
@@ -179,5 +179,48 @@ def test_stack_decode_matches_oracle_eager_and_graph(k3, oracle, layout):
                 assert nxt[0] == int(np.argmax(want)), step
             tok = int(nxt[0])
         assert int(download(k3, model, "pos", np.int32)[0]) == 9
+    finally:
+        k3.k3d_model_destroy(model)
+
+
+def sequence_state(c, S, b, batch):
+    """Sequence b's own caches and states (copies the oracle updates in place)."""
+    out = {"pos": S["pos"]}
+    for l in range(c["n_layers"]):
+        p = f"layer{l}."
+        if p + "mla.cache" in S:
+            out[p + "mla.cache"] = S[p + "mla.cache"][b:b + 1].copy()
+        else:
+            st = S[p + "kda.state"]
+            n = st.size // batch
+            out[p + "kda.state"] = st[b * n:(b + 1) * n].copy()
+    return out
+
+
+def test_stack_batch_decode_matches_oracle_per_sequence(k3, oracle):
+    """A batch of 6 sequences (above 4: every projection runs the tensor-core GEMM, the MoE
+    layers route 6 tokens), eager then graph-captured; each sequence's logits against the
+    oracle stepping that sequence alone from its own cache and state."""
+    c, B = CFG, 6
+    model = k3.k3d_model_create(ctypes.byref(make_cfg(c, batch=B, layout=1)), 4321)
+    assert model, k3.k3d_last_message()
+    try:
+        k3cuda.check(k3.k3d_model_fill_context(model, 7, 55))
+        k3cuda.check(k3.k3d_sync())
+        W, S = host_copy(k3, model, c, 1, batch=B)
+        seqs = [sequence_state(c, S, b, B) for b in range(B)]
+        toks = np.array([3, 17, 17, 500, 1023, 42], np.int32)
+        for step in range(3):          # eager, capture, replay
+            nxt = np.zeros(B, np.int32)
+            k3cuda.check(k3.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
+            got = download(k3, model, "logits", np.float32).reshape(B, c["vocab"])
+            for b in range(B):
+                want = orc_mod.stack_step(oracle, c, W, seqs[b], int(toks[b]))
+                err = max_rel_err(got[b], want)
+                assert err <= 1e-3, (step, b, err)
+                top2 = np.sort(want)[-2:]
+                if top2[1] - top2[0] > 1e-3 * np.abs(want).max():
+                    assert nxt[b] == int(np.argmax(want)), (step, b)
+            toks = nxt.copy()
     finally:
         k3.k3d_model_destroy(model)
