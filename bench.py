@@ -33,7 +33,8 @@ EXPERT_BYTES = 3 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)   # 23,396,352
 METRIC = "decode tok/s at 1/2/4/8 B200; MXFP4 expert GEMV HBM GB/s vs peak"
 EXPERT_KERNEL = {0: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA (k_mxfp4_umma gate/up + down)",
                  1: "MXFP4 expert GEMV, mma.sync m16n8k16 (k_mxfp4_mma gate/up + down)",
-                 2: "MXFP4 expert GEMV, CUDA cores (k_moe_gate_up + k_moe_down)"}
+                 2: "MXFP4 expert GEMV, CUDA cores (k_moe_gate_up + k_moe_down)",
+                 3: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA, one token per item"}
 
 
 def dist_env():
@@ -272,7 +273,7 @@ def bench_moe(args, rank, world):
     sh = (synth.bf16_normal(g, (SHARED, HIDDEN), 0.02), synth.bf16_normal(g, (SHARED, HIDDEN), 0.02),
           synth.bf16_normal(g, (HIDDEN, SHARED), 0.02))
     mw = k3cuda.MoeWeights(HIDDEN, INTER, n_exp, TOPK, W, bias, shared=sh, seed=7, lo=lo, hi=hi,
-                           add_shared=1 if rank == 0 else 0, tiled=args.expert_kernel == 0,
+                           add_shared=1 if rank == 0 else 0, tiled=args.expert_kernel in (0, 3),
                            lib=lib)
     P = 64
     xs = synth.bf16_to_f32(synth.bf16_normal(g, (P, HIDDEN), 1.0))
@@ -477,7 +478,7 @@ def bench_stack(args, rank, world):
     cap = ctx + args.steps * 2 + args.warmup * 2 + 16
     # the tcgen05 kernel streams experts stored in the tiled layout; the other two
     # kernels read the checkpoint layout
-    cfg = stack_cfg(world, rank, args.batch, cap, 1 if args.expert_kernel == 0 else 0)
+    cfg = stack_cfg(world, rank, args.batch, cap, 1 if args.expert_kernel in (0, 3) else 0)
     t0 = time.time()
     model = lib.k3d_model_create(C.byref(cfg), 2024)
     if not model:
@@ -639,8 +640,9 @@ def main():
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bounded CPU-baseline sample length; 0 skips it")
-    ap.add_argument("--expert-kernel", type=int, default=0, choices=[0, 1, 2],
-                    help="0 tcgen05 block-scaled (default), 1 mma.sync, 2 CUDA cores")
+    ap.add_argument("--expert-kernel", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="0 tcgen05 block-scaled (default), 1 mma.sync, 2 CUDA cores, 3 tcgen05 "
+                         "with one token per work item")
     ap.add_argument("--n-experts", type=int, default=N_EXPERTS,
                     help="routed experts resident per layer (384 = config 1; fewer only for "
                          "profiling captures that must stay small)")

@@ -169,10 +169,12 @@ int    k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoe
 int    k3d_expert_pretile(const K3ExpertQ *dst, const K3ExpertQ *src, int hidden, int inter);
 /* Which MXFP4 expert kernel k3d_expert_swiglu / k3d_moe_swiglu run: 0 (default) the
  * tcgen05 block-scaled tensor-core kernel whenever the shapes allow it (hidden and inter
- * multiples of 512, T * topk <= 64), 1 the mma.sync kernel, 2 the CUDA-core kernels.
+ * multiples of 512, T * topk <= 64), 1 the mma.sync kernel, 2 the CUDA-core kernels, 3 the
+ * tcgen05 kernel with one token per work item (kind 0 lets up to four tokens routed to the
+ * same tiled expert share its weight stages when there are more than 64 assignments).
  * Experts in the tiled layout always run on the tcgen05 kernel.
- * All three give the same results within the expert tolerance; the switch exists to
- * measure and test each. */
+ * All give the same results within the expert tolerance; the switch exists to measure
+ * and test each. */
 int    k3d_set_expert_kernel(int kind);
 /* The router alone on a bf16 W: idx/w [T][topk], device. */
 int    k3d_router_bf16(int *idx, float *w, const float *x, const uint16_t *W,

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256, 2) k_moe_down(float *contrib, const float
 // ---- ordered combine ------------------------------------------------------------------
 __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t slice_stride,
                               const int *idx, const float *wts, const float *sh_out, int hidden,
-                              int K, int lo, int hi, int accumulate)
+                              int K, int lo, int hi, int accumulate, const int *pos_of)
 {
     pdl_wait();
     pdl_trigger();
@@ -151,7 +151,11 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
             const int a = t * K + min(j0 + k, K - 1);
             e[k] = __ldg(idx + a);
             w[k] = __ldg(wts + a);
-            c[k] = contrib + (size_t)a * hidden + r;
+            // contributions by assignment, or by grouped position (only this rank's experts
+            // have one: another rank's slot reads row 0 and is not added)
+            const bool local = e[k] >= lo && e[k] < hi;
+            const int row = !pos_of ? a : (local ? __ldcg(pos_of + a) : 0);
+            c[k] = contrib + (size_t)row * hidden + r;
             v[k] = c[k][0];
         }
         for (int s0 = 1; s0 < ks; s0 += 4) {
@@ -256,6 +260,8 @@ struct ExpertBufs {
     __half *xb_x; float *xs_x; __half *xb_a; float *xs_a;   // mma.sync activation splits
     uint8_t *bq_x, *bs_x, *bq_a, *bs_a;    // tcgen05: E2M1 pieces of x and of act
     float *part_gu, *part_d;               // tcgen05: K-slice partials
+    uint8_t *bqg_x, *bsg_x, *bqg_a, *bsg_a;   // tcgen05 grouped: pieces of x and act by group
+    UmmaGroups grp;                        // tcgen05 grouped: the groups (null when absent)
 };
 
 // Where the per-assignment contributions ended up: contrib[s * slice + a * hidden + r].
@@ -263,6 +269,7 @@ struct ExpertOut {
     const float *contrib;
     int ks;
     size_t slice;
+    const int *pos_of;       // grouped pass: contributions are by position; pos_of[a] = row
 };
 
 static bool umma_shapes(int hidden, int inter)
@@ -285,10 +292,23 @@ static int umma_ks_cap(int K, int TK)
     return TK <= kUmmaMaxTK ? K / 512 : 1;
 }
 
+// The grouped tcgen05 pass (several tokens of an expert share each weight stage) for
+// batches: tiled experts, more than kUmmaMaxTK assignments, unless kind 3 turns it off.
+static bool grouped_eligible(int hidden, int inter, int TK, int layout)
+{
+    return layout == 1 && TK > kUmmaMaxTK && umma_shapes(hidden, inter);
+}
+
 // True when run_experts takes the tcgen05 path.
 static bool use_umma(const ExpertBufs &B, int hidden, int inter, int TK, int layout)
 {
-    return (layout == 1 || g_expert_kernel == 0) && B.bq_x && umma_eligible(hidden, inter, TK, layout);
+    return (layout == 1 || g_expert_kernel == 0 || g_expert_kernel == 3) && B.bq_x &&
+           umma_eligible(hidden, inter, TK, layout);
+}
+
+static bool use_grouped(const ExpertBufs &B, int TK, int layout, int hidden, int inter)
+{
+    return g_expert_kernel != 3 && B.bqg_x && grouped_eligible(hidden, inter, TK, layout);
 }
 
 // gate/up -> act -> down -> contributions for a work list. tcgen05 block-scaled MMA
@@ -306,6 +326,28 @@ static int run_experts(const MoeWork &mw, const int *idx, const int *count, int 
     const int topk = mw.single_mode ? 1 : mw.K;
     if (layout == 1 && (!B.bq_x || !umma_eligible(hidden, inter, TK, 1)))
         return fail(K3D_EINVAL, "tiled experts need hidden and inter multiples of 512");
+    O.pos_of = nullptr;
+    if (!mw.single_mode && count && use_grouped(B, TK, layout, hidden, inter)) {
+        // groups of up to four tokens of one expert share each weight stage; partials by
+        // position (one K slice: a batch fills the GPU without splitting K)
+        const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
+        K3_TRY(umma_make_groups(mw, B.grp, st));
+        K3_TRY(umma_bsplit_group_x(B.bqg_x, B.bsg_x, x, hidden, mw.assign, topk, B.grp, TK, st));
+        prof_begin("experts.gateup");
+        K3_TRY(umma_launch_grouped(0, mw, B.grp, TK, hidden, inter, 1, B.bqg_x, B.bsg_x, B.part_gu, 2 * inter,
+                                   sl_gu, st));
+        prof_end("experts.gateup");
+        K3_TRY(umma_bsplit_swiglu_group(B.bqg_a, B.bsg_a, B.part_gu, 1, sl_gu, inter, B.grp, TK, st));
+        prof_begin("experts.down");
+        K3_TRY(umma_launch_grouped(1, mw, B.grp, TK, inter, hidden, 1, B.bqg_a, B.bsg_a, B.part_d, hidden, sl_d,
+                                   st));
+        prof_end("experts.down");
+        O.contrib = B.part_d;
+        O.ks = 1;
+        O.slice = sl_d;
+        O.pos_of = B.grp.pos_of;
+        return K3D_OK;
+    }
     if (use_umma(B, hidden, inter, TK, layout)) {
         const int ks_gu = std::min(umma_slices(TK, hidden, inter, 0), umma_ks_cap(hidden, TK));
         const int ks_d = std::min(umma_slices(TK, inter, hidden, 1), umma_ks_cap(inter, TK));
@@ -376,6 +418,21 @@ static void expert_bufs_layout(ExpertBufs &eb, const K3dMoeShape *s, size_t T, s
     } else {
         eb.bq_x = eb.bs_x = eb.bq_a = eb.bs_a = nullptr;
         eb.part_gu = eb.part_d = nullptr;
+    }
+    if (grouped_eligible(s->hidden, s->inter, (int)TK, s->expert_layout)) {
+        // at most one group per assignment
+        eb.bqg_x = (uint8_t *)take(TK * umma_bq_group_bytes(s->hidden));
+        eb.bsg_x = (uint8_t *)take(TK * umma_bs_bytes(s->hidden));
+        eb.bqg_a = (uint8_t *)take(TK * umma_bq_group_bytes(s->inter));
+        eb.bsg_a = (uint8_t *)take(TK * umma_bs_bytes(s->inter));
+        eb.grp.ng = (int *)take(16);
+        eb.grp.p0 = (int *)take(TK * sizeof(int));
+        eb.grp.n = (int *)take(TK * sizeof(int));
+        eb.grp.e = (int *)take(TK * sizeof(int));
+        eb.grp.pos_of = (int *)take(TK * sizeof(int));
+    } else {
+        eb.bqg_x = eb.bsg_x = eb.bqg_a = eb.bsg_a = nullptr;
+        eb.grp = UmmaGroups{nullptr, nullptr, nullptr, nullptr, nullptr};
     }
 }
 
@@ -457,6 +514,8 @@ static ExpertWs expert_ws_layout(int hidden, int inter, void *base)
         L.eb.bq_x = L.eb.bs_x = L.eb.bq_a = L.eb.bs_a = nullptr;
         L.eb.part_gu = L.eb.part_d = nullptr;
     }
+    L.eb.bqg_x = L.eb.bsg_x = L.eb.bqg_a = L.eb.bsg_a = nullptr;   // one expert: no groups
+    L.eb.grp = UmmaGroups{nullptr, nullptr, nullptr, nullptr, nullptr};
     L.total = off;
     return L;
 }
@@ -497,6 +556,17 @@ __global__ void k_a2a_pack(float *sendbuf, int *send_ids, const float *x, const 
     float4 *dst = reinterpret_cast<float4 *>(sendbuf + (size_t)row * hidden);
     for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) dst[i] = src[i];
     if (threadIdx.x == 0) send_ids[row] = idx[a];
+}
+
+// dst[a] = src[pos_of[a]] (rows of hidden floats). grid = rows, 256 threads.
+__global__ void k_gather_rows(float *dst, const float *src, const int *pos_of, int hidden)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int a = blockIdx.x;
+    const float4 *s4 = reinterpret_cast<const float4 *>(src + (size_t)__ldcg(pos_of + a) * hidden);
+    float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)a * hidden);
+    for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
 }
 
 // out[t] (+)= sum over slots k, in top-k order, of w[t][k] * back[pos[t K + k]], then the
@@ -719,7 +789,14 @@ int k3d_moe_swiglu_a2a(float *out, const float *x, const K3dMoeW *w, const K3dMo
                            s->inter, s->expert_layout, L.eb, O, st));
         prof_end("moe.experts");
         ybuf = O.contrib;
-        if (O.ks > 1) {
+        if (O.pos_of) {
+            // grouped pass: rows by position; the exchange sends them by received row
+            launch_pdl(k_gather_rows, dim3((unsigned)R), dim3(256), 0, st, L.eb.contrib, O.contrib, O.pos_of,
+                       s->hidden);
+            note_launch();
+            K3_TRY(check_launch("moe a2a gather"));
+            ybuf = L.eb.contrib;
+        } else if (O.ks > 1) {
             K3_TRY(umma_slice_sum(L.eb.contrib, O.contrib, O.ks, O.slice, (int)(R * s->hidden), st));
             ybuf = L.eb.contrib;
         }
@@ -744,7 +821,7 @@ size_t k3d_expert_ws_bytes(int hidden, int inter)
 
 int k3d_set_expert_kernel(int kind)
 {
-    if (kind < 0 || kind > 2) return fail(K3D_EINVAL, "k3d_set_expert_kernel(%d): 0, 1 or 2", kind);
+    if (kind < 0 || kind > 3) return fail(K3D_EINVAL, "k3d_set_expert_kernel(%d): 0 to 3", kind);
     g_expert_kernel = kind;
     return K3D_OK;
 }
@@ -808,7 +885,8 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     // time is measured on its own.
     const bool shared = s->shared_inter > 0 && s->add_shared;
     const int umax = TK < (s->expert_hi - s->expert_lo) ? TK : (s->expert_hi - s->expert_lo);
-    const bool early_split = umax > 0 && use_umma(L.eb, s->hidden, s->inter, TK, s->expert_layout);
+    const bool early_split = umax > 0 && use_umma(L.eb, s->hidden, s->inter, TK, s->expert_layout) &&
+                             !use_grouped(L.eb, TK, s->expert_layout, s->hidden, s->inter);
     cudaStream_t sst = (!profiling() && side_stream()) ? side_stream() : st;
     if ((shared || early_split) && sst != st) {
         if (cudaEventRecord(side_event(0), st) != cudaSuccess ||
@@ -861,7 +939,7 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
         return fail(K3D_ECUDA, "moe: join from the side stream");
     dim3 grid((s->hidden + 255) / 256, T);
     launch_pdl(k_moe_combine, dim3(grid), dim3(256), 0, st, out, O.contrib, O.ks, O.slice, I, Wt, shared ? L.sh_out : nullptr,
-                                        s->hidden, K, s->expert_lo, s->expert_hi, accumulate);
+                                        s->hidden, K, s->expert_lo, s->expert_hi, accumulate, O.pos_of);
     note_launch();
     K3_TRY(check_launch("moe combine"));
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;

@@ -57,7 +57,6 @@ constexpr int kOffSFB = kOffSFA + 4 * 512;       // 38912
 constexpr int kOffRawA = kOffSFB + 4 * 512;      // 40960: scale rows as loaded, 128 x 16 B
 constexpr int kStageBytes = kOffRawA + 128 * 16;  // 43008 (multiple of 1024)
 constexpr int kTileA = 32768, kTileSF = 2048, kTileB = 4096;   // tiled-layout units per stage
-constexpr uint32_t kStageTx = kTileA + kTileSF + kTileB + kTileSF;
 constexpr int kStages = 5;
 constexpr int kLag = 3;                      // producer publishes a stage kLag stages later
 constexpr int kProducers = 128;
@@ -89,6 +88,8 @@ struct Job {
     int vec_pos;             // 1: B vector = grouped position p (down: act pieces by position)
     int out_pos;             // 1: partial row block = p (gate/up), else the assignment a
     int n_experts;           // MoE mode: expert ids must lie in [0, n_experts)
+    const int *g_p0, *g_n, *g_e;   // grouped items: first position, tokens (<= 4) and expert
+                                   // of each group; the count is the number of groups
     int early;               // 1: the work list and the weights do not depend on the kernel
                              //    launched just before (only the B operand does): the work
                              //    list is read and the first stages' weights are requested
@@ -192,9 +193,10 @@ __device__ __forceinline__ uint64_t desc_sf(uint32_t a)
 
 // Instruction descriptor: kind::mxf4, A and B E2M1 (format 1), UE8M0 scales, K-major
 // operands, M = 128, N = 16, scale-factor byte ids for A and B.
+template <int N>
 __device__ __forceinline__ uint32_t idesc_mxf4(uint32_t sf_id)
 {
-    return (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) | (1u << 23) |
+    return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
            ((uint32_t)(128 >> 4) << 24) | (sf_id << 29) | (sf_id << 4);
 }
 
@@ -262,17 +264,43 @@ __device__ __forceinline__ void publish(unsigned char *st, int tid)
 // -> expert table entry).
 struct ItemEnt {
     const uint8_t *c0, *c1, *s0, *s1;   // weight codes / scales (gate and up, or down twice)
-    int out;                            // partial row block (position or assignment)
+    int out;                            // partial row block (position or assignment; grouped:
+                                        // the first of nv consecutive positions)
     int tile, s;                        // 128-row tile, K slice
-    int vec;                            // B operand vector
+    int vec;                            // B operand vector (grouped: the group)
+    int nv;                             // vectors of the item (1, or up to 4 when grouped)
+    int pad[3];
 };
-static_assert(sizeof(ItemEnt) == 48, "item entry size");
+static_assert(sizeof(ItemEnt) == 64, "item entry size");
 constexpr int kMaxItems = 128;          // table entries per round
 constexpr int kOffItems = 1024;         // after the barrier header
-constexpr int kStage0 = kOffItems + kMaxItems * 48;   // 7168, 1024-aligned
+constexpr int kStage0 = kOffItems + kMaxItems * 64;   // 9216, 1024-aligned
 constexpr int kAccBufs = 4;             // accumulator ring depth
-constexpr size_t kSmemTotal = 1024 + kStage0 + (size_t)kStages * kStageBytes;
 
+// Stage geometry for NV activation vectors per item. NV = 1: one vector (the assignment's
+// token) per item, B = 16 piece rows. NV = 4 (grouped): up to four tokens routed to the
+// same expert share each weight stage; B stacks their pieces as 64 rows (row 16 v + p =
+// piece p of slot v), one MMA of N = 64 per K step, and the scale atoms hold B row m at
+// byte 16 (m % 32) + 4 (m / 32) + block (the layout of A's 128 rows).
+template <int NV>
+struct Geo {
+    static constexpr int kBTile = NV * kTileB;                  // B tile per stage
+    static constexpr int kB = kTileA;                           // 32768
+    static constexpr int kSFA = kB + kBTile;
+    static constexpr int kSFB = kSFA + kTileSF;
+    static constexpr int kBytes = NV == 1 ? kStageBytes : kSFB + kTileSF;
+    static constexpr int kNStages = NV == 1 ? kStages : 4;
+    static constexpr int kCols = kN * NV;                       // MMA N, accumulator columns
+    static constexpr int kTmem = NV == 1 ? kTmemCols : 512;
+    static constexpr uint32_t kSfaCol = NV == 1 ? umma::kSfaCol : 256;
+    static constexpr uint32_t kSfbCol = NV == 1 ? umma::kSfbCol : 288;
+    static constexpr uint32_t kTx = kTileA + kTileSF + kBTile + kTileSF;
+    static constexpr size_t kSmem = 1024 + kStage0 + (size_t)kNStages * kBytes;
+    static_assert(kBytes % 1024 == 0, "stage alignment");
+    static_assert(kAccBufs * kCols + 64 <= kTmem, "tensor memory");
+};
+
+template <int NV>
 __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
 {
     ItemEnt it;
@@ -280,6 +308,25 @@ __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
     const int rest = item / J.ks;
     it.tile = rest % J.ntiles;
     const int p = rest / J.ntiles;
+    it.nv = 1;
+    it.pad[0] = it.pad[1] = it.pad[2] = 0;
+    if (NV > 1) {
+        // p is a group: nv consecutive positions of one expert
+        const int nv = __ldcg(J.g_n + p), e = __ldcg(J.g_e + p);
+        if (e < 0 || e >= J.n_experts || nv < 1 || nv > NV) {
+            k3_raise(K3D_EBOUND, K3_SITE_MXFP4);
+            it.c0 = it.c1 = it.s0 = it.s1 = nullptr;
+            it.out = it.tile = it.s = it.vec = 0;
+            return it;
+        }
+        const K3ExpertQ q = J.table[e];
+        if (J.mode == GATEUP) { it.c0 = q.p1; it.c1 = q.p3; it.s0 = q.s1; it.s1 = q.s3; }
+        else { it.c0 = it.c1 = q.p2; it.s0 = it.s1 = q.s2; }
+        it.out = __ldcg(J.g_p0 + p);
+        it.vec = p;
+        it.nv = nv;
+        return it;
+    }
     int a;
     K3ExpertQ q;
     if (J.single_mode) {
@@ -318,58 +365,62 @@ __device__ __forceinline__ bool item_ok(const ItemEnt &it)
 }
 
 // Tiled layout: the weight tile of one stage and its scale atoms, completing on `fb`.
+template <int NV>
 __device__ __forceinline__ void issue_weights(uint32_t sb, uint32_t fb, const Job &J, const ItemEnt &it,
                                               int chunk)
 {
     const size_t tix = (size_t)it.tile * J.nch + chunk;
     bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
-    bulk_g2s(sb + kOffSFA, it.s0 + tix * kTileSF, kTileSF, fb);
+    bulk_g2s(sb + Geo<NV>::kSFA, it.s0 + tix * kTileSF, kTileSF, fb);
 }
 
 // The B tile of one stage and its scale atoms, completing on `fb`.
+template <int NV>
 __device__ __forceinline__ void issue_operand(uint32_t sb, uint32_t fb, const Job &J, const ItemEnt &it,
                                               int chunk)
 {
     const size_t vix = (size_t)it.vec * J.nch + chunk;
-    bulk_g2s(sb + kOffB, J.bq + vix * kTileB, kTileB, fb);
-    bulk_g2s(sb + kOffSFB, J.bs + vix * kTileSF, kTileSF, fb);
+    bulk_g2s(sb + Geo<NV>::kB, J.bq + vix * Geo<NV>::kBTile, Geo<NV>::kBTile, fb);
+    bulk_g2s(sb + Geo<NV>::kSFB, J.bs + vix * kTileSF, kTileSF, fb);
 }
 
 // MMA issuer (one thread): the J.cps stages of each of `nr` items into the accumulator
 // buffer of the item, releasing each stage and publishing each accumulator on its
 // mbarrier. The stage and item positions carry across calls. False when a wait gave up.
+template <int NV>
 __device__ __forceinline__ bool mma_items(const Job &J, int nr, int &g_mma, int &n_mma, uint32_t tmem,
                                           uint32_t stage0, uint32_t b_full, uint32_t b_empty,
                                           uint32_t b_accf, uint32_t b_acce, volatile int *abort)
 {
+    using G = Geo<NV>;
     for (int k = 0; k < nr; k++, n_mma++) {
         const int buf = n_mma % kAccBufs;
         if (n_mma >= kAccBufs && !mbar_wait(b_acce + 8 * buf, ((n_mma / kAccBufs) - 1) & 1, abort))
             return false;
         tc_fence_after();
-        const uint32_t dcol = tmem + (uint32_t)(buf * kN);
+        const uint32_t dcol = tmem + (uint32_t)(buf * G::kCols);
         for (int c = 0; c < J.cps; c++) {
-            const int st = g_mma % kStages;
-            if (!mbar_wait(b_full + 8 * st, (g_mma / kStages) & 1, abort)) return false;
+            const int st = g_mma % G::kNStages;
+            if (!mbar_wait(b_full + 8 * st, (g_mma / G::kNStages) & 1, abort)) return false;
             tc_fence_after();
-            const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
-            const uint32_t sfa = tmem + kSfaCol + (uint32_t)((g_mma & 1) * 16);
-            const uint32_t sfb = tmem + kSfbCol + (uint32_t)((g_mma & 1) * 16);
+            const uint32_t sb = stage0 + (uint32_t)st * G::kBytes;
+            const uint32_t sfa = tmem + G::kSfaCol + (uint32_t)((g_mma & 1) * 16);
+            const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)((g_mma & 1) * 16);
 #pragma unroll
             for (int a4 = 0; a4 < 4; a4++) {
-                tc_cp_sf(sfa + 4 * a4, desc_sf(sb + kOffSFA + 512 * a4));
-                tc_cp_sf(sfb + 4 * a4, desc_sf(sb + kOffSFB + 512 * a4));
+                tc_cp_sf(sfa + 4 * a4, desc_sf(sb + G::kSFA + 512 * a4));
+                tc_cp_sf(sfb + 4 * a4, desc_sf(sb + G::kSFB + 512 * a4));
             }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
                 const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
-                const uint64_t bd = desc_sw128(sb + kOffB + kb * 2048u + off);
+                const uint64_t bd = desc_sw128(sb + G::kB + kb * (uint32_t)(NV * 2048) + off);
                 const uint32_t id = (uint32_t)((j & 1) * 2);
                 // blocks 2j, 2j+1: the scales in atom j/2 (a scale address is a 4-column
                 // group); the byte id picks the pair
                 const uint32_t atom = (uint32_t)(4 * (j >> 1));
-                tc_mma(dcol, ad, bd, idesc_mxf4(id), (c > 0 || j > 0) ? 1u : 0u,
+                tc_mma(dcol, ad, bd, idesc_mxf4<G::kCols>(id), (c > 0 || j > 0) ? 1u : 0u,
                        (sfa + atom) | (id << 30), (sfb + atom) | (id << 30));
             }
             tc_commit(b_empty + 8 * st);
@@ -383,10 +434,12 @@ __device__ __forceinline__ bool mma_items(const Job &J, int nr, int &g_mma, int 
 // Epilogue warp of tensor-memory lane quadrant q: for each of `nr` items, its 32 rows of
 // the 128 x 16 accumulator, summed over the 16 pieces and stored as the item's partial.
 // False when a wait gave up.
+template <int NV>
 __device__ __forceinline__ bool epilogue_items(const Job &J, const ItemEnt *items, int nr, int &n_epi,
                                                uint32_t tmem, uint32_t b_accf, uint32_t b_acce,
                                                volatile int *abort, int q, int lane)
 {
+    using G = Geo<NV>;
     const int m = q * 32 + lane;            // tile row
     for (int k = 0; k < nr; k++, n_epi++) {
         const ItemEnt &it = items[k];
@@ -397,21 +450,30 @@ __device__ __forceinline__ bool epilogue_items(const Job &J, const ItemEnt *item
         const int buf = n_epi % kAccBufs;
         if (!mbar_wait(b_accf + 8 * buf, (n_epi / kAccBufs) & 1, abort)) return false;
         tc_fence_after();
-        float v[16];
-        tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kN), v);
+        float v[G::kCols];
+#pragma unroll
+        for (int u = 0; u < NV; u++)
+            tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * G::kCols + u * kN), v + u * kN);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(b_acce + 8 * buf);
-        float sum = v[15];
+        // each vector's 16 pieces, smallest first; vector u is position out + u
 #pragma unroll
-        for (int i = 14; i >= 0; i--) sum += v[i];
-        *dst = sum;
+        for (int u = 0; u < NV; u++) {
+            if (u >= it.nv) break;
+            float sum = v[u * kN + 15];
+#pragma unroll
+            for (int i = 14; i >= 0; i--) sum += v[u * kN + i];
+            dst[(size_t)u * J.out_w] = sum;
+        }
     }
     return true;
 }
 
+template <int NV>
 __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 {
+    using G = Geo<NV>;
     extern __shared__ unsigned char smem_raw[];
     // 1024-aligned base (the SWIZZLE_128B pattern is a function of the absolute address)
     const uint32_t raw = saddr(smem_raw);
@@ -432,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < G::kNStages; s++) {
             mbar_init(b_full + 8 * s, J.tiled ? 1 : kProducers);
             mbar_init(b_empty + 8 * s, 1);
         }
@@ -443,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     }
     if (warp == 4) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(saddr(tmem_slot)), "r"(kTmemCols) : "memory");
+                     :: "r"(saddr(tmem_slot)), "r"(G::kTmem) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         tc_fence_before();
     }
@@ -469,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 
     for (int r0 = i_beg; r0 < i_end; r0 += kMaxItems) {
         const int r1 = min(i_end, r0 + kMaxItems);
-        for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) items[i - r0] = decode(J, i);
+        for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) items[i - r0] = decode<NV>(J, i);
         __syncthreads();
         const int nr = r1 - r0;
         const bool prefetch = J.early && J.tiled && r0 == i_beg;
@@ -489,26 +551,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                 // requested before waiting for the kernel that writes the B operand
                 int pre = 0;
                 if (prefetch) {
-                    pre = min(kStages, nr * J.cps);
+                    pre = min(G::kNStages, nr * J.cps);
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h / J.cps];
                         if (!item_ok(it)) continue;
-                        const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
-                        const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
-                        mbar_expect_tx(fb, kStageTx);
-                        issue_weights(sb, fb, J, it, it.s * J.cps + h % J.cps);
+                        const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % G::kNStages) * G::kBytes;
+                        const uint32_t fb = b_full + 8 * ((g_prod + h) % G::kNStages);
+                        mbar_expect_tx(fb, G::kTx);
+                        issue_weights<NV>(sb, fb, J, it, it.s * J.cps + h % J.cps);
                     }
                     pdl_wait();
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h / J.cps];
-                        const uint32_t fb = b_full + 8 * ((g_prod + h) % kStages);
+                        const uint32_t fb = b_full + 8 * ((g_prod + h) % G::kNStages);
                         if (!item_ok(it)) {
                             k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
                             mbar_arrive(fb);
                             continue;
                         }
-                        const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % kStages) * kStageBytes;
-                        issue_operand(sb, fb, J, it, it.s * J.cps + h % J.cps);
+                        const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % G::kNStages) * G::kBytes;
+                        issue_operand<NV>(sb, fb, J, it, it.s * J.cps + h % J.cps);
                     }
                 }
                 int h = 0;       // stage index within this round
@@ -519,18 +581,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                     for (int c = 0; c < J.cps; c++, h++) {
                         if (h < pre) { g_prod++; continue; }     // issued above
                         const int chunk = it.s * J.cps + c;
-                        const int st = g_prod % kStages;
-                        if (g_prod >= kStages &&
-                            !mbar_wait(b_empty + 8 * st, ((g_prod / kStages) - 1) & 1, abort)) {
+                        const int st = g_prod % G::kNStages;
+                        if (g_prod >= G::kNStages &&
+                            !mbar_wait(b_empty + 8 * st, ((g_prod / G::kNStages) - 1) & 1, abort)) {
                             stop = true;
                             break;
                         }
-                        const uint32_t sb = stage0 + (uint32_t)st * kStageBytes;
+                        const uint32_t sb = stage0 + (uint32_t)st * G::kBytes;
                         const uint32_t fb = b_full + 8 * st;
                         if (aligned) {
-                            mbar_expect_tx(fb, kStageTx);
-                            issue_weights(sb, fb, J, it, chunk);
-                            issue_operand(sb, fb, J, it, chunk);
+                            mbar_expect_tx(fb, G::kTx);
+                            issue_weights<NV>(sb, fb, J, it, chunk);
+                            issue_operand<NV>(sb, fb, J, it, chunk);
                         } else {
                             mbar_arrive(fb);
                         }
@@ -539,6 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                 }
             }
         } else if (warp < 4) {
+          if constexpr (NV == 1) {
             // -------------------------- producers, checkpoint layout: 128 threads, cp.async
             const int tid = threadIdx.x;
             const int g_round = g_prod;          // stages of this round are published here
@@ -602,15 +665,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                 publish(gstage0 + (size_t)(h % kStages) * kStageBytes, tid);
                 mbar_arrive(b_full + 8 * (h % kStages));
             }
+          }
         } else if (warp == 4) {
             // ----------------------------------------------------------- MMA issuer
             if (lane == 0 && !stop &&
-                !mma_items(J, nr, g_mma, n_mma, tmem, stage0, b_full, b_empty, b_accf, b_acce, abort))
+                !mma_items<NV>(J, nr, g_mma, n_mma, tmem, stage0, b_full, b_empty, b_accf, b_acce, abort))
                 stop = true;
             __syncwarp();
         } else {
             // ------------------------------------------------------------- epilogue
-            epilogue_items(J, items, nr, n_epi, tmem, b_accf, b_acce, abort, warp & 3, lane);
+            epilogue_items<NV>(J, items, nr, n_epi, tmem, b_accf, b_acce, abort, warp & 3, lane);
         }
         __syncthreads();          // every role is done with this round's table
     }
@@ -623,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     if (warp == 4) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-                     :: "r"(tmem), "r"(kTmemCols) : "memory");
+                     :: "r"(tmem), "r"(G::kTmem) : "memory");
     }
 }
 
@@ -652,18 +716,26 @@ __device__ __forceinline__ uint32_t e2m1_code(float v)
     return r & 0xFu;          // both halves hold v's code
 }
 
-__device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, int blk, int lane)
+// NV vectors per B operand (the grouped layout, NV = 4): slot v's piece p is B row
+// m = 16 v + p, at row m of each K block's (16 NV) x 128-byte SWIZZLE_128B image, and its
+// scale at byte 16 (m % 32) + 4 (m / 32) + (block % 4) of the block's atom.
+template <int NV>
+__device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, int blk, int v, int lane)
 {
     const int c = blk >> 4, j = blk & 15;
-    uint8_t *tile = bq + (size_t)c * kTileB + (j >> 3) * 2048;
+    uint8_t *tile = bq + (size_t)c * (NV * kTileB) + (j >> 3) * (NV * 2048) + v * 2048;
     uint8_t *atom = bs + (size_t)c * kTileSF + (j >> 2) * 512;
-    if ((j & 3) == 0) {
+    if ((j & 3) == 0 && v == 0) {
         // the zero bytes of this atom (its data bytes are written below by 4 blocks)
-        if (lane < 16) {
-            uint32_t *z = reinterpret_cast<uint32_t *>(atom + 16 * lane + 4);
-            z[0] = 0u; z[1] = 0u; z[2] = 0u;
+        if (NV == 1) {
+            if (lane < 16) {
+                uint32_t *z = reinterpret_cast<uint32_t *>(atom + 16 * lane + 4);
+                z[0] = 0u; z[1] = 0u; z[2] = 0u;
+            } else {
+                *reinterpret_cast<uint4 *>(atom + 256 + 16 * (lane - 16)) = make_uint4(0, 0, 0, 0);
+            }
         } else {
-            *reinterpret_cast<uint4 *>(atom + 256 + 16 * (lane - 16)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint2 *>(atom + 16 * lane + 8) = make_uint2(0u, 0u);   // words 2, 3
         }
     }
     int my_code = 255;                       // lane p < 16 keeps piece p's scale code
@@ -691,7 +763,7 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
                     (uint8_t)(nib | (hi << 4));
         }
     }
-    if (lane < kN) atom[16 * lane + (j & 3)] = (uint8_t)my_code;
+    if (lane < kN) atom[16 * (16 * (v & 1) + lane) + 4 * (v >> 1) + (j & 3)] = (uint8_t)my_code;
 }
 
 // B operands of fp32 vectors: grid (ceil(K/32 / 8), nvec), 256 threads, a warp per block.
@@ -705,7 +777,7 @@ __global__ void k_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, size_t
     const int v = blockIdx.y;
     const int nch = K / kStageK;
     const float r = x[(size_t)v * ld + blk * 32 + lane];
-    split_block(bq + (size_t)v * nch * kTileB, bs + (size_t)v * nch * kTileSF, r, blk, lane);
+    split_block<1>(bq + (size_t)v * nch * kTileB, bs + (size_t)v * nch * kTileSF, r, blk, 0, lane);
 }
 
 // silu(gate) * up of one element, gate and up summed over the K slices in slice order from
@@ -752,7 +824,100 @@ __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int
     const float act = act_value(part + (size_t)p * 2 * inter + blk * 32 + lane, ks, slice_stride, inter);
     if (p >= n) return;
     const int nch = inter / kStageK;
-    split_block(bq + (size_t)p * nch * kTileB, bs + (size_t)p * nch * kTileSF, act, blk, lane);
+    split_block<1>(bq + (size_t)p * nch * kTileB, bs + (size_t)p * nch * kTileSF, act, blk, 0, lane);
+}
+
+// ------------------------------------------------------------- grouped items (T > 8)
+// Groups of up to four consecutive grouped positions of one expert: g_p0, g_n, g_e per
+// group (experts in grouping order), ng[0] their count; pos_of[a] = the position of
+// assignment a (the grouped passes write partials by position). One CTA, 1024 threads.
+__global__ void __launch_bounds__(1024) k_make_groups(const int *n_active, const int *act_expert,
+                                                      const int *act_off, const int *assign, int *ng,
+                                                      int *g_p0, int *g_n, int *g_e, int *pos_of)
+{
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int wsum[32];
+    const int nu = __ldcg(n_active), npos = __ldcg(n_active + 1);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int per = (nu + 1023) / 1024;
+    const int u0 = min(nu, (int)threadIdx.x * per), u1 = min(nu, u0 + per);
+    int local = 0;
+    for (int u = u0; u < u1; u++) local += (__ldcg(act_off + u + 1) - __ldcg(act_off + u) + 3) >> 2;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = wsum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += t;
+        }
+        wsum[lane] = w;
+    }
+    __syncthreads();
+    int g = incl - local + (warp > 0 ? wsum[warp - 1] : 0);
+    for (int u = u0; u < u1; u++) {
+        const int base = __ldcg(act_off + u), cnt = __ldcg(act_off + u + 1) - base, e = __ldcg(act_expert + u);
+        for (int i = 0; i < cnt; i += 4, g++) {
+            g_p0[g] = base + i;
+            g_n[g] = min(4, cnt - i);
+            g_e[g] = e;
+        }
+    }
+    if (threadIdx.x == 1023) ng[0] = g;
+    for (int p = threadIdx.x; p < npos; p += 1024) pos_of[__ldcg(assign + p)] = p;
+}
+
+// B operand of the grouped gate/up pass: slot v of group g holds the token of position
+// g_p0[g] + v (assignment a = assign[p], token a / K); empty slots split 0 (zero codes and
+// scales). grid (ceil(hidden / 32 / 8), groups at most), 256 threads, a warp per block.
+__global__ void k_bsplit_group_x(uint8_t *bq, uint8_t *bs, const float *x, int hidden, const int *assign,
+                                 int K, const int *ng, const int *g_p0, const int *g_n)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = blockIdx.y, blk = blockIdx.x * 8 + warp;
+    if (g >= __ldcg(ng) || blk >= hidden / 32) return;
+    const int p0 = __ldcg(g_p0 + g), n = __ldcg(g_n + g);
+    int tok[4];
+#pragma unroll
+    for (int v = 0; v < 4; v++) tok[v] = v < n ? __ldcg(assign + p0 + v) / K : 0;
+    float r[4];
+#pragma unroll
+    for (int v = 0; v < 4; v++) r[v] = v < n ? __ldcg(x + (size_t)tok[v] * hidden + blk * 32 + lane) : 0.0f;
+    const int nch = hidden / kStageK;
+#pragma unroll
+    for (int v = 0; v < 4; v++)
+        split_block<4>(bq + (size_t)g * nch * (4 * kTileB), bs + (size_t)g * nch * kTileSF, r[v], blk, v, lane);
+}
+
+// B operand of the grouped down pass: silu(gate) * up of positions g_p0[g] + v, as
+// k_bsplit_swiglu computes it; empty slots split 0.
+__global__ void k_bsplit_swiglu_group(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride,
+                                      int inter, const int *ng, const int *g_p0, const int *g_n)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = blockIdx.y, blk = blockIdx.x * 8 + warp;
+    if (g >= __ldcg(ng) || blk >= inter / 32) return;
+    const int p0 = __ldcg(g_p0 + g), n = __ldcg(g_n + g);
+    const int nch = inter / kStageK;
+#pragma unroll
+    for (int v = 0; v < 4; v++) {
+        const float act = v < n ? act_value(part + (size_t)(p0 + v) * 2 * inter + blk * 32 + lane, ks,
+                                            slice_stride, inter)
+                                : 0.0f;
+        split_block<4>(bq + (size_t)g * nch * (4 * kTileB), bs + (size_t)g * nch * kTileSF, act, blk, v, lane);
+    }
 }
 
 // ------------------------------------------------------------- weight tiling
@@ -913,7 +1078,25 @@ static int make_job(Job &J, int mode, int tiled, const MoeWork &w, const int *id
     J.part = part;
     J.out_w = out_w;
     J.slice_stride = slice_stride;
+    J.g_p0 = J.g_n = J.g_e = nullptr;
     return K3D_OK;
+}
+
+template <int NV>
+static int launch_job(const Job &J, long long items, cudaStream_t st)
+{
+    static bool init = false;
+    if (!init) {
+        cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)Geo<NV>::kSmem);
+        if (e != cudaSuccess) return fail(K3D_ECUDA, "umma smem attribute: %s", cudaGetErrorString(e));
+        init = true;
+    }
+    if (items <= 0) return K3D_OK;
+    const int grid = (int)(items < sm_count() ? items : sm_count());
+    launch_pdl(k_mxfp4_umma<NV>, dim3(grid), dim3(kThreads), Geo<NV>::kSmem, st, J);
+    note_launch();
+    return check_launch("mxfp4 umma");
 }
 
 int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
@@ -924,19 +1107,53 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     Job J;
     K3_TRY(make_job(J, mode, tiled, w, idx, count, npos_max, K, rows, ks, bq, bs, vec_div, part, out_w,
                     slice_stride, early));
-    static bool init = false;
-    if (!init) {
-        cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kSmemTotal);
-        if (e != cudaSuccess) return fail(K3D_ECUDA, "umma smem attribute: %s", cudaGetErrorString(e));
-        init = true;
-    }
-    const long long items = (long long)npos_max * J.ntiles * ks;
-    if (items <= 0) return K3D_OK;
-    const int grid = (int)(items < sm_count() ? items : sm_count());
-    launch_pdl(k_mxfp4_umma, dim3(grid), dim3(kThreads), kSmemTotal, st, J);
+    return launch_job<1>(J, (long long)npos_max * J.ntiles * ks, st);
+}
+
+// The grouped pass: items over the groups of G (ng = their device count, at most
+// max_groups), four vectors per item, partials by position; tiled experts only.
+int umma_launch_grouped(int mode, const MoeWork &w, const UmmaGroups &G, int max_groups, int K, int rows,
+                        int ks, const uint8_t *bq, const uint8_t *bs, float *part, int out_w,
+                        size_t slice_stride, cudaStream_t st)
+{
+    Job J;
+    K3_TRY(make_job(J, mode, 1, w, nullptr, G.ng, max_groups, K, rows, ks, bq, bs, 1, part, out_w,
+                    slice_stride, 0));
+    J.out_pos = 1;
+    J.g_p0 = G.p0;
+    J.g_n = G.n;
+    J.g_e = G.e;
+    return launch_job<4>(J, (long long)max_groups * J.ntiles * ks, st);
+}
+
+size_t umma_bq_group_bytes(int K) { return (size_t)(K / kStageK) * 4 * kTileB; }
+
+int umma_make_groups(const MoeWork &w, const UmmaGroups &G, cudaStream_t st)
+{
+    launch_pdl(k_make_groups, dim3(1), dim3(1024), 0, st, (const int *)w.n_active, (const int *)w.act_expert,
+               (const int *)w.act_off, (const int *)w.assign, G.ng, G.p0, G.n, G.e, G.pos_of);
     note_launch();
-    return check_launch("mxfp4 umma");
+    return check_launch("umma groups");
+}
+
+int umma_bsplit_group_x(uint8_t *bq, uint8_t *bs, const float *x, int hidden, const int *assign, int K,
+                        const UmmaGroups &G, int max_groups, cudaStream_t st)
+{
+    dim3 grid((hidden / 32 + 7) / 8, max_groups);
+    launch_pdl(k_bsplit_group_x, dim3(grid), dim3(256), 0, st, bq, bs, x, hidden, assign, K, (const int *)G.ng,
+               (const int *)G.p0, (const int *)G.n);
+    note_launch();
+    return check_launch("umma bsplit group");
+}
+
+int umma_bsplit_swiglu_group(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride, int inter,
+                             const UmmaGroups &G, int max_groups, cudaStream_t st)
+{
+    dim3 grid((inter / 32 + 7) / 8, max_groups);
+    launch_pdl(k_bsplit_swiglu_group, dim3(grid), dim3(256), 0, st, bq, bs, part, ks, slice_stride, inter,
+               (const int *)G.ng, (const int *)G.p0, (const int *)G.n);
+    note_launch();
+    return check_launch("umma bsplit swiglu group");
 }
 
 }  // namespace k3

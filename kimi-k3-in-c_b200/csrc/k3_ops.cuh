@@ -66,6 +66,22 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
                 int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
                 int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
                 int early);
+// Grouped items (a batch: several tokens per expert): groups of up to four consecutive
+// grouped positions of one expert share each weight stage (tiled experts).
+struct UmmaGroups {
+    int *ng;                 // [1] number of groups
+    int *p0, *n, *e;         // per group: first position, positions (<= 4), expert
+    int *pos_of;             // per assignment: its grouped position
+};
+size_t umma_bq_group_bytes(int K);
+int umma_make_groups(const MoeWork &w, const UmmaGroups &G, cudaStream_t st);
+int umma_bsplit_group_x(uint8_t *bq, uint8_t *bs, const float *x, int hidden, const int *assign, int K,
+                        const UmmaGroups &G, int max_groups, cudaStream_t st);
+int umma_bsplit_swiglu_group(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride, int inter,
+                             const UmmaGroups &G, int max_groups, cudaStream_t st);
+int umma_launch_grouped(int mode, const MoeWork &w, const UmmaGroups &G, int max_groups, int K, int rows,
+                        int ks, const uint8_t *bq, const uint8_t *bs, float *part, int out_w,
+                        size_t slice_stride, cudaStream_t st);
 
 // k3_gemm_tc.cu: Y[j][T][rows[j]] (+)= x[T][in] . W[j]^T on the tensor cores (more than four
 // tokens); swiglu: two matrices (gate, up), Y[0] = silu(gate) * up

@@ -142,3 +142,41 @@ def test_moe_layer_tiled_experts(k3, oracle, T):
                                      *sh)
     assert np.array_equal(idx, oi)
     assert max_rel_err(y, want) <= 1e-4
+
+
+@pytest.mark.parametrize("T,E", [(9, 16), (16, 16), (64, 16), (33, 64)])
+def test_grouped_pass_matches_one_token_items_and_oracle(k3, oracle, T, E):
+    """Batches (more than 64 assignments, tiled experts): up to four tokens routed to one
+    expert share each weight stage (B = their stacked pieces, N = 64, partials by position,
+    the combine maps assignments to positions). Against one token per item (kind 3) and the
+    oracle; E = 64 leaves single-token experts and groups of every size."""
+    g, experts, W, bias, sh = small_layer(1100 + T, E=E)
+    hidden, inter = 1024, 512
+    mw = k3cuda.MoeWeights(hidden, inter, E, 8, W, bias, shared=sh, experts=experts, tiled=True)
+    x = synth.bf16_to_f32(synth.bf16_normal(g, (T, hidden), 1.0))
+    ys = {}
+    try:
+        for kind in (0, 3, 0):
+            k3cuda.check(k3.k3d_set_expert_kernel(kind))
+            y, idx, _ = run_layer(k3, mw, x, T)
+            ys.setdefault(kind, []).append(y)
+    finally:
+        k3cuda.check(k3.k3d_set_expert_kernel(0))
+    assert np.array_equal(ys[0][0], ys[0][1])
+    assert max_rel_err(ys[0][0], ys[3][0]) <= 1e-5
+    want, oi, _ = oracle.moe_swiglu(x, T, hidden, inter, E, 8, 1, 2.5, W, bias, experts, 256, *sh)
+    assert np.array_equal(idx, oi)
+    assert max_rel_err(ys[0][0], want) <= 1e-4
+
+
+def test_grouped_pass_config1_shapes(k3, oracle):
+    """The grouped pass at config 1's expert shapes (7168 -> 2048) for 16 tokens over 16
+    tiled experts (many tokens per expert), against the oracle."""
+    hidden, inter, E, T = 7168, 2048, 16, 16
+    g, experts, W, bias, sh = small_layer(1211, hidden=hidden, inter=inter, E=E, shared_inter=256)
+    mw = k3cuda.MoeWeights(hidden, inter, E, 8, W, bias, shared=sh, experts=experts, tiled=True)
+    x = synth.bf16_to_f32(synth.bf16_normal(g, (T, hidden), 1.0))
+    y, idx, _ = run_layer(k3, mw, x, T)
+    want, oi, _ = oracle.moe_swiglu(x, T, hidden, inter, E, 8, 1, 2.5, W, bias, experts, 256, *sh)
+    assert np.array_equal(idx, oi)
+    assert max_rel_err(y, want) <= 1e-4
