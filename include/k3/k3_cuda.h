@@ -108,6 +108,9 @@ int    k3d_sm_count(void);
  * element i depends only on (seed, i). Normal values are an Irwin-Hall sum of four
  * 16-bit uniforms scaled to the requested standard deviation. */
 int k3d_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float stddev);
+/* Elements [offset, offset + n) of the sequence k3d_fill_bf16_normal writes for `seed`
+ * (a slice of a larger seeded matrix, e.g. one rank's rows). */
+int k3d_fill_bf16_normal_at(uint16_t *dst, size_t n, uint64_t seed, float sd, size_t offset);
 int k3d_fill_f32_normal(float *dst, size_t n, uint64_t seed, float stddev);
 int k3d_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi);
 /* E2M1 codes uniform over all 16 values; E8M0 bytes uniform in [s_lo, s_hi]. */
@@ -308,6 +311,15 @@ int k3d_lm_head_argmax(int *next, float *logits, const float *x, const uint16_t 
 int k3d_lm_head_argmax_normed(int *next, float *logits, const float *x, const float *norm_w,
                               float eps, const uint16_t *W, int vocab, int hidden, int B,
                               void *key_ws);
+/* The LM head over one slice of the vocabulary (rows [v0, v0 + vocab_shard) in W_shard),
+ * for expert-parallel decode where each rank holds a slice: the ranks' packed (logit,
+ * index) maxima are combined with an all-reduce max over NCCL (k3d_ep_init; on one rank
+ * none is needed), so next[B] is the argmax over the whole vocabulary, first maximum on
+ * ties, as k3d_lm_head_argmax_normed gives it. logits (optional) receives this slice's
+ * [B][vocab_shard] logits. No reference counterpart (the CPU engine is single-process). */
+int k3d_lm_head_argmax_shard_normed(int *next, float *logits, const float *x, const float *norm_w,
+                                    float eps, const uint16_t *W_shard, int v0, int vocab_shard,
+                                    int hidden, int B, void *key_ws);
 /* y[i] += x[i] for i < n (device floats) */
 int k3d_add_f32(float *y, const float *x, size_t n);
 /* p[i] += delta for i < n (device ints; advances cache positions inside a graph) */
@@ -379,7 +391,9 @@ void      k3d_model_destroy(K3dModel *m);
  * seeded synthetic values (latent ~N(0,1), state ~N(0,0.01), conv history ~N(0,1)). */
 int       k3d_model_fill_context(K3dModel *m, int len, uint64_t seed);
 /* One decode step for the batch: ids (device [B]) in, next ids (device [B], argmax of
- * the logits) out, logits (device [B][vocab]) optional. Captures into a graph. */
+ * the logits) out, logits (device [B][vocab]) optional. Captures into a graph. Under EP
+ * (k3d_ep_init with more than one rank) each rank holds a slice of the LM head and logits
+ * receives that slice, [B][rows of the slice]; next is the argmax over all of them. */
 int       k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits);
 /* The same through host buffers: copies ids in, runs the step, copies next ids out. */
 int       k3d_model_step_host(K3dModel *m, const int *ids_host, int *next_host);

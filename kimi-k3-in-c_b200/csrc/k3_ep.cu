@@ -43,6 +43,15 @@ int ep_exchange(const void *send, const size_t *scnt, const size_t *soff, void *
     return K3D_OK;
 }
 
+int ep_allreduce_max_u64(unsigned long long *buf, size_t n, cudaStream_t st)
+{
+    if (g_size == 1) return K3D_OK;
+    if (!g_comm) return fail(K3D_ENCCL, "ep max before k3d_ep_init");
+    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclUint64, ncclMax, g_comm, st);
+    if (r != ncclSuccess) return fail(K3D_ENCCL, "ncclAllReduce max: %s", ncclGetErrorString(r));
+    return K3D_OK;
+}
+
 }  // namespace k3
 
 using namespace k3;

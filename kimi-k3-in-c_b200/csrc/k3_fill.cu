@@ -28,11 +28,11 @@ __device__ __forceinline__ float normal_at(uint64_t seed, uint64_t i, float stdd
     return (float)s * (stddev / 37837.23f);
 }
 
-__global__ void k_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float sd)
+__global__ void k_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float sd, size_t offset)
 {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
-        dst[i] = f32_to_bf16_bits(normal_at(seed, i, sd));
+        dst[i] = f32_to_bf16_bits(normal_at(seed, offset + i, sd));
 }
 
 __global__ void k_fill_f32_normal(float *dst, size_t n, uint64_t seed, float sd)
@@ -102,9 +102,19 @@ int k3d_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float sd)
     K3_TRY(ensure_ctx());
     if (!dst) return fail(K3D_EINVAL, "fill null pointer");
     if (!n) return K3D_OK;
-    k_fill_bf16_normal<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, sd);
+    k_fill_bf16_normal<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, sd, 0);
     note_launch();
     return check_launch("fill bf16");
+}
+
+int k3d_fill_bf16_normal_at(uint16_t *dst, size_t n, uint64_t seed, float sd, size_t offset)
+{
+    K3_TRY(ensure_ctx());
+    if (!dst) return fail(K3D_EINVAL, "fill null pointer");
+    if (!n) return K3D_OK;
+    k_fill_bf16_normal<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, sd, offset);
+    note_launch();
+    return check_launch("fill bf16 at");
 }
 
 int k3d_fill_f32_normal(float *dst, size_t n, uint64_t seed, float sd)

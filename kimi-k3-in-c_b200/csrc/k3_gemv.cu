@@ -269,7 +269,7 @@ __global__ void k_argmax_finish(int *next, const unsigned long long *key, int T)
 {
     pdl_wait();
     pdl_trigger();
-    const int t = threadIdx.x;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t < T) next[t] = (int)(0xffffffffu - (uint32_t)(key[t] & 0xffffffffu));
 }
 
@@ -282,9 +282,9 @@ static bool use_gemm_tc(int in, int T, const float *x, cudaStream_t s)
     return T > 4 && in % 64 == 0 && al16(x) && (s == stream() || s == side_stream());
 }
 
-// next[t] = the first maximum of logits row t (lowest index among equal values; NaN never
-// wins), by the packing of argmax_pack. grid T, 1024 threads.
-__global__ void k_rows_argmax(int *next, const float *y, int out)
+// key[t] = the packed first maximum of logits row t (lowest index among equal values; NaN
+// never wins), as argmax_pack makes it. grid T, 1024 threads.
+__global__ void k_rows_argmax(unsigned long long *key, const float *y, int out)
 {
     pdl_wait();
     pdl_trigger();
@@ -310,8 +310,18 @@ __global__ void k_rows_argmax(int *next, const float *y, int out)
             const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
             best = v > best ? v : best;
         }
-        if (threadIdx.x == 0) next[t] = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
+        if (threadIdx.x == 0) key[t] = best;
     }
+}
+
+// Keys of rows [v0, v0 + n) of a larger vocabulary: local row r becomes global row v0 + r
+// (the low word holds 0xffffffff - row); an empty key (no finite logit) stays empty.
+__global__ void k_key_offset(unsigned long long *key, int T, int v0)
+{
+    const int t = threadIdx.x;
+    if (t >= T || !key[t]) return;
+    const uint32_t lo = (uint32_t)(key[t] & 0xffffffffu) - (uint32_t)v0;
+    key[t] = (key[t] & 0xffffffff00000000ull) | lo;
 }
 
 // The streamed GEMVs (k3_gemv_stream.cu) where the shape allows, on the library stream
@@ -445,8 +455,10 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
     return check_launch("gemv bf16 multi");
 }
 
-int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
-                     const uint16_t *W, int in, int out, int T, cudaStream_t s, const NormIn *ni)
+// The LM head's argmax keys: key[t] = argmax_pack of the first maximum of logits row t
+// (local rows 0..out-1); y receives the logits when non-null.
+int lm_head_keys(float *y, unsigned long long *key, const float *x, const uint16_t *W, int in, int out, int T,
+                 cudaStream_t s, const NormIn *ni)
 {
     if (T < 1 || (in % 8) != 0 || !al16(W))
         return fail(K3D_EINVAL, "lm head: T=%d in=%d", T, in);
@@ -462,7 +474,7 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
             if (!y) return k3d_status();
         }
         K3_TRY(gemm_bf16_tc(1, &W, &y, &out, x, in, T, 0, 0, s));
-        launch_pdl(k_rows_argmax, dim3(T), dim3(1024), 0, s, next, (const float *)y, out);
+        launch_pdl(k_rows_argmax, dim3(T), dim3(1024), 0, s, key, (const float *)y, out);
         note_launch();
         return check_launch("lm head rows argmax");
     }
@@ -470,19 +482,37 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
     if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
                ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
-    if (g_gemv_stream && s == stream() && gemv_stream_argmax(y, key, x, W, in, out, T, s, ni)) {
-        launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);
-        note_launch();
+    if (g_gemv_stream && s == stream() && gemv_stream_argmax(y, key, x, W, in, out, T, s, ni))
         return check_launch("lm head argmax stream");
-    }
     if (ni) {
         x = norm_to_scratch(x, *ni, in, T, s);
         if (!x) return k3d_status();
     }
     launch_pdl(k_gemv_bf16_argmax<2, 7>, dim3(grid_for(out, 16)), dim3(256), (size_t)T * in * 4, s, y, key, x, W, in, out, T);
-    launch_pdl(k_argmax_finish, dim3(1), dim3(32), 0, s, next, key, T);
-    note_launch(2);
+    note_launch();
     return check_launch("lm head argmax");
+}
+
+int argmax_finish(int *next, const unsigned long long *key, int T, cudaStream_t s)
+{
+    launch_pdl(k_argmax_finish, dim3((T + 255) / 256), dim3(256), 0, s, next, key, T);
+    note_launch();
+    return check_launch("argmax finish");
+}
+
+int key_offset(unsigned long long *key, int T, int v0, cudaStream_t s)
+{
+    if (T > 1024) return fail(K3D_EINVAL, "key offset: T=%d", T);
+    k_key_offset<<<1, 1024, 0, s>>>(key, T, v0);
+    note_launch();
+    return check_launch("argmax key offset");
+}
+
+int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *x,
+                     const uint16_t *W, int in, int out, int T, cudaStream_t s, const NormIn *ni)
+{
+    K3_TRY(lm_head_keys(y, key, x, W, in, out, T, s, ni));
+    return argmax_finish(next, key, T, s);
 }
 
 int gemv_tagged(float *y, const float *x, const void *W, int wdt, int in, int out, cudaStream_t s)

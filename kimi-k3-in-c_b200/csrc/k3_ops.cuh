@@ -88,6 +88,14 @@ int umma_launch_grouped(int mode, const MoeWork &w, const UmmaGroups &G, int max
 int gemm_bf16_tc(int nmat, const uint16_t *const *W, float *const *Y, const int *rows, const float *x,
                  int in, int T, int accumulate, int swiglu, cudaStream_t st);
 
+// k3_gemv.cu: the LM head in pieces (keys of a vocabulary slice, global index shift, finish)
+int lm_head_keys(float *y, unsigned long long *key, const float *x, const uint16_t *W, int in, int out, int T,
+                 cudaStream_t s, const NormIn *ni);
+int key_offset(unsigned long long *key, int T, int v0, cudaStream_t s);
+int argmax_finish(int *next, const unsigned long long *key, int T, cudaStream_t s);
+// k3_ep.cu: element-wise max of n uint64 over the ranks, in place (no-op on one rank)
+int ep_allreduce_max_u64(unsigned long long *buf, size_t n, cudaStream_t s);
+
 // k3_ep.cu: grouped byte exchange with every rank (a device copy on one rank)
 int ep_exchange(const void *send, const size_t *scnt, const size_t *soff, void *recv,
                 const size_t *rcnt, const size_t *roff, cudaStream_t st);

@@ -90,6 +90,25 @@ int k3d_lm_head_argmax_normed(int *next, float *logits, const float *x, const fl
     return r;
 }
 
+int k3d_lm_head_argmax_shard_normed(int *next, float *logits, const float *x, const float *norm_w,
+                                    float eps, const uint16_t *W_shard, int v0, int vocab_shard,
+                                    int hidden, int B, void *key_ws)
+{
+    K3_TRY(ensure_ctx());
+    if (!next || !x || !norm_w || !W_shard || !key_ws || v0 < 0 || vocab_shard < 1 || B < 1)
+        return fail(K3D_EINVAL, "k3d_lm_head_argmax_shard_normed");
+    const NormIn ni{norm_w, eps};
+    unsigned long long *key = (unsigned long long *)key_ws;
+    cudaStream_t st = stream();
+    prof_begin("lm_head");
+    K3_TRY(lm_head_keys(logits, key, x, W_shard, hidden, vocab_shard, B, st, &ni));
+    if (v0) K3_TRY(key_offset(key, B, v0, st));
+    K3_TRY(ep_allreduce_max_u64(key, (size_t)B, st));
+    const int r = argmax_finish(next, key, B, st);
+    prof_end("lm_head");
+    return r;
+}
+
 int k3d_add_f32(float *y, const float *x, size_t n)
 {
     K3_TRY(ensure_ctx());

@@ -50,7 +50,8 @@ typedef struct {
 struct K3dModel {
     K3dStackCfg c;
     K3sLayer L[K3S_MAX_LAYERS];
-    uint16_t *embed, *lm_head;
+    uint16_t *embed, *lm_head;     /* lm_head: rows [v0, v0 + vshard) of the vocabulary */
+    int v0, vshard;                /* the whole vocabulary on one rank; a slice per rank under EP */
     float *final_norm;
     float *h, *xn, *mo;            /* [B][hidden] */
     float *logits;                 /* [B][vocab] */
@@ -142,7 +143,18 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
     size_t ws = 0;
 
     m->embed = bf16_param(m, "embed", (size_t)c->vocab * E, 0.02f, &err);
-    m->lm_head = bf16_param(m, "lm_head", (size_t)c->vocab * E, 0.02f, &err);
+    {
+        /* under EP each rank holds one slice of the LM head: the same rows of the same
+         * seeded matrix a single GPU holds, so the argmax over the slices is the same */
+        const int nr = k3d_ep_size(), r = k3d_ep_rank();
+        m->v0 = (int)((long long)r * c->vocab / nr);
+        m->vshard = (int)((long long)(r + 1) * c->vocab / nr) - m->v0;
+        const uint64_t sd = next_seed(m);
+        m->lm_head = (uint16_t *)dalloc(m, "lm_head", (size_t)m->vshard * E * 2);
+        if (!m->lm_head || k3d_fill_bf16_normal_at(m->lm_head, (size_t)m->vshard * E, sd, 0.02f,
+                                                   (size_t)m->v0 * E))
+            err = 1;
+    }
     m->final_norm = f32_uniform(m, "final_norm", E, 0.9f, 1.1f, &err);
 
     for (int l = 0; l < c->n_layers && !err; l++) {
@@ -378,8 +390,12 @@ static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
             TRY(k3d_moe_swiglu(m->h, m->xn, &L->moe, &c->moe, B, 1, NULL, NULL, m->ws, m->ws_bytes));
         }
     }
-    TRY(k3d_lm_head_argmax_normed(next, logits, m->h, m->final_norm, c->eps, m->lm_head, c->vocab,
-                                  E, B, m->key));
+    if (m->vshard == c->vocab)
+        TRY(k3d_lm_head_argmax_normed(next, logits, m->h, m->final_norm, c->eps, m->lm_head, c->vocab,
+                                      E, B, m->key));
+    else
+        TRY(k3d_lm_head_argmax_shard_normed(next, logits, m->h, m->final_norm, c->eps, m->lm_head, m->v0,
+                                            m->vshard, E, B, m->key));
     TRY(k3d_add_i32(m->pos, 1, 1));
 #undef TRY
     return K3D_OK;
@@ -449,7 +465,7 @@ double k3d_model_last_step_bytes(K3dModel *m)
     if (!m) return 0.0;
     const K3dStackCfg *c = &m->c;
     const double E = c->hidden, B = c->batch;
-    double bytes = 2.0 * c->vocab * E + 2.0 * B * E * 4;    /* lm_head + embed rows */
+    double bytes = 2.0 * m->vshard * E + 2.0 * B * E * 4;   /* lm_head (this rank's rows) + embed rows */
     int pos = 0;
     k3d_download(&pos, m->pos, sizeof pos);
     const int U = k3d_moe_last_unique();

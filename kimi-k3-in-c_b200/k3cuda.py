@@ -179,6 +179,7 @@ _PROTOS = {
     "k3d_sm_count": (i32, []),
     # fills
     "k3d_fill_bf16_normal": (i32, [vp, sz, u64, f32]),
+    "k3d_fill_bf16_normal_at": (i32, [vp, sz, u64, f32, sz]),
     "k3d_fill_f32_normal": (i32, [vp, sz, u64, f32]),
     "k3d_fill_f32_uniform": (i32, [vp, sz, u64, f32, f32]),
     "k3d_fill_mxfp4": (i32, [vp, sz, vp, sz, u64, i32, i32]),
@@ -209,6 +210,7 @@ _PROTOS = {
     "k3d_swiglu_mlp_bf16": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "k3d_lm_head_argmax": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
     "k3d_lm_head_argmax_normed": (i32, [vp, vp, vp, vp, f32, vp, i32, i32, i32, vp]),
+    "k3d_lm_head_argmax_shard_normed": (i32, [vp, vp, vp, vp, f32, vp, i32, i32, i32, i32, vp]),
     "k3d_add_f32": (i32, [vp, vp, sz]),
     "k3d_add_i32": (i32, [vp, i32, i32]),
     "k3d_kda_layer_ws_bytes": (sz, [C.POINTER(K3dKdaShape), i32]),

@@ -79,3 +79,25 @@ def test_moe_a2a_two_gpus_matches_oracle(tiled):
         if p.exitcode is None:
             p.kill()
     assert codes == [0, 0], codes
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+def test_lm_head_vocab_split_two_gpus():
+    """Each rank holds half of the LM head's rows; the packed (logit, index) maxima are
+    combined by an NCCL max, so every rank gets the argmax over the whole vocabulary (the
+    streamed GEMV path at batch 3, the tensor-core GEMM path at batch 6)."""
+    import ep_lm_gpu_worker
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=ep_lm_gpu_worker.run, args=(r, 2, port, 41)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert codes == [0, 0], codes
