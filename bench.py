@@ -275,19 +275,20 @@ def bench_moe(args, rank, world):
     mw = k3cuda.MoeWeights(HIDDEN, INTER, n_exp, TOPK, W, bias, shared=sh, seed=7, lo=lo, hi=hi,
                            add_shared=1 if rank == 0 else 0, tiled=args.expert_kernel in (0, 3),
                            lib=lib)
-    P = 64
-    xs = synth.bf16_to_f32(synth.bf16_normal(g, (P, HIDDEN), 1.0))
+    T = max(1, args.tokens)
+    P = 64 if T == 1 else 8
+    xs = synth.bf16_to_f32(synth.bf16_normal(g, (P * T, HIDDEN), 1.0))
     X = k3cuda.DevBuf.from_array(xs, lib)
-    Y = k3cuda.DevBuf(HIDDEN * 4, lib)
-    nws = mw.ws_bytes(1)
+    Y = k3cuda.DevBuf(T * HIDDEN * 4, lib)
+    nws = mw.ws_bytes(T)
     WS = k3cuda.DevBuf(nws, lib)
     FL = k3cuda.DevBuf(256 << 20, lib)
     ev = [lib.k3d_event_create() for _ in range(2)]
 
     def step(i):
-        k3cuda.check(mw.run(Y.ptr, X.ptr + (i % P) * HIDDEN * 4, 1, WS.ptr, nws), "moe step")
+        k3cuda.check(mw.run(Y.ptr, X.ptr + (i % P) * T * HIDDEN * 4, T, WS.ptr, nws), "moe step")
         if world > 1:
-            k3cuda.check(lib.k3d_ep_allreduce_f32(Y.ptr, HIDDEN), "ep combine")
+            k3cuda.check(lib.k3d_ep_allreduce_f32(Y.ptr, T * HIDDEN), "ep combine")
 
     for i in range(args.warmup):
         step(i)
@@ -329,32 +330,32 @@ def bench_moe(args, rank, world):
     tot_ms = reduce_max(tot_ms)
     exp_ms_avg = exp_ms / max(1, n_prof)
     u_avg = float(np.mean(uniq))
-    alg_bytes = u_avg * (EXPERT_BYTES + INTER * 8 + HIDDEN * 4) + HIDDEN * 4
+    alg_bytes = u_avg * EXPERT_BYTES + T * TOPK * (INTER * 8 + HIDDEN * 4) + T * HIDDEN * 4
     hbm, peak_kind = measured_peaks()
     achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
     # end to end through the public API with host buffers
-    hx = lib.k3d_host_alloc(HIDDEN * 4)
-    hy = lib.k3d_host_alloc(HIDDEN * 4)
-    C.memmove(hx, xs[0].ctypes.data, HIDDEN * 4)
+    hx = lib.k3d_host_alloc(T * HIDDEN * 4)
+    hy = lib.k3d_host_alloc(T * HIDDEN * 4)
+    C.memmove(hx, xs[:T].ctypes.data, T * HIDDEN * 4)
     barrier()
     t0 = time.perf_counter()
     for i in range(args.steps):
-        k3cuda.check(lib.k3d_upload(X.ptr, hx, HIDDEN * 4))
-        k3cuda.check(mw.run(Y.ptr, X.ptr, 1, WS.ptr, nws))
+        k3cuda.check(lib.k3d_upload(X.ptr, hx, T * HIDDEN * 4))
+        k3cuda.check(mw.run(Y.ptr, X.ptr, T, WS.ptr, nws))
         if world > 1:
-            k3cuda.check(lib.k3d_ep_allreduce_f32(Y.ptr, HIDDEN))
-        k3cuda.check(lib.k3d_download(hy, Y.ptr, HIDDEN * 4))
+            k3cuda.check(lib.k3d_ep_allreduce_f32(Y.ptr, T * HIDDEN))
+        k3cuda.check(lib.k3d_download(hy, Y.ptr, T * HIDDEN * 4))
     e2e_s = reduce_max(time.perf_counter() - t0)
     lib.k3d_host_free(hx)
     lib.k3d_host_free(hy)
     res = {
-        "metric": METRIC, "value": args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "metric": METRIC, "value": T * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded MXFP4 experts, E8M0 117..121; bf16 ~N(0,0.02) router and "
                 "shared expert; bf16 ~N(0,1) tokens)",
-        "config": {"workload": "config1 MoE layer decode, T=1", "hidden": HIDDEN,
+        "config": {"workload": f"config1 MoE layer decode, T={T}", "hidden": HIDDEN,
                    "n_experts": n_exp, "topk": TOPK, "inter": INTER, "shared_inter": SHARED,
                    "parallelism": f"ep{world}", "l2": "flushed between steps (256 MB write)"},
         "roofline": {"kernel": EXPERT_KERNEL[args.expert_kernel], "bound": "hbm",
@@ -363,8 +364,8 @@ def bench_moe(args, rank, world):
                      "traffic": load_traffic("moe_experts_traffic.json"),
                      "alg_bytes_per_launch": alg_bytes, "unique_experts": u_avg,
                      "kernel_ms": kern_ms, "expert_section_ms": exp_ms_avg},
-        "e2e": {"value": args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
-                "d2h_bytes_per_step": HIDDEN * 4},
+        "e2e": {"value": T * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": T * HIDDEN * 4,
+                "d2h_bytes_per_step": T * HIDDEN * 4},
         "gpu_launches": int(launches),
         "clocks": clk,
     }
@@ -637,6 +638,8 @@ def main():
     ap.add_argument("--workload", default="stack", choices=["stack", "moe", "moe_a2a"],
                     help="moe_a2a: the MoE layer for a --batch split over the ranks (Mode A)")
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--tokens", type=int, default=1,
+                    help="moe workload: tokens per step (config 1 lists T = 1, 8, 64, 512)")
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bounded CPU-baseline sample length; 0 skips it")
