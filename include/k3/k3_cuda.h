@@ -173,8 +173,9 @@ int    k3d_expert_pretile(const K3ExpertQ *dst, const K3ExpertQ *src, int hidden
 /* Which MXFP4 expert kernel k3d_expert_swiglu / k3d_moe_swiglu run: 0 (default) the
  * tcgen05 block-scaled tensor-core kernel whenever the shapes allow it (hidden and inter
  * multiples of 512, T * topk <= 64), 1 the mma.sync kernel, 2 the CUDA-core kernels, 3 the
- * tcgen05 kernel with one token per work item (kind 0 lets up to four tokens routed to the
- * same tiled expert share its weight stages when there are more than 64 assignments).
+ * tcgen05 kernel with the activation operand in every pipeline stage (kind 0, for tiled
+ * experts, keeps it resident across the stages that share it up to 64 assignments, and
+ * lets up to four tokens routed to one expert share its weight stages above 64).
  * Experts in the tiled layout always run on the tcgen05 kernel.
  * All give the same results within the expert tolerance; the switch exists to measure
  * and test each. */

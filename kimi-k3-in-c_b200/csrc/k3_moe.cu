@@ -349,20 +349,25 @@ static int run_experts(const MoeWork &mw, const int *idx, const int *count, int 
         return K3D_OK;
     }
     if (use_umma(B, hidden, inter, TK, layout)) {
-        const int ks_gu = std::min(umma_slices(TK, hidden, inter, 0), umma_ks_cap(hidden, TK));
-        const int ks_d = std::min(umma_slices(TK, inter, hidden, 1), umma_ks_cap(inter, TK));
+        // tiled experts keep B resident across the stages of a run (one K chunk per item);
+        // kind 3 keeps B in every stage
+        const int resident = layout == 1 && g_expert_kernel != 3 && TK <= kUmmaMaxTK;
+        const int ks_gu = resident ? hidden / 512
+                                   : std::min(umma_slices(TK, hidden, inter, 0), umma_ks_cap(hidden, TK));
+        const int ks_d = resident ? inter / 512
+                                  : std::min(umma_slices(TK, inter, hidden, 1), umma_ks_cap(inter, TK));
         const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
         if (!x_split) K3_TRY(umma_bsplit(B.bq_x, B.bs_x, x, hidden, T, hidden, st));
         prof_begin("experts.gateup");
         // the gate/up work list comes from the router just before (MoE); the down pass's
         // does not depend on the split just before it, nor does a single expert's
         K3_TRY(umma_launch(0, layout, mw, idx, count, TK, hidden, inter, ks_gu, B.bq_x, B.bs_x, topk,
-                           B.part_gu, 2 * inter, sl_gu, st, mw.single_mode ? 1 : 0));
+                           B.part_gu, 2 * inter, sl_gu, st, mw.single_mode ? 1 : 0, resident));
         prof_end("experts.gateup");
         K3_TRY(umma_bsplit_swiglu(B.bq_a, B.bs_a, B.part_gu, ks_gu, sl_gu, inter, count, TK, st));
         prof_begin("experts.down");
         K3_TRY(umma_launch(1, layout, mw, idx, count, TK, inter, hidden, ks_d, B.bq_a, B.bs_a, 1,
-                           B.part_d, hidden, sl_d, st, 1));
+                           B.part_d, hidden, sl_d, st, 1, resident));
         prof_end("experts.down");
         O.contrib = B.part_d;
         O.ks = ks_d;

@@ -284,6 +284,7 @@ constexpr int kAccBufs = 4;             // accumulator ring depth
 // byte 16 (m % 32) + 4 (m / 32) + block (the layout of A's 128 rows).
 template <int NV>
 struct Geo {
+    static constexpr int kVec = NV;                             // vectors per item
     static constexpr int kBTile = NV * kTileB;                  // B tile per stage
     static constexpr int kB = kTileA;                           // 32768
     static constexpr int kSFA = kB + kBTile;
@@ -300,14 +301,45 @@ struct Geo {
     static_assert(kAccBufs * kCols + 64 <= kTmem, "tensor memory");
 };
 
+// NV = 0: one vector per item, items ordered (vector, K chunk, tile) with one stage each,
+// so consecutive items share their B chunk: B and its scale atoms are loaded once per run
+// of items into one of two slots beside the ring, and the ring's stages carry only the
+// weight tile and its scales (34 KB): six of them fit instead of five, and B's scales go
+// to tensor memory once per run instead of once per stage.
+template <>
+struct Geo<0> {
+    static constexpr int kVec = 1;
+    static constexpr int kSFA = kTileA;                         // 32768
+    static constexpr int kBytes = kTileA + kTileSF;             // 34816
+    static constexpr int kNStages = 6;
+    static constexpr int kCols = kN;
+    static constexpr int kTmem = kTmemCols;
+    static constexpr uint32_t kSfaCol = umma::kSfaCol, kSfbCol = umma::kSfbCol;   // SFB: 16 columns per slot
+    static constexpr uint32_t kTx = kTileA + kTileSF;
+    static constexpr int kBSlot = kTileB + kTileSF;             // 6144: B tile, then its atoms
+    static constexpr int kBSlots = kStage0 + kNStages * kBytes; // offset of the two slots
+    static constexpr size_t kSmem = 1024 + kBSlots + 2 * kBSlot;
+    static_assert(kBytes % 1024 == 0 && kBSlots % 1024 == 0 && kBSlot % 1024 == 0, "alignment");
+    static_assert(kSmem <= 232448, "shared memory");
+};
+
 template <int NV>
 __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
 {
     ItemEnt it;
     it.s = item % J.ks;
-    const int rest = item / J.ks;
-    it.tile = rest % J.ntiles;
-    const int p = rest / J.ntiles;
+    int rest, p;
+    if (NV == 0) {
+        // (vector, K chunk, tile), tile fastest (one stage per item)
+        it.tile = item % J.ntiles;
+        rest = item / J.ntiles;
+        it.s = rest % J.ks;
+        p = rest / J.ks;
+    } else {
+        rest = item / J.ks;
+        it.tile = rest % J.ntiles;
+        p = rest / J.ntiles;
+    }
     it.nv = 1;
     it.pad[0] = it.pad[1] = it.pad[2] = 0;
     if (NV > 1) {
@@ -431,6 +463,70 @@ __device__ __forceinline__ bool mma_items(const Job &J, int nr, int &g_mma, int 
     return true;
 }
 
+// Runs of items sharing a B chunk (the resident-B geometry): true when item `it` starts a
+// new run after (vec, chunk).
+__device__ __forceinline__ bool new_run(const ItemEnt &it, int vec, int chunk)
+{
+    return it.vec != vec || it.s != chunk;
+}
+
+// MMA issuer of the resident-B geometry: one stage per item; at the start of each run the
+// previous run's B slot is released (a commit: it frees once that run's MMAs finish) and
+// the new slot's scale atoms are copied to tensor memory after its B has landed.
+__device__ __forceinline__ bool mma_items_rb(const Job &J, const ItemEnt *items, int nr, int &g_mma, int &n_mma,
+                                             int &rb_n, int &rb_vec, int &rb_chunk, uint32_t tmem,
+                                             uint32_t stage0, uint32_t bslots, uint32_t b_full,
+                                             uint32_t b_empty, uint32_t b_accf, uint32_t b_acce,
+                                             uint32_t b_bfull, uint32_t b_bempty, volatile int *abort)
+{
+    using G = Geo<0>;
+    for (int k = 0; k < nr; k++, n_mma++) {
+        const ItemEnt &it = items[k];
+        const int buf = n_mma % kAccBufs;
+        if (n_mma >= kAccBufs && !mbar_wait(b_acce + 8 * buf, ((n_mma / kAccBufs) - 1) & 1, abort))
+            return false;
+        tc_fence_after();
+        if (new_run(it, rb_vec, rb_chunk)) {
+            if (rb_n > 0) tc_commit(b_bempty + 8 * ((rb_n - 1) & 1));
+            const int slot = rb_n & 1;
+            if (!mbar_wait(b_bfull + 8 * slot, (rb_n >> 1) & 1, abort)) return false;
+            tc_fence_after();
+            const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)(slot * 16);
+#pragma unroll
+            for (int a4 = 0; a4 < 4; a4++)
+                tc_cp_sf(sfb + 4 * a4, desc_sf(bslots + (uint32_t)(slot * G::kBSlot + kTileB + 512 * a4)));
+            rb_n++;
+            rb_vec = it.vec;
+            rb_chunk = it.s;
+        }
+        const int slot = (rb_n - 1) & 1;
+        const uint32_t bs = bslots + (uint32_t)(slot * G::kBSlot);
+        const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)(slot * 16);
+        const uint32_t dcol = tmem + (uint32_t)(buf * kN);
+        const int st = g_mma % G::kNStages;
+        if (!mbar_wait(b_full + 8 * st, (g_mma / G::kNStages) & 1, abort)) return false;
+        tc_fence_after();
+        const uint32_t sb = stage0 + (uint32_t)st * G::kBytes;
+        const uint32_t sfa = tmem + G::kSfaCol + (uint32_t)((g_mma & 1) * 16);
+#pragma unroll
+        for (int a4 = 0; a4 < 4; a4++) tc_cp_sf(sfa + 4 * a4, desc_sf(sb + G::kSFA + 512 * a4));
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
+            const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
+            const uint64_t bd = desc_sw128(bs + kb * 2048u + off);
+            const uint32_t id = (uint32_t)((j & 1) * 2);
+            const uint32_t atom = (uint32_t)(4 * (j >> 1));
+            tc_mma(dcol, ad, bd, idesc_mxf4<kN>(id), j > 0 ? 1u : 0u, (sfa + atom) | (id << 30),
+                   (sfb + atom) | (id << 30));
+        }
+        tc_commit(b_empty + 8 * st);
+        g_mma++;
+        tc_commit(b_accf + 8 * buf);
+    }
+    return true;
+}
+
 // Epilogue warp of tensor-memory lane quadrant q: for each of `nr` items, its 32 rows of
 // the 128 x 16 accumulator, summed over the 16 pieces and stored as the item's partial.
 // False when a wait gave up.
@@ -452,14 +548,14 @@ __device__ __forceinline__ bool epilogue_items(const Job &J, const ItemEnt *item
         tc_fence_after();
         float v[G::kCols];
 #pragma unroll
-        for (int u = 0; u < NV; u++)
+        for (int u = 0; u < G::kVec; u++)
             tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * G::kCols + u * kN), v + u * kN);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(b_acce + 8 * buf);
         // each vector's 16 pieces, smallest first; vector u is position out + u
 #pragma unroll
-        for (int u = 0; u < NV; u++) {
+        for (int u = 0; u < G::kVec; u++) {
             if (u >= it.nv) break;
             float sum = v[u * kN + 15];
 #pragma unroll
@@ -480,11 +576,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *gbase = smem_raw + (base - raw);
     // header: barriers, abort flag, tensor-memory address slot
-    const uint32_t b_full = base;                       // [kStages] x 8
-    const uint32_t b_empty = base + 8 * kStages;        // [kStages] x 8
-    const uint32_t b_accf = base + 16 * kStages;        // [kAccBufs] x 8
+    const uint32_t b_full = base;                       // [8] x 8 (G::kNStages used)
+    const uint32_t b_empty = base + 64;                 // [8] x 8
+    const uint32_t b_accf = base + 128;                 // [kAccBufs] x 8
     const uint32_t b_acce = b_accf + 8 * kAccBufs;      // [kAccBufs] x 8
     const uint32_t b_drain = b_acce + 8 * kAccBufs;
+    const uint32_t b_bfull = b_drain + 8;               // [2] x 8: resident B slots (NV = 0)
+    const uint32_t b_bempty = b_bfull + 16;             // [2] x 8
+    static_assert(G::kNStages <= 8, "barrier header");
     volatile int *abort = reinterpret_cast<volatile int *>(gbase + 512);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + 520);
     ItemEnt *items = reinterpret_cast<ItemEnt *>(gbase + kOffItems);
@@ -500,6 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
         }
         for (int i = 0; i < kAccBufs; i++) { mbar_init(b_accf + 8 * i, 1); mbar_init(b_acce + 8 * i, 4); }
         mbar_init(b_drain, 1);
+        for (int i = 0; i < 2; i++) { mbar_init(b_bfull + 8 * i, 1); mbar_init(b_bempty + 8 * i, 1); }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -528,6 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     int n_mma = 0;       // items issued by the MMA thread
     int n_epi = 0;       // items finished by this epilogue warp
     bool stop = false;
+    // resident-B runs (NV = 0): runs begun and the current run's (vector, chunk), kept by
+    // the producer and the MMA issuer each
+    int rb_n = 0, rb_vec = -1, rb_chunk = -1;
+    const uint32_t bslots = base + (uint32_t)(NV == 0 ? Geo<0>::kBSlots : 0);
 
     for (int r0 = i_beg; r0 < i_end; r0 += kMaxItems) {
         const int r1 = min(i_end, r0 + kMaxItems);
@@ -542,7 +646,64 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             pdl_trigger();
         }
 
-        if (warp < 4 && J.tiled) {
+        if (NV == 0 && warp < 4) {
+          if constexpr (NV == 0) {
+            // ------------------- producer, resident B: one thread; a run's B chunk and its
+            // atoms once into a slot, each stage the weight tile and its scale atoms
+            if (threadIdx.x == 0) {
+                int pre = 0;
+                if (prefetch) {
+                    // early launch: the first stages' weights before the programmatic wait
+                    pre = min(G::kNStages, nr);
+                    for (int h = 0; h < pre; h++) {
+                        const ItemEnt &it = items[h];
+                        if (!item_ok(it)) continue;
+                        const int st = (g_prod + h) % G::kNStages;
+                        const uint32_t fb = b_full + 8 * st;
+                        mbar_expect_tx(fb, G::kTx);
+                        issue_weights<0>(stage0 + (uint32_t)st * G::kBytes, fb, J, it, it.s);
+                    }
+                    pdl_wait();
+                }
+                for (int k = 0; k < nr && !stop; k++) {
+                    const ItemEnt &it = items[k];
+                    const bool aligned = item_ok(it);
+                    if (!aligned) k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
+                    if (new_run(it, rb_vec, rb_chunk)) {
+                        const int slot = rb_n & 1;
+                        if (rb_n >= 2 && !mbar_wait(b_bempty + 8 * slot, ((rb_n >> 1) - 1) & 1, abort)) {
+                            stop = true;
+                            break;
+                        }
+                        const uint32_t bb = b_bfull + 8 * slot, dst = bslots + (uint32_t)(slot * G::kBSlot);
+                        const size_t vix = (size_t)it.vec * J.nch + it.s;
+                        mbar_expect_tx(bb, kTileB + kTileSF);
+                        bulk_g2s(dst, J.bq + vix * kTileB, kTileB, bb);
+                        bulk_g2s(dst + kTileB, J.bs + vix * kTileSF, kTileSF, bb);
+                        rb_n++;
+                        rb_vec = it.vec;
+                        rb_chunk = it.s;
+                    }
+                    if (k < pre) { g_prod++; continue; }     // weights issued above
+                    const int st = g_prod % G::kNStages;
+                    if (g_prod >= G::kNStages &&
+                        !mbar_wait(b_empty + 8 * st, ((g_prod / G::kNStages) - 1) & 1, abort)) {
+                        stop = true;
+                        break;
+                    }
+                    const uint32_t fb = b_full + 8 * st;
+                    if (aligned) {
+                        mbar_expect_tx(fb, G::kTx);
+                        issue_weights<0>(stage0 + (uint32_t)st * G::kBytes, fb, J, it, it.s);
+                    } else {
+                        mbar_arrive(fb);
+                    }
+                    g_prod++;
+                }
+            }
+          }
+        } else if (warp < 4 && J.tiled) {
+          if constexpr (NV != 0) {
             // ------------------------------------------ producer, tiled layout: one thread
             // streams each stage as four bulk copies (weight tile, its scale atoms, the B
             // tile and its scale atoms), all completing on the stage's mbarrier
@@ -600,6 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                     }
                 }
             }
+          }
         } else if (warp < 4) {
           if constexpr (NV == 1) {
             // -------------------------- producers, checkpoint layout: 128 threads, cp.async
@@ -668,9 +830,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
           }
         } else if (warp == 4) {
             // ----------------------------------------------------------- MMA issuer
-            if (lane == 0 && !stop &&
-                !mma_items<NV>(J, nr, g_mma, n_mma, tmem, stage0, b_full, b_empty, b_accf, b_acce, abort))
-                stop = true;
+            if (lane == 0 && !stop) {
+                bool ok;
+                if constexpr (NV == 0)
+                    ok = mma_items_rb(J, items, nr, g_mma, n_mma, rb_n, rb_vec, rb_chunk, tmem, stage0, bslots,
+                                      b_full, b_empty, b_accf, b_acce, b_bfull, b_bempty, abort);
+                else
+                    ok = mma_items<NV>(J, nr, g_mma, n_mma, tmem, stage0, b_full, b_empty, b_accf, b_acce, abort);
+                if (!ok) stop = true;
+            }
             __syncwarp();
         } else {
             // ------------------------------------------------------------- epilogue
@@ -1102,11 +1270,16 @@ static int launch_job(const Job &J, long long items, cudaStream_t st)
 int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
                 int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
                 int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
-                int early)
+                int early, int resident)
 {
     Job J;
     K3_TRY(make_job(J, mode, tiled, w, idx, count, npos_max, K, rows, ks, bq, bs, vec_div, part, out_w,
                     slice_stride, early));
+    if (resident) {
+        // one stage per item: the (vector, chunk, tile) order needs one K chunk per slice
+        if (!tiled || J.cps != 1) return fail(K3D_EINVAL, "umma: resident B needs tiled experts, ks = K / 512");
+        return launch_job<0>(J, (long long)npos_max * J.ntiles * ks, st);
+    }
     return launch_job<1>(J, (long long)npos_max * J.ntiles * ks, st);
 }
 

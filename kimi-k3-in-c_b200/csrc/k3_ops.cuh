@@ -65,7 +65,7 @@ int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int
 int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int *count,
                 int npos_max, int K, int rows, int ks, const uint8_t *bq, const uint8_t *bs,
                 int vec_div, float *part, int out_w, size_t slice_stride, cudaStream_t st,
-                int early);
+                int early, int resident = 0);
 // Grouped items (a batch: several tokens per expert): groups of up to four consecutive
 // grouped positions of one expert share each weight stage (tiled experts).
 struct UmmaGroups {

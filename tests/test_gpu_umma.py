@@ -180,3 +180,27 @@ def test_grouped_pass_config1_shapes(k3, oracle):
     want, oi, _ = oracle.moe_swiglu(x, T, hidden, inter, E, 8, 1, 2.5, W, bias, experts, 256, *sh)
     assert np.array_equal(idx, oi)
     assert max_rel_err(y, want) <= 1e-4
+
+
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_resident_b_matches_per_stage_b_and_oracle(k3, oracle, T):
+    """Tiled experts up to 64 assignments: items ordered (token, K chunk, tile) so that B is
+    loaded once per run into a slot beside a 6-stage weight ring; against the kernel that
+    carries B in every stage (kind 3) and the oracle."""
+    g, experts, W, bias, sh = small_layer(1300 + T, E=16)
+    hidden, inter, E = 1024, 512, 16
+    mw = k3cuda.MoeWeights(hidden, inter, E, 8, W, bias, shared=sh, experts=experts, tiled=True)
+    x = synth.bf16_to_f32(synth.bf16_normal(g, (T, hidden), 1.0))
+    ys = {}
+    try:
+        for kind in (0, 3, 0):
+            k3cuda.check(k3.k3d_set_expert_kernel(kind))
+            y, idx, _ = run_layer(k3, mw, x, T)
+            ys.setdefault(kind, []).append(y)
+    finally:
+        k3cuda.check(k3.k3d_set_expert_kernel(0))
+    assert np.array_equal(ys[0][0], ys[0][1])
+    assert max_rel_err(ys[0][0], ys[3][0]) <= 1e-5
+    want, oi, _ = oracle.moe_swiglu(x, T, hidden, inter, E, 8, 1, 2.5, W, bias, experts, 256, *sh)
+    assert np.array_equal(idx, oi)
+    assert max_rel_err(ys[0][0], want) <= 1e-4
