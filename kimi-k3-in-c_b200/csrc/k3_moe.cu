@@ -328,22 +328,24 @@ static int run_experts(const MoeWork &mw, const int *idx, const int *count, int 
         return fail(K3D_EINVAL, "tiled experts need hidden and inter multiples of 512");
     O.pos_of = nullptr;
     if (!mw.single_mode && count && use_grouped(B, TK, layout, hidden, inter)) {
-        // groups of up to four tokens of one expert share each weight stage; partials by
-        // position (one K slice: a batch fills the GPU without splitting K)
+        // groups of up to four tokens of one expert share each weight stage; one K chunk
+        // per slice (items ordered (group, chunk, tile), B resident across a run); partials
+        // by position
+        const int ks_gu = hidden / 512, ks_d = inter / 512;
         const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
         K3_TRY(umma_make_groups(mw, B.grp, st));
         K3_TRY(umma_bsplit_group_x(B.bqg_x, B.bsg_x, x, hidden, mw.assign, topk, B.grp, TK, st));
         prof_begin("experts.gateup");
-        K3_TRY(umma_launch_grouped(0, mw, B.grp, TK, hidden, inter, 1, B.bqg_x, B.bsg_x, B.part_gu, 2 * inter,
+        K3_TRY(umma_launch_grouped(0, mw, B.grp, TK, hidden, inter, ks_gu, B.bqg_x, B.bsg_x, B.part_gu, 2 * inter,
                                    sl_gu, st));
         prof_end("experts.gateup");
-        K3_TRY(umma_bsplit_swiglu_group(B.bqg_a, B.bsg_a, B.part_gu, 1, sl_gu, inter, B.grp, TK, st));
+        K3_TRY(umma_bsplit_swiglu_group(B.bqg_a, B.bsg_a, B.part_gu, ks_gu, sl_gu, inter, B.grp, TK, st));
         prof_begin("experts.down");
-        K3_TRY(umma_launch_grouped(1, mw, B.grp, TK, inter, hidden, 1, B.bqg_a, B.bsg_a, B.part_d, hidden, sl_d,
+        K3_TRY(umma_launch_grouped(1, mw, B.grp, TK, inter, hidden, ks_d, B.bqg_a, B.bsg_a, B.part_d, hidden, sl_d,
                                    st));
         prof_end("experts.down");
         O.contrib = B.part_d;
-        O.ks = 1;
+        O.ks = ks_d;
         O.slice = sl_d;
         O.pos_of = B.grp.pos_of;
         return K3D_OK;
@@ -414,12 +416,16 @@ static void expert_bufs_layout(ExpertBufs &eb, const K3dMoeShape *s, size_t T, s
     eb.xb_a = (__half *)take(TK * 2 * s->inter * sizeof(__half));
     eb.xs_a = (float *)take(TK * sizeof(float));
     if (umma_eligible(s->hidden, s->inter, (int)TK, s->expert_layout)) {
+        // the grouped pass keeps one slice per K chunk at any count
+        const bool grp = grouped_eligible(s->hidden, s->inter, (int)TK, s->expert_layout);
+        const size_t cap_gu = grp ? (size_t)s->hidden / 512 : (size_t)umma_ks_cap(s->hidden, (int)TK);
+        const size_t cap_d = grp ? (size_t)s->inter / 512 : (size_t)umma_ks_cap(s->inter, (int)TK);
         eb.bq_x = (uint8_t *)take(T * umma_bq_bytes(s->hidden));
         eb.bs_x = (uint8_t *)take(T * umma_bs_bytes(s->hidden));
         eb.bq_a = (uint8_t *)take(TK * umma_bq_bytes(s->inter));
         eb.bs_a = (uint8_t *)take(TK * umma_bs_bytes(s->inter));
-        eb.part_gu = (float *)take((size_t)umma_ks_cap(s->hidden, (int)TK) * TK * 2 * s->inter * sizeof(float));
-        eb.part_d = (float *)take((size_t)umma_ks_cap(s->inter, (int)TK) * TK * s->hidden * sizeof(float));
+        eb.part_gu = (float *)take(cap_gu * TK * 2 * s->inter * sizeof(float));
+        eb.part_d = (float *)take(cap_d * TK * s->hidden * sizeof(float));
     } else {
         eb.bq_x = eb.bs_x = eb.bq_a = eb.bs_a = nullptr;
         eb.part_gu = eb.part_d = nullptr;
@@ -795,12 +801,17 @@ int k3d_moe_swiglu_a2a(float *out, const float *x, const K3dMoeW *w, const K3dMo
         prof_end("moe.experts");
         ybuf = O.contrib;
         if (O.pos_of) {
-            // grouped pass: rows by position; the exchange sends them by received row
-            launch_pdl(k_gather_rows, dim3((unsigned)R), dim3(256), 0, st, L.eb.contrib, O.contrib, O.pos_of,
-                       s->hidden);
+            // grouped pass: K slices by position; summed, then gathered into received-row
+            // order (the rows received are no longer needed: their buffer takes the result)
+            const float *src = O.contrib;
+            if (O.ks > 1) {
+                K3_TRY(umma_slice_sum(L.eb.contrib, O.contrib, O.ks, O.slice, (int)(R * s->hidden), st));
+                src = L.eb.contrib;
+            }
+            launch_pdl(k_gather_rows, dim3((unsigned)R), dim3(256), 0, st, L.recvbuf, src, O.pos_of, s->hidden);
             note_launch();
             K3_TRY(check_launch("moe a2a gather"));
-            ybuf = L.eb.contrib;
+            ybuf = L.recvbuf;
         } else if (O.ks > 1) {
             K3_TRY(umma_slice_sum(L.eb.contrib, O.contrib, O.ks, O.slice, (int)(R * s->hidden), st));
             ybuf = L.eb.contrib;

@@ -282,7 +282,7 @@ constexpr int kAccBufs = 4;             // accumulator ring depth
 // same expert share each weight stage; B stacks their pieces as 64 rows (row 16 v + p =
 // piece p of slot v), one MMA of N = 64 per K step, and the scale atoms hold B row m at
 // byte 16 (m % 32) + 4 (m / 32) + block (the layout of A's 128 rows).
-template <int NV>
+template <int NV, int RES = 0>
 struct Geo {
     static constexpr int kVec = NV;                             // vectors per item
     static constexpr int kBTile = NV * kTileB;                  // B tile per stage
@@ -301,36 +301,40 @@ struct Geo {
     static_assert(kAccBufs * kCols + 64 <= kTmem, "tensor memory");
 };
 
-// NV = 0: one vector per item, items ordered (vector, K chunk, tile) with one stage each,
-// so consecutive items share their B chunk: B and its scale atoms are loaded once per run
-// of items into one of two slots beside the ring, and the ring's stages carry only the
-// weight tile and its scales (34 KB): six of them fit instead of five, and B's scales go
-// to tensor memory once per run instead of once per stage.
-template <>
-struct Geo<0> {
-    static constexpr int kVec = 1;
+// RES = 1 (resident B): one stage per item, items ordered (vector or group, K chunk,
+// tile), so consecutive items share their B chunk: B and its scale atoms are loaded once
+// per run of items into one of two slots beside the ring, and the ring's stages carry only
+// the weight tile and its scales (34 KB), six of them for one vector (five when B rode
+// along) and five for a group of four (four when B rode along); B's scales go to tensor
+// memory once per run instead of once per stage.
+template <int NV>
+struct Geo<NV, 1> {
+    static constexpr int kVec = NV;
     static constexpr int kSFA = kTileA;                         // 32768
     static constexpr int kBytes = kTileA + kTileSF;             // 34816
-    static constexpr int kNStages = 6;
-    static constexpr int kCols = kN;
-    static constexpr int kTmem = kTmemCols;
-    static constexpr uint32_t kSfaCol = umma::kSfaCol, kSfbCol = umma::kSfbCol;   // SFB: 16 columns per slot
+    static constexpr int kNStages = NV == 1 ? 6 : 5;
+    static constexpr int kCols = kN * NV;
+    static constexpr int kTmem = NV == 1 ? kTmemCols : 512;
+    static constexpr uint32_t kSfaCol = NV == 1 ? umma::kSfaCol : 256;
+    static constexpr uint32_t kSfbCol = NV == 1 ? umma::kSfbCol : 288;   // 16 columns per slot
     static constexpr uint32_t kTx = kTileA + kTileSF;
-    static constexpr int kBSlot = kTileB + kTileSF;             // 6144: B tile, then its atoms
+    static constexpr int kBTile = NV * kTileB;
+    static constexpr int kBSlot = kBTile + kTileSF;             // B tile, then its atoms
     static constexpr int kBSlots = kStage0 + kNStages * kBytes; // offset of the two slots
     static constexpr size_t kSmem = 1024 + kBSlots + 2 * kBSlot;
     static_assert(kBytes % 1024 == 0 && kBSlots % 1024 == 0 && kBSlot % 1024 == 0, "alignment");
     static_assert(kSmem <= 232448, "shared memory");
+    static_assert(kAccBufs * kCols <= (int)kSfaCol && kSfbCol + 32 <= (uint32_t)kTmem, "tensor memory");
 };
 
-template <int NV>
+template <int NV, int RES>
 __device__ __forceinline__ ItemEnt decode(const Job &J, int item)
 {
     ItemEnt it;
     it.s = item % J.ks;
     int rest, p;
-    if (NV == 0) {
-        // (vector, K chunk, tile), tile fastest (one stage per item)
+    if (RES) {
+        // (vector or group, K chunk, tile), tile fastest (one stage per item)
         it.tile = item % J.ntiles;
         rest = item / J.ntiles;
         it.s = rest % J.ks;
@@ -397,13 +401,13 @@ __device__ __forceinline__ bool item_ok(const ItemEnt &it)
 }
 
 // Tiled layout: the weight tile of one stage and its scale atoms, completing on `fb`.
-template <int NV>
+template <int NV, int RES>
 __device__ __forceinline__ void issue_weights(uint32_t sb, uint32_t fb, const Job &J, const ItemEnt &it,
                                               int chunk)
 {
     const size_t tix = (size_t)it.tile * J.nch + chunk;
     bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
-    bulk_g2s(sb + Geo<NV>::kSFA, it.s0 + tix * kTileSF, kTileSF, fb);
+    bulk_g2s(sb + Geo<NV, RES>::kSFA, it.s0 + tix * kTileSF, kTileSF, fb);
 }
 
 // The B tile of one stage and its scale atoms, completing on `fb`.
@@ -473,13 +477,14 @@ __device__ __forceinline__ bool new_run(const ItemEnt &it, int vec, int chunk)
 // MMA issuer of the resident-B geometry: one stage per item; at the start of each run the
 // previous run's B slot is released (a commit: it frees once that run's MMAs finish) and
 // the new slot's scale atoms are copied to tensor memory after its B has landed.
+template <int NV>
 __device__ __forceinline__ bool mma_items_rb(const Job &J, const ItemEnt *items, int nr, int &g_mma, int &n_mma,
                                              int &rb_n, int &rb_vec, int &rb_chunk, uint32_t tmem,
                                              uint32_t stage0, uint32_t bslots, uint32_t b_full,
                                              uint32_t b_empty, uint32_t b_accf, uint32_t b_acce,
                                              uint32_t b_bfull, uint32_t b_bempty, volatile int *abort)
 {
-    using G = Geo<0>;
+    using G = Geo<NV, 1>;
     for (int k = 0; k < nr; k++, n_mma++) {
         const ItemEnt &it = items[k];
         const int buf = n_mma % kAccBufs;
@@ -494,7 +499,7 @@ __device__ __forceinline__ bool mma_items_rb(const Job &J, const ItemEnt *items,
             const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)(slot * 16);
 #pragma unroll
             for (int a4 = 0; a4 < 4; a4++)
-                tc_cp_sf(sfb + 4 * a4, desc_sf(bslots + (uint32_t)(slot * G::kBSlot + kTileB + 512 * a4)));
+                tc_cp_sf(sfb + 4 * a4, desc_sf(bslots + (uint32_t)(slot * G::kBSlot + G::kBTile + 512 * a4)));
             rb_n++;
             rb_vec = it.vec;
             rb_chunk = it.s;
@@ -502,7 +507,7 @@ __device__ __forceinline__ bool mma_items_rb(const Job &J, const ItemEnt *items,
         const int slot = (rb_n - 1) & 1;
         const uint32_t bs = bslots + (uint32_t)(slot * G::kBSlot);
         const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)(slot * 16);
-        const uint32_t dcol = tmem + (uint32_t)(buf * kN);
+        const uint32_t dcol = tmem + (uint32_t)(buf * G::kCols);
         const int st = g_mma % G::kNStages;
         if (!mbar_wait(b_full + 8 * st, (g_mma / G::kNStages) & 1, abort)) return false;
         tc_fence_after();
@@ -514,10 +519,10 @@ __device__ __forceinline__ bool mma_items_rb(const Job &J, const ItemEnt *items,
         for (int j = 0; j < 8; j++) {
             const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
             const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
-            const uint64_t bd = desc_sw128(bs + kb * 2048u + off);
+            const uint64_t bd = desc_sw128(bs + kb * (uint32_t)(NV * 2048) + off);
             const uint32_t id = (uint32_t)((j & 1) * 2);
             const uint32_t atom = (uint32_t)(4 * (j >> 1));
-            tc_mma(dcol, ad, bd, idesc_mxf4<kN>(id), j > 0 ? 1u : 0u, (sfa + atom) | (id << 30),
+            tc_mma(dcol, ad, bd, idesc_mxf4<G::kCols>(id), j > 0 ? 1u : 0u, (sfa + atom) | (id << 30),
                    (sfb + atom) | (id << 30));
         }
         tc_commit(b_empty + 8 * st);
@@ -530,12 +535,12 @@ __device__ __forceinline__ bool mma_items_rb(const Job &J, const ItemEnt *items,
 // Epilogue warp of tensor-memory lane quadrant q: for each of `nr` items, its 32 rows of
 // the 128 x 16 accumulator, summed over the 16 pieces and stored as the item's partial.
 // False when a wait gave up.
-template <int NV>
+template <int NV, int RES>
 __device__ __forceinline__ bool epilogue_items(const Job &J, const ItemEnt *items, int nr, int &n_epi,
                                                uint32_t tmem, uint32_t b_accf, uint32_t b_acce,
                                                volatile int *abort, int q, int lane)
 {
-    using G = Geo<NV>;
+    using G = Geo<NV, RES>;
     const int m = q * 32 + lane;            // tile row
     for (int k = 0; k < nr; k++, n_epi++) {
         const ItemEnt &it = items[k];
@@ -566,10 +571,10 @@ __device__ __forceinline__ bool epilogue_items(const Job &J, const ItemEnt *item
     return true;
 }
 
-template <int NV>
+template <int NV, int RES>
 __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 {
-    using G = Geo<NV>;
+    using G = Geo<NV, RES>;
     extern __shared__ unsigned char smem_raw[];
     // 1024-aligned base (the SWIZZLE_128B pattern is a function of the absolute address)
     const uint32_t raw = saddr(smem_raw);
@@ -628,14 +633,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
     int n_mma = 0;       // items issued by the MMA thread
     int n_epi = 0;       // items finished by this epilogue warp
     bool stop = false;
-    // resident-B runs (NV = 0): runs begun and the current run's (vector, chunk), kept by
+    // resident-B runs (RES = 1): runs begun and the current run's (vector, chunk), kept by
     // the producer and the MMA issuer each
     int rb_n = 0, rb_vec = -1, rb_chunk = -1;
-    const uint32_t bslots = base + (uint32_t)(NV == 0 ? Geo<0>::kBSlots : 0);
+    const uint32_t bslots = base + (uint32_t)(RES ? Geo<NV, 1>::kBSlots : 0);
 
     for (int r0 = i_beg; r0 < i_end; r0 += kMaxItems) {
         const int r1 = min(i_end, r0 + kMaxItems);
-        for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) items[i - r0] = decode<NV>(J, i);
+        for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) items[i - r0] = decode<NV, RES>(J, i);
         __syncthreads();
         const int nr = r1 - r0;
         const bool prefetch = J.early && J.tiled && r0 == i_beg;
@@ -646,8 +651,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             pdl_trigger();
         }
 
-        if (NV == 0 && warp < 4) {
-          if constexpr (NV == 0) {
+        if (RES && warp < 4) {
+          if constexpr (RES == 1) {
             // ------------------- producer, resident B: one thread; a run's B chunk and its
             // atoms once into a slot, each stage the weight tile and its scale atoms
             if (threadIdx.x == 0) {
@@ -661,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                         const int st = (g_prod + h) % G::kNStages;
                         const uint32_t fb = b_full + 8 * st;
                         mbar_expect_tx(fb, G::kTx);
-                        issue_weights<0>(stage0 + (uint32_t)st * G::kBytes, fb, J, it, it.s);
+                        issue_weights<NV, RES>(stage0 + (uint32_t)st * G::kBytes, fb, J, it, it.s);
                     }
                     pdl_wait();
                 }
@@ -677,9 +682,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                         }
                         const uint32_t bb = b_bfull + 8 * slot, dst = bslots + (uint32_t)(slot * G::kBSlot);
                         const size_t vix = (size_t)it.vec * J.nch + it.s;
-                        mbar_expect_tx(bb, kTileB + kTileSF);
-                        bulk_g2s(dst, J.bq + vix * kTileB, kTileB, bb);
-                        bulk_g2s(dst + kTileB, J.bs + vix * kTileSF, kTileSF, bb);
+                        mbar_expect_tx(bb, G::kBTile + kTileSF);
+                        bulk_g2s(dst, J.bq + vix * G::kBTile, G::kBTile, bb);
+                        bulk_g2s(dst + G::kBTile, J.bs + vix * kTileSF, kTileSF, bb);
                         rb_n++;
                         rb_vec = it.vec;
                         rb_chunk = it.s;
@@ -694,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                     const uint32_t fb = b_full + 8 * st;
                     if (aligned) {
                         mbar_expect_tx(fb, G::kTx);
-                        issue_weights<0>(stage0 + (uint32_t)st * G::kBytes, fb, J, it, it.s);
+                        issue_weights<NV, RES>(stage0 + (uint32_t)st * G::kBytes, fb, J, it, it.s);
                     } else {
                         mbar_arrive(fb);
                     }
@@ -703,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             }
           }
         } else if (warp < 4 && J.tiled) {
-          if constexpr (NV != 0) {
+          if constexpr (RES == 0) {
             // ------------------------------------------ producer, tiled layout: one thread
             // streams each stage as four bulk copies (weight tile, its scale atoms, the B
             // tile and its scale atoms), all completing on the stage's mbarrier
@@ -719,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                         const uint32_t sb = stage0 + (uint32_t)((g_prod + h) % G::kNStages) * G::kBytes;
                         const uint32_t fb = b_full + 8 * ((g_prod + h) % G::kNStages);
                         mbar_expect_tx(fb, G::kTx);
-                        issue_weights<NV>(sb, fb, J, it, it.s * J.cps + h % J.cps);
+                        issue_weights<NV, RES>(sb, fb, J, it, it.s * J.cps + h % J.cps);
                     }
                     pdl_wait();
                     for (int h = 0; h < pre; h++) {
@@ -752,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
                         const uint32_t fb = b_full + 8 * st;
                         if (aligned) {
                             mbar_expect_tx(fb, G::kTx);
-                            issue_weights<NV>(sb, fb, J, it, chunk);
+                            issue_weights<NV, RES>(sb, fb, J, it, chunk);
                             issue_operand<NV>(sb, fb, J, it, chunk);
                         } else {
                             mbar_arrive(fb);
@@ -763,7 +768,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             }
           }
         } else if (warp < 4) {
-          if constexpr (NV == 1) {
+          if constexpr (NV == 1 && RES == 0) {
             // -------------------------- producers, checkpoint layout: 128 threads, cp.async
             const int tid = threadIdx.x;
             const int g_round = g_prod;          // stages of this round are published here
@@ -832,8 +837,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             // ----------------------------------------------------------- MMA issuer
             if (lane == 0 && !stop) {
                 bool ok;
-                if constexpr (NV == 0)
-                    ok = mma_items_rb(J, items, nr, g_mma, n_mma, rb_n, rb_vec, rb_chunk, tmem, stage0, bslots,
+                if constexpr (RES == 1)
+                    ok = mma_items_rb<NV>(J, items, nr, g_mma, n_mma, rb_n, rb_vec, rb_chunk, tmem, stage0, bslots,
                                       b_full, b_empty, b_accf, b_acce, b_bfull, b_bempty, abort);
                 else
                     ok = mma_items<NV>(J, nr, g_mma, n_mma, tmem, stage0, b_full, b_empty, b_accf, b_acce, abort);
@@ -842,7 +847,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             __syncwarp();
         } else {
             // ------------------------------------------------------------- epilogue
-            epilogue_items<NV>(J, items, nr, n_epi, tmem, b_accf, b_acce, abort, warp & 3, lane);
+            epilogue_items<NV, RES>(J, items, nr, n_epi, tmem, b_accf, b_acce, abort, warp & 3, lane);
         }
         __syncthreads();          // every role is done with this round's table
     }
@@ -1250,19 +1255,19 @@ static int make_job(Job &J, int mode, int tiled, const MoeWork &w, const int *id
     return K3D_OK;
 }
 
-template <int NV>
+template <int NV, int RES>
 static int launch_job(const Job &J, long long items, cudaStream_t st)
 {
     static bool init = false;
     if (!init) {
-        cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)Geo<NV>::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma<NV, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)Geo<NV, RES>::kSmem);
         if (e != cudaSuccess) return fail(K3D_ECUDA, "umma smem attribute: %s", cudaGetErrorString(e));
         init = true;
     }
     if (items <= 0) return K3D_OK;
     const int grid = (int)(items < sm_count() ? items : sm_count());
-    launch_pdl(k_mxfp4_umma<NV>, dim3(grid), dim3(kThreads), Geo<NV>::kSmem, st, J);
+    launch_pdl(k_mxfp4_umma<NV, RES>, dim3(grid), dim3(kThreads), Geo<NV, RES>::kSmem, st, J);
     note_launch();
     return check_launch("mxfp4 umma");
 }
@@ -1278,9 +1283,9 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
     if (resident) {
         // one stage per item: the (vector, chunk, tile) order needs one K chunk per slice
         if (!tiled || J.cps != 1) return fail(K3D_EINVAL, "umma: resident B needs tiled experts, ks = K / 512");
-        return launch_job<0>(J, (long long)npos_max * J.ntiles * ks, st);
+        return launch_job<1, 1>(J, (long long)npos_max * J.ntiles * ks, st);
     }
-    return launch_job<1>(J, (long long)npos_max * J.ntiles * ks, st);
+    return launch_job<1, 0>(J, (long long)npos_max * J.ntiles * ks, st);
 }
 
 // The grouped pass: items over the groups of G (ng = their device count, at most
@@ -1296,7 +1301,9 @@ int umma_launch_grouped(int mode, const MoeWork &w, const UmmaGroups &G, int max
     J.g_p0 = G.p0;
     J.g_n = G.n;
     J.g_e = G.e;
-    return launch_job<4>(J, (long long)max_groups * J.ntiles * ks, st);
+    // one stage per item: resident B when every slice is one K chunk
+    if (J.cps == 1) return launch_job<4, 1>(J, (long long)max_groups * J.ntiles * ks, st);
+    return launch_job<4, 0>(J, (long long)max_groups * J.ntiles * ks, st);
 }
 
 size_t umma_bq_group_bytes(int K) { return (size_t)(K / kStageK) * 4 * kTileB; }
