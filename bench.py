@@ -1,7 +1,7 @@
 """Benchmark of the B200 decode hot path (libk3cuda) and of the reference's CPU path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload moe|expert|stack]
+                    [--workload stack|moe|moe_a2a|kda_prefill]
 
 One JSON line on rank 0. Under torchrun (N > 1) every rank owns 1/N of the routed experts
 (expert parallelism), the partial MoE outputs are summed over NCCL, and the reported time
@@ -454,6 +454,144 @@ def bench_moe_a2a(args, rank, world):
     }
 
 
+# ------------------------------------------------------------ KDA prefill (config 3) ----
+KDA_H, KDA_D = 64, 128
+
+
+def kda_prefill_bytes(T):
+    """Algorithmic bytes of one prefill: q, k, v, decay and o (fp32 [T][64][128] each),
+    beta [T][64], and the 64 fp32 128x128 states read and written once."""
+    return 5 * T * KDA_H * KDA_D * 4 + T * KDA_H * 4 + 2 * KDA_H * KDA_D * KDA_D * 4
+
+
+def kda_prefill_inputs(T, seed):
+    g = np.random.default_rng(seed)
+
+    def unit(x):
+        x /= np.linalg.norm(x, axis=-1, keepdims=True)
+        return x
+
+    shp = (T, KDA_H, KDA_D)
+    q = unit(g.standard_normal(shp, dtype=np.float32))
+    k = unit(g.standard_normal(shp, dtype=np.float32))
+    v = g.standard_normal(shp, dtype=np.float32)
+    al = g.uniform(0.9, 1.0, shp).astype(np.float32)
+    be = g.uniform(0, 1, (T, KDA_H)).astype(np.float32)
+    S = (g.standard_normal((KDA_H, KDA_D, KDA_D), dtype=np.float32) * np.float32(0.01))
+    return S, q, k, v, al, be
+
+
+def cpu_kda_prefill_sample(seconds=12.0, max_tokens=4096):
+    """The reference's k3_kda_step (k3_ops.c:186-243, compiled in oracle/_ref) over the 64
+    heads of a config-3 prefill, token after token on one core, for about `seconds`."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as orc
+    if orc.Reference.available():
+        impl, kind = orc.Reference(), "reference"
+    else:
+        impl, kind = orc.Oracle(), "port"
+    S, q, k, v, al, be = kda_prefill_inputs(64, 11)
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds and n < max_tokens:
+        t = n % 64
+        for h in range(KDA_H):
+            S[h] = impl.kda_step(S[h], q[t, h], k[t, h], v[t, h], al[t, h], float(be[t, h]))[0]
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": 1, "kind": kind,
+            "sample": f"{n} prefill tokens x 64 heads of k3_kda_step (128x128 state) in {dt:.1f} s "
+                      f"on one core; the reference runs heads in parallel under OpenMP"}
+
+
+def bench_kda_prefill(args, rank, world):
+    """BASELINE config 3 prefill: one step = k3d_kda_prefill(chunk = 64) over T = 8192 tokens
+    x 64 heads x 128x128 fp32 states, the state carried from step to step. The inputs
+    (1.35 GB) exceed L2, so no flush is needed. Ranks run independent sequences (weak)."""
+    import k3cuda
+    lib = k3cuda.init(0)
+    T = args.prefill_tokens
+    S, q, k, v, al, be = kda_prefill_inputs(T, 3303 + rank)
+    bufs = [k3cuda.DevBuf.from_array(a, lib) for a in (S, q, k, v, al, be)]
+    O = k3cuda.DevBuf(T * KDA_H * KDA_D * 4, lib)
+    ev = [lib.k3d_event_create() for _ in range(2)]
+
+    def step(chunk=64):
+        k3cuda.check(lib.k3d_kda_prefill(bufs[0].ptr, O.ptr, bufs[1].ptr, bufs[2].ptr, bufs[3].ptr,
+                                         bufs[4].ptr, bufs[5].ptr, T, KDA_H, KDA_D, KDA_D, chunk),
+                     "kda prefill")
+
+    for _ in range(args.warmup):
+        step()
+    k3cuda.check(lib.k3d_sync())
+    barrier()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0)))
+    clocks.start()
+    lib.k3d_launch_count_reset()
+    step_ms = []
+    for _ in range(args.steps):
+        barrier()
+        lib.k3d_event_record(ev[0])
+        step()
+        lib.k3d_event_record(ev[1])
+        step_ms.append(lib.k3d_event_elapsed_ms(ev[0], ev[1]))
+    k3cuda.check(lib.k3d_sync())
+    launches = lib.k3d_launch_count()
+    clk = clocks.stop()
+    tot_ms = reduce_max(sum(step_ms))
+    # the sequential recurrence (chunk = 0, bit-identical to k3_kda_step) once, for scale
+    lib.k3d_event_record(ev[0])
+    step(0)
+    lib.k3d_event_record(ev[1])
+    k3cuda.check(lib.k3d_sync())
+    seq_ms = lib.k3d_event_elapsed_ms(ev[0], ev[1])
+    # end to end with host buffers: inputs up, prefill, o down
+    names = ("q", "k", "v", "al", "be")
+    host = {}
+    for n_, a in zip(names, (q, k, v, al, be)):
+        host[n_] = (lib.k3d_host_alloc(a.nbytes), a.nbytes)
+        C.memmove(host[n_][0], a.ctypes.data, a.nbytes)
+    ho = lib.k3d_host_alloc(O.nbytes)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for b, n_ in zip(bufs[1:], names):
+            k3cuda.check(lib.k3d_upload(b.ptr, host[n_][0], host[n_][1]))
+        step()
+        k3cuda.check(lib.k3d_download(ho, O.ptr, O.nbytes))
+    e2e_s = reduce_max(time.perf_counter() - t0)
+    for p_, _ in host.values():
+        lib.k3d_host_free(p_)
+    lib.k3d_host_free(ho)
+    h2d = sum(a.nbytes for a in (q, k, v, al, be))
+    alg = kda_prefill_bytes(T)
+    ms = tot_ms / args.steps
+    peak, pk = measured_peaks()
+    ach = alg / (ms * 1e-3) / 1e9
+    nch = (T + 63) // 64
+    fma = KDA_H * nch * (3 * 64 * KDA_D * KDA_D + 64 * 64 * KDA_D // 2 + 64 * KDA_D * KDA_D)
+    return {
+        "metric": "KDA prefill tok/s (config 3: 64 heads, 128x128 fp32 state, chunk 64)",
+        "value": world * T * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (q, k L2-normalised N(0,1); v N(0,1); decay U(0.9,1); beta U(0,1); "
+                "state N(0,0.01)), one sequence per rank",
+        "config": {"workload": f"config3 KDA chunked prefill, {T} tokens", "heads": KDA_H,
+                   "head_dim": KDA_D, "chunk": 64, "parallelism": f"replicas{world}",
+                   "l2": "inputs 1.35 GB > L2", "sequential_ms": seq_ms,
+                   "scan_fp32_fma_per_step": fma},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                     "frac": ach / peak, "peak_kind": pk, "traffic": None,
+                     "note": "whole step (prep + scan kernels); the scan is fp32-FMA bound on "
+                             "CUDA cores, the bytes are the algorithmic floor"},
+        "e2e": {"value": world * T * args.steps / e2e_s, "unit": "tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": O.nbytes},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+
+
 # ----------------------------------------------------------------- stack (config 4) ----
 def stack_cfg(world, rank, batch, cap, layout=1):
     import k3cuda
@@ -635,8 +773,11 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack", "moe", "moe_a2a"],
-                    help="moe_a2a: the MoE layer for a --batch split over the ranks (Mode A)")
+    ap.add_argument("--workload", default="stack", choices=["stack", "moe", "moe_a2a", "kda_prefill"],
+                    help="moe_a2a: the MoE layer for a --batch split over the ranks (Mode A); "
+                         "kda_prefill: config 3 chunked prefill")
+    ap.add_argument("--prefill-tokens", type=int, default=8192,
+                    help="kda_prefill workload: tokens per step (config 3: 8192)")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--tokens", type=int, default=1,
                     help="moe workload: tokens per step (config 1 lists T = 1, 8, 64, 512)")
@@ -655,15 +796,21 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
+        metric = METRIC
         if args.workload == "stack":
             cb = cpu_stack_sample(args.cpu_seconds)
             wl = {"workload": "config4 8-layer K3 stack decode", "batch": 1, "context": args.context,
                   "hidden": HIDDEN, "vocab": 163840, "parallelism": "cpu"}
+        elif args.workload == "kda_prefill":
+            cb = cpu_kda_prefill_sample(args.cpu_seconds)
+            metric = "KDA prefill tok/s (config 3: 64 heads, 128x128 fp32 state, chunk 64)"
+            wl = {"workload": f"config3 KDA chunked prefill, {args.prefill_tokens} tokens",
+                  "heads": KDA_H, "head_dim": KDA_D, "chunk": 64, "parallelism": "cpu"}
         else:
             cb = cpu_moe_sample(seconds=args.cpu_seconds)
             wl = {"workload": "config1 MoE layer decode, T=1", "hidden": HIDDEN,
                   "n_experts": N_EXPERTS, "topk": TOPK, "parallelism": "cpu"}
-        res = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": world,
+        res = {"metric": metric, "value": cb["value"], "unit": "tok/s", "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cb["value"],
                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                "dtype": "fp64-accumulate/fp32", "data": "synthetic",
@@ -680,11 +827,15 @@ def main():
         res = bench_stack(args, rank, world)
     elif args.workload == "moe":
         res = bench_moe(args, rank, world)
+    elif args.workload == "kda_prefill":
+        res = bench_kda_prefill(args, rank, world)
     else:
         res = bench_moe_a2a(args, rank, world)
     if rank == 0:
         if world == 1 and args.cpu_seconds > 0 and args.workload != "moe_a2a":
             res["cpu_baseline"] = (cpu_stack_sample(args.cpu_seconds) if args.workload == "stack"
+                                   else cpu_kda_prefill_sample(args.cpu_seconds)
+                                   if args.workload == "kda_prefill"
                                    else cpu_moe_sample(seconds=args.cpu_seconds))
         print(json.dumps(res), flush=True)
     if world > 1:

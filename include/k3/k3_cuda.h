@@ -222,7 +222,13 @@ int k3d_kda_decode(float *S, float *o, const float *q, const float *k, const flo
                    const float *alpha, const float *beta, int B, int H, int dk, int dv);
 /* T-step recurrence for one sequence, all heads: the same result as T sequential
  * k3d_kda_decode calls. q,k,alpha [T][H][dk]; v,o [T][H][dv]; beta [T][H].
- * chunk = 0 runs the sequential recurrence; chunk = 64 runs the chunked (WY) form. */
+ * chunk = 0 runs the sequential recurrence, bit-identical to k3_kda_step.
+ * chunk = 64 runs the chunked (WY) form: the same recurrence regrouped into 64-step
+ * chunks, equal to the sequential result within fp32 rounding (decays in [0, 1]; a decay
+ * of 0 acts as 2^-126). It needs dk a multiple of 8 up to 128, dv a multiple of 32 up to
+ * 128, and 16-byte aligned S and o; its per-chunk records use library scratch
+ * (about 148 KB per (chunk, head) at dk = dv = 128, for at most 8 chunks at a time).
+ * Other chunk values return K3D_EINVAL. */
 int k3d_kda_prefill(float *S, float *o, const float *q, const float *k, const float *v,
                     const float *alpha, const float *beta, int T, int H, int dk, int dv,
                     int chunk);

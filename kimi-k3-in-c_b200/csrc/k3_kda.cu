@@ -153,6 +153,446 @@ int kda_seq(float *S, float *o, const float *q, const float *k, const float *v,
     return check_launch("kda seq");
 }
 
+// ------------------------------------------------------------- chunked prefill ----
+// The T-step recurrence in chunks of C = 64 steps (the WY / UT form of the delta rule).
+// Within a chunk that starts from state S0, with a_t the running product of the decays up
+// to and including step t (G_t = log2 a_t, per key channel i):
+//     L_ts = sum_i k_t[i] k_s[i] 2^(G_t[i]-G_s[i])   (s < t)
+//     M_ts = sum_i q_t[i] k_s[i] 2^(G_t[i]-G_s[i])   (s <= t)
+//     (I + diag(beta) L) X = diag(beta) (V - Kt S0),  Kt_t = 2^G_t * k_t
+//     X = U - W S0 with U, W the forward substitutions of beta*V and beta*Kt
+//     O = Qt S0 + M X,                                  Qt_t = 2^G_t * q_t
+//     S_C = diag(2^G_last) S0 + Kb^T X,                 Kb_s = 2^(G_last-G_s) * k_s
+// which is the sequential step of k3_kda_step (k3_ops.c:186-243) unrolled over the chunk:
+// X_t = beta_t (v_t - u_t) is the delta row step t writes. The result matches the
+// sequential recurrence within floating-point rounding, not bit for bit.
+//
+// k_kda_chunk_prep, one CTA per (chunk, head), all chunks of a segment in parallel:
+// computes W, U, Qt, Kb, M and 2^G_last into a per-(chunk, head) record. Every exponent
+// 2^(G_t-G_s) has t >= s, so it is <= 1 for decays in [0, 1]. When every |G| of the chunk
+// is at most 60 (no overflow of 2^-G), L and M are plain products of 2^G*k and 2^-G*k;
+// otherwise (strong decay) each pair takes its own exponential. log2 of a decay is clamped
+// at -126, so a decay of exactly 0 acts as 2^-126.
+// k_kda_chunk_scan, one CTA per (head, 32 value columns): walks the chunks in order with
+// the state block in shared memory; per chunk X = U - W S, O = Qt S + M X, S = g S + Kb^T X.
+// The next phase's operand is copied in (cp.async) while the current phase computes.
+namespace kdc {
+
+constexpr int C = 64;            // steps per chunk
+constexpr int DKM = 128;         // largest key dim
+constexpr int LDT = C + 4;       // row stride of the transposed [dk][C] tiles
+constexpr int THREADS = 256;
+constexpr int DVB = 32;          // value columns per scan CTA
+constexpr int SEG = 8;           // chunks per prep/scan pair (records stay in L2)
+
+struct Rec {
+    size_t wt, qt, kb, mt, u, gc, total;
+};
+
+__host__ __device__ __forceinline__ Rec rec(int dk, int dv)
+{
+    Rec r;
+    r.wt = 0;                                   // W^T [dk][C]
+    r.qt = (size_t)dk * C;                      // Qt^T [dk][C]
+    r.kb = r.qt + (size_t)dk * C;               // Kb [C][dk]
+    r.mt = r.kb + (size_t)C * dk;               // M^T [C][C] (M^T[s][t], zero for s > t)
+    r.u = r.mt + (size_t)C * C;                 // U [C][dv]
+    r.gc = r.u + (size_t)C * dv;                // 2^G_last [dk]
+    r.total = r.gc + (size_t)((dk + 3) & ~3);
+    return r;
+}
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float at4(const float4 &v, int a)
+{
+    return a == 0 ? v.x : a == 1 ? v.y : a == 2 ? v.z : v.w;
+}
+
+constexpr size_t prep_smem()
+{
+    return (3 * (size_t)DKM * LDT + (size_t)C * 128 + (size_t)C * C + C) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
+                 const float *__restrict__ v, const float *__restrict__ alpha,
+                 const float *__restrict__ beta, float *__restrict__ ws, long tok0, int T, int H,
+                 int dk, int dv)
+{
+    extern __shared__ __align__(16) float sh[];
+    float *kT = sh;                          // k, then 2^G k on the product path [dk][LDT]
+    float *qT = kT + DKM * LDT;              // q, then 2^G q
+    float *gT = qT + DKM * LDT;              // alpha, then G, then 2^-G k
+    float *vs = gT + DKM * LDT;              // v [C][dv]
+    float *Ls = vs + C * 128;                // L [C][C]
+    float *bs = Ls + C * C;                  // beta [C]
+    const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const long tc0 = tok0 + (long)c * C;
+    const int cn = (int)min((long)C, (long)T - tc0);
+    const Rec R = rec(dk, dv);
+    float *out = ws + ((size_t)c * H + h) * R.total;
+
+    // Padded steps (t >= cn) are identities: k = q = v = 0, decay 1, beta 0.
+    for (int e = tid; e < C * dk; e += THREADS) {
+        const int t = e / dk, i = e - t * dk;
+        float kv = 0.0f, qv = 0.0f, av = 1.0f;
+        if (t < cn) {
+            const size_t g = ((size_t)(tc0 + t) * H + h) * dk + i;
+            kv = k[g];
+            qv = q[g];
+            av = alpha[g];
+        }
+        kT[i * LDT + t] = kv;
+        qT[i * LDT + t] = qv;
+        gT[i * LDT + t] = av;
+    }
+    for (int e = tid; e < C * dv; e += THREADS) {
+        const int t = e / dv, j = e - t * dv;
+        vs[e] = t < cn ? v[((size_t)(tc0 + t) * H + h) * dv + j] : 0.0f;
+    }
+    if (tid < C) bs[tid] = tid < cn ? beta[(size_t)(tc0 + tid) * H + h] : 0.0f;
+    __syncthreads();
+
+    bool big = false;
+    if (tid < dk) {
+        float g = 0.0f;
+        for (int t = 0; t < C; t++) {
+            g += fmaxf(log2f(gT[tid * LDT + t]), -126.0f);
+            gT[tid * LDT + t] = g;
+            big |= !(fabsf(g) <= 60.0f);
+        }
+        out[R.gc + tid] = exp2f(g);
+    }
+    const bool direct = __syncthreads_or(big);
+
+    for (int e = tid; e < C * dk; e += THREADS) {
+        const int s = e / dk, i = e - s * dk;
+        out[R.kb + e] = kT[i * LDT + s] * exp2f(gT[i * LDT + C - 1] - gT[i * LDT + s]);
+    }
+    for (int e = tid; e < dk * C; e += THREADS) {
+        const int i = e / C, t = e - i * C;
+        out[R.qt + e] = qT[i * LDT + t] * exp2f(gT[i * LDT + t]);
+    }
+    if (!direct) {
+        __syncthreads();
+        for (int e = tid; e < dk * C; e += THREADS) {
+            const int i = e / C, t = e - i * C;
+            const float g = gT[i * LDT + t], kk = kT[i * LDT + t];
+            kT[i * LDT + t] = kk * exp2f(g);
+            qT[i * LDT + t] *= exp2f(g);
+            gT[i * LDT + t] = kk * exp2f(-g);
+        }
+    }
+    __syncthreads();
+
+    // L and M in 4x4 tiles: thread (bt, bsb) owns t = 4bt.., s = 4bsb..; tiles above the
+    // diagonal are written as zeros.
+    {
+        const int bt = tid >> 4, bsb = tid & 15;
+        float La[4][4], Ma[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) La[a][b] = Ma[a][b] = 0.0f;
+        if (bsb <= bt) {
+            if (!direct) {
+                for (int i = 0; i < dk; i++) {
+                    const float4 kt = ld4(kT + i * LDT + 4 * bt), qt = ld4(qT + i * LDT + 4 * bt);
+                    const float4 ns = ld4(gT + i * LDT + 4 * bsb);
+#pragma unroll
+                    for (int a = 0; a < 4; a++)
+#pragma unroll
+                        for (int b = 0; b < 4; b++) {
+                            La[a][b] = fmaf(at4(kt, a), at4(ns, b), La[a][b]);
+                            Ma[a][b] = fmaf(at4(qt, a), at4(ns, b), Ma[a][b]);
+                        }
+                }
+            } else {
+                for (int i = 0; i < dk; i++) {
+                    const float4 gt = ld4(gT + i * LDT + 4 * bt), gs = ld4(gT + i * LDT + 4 * bsb);
+                    const float4 kt = ld4(kT + i * LDT + 4 * bt), ks = ld4(kT + i * LDT + 4 * bsb);
+                    const float4 qt = ld4(qT + i * LDT + 4 * bt);
+#pragma unroll
+                    for (int a = 0; a < 4; a++)
+#pragma unroll
+                        for (int b = 0; b < 4; b++) {
+                            if (bsb < bt || b <= a) {
+                                const float kse = at4(ks, b) * exp2f(at4(gt, a) - at4(gs, b));
+                                La[a][b] = fmaf(at4(kt, a), kse, La[a][b]);
+                                Ma[a][b] = fmaf(at4(qt, a), kse, Ma[a][b]);
+                            }
+                        }
+                }
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+            const int t = 4 * bt + a;
+            float4 r;
+            r.x = t > 4 * bsb + 0 ? La[a][0] : 0.0f;
+            r.y = t > 4 * bsb + 1 ? La[a][1] : 0.0f;
+            r.z = t > 4 * bsb + 2 ? La[a][2] : 0.0f;
+            r.w = t > 4 * bsb + 3 ? La[a][3] : 0.0f;
+            *reinterpret_cast<float4 *>(Ls + t * C + 4 * bsb) = r;
+        }
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const int s = 4 * bsb + b;
+            float4 r;
+            r.x = 4 * bt + 0 >= s ? Ma[0][b] : 0.0f;
+            r.y = 4 * bt + 1 >= s ? Ma[1][b] : 0.0f;
+            r.z = 4 * bt + 2 >= s ? Ma[2][b] : 0.0f;
+            r.w = 4 * bt + 3 >= s ? Ma[3][b] : 0.0f;
+            *reinterpret_cast<float4 *>(out + R.mt + (size_t)s * C + 4 * bt) = r;
+        }
+    }
+    __syncthreads();
+
+    // Forward substitution, one thread per right-hand-side column: columns < dv are
+    // beta*V (giving U), the next dk columns beta*Kt (giving W).
+    const int col = tid;
+    if (col < dv + dk) {
+        const bool isv = col < dv;
+        const int i = col - dv;
+        float x[C];
+#pragma unroll
+        for (int t = 0; t < C; t++) {
+            if (isv) x[t] = vs[t * dv + col];
+            else x[t] = direct ? kT[i * LDT + t] * exp2f(gT[i * LDT + t]) : kT[i * LDT + t];
+        }
+#pragma unroll
+        for (int t = 0; t < C; t++) {
+            float acc = x[t];
+#pragma unroll
+            for (int s = 0; s < t; s++) acc = fmaf(-Ls[t * C + s], x[s], acc);
+            x[t] = bs[t] * acc;
+        }
+        if (isv) {
+#pragma unroll
+            for (int t = 0; t < C; t++) out[R.u + (size_t)t * dv + col] = x[t];
+        } else {
+            float4 *w4 = reinterpret_cast<float4 *>(out + R.wt + (size_t)i * C);
+#pragma unroll
+            for (int t = 0; t < C; t += 4) w4[t / 4] = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+        }
+    }
+}
+
+__device__ __forceinline__ void cp16(void *dst, const void *src)
+{
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void stage(float *dst, const float *src, int nfloats)
+{
+    for (int f = threadIdx.x; f < nfloats / 4; f += THREADS) cp16(dst + 4 * f, src + 4 * f);
+}
+
+constexpr size_t scan_smem()
+{
+    return ((size_t)DKM * DVB + (size_t)C * DVB + 2 * (size_t)DKM * C + (size_t)C * C + DKM) *
+           sizeof(float);
+}
+
+__global__ void __launch_bounds__(THREADS, 2)
+k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__restrict__ ws,
+                 long tok0, int nch, int T, int H, int dk, int dv)
+{
+    extern __shared__ __align__(16) float sh[];
+    float *Sb = sh;                          // state block [dk][DVB]
+    float *Xs = Sb + DKM * DVB;              // X [C][DVB]
+    float *const b0 = Xs + C * DVB, *const b1 = b0 + DKM * C;   // W^T / Qt^T / Kb
+    float *Ms = b1 + DKM * C;             // M^T [C][C]
+    float *gs = Ms + C * C;                  // 2^G_last [dk]
+    const int h = blockIdx.x, j0 = blockIdx.y * DVB, tid = threadIdx.x;
+    const int ty = tid >> 4, tx = tid & 15;
+    const Rec R = rec(dk, dv);
+    float *Sh = S + (size_t)h * dk * dv;
+    auto recp = [&](int c) { return ws + ((size_t)c * H + h) * R.total; };
+    auto Bf = [&](int i) { return i ? b1 : b0; };
+
+    int p = 0;
+    stage(Bf(0), recp(0) + R.wt, dk * C);
+    cp_commit();
+    for (int e = tid; e < dk * (DVB / 4); e += THREADS) {
+        const int i = e / (DVB / 4), j = (e - i * (DVB / 4)) * 4;
+        *reinterpret_cast<float4 *>(Sb + i * DVB + j) = ld4(Sh + (size_t)i * dv + j0 + j);
+    }
+    float u[4][2];
+    {
+        const float *U = recp(0) + R.u;
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+            const float2 r = *reinterpret_cast<const float2 *>(U + (size_t)(4 * ty + a) * dv + j0 + 2 * tx);
+            u[a][0] = r.x;
+            u[a][1] = r.y;
+        }
+    }
+
+    for (int c = 0; c < nch; c++) {
+        const float *rc = recp(c);
+        // P1: X = U - W S
+        stage(Bf(p ^ 1), rc + R.qt, dk * C);
+        stage(Ms, rc + R.mt, C * C);
+        cp_commit();
+        cp_wait1();
+        __syncthreads();
+        {
+            const float *W = Bf(p);
+            float acc[4][2];
+#pragma unroll
+            for (int a = 0; a < 4; a++) acc[a][0] = u[a][0], acc[a][1] = u[a][1];
+#pragma unroll 4
+            for (int i = 0; i < dk; i++) {
+                const float4 w = ld4(W + i * C + 4 * ty);
+                const float2 s2 = *reinterpret_cast<const float2 *>(Sb + i * DVB + 2 * tx);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    acc[a][0] = fmaf(-at4(w, a), s2.x, acc[a][0]);
+                    acc[a][1] = fmaf(-at4(w, a), s2.y, acc[a][1]);
+                }
+            }
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+                *reinterpret_cast<float2 *>(Xs + (4 * ty + a) * DVB + 2 * tx) = make_float2(acc[a][0], acc[a][1]);
+        }
+        __syncthreads();
+        p ^= 1;
+        // P2: O = Qt S + M X
+        stage(Bf(p ^ 1), rc + R.kb, C * dk);
+        stage(gs, rc + R.gc, (dk + 3) & ~3);
+        cp_commit();
+        cp_wait1();
+        __syncthreads();
+        {
+            const float *Q = Bf(p);
+            float acc[4][2] = {};
+#pragma unroll 4
+            for (int i = 0; i < dk; i++) {
+                const float4 w = ld4(Q + i * C + 4 * ty);
+                const float2 s2 = *reinterpret_cast<const float2 *>(Sb + i * DVB + 2 * tx);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    acc[a][0] = fmaf(at4(w, a), s2.x, acc[a][0]);
+                    acc[a][1] = fmaf(at4(w, a), s2.y, acc[a][1]);
+                }
+            }
+            for (int s = 0; s < 4 * ty + 4; s++) {
+                const float4 m = ld4(Ms + s * C + 4 * ty);
+                const float2 x2 = *reinterpret_cast<const float2 *>(Xs + s * DVB + 2 * tx);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    acc[a][0] = fmaf(at4(m, a), x2.x, acc[a][0]);
+                    acc[a][1] = fmaf(at4(m, a), x2.y, acc[a][1]);
+                }
+            }
+            const long tc0 = tok0 + (long)c * C;
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                const long t = tc0 + 4 * ty + a;
+                if (t < T)
+                    *reinterpret_cast<float2 *>(o + ((size_t)t * H + h) * dv + j0 + 2 * tx) =
+                        make_float2(acc[a][0], acc[a][1]);
+            }
+        }
+        __syncthreads();
+        p ^= 1;
+        // P3: S = diag(2^G_last) S + Kb^T X; the next chunk's W is copied in meanwhile.
+        if (c + 1 < nch) {
+            const float *rn = recp(c + 1);
+            stage(Bf(p ^ 1), rn + R.wt, dk * C);
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                const float2 r = *reinterpret_cast<const float2 *>(rn + R.u + (size_t)(4 * ty + a) * dv + j0 + 2 * tx);
+                u[a][0] = r.x;
+                u[a][1] = r.y;
+            }
+        }
+        cp_commit();
+        cp_wait1();
+        __syncthreads();
+        {
+            const float *Kb = Bf(p);
+            const int i0 = 8 * ty;
+            if (i0 < dk) {
+                float acc[8][2];
+#pragma unroll
+                for (int a = 0; a < 8; a++) {
+                    const float2 s2 = *reinterpret_cast<const float2 *>(Sb + (i0 + a) * DVB + 2 * tx);
+                    acc[a][0] = gs[i0 + a] * s2.x;
+                    acc[a][1] = gs[i0 + a] * s2.y;
+                }
+#pragma unroll 4
+                for (int s = 0; s < C; s++) {
+                    const float4 k0 = ld4(Kb + s * dk + i0), k1 = ld4(Kb + s * dk + i0 + 4);
+                    const float2 x2 = *reinterpret_cast<const float2 *>(Xs + s * DVB + 2 * tx);
+#pragma unroll
+                    for (int a = 0; a < 4; a++) {
+                        acc[a][0] = fmaf(at4(k0, a), x2.x, acc[a][0]);
+                        acc[a][1] = fmaf(at4(k0, a), x2.y, acc[a][1]);
+                        acc[a + 4][0] = fmaf(at4(k1, a), x2.x, acc[a + 4][0]);
+                        acc[a + 4][1] = fmaf(at4(k1, a), x2.y, acc[a + 4][1]);
+                    }
+                }
+#pragma unroll
+                for (int a = 0; a < 8; a++)
+                    *reinterpret_cast<float2 *>(Sb + (i0 + a) * DVB + 2 * tx) = make_float2(acc[a][0], acc[a][1]);
+            }
+        }
+        __syncthreads();
+        p ^= 1;
+    }
+    cp_wait0();
+    for (int e = tid; e < dk * (DVB / 4); e += THREADS) {
+        const int i = e / (DVB / 4), j = (e - i * (DVB / 4)) * 4;
+        *reinterpret_cast<float4 *>(Sh + (size_t)i * dv + j0 + j) = ld4(Sb + i * DVB + j);
+    }
+}
+
+}  // namespace kdc
+
+// Chunked prefill: dk a multiple of 8 up to 128, dv a multiple of 32 up to 128, 16-byte
+// aligned S and o. Segments of SEG chunks: prep then scan, the records in scratch slot 2.
+int kda_chunked(float *S, float *o, const float *q, const float *k, const float *v,
+                const float *alpha, const float *beta, int T, int H, int dk, int dv,
+                cudaStream_t st)
+{
+    using namespace kdc;
+    if (T <= 0 || H <= 0) return K3D_OK;
+    if (dk < 8 || dk > DKM || dk % 8 || dv < DVB || dv > 128 || dv % DVB)
+        return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: dk %d (8..128, multiple of 8), "
+                                "dv %d (32..128, multiple of 32)", dk, dv);
+    if (((uintptr_t)S | (uintptr_t)o) & 15u)
+        return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: S and o must be 16-byte aligned");
+    static bool init = false;
+    if (!init) {
+        allow_smem_max(k_kda_chunk_prep);
+        allow_smem_max(k_kda_chunk_scan);
+        init = true;
+    }
+    const Rec R = rec(dk, dv);
+    const int nch = (T + C - 1) / C;
+    const int seg = nch < SEG ? nch : SEG;
+    float *ws = (float *)scratch((size_t)seg * H * R.total * sizeof(float), 2);
+    if (!ws) return fail(K3D_ENOMEM, "k3d_kda_prefill: chunk records");
+    for (int c0 = 0; c0 < nch; c0 += seg) {
+        const int n = nch - c0 < seg ? nch - c0 : seg;
+        const long tok0 = (long)c0 * C;
+        k_kda_chunk_prep<<<dim3(n, H), THREADS, prep_smem(), st>>>(q, k, v, alpha, beta, ws, tok0,
+                                                                    T, H, dk, dv);
+        note_launch();
+        K3_TRY(check_launch("kda chunk prep"));
+        k_kda_chunk_scan<<<dim3(H, dv / DVB), THREADS, scan_smem(), st>>>(S, o, ws, tok0, n, T, H,
+                                                                           dk, dv);
+        note_launch();
+        K3_TRY(check_launch("kda chunk scan"));
+    }
+    return K3D_OK;
+}
+
 }  // namespace k3
 
 using namespace k3;
@@ -193,8 +633,9 @@ int k3d_kda_prefill(float *S, float *o, const float *q, const float *k, const fl
     K3_TRY(ensure_ctx());
     if (!S || !o || !q || !k || !v || !alpha || !beta)
         return fail(K3D_EINVAL, "k3d_kda_prefill null pointer");
+    if (chunk == 64) return kda_chunked(S, o, q, k, v, alpha, beta, T, H, dk, dv, stream());
     if (chunk != 0)
-        return fail(K3D_EUNSUPPORTED, "k3d_kda_prefill: chunked form not built yet (chunk=%d)", chunk);
+        return fail(K3D_EINVAL, "k3d_kda_prefill: chunk %d (0 sequential, 64 chunked)", chunk);
     return kda_seq(S, o, q, k, v, alpha, beta, T, H, dk, dv, stream());
 }
 
