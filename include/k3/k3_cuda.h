@@ -226,7 +226,7 @@ int k3d_kda_decode(float *S, float *o, const float *q, const float *k, const flo
  * chunk = 64 runs the chunked (WY) form: the same recurrence regrouped into 64-step
  * chunks, equal to the sequential result within fp32 rounding (decays in [0, 1]; a decay
  * of 0 acts as 2^-126). It needs dk a multiple of 8 up to 128, dv a multiple of 32 up to
- * 128, and 16-byte aligned S and o; its per-chunk records use library scratch
+ * 128, and 16-byte aligned S, o, q, k and alpha; its per-chunk records use library scratch
  * (about 148 KB per (chunk, head) at dk = dv = 128, for at most 8 chunks at a time).
  * Other chunk values return K3D_EINVAL. */
 int k3d_kda_prefill(float *S, float *o, const float *q, const float *k, const float *v,

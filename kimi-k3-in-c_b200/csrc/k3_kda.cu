@@ -208,133 +208,173 @@ __device__ __forceinline__ float at4(const float4 &v, int a)
     return a == 0 ? v.x : a == 1 ? v.y : a == 2 ? v.z : v.w;
 }
 
-constexpr size_t prep_smem()
-{
-    return (3 * (size_t)DKM * LDT + (size_t)C * 128 + (size_t)C * C + C) * sizeof(float);
-}
+constexpr size_t prep_smem() { return (3 * (size_t)DKM * LDT + C) * sizeof(float); }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__device__ __forceinline__ float4 ldg4(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+
+__global__ void __launch_bounds__(THREADS, 2)
 k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
                  const float *__restrict__ v, const float *__restrict__ alpha,
                  const float *__restrict__ beta, float *__restrict__ ws, long tok0, int T, int H,
                  int dk, int dv)
 {
     extern __shared__ __align__(16) float sh[];
-    float *kT = sh;                          // k, then 2^G k on the product path [dk][LDT]
-    float *qT = kT + DKM * LDT;              // q, then 2^G q
-    float *gT = qT + DKM * LDT;              // alpha, then G, then 2^-G k
-    float *vs = gT + DKM * LDT;              // v [C][dv]
-    float *Ls = vs + C * 128;                // L [C][C]
-    float *bs = Ls + C * C;                  // beta [C]
+    float *kT = sh;                          // k, then 2^G k                      [dk][LDT]
+    float *qT = kT + DKM * LDT;              // q, then 2^G q on the product path
+    float *gT = qT + DKM * LDT;              // decay, then G, then 2^-G k, then L [C][C]
+    float *bs = gT + DKM * LDT;              // beta [C]
     const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     const long tc0 = tok0 + (long)c * C;
     const int cn = (int)min((long)C, (long)T - tc0);
     const Rec R = rec(dk, dv);
     float *out = ws + ((size_t)c * H + h) * R.total;
 
-    // Padded steps (t >= cn) are identities: k = q = v = 0, decay 1, beta 0.
-    for (int e = tid; e < C * dk; e += THREADS) {
-        const int t = e / dk, i = e - t * dk;
-        float kv = 0.0f, qv = 0.0f, av = 1.0f;
-        if (t < cn) {
-            const size_t g = ((size_t)(tc0 + t) * H + h) * dk + i;
-            kv = k[g];
-            qv = q[g];
-            av = alpha[g];
+    // k, q and the decay, transposed to [i][t]: a warp pass covers 16 steps x 8 channels
+    // (two float4 per step), which lands on 32 distinct banks. All loads of a half are
+    // issued before its stores. Padded steps (t >= cn) are identities: k = q = 0, decay 1.
+    {
+        const int tl = lane & 15, ih = (lane >> 4) * 4;
+        const int nb = dk / 2;               // (16-step group, 8-channel group) pairs
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            float4 kr[4], qr[4], ar[4];
+#pragma unroll
+            for (int n = 0; n < 4; n++) {
+                const int b = warp + 8 * (4 * half + n);
+                const int t = (b & 3) * 16 + tl, i = (b >> 2) * 8 + ih;
+                kr[n] = qr[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+                ar[n] = make_float4(1.f, 1.f, 1.f, 1.f);
+                if (b < nb && t < cn) {
+                    const size_t g = ((size_t)(tc0 + t) * H + h) * dk + i;
+                    kr[n] = ldg4(k + g);
+                    qr[n] = ldg4(q + g);
+                    ar[n] = ldg4(alpha + g);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < 4; n++) {
+                const int b = warp + 8 * (4 * half + n);
+                if (b < nb) {
+                    const int t = (b & 3) * 16 + tl, i = (b >> 2) * 8 + ih;
+#pragma unroll
+                    for (int a = 0; a < 4; a++) {
+                        kT[(i + a) * LDT + t] = at4(kr[n], a);
+                        qT[(i + a) * LDT + t] = at4(qr[n], a);
+                        gT[(i + a) * LDT + t] = at4(ar[n], a);
+                    }
+                }
+            }
         }
-        kT[i * LDT + t] = kv;
-        qT[i * LDT + t] = qv;
-        gT[i * LDT + t] = av;
-    }
-    for (int e = tid; e < C * dv; e += THREADS) {
-        const int t = e / dv, j = e - t * dv;
-        vs[e] = t < cn ? v[((size_t)(tc0 + t) * H + h) * dv + j] : 0.0f;
     }
     if (tid < C) bs[tid] = tid < cn ? beta[(size_t)(tc0 + tid) * H + h] : 0.0f;
     __syncthreads();
 
+    // Cumulative log2 decay per channel (float4 along t: conflict-free).
     bool big = false;
     if (tid < dk) {
         float g = 0.0f;
-        for (int t = 0; t < C; t++) {
-            g += fmaxf(log2f(gT[tid * LDT + t]), -126.0f);
-            gT[tid * LDT + t] = g;
-            big |= !(fabsf(g) <= 60.0f);
+        float *row = gT + tid * LDT;
+#pragma unroll 4
+        for (int t = 0; t < C; t += 4) {
+            float4 a = ld4(row + t);
+            g += fmaxf(log2f(a.x), -126.0f); a.x = g;
+            g += fmaxf(log2f(a.y), -126.0f); a.y = g;
+            g += fmaxf(log2f(a.z), -126.0f); a.z = g;
+            g += fmaxf(log2f(a.w), -126.0f); a.w = g;
+            st4(row + t, a);
+            big |= !(fabsf(a.x) <= 60.0f && fabsf(a.w) <= 60.0f && fabsf(a.y) <= 60.0f &&
+                     fabsf(a.z) <= 60.0f);
         }
         out[R.gc + tid] = exp2f(g);
     }
     const bool direct = __syncthreads_or(big);
 
-    for (int e = tid; e < C * dk; e += THREADS) {
-        const int s = e / dk, i = e - s * dk;
-        out[R.kb + e] = kT[i * LDT + s] * exp2f(gT[i * LDT + C - 1] - gT[i * LDT + s]);
+    // Kb [s][i] = 2^(G_last - G_s) k_s and Qt^T [i][t] = 2^G_t q_t, read as float4 along t.
+    for (int e = tid; e < dk * (C / 4); e += THREADS) {
+        const int i = e % dk, s = (e / dk) * 4;
+        const float gl = gT[i * LDT + C - 1];
+        const float4 kk = ld4(kT + i * LDT + s), gg = ld4(gT + i * LDT + s);
+        float *o = out + R.kb + (size_t)s * dk + i;
+        o[0] = kk.x * exp2f(gl - gg.x);
+        o[dk] = kk.y * exp2f(gl - gg.y);
+        o[2 * dk] = kk.z * exp2f(gl - gg.z);
+        o[3 * dk] = kk.w * exp2f(gl - gg.w);
     }
-    for (int e = tid; e < dk * C; e += THREADS) {
-        const int i = e / C, t = e - i * C;
-        out[R.qt + e] = qT[i * LDT + t] * exp2f(gT[i * LDT + t]);
+    for (int e = tid; e < dk * (C / 4); e += THREADS) {
+        const int i = e / (C / 4), t = (e % (C / 4)) * 4;
+        const float4 qq = ld4(qT + i * LDT + t), gg = ld4(gT + i * LDT + t);
+        st4(out + R.qt + (size_t)i * C + t,
+            make_float4(qq.x * exp2f(gg.x), qq.y * exp2f(gg.y), qq.z * exp2f(gg.z), qq.w * exp2f(gg.w)));
     }
     if (!direct) {
         __syncthreads();
-        for (int e = tid; e < dk * C; e += THREADS) {
-            const int i = e / C, t = e - i * C;
-            const float g = gT[i * LDT + t], kk = kT[i * LDT + t];
-            kT[i * LDT + t] = kk * exp2f(g);
-            qT[i * LDT + t] *= exp2f(g);
-            gT[i * LDT + t] = kk * exp2f(-g);
+        for (int e = tid; e < dk * (C / 4); e += THREADS) {
+            const int i = e / (C / 4), t = (e % (C / 4)) * 4;
+            const float4 k0 = ld4(kT + i * LDT + t), gg = ld4(gT + i * LDT + t);
+            float4 qq = ld4(qT + i * LDT + t), kk, n;
+            float p;
+            p = exp2f(gg.x); kk.x = k0.x * p; qq.x *= p; n.x = k0.x * exp2f(-gg.x);
+            p = exp2f(gg.y); kk.y = k0.y * p; qq.y *= p; n.y = k0.y * exp2f(-gg.y);
+            p = exp2f(gg.z); kk.z = k0.z * p; qq.z *= p; n.z = k0.z * exp2f(-gg.z);
+            p = exp2f(gg.w); kk.w = k0.w * p; qq.w *= p; n.w = k0.w * exp2f(-gg.w);
+            st4(kT + i * LDT + t, kk);
+            st4(qT + i * LDT + t, qq);
+            st4(gT + i * LDT + t, n);
         }
     }
     __syncthreads();
 
-    // L and M in 4x4 tiles: thread (bt, bsb) owns t = 4bt.., s = 4bsb..; tiles above the
-    // diagonal are written as zeros.
-    {
-        const int bt = tid >> 4, bsb = tid & 15;
-        float La[4][4], Ma[4][4];
+    // L and M over the 136 lower-triangular 4x4 tiles, one per thread of the first 136:
+    // thread (bt, bsb) owns t = 4bt.., s = 4bsb.. with bsb <= bt.
+    float La[4][4], Ma[4][4];
 #pragma unroll
-        for (int a = 0; a < 4; a++)
+    for (int a = 0; a < 4; a++)
 #pragma unroll
-            for (int b = 0; b < 4; b++) La[a][b] = Ma[a][b] = 0.0f;
-        if (bsb <= bt) {
-            if (!direct) {
-                for (int i = 0; i < dk; i++) {
-                    const float4 kt = ld4(kT + i * LDT + 4 * bt), qt = ld4(qT + i * LDT + 4 * bt);
-                    const float4 ns = ld4(gT + i * LDT + 4 * bsb);
+        for (int b = 0; b < 4; b++) La[a][b] = Ma[a][b] = 0.0f;
+    int bt = 0;
+    while ((bt + 1) * (bt + 2) / 2 <= tid) bt++;
+    const int bsb = tid - bt * (bt + 1) / 2;
+    const bool tile = tid < (C / 4) * (C / 4 + 1) / 2;
+    if (tile) {
+        if (!direct) {
+#pragma unroll 2
+            for (int i = 0; i < dk; i++) {
+                const float4 kt = ld4(kT + i * LDT + 4 * bt), qt = ld4(qT + i * LDT + 4 * bt);
+                const float4 ns = ld4(gT + i * LDT + 4 * bsb);
+                const float2 n01 = make_float2(ns.x, ns.y), n23 = make_float2(ns.z, ns.w);
 #pragma unroll
-                    for (int a = 0; a < 4; a++)
-#pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            La[a][b] = fmaf(at4(kt, a), at4(ns, b), La[a][b]);
-                            Ma[a][b] = fmaf(at4(qt, a), at4(ns, b), Ma[a][b]);
-                        }
-                }
-            } else {
-                for (int i = 0; i < dk; i++) {
-                    const float4 gt = ld4(gT + i * LDT + 4 * bt), gs = ld4(gT + i * LDT + 4 * bsb);
-                    const float4 kt = ld4(kT + i * LDT + 4 * bt), ks = ld4(kT + i * LDT + 4 * bsb);
-                    const float4 qt = ld4(qT + i * LDT + 4 * bt);
-#pragma unroll
-                    for (int a = 0; a < 4; a++)
-#pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            if (bsb < bt || b <= a) {
-                                const float kse = at4(ks, b) * exp2f(at4(gt, a) - at4(gs, b));
-                                La[a][b] = fmaf(at4(kt, a), kse, La[a][b]);
-                                Ma[a][b] = fmaf(at4(qt, a), kse, Ma[a][b]);
-                            }
-                        }
+                for (int a = 0; a < 4; a++) {
+                    const float2 ka = make_float2(at4(kt, a), at4(kt, a));
+                    const float2 qa = make_float2(at4(qt, a), at4(qt, a));
+                    float2 l01 = ffma2(ka, n01, make_float2(La[a][0], La[a][1]));
+                    float2 l23 = ffma2(ka, n23, make_float2(La[a][2], La[a][3]));
+                    float2 m01 = ffma2(qa, n01, make_float2(Ma[a][0], Ma[a][1]));
+                    float2 m23 = ffma2(qa, n23, make_float2(Ma[a][2], Ma[a][3]));
+                    La[a][0] = l01.x; La[a][1] = l01.y; La[a][2] = l23.x; La[a][3] = l23.y;
+                    Ma[a][0] = m01.x; Ma[a][1] = m01.y; Ma[a][2] = m23.x; Ma[a][3] = m23.y;
                 }
             }
-        }
+        } else {
+            for (int i = 0; i < dk; i++) {
+                const float4 gt = ld4(gT + i * LDT + 4 * bt), gs = ld4(gT + i * LDT + 4 * bsb);
+                const float4 kt = ld4(kT + i * LDT + 4 * bt), ks = ld4(kT + i * LDT + 4 * bsb);
+                const float4 qt = ld4(qT + i * LDT + 4 * bt);
 #pragma unroll
-        for (int a = 0; a < 4; a++) {
-            const int t = 4 * bt + a;
-            float4 r;
-            r.x = t > 4 * bsb + 0 ? La[a][0] : 0.0f;
-            r.y = t > 4 * bsb + 1 ? La[a][1] : 0.0f;
-            r.z = t > 4 * bsb + 2 ? La[a][2] : 0.0f;
-            r.w = t > 4 * bsb + 3 ? La[a][3] : 0.0f;
-            *reinterpret_cast<float4 *>(Ls + t * C + 4 * bsb) = r;
+                for (int a = 0; a < 4; a++)
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        if (bsb < bt || b <= a) {
+                            const float kse = at4(ks, b) * exp2f(at4(gt, a) - at4(gs, b));
+                            La[a][b] = fmaf(at4(kt, a), kse, La[a][b]);
+                            Ma[a][b] = fmaf(at4(qt, a), kse, Ma[a][b]);
+                        }
+                    }
+            }
         }
+        // M^T [s][t], zero above the diagonal inside the diagonal tile (the scan reads
+        // M^T[s][t] for s up to the end of t's 4-row tile).
 #pragma unroll
         for (int b = 0; b < 4; b++) {
             const int s = 4 * bsb + b;
@@ -343,37 +383,74 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
             r.y = 4 * bt + 1 >= s ? Ma[1][b] : 0.0f;
             r.z = 4 * bt + 2 >= s ? Ma[2][b] : 0.0f;
             r.w = 4 * bt + 3 >= s ? Ma[3][b] : 0.0f;
-            *reinterpret_cast<float4 *>(out + R.mt + (size_t)s * C + 4 * bt) = r;
+            st4(out + R.mt + (size_t)s * C + 4 * bt, r);
+        }
+    }
+    __syncthreads();
+    if (direct) {
+        for (int e = tid; e < dk * (C / 4); e += THREADS) {
+            const int i = e / (C / 4), t = (e % (C / 4)) * 4;
+            float4 kk = ld4(kT + i * LDT + t);
+            const float4 gg = ld4(gT + i * LDT + t);
+            kk.x *= exp2f(gg.x); kk.y *= exp2f(gg.y); kk.z *= exp2f(gg.z); kk.w *= exp2f(gg.w);
+            st4(kT + i * LDT + t, kk);
+        }
+        __syncthreads();
+    }
+    // -L (strictly lower; the substitution reads nothing else) into the G region.
+    float *Ls = gT;
+    if (tile) {
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+            const int t = 4 * bt + a;
+            float4 r;
+            r.x = t > 4 * bsb + 0 ? -La[a][0] : 0.0f;
+            r.y = t > 4 * bsb + 1 ? -La[a][1] : 0.0f;
+            r.z = t > 4 * bsb + 2 ? -La[a][2] : 0.0f;
+            r.w = t > 4 * bsb + 3 ? -La[a][3] : 0.0f;
+            st4(Ls + t * C + 4 * bsb, r);
         }
     }
     __syncthreads();
 
     // Forward substitution, one thread per right-hand-side column: columns < dv are
-    // beta*V (giving U), the next dk columns beta*Kt (giving W).
+    // beta*V (giving U, V read straight from global), the next dk columns beta*Kt (W).
     const int col = tid;
     if (col < dv + dk) {
         const bool isv = col < dv;
         const int i = col - dv;
         float x[C];
+        if (isv) {
 #pragma unroll
-        for (int t = 0; t < C; t++) {
-            if (isv) x[t] = vs[t * dv + col];
-            else x[t] = direct ? kT[i * LDT + t] * exp2f(gT[i * LDT + t]) : kT[i * LDT + t];
+            for (int t = 0; t < C; t++)
+                x[t] = t < cn ? __ldg(v + ((size_t)(tc0 + t) * H + h) * dv + col) : 0.0f;
+        } else {
+#pragma unroll
+            for (int t = 0; t < C; t += 4) {
+                const float4 kk = ld4(kT + i * LDT + t);
+                x[t] = kk.x; x[t + 1] = kk.y; x[t + 2] = kk.z; x[t + 3] = kk.w;
+            }
         }
 #pragma unroll
         for (int t = 0; t < C; t++) {
-            float acc = x[t];
+            float2 p0 = make_float2(x[t], 0.0f), p1 = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int s = 0; s < t; s++) acc = fmaf(-Ls[t * C + s], x[s], acc);
-            x[t] = bs[t] * acc;
+            for (int s = 0; s + 3 < t; s += 4) {
+                const float4 l = ld4(Ls + t * C + s);
+                p0 = ffma2(make_float2(l.x, l.y), make_float2(x[s], x[s + 1]), p0);
+                p1 = ffma2(make_float2(l.z, l.w), make_float2(x[s + 2], x[s + 3]), p1);
+            }
+#pragma unroll
+            for (int s = t & ~3; s < t; s++) p0.x = fmaf(Ls[t * C + s], x[s], p0.x);
+            x[t] = bs[t] * ((p0.x + p0.y) + (p1.x + p1.y));
         }
         if (isv) {
 #pragma unroll
             for (int t = 0; t < C; t++) out[R.u + (size_t)t * dv + col] = x[t];
         } else {
-            float4 *w4 = reinterpret_cast<float4 *>(out + R.wt + (size_t)i * C);
 #pragma unroll
-            for (int t = 0; t < C; t += 4) w4[t / 4] = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+            for (int t = 0; t < C; t += 4)
+                st4(out + R.wt + (size_t)i * C + t, make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]));
         }
     }
 }
@@ -397,10 +474,13 @@ constexpr size_t scan_smem()
            sizeof(float);
 }
 
+// DKC = 128 compiles the key dimension in (the config-3 head); DKC = 0 reads it from dk.
+template <int DKC>
 __global__ void __launch_bounds__(THREADS, 2)
 k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__restrict__ ws,
-                 long tok0, int nch, int T, int H, int dk, int dv)
+                 long tok0, int nch, int T, int H, int dk_, int dv)
 {
+    const int dk = DKC ? DKC : dk_;
     extern __shared__ __align__(16) float sh[];
     float *Sb = sh;                          // state block [dk][DVB]
     float *Xs = Sb + DKM * DVB;              // X [C][DVB]
@@ -442,22 +522,22 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
         __syncthreads();
         {
             const float *W = Bf(p);
-            float acc[4][2];
+            float2 acc[4];
 #pragma unroll
-            for (int a = 0; a < 4; a++) acc[a][0] = u[a][0], acc[a][1] = u[a][1];
-#pragma unroll 4
+            for (int a = 0; a < 4; a++) acc[a] = make_float2(u[a][0], u[a][1]);
+#pragma unroll 16
             for (int i = 0; i < dk; i++) {
                 const float4 w = ld4(W + i * C + 4 * ty);
                 const float2 s2 = *reinterpret_cast<const float2 *>(Sb + i * DVB + 2 * tx);
 #pragma unroll
                 for (int a = 0; a < 4; a++) {
-                    acc[a][0] = fmaf(-at4(w, a), s2.x, acc[a][0]);
-                    acc[a][1] = fmaf(-at4(w, a), s2.y, acc[a][1]);
+                    const float nw = -at4(w, a);
+                    acc[a] = ffma2(make_float2(nw, nw), s2, acc[a]);
                 }
             }
 #pragma unroll
             for (int a = 0; a < 4; a++)
-                *reinterpret_cast<float2 *>(Xs + (4 * ty + a) * DVB + 2 * tx) = make_float2(acc[a][0], acc[a][1]);
+                *reinterpret_cast<float2 *>(Xs + (4 * ty + a) * DVB + 2 * tx) = acc[a];
         }
         __syncthreads();
         p ^= 1;
@@ -469,15 +549,16 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
         __syncthreads();
         {
             const float *Q = Bf(p);
-            float acc[4][2] = {};
-#pragma unroll 4
+            float2 acc[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) acc[a] = make_float2(0.0f, 0.0f);
+#pragma unroll 16
             for (int i = 0; i < dk; i++) {
                 const float4 w = ld4(Q + i * C + 4 * ty);
                 const float2 s2 = *reinterpret_cast<const float2 *>(Sb + i * DVB + 2 * tx);
 #pragma unroll
                 for (int a = 0; a < 4; a++) {
-                    acc[a][0] = fmaf(at4(w, a), s2.x, acc[a][0]);
-                    acc[a][1] = fmaf(at4(w, a), s2.y, acc[a][1]);
+                    acc[a] = ffma2(make_float2(at4(w, a), at4(w, a)), s2, acc[a]);
                 }
             }
             for (int s = 0; s < 4 * ty + 4; s++) {
@@ -485,8 +566,7 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
                 const float2 x2 = *reinterpret_cast<const float2 *>(Xs + s * DVB + 2 * tx);
 #pragma unroll
                 for (int a = 0; a < 4; a++) {
-                    acc[a][0] = fmaf(at4(m, a), x2.x, acc[a][0]);
-                    acc[a][1] = fmaf(at4(m, a), x2.y, acc[a][1]);
+                    acc[a] = ffma2(make_float2(at4(m, a), at4(m, a)), x2, acc[a]);
                 }
             }
             const long tc0 = tok0 + (long)c * C;
@@ -494,8 +574,7 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
             for (int a = 0; a < 4; a++) {
                 const long t = tc0 + 4 * ty + a;
                 if (t < T)
-                    *reinterpret_cast<float2 *>(o + ((size_t)t * H + h) * dv + j0 + 2 * tx) =
-                        make_float2(acc[a][0], acc[a][1]);
+                    *reinterpret_cast<float2 *>(o + ((size_t)t * H + h) * dv + j0 + 2 * tx) = acc[a];
             }
         }
         __syncthreads();
@@ -518,28 +597,25 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
             const float *Kb = Bf(p);
             const int i0 = 8 * ty;
             if (i0 < dk) {
-                float acc[8][2];
+                float2 acc[8];
 #pragma unroll
                 for (int a = 0; a < 8; a++) {
                     const float2 s2 = *reinterpret_cast<const float2 *>(Sb + (i0 + a) * DVB + 2 * tx);
-                    acc[a][0] = gs[i0 + a] * s2.x;
-                    acc[a][1] = gs[i0 + a] * s2.y;
+                    acc[a] = make_float2(gs[i0 + a] * s2.x, gs[i0 + a] * s2.y);
                 }
-#pragma unroll 4
+#pragma unroll 16
                 for (int s = 0; s < C; s++) {
                     const float4 k0 = ld4(Kb + s * dk + i0), k1 = ld4(Kb + s * dk + i0 + 4);
                     const float2 x2 = *reinterpret_cast<const float2 *>(Xs + s * DVB + 2 * tx);
 #pragma unroll
                     for (int a = 0; a < 4; a++) {
-                        acc[a][0] = fmaf(at4(k0, a), x2.x, acc[a][0]);
-                        acc[a][1] = fmaf(at4(k0, a), x2.y, acc[a][1]);
-                        acc[a + 4][0] = fmaf(at4(k1, a), x2.x, acc[a + 4][0]);
-                        acc[a + 4][1] = fmaf(at4(k1, a), x2.y, acc[a + 4][1]);
+                        acc[a] = ffma2(make_float2(at4(k0, a), at4(k0, a)), x2, acc[a]);
+                        acc[a + 4] = ffma2(make_float2(at4(k1, a), at4(k1, a)), x2, acc[a + 4]);
                     }
                 }
 #pragma unroll
                 for (int a = 0; a < 8; a++)
-                    *reinterpret_cast<float2 *>(Sb + (i0 + a) * DVB + 2 * tx) = make_float2(acc[a][0], acc[a][1]);
+                    *reinterpret_cast<float2 *>(Sb + (i0 + a) * DVB + 2 * tx) = acc[a];
             }
         }
         __syncthreads();
@@ -555,7 +631,7 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
 }  // namespace kdc
 
 // Chunked prefill: dk a multiple of 8 up to 128, dv a multiple of 32 up to 128, 16-byte
-// aligned S and o. Segments of SEG chunks: prep then scan, the records in scratch slot 2.
+// aligned S, o, q, k and alpha. Segments of SEG chunks: prep then scan, the records in scratch slot 2.
 int kda_chunked(float *S, float *o, const float *q, const float *k, const float *v,
                 const float *alpha, const float *beta, int T, int H, int dk, int dv,
                 cudaStream_t st)
@@ -565,12 +641,13 @@ int kda_chunked(float *S, float *o, const float *q, const float *k, const float 
     if (dk < 8 || dk > DKM || dk % 8 || dv < DVB || dv > 128 || dv % DVB)
         return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: dk %d (8..128, multiple of 8), "
                                 "dv %d (32..128, multiple of 32)", dk, dv);
-    if (((uintptr_t)S | (uintptr_t)o) & 15u)
-        return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: S and o must be 16-byte aligned");
+    if (((uintptr_t)S | (uintptr_t)o | (uintptr_t)q | (uintptr_t)k | (uintptr_t)alpha) & 15u)
+        return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: S, o, q, k and alpha must be 16-byte aligned");
     static bool init = false;
     if (!init) {
         allow_smem_max(k_kda_chunk_prep);
-        allow_smem_max(k_kda_chunk_scan);
+        allow_smem_max(k_kda_chunk_scan<128>);
+        allow_smem_max(k_kda_chunk_scan<0>);
         init = true;
     }
     const Rec R = rec(dk, dv);
@@ -585,8 +662,12 @@ int kda_chunked(float *S, float *o, const float *q, const float *k, const float 
                                                                     T, H, dk, dv);
         note_launch();
         K3_TRY(check_launch("kda chunk prep"));
-        k_kda_chunk_scan<<<dim3(H, dv / DVB), THREADS, scan_smem(), st>>>(S, o, ws, tok0, n, T, H,
-                                                                           dk, dv);
+        if (dk == 128)
+            k_kda_chunk_scan<128><<<dim3(H, dv / DVB), THREADS, scan_smem(), st>>>(S, o, ws, tok0, n,
+                                                                                T, H, dk, dv);
+        else
+            k_kda_chunk_scan<0><<<dim3(H, dv / DVB), THREADS, scan_smem(), st>>>(S, o, ws, tok0, n,
+                                                                              T, H, dk, dv);
         note_launch();
         K3_TRY(check_launch("kda chunk scan"));
     }

@@ -100,3 +100,8 @@ def test_kda_prefill_rejects_other_chunks_and_shapes(k3):
                                 bufs[4].ptr, bufs[5].ptr, 8, 1, dk, dv, chunk)
         assert rc == k3cuda.K3D_EINVAL
         k3.k3d_clear_status()
+    # q, k and the decay are read as float4 rows: a pointer off a 16-byte boundary is refused
+    rc = k3.k3d_kda_prefill(bufs[0].ptr, O.ptr, bufs[1].ptr + 4, bufs[2].ptr, bufs[3].ptr,
+                            bufs[4].ptr, bufs[5].ptr, 4, 1, 128, 128, 64)
+    assert rc == k3cuda.K3D_EINVAL
+    k3.k3d_clear_status()
