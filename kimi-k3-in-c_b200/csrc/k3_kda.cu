@@ -174,8 +174,9 @@ int kda_seq(float *S, float *o, const float *q, const float *k, const float *v,
 // otherwise (strong decay) each pair takes its own exponential. log2 of a decay is clamped
 // at -126, so a decay of exactly 0 acts as 2^-126.
 // k_kda_chunk_scan, one CTA per (head, 32 value columns): walks the chunks in order with
-// the state block in shared memory; per chunk X = U - W S, O = Qt S + M X, S = g S + Kb^T X.
-// The next phase's operand is copied in (cp.async) while the current phase computes.
+// the state block in shared memory; per chunk X = U - W S, O = Qt S + M X, S = g S + Kb^T X,
+// each product on the tensor cores (mma.sync tf32, fp32 operands split in two, 3 MMAs per
+// step). The next phase's operand is copied in (cp.async) while the current phase computes.
 namespace kdc {
 
 constexpr int C = 64;            // steps per chunk
@@ -373,8 +374,7 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
                     }
             }
         }
-        // M^T [s][t], zero above the diagonal inside the diagonal tile (the scan reads
-        // M^T[s][t] for s up to the end of t's 4-row tile).
+        // M^T [s][t], zero above the diagonal inside the diagonal tile.
 #pragma unroll
         for (int b = 0; b < 4; b++) {
             const int s = 4 * bsb + b;
@@ -385,6 +385,15 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
             r.w = 4 * bt + 3 >= s ? Ma[3][b] : 0.0f;
             st4(out + R.mt + (size_t)s * C + 4 * bt, r);
         }
+    } else {
+        // the 120 tiles above the diagonal, one per remaining thread: zeros, since the
+        // scan's 16-row MMA tiles read M^T[s][t] for s up to the end of t's 16-row block
+        int j = tid - (C / 4) * (C / 4 + 1) / 2, ut = 0;
+        while (j >= C / 4 - 1 - ut) { j -= C / 4 - 1 - ut; ut++; }
+        const int us = ut + 1 + j;
+#pragma unroll
+        for (int b = 0; b < 4; b++)
+            st4(out + R.mt + (size_t)(4 * us + b) * C + 4 * ut, make_float4(0.f, 0.f, 0.f, 0.f));
     }
     __syncthreads();
     if (direct) {
@@ -468,6 +477,71 @@ __device__ __forceinline__ void stage(float *dst, const float *src, int nfloats)
     for (int f = threadIdx.x; f < nfloats / 4; f += THREADS) cp16(dst + 4 * f, src + 4 * f);
 }
 
+// tf32 helpers for the scan's products on the tensor cores (mma.sync m16n8k8, fp32
+// accumulate). Every fp32 operand x is split into big = tf32(x) and small = tf32(x - big),
+// and a product is accumulated as small*big + big*small + big*big ("3xTF32"): the dropped
+// small*small term is below 2^-21 of |a||b|, so the result carries fp32-class accuracy.
+__device__ __forceinline__ uint32_t to_tf32(float x)
+{
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small)
+{
+    big = to_tf32(x);
+    small = to_tf32(x - __uint_as_float(big));
+}
+
+__device__ __forceinline__ void mma_tf32(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// c += A B for one 16x8x8 step: A given as fp32 fragment values (split here), B as two.
+__device__ __forceinline__ void mma3(float c[4], const uint32_t ab[4], const uint32_t as[4], float b0f, float b1f)
+{
+    uint32_t bb0, bs0, bb1, bs1;
+    split_tf32(b0f, bb0, bs0);
+    split_tf32(b1f, bb1, bs1);
+    mma_tf32(c, as, bb0, bb1);
+    mma_tf32(c, ab, bs0, bs1);
+    mma_tf32(c, ab, bb0, bb1);
+}
+
+// Shared-memory row swizzle: element n of row k sits at n ^ 8 (k mod 4) when the row width
+// is a multiple of 32, so the four K rows a fragment load touches land on distinct banks.
+__device__ __forceinline__ int swz(int k, int n, int width)
+{
+    return (width & 31) ? n : (n ^ ((k & 3) << 3));
+}
+
+// cp.async copy of a [rows][width] record block into the swizzled layout.
+__device__ __forceinline__ void stage_sw(float *dst, const float *src, int rows, int width)
+{
+    const int cpr = width / 4;
+    for (int f = threadIdx.x; f < rows * cpr; f += THREADS) {
+        const int r = f / cpr, c = f - r * cpr;
+        cp16(dst + r * width + swz(r, 4 * c, width), src + 4 * f);
+    }
+}
+
+// A fragment (16 rows m0.., 8 K rows k0..) of a matrix stored K-major as P[k][m] (row width
+// `width`, swizzled): a0 = A[g][q], a1 = A[g+8][q], a2 = A[g][q+4], a3 = A[g+8][q+4].
+__device__ __forceinline__ void frag_a(const float *P, int width, int k0, int m0, int g, int q,
+                                       uint32_t ab[4], uint32_t as[4])
+{
+    const int ka = k0 + q, kb = ka + 4;
+    split_tf32(P[ka * width + swz(ka, m0 + g, width)], ab[0], as[0]);
+    split_tf32(P[ka * width + swz(ka, m0 + g + 8, width)], ab[1], as[1]);
+    split_tf32(P[kb * width + swz(kb, m0 + g, width)], ab[2], as[2]);
+    split_tf32(P[kb * width + swz(kb, m0 + g + 8, width)], ab[3], as[3]);
+}
+
 constexpr size_t scan_smem()
 {
     return ((size_t)DKM * DVB + (size_t)C * DVB + 2 * (size_t)DKM * C + (size_t)C * C + DKM) *
@@ -475,6 +549,8 @@ constexpr size_t scan_smem()
 }
 
 // DKC = 128 compiles the key dimension in (the config-3 head); DKC = 0 reads it from dk.
+// Warps: in X and O, warp w owns rows 16 (w mod 4).. and columns 16 (w / 4).. (two 8-column
+// MMA tiles); in the state update, rows 16 w.. of the key dimension and all 32 columns.
 template <int DKC>
 __global__ void __launch_bounds__(THREADS, 2)
 k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__restrict__ ws,
@@ -482,99 +558,108 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
 {
     const int dk = DKC ? DKC : dk_;
     extern __shared__ __align__(16) float sh[];
-    float *Sb = sh;                          // state block [dk][DVB]
-    float *Xs = Sb + DKM * DVB;              // X [C][DVB]
-    float *const b0 = Xs + C * DVB, *const b1 = b0 + DKM * C;   // W^T / Qt^T / Kb
-    float *Ms = b1 + DKM * C;             // M^T [C][C]
+    float *Sb = sh;                          // state block [dk][DVB], swizzled
+    float *Xs = Sb + DKM * DVB;              // X [C][DVB], swizzled
+    float *const b0 = Xs + C * DVB, *const b1 = b0 + DKM * C;   // W^T / Qt^T / Kb, swizzled
+    float *Ms = b1 + DKM * C;                // M^T [C][C], swizzled
     float *gs = Ms + C * C;                  // 2^G_last [dk]
     const int h = blockIdx.x, j0 = blockIdx.y * DVB, tid = threadIdx.x;
-    const int ty = tid >> 4, tx = tid & 15;
+    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
+    const int t0 = 16 * (warp & 3), n0 = 16 * (warp >> 2);
     const Rec R = rec(dk, dv);
     float *Sh = S + (size_t)h * dk * dv;
     auto recp = [&](int c) { return ws + ((size_t)c * H + h) * R.total; };
     auto Bf = [&](int i) { return i ? b1 : b0; };
+    // U at this thread's X fragment: rows t0+g, t0+g+8; columns n0 + 8 nt + 2q, +1
+    float u[2][4];
+    auto load_u = [&](const float *U) {
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            const int col = j0 + n0 + 8 * nt + 2 * q;
+            const float2 r0 = *reinterpret_cast<const float2 *>(U + (size_t)(t0 + g) * dv + col);
+            const float2 r1 = *reinterpret_cast<const float2 *>(U + (size_t)(t0 + g + 8) * dv + col);
+            u[nt][0] = r0.x; u[nt][1] = r0.y; u[nt][2] = r1.x; u[nt][3] = r1.y;
+        }
+    };
 
     int p = 0;
-    stage(Bf(0), recp(0) + R.wt, dk * C);
+    stage_sw(Bf(0), recp(0) + R.wt, dk, C);
     cp_commit();
     for (int e = tid; e < dk * (DVB / 4); e += THREADS) {
         const int i = e / (DVB / 4), j = (e - i * (DVB / 4)) * 4;
-        *reinterpret_cast<float4 *>(Sb + i * DVB + j) = ld4(Sh + (size_t)i * dv + j0 + j);
+        *reinterpret_cast<float4 *>(Sb + i * DVB + swz(i, j, DVB)) = ld4(Sh + (size_t)i * dv + j0 + j);
     }
-    float u[4][2];
-    {
-        const float *U = recp(0) + R.u;
-#pragma unroll
-        for (int a = 0; a < 4; a++) {
-            const float2 r = *reinterpret_cast<const float2 *>(U + (size_t)(4 * ty + a) * dv + j0 + 2 * tx);
-            u[a][0] = r.x;
-            u[a][1] = r.y;
-        }
-    }
+    load_u(recp(0) + R.u);
 
     for (int c = 0; c < nch; c++) {
         const float *rc = recp(c);
         // P1: X = U - W S
-        stage(Bf(p ^ 1), rc + R.qt, dk * C);
-        stage(Ms, rc + R.mt, C * C);
+        stage_sw(Bf(p ^ 1), rc + R.qt, dk, C);
+        stage_sw(Ms, rc + R.mt, C, C);
         cp_commit();
         cp_wait1();
         __syncthreads();
         {
             const float *W = Bf(p);
-            float2 acc[4];
+            float acc[2][4] = {};
+#pragma unroll 4
+            for (int k0 = 0; k0 < dk; k0 += 8) {
+                uint32_t ab[4], as[4];
+                frag_a(W, C, k0, t0, g, q, ab, as);
 #pragma unroll
-            for (int a = 0; a < 4; a++) acc[a] = make_float2(u[a][0], u[a][1]);
-#pragma unroll 16
-            for (int i = 0; i < dk; i++) {
-                const float4 w = ld4(W + i * C + 4 * ty);
-                const float2 s2 = *reinterpret_cast<const float2 *>(Sb + i * DVB + 2 * tx);
-#pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    const float nw = -at4(w, a);
-                    acc[a] = ffma2(make_float2(nw, nw), s2, acc[a]);
+                for (int nt = 0; nt < 2; nt++) {
+                    const int n = n0 + 8 * nt + g, ka = k0 + q, kb = ka + 4;
+                    mma3(acc[nt], ab, as, Sb[ka * DVB + swz(ka, n, DVB)], Sb[kb * DVB + swz(kb, n, DVB)]);
                 }
             }
 #pragma unroll
-            for (int a = 0; a < 4; a++)
-                *reinterpret_cast<float2 *>(Xs + (4 * ty + a) * DVB + 2 * tx) = acc[a];
+            for (int nt = 0; nt < 2; nt++) {
+                const int col = n0 + 8 * nt + 2 * q, r0 = t0 + g, r1 = t0 + g + 8;
+                *reinterpret_cast<float2 *>(Xs + r0 * DVB + swz(r0, col, DVB)) =
+                    make_float2(u[nt][0] - acc[nt][0], u[nt][1] - acc[nt][1]);
+                *reinterpret_cast<float2 *>(Xs + r1 * DVB + swz(r1, col, DVB)) =
+                    make_float2(u[nt][2] - acc[nt][2], u[nt][3] - acc[nt][3]);
+            }
         }
         __syncthreads();
         p ^= 1;
-        // P2: O = Qt S + M X
-        stage(Bf(p ^ 1), rc + R.kb, C * dk);
+        // P2: O = Qt S + M X (M^T[s][t] is zero for s > t inside the diagonal 16x16 block)
+        stage_sw(Bf(p ^ 1), rc + R.kb, C, dk);
         stage(gs, rc + R.gc, (dk + 3) & ~3);
         cp_commit();
         cp_wait1();
         __syncthreads();
         {
             const float *Q = Bf(p);
-            float2 acc[4];
+            float acc[2][4] = {};
+#pragma unroll 4
+            for (int k0 = 0; k0 < dk; k0 += 8) {
+                uint32_t ab[4], as[4];
+                frag_a(Q, C, k0, t0, g, q, ab, as);
 #pragma unroll
-            for (int a = 0; a < 4; a++) acc[a] = make_float2(0.0f, 0.0f);
-#pragma unroll 16
-            for (int i = 0; i < dk; i++) {
-                const float4 w = ld4(Q + i * C + 4 * ty);
-                const float2 s2 = *reinterpret_cast<const float2 *>(Sb + i * DVB + 2 * tx);
-#pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    acc[a] = ffma2(make_float2(at4(w, a), at4(w, a)), s2, acc[a]);
+                for (int nt = 0; nt < 2; nt++) {
+                    const int n = n0 + 8 * nt + g, ka = k0 + q, kb = ka + 4;
+                    mma3(acc[nt], ab, as, Sb[ka * DVB + swz(ka, n, DVB)], Sb[kb * DVB + swz(kb, n, DVB)]);
                 }
             }
-            for (int s = 0; s < 4 * ty + 4; s++) {
-                const float4 m = ld4(Ms + s * C + 4 * ty);
-                const float2 x2 = *reinterpret_cast<const float2 *>(Xs + s * DVB + 2 * tx);
+            for (int k0 = 0; k0 < t0 + 16; k0 += 8) {
+                uint32_t ab[4], as[4];
+                frag_a(Ms, C, k0, t0, g, q, ab, as);
 #pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    acc[a] = ffma2(make_float2(at4(m, a), at4(m, a)), x2, acc[a]);
+                for (int nt = 0; nt < 2; nt++) {
+                    const int n = n0 + 8 * nt + g, ka = k0 + q, kb = ka + 4;
+                    mma3(acc[nt], ab, as, Xs[ka * DVB + swz(ka, n, DVB)], Xs[kb * DVB + swz(kb, n, DVB)]);
                 }
             }
             const long tc0 = tok0 + (long)c * C;
 #pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const long t = tc0 + 4 * ty + a;
-                if (t < T)
-                    *reinterpret_cast<float2 *>(o + ((size_t)t * H + h) * dv + j0 + 2 * tx) = acc[a];
+            for (int nt = 0; nt < 2; nt++) {
+                const int col = j0 + n0 + 8 * nt + 2 * q;
+                const long ta = tc0 + t0 + g, tb = ta + 8;
+                if (ta < T)
+                    *reinterpret_cast<float2 *>(o + ((size_t)ta * H + h) * dv + col) = make_float2(acc[nt][0], acc[nt][1]);
+                if (tb < T)
+                    *reinterpret_cast<float2 *>(o + ((size_t)tb * H + h) * dv + col) = make_float2(acc[nt][2], acc[nt][3]);
             }
         }
         __syncthreads();
@@ -582,40 +667,36 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
         // P3: S = diag(2^G_last) S + Kb^T X; the next chunk's W is copied in meanwhile.
         if (c + 1 < nch) {
             const float *rn = recp(c + 1);
-            stage(Bf(p ^ 1), rn + R.wt, dk * C);
-#pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const float2 r = *reinterpret_cast<const float2 *>(rn + R.u + (size_t)(4 * ty + a) * dv + j0 + 2 * tx);
-                u[a][0] = r.x;
-                u[a][1] = r.y;
-            }
+            stage_sw(Bf(p ^ 1), rn + R.wt, dk, C);
+            load_u(rn + R.u);
         }
         cp_commit();
         cp_wait1();
         __syncthreads();
         {
             const float *Kb = Bf(p);
-            const int i0 = 8 * ty;
+            const int i0 = 16 * warp;
             if (i0 < dk) {
-                float2 acc[8];
+                float acc[4][4] = {};
 #pragma unroll
-                for (int a = 0; a < 8; a++) {
-                    const float2 s2 = *reinterpret_cast<const float2 *>(Sb + (i0 + a) * DVB + 2 * tx);
-                    acc[a] = make_float2(gs[i0 + a] * s2.x, gs[i0 + a] * s2.y);
-                }
-#pragma unroll 16
-                for (int s = 0; s < C; s++) {
-                    const float4 k0 = ld4(Kb + s * dk + i0), k1 = ld4(Kb + s * dk + i0 + 4);
-                    const float2 x2 = *reinterpret_cast<const float2 *>(Xs + s * DVB + 2 * tx);
+                for (int k0 = 0; k0 < C; k0 += 8) {
+                    uint32_t ab[4], as[4];
+                    frag_a(Kb, dk, k0, i0, g, q, ab, as);
 #pragma unroll
-                    for (int a = 0; a < 4; a++) {
-                        acc[a] = ffma2(make_float2(at4(k0, a), at4(k0, a)), x2, acc[a]);
-                        acc[a + 4] = ffma2(make_float2(at4(k1, a), at4(k1, a)), x2, acc[a + 4]);
+                    for (int nt = 0; nt < 4; nt++) {
+                        const int n = 8 * nt + g, ka = k0 + q, kb = ka + 4;
+                        mma3(acc[nt], ab, as, Xs[ka * DVB + swz(ka, n, DVB)], Xs[kb * DVB + swz(kb, n, DVB)]);
                     }
                 }
 #pragma unroll
-                for (int a = 0; a < 8; a++)
-                    *reinterpret_cast<float2 *>(Sb + (i0 + a) * DVB + 2 * tx) = acc[a];
+                for (int nt = 0; nt < 4; nt++) {
+                    const int col = 8 * nt + 2 * q, r0 = i0 + g, r1 = i0 + g + 8;
+                    float2 *p0 = reinterpret_cast<float2 *>(Sb + r0 * DVB + swz(r0, col, DVB));
+                    float2 *p1 = reinterpret_cast<float2 *>(Sb + r1 * DVB + swz(r1, col, DVB));
+                    const float2 s0 = *p0, s1 = *p1;
+                    *p0 = make_float2(gs[r0] * s0.x + acc[nt][0], gs[r0] * s0.y + acc[nt][1]);
+                    *p1 = make_float2(gs[r1] * s1.x + acc[nt][2], gs[r1] * s1.y + acc[nt][3]);
+                }
             }
         }
         __syncthreads();
@@ -624,7 +705,7 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
     cp_wait0();
     for (int e = tid; e < dk * (DVB / 4); e += THREADS) {
         const int i = e / (DVB / 4), j = (e - i * (DVB / 4)) * 4;
-        *reinterpret_cast<float4 *>(Sh + (size_t)i * dv + j0 + j) = ld4(Sb + i * DVB + j);
+        *reinterpret_cast<float4 *>(Sh + (size_t)i * dv + j0 + j) = ld4(Sb + i * DVB + swz(i, j, DVB));
     }
 }
 
