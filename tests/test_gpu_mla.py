@@ -55,7 +55,8 @@ def run_gpu(k3, d, w, cache, x, pos, cap, accumulate=None):
     return O.download(np.float32, (B, d["hidden"])), C.download(np.uint16, cache.shape)
 
 
-@pytest.mark.parametrize("B,L", [(1, 200), (2, 37)])
+# B = 32 is config 2's batched decode (128 attention CTAs of one or two position splits)
+@pytest.mark.parametrize("B,L", [(1, 200), (2, 37), (32, 64)])
 def test_mla_decode_matches_oracle(k3, oracle, B, L):
     cap = 256
     w, cache, x = make(10 + B, DIMS, B, cap, L)
