@@ -173,17 +173,17 @@ int kda_seq(float *S, float *o, const float *q, const float *k, const float *v,
 // is at most 60 (no overflow of 2^-G), L and M are plain products of 2^G*k and 2^-G*k;
 // otherwise (strong decay) each pair takes its own exponential. log2 of a decay is clamped
 // at -126, so a decay of exactly 0 acts as 2^-126.
-// k_kda_chunk_scan, one CTA per (head, 32 value columns): walks the chunks in order with
-// the state block in shared memory; per chunk X = U - W S, O = Qt S + M X, S = g S + Kb^T X,
-// each product on the tensor cores (mma.sync tf32, fp32 operands split in two, 3 MMAs per
-// step). The next phase's operand is copied in (cp.async) while the current phase computes.
+// k_kda_chunk_scan, one CTA per (head, 64 value columns; 32 when dv is not a multiple of
+// 64): walks the chunks in order with the state block in shared memory; per chunk
+// X = U - W S, O = Qt S + M X, S = g S + Kb^T X, each product on the tensor cores
+// (mma.sync tf32, fp32 operands split in two, 3 MMAs per step). Operands are copied in
+// with cp.async two phases ahead of their use, through three rotating buffers.
 namespace kdc {
 
 constexpr int C = 64;            // steps per chunk
 constexpr int DKM = 128;         // largest key dim
 constexpr int LDT = C + 4;       // row stride of the transposed [dk][C] tiles
 constexpr int THREADS = 256;
-constexpr int DVB = 32;          // value columns per scan CTA
 constexpr int SEG = 8;           // chunks per prep/scan pair (records stay in L2)
 
 struct Rec {
@@ -470,7 +470,7 @@ __device__ __forceinline__ void cp16(void *dst, const void *src)
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void stage(float *dst, const float *src, int nfloats)
 {
@@ -542,39 +542,62 @@ __device__ __forceinline__ void frag_a(const float *P, int width, int k0, int m0
     split_tf32(P[kb * width + swz(kb, m0 + g + 8, width)], ab[3], as[3]);
 }
 
-constexpr size_t scan_smem()
+// Shared memory of the scan for NB value columns per CTA: state block, X, three operand
+// buffers (W^T, Qt^T and Kb rotate through them), M^T and 2^G_last.
+constexpr size_t scan_smem(int nb)
 {
-    return ((size_t)DKM * DVB + (size_t)C * DVB + 2 * (size_t)DKM * C + (size_t)C * C + DKM) *
+    return ((size_t)DKM * nb + (size_t)C * nb + 3 * (size_t)DKM * C + (size_t)C * C + DKM) *
            sizeof(float);
 }
 
 // DKC = 128 compiles the key dimension in (the config-3 head); DKC = 0 reads it from dk.
-// Warps: in X and O, warp w owns rows 16 (w mod 4).. and columns 16 (w / 4).. (two 8-column
-// MMA tiles); in the state update, rows 16 w.. of the key dimension and all 32 columns.
-template <int DKC>
-__global__ void __launch_bounds__(THREADS, 2)
+// NB value columns per CTA (64 when dv allows, else 32). A chunk is three phases (X, O, the
+// state update), each reading one operand; the operand of phase p + 2 is copied in while
+// phase p computes, so every copy has two phases to land.
+// Warps: in X and O, warp w owns rows 16 (w mod 4).. and columns (w / 4) NB/2.. (NB/16
+// MMA tiles of 8 columns); in the state update, key rows 16 w.. and all NB columns.
+template <int DKC, int NB>
+__global__ void __launch_bounds__(THREADS, 1)
 k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__restrict__ ws,
                  long tok0, int nch, int T, int H, int dk_, int dv)
 {
+    constexpr int NT1 = NB / 16, NT3 = NB / 8;
     const int dk = DKC ? DKC : dk_;
     extern __shared__ __align__(16) float sh[];
-    float *Sb = sh;                          // state block [dk][DVB], swizzled
-    float *Xs = Sb + DKM * DVB;              // X [C][DVB], swizzled
-    float *const b0 = Xs + C * DVB, *const b1 = b0 + DKM * C;   // W^T / Qt^T / Kb, swizzled
-    float *Ms = b1 + DKM * C;                // M^T [C][C], swizzled
+    float *Sb = sh;                          // state block [dk][NB], swizzled
+    float *Xs = Sb + DKM * NB;               // X [C][NB], swizzled
+    float *const bufs = Xs + C * NB;         // 3 x [DKM * C]: W^T / Qt^T / Kb, swizzled
+    float *Ms = bufs + 3 * DKM * C;          // M^T [C][C], swizzled
     float *gs = Ms + C * C;                  // 2^G_last [dk]
-    const int h = blockIdx.x, j0 = blockIdx.y * DVB, tid = threadIdx.x;
+    const int h = blockIdx.x, j0 = blockIdx.y * NB, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
-    const int t0 = 16 * (warp & 3), n0 = 16 * (warp >> 2);
+    const int t0 = 16 * (warp & 3), n0 = (warp >> 2) * (NB / 2);
     const Rec R = rec(dk, dv);
     float *Sh = S + (size_t)h * dk * dv;
     auto recp = [&](int c) { return ws + ((size_t)c * H + h) * R.total; };
-    auto Bf = [&](int i) { return i ? b1 : b0; };
+    auto buf = [&](int phase) { return bufs + (phase % 3) * (DKM * C); };
+    // the copies for phase p of the chunk sequence (3 phases per chunk), one commit group
+    auto issue = [&](int p) {
+        const int c = p / 3, k = p - 3 * c;
+        if (c < nch) {
+            const float *rc = recp(c);
+            if (k == 0) {
+                stage_sw(buf(p), rc + R.wt, dk, C);
+            } else if (k == 1) {
+                stage_sw(buf(p), rc + R.qt, dk, C);
+                stage_sw(Ms, rc + R.mt, C, C);
+            } else {
+                stage_sw(buf(p), rc + R.kb, C, dk);
+                stage(gs, rc + R.gc, (dk + 3) & ~3);
+            }
+        }
+        cp_commit();
+    };
     // U at this thread's X fragment: rows t0+g, t0+g+8; columns n0 + 8 nt + 2q, +1
-    float u[2][4];
+    float u[NT1][4];
     auto load_u = [&](const float *U) {
 #pragma unroll
-        for (int nt = 0; nt < 2; nt++) {
+        for (int nt = 0; nt < NT1; nt++) {
             const int col = j0 + n0 + 8 * nt + 2 * q;
             const float2 r0 = *reinterpret_cast<const float2 *>(U + (size_t)(t0 + g) * dv + col);
             const float2 r1 = *reinterpret_cast<const float2 *>(U + (size_t)(t0 + g + 8) * dv + col);
@@ -582,78 +605,73 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
         }
     };
 
-    int p = 0;
-    stage_sw(Bf(0), recp(0) + R.wt, dk, C);
-    cp_commit();
-    for (int e = tid; e < dk * (DVB / 4); e += THREADS) {
-        const int i = e / (DVB / 4), j = (e - i * (DVB / 4)) * 4;
-        *reinterpret_cast<float4 *>(Sb + i * DVB + swz(i, j, DVB)) = ld4(Sh + (size_t)i * dv + j0 + j);
+    issue(0);
+    issue(1);
+    for (int e = tid; e < dk * (NB / 4); e += THREADS) {
+        const int i = e / (NB / 4), j = (e - i * (NB / 4)) * 4;
+        *reinterpret_cast<float4 *>(Sb + i * NB + swz(i, j, NB)) = ld4(Sh + (size_t)i * dv + j0 + j);
     }
     load_u(recp(0) + R.u);
 
     for (int c = 0; c < nch; c++) {
-        const float *rc = recp(c);
+        const int p1 = 3 * c;
         // P1: X = U - W S
-        stage_sw(Bf(p ^ 1), rc + R.qt, dk, C);
-        stage_sw(Ms, rc + R.mt, C, C);
-        cp_commit();
-        cp_wait1();
+        issue(p1 + 2);
+        cp_wait2();
         __syncthreads();
         {
-            const float *W = Bf(p);
-            float acc[2][4] = {};
+            const float *W = buf(p1);
+            float acc[NT1][4] = {};
 #pragma unroll 4
             for (int k0 = 0; k0 < dk; k0 += 8) {
                 uint32_t ab[4], as[4];
                 frag_a(W, C, k0, t0, g, q, ab, as);
 #pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
+                for (int nt = 0; nt < NT1; nt++) {
                     const int n = n0 + 8 * nt + g, ka = k0 + q, kb = ka + 4;
-                    mma3(acc[nt], ab, as, Sb[ka * DVB + swz(ka, n, DVB)], Sb[kb * DVB + swz(kb, n, DVB)]);
+                    mma3(acc[nt], ab, as, Sb[ka * NB + swz(ka, n, NB)], Sb[kb * NB + swz(kb, n, NB)]);
                 }
             }
 #pragma unroll
-            for (int nt = 0; nt < 2; nt++) {
+            for (int nt = 0; nt < NT1; nt++) {
                 const int col = n0 + 8 * nt + 2 * q, r0 = t0 + g, r1 = t0 + g + 8;
-                *reinterpret_cast<float2 *>(Xs + r0 * DVB + swz(r0, col, DVB)) =
+                *reinterpret_cast<float2 *>(Xs + r0 * NB + swz(r0, col, NB)) =
                     make_float2(u[nt][0] - acc[nt][0], u[nt][1] - acc[nt][1]);
-                *reinterpret_cast<float2 *>(Xs + r1 * DVB + swz(r1, col, DVB)) =
+                *reinterpret_cast<float2 *>(Xs + r1 * NB + swz(r1, col, NB)) =
                     make_float2(u[nt][2] - acc[nt][2], u[nt][3] - acc[nt][3]);
             }
         }
         __syncthreads();
-        p ^= 1;
         // P2: O = Qt S + M X (M^T[s][t] is zero for s > t inside the diagonal 16x16 block)
-        stage_sw(Bf(p ^ 1), rc + R.kb, C, dk);
-        stage(gs, rc + R.gc, (dk + 3) & ~3);
-        cp_commit();
-        cp_wait1();
+        issue(p1 + 3);
+        if (c + 1 < nch) load_u(recp(c + 1) + R.u);
+        cp_wait2();
         __syncthreads();
         {
-            const float *Q = Bf(p);
-            float acc[2][4] = {};
+            const float *Q = buf(p1 + 1);
+            float acc[NT1][4] = {};
 #pragma unroll 4
             for (int k0 = 0; k0 < dk; k0 += 8) {
                 uint32_t ab[4], as[4];
                 frag_a(Q, C, k0, t0, g, q, ab, as);
 #pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
+                for (int nt = 0; nt < NT1; nt++) {
                     const int n = n0 + 8 * nt + g, ka = k0 + q, kb = ka + 4;
-                    mma3(acc[nt], ab, as, Sb[ka * DVB + swz(ka, n, DVB)], Sb[kb * DVB + swz(kb, n, DVB)]);
+                    mma3(acc[nt], ab, as, Sb[ka * NB + swz(ka, n, NB)], Sb[kb * NB + swz(kb, n, NB)]);
                 }
             }
             for (int k0 = 0; k0 < t0 + 16; k0 += 8) {
                 uint32_t ab[4], as[4];
                 frag_a(Ms, C, k0, t0, g, q, ab, as);
 #pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
+                for (int nt = 0; nt < NT1; nt++) {
                     const int n = n0 + 8 * nt + g, ka = k0 + q, kb = ka + 4;
-                    mma3(acc[nt], ab, as, Xs[ka * DVB + swz(ka, n, DVB)], Xs[kb * DVB + swz(kb, n, DVB)]);
+                    mma3(acc[nt], ab, as, Xs[ka * NB + swz(ka, n, NB)], Xs[kb * NB + swz(kb, n, NB)]);
                 }
             }
             const long tc0 = tok0 + (long)c * C;
 #pragma unroll
-            for (int nt = 0; nt < 2; nt++) {
+            for (int nt = 0; nt < NT1; nt++) {
                 const int col = j0 + n0 + 8 * nt + 2 * q;
                 const long ta = tc0 + t0 + g, tb = ta + 8;
                 if (ta < T)
@@ -663,49 +681,42 @@ k_kda_chunk_scan(float *__restrict__ S, float *__restrict__ o, const float *__re
             }
         }
         __syncthreads();
-        p ^= 1;
-        // P3: S = diag(2^G_last) S + Kb^T X; the next chunk's W is copied in meanwhile.
-        if (c + 1 < nch) {
-            const float *rn = recp(c + 1);
-            stage_sw(Bf(p ^ 1), rn + R.wt, dk, C);
-            load_u(rn + R.u);
-        }
-        cp_commit();
-        cp_wait1();
+        // P3: S = diag(2^G_last) S + Kb^T X
+        issue(p1 + 4);
+        cp_wait2();
         __syncthreads();
         {
-            const float *Kb = Bf(p);
+            const float *Kb = buf(p1 + 2);
             const int i0 = 16 * warp;
             if (i0 < dk) {
-                float acc[4][4] = {};
+                float acc[NT3][4] = {};
 #pragma unroll
                 for (int k0 = 0; k0 < C; k0 += 8) {
                     uint32_t ab[4], as[4];
                     frag_a(Kb, dk, k0, i0, g, q, ab, as);
 #pragma unroll
-                    for (int nt = 0; nt < 4; nt++) {
+                    for (int nt = 0; nt < NT3; nt++) {
                         const int n = 8 * nt + g, ka = k0 + q, kb = ka + 4;
-                        mma3(acc[nt], ab, as, Xs[ka * DVB + swz(ka, n, DVB)], Xs[kb * DVB + swz(kb, n, DVB)]);
+                        mma3(acc[nt], ab, as, Xs[ka * NB + swz(ka, n, NB)], Xs[kb * NB + swz(kb, n, NB)]);
                     }
                 }
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++) {
+                for (int nt = 0; nt < NT3; nt++) {
                     const int col = 8 * nt + 2 * q, r0 = i0 + g, r1 = i0 + g + 8;
-                    float2 *p0 = reinterpret_cast<float2 *>(Sb + r0 * DVB + swz(r0, col, DVB));
-                    float2 *p1 = reinterpret_cast<float2 *>(Sb + r1 * DVB + swz(r1, col, DVB));
-                    const float2 s0 = *p0, s1 = *p1;
+                    float2 *p0 = reinterpret_cast<float2 *>(Sb + r0 * NB + swz(r0, col, NB));
+                    float2 *pp1 = reinterpret_cast<float2 *>(Sb + r1 * NB + swz(r1, col, NB));
+                    const float2 s0 = *p0, s1 = *pp1;
                     *p0 = make_float2(gs[r0] * s0.x + acc[nt][0], gs[r0] * s0.y + acc[nt][1]);
-                    *p1 = make_float2(gs[r1] * s1.x + acc[nt][2], gs[r1] * s1.y + acc[nt][3]);
+                    *pp1 = make_float2(gs[r1] * s1.x + acc[nt][2], gs[r1] * s1.y + acc[nt][3]);
                 }
             }
         }
         __syncthreads();
-        p ^= 1;
     }
     cp_wait0();
-    for (int e = tid; e < dk * (DVB / 4); e += THREADS) {
-        const int i = e / (DVB / 4), j = (e - i * (DVB / 4)) * 4;
-        *reinterpret_cast<float4 *>(Sh + (size_t)i * dv + j0 + j) = ld4(Sb + i * DVB + swz(i, j, DVB));
+    for (int e = tid; e < dk * (NB / 4); e += THREADS) {
+        const int i = e / (NB / 4), j = (e - i * (NB / 4)) * 4;
+        *reinterpret_cast<float4 *>(Sh + (size_t)i * dv + j0 + j) = ld4(Sb + i * NB + swz(i, j, NB));
     }
 }
 
@@ -719,7 +730,7 @@ int kda_chunked(float *S, float *o, const float *q, const float *k, const float 
 {
     using namespace kdc;
     if (T <= 0 || H <= 0) return K3D_OK;
-    if (dk < 8 || dk > DKM || dk % 8 || dv < DVB || dv > 128 || dv % DVB)
+    if (dk < 8 || dk > DKM || dk % 8 || dv < 32 || dv > 128 || dv % 32)
         return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: dk %d (8..128, multiple of 8), "
                                 "dv %d (32..128, multiple of 32)", dk, dv);
     if (((uintptr_t)S | (uintptr_t)o | (uintptr_t)q | (uintptr_t)k | (uintptr_t)alpha) & 15u)
@@ -727,8 +738,10 @@ int kda_chunked(float *S, float *o, const float *q, const float *k, const float 
     static bool init = false;
     if (!init) {
         allow_smem_max(k_kda_chunk_prep);
-        allow_smem_max(k_kda_chunk_scan<128>);
-        allow_smem_max(k_kda_chunk_scan<0>);
+        allow_smem_max(k_kda_chunk_scan<128, 64>);
+        allow_smem_max(k_kda_chunk_scan<0, 64>);
+        allow_smem_max(k_kda_chunk_scan<128, 32>);
+        allow_smem_max(k_kda_chunk_scan<0, 32>);
         init = true;
     }
     const Rec R = rec(dk, dv);
@@ -743,12 +756,19 @@ int kda_chunked(float *S, float *o, const float *q, const float *k, const float 
                                                                     T, H, dk, dv);
         note_launch();
         K3_TRY(check_launch("kda chunk prep"));
-        if (dk == 128)
-            k_kda_chunk_scan<128><<<dim3(H, dv / DVB), THREADS, scan_smem(), st>>>(S, o, ws, tok0, n,
-                                                                                T, H, dk, dv);
-        else
-            k_kda_chunk_scan<0><<<dim3(H, dv / DVB), THREADS, scan_smem(), st>>>(S, o, ws, tok0, n,
-                                                                              T, H, dk, dv);
+        if (dv % 64 == 0) {
+            const dim3 grid(H, dv / 64);
+            if (dk == 128)
+                k_kda_chunk_scan<128, 64><<<grid, THREADS, scan_smem(64), st>>>(S, o, ws, tok0, n, T, H, dk, dv);
+            else
+                k_kda_chunk_scan<0, 64><<<grid, THREADS, scan_smem(64), st>>>(S, o, ws, tok0, n, T, H, dk, dv);
+        } else {
+            const dim3 grid(H, dv / 32);
+            if (dk == 128)
+                k_kda_chunk_scan<128, 32><<<grid, THREADS, scan_smem(32), st>>>(S, o, ws, tok0, n, T, H, dk, dv);
+            else
+                k_kda_chunk_scan<0, 32><<<grid, THREADS, scan_smem(32), st>>>(S, o, ws, tok0, n, T, H, dk, dv);
+        }
         note_launch();
         K3_TRY(check_launch("kda chunk scan"));
     }
