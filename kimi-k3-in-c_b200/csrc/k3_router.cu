@@ -654,8 +654,6 @@ __host__ __device__ inline size_t fused_smem_bytes(int hidden, int n_experts)
 template <typename WT>
 __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
 {
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ __align__(16) unsigned char rsm[];
     __shared__ double p_s[2][4];
     __shared__ float p_a[2][4];
@@ -687,9 +685,21 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
         const WT *row1 = W + (size_t)(e0 + 1) * hidden;
         double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
         float a[2] = {0.0f, 0.0f};
+        WChunk<WT> wv[2][8];
+        // the first batch of weights before waiting for the kernel that writes x (weights
+        // never depend on it), so their latency overlaps that kernel's tail
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (j < nj) {
+                const int c = cbase + 32 * j;
+                if (act0) wv[0][j].load(row0, c);
+                if (act1) wv[1][j].load(row1, c);
+            }
+        }
+        pdl_wait();
+        pdl_trigger();
         for (int j0 = 0; j0 < nj; j0 += 8) {
             float4 xv[8][2];
-            WChunk<WT> wv[2][8];
             // every load of the batch is issued before any arithmetic
 #pragma unroll
             for (int j = 0; j < 8; j++) {
@@ -697,8 +707,8 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
                     const int c = cbase + 32 * (j0 + j);
                     xv[j][0] = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c);
                     xv[j][1] = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c + 1);
-                    if (act0) wv[0][j].load(row0, c);
-                    if (act1) wv[1][j].load(row1, c);
+                    if (j0 > 0 && act0) wv[0][j].load(row0, c);
+                    if (j0 > 0 && act1) wv[1][j].load(row1, c);
                 }
             }
 #pragma unroll
