@@ -197,11 +197,13 @@ def sequence_state(c, S, b, batch):
     return out
 
 
-def test_stack_batch_decode_matches_oracle_per_sequence(k3, oracle):
-    """A batch of 6 sequences (above 4: every projection runs the tensor-core GEMM, the MoE
-    layers route 6 tokens), eager then graph-captured; each sequence's logits against the
+@pytest.mark.parametrize("B", [6, 64])
+def test_stack_batch_decode_matches_oracle_per_sequence(k3, oracle, B):
+    """A batch of 6 sequences (above 4: every projection runs the tensor-core GEMM; 24
+    expert assignments per MoE layer, the resident expert pass) and of 64 (256 assignments:
+    the grouped expert pass), eager then graph-captured; each sequence's logits against the
     oracle stepping that sequence alone from its own cache and state."""
-    c, B = CFG, 6
+    c = CFG
     model = k3.k3d_model_create(ctypes.byref(make_cfg(c, batch=B, layout=1)), 4321)
     assert model, k3.k3d_last_message()
     try:
@@ -209,7 +211,8 @@ def test_stack_batch_decode_matches_oracle_per_sequence(k3, oracle):
         k3cuda.check(k3.k3d_sync())
         W, S = host_copy(k3, model, c, 1, batch=B)
         seqs = [sequence_state(c, S, b, B) for b in range(B)]
-        toks = np.array([3, 17, 17, 500, 1023, 42], np.int32)
+        toks = (np.array([3, 17, 17, 500, 1023, 42], np.int32) if B == 6 else
+                ((np.arange(B) * 37 + 5) % c["vocab"]).astype(np.int32))
         for step in range(3):          # eager, capture, replay
             nxt = np.zeros(B, np.int32)
             k3cuda.check(k3.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
