@@ -158,9 +158,12 @@ def test_kda_step_fixture_and_bit_exact(k3, oracle):
     assert_close_elementwise(outs, d["out"], atol, rtol, "kda out")
 
 
-def test_kda_decode_config3_bit_exact(k3, oracle):
-    g = synth.rng(21)
-    B, H, D = 2, 64, 128
+@pytest.mark.parametrize("B", [1, 2, 32])
+def test_kda_decode_config3_bit_exact(k3, oracle, B):
+    """Config 3 decode (batches 1 and 32 in BASELINE): every state and output bit-identical
+    to the oracle's k3_kda_step."""
+    g = synth.rng(21 + B)
+    H, D = 64, 128
     S = (g.standard_normal((B, H, D, D), dtype=np.float32) * np.float32(0.01))
     q = g.standard_normal((B, H, D), dtype=np.float32)
     k = g.standard_normal((B, H, D), dtype=np.float32)
