@@ -8,7 +8,7 @@
    seeded synthetic inputs at the benchmark shapes (tests/golden/synth.py), with a digest
    of the inputs.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <path of the reference source tree>]
 """
 import argparse
 import json
