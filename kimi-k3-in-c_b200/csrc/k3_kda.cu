@@ -172,7 +172,8 @@ int kda_seq(float *S, float *o, const float *q, const float *k, const float *v,
 // 2^(G_t-G_s) has t >= s, so it is <= 1 for decays in [0, 1]. When every |G| of the chunk
 // is at most 60 (no overflow of 2^-G), L and M are plain products of 2^G*k and 2^-G*k;
 // otherwise (strong decay) each pair takes its own exponential. log2 of a decay is clamped
-// at -126, so a decay of exactly 0 acts as 2^-126.
+// at -126, so a decay of exactly 0 acts as 2^-126. Exponentials and logarithms are the
+// hardware approximations (ex2.approx, lg2.approx).
 // k_kda_chunk_scan, one CTA per (head, 64 value columns; 32 when dv is not a multiple of
 // 64): walks the chunks in order with the state block in shared memory; per chunk
 // X = U - W S, O = Qt S + M X, S = g S + Kb^T X, each product on the tensor cores
@@ -207,6 +208,23 @@ __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast
 __device__ __forceinline__ float at4(const float4 &v, int a)
 {
     return a == 0 ? v.x : a == 1 ? v.y : a == 2 ? v.z : v.w;
+}
+
+// The hardware base-2 exponential and logarithm (ex2.approx / lg2.approx, about 2^-22
+// relative error; subnormal results flush to zero). The chunked form's decays enter only
+// through 2^(difference of cumulative log2 decays), so errors of this size stay far below
+// the 1e-3 tolerance of the chunked result.
+__device__ __forceinline__ float ex2a(float x)
+{
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float lg2a(float x)
+{
+    float r;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
 }
 
 constexpr size_t prep_smem() { return (3 * (size_t)DKM * LDT + C) * sizeof(float); }
@@ -280,15 +298,15 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
 #pragma unroll 4
         for (int t = 0; t < C; t += 4) {
             float4 a = ld4(row + t);
-            g += fmaxf(log2f(a.x), -126.0f); a.x = g;
-            g += fmaxf(log2f(a.y), -126.0f); a.y = g;
-            g += fmaxf(log2f(a.z), -126.0f); a.z = g;
-            g += fmaxf(log2f(a.w), -126.0f); a.w = g;
+            g += fmaxf(lg2a(a.x), -126.0f); a.x = g;
+            g += fmaxf(lg2a(a.y), -126.0f); a.y = g;
+            g += fmaxf(lg2a(a.z), -126.0f); a.z = g;
+            g += fmaxf(lg2a(a.w), -126.0f); a.w = g;
             st4(row + t, a);
             big |= !(fabsf(a.x) <= 60.0f && fabsf(a.w) <= 60.0f && fabsf(a.y) <= 60.0f &&
                      fabsf(a.z) <= 60.0f);
         }
-        out[R.gc + tid] = exp2f(g);
+        out[R.gc + tid] = ex2a(g);
     }
     const bool direct = __syncthreads_or(big);
 
@@ -298,16 +316,16 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
         const float gl = gT[i * LDT + C - 1];
         const float4 kk = ld4(kT + i * LDT + s), gg = ld4(gT + i * LDT + s);
         float *o = out + R.kb + (size_t)s * dk + i;
-        o[0] = kk.x * exp2f(gl - gg.x);
-        o[dk] = kk.y * exp2f(gl - gg.y);
-        o[2 * dk] = kk.z * exp2f(gl - gg.z);
-        o[3 * dk] = kk.w * exp2f(gl - gg.w);
+        o[0] = kk.x * ex2a(gl - gg.x);
+        o[dk] = kk.y * ex2a(gl - gg.y);
+        o[2 * dk] = kk.z * ex2a(gl - gg.z);
+        o[3 * dk] = kk.w * ex2a(gl - gg.w);
     }
     for (int e = tid; e < dk * (C / 4); e += THREADS) {
         const int i = e / (C / 4), t = (e % (C / 4)) * 4;
         const float4 qq = ld4(qT + i * LDT + t), gg = ld4(gT + i * LDT + t);
         st4(out + R.qt + (size_t)i * C + t,
-            make_float4(qq.x * exp2f(gg.x), qq.y * exp2f(gg.y), qq.z * exp2f(gg.z), qq.w * exp2f(gg.w)));
+            make_float4(qq.x * ex2a(gg.x), qq.y * ex2a(gg.y), qq.z * ex2a(gg.z), qq.w * ex2a(gg.w)));
     }
     if (!direct) {
         __syncthreads();
@@ -316,10 +334,10 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
             const float4 k0 = ld4(kT + i * LDT + t), gg = ld4(gT + i * LDT + t);
             float4 qq = ld4(qT + i * LDT + t), kk, n;
             float p;
-            p = exp2f(gg.x); kk.x = k0.x * p; qq.x *= p; n.x = k0.x * exp2f(-gg.x);
-            p = exp2f(gg.y); kk.y = k0.y * p; qq.y *= p; n.y = k0.y * exp2f(-gg.y);
-            p = exp2f(gg.z); kk.z = k0.z * p; qq.z *= p; n.z = k0.z * exp2f(-gg.z);
-            p = exp2f(gg.w); kk.w = k0.w * p; qq.w *= p; n.w = k0.w * exp2f(-gg.w);
+            p = ex2a(gg.x); kk.x = k0.x * p; qq.x *= p; n.x = k0.x * ex2a(-gg.x);
+            p = ex2a(gg.y); kk.y = k0.y * p; qq.y *= p; n.y = k0.y * ex2a(-gg.y);
+            p = ex2a(gg.z); kk.z = k0.z * p; qq.z *= p; n.z = k0.z * ex2a(-gg.z);
+            p = ex2a(gg.w); kk.w = k0.w * p; qq.w *= p; n.w = k0.w * ex2a(-gg.w);
             st4(kT + i * LDT + t, kk);
             st4(qT + i * LDT + t, qq);
             st4(gT + i * LDT + t, n);
@@ -367,7 +385,7 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
                         if (bsb < bt || b <= a) {
-                            const float kse = at4(ks, b) * exp2f(at4(gt, a) - at4(gs, b));
+                            const float kse = at4(ks, b) * ex2a(at4(gt, a) - at4(gs, b));
                             La[a][b] = fmaf(at4(kt, a), kse, La[a][b]);
                             Ma[a][b] = fmaf(at4(qt, a), kse, Ma[a][b]);
                         }
@@ -401,7 +419,7 @@ k_kda_chunk_prep(const float *__restrict__ q, const float *__restrict__ k,
             const int i = e / (C / 4), t = (e % (C / 4)) * 4;
             float4 kk = ld4(kT + i * LDT + t);
             const float4 gg = ld4(gT + i * LDT + t);
-            kk.x *= exp2f(gg.x); kk.y *= exp2f(gg.y); kk.z *= exp2f(gg.z); kk.w *= exp2f(gg.w);
+            kk.x *= ex2a(gg.x); kk.y *= ex2a(gg.y); kk.z *= ex2a(gg.z); kk.w *= ex2a(gg.w);
             st4(kT + i * LDT + t, kk);
         }
         __syncthreads();
