@@ -754,6 +754,11 @@ def setup_dist(world, rank, local):
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
     _PG = True
+    # stdout carries the one JSON line: NCCL's version banner (printed at NCCL_DEBUG=VERSION)
+    # stays off and NCCL's own log goes to stderr
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     # one process per GPU: the library uses the device torchrun assigned
     os.environ["CUDA_VISIBLE_DEVICES"] = str(local)
     import k3cuda
