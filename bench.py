@@ -149,6 +149,7 @@ def cpu_moe_sample(seconds=12.0, max_tokens=2000):
         act = (a / (np.float32(1) + np.exp(-a))).astype(np.float32) * b
         return acc + impl.matmul_bf16(act, sd)
 
+    cores, cpu_model, _ = cpu_threads(impl.lib)
     token(xs[0])
     n = 0
     t0 = time.perf_counter()
@@ -156,106 +157,214 @@ def cpu_moe_sample(seconds=12.0, max_tokens=2000):
         token(xs[n % 64])
         n += 1
     dt = time.perf_counter() - t0
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
-    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": kind,
+    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": kind, "cpu_model": cpu_model,
             "sample": f"{n} tokens through one config-1 MoE layer (router + 8 MXFP4 experts + "
                       f"bf16 shared expert) in {dt:.1f} s; AVX2 k3_ops.c, OpenMP"}
 
 
-def cpu_stack_sample(seconds=20.0):
-    """The reference's k3_ops.c (oracle/_ref) on the pieces of one config-4 decode token,
-    each timed on the host's cores and composed: 6 x k3_kda_layer (timed at 16 of the 64
-    heads, x4: every term but the 128-row f_a scales with heads) + 2 x k3_mla_cached with
-    its own fp32 expanded cache at 4096 cached positions + 7 x the config-1 MoE token
-    (cpu_moe_sample) + the dense SwiGLU layer and the LM head through k3_matmul_bf16
-    (timed on 1/4 and 1/10 of the rows and scaled). Returns tok/s."""
+def cpu_threads(lib):
+    """Sets the OpenMP thread count of the CPU arm explicitly, whatever the launcher put in
+    OMP_NUM_THREADS (torchrun exports 1): one thread per physical core the process may run
+    on. Returns (threads in force, CPU model)."""
+    import psutil
+    aff = len(os.sched_getaffinity(0))
+    phys = psutil.cpu_count(logical=False) or aff
+    n = max(1, min(aff, phys))
+    gomp = C.CDLL("libgomp.so.1")              # the instance libk3ref.so is linked with
+    gomp.omp_set_num_threads(C.c_int(n))
+    got = int(gomp.omp_get_max_threads())
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return got, model, gomp
+
+
+def fnv1a(a):
+    """FNV-1a over the bytes of an array (the reference bench_kernels.c output hash)."""
+    h = 1469598103934665603
+    for b in np.ascontiguousarray(a).view(np.uint8).tobytes():
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return f"{h:016x}"
+
+
+def cpu_stack_run(context=4096, reps=5, one_thread_reps=2):
+    """The reference's own k3_ops.c (oracle/_ref/libk3ref.so; the C restatement when absent)
+    running whole config-4 decode tokens at full width on the host cores: 8 layers (KDA at
+    0-based 0,1,2,4,5,6 through k3_kda_layer with all 64 heads; MLA at 3 and 7 through
+    k3_mla_cached over `context` cached positions in its fp32 expanded cache), the dense
+    SwiGLU layer and the seven config-1 MoE layers composed from k3_rmsnorm, k3_matmul_bf16,
+    k3_router and k3_matmul_mxfp4 (SURVEY's per-config composition), then the final norm and
+    the 163840-row LM head with argmax. bf16 weights ~N(0, 0.02) (a 32 MB seeded block tiled
+    over each matrix: the bytes read per token are the full model's), MXFP4 experts from a
+    pool of 32 distinct experts (expert e reads pool[e % 32], 749 MB). One warm-up token,
+    then `reps` timed tokens on all physical cores and `one_thread_reps` on one core."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as orc
     import synth
     if orc.Reference.available():
-        impl, kind = orc.Reference(), "reference"
+        impl, kind, pre = orc.Reference(), "reference", "k3_"
     else:
-        impl, kind = orc.Oracle(), "port"
+        impl, kind, pre = orc.Oracle(), "port", "orc_"
     lib = impl.lib
-    pre = "k3_" if kind == "reference" else "orc_"
-    g = synth.rng(909)
-    E = HIDDEN
+    threads, cpu_model, gomp = cpu_threads(lib)
+    g = synth.rng(2029)
+    E, V, P, H, D = HIDDEN, 163840, 64 * 128, 64, 128
+    block = synth.bf16_normal(g, (1 << 24,), 0.02)
 
-    def timeit(fn, reps=2):
-        fn()
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            fn()
-        return (time.perf_counter() - t0) / reps
+    def bf16(shape):
+        a = np.empty(shape, np.uint16)
+        f = a.reshape(-1)
+        for o in range(0, f.size, block.size):
+            n = min(block.size, f.size - o)
+            f[o:o + n] = block[:n]
+        return a
 
-    # KDA at 16 heads, bf16 weights (wdt = 1)
-    H, D = 16, 128
-    P = H * D
-    kw = {k: synth.bf16_normal(g, shp, 0.02) for k, shp in
-          (("q", (P, E)), ("k", (P, E)), ("v", (P, E)), ("g", (P, E)), ("b", (H, E)), ("f_a", (D, E)),
-           ("f_b", (P, D)), ("o", (E, P)))}
-    for k in ("q_conv", "k_conv", "v_conv"):
-        kw[k] = g.standard_normal(P * 4, dtype=np.float32) * np.float32(0.5)
-    kw["A_log"] = g.uniform(0, 1.5, H).astype(np.float32)
-    kw["dt_bias"] = g.standard_normal(P, dtype=np.float32) * np.float32(0.5)
-    kw["o_norm"] = np.ones(D, np.float32)
-    cfg = orc.K3Cfg(hidden=E, kda_heads=H, kda_head_dim=D, conv_k=4, gate_lb=-5.0, rms_eps=1e-6)
-    KW = orc.K3KdaW(*(kw[k].ctypes.data for k in ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a",
-                                                    "f_b", "A_log", "dt_bias", "b", "g", "o_norm", "o")), 1)
-    fn = getattr(lib, pre + "kda_layer")
-    fn.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(orc.K3KdaW), C.POINTER(orc.K3Cfg), C.c_int,
-                   C.c_void_p, C.c_void_p]
-    fn.restype = None
-    sfn = getattr(lib, pre + "kda_scratch")
-    sfn.argtypes = [C.POINTER(orc.K3Cfg), C.c_int]
-    sfn.restype = C.c_size_t
-    scratch = np.empty(sfn(C.byref(cfg), 1) + 1024, np.float32)
-    state = (g.standard_normal(H * D * D + 3 * P * 3, dtype=np.float32) * np.float32(0.01))
-    x = g.standard_normal(E, dtype=np.float32)
-    out = np.empty(E, np.float32)
-    t_kda = 4.0 * timeit(lambda: fn(out.ctypes.data, x.ctypes.data, C.byref(KW), C.byref(cfg), 1,
-                                    state.ctypes.data, scratch.ctypes.data))
-    del kw
-    # MLA with the reference's fp32 expanded cache, 4096 cached positions
-    Hm, ql, kvl, qn, qr, vh = 64, 1536, 512, 128, 64, 128
-    mw = {"q_a": synth.bf16_normal(g, (ql, E), 0.02), "q_b": synth.bf16_normal(g, (Hm * (qn + qr), ql), 0.02),
-          "kv_a": synth.bf16_normal(g, (kvl + qr, E), 0.02),
-          "kv_b": synth.bf16_normal(g, (Hm * (qn + vh), kvl), 0.02),
-          "o": synth.bf16_normal(g, (E, Hm * vh), 0.02), "g": synth.bf16_normal(g, (Hm * vh, E), 0.02),
-          "q_a_norm": np.ones(ql, np.float32), "kv_a_norm": np.ones(kvl, np.float32)}
-    MW = orc.K3MlaW(*(mw[k].ctypes.data for k in ("q_a", "q_b", "kv_a", "kv_b", "o", "g",
-                                                    "q_a_norm", "kv_a_norm")), 1)
-    mcfg = orc.K3Cfg(hidden=E, n_heads=Hm, q_lora=ql, kv_lora=kvl, qk_nope=qn, qk_rope=qr, v_head=vh,
-                     mla_out_gate=1, rms_eps=1e-6)
-    cached, cap = 4096, 4097
-    kvc = g.standard_normal(cap * Hm * (qn + vh), dtype=np.float32)
-    ropec = g.standard_normal(cap * qr, dtype=np.float32)
-    mf = getattr(lib, pre + "mla_cached")
-    mf.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(orc.K3MlaW), C.POINTER(orc.K3Cfg), C.c_int,
-                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
-    mf.restype = None
-    msf = getattr(lib, pre + "mla_scratch_cached")
-    msf.argtypes = [C.POINTER(orc.K3Cfg), C.c_int, C.c_int, C.c_int]
-    msf.restype = C.c_size_t
-    mscratch = np.empty(msf(C.byref(mcfg), 1, cap, 1) + 1024, np.float32)
-    t_mla = timeit(lambda: mf(out.ctypes.data, x.ctypes.data, C.byref(MW), C.byref(mcfg), 1,
-                              mscratch.ctypes.data, kvc.ctypes.data, ropec.ctypes.data, cached, cap), 1)
-    del mw, kvc
-    # dense SwiGLU (1/4 of the rows) and the LM head (1/10 of the rows), bf16
-    Wd = synth.bf16_normal(g, (18432 // 4, E), 0.02)
-    t_dense = 4.0 * 3.0 * timeit(lambda: impl.matmul_bf16(x, Wd))
-    Wl = synth.bf16_normal(g, (16384, E), 0.02)
-    t_lm = 10.0 * timeit(lambda: impl.matmul_bf16(x, Wl))
-    del Wd, Wl
-    moe = cpu_moe_sample(seconds=max(3.0, seconds / 4))
-    t_moe = 1.0 / moe["value"]
-    t_tok = 6 * t_kda + 2 * t_mla + 7 * t_moe + t_dense + t_lm
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
-    return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": cores, "kind": kind,
-            "sample": f"one config-4 token composed from timed pieces: KDA layer {t_kda * 1e3:.1f} ms x6, "
-                      f"MLA layer (4096 cached, fp32 expanded cache) {t_mla * 1e3:.1f} ms x2, MoE layer "
-                      f"{t_moe * 1e3:.1f} ms x7, dense {t_dense * 1e3:.1f} ms, LM head {t_lm * 1e3:.1f} ms; "
-                      "AVX2 k3_ops.c, OpenMP"}
+    vp = C.c_void_p
+    fn = {}
+    for name, args in (("rmsnorm", [vp, vp, vp, C.c_int, C.c_float]),
+                       ("matmul_bf16", [vp, vp, vp, C.c_int, C.c_int]),
+                       ("matmul_mxfp4", [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int]),
+                       ("router", [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float])):
+        f = getattr(lib, pre + name)
+        f.argtypes, f.restype = args, None
+        fn[name] = f
+    kda = getattr(lib, pre + "kda_layer")
+    kda.argtypes = [vp, vp, C.POINTER(orc.K3KdaW), C.POINTER(orc.K3Cfg), C.c_int, vp, vp]
+    kda.restype = None
+    ksz = getattr(lib, pre + "kda_scratch")
+    ksz.argtypes, ksz.restype = [C.POINTER(orc.K3Cfg), C.c_int], C.c_size_t
+    mla = getattr(lib, pre + "mla_cached")
+    mla.argtypes = [vp, vp, C.POINTER(orc.K3MlaW), C.POINTER(orc.K3Cfg), C.c_int, vp, vp, vp,
+                    C.c_int, C.c_int]
+    mla.restype = None
+    msz = getattr(lib, pre + "mla_scratch_cached")
+    msz.argtypes, msz.restype = [C.POINTER(orc.K3Cfg), C.c_int, C.c_int, C.c_int], C.c_size_t
+
+    kcfg = orc.K3Cfg(hidden=E, kda_heads=H, kda_head_dim=D, conv_k=4, gate_lb=-5.0, rms_eps=1e-6)
+    mcfg = orc.K3Cfg(hidden=E, n_heads=64, q_lora=1536, kv_lora=512, qk_nope=128, qk_rope=64,
+                     v_head=128, mla_out_gate=1, rms_eps=1e-6)
+    cap = context + 1
+    layers = []
+    keep = []
+    for l in range(8):
+        L = {"in_norm": np.ones(E, np.float32), "post_norm": np.ones(E, np.float32)}
+        if l in (3, 7):
+            w = {"q_a": bf16((1536, E)), "q_b": bf16((64 * 192, 1536)), "kv_a": bf16((576, E)),
+                 "kv_b": bf16((64 * 256, 512)), "o": bf16((E, 64 * 128)), "g": bf16((64 * 128, E)),
+                 "q_a_norm": np.ones(1536, np.float32), "kv_a_norm": np.ones(512, np.float32)}
+            keep.append(w)
+            L["mla"] = orc.K3MlaW(*(w[k].ctypes.data for k in ("q_a", "q_b", "kv_a", "kv_b", "o",
+                                                                 "g", "q_a_norm", "kv_a_norm")), 1)
+            kvc = np.empty((cap, 64 * 256), np.float32)
+            kvc.reshape(-1)[:] = np.resize(synth.bf16_to_f32(block), kvc.size) * np.float32(50.0)
+            L["kvc"], L["ropec"] = kvc, g.standard_normal((cap, 64), dtype=np.float32)
+        else:
+            w = {k: bf16(shp) for k, shp in (("q", (P, E)), ("k", (P, E)), ("v", (P, E)),
+                                            ("g", (P, E)), ("b", (H, E)), ("f_a", (D, E)),
+                                            ("f_b", (P, D)), ("o", (E, P)))}
+            for k in ("q_conv", "k_conv", "v_conv"):
+                w[k] = g.standard_normal(P * 4, dtype=np.float32) * np.float32(0.5)
+            w["A_log"] = g.uniform(0, 1.5, H).astype(np.float32)
+            w["dt_bias"] = g.standard_normal(P, dtype=np.float32) * np.float32(0.5)
+            w["o_norm"] = np.ones(D, np.float32)
+            keep.append(w)
+            L["kda"] = orc.K3KdaW(*(w[k].ctypes.data for k in (
+                "q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a", "f_b", "A_log", "dt_bias",
+                "b", "g", "o_norm", "o")), 1)
+            L["state"] = g.standard_normal(H * D * D + 3 * P * 3, dtype=np.float32) * np.float32(0.01)
+        if l == 0:
+            L["dense"] = (bf16((18432, E)), bf16((18432, E)), bf16((E, 18432)))
+        else:
+            L["router"] = synth.bf16_to_f32(bf16((N_EXPERTS, E)))
+            L["bias"] = g.uniform(-0.1, 0.1, N_EXPERTS).astype(np.float32)
+            L["shared"] = (bf16((SHARED, E)), bf16((SHARED, E)), bf16((E, SHARED)))
+        layers.append(L)
+    pool = [synth.mxfp4_expert(g, E, INTER) for _ in range(32)]
+    lm_head = bf16((V, E))
+    final_norm = np.ones(E, np.float32)
+    kscr = np.empty(ksz(C.byref(kcfg), 1) + 64, np.float32)
+    mscr = np.empty(msz(C.byref(mcfg), 1, cap, 1) + 64, np.float32)
+    x0 = synth.bf16_to_f32(block[:E].copy()) * np.float32(50.0)
+    buf = {k: np.empty(n, np.float32) for k, n in (("xn", E), ("out", E), ("g", 18432),
+                                                   ("u", 18432), ("e", E), ("lg", V))}
+    idx, wt = np.empty(TOPK, np.int32), np.empty(TOPK, np.float32)
+
+    def mm(y, x, W):
+        fn["matmul_bf16"](y.ctypes.data, x.ctypes.data, W.ctypes.data, W.shape[1], W.shape[0])
+        return y
+
+    def swiglu(x, Wg, Wu, Wd, out):
+        n = Wg.shape[0]
+        a = mm(buf["g"][:n], x, Wg)
+        b = mm(buf["u"][:n], x, Wu)
+        act = ((a / (np.float32(1) + np.exp(-a))) * b).astype(np.float32)
+        return mm(out, act, Wd)
+
+    def token():
+        h = x0.copy()
+        xn, out = buf["xn"], buf["out"]
+        for l, L in enumerate(layers):
+            fn["rmsnorm"](xn.ctypes.data, h.ctypes.data, L["in_norm"].ctypes.data, E, C.c_float(1e-6))
+            if "mla" in L:
+                mla(out.ctypes.data, xn.ctypes.data, C.byref(L["mla"]), C.byref(mcfg), 1,
+                    mscr.ctypes.data, L["kvc"].ctypes.data, L["ropec"].ctypes.data, context, cap)
+            else:
+                kda(out.ctypes.data, xn.ctypes.data, C.byref(L["kda"]), C.byref(kcfg), 1,
+                    L["state"].ctypes.data, kscr.ctypes.data)
+            h += out
+            fn["rmsnorm"](xn.ctypes.data, h.ctypes.data, L["post_norm"].ctypes.data, E, C.c_float(1e-6))
+            if "dense" in L:
+                h += swiglu(xn, *L["dense"], out)
+                continue
+            fn["router"](idx.ctypes.data, wt.ctypes.data, xn.ctypes.data, L["router"].ctypes.data,
+                         L["bias"].ctypes.data, E, N_EXPERTS, TOPK, 1, C.c_float(2.5))
+            acc = np.zeros(E, np.float32)
+            for j in range(TOPK):
+                e = pool[int(idx[j]) % len(pool)]
+                a, b = buf["g"][:INTER], buf["u"][:INTER]
+                fn["matmul_mxfp4"](a.ctypes.data, xn.ctypes.data, e["p1"].ctypes.data,
+                                   e["s1"].ctypes.data, E, INTER, 32)
+                fn["matmul_mxfp4"](b.ctypes.data, xn.ctypes.data, e["p3"].ctypes.data,
+                                   e["s3"].ctypes.data, E, INTER, 32)
+                act = ((a / (np.float32(1) + np.exp(-a))) * b).astype(np.float32)
+                fn["matmul_mxfp4"](buf["e"].ctypes.data, act.ctypes.data, e["p2"].ctypes.data,
+                                   e["s2"].ctypes.data, INTER, E, 32)
+                acc += wt[j] * buf["e"]
+            h += acc + swiglu(xn, *L["shared"], out)
+        fn["rmsnorm"](xn.ctypes.data, h.ctypes.data, final_norm.ctypes.data, E, C.c_float(1e-6))
+        mm(buf["lg"], xn, lm_head)
+        return int(np.argmax(buf["lg"]))
+
+    def timed(n):
+        ts = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            token()
+            ts.append(time.perf_counter() - t0)
+        return ts
+
+    token()                                               # warm-up
+    ts = timed(reps)
+    digest = fnv1a(buf["lg"])
+    gomp.omp_set_num_threads(1)
+    ts1 = timed(one_thread_reps)
+    gomp.omp_set_num_threads(threads)
+    best, med = min(ts), statistics.median(ts)
+    return {"value": 1.0 / med, "unit": "tok/s", "cores": threads, "kind": kind,
+            "best_tok_s": 1.0 / best, "median_tok_s": 1.0 / med,
+            "one_thread_tok_s": 1.0 / statistics.median(ts1), "reps": reps,
+            "one_thread_reps": one_thread_reps, "cpu_model": cpu_model,
+            "logits_fnv1a": digest,
+            "sample": f"{reps} whole config-4 tokens (8 layers at full width, context {context}, "
+                      f"LM head 163840 x 7168) after one warm-up, median {med * 1e3:.0f} ms, best "
+                      f"{best * 1e3:.0f} ms on {threads} threads; one thread "
+                      f"{statistics.median(ts1) * 1e3:.0f} ms; AVX2 k3_ops.c (-mavx2 -mfma: the "
+                      "path -march=native selects on an AVX-512 host), OpenMP"}
 
 
 # --------------------------------------------------------------------- GPU arm ----
@@ -609,6 +718,15 @@ def stack_cfg(world, rank, batch, cap, layout=1):
     return sc
 
 
+def stack_config(args, world):
+    """The workload description both arms print (the reference arm times the same model)."""
+    return {"workload": "config4 8-layer K3 stack decode", "batch": args.batch,
+            "context": args.context, "hidden": HIDDEN,
+            "layers": "KDA x6 + MLA x2 (one-based 4, 8); layer 0 dense 18432, layers 1-7 MoE "
+                      "384x top-8 + shared", "vocab": 163840, "parallelism": f"ep{world}",
+            "l2": "per-step weight stream of GBs >> 126 MB L2 (no flush needed)"}
+
+
 def bench_stack(args, rank, world):
     import k3cuda
     lib = k3cuda.init(0)
@@ -640,17 +758,17 @@ def bench_stack(args, rank, world):
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0)))
     clocks.start()
     lib.k3d_launch_count_reset()
-    step_ms = []
+    # one event pair around the K steps on the library stream, no host synchronisation
+    # inside the region: the host enqueues graph replays back to back
+    lib.k3d_event_record(ev[0])
     for i in range(args.steps):
-        lib.k3d_event_record(ev[0])
         k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "step")
-        lib.k3d_event_record(ev[1])
-        step_ms.append(lib.k3d_event_elapsed_ms(ev[0], ev[1]))
         k3cuda.check(lib.k3d_copy(ids.ptr, nxt.ptr, B * 4))   # greedy: next token in
+    lib.k3d_event_record(ev[1])
     k3cuda.check(lib.k3d_sync())
     clk = clocks.stop()
     barrier()
-    tot_ms = reduce_max(sum(step_ms))
+    tot_ms = reduce_max(lib.k3d_event_elapsed_ms(ev[0], ev[1]))
     step_bytes = lib.k3d_model_last_step_bytes(model)
     hbm, peak_kind = measured_peaks()
     # per-kernel device times from an eager pass with the section timers on (graph
@@ -685,14 +803,22 @@ def bench_stack(args, rank, world):
     if world > 1:
         alg_exp /= world
     achieved = alg_exp / (exp_ms * 1e-3) / 1e9
-    # end to end through the public API with host buffers: token ids in, next ids out
+    # end to end through the public API with host buffers: token ids in from host memory,
+    # next ids out to host memory, every step (greedy decoding); a few untimed steps first,
+    # then at least 200 timed steps so that host jitter averages out
     hid = np.zeros(B, np.int32)
     hnx = np.zeros(B, np.int32)
+    for i in range(3):
+        k3cuda.check(lib.k3d_model_step_host(model, hid.ctypes.data, hnx.ctypes.data), "e2e warm-up")
+        hid[:] = hnx
+    e2e_steps = max(args.steps, 200)
+    gen = np.zeros((e2e_steps, B), np.int32)
     barrier()
     t0 = time.perf_counter()
-    for i in range(args.steps):
+    for i in range(e2e_steps):
         k3cuda.check(lib.k3d_model_step_host(model, hid.ctypes.data, hnx.ctypes.data), "e2e step")
         hid[:] = hnx
+        gen[i] = hnx
     e2e_s = reduce_max(time.perf_counter() - t0)
     lib.k3d_model_destroy(model)
     ms = tot_ms / args.steps
@@ -702,11 +828,7 @@ def bench_stack(args, rank, world):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic random-init weights (bf16 ~N(0,0.02), MXFP4 experts E8M0 117..121); "
                 f"MLA latent caches ~N(0,1) and KDA states ~N(0,0.01) filled as after {ctx} tokens",
-        "config": {"workload": "config4 8-layer K3 stack decode", "batch": B, "context": ctx,
-                   "hidden": HIDDEN, "layers": "KDA x6 + MLA x2 (one-based 4, 8); layer 0 dense 18432, "
-                   "layers 1-7 MoE 384x top-8 + shared", "vocab": 163840,
-                   "parallelism": f"ep{world}", "graph": True,
-                   "l2": f"per-step working set {step_bytes / 1e9:.2f} GB >> 126 MB L2"},
+        "config": stack_config(args, world),
         "roofline": {"kernel": EXPERT_KERNEL[args.expert_kernel], "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": load_traffic("moe_experts_traffic.json"),
@@ -715,8 +837,9 @@ def bench_stack(args, rank, world):
                           "achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm},
         "sections_ms": sections,
-        "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                "d2h_bytes_per_step": 4 * B},
+        "e2e": {"value": B * e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B, "steps": e2e_steps,
+                "tokens_fnv1a": fnv1a(gen), "first_tokens": gen[:8, 0].tolist()},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clk,
         "init_s": init_s,
@@ -803,9 +926,8 @@ def main():
             return
         metric = METRIC
         if args.workload == "stack":
-            cb = cpu_stack_sample(args.cpu_seconds)
-            wl = {"workload": "config4 8-layer K3 stack decode", "batch": 1, "context": args.context,
-                  "hidden": HIDDEN, "vocab": 163840, "parallelism": "cpu"}
+            cb = cpu_stack_run(args.context, reps=max(5, min(args.steps, 10)))
+            wl = stack_config(args, world)
         elif args.workload == "kda_prefill":
             cb = cpu_kda_prefill_sample(args.cpu_seconds)
             metric = "KDA prefill tok/s (config 3: 64 heads, 128x128 fp32 state, chunk 64)"
@@ -838,7 +960,7 @@ def main():
         res = bench_moe_a2a(args, rank, world)
     if rank == 0:
         if world == 1 and args.cpu_seconds > 0 and args.workload != "moe_a2a":
-            res["cpu_baseline"] = (cpu_stack_sample(args.cpu_seconds) if args.workload == "stack"
+            res["cpu_baseline"] = (cpu_stack_run(args.context) if args.workload == "stack"
                                    else cpu_kda_prefill_sample(args.cpu_seconds)
                                    if args.workload == "kda_prefill"
                                    else cpu_moe_sample(seconds=args.cpu_seconds))

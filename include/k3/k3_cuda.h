@@ -44,7 +44,9 @@ enum {
 };
 
 /* Select the CUDA device and create the library stream. Idempotent for the same
- * device; the k3.h entry points call k3d_init(0) on first use if nobody did. */
+ * device; the k3.h entry points call k3d_init(0) on first use if nobody did. One device
+ * per process: once the context exists, k3d_init with another device returns K3D_EINVAL
+ * (run one process per GPU, as the expert-parallel launch does). */
 int         k3d_init(int device);
 int         k3d_device(void);
 /* The first error since the last k3d_clear_status(); also folds in the device error

@@ -7,6 +7,8 @@
 #include <stdint.h>
 #include <stddef.h>
 
+#include <mutex>
+
 #include "k3.h"
 #include "k3_cuda.h"
 
@@ -17,6 +19,8 @@ namespace k3 {
 int fail(int code, const char *fmt, ...);
 // Ensures the context exists on the current device; returns K3D_OK or an error.
 int ensure_ctx();
+// Guards the context's one-time set-up (k3d_init and the per-device look-ups).
+extern std::recursive_mutex g_mu;
 cudaStream_t stream();
 cudaStream_t side_stream();          // null if it could not be created
 cudaEvent_t side_event(int i);       // fork/join events of the side stream (i = 0..3)

@@ -51,7 +51,6 @@ struct Ctx {
 };
 
 Ctx g;
-std::recursive_mutex g_mu;
 
 void record(int code, const char *text)
 {
@@ -99,6 +98,8 @@ void prof_collect(Ctx::Sec &sec)
 }
 
 }  // namespace
+
+std::recursive_mutex g_mu;
 
 void allow_dyn_smem(const void *func)
 {
@@ -373,6 +374,11 @@ int k3d_init(int device)
 {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     if (g.ready && g.device == device) { cudaSetDevice(device); return K3D_OK; }
+    // One device per process: the workspaces, the side stream and each kernel's one-time
+    // shared-memory opt-in belong to the device the context was made on.
+    if (g.ready)
+        return fail(K3D_EINVAL, "k3d_init(%d): this process's context is on device %d; one "
+                    "device per process", device, g.device);
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
         cudaGetLastError();

@@ -18,6 +18,28 @@
  *
  * The 2^(i/32) table holds the correctly rounded doubles; the CPU tests recompute them
  * with 60-digit decimal arithmetic.
+ *
+ * Attribution and licence of the restated method and its table: ARM optimized-routines,
+ * single-precision e^x, Copyright (c) 2017-2018, Arm Limited, SPDX-License-Identifier: MIT
+ * (the project is also offered under Apache-2.0 WITH LLVM-exception); GNU libc carries the
+ * same method. The MIT licence notice:
+ *
+ *   Permission is hereby granted, free of charge, to any person obtaining a copy of this
+ *   software and associated documentation files (the "Software"), to deal in the Software
+ *   without restriction, including without limitation the rights to use, copy, modify,
+ *   merge, publish, distribute, sublicense, and/or sell copies of the Software, and to
+ *   permit persons to whom the Software is furnished to do so, subject to the following
+ *   conditions:
+ *
+ *   The above copyright notice and this permission notice shall be included in all copies
+ *   or substantial portions of the Software.
+ *
+ *   THE SOFTWARE IS PROVIDED "AS IS", WITHOUT WARRANTY OF ANY KIND, EXPRESS OR IMPLIED,
+ *   INCLUDING BUT NOT LIMITED TO THE WARRANTIES OF MERCHANTABILITY, FITNESS FOR A
+ *   PARTICULAR PURPOSE AND NONINFRINGEMENT. IN NO EVENT SHALL THE AUTHORS OR COPYRIGHT
+ *   HOLDERS BE LIABLE FOR ANY CLAIM, DAMAGES OR OTHER LIABILITY, WHETHER IN AN ACTION OF
+ *   CONTRACT, TORT OR OTHERWISE, ARISING FROM, OUT OF OR IN CONNECTION WITH THE SOFTWARE
+ *   OR THE USE OR OTHER DEALINGS IN THE SOFTWARE.
  */
 #ifndef K3_EXPF_H
 #define K3_EXPF_H

@@ -1076,18 +1076,24 @@ int k3d_router_bf16_noalloc(int *idx, float *w, const float *x, const uint16_t *
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return fail(K3D_ECUDA, "k3d_router_bf16_noalloc: device %d: %s", dev, cudaGetErrorString(e));
-    // set-up once per device: the address of the scratch array in this device's module
+    // set-up once per device: the address of the scratch array in this device's module,
+    // looked up under the context lock so that first calls from two threads do not race
     static void *ws_of[kMaxDevices];
-    if (!ws_of[dev]) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_router_noalloc_ws);
-        if (e != cudaSuccess || !p)
-            return fail(K3D_ECUDA, "k3d_router_bf16_noalloc: scratch address: %s",
-                        cudaGetErrorString(e));
-        ws_of[dev] = p;
+    void *ws = nullptr;
+    {
+        std::lock_guard<std::recursive_mutex> lk(g_mu);
+        if (!ws_of[dev]) {
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_router_noalloc_ws);
+            if (e != cudaSuccess || !p)
+                return fail(K3D_ECUDA, "k3d_router_bf16_noalloc: scratch address: %s",
+                            cudaGetErrorString(e));
+            ws_of[dev] = p;
+        }
+        ws = ws_of[dev];
     }
     return router_bf16(idx, w, x, W, bias, T, hidden, n_experts, topk, renorm, routed_scale,
-                       ws_of[dev], stream());
+                       ws, stream());
 }
 
 }  // extern "C"

@@ -151,12 +151,14 @@ static double dot16(const float *row, const float *x, int in, const uint16_t *br
 
 void orc_matmul(float *y, const float *x, const float *W, int in, int out)
 {
+    #pragma omp parallel for schedule(static) if ((long)in * out > 262144)
     for (int o = 0; o < out; o++) y[o] = (float)dot16(W + (size_t)o * in, x, in, NULL);
 }
 
 /* k3_ops.c:1108-1213 (scalar path): bit-identical to orc_matmul on widened weights */
 void orc_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out)
 {
+    #pragma omp parallel for schedule(static) if ((long)in * out > 262144)
     for (int o = 0; o < out; o++) y[o] = (float)dot16(NULL, x, in, W + (size_t)o * in);
 }
 
@@ -364,6 +366,7 @@ void orc_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
         abort();
     }
     const int pcols = in / 2, ngrp = (in + group - 1) / group;
+    #pragma omp parallel for schedule(static) if ((long)in * rows > 262144)
     for (int r = 0; r < rows; r++) {
         const unsigned char *pr = packed + (size_t)r * pcols;
         const unsigned char *sr = scales + (size_t)r * ngrp;
@@ -676,6 +679,13 @@ void orc_rope(float *x, int d, int pos, float theta)
  * token's latent and rotated rope key are rounded to bf16 when written, and attention
  * reads them back from the cache. cache [B][cap][kv_lora + rope]; positions [0, pos) are
  * filled and the new token is written at pos. */
+/* When set, the attention of orc_mla_decode reads the new token's latent and rope key in
+ * fp32, as the reference's k3_mla_cached does with its fp32 cache; the cache still receives
+ * the bf16 rounding. Only the test that pins this restatement against the compiled
+ * reference sets it: with it, the two compute the same arithmetic. */
+static int g_mla_new_entry_fp32 = 0;
+void orc_set_mla_new_entry_fp32(int on) { g_mla_new_entry_fp32 = on != 0; }
+
 void orc_mla_decode(float *out, const float *x, int B, int hidden, int H, int q_lora,
                     int kv_lora, int qn, int qr, int vh, float theta, float eps,
                     const uint16_t *q_a, const uint16_t *q_b, const uint16_t *kv_a,
@@ -706,8 +716,10 @@ void orc_mla_decode(float *out, const float *x, int B, int hidden, int H, int q_
         orc_rope(c + kv_lora, qr, pos, theta);
         for (int i = 0; i < kvw; i++) cb[(size_t)pos * kvw + i] = orc_f2bf(c[i]);
         for (int s = 0; s <= pos; s++) {
-            for (int i = 0; i < kv_lora; i++) cl[i] = orc_bf16f(cb[(size_t)s * kvw + i]);
-            for (int i = 0; i < qr; i++) kr[(size_t)s * qr + i] = orc_bf16f(cb[(size_t)s * kvw + kv_lora + i]);
+            const int wide = g_mla_new_entry_fp32 && s == pos;
+            for (int i = 0; i < kv_lora; i++) cl[i] = wide ? c[i] : orc_bf16f(cb[(size_t)s * kvw + i]);
+            for (int i = 0; i < qr; i++)
+                kr[(size_t)s * qr + i] = wide ? c[kv_lora + i] : orc_bf16f(cb[(size_t)s * kvw + kv_lora + i]);
             orc_matmul_bf16(kv + (size_t)s * H * kvd, cl, kv_b, kv_lora, H * kvd);
         }
         for (int h = 0; h < H; h++) {
@@ -738,4 +750,90 @@ void orc_mla_decode(float *out, const float *x, int B, int hidden, int H, int q_
         orc_matmul_bf16(out + (size_t)b * hidden, acc, o, H * vh, hidden);
     }
     free(ql); free(q); free(c); free(cl); free(kv); free(kr); free(sc); free(acc); free(gb);
+}
+
+/* config 2 in the ABSORBED form: the same attention as orc_mla_decode (k3_ops.c:321-410's
+ * arithmetic with this file's RoPE and bf16 latent cache), with kv_b folded into the query
+ * and the output instead of expanding every cached latent. Per head h, with W_uk[h] the
+ * qn rows of kv_b that make the keys and W_uv[h] the vh rows that make the values:
+ *   q_lat = W_uk[h]^T q_nope,  score_s = (q_lat . c_s + q_rope . kr_s) * scale,
+ *   p = softmax(score) (float exp, double sum, as the reference),
+ *   ctx = sum_s p_s c_s,  o_h = W_uv[h] ctx.
+ * Every sum runs in double, so the only roundings are the float score, the float exp and
+ * the float probability, as in the expanded form; the expanded form's fp32 rounding of each
+ * expanded key and value is absent here, a difference of a few fp32 ulps. O(L (2 kv_lora +
+ * rope)) per head instead of O(L kv_lora (qn + vh)), which makes config 2's L = 32768 and
+ * B = 32 checkable. OpenMP runs heads in parallel; each head's arithmetic is fixed. */
+void orc_mla_decode_absorbed(float *out, const float *x, int B, int hidden, int H, int q_lora,
+                             int kv_lora, int qn, int qr, int vh, float theta, float eps,
+                             const uint16_t *q_a, const uint16_t *q_b, const uint16_t *kv_a,
+                             const uint16_t *kv_b, const uint16_t *o, const uint16_t *g,
+                             const float *q_a_norm, const float *kv_a_norm, uint16_t *cache,
+                             int cap, int pos)
+{
+    const int qh = qn + qr, kvw = kv_lora + qr, kvd = qn + vh;
+    const float scale = 1.0f / sqrtf((float)qh);
+    const int L = pos + 1;
+    float *ql = (float *)xmalloc((size_t)q_lora * sizeof(float));
+    float *q = (float *)xmalloc((size_t)H * qh * sizeof(float));
+    float *c = (float *)xmalloc((size_t)kvw * sizeof(float));
+    float *cf = (float *)xmalloc((size_t)L * kvw * sizeof(float));
+    float *acc = (float *)xmalloc((size_t)H * vh * sizeof(float));
+    float *gb = (float *)xmalloc((size_t)H * vh * sizeof(float));
+    for (int b = 0; b < B; b++) {
+        const float *xb = x + (size_t)b * hidden;
+        uint16_t *cb = cache + (size_t)b * cap * kvw;
+        orc_matmul_bf16(ql, xb, q_a, hidden, q_lora);
+        orc_rmsnorm(ql, ql, q_a_norm, q_lora, eps);
+        orc_matmul_bf16(q, ql, q_b, q_lora, H * qh);
+        for (int h = 0; h < H; h++) orc_rope(q + (size_t)h * qh + qn, qr, pos, theta);
+        orc_matmul_bf16(c, xb, kv_a, hidden, kvw);
+        orc_rmsnorm(c, c, kv_a_norm, kv_lora, eps);
+        orc_rope(c + kv_lora, qr, pos, theta);
+        for (int i = 0; i < kvw; i++) cb[(size_t)pos * kvw + i] = orc_f2bf(c[i]);
+        #pragma omp parallel for schedule(static)
+        for (long i = 0; i < (long)L * kvw; i++) cf[i] = orc_bf16f(cb[i]);
+        #pragma omp parallel for schedule(dynamic, 1)
+        for (int h = 0; h < H; h++) {
+            const float *qt = q + (size_t)h * qh;
+            double *qlat = (double *)xmalloc((size_t)kv_lora * sizeof(double));
+            double *ctx = (double *)xmalloc((size_t)kv_lora * sizeof(double));
+            float *sc = (float *)xmalloc((size_t)L * sizeof(float));
+            for (int i = 0; i < kv_lora; i++) { qlat[i] = 0.0; ctx[i] = 0.0; }
+            for (int j = 0; j < qn; j++) {
+                const uint16_t *wr = kv_b + ((size_t)h * kvd + j) * kv_lora;
+                const double qj = (double)qt[j];
+                for (int i = 0; i < kv_lora; i++) qlat[i] += qj * (double)orc_bf16f(wr[i]);
+            }
+            float m = -INFINITY;
+            for (int s_ = 0; s_ < L; s_++) {
+                const float *cs = cf + (size_t)s_ * kvw;
+                double d = 0.0;
+                for (int i = 0; i < kv_lora; i++) d += qlat[i] * (double)cs[i];
+                for (int i = 0; i < qr; i++) d += (double)qt[qn + i] * (double)cs[kv_lora + i];
+                sc[s_] = (float)d * scale;
+                if (sc[s_] > m) m = sc[s_];
+            }
+            double z = 0.0;
+            for (int s_ = 0; s_ < L; s_++) { sc[s_] = expf(sc[s_] - m); z += sc[s_]; }
+            for (int s_ = 0; s_ < L; s_++) {
+                const double pr = (double)(float)(sc[s_] / z);
+                const float *cs = cf + (size_t)s_ * kvw;
+                for (int i = 0; i < kv_lora; i++) ctx[i] += pr * (double)cs[i];
+            }
+            for (int j = 0; j < vh; j++) {
+                const uint16_t *wr = kv_b + ((size_t)h * kvd + qn + j) * kv_lora;
+                double d = 0.0;
+                for (int i = 0; i < kv_lora; i++) d += (double)orc_bf16f(wr[i]) * ctx[i];
+                acc[(size_t)h * vh + j] = (float)d;
+            }
+            free(qlat); free(ctx); free(sc);
+        }
+        if (g) {
+            orc_matmul_bf16(gb, xb, g, hidden, H * vh);
+            for (int i = 0; i < H * vh; i++) acc[i] *= 1.0f / (1.0f + expf(-gb[i]));
+        }
+        orc_matmul_bf16(out + (size_t)b * hidden, acc, o, H * vh, hidden);
+    }
+    free(ql); free(q); free(c); free(cf); free(acc); free(gb);
 }

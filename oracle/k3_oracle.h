@@ -85,7 +85,14 @@ void  orc_moe_swiglu(float *out, const float *x, int T, int hidden, int inter,
 /* RoPE on interleaved pairs, frequency theta^(-2i/d) */
 void  orc_rope(float *x, int d, int pos, float theta);
 /* config 2: MLA decode over a bf16 latent cache, expanded form (see the .c file) */
+void  orc_set_mla_new_entry_fp32(int on);
 void  orc_mla_decode(float *out, const float *x, int B, int hidden, int H, int q_lora,
+                     int kv_lora, int qn, int qr, int vh, float theta, float eps,
+                     const uint16_t *q_a, const uint16_t *q_b, const uint16_t *kv_a,
+                     const uint16_t *kv_b, const uint16_t *o, const uint16_t *g,
+                     const float *q_a_norm, const float *kv_a_norm, uint16_t *cache, int cap,
+                     int pos);
+void  orc_mla_decode_absorbed(float *out, const float *x, int B, int hidden, int H, int q_lora,
                      int kv_lora, int qn, int qr, int vh, float theta, float eps,
                      const uint16_t *q_a, const uint16_t *q_b, const uint16_t *kv_a,
                      const uint16_t *kv_b, const uint16_t *o, const uint16_t *g,

@@ -162,9 +162,10 @@ class Oracle(_Common):
         L.orc_moe_swiglu.restype = None
         L.orc_kda_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]
         L.orc_kda_decode.restype = None
-        L.orc_mla_decode.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, f32,
-                                     vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32]
-        L.orc_mla_decode.restype = None
+        for fn in (L.orc_mla_decode, L.orc_mla_decode_absorbed):
+            fn.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, f32,
+                           vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32]
+            fn.restype = None
 
     def expert_swiglu(self, x, e, hidden, inter):
         """e: dict with numpy arrays p1,s1,p3,s3,p2,s2."""
@@ -224,12 +225,16 @@ class Reference(_Common):
         _declare(self.lib, "k3_")
 
 
-def mla_decode(orc, x, dims, w, cache, pos):
+def mla_decode(orc, x, dims, w, cache, pos, absorbed=False):
     """config-2 oracle: x [B][hidden]; dims dict; w dict of numpy weights (bf16 as uint16,
-    norms fp32); cache [B][cap][kvw] uint16, updated in place at `pos`."""
+    norms fp32); cache [B][cap][kvw] uint16, updated in place at `pos`. absorbed=True takes
+    the absorbed form (orc_mla_decode_absorbed: same attention, O(L) per head), which the
+    CPU tests check against the expanded form; the expanded form is checked against the
+    compiled reference's k3_mla_cached."""
     B = x.shape[0]
     out = np.empty((B, dims["hidden"]), np.float32)
-    orc.lib.orc_mla_decode(ptr(out), ptr(np.ascontiguousarray(x, np.float32)), B, dims["hidden"],
+    fn = orc.lib.orc_mla_decode_absorbed if absorbed else orc.lib.orc_mla_decode
+    fn(ptr(out), ptr(np.ascontiguousarray(x, np.float32)), B, dims["hidden"],
                            dims["H"], dims["q_lora"], dims["kv_lora"], dims["qn"], dims["qr"],
                            dims["vh"], dims["theta"], dims["eps"], ptr(w["q_a"]), ptr(w["q_b"]),
                            ptr(w["kv_a"]), ptr(w["kv_b"]), ptr(w["o"]), ptr(w.get("g")),
@@ -282,9 +287,11 @@ def silu_mul(g, u):
 
 
 def stack_step(orc, cfg, W, S, token):
-    """One decode step of the synthetic stack on host copies. cfg: dict; W: weights by
-    name (numpy); S: mutable state {"pos", "layer<l>.kda.state", "layer<l>.mla.cache"}.
-    Returns logits (float32 [vocab])."""
+    """One decode step of the synthetic stack on host copies. cfg: dict (cfg["mla_absorbed"]
+    selects the absorbed MLA form); W: weights by name (numpy; a layer's "moe.experts" is a
+    list of expert dicts, or an object whose select(idx) returns such a list holding at least
+    the experts idx names); S: mutable state {"pos", "layer<l>.kda.state",
+    "layer<l>.mla.cache"}. Returns logits (float32 [vocab])."""
     E = cfg["hidden"]
     h = (W["embed"].reshape(cfg["vocab"], E)[token].astype(np.uint32) << 16).view(np.float32).copy()
     for l in range(cfg["n_layers"]):
@@ -295,7 +302,8 @@ def stack_step(orc, cfg, W, S, token):
             w = {k: W[p + "mla." + k] for k in ("q_a", "q_b", "kv_a", "kv_b", "o", "g",
                                                  "q_a_norm", "kv_a_norm")}
             cache = S[p + "mla.cache"]
-            out = mla_decode(orc, xn[None], m, w, cache, S["pos"])[0]
+            out = mla_decode(orc, xn[None], m, w, cache, S["pos"],
+                             absorbed=cfg.get("mla_absorbed", False))[0]
         else:
             w = {k: W[p + "kda." + k] for k in ("q", "k", "v", "q_conv", "k_conv", "v_conv", "f_a",
                                                  "f_b", "A_log", "dt_bias", "b", "g", "o_norm", "o")}
@@ -308,9 +316,16 @@ def stack_step(orc, cfg, W, S, token):
             out = orc.matmul_bf16(a, W[p + "dense.down"])
         else:
             mo = cfg["moe"]
+            experts = W[p + "moe.experts"]
+            if hasattr(experts, "select"):
+                # experts held on the device and fetched on demand: route first (the same
+                # deterministic router the layer runs again), then fetch the selected ones
+                idx, _ = orc.router_bf16(xn, W[p + "moe.router_w"], W[p + "moe.router_bias"],
+                                         mo["topk"], 1, mo["routed_scale"])
+                experts = experts.select(idx)
             out, _, _ = orc.moe_swiglu(xn[None], 1, E, mo["inter"], mo["n_experts"], mo["topk"], 1,
                                        mo["routed_scale"], W[p + "moe.router_w"],
-                                       W[p + "moe.router_bias"], W[p + "moe.experts"],
+                                       W[p + "moe.router_bias"], experts,
                                        mo["shared_inter"], W[p + "moe.sh_gate"], W[p + "moe.sh_up"],
                                        W[p + "moe.sh_down"])
             out = out[0]

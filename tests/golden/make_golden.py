@@ -8,7 +8,7 @@
    seeded synthetic inputs at the benchmark shapes (tests/golden/synth.py), with a digest
    of the inputs.
 
-    python tests/golden/make_golden.py [--reference <path of the reference source tree>]
+    python tests/golden/make_golden.py --reference <path of the reference source tree>
 """
 import argparse
 import json
@@ -76,7 +76,8 @@ def reference_goldens():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="path of the reference source tree (read only)")
     args = ap.parse_args()
     fx = os.path.join(args.reference, "tests", "fixtures")
     os.makedirs(os.path.join(HERE, "ref_ops"), exist_ok=True)

@@ -35,3 +35,18 @@ def test_reference_arm_prints_one_json_line(workload):
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
     assert d["config"]["workload"]
+
+
+def test_reference_arm_threads_ignore_launcher_omp_setting():
+    """torchrun exports OMP_NUM_THREADS=1; the CPU arm sets its own thread count (one per
+    physical core it may run on), so the figure at N > 1 is taken like the one at N = 1."""
+    import psutil
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference",
+                        "--workload", "moe", "--steps", "3", "--warmup", "3", "--cpu-seconds", "1"],
+                       cwd=REPO, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    aff = len(os.sched_getaffinity(0))
+    want = max(1, min(aff, psutil.cpu_count(logical=False) or aff))
+    assert d["cpu_baseline"]["cores"] == want

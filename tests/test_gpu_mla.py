@@ -71,6 +71,24 @@ def test_mla_decode_matches_oracle(k3, oracle, B, L):
     assert max_rel_err(y, want) <= 1e-3
 
 
+# config 2 at its own sizes: L = 4096 at B = 1 (the stack's context; 37 position splits
+# and the merge) and at B = 32, and L = 32768 at B = 1; against the absorbed-form oracle
+# (pinned to the expanded form and, through it, to the reference's k3_mla_cached)
+@pytest.mark.parametrize("B,L", [(1, 4096), (32, 4096), (1, 32768)])
+def test_mla_decode_config2_sizes_match_oracle(k3, oracle, B, L):
+    cap = L + 8
+    w, cache, x = make(20 + B + L, DIMS, B, cap, L)
+    y, cache_gpu = run_gpu(k3, DIMS, w, cache, x, L, cap)
+    cache_cpu = cache.copy()
+    want = orc_mod.mla_decode(oracle, x, DIMS, w, cache_cpu, L, absorbed=True)
+    new_g = synth.bf16_to_f32(cache_gpu[:, L])
+    new_c = synth.bf16_to_f32(cache_cpu[:, L])
+    assert max_rel_err(new_g, new_c) <= 1e-2
+    assert np.array_equal(cache_gpu[:, :L], cache[:, :L]), "earlier positions must be untouched"
+    for b in range(B):
+        assert max_rel_err(y[b], want[b]) <= 1e-3, b
+
+
 def test_mla_decode_nope_small_dims_and_accumulate(k3, oracle):
     d = dict(hidden=256, H=8, q_lora=64, kv_lora=128, qn=32, qr=16, vh=32, theta=0.0, eps=1e-5)
     cap, L = 96, 70

@@ -91,7 +91,45 @@ def untile_expert(slot, hidden, inter):
             (("p1", p1), ("s1", s1), ("p3", p3), ("s3", s3), ("p2", p2), ("s2", s2))}
 
 
-def host_copy(k3, model, c, layout=0, batch=1, cap=64):
+class DeviceExperts:
+    """A layer's routed experts left on the device and downloaded on demand (a full-width
+    layer holds 8.98 GB of them): select(idx) returns the oracle's expert list with the
+    experts idx names filled in (un-tiled for the tiled layout) and None elsewhere."""
+
+    def __init__(self, k3, model, name, hidden, inter, n_experts, slot, layout):
+        n = ctypes.c_size_t()
+        self.base = k3.k3d_model_tensor(model, name.encode(), ctypes.byref(n))
+        assert self.base, name
+        self.k3, self.hidden, self.inter, self.n, self.slot, self.layout = (
+            k3, hidden, inter, n_experts, slot, layout)
+        gu, gus = inter * hidden // 2, inter * hidden // 32
+        self.sizes = [gu, gus, gu, gus, gu, gus]
+        self.offs, o = [], 0
+        for s_ in self.sizes:
+            self.offs.append(o)
+            o += (s_ + 255) // 256 * 256
+        assert o == slot
+        self.cache = {}
+
+    def get(self, e):
+        if e not in self.cache:
+            raw = np.empty(self.slot, np.uint8)
+            k3cuda.check(self.k3.k3d_download(raw.ctypes.data, self.base + e * self.slot, self.slot))
+            if self.layout == 1:
+                self.cache[e] = untile_expert(raw, self.hidden, self.inter)
+            else:
+                self.cache[e] = {k: np.ascontiguousarray(raw[off:off + s_]) for k, off, s_ in
+                                 zip(("p1", "s1", "p3", "s3", "p2", "s2"), self.offs, self.sizes)}
+        return self.cache[e]
+
+    def select(self, idx):
+        out = [None] * self.n
+        for e in np.asarray(idx).ravel():
+            out[int(e)] = self.get(int(e))
+        return out
+
+
+def host_copy(k3, model, c, layout=0, batch=1, cap=64, lazy_experts=False):
     E, P, D, H = c["hidden"], c["kda_heads"] * c["kda_head_dim"], c["kda_head_dim"], c["kda_heads"]
     m, mo = c["mla"], c["moe"]
     W, S = {}, {}
@@ -131,13 +169,17 @@ def host_copy(k3, model, c, layout=0, batch=1, cap=64):
             for k, shp in (("sh_gate", (mo["shared_inter"], E)), ("sh_up", (mo["shared_inter"], E)),
                            ("sh_down", (E, mo["shared_inter"]))):
                 W[p + "moe." + k] = download(k3, model, p + "moe." + k, np.uint16, shp)
-            pool = download(k3, model, p + "moe.pool", np.uint8)
             gu, gus = mo["inter"] * E // 2, mo["inter"] * E // 32
             sizes = [gu, gus, gu, gus, gu, gus]
             offs, o = [], 0
             for s_ in sizes:
                 offs.append(o)
                 o += (s_ + 255) // 256 * 256
+            if lazy_experts:
+                W[p + "moe.experts"] = DeviceExperts(k3, model, p + "moe.pool", E, mo["inter"],
+                                                     mo["n_experts"], o, layout)
+                continue
+            pool = download(k3, model, p + "moe.pool", np.uint8)
             experts = []
             for e in range(mo["n_experts"]):
                 base = e * o
