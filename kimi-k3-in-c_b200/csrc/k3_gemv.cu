@@ -517,8 +517,8 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
 
 int gemv_tagged(float *y, const float *x, const void *W, int wdt, int in, int out, cudaStream_t s)
 {
-    if (wdt == K3_WBF16) return gemv_bf16(y, x, (const uint16_t *)W, in, out, 1, 0, s);
-    if (wdt == K3_WF32) return gemv_f32(y, x, (const float *)W, in, out, s);
+    if (wdt == K3_WBF16) return gemv_ref_bf16(y, x, (const uint16_t *)W, in, out, 1, 0, s);
+    if (wdt == K3_WF32) return gemv_ref_f32(y, x, (const float *)W, in, out, 1, 0, s);
     return fail(K3D_EUNSUPPORTED, "weight tag %d (the int8 draft format is not served here)", wdt);
 }
 
@@ -553,7 +553,7 @@ void k3_matmul(float *y, const float *x, const float *W, int in, int out)
     const float *X = (const float *)st.in(x, (size_t)in * sizeof(float));
     float *Y = (float *)st.out(y, (size_t)out * sizeof(float));
     if (st.err) return;
-    if (gemv_f32(Y, X, Wd, in, out, stream())) return;
+    if (gemv_ref_f32(Y, X, Wd, in, out, 1, 0, stream())) return;
     st.finish();
 }
 
@@ -566,7 +566,7 @@ void k3_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out
     const float *X = (const float *)st.in(x, (size_t)in * sizeof(float));
     float *Y = (float *)st.out(y, (size_t)out * sizeof(float));
     if (st.err) return;
-    if (gemv_bf16(Y, X, Wd, in, out, 1, 0, stream())) return;
+    if (gemv_ref_bf16(Y, X, Wd, in, out, 1, 0, stream())) return;
     st.finish();
 }
 

@@ -405,7 +405,7 @@ template <int NV, int RES>
 __device__ __forceinline__ void issue_weights(uint32_t sb, uint32_t fb, const Job &J, const ItemEnt &it,
                                               int chunk)
 {
-    const size_t tix = (size_t)it.tile * J.nch + chunk;
+    const size_t tix = (size_t)chunk * J.ntiles + it.tile;
     bulk_g2s(sb, it.c0 + tix * kTileA, kTileA, fb);
     bulk_g2s(sb + Geo<NV, RES>::kSFA, it.s0 + tix * kTileSF, kTileSF, fb);
 }
@@ -1095,17 +1095,20 @@ __global__ void k_bsplit_swiglu_group(uint8_t *bq, uint8_t *bs, const float *par
 
 // ------------------------------------------------------------- weight tiling
 // Rewrites MXFP4 weights from the checkpoint layout into the stage-ordered tiled layout:
-// for 128-row tile t and 512-element chunk c, a 32 KB block at codes + 32768 (t * nch + c)
+// for 128-row tile t and 512-element chunk c, a 32 KB block at codes + 32768 (c * ntiles + t)
 // holding the tile's codes exactly as the kernel's shared-memory stage (SWIZZLE_128B
-// K-major), and a 2 KB block at sf + 2048 (t * nch + c) holding its scales as the four
-// tcgen05.cp atoms, with E8M0 255 replaced by 0. Gate/up tiles interleave 64 gate rows and
-// the same 64 up rows (c1/s1 given); down tiles are 128 rows of one matrix (c1 null).
-// grid (ntiles * nch), 256 threads.
+// K-major), and a 2 KB block at sf + 2048 (c * ntiles + t) holding its scales as the four
+// tcgen05.cp atoms, with E8M0 255 replaced by 0. Blocks are chunk-major: the kernel walks
+// its items (vector, chunk, tile) with the tile fastest, so the weight stream of a CTA is
+// one contiguous region of memory, as a GEMV's row stream is. Gate/up tiles interleave 64
+// gate rows and the same 64 up rows (c1/s1 given); down tiles are 128 rows of one matrix
+// (c1 null). grid (ntiles * nch), 256 threads.
 __global__ void k_pretile(uint8_t *dc, uint8_t *ds, const uint8_t *c0, const uint8_t *s0,
                           const uint8_t *c1, const uint8_t *s1, int K)
 {
     const int nch = K / kStageK;
-    const int t = blockIdx.x / nch, c = blockIdx.x % nch;
+    const int ntiles = gridDim.x / nch;
+    const int c = blockIdx.x / ntiles, t = blockIdx.x % ntiles;
     const int rowbytes = K >> 1, sfrow = K >> 5;
     const bool gu = c1 != nullptr;
     uint8_t *dtile = dc + (size_t)blockIdx.x * kTileA;

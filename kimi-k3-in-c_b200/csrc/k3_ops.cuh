@@ -40,7 +40,13 @@ int gemv_bf16_argmax(float *y, unsigned long long *key, int *next, const float *
 // x RMS-normalised into the library scratch (slot 0) for consumers that cannot normalise on
 // load; returns the normalised copy, or null with the error recorded.
 const float *norm_to_scratch(const float *x, const NormIn &ni, int n, int rows, cudaStream_t s);
-// tagged weight: wdt 0 fp32, 1 bf16
+// k3_gemv_ref.cu: k3_matmul's double-accumulator order, bit-exact with the CPU engine
+// (the reference-semantics entry points); T rows of x one after another
+int gemv_ref_f32(float *y, const float *x, const float *W, int in, int out, int T, int accumulate,
+                 cudaStream_t s);
+int gemv_ref_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int T, int accumulate,
+                  cudaStream_t s);
+// tagged weight: wdt 0 fp32, 1 bf16 (the CPU engine's arithmetic, through gemv_ref_*)
 int gemv_tagged(float *y, const float *x, const void *W, int wdt, int in, int out,
                 cudaStream_t s);
 

@@ -324,10 +324,10 @@ static int moe_dev(float *out, const float *x, const K3MoeW *w, const K3Cfg *c, 
                 K3_TRY(es.finish());
             } else {
                 const size_t e = (size_t)idx_host[j];
-                K3_TRY(gemv_f32(gu, z, w->w1 + e * I * L, L, I, st));
-                K3_TRY(gemv_f32(gu + I, z, w->w3 + e * I * L, L, I, st));
+                K3_TRY(gemv_ref_f32(gu, z, w->w1 + e * I * L, L, I, 1, 0, st));
+                K3_TRY(gemv_ref_f32(gu + I, z, w->w3 + e * I * L, L, I, 1, 0, st));
                 K3_TRY(situ_glu(act, gu, I, 1, c->situ_b1, c->situ_b2, st));
-                K3_TRY(gemv_f32(edn, act, w->w2 + e * L * I, I, L, st));
+                K3_TRY(gemv_ref_f32(edn, act, w->w2 + e * L * I, I, L, 1, 0, st));
             }
             EW(k_axpy_ordered, (size_t)L, accL, dwt, j, edn, (size_t)L);
         }

@@ -132,6 +132,28 @@ def test_gemv_bf16_and_f32(k3, oracle, inp, out):
     assert max_rel_err(y, oracle.matmul(x, W)) <= 1e-5
 
 
+@pytest.mark.parametrize("inp,out", [(7168, 4096), (257, 129), (100, 33), (15, 7), (16, 1)])
+def test_k3_matmul_bit_exact_with_cpu_engine(k3, oracle, reference, inp, out):
+    """k3_matmul and k3_matmul_bf16 reproduce the CPU engine's sixteen double accumulators
+    and reduction tree (k3_ops.c:265-291) bit for bit, tails included; the CPU side is the
+    compiled reference and the oracle's restatement of it."""
+    g = synth.rng(3 * inp + out)
+    W = g.standard_normal((out, inp), dtype=np.float32) * np.float32(0.5)
+    Wb = synth.f32_to_bf16(W)
+    x = g.standard_normal(inp, dtype=np.float32)
+    y = np.empty(out, np.float32)
+    k3.k3_matmul(y.ctypes.data, x.ctypes.data, W.ctypes.data, inp, out)
+    assert np.array_equal(y.view(np.uint32), reference.matmul(x, W).view(np.uint32))
+    assert np.array_equal(y.view(np.uint32), oracle.matmul(x, W).view(np.uint32))
+    yb = np.empty(out, np.float32)
+    k3.k3_matmul_bf16(yb.ctypes.data, x.ctypes.data, Wb.ctypes.data, inp, out)
+    assert np.array_equal(yb.view(np.uint32), reference.matmul_bf16(x, Wb).view(np.uint32))
+    # the engine's own gate: the bf16 path equals the fp32 path on the widened weights
+    Ww = np.ascontiguousarray(synth.bf16_to_f32(Wb))
+    k3.k3_matmul(y.ctypes.data, x.ctypes.data, Ww.ctypes.data, inp, out)
+    assert np.array_equal(y.view(np.uint32), yb.view(np.uint32))
+
+
 def test_kda_step_fixture_and_bit_exact(k3, oracle):
     d, meta = load_npz("ref_ops/kda_recur8.npz")
     atol, rtol = manifest_tol()

@@ -48,7 +48,8 @@ def download(k3, model, name, dtype, shape=None):
 
 def _untile(codes, sf, K, rows, gu):
     """Inverse of k3d_expert_pretile for one matrix pair: tiles of 128 rows x 512 elements
-    (codes in the SWIZZLE_128B K-major image, scales as four 32x16-byte atoms)."""
+    (codes in the SWIZZLE_128B K-major image, scales as four 32x16-byte atoms), the block of
+    (tile t, chunk c) at position c * ntiles + t."""
     nch = K // 512
     ntiles = rows // 64 if gu else rows // 128
     r = np.arange(128)[:, None]
@@ -63,7 +64,7 @@ def _untile(codes, sf, K, rows, gu):
     out_s = np.zeros((ntiles * 128, K // 32), np.uint8)
     for t in range(ntiles):
         for c in range(nch):
-            blk = (t * nch + c)
+            blk = c * ntiles + t          # chunk-major blocks
             tile = codes[blk * 32768:(blk + 1) * 32768]
             out_c[t * 128:(t + 1) * 128, c * 256:(c + 1) * 256] = tile[byte_idx]
             atoms = sf[blk * 2048:(blk + 1) * 2048]
