@@ -34,7 +34,24 @@ METRIC = "decode tok/s at 1/2/4/8 B200; MXFP4 expert GEMV HBM GB/s vs peak"
 EXPERT_KERNEL = {0: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA (k_mxfp4_umma gate/up + down)",
                  1: "MXFP4 expert GEMV, mma.sync m16n8k16 (k_mxfp4_mma gate/up + down)",
                  2: "MXFP4 expert GEMV, CUDA cores (k_moe_gate_up + k_moe_down)",
-                 3: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA, one token per item"}
+                 3: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA, one token per item",
+                 4: "MXFP4 expert GEMV, tcgen05 kind::mxf4 block-scaled MMA, gate/up + act split + down "
+                    "in one launch (k_mxfp4_fused)"}
+
+
+def expert_kernel_ms(lib, sections=None):
+    """Device time per MoE layer of the expert launches from the section timers: the fused
+    launch when it ran, else the gate/up and down launches (the act split between them is
+    not counted, as before)."""
+    out = {}
+    for name in ("experts.fused", "experts.gateup", "experts.down"):
+        c = C.c_long()
+        ms = lib.k3d_prof_ms(name.encode(), C.byref(c))
+        if c.value:
+            out[name] = ms / c.value
+    if "experts.fused" in out:
+        return out["experts.fused"], out
+    return out.get("experts.gateup", float("nan")) + out.get("experts.down", float("nan")), out
 
 
 def dist_env():
@@ -382,7 +399,7 @@ def bench_moe(args, rank, world):
     sh = (synth.bf16_normal(g, (SHARED, HIDDEN), 0.02), synth.bf16_normal(g, (SHARED, HIDDEN), 0.02),
           synth.bf16_normal(g, (HIDDEN, SHARED), 0.02))
     mw = k3cuda.MoeWeights(HIDDEN, INTER, n_exp, TOPK, W, bias, shared=sh, seed=7, lo=lo, hi=hi,
-                           add_shared=1 if rank == 0 else 0, tiled=args.expert_kernel in (0, 3),
+                           add_shared=1 if rank == 0 else 0, tiled=args.expert_kernel in (0, 3, 4),
                            lib=lib)
     T = max(1, args.tokens)
     P = 64 if T == 1 else 8
@@ -429,10 +446,7 @@ def bench_moe(args, rank, world):
     cnt = C.c_long()
     exp_ms = lib.k3d_prof_ms(b"moe.experts", C.byref(cnt))
     n_prof = cnt.value
-    kern_ms = 0.0
-    for name in (b"experts.gateup", b"experts.down"):
-        c2 = C.c_long()
-        kern_ms += lib.k3d_prof_ms(name, C.byref(c2)) / max(1, c2.value)
+    kern_ms, _ = expert_kernel_ms(lib)
     lib.k3d_prof_enable(0)
     barrier()
     tot_ms = sum(step_ms)
@@ -735,7 +749,7 @@ def bench_stack(args, rank, world):
     cap = ctx + args.steps * 2 + args.warmup * 2 + 16
     # the tcgen05 kernel streams experts stored in the tiled layout; the other two
     # kernels read the checkpoint layout
-    cfg = stack_cfg(world, rank, args.batch, cap, 1 if args.expert_kernel in (0, 3) else 0)
+    cfg = stack_cfg(world, rank, args.batch, cap, 1 if args.expert_kernel in (0, 3, 4) else 0)
     t0 = time.time()
     model = lib.k3d_model_create(C.byref(cfg), 2024)
     if not model:
@@ -783,7 +797,9 @@ def bench_stack(args, rank, world):
     k3cuda.check(lib.k3d_sync())
     launches_per_step = lib.k3d_launch_count() / n_prof
     sections = {}
-    for name in ("moe.experts", "experts.gateup", "experts.down", "moe.shared", "moe.router", "kda.proj_in", "kda.core",
+    exp_ms, _ = expert_kernel_ms(lib)
+    for name in ("moe.experts", "experts.fused", "experts.gateup", "experts.down", "moe.shared", "moe.router",
+                 "kda.proj_in", "kda.core",
                  "kda.proj_out", "mla.proj_in", "mla.core", "mla.proj_out", "dense.mlp", "lm_head",
                  "ep.combine"):
         cnt = C.c_long()
@@ -792,8 +808,6 @@ def bench_stack(args, rank, world):
             sections[name] = {"ms_per_call": ms / cnt.value, "calls_per_step": cnt.value / n_prof}
     lib.k3d_prof_enable(0)
     k3cuda.check(lib.k3d_model_use_graph(model, 1))
-    exp_ms = sum(sections.get(k, {}).get("ms_per_call", float("nan"))
-                 for k in ("experts.gateup", "experts.down"))
     # algorithmic bytes: the weights of the distinct experts the step routed to (measured:
     # the last MoE layer's count), read once, plus the activation and output rows
     uniq = lib.k3d_moe_last_unique()
@@ -912,9 +926,10 @@ def main():
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bounded CPU-baseline sample length; 0 skips it")
-    ap.add_argument("--expert-kernel", type=int, default=0, choices=[0, 1, 2, 3],
-                    help="0 tcgen05 block-scaled (default), 1 mma.sync, 2 CUDA cores, 3 tcgen05 "
-                         "with one token per work item")
+    ap.add_argument("--expert-kernel", type=int, default=0, choices=[0, 1, 2, 3, 4],
+                    help="0 tcgen05 block-scaled (default), 1 mma.sync, 2 CUDA cores, 3 tcgen05 with "
+                         "one token per work item, 4 tcgen05 with gate/up, act split and down as "
+                         "one launch at decode sizes")
     ap.add_argument("--n-experts", type=int, default=N_EXPERTS,
                     help="routed experts resident per layer (384 = config 1; fewer only for "
                          "profiling captures that must stay small)")

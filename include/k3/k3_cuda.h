@@ -59,6 +59,11 @@ const char *k3d_last_message(void);
 void        k3d_set_abort_on_error(int on);
 /* Device-side error detail: the code a kernel stored and the site id that stored it. */
 int         k3d_device_error(int *code, int *site);
+/* Limit of the pipelined kernels' bounded waits (mbarriers, cross-CTA counters), in SM
+ * clock cycles; <= 0 restores the default 4e9 (about 2 s). A wait that runs out records
+ * K3D_ETIMEOUT (read by k3d_sync / k3d_status); its kernel waits for the copies it
+ * issued, frees its tensor memory and returns, so the context stays usable. */
+int         k3d_set_wait_limit(long long cycles);
 
 /* Memory. k3d_alloc returns 256-byte aligned device memory or NULL. */
 void  *k3d_alloc(size_t bytes);
@@ -67,6 +72,9 @@ int    k3d_upload(void *dst_dev, const void *src_host, size_t bytes);
 int    k3d_download(void *dst_host, const void *src_dev, size_t bytes);
 int    k3d_memset(void *dst_dev, int value, size_t bytes);
 int    k3d_copy(void *dst_dev, const void *src_dev, size_t bytes);
+/* rows x width bytes from src (rows spitch bytes apart) to dst (dpitch apart), device. */
+int    k3d_copy2d(void *dst_dev, size_t dpitch, const void *src_dev, size_t spitch, size_t width,
+                  size_t rows);
 /* Page-locked host memory, for host<->device copies at full PCIe speed. */
 void  *k3d_host_alloc(size_t bytes);
 void   k3d_host_free(void *p);
@@ -177,7 +185,10 @@ int    k3d_expert_pretile(const K3ExpertQ *dst, const K3ExpertQ *src, int hidden
  * multiples of 512, T * topk <= 64), 1 the mma.sync kernel, 2 the CUDA-core kernels, 3 the
  * tcgen05 kernel with the activation operand in every pipeline stage (kind 0, for tiled
  * experts, keeps it resident across the stages that share it up to 64 assignments, and
- * lets up to four tokens routed to one expert share its weight stages above 64).
+ * lets up to four tokens routed to one expert share its weight stages above 64), 4 as 0
+ * but decode-sized MoE work lists (up to 16 assignments at config 1) run as ONE launch that
+ * does gate/up, the act split and down (bit-identical; measured slower than the three
+ * launches of kind 0 so far, so not the default).
  * Experts in the tiled layout always run on the tcgen05 kernel.
  * All give the same results within the expert tolerance; the switch exists to measure
  * and test each. */
@@ -343,8 +354,19 @@ int k3d_ep_init(int rank, int nranks, const unsigned char id[128]);
 int k3d_ep_finalize(void);
 int k3d_ep_rank(void);
 int k3d_ep_size(void);
-/* In-place sum of a float buffer over all ranks (the MoE combine). */
+/* In-place sum of a float buffer over all ranks (NCCL). */
 int k3d_ep_allreduce_f32(float *buf, size_t n);
+/* The MoE combine of expert parallelism over NVLink peer memory: every rank exports one
+ * receive buffer (CUDA IPC) and maps every other rank's; collective, call on every rank
+ * after k3d_ep_init with the largest vector the combine will carry (floats). */
+int k3d_ep_peer_init(size_t max_floats);
+/* h[i] (+)= sum over ranks of partial[i] (accumulate = 1 adds into h), the same on every
+ * rank: one kernel stores this rank's partial into every rank's buffer, publishes it with
+ * a release flag per destination, waits (bounded; K3D_ETIMEOUT) for every rank's flag and
+ * sums the partials in rank order. Device pointers, 16-byte aligned; asynchronous on the
+ * library stream and capturable in a CUDA graph. Without k3d_ep_peer_init (or for vectors
+ * longer than it was sized for) it runs ncclAllReduce and an add instead. */
+int k3d_ep_combine_add(float *h, const float *partial, size_t n, int accumulate);
 
 /* Mode A expert parallelism: all-to-all dispatch and combine for data-parallel tokens (a
  * batch split over the ranks, e.g. B = 64). Every rank passes ITS OWN tokens x[T][hidden]

@@ -113,6 +113,10 @@ bool is_device_ptr(const void *p);
 extern __device__ int k3_dev_err[2];
 // Where the first error happened, when its kernel says (three integers and a valid flag).
 extern __device__ int k3_dev_diag[4];
+// Limit of the bounded waits on mbarriers and cross-CTA counters, in SM clock cycles
+// (k3d_set_wait_limit; default 4e9, about 2 s at 1.9 GHz). A wait that runs out records
+// K3D_ETIMEOUT and its kernel drains what it started and returns.
+extern __device__ long long k3_wait_cycles;
 
 __device__ __forceinline__ void k3_raise(int code, int site)
 {

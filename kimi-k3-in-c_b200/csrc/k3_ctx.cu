@@ -15,6 +15,7 @@
 
 __device__ int k3_dev_err[2];
 __device__ int k3_dev_diag[4];
+__device__ long long k3_wait_cycles = 4000000000LL;
 
 namespace k3 {
 
@@ -439,6 +440,15 @@ const char *k3d_strerror(int code)
 }
 
 const char *k3d_last_message(void) { return g.msg; }
+
+int k3d_set_wait_limit(long long cycles)
+{
+    K3_TRY(ensure_ctx());
+    const long long v = cycles > 0 ? cycles : 4000000000LL;
+    if (cudaMemcpyToSymbol(k3_wait_cycles, &v, sizeof v) != cudaSuccess)
+        return fail(K3D_ECUDA, "k3d_set_wait_limit");
+    return K3D_OK;
+}
 void k3d_set_abort_on_error(int on) { g.abort_on_error = on; }
 
 int k3d_device_error(int *code, int *site)
@@ -510,6 +520,17 @@ int k3d_copy(void *dst, const void *src, size_t bytes)
     if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, g.stream) != cudaSuccess) {
         cudaGetLastError();
         return fail(K3D_ECUDA, "k3d_copy");
+    }
+    return K3D_OK;
+}
+
+int k3d_copy2d(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t rows)
+{
+    K3_TRY(ensure_ctx());
+    if (cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, cudaMemcpyDeviceToDevice, g.stream) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return fail(K3D_ECUDA, "k3d_copy2d");
     }
     return K3D_OK;
 }

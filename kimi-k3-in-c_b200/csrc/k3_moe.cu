@@ -29,12 +29,13 @@ namespace k3 {
 // ---- prep: group assignments by expert (one CTA) --------------------------------
 __global__ void __launch_bounds__(1024) k_moe_prep(const int *idx, int TK, int n_experts,
                                                    int lo, int hi, int *n_active,
-                                                   int *act_expert, int *act_off, int *assign)
+                                                   int *act_expert, int *act_off, int *assign,
+                                                   int *zero, int nzero)
 {
     pdl_wait();
     pdl_trigger();
     extern __shared__ int sm[];
-    group_assignments(idx, TK, n_experts, lo, hi, n_active, act_expert, act_off, assign, sm);
+    group_assignments(idx, TK, n_experts, lo, hi, n_active, act_expert, act_off, assign, sm, zero, nzero);
 }
 
 // ---- gate/up + SiLU*mul -------------------------------------------------------------
@@ -250,7 +251,9 @@ static int launch_down(float *contrib, const float *act, const MoeWork &w, int h
 static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 // Which expert kernel runs (k3d_set_expert_kernel): 0 chooses the tcgen05 block-scaled
-// kernel whenever the shapes allow, 1 forces the mma.sync kernel, 2 the CUDA-core kernels.
+// kernel whenever the shapes allow (gate/up, act split and down as three launches), 1 forces
+// the mma.sync kernel, 2 the CUDA-core kernels, 3 the tcgen05 kernel with B in every stage,
+// 4 the same as 0 but decode-sized work lists as ONE launch (k_mxfp4_fused).
 static int g_expert_kernel = 0;
 static const int kUmmaMaxTK = 64;     // assignments per call for the tcgen05 path
 
@@ -262,6 +265,8 @@ struct ExpertBufs {
     float *part_gu, *part_d;               // tcgen05: K-slice partials
     uint8_t *bqg_x, *bsg_x, *bqg_a, *bsg_a;   // tcgen05 grouped: pieces of x and act by group
     UmmaGroups grp;                        // tcgen05 grouped: the groups (null when absent)
+    int *fcnt;                             // tcgen05 fused pass: its counters (null when absent)
+    int fcnt_n;                            // their count (ints)
 };
 
 // Where the per-assignment contributions ended up: contrib[s * slice + a * hidden + r].
@@ -302,7 +307,7 @@ static bool grouped_eligible(int hidden, int inter, int TK, int layout)
 // True when run_experts takes the tcgen05 path.
 static bool use_umma(const ExpertBufs &B, int hidden, int inter, int TK, int layout)
 {
-    return (layout == 1 || g_expert_kernel == 0 || g_expert_kernel == 3) && B.bq_x &&
+    return (layout == 1 || g_expert_kernel == 0 || g_expert_kernel >= 3) && B.bq_x &&
            umma_eligible(hidden, inter, TK, layout);
 }
 
@@ -316,9 +321,12 @@ static bool use_grouped(const ExpertBufs &B, int TK, int layout, int hidden, int
 // else the mma.sync kernel (k3_mxfp4_mma.cu), else the CUDA-core kernels. `count` is the
 // device count of local assignments (MoE) or null (single expert, one assignment).
 // x_split: the caller already wrote x's tcgen05 B operand (umma_bsplit into B.bq_x/bs_x).
+// cnt_zeroed: B.fcnt was zeroed by the grouping that wrote this work list (the fused launch
+// needs its counters at zero).
 static int run_experts(const MoeWork &mw, const int *idx, const int *count, int umax,
                        const float *x, int T, int TK, int hidden, int inter, int layout,
-                       const ExpertBufs &B, ExpertOut &O, cudaStream_t st, bool x_split = false)
+                       const ExpertBufs &B, ExpertOut &O, cudaStream_t st, bool x_split = false,
+                       bool cnt_zeroed = false)
 {
     O.contrib = B.contrib;
     O.ks = 1;
@@ -348,6 +356,21 @@ static int run_experts(const MoeWork &mw, const int *idx, const int *count, int 
         O.ks = ks_d;
         O.slice = sl_d;
         O.pos_of = B.grp.pos_of;
+        return K3D_OK;
+    }
+    if (!mw.single_mode && count && cnt_zeroed && B.fcnt && layout == 1 && g_expert_kernel == 4 &&
+        use_umma(B, hidden, inter, TK, layout) && umma_fused_ok(TK, hidden, inter)) {
+        // decode-sized work lists: gate/up, act split and down in one launch; partials and
+        // operands as in the three-launch resident path below
+        const size_t sl_gu = (size_t)TK * 2 * inter, sl_d = (size_t)TK * hidden;
+        if (!x_split) K3_TRY(umma_bsplit(B.bq_x, B.bs_x, x, hidden, T, hidden, st));
+        prof_begin("experts.fused");
+        K3_TRY(umma_launch_fused(mw, idx, count, TK, hidden, inter, B.bq_x, B.bs_x, topk, B.part_gu, sl_gu,
+                                 B.bq_a, B.bs_a, B.part_d, sl_d, B.fcnt, st));
+        prof_end("experts.fused");
+        O.contrib = B.part_d;
+        O.ks = inter / 512;
+        O.slice = sl_d;
         return K3D_OK;
     }
     if (use_umma(B, hidden, inter, TK, layout)) {
@@ -426,9 +449,18 @@ static void expert_bufs_layout(ExpertBufs &eb, const K3dMoeShape *s, size_t T, s
         eb.bs_a = (uint8_t *)take(TK * umma_bs_bytes(s->inter));
         eb.part_gu = (float *)take(cap_gu * TK * 2 * s->inter * sizeof(float));
         eb.part_d = (float *)take(cap_d * TK * s->hidden * sizeof(float));
+        if (s->expert_layout == 1 && !grp) {
+            eb.fcnt_n = (int)umma_fused_cnt_ints((int)TK, s->inter);
+            eb.fcnt = (int *)take((size_t)eb.fcnt_n * sizeof(int));
+        } else {
+            eb.fcnt = nullptr;
+            eb.fcnt_n = 0;
+        }
     } else {
         eb.bq_x = eb.bs_x = eb.bq_a = eb.bs_a = nullptr;
         eb.part_gu = eb.part_d = nullptr;
+        eb.fcnt = nullptr;
+        eb.fcnt_n = 0;
     }
     if (grouped_eligible(s->hidden, s->inter, (int)TK, s->expert_layout)) {
         // at most one group per assignment
@@ -782,7 +814,8 @@ int k3d_moe_swiglu_a2a(float *out, const float *x, const K3dMoeW *w, const K3dMo
     if (R > 0) {
         const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
         launch_pdl(k_moe_prep, dim3(1), dim3(1024), smem, st, (const int *)L.recv_ids, (int)R, s->n_experts,
-                   s->expert_lo, s->expert_hi, L.n_active, L.act_expert, L.act_off, L.assign);
+                   s->expert_lo, s->expert_hi, L.n_active, L.act_expert, L.act_off, L.assign, L.eb.fcnt,
+                   L.eb.fcnt_n);
         note_launch();
         K3_TRY(check_launch("moe a2a prep"));
         MoeWork mw{};
@@ -837,7 +870,7 @@ size_t k3d_expert_ws_bytes(int hidden, int inter)
 
 int k3d_set_expert_kernel(int kind)
 {
-    if (kind < 0 || kind > 3) return fail(K3D_EINVAL, "k3d_set_expert_kernel(%d): 0 to 3", kind);
+    if (kind < 0 || kind > 4) return fail(K3D_EINVAL, "k3d_set_expert_kernel(%d): 0 to 4", kind);
     g_expert_kernel = kind;
     return K3D_OK;
 }
@@ -924,13 +957,15 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     }
     prof_begin("moe.router");
     RouterGroup grp{L.n_active, L.act_expert, L.act_off, L.assign, s->expert_lo, s->expert_hi, 0};
+    grp.zero = L.eb.fcnt;
+    grp.nzero = L.eb.fcnt_n;
     K3_TRY(router_bf16(I, Wt, x, w->router_w, w->router_bias, T, s->hidden, s->n_experts, K,
                        s->renorm, s->routed_scale, L.router, st, &grp));
     prof_end("moe.router");
     if (!grp.done) {
         const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
         launch_pdl(k_moe_prep, dim3(1), dim3(1024), smem, st, I, TK, s->n_experts, s->expert_lo, s->expert_hi,
-                                          L.n_active, L.act_expert, L.act_off, L.assign);
+                                          L.n_active, L.act_expert, L.act_off, L.assign, L.eb.fcnt, L.eb.fcnt_n);
         note_launch();
         K3_TRY(check_launch("moe prep"));
     }
@@ -948,7 +983,7 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
     if (umax > 0) {
         prof_begin("moe.experts");
         K3_TRY(run_experts(mw, I, L.n_active + 1, umax, x, T, TK, s->hidden, s->inter,
-                           s->expert_layout, L.eb, O, st, early_split));
+                           s->expert_layout, L.eb, O, st, early_split, true));
         prof_end("moe.experts");
     }
     if (shared && sst != st && cudaStreamWaitEvent(st, side_event(1), 0) != cudaSuccess)

@@ -45,10 +45,13 @@ __device__ __forceinline__ int work_assign(const MoeWork &w, int p)
 // lists the assignment ids a = t*K + j of each expert. Any block size >= 32; `sm` holds
 // 2 * n_experts ints. idx is read through L2 (it may have been written by other CTAs of
 // the same grid).
+// zero/nzero: a region zeroed on the way (the fused expert pass's counters).
 __device__ __forceinline__ void group_assignments(const int *idx, int TK, int n_experts, int lo,
                                                   int hi, int *n_active, int *act_expert,
-                                                  int *act_off, int *assign, int *sm)
+                                                  int *act_off, int *assign, int *sm,
+                                                  int *zero = nullptr, int nzero = 0)
 {
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
     int *cnt = sm;                 // [n_experts]
     int *cur = sm + n_experts;     // [n_experts]
     for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;

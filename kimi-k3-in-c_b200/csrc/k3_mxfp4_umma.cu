@@ -63,7 +63,7 @@ constexpr int kProducers = 128;
 constexpr int kThreads = 288;
 constexpr int kTmemCols = 128;               // acc 4 x 16 @0, SFA 2 x 16 @64, SFB 2 x 16 @96
 constexpr uint32_t kSfaCol = 64, kSfbCol = 96;
-constexpr long long kSpinLimit = 4000000000LL;   // ~2 s at 1.9 GHz
+constexpr long long kSpinLimit = 4000000000LL;   // drain waits: ~2 s at 1.9 GHz
 
 enum { GATEUP = 0, DOWN = 1 };
 
@@ -124,14 +124,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase completes or about
+// `ns` nanoseconds pass, so a waiting role does not take issue slots from the warps that
+// share its scheduler.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t b, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.b32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(b), "r"(parity), "r"(ns) : "memory");
+    return ok != 0;
+}
+
 // Bounded wait; false when it gave up (time limit, or another role already aborted).
 __device__ __forceinline__ bool mbar_wait(uint32_t b, uint32_t parity, volatile int *abort)
 {
     if (mbar_try(b, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try(b, parity)) {
+    const long long t0 = clock64(), lim = k3_wait_cycles;
+    while (!mbar_try_sleep(b, parity, 1000u)) {
         if (*abort) return false;
-        if (clock64() - t0 > kSpinLimit) {
+        if (clock64() - t0 > lim) {
             k3_raise(K3D_ETIMEOUT, K3_SITE_MXFP4);
             *abort = 1;
             return false;
@@ -877,16 +890,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
 //   the later codes follow the schedule s_1 = s_0 - 2, s_{p+1} = s_p - 3; every code is
 //   clamped at 0 (blocks below 2^-80 or so share the smallest scale, 2^-127, which only
 //   makes their scaled residuals smaller);
-//   per piece, the E2M1 code of r / 2^s by the hardware conversion (round to nearest even;
-//   the scaled value never exceeds 6, so saturation never acts), its value q, and the
-//   residual (r / 2^s - q) * 2^s.
+//   per piece, the E2M1 code of r / 2^s rounded to nearest even (e2m1_rne; the scaled value
+//   never exceeds 6, so saturation never acts), its value q, and the residual
+//   (r / 2^s - q) * 2^s.
 // A block holding an inf or NaN gets scale code 255 (NaN) on every piece, zero codes.
-__device__ __forceinline__ uint32_t e2m1_code(float v)
+
+// Round to the nearest E2M1 value, ties to the even code, for |v| <= 6 (saturating above,
+// as the hardware conversion's satfinite does): the value and its 4-bit code (sign bit 8;
+// zero always +0). Plain float arithmetic, exact at every step (a power-of-two scaling and
+// an integer rounding), so it equals cvt.rn.satfinite.e2m1x2.f32 on this range, without
+// branches.
+__device__ __forceinline__ float e2m1_rne(float v, uint32_t &nib)
 {
-    uint32_t r;
-    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %1;\n\tcvt.u32.u8 %0, t;\n\t}"
-        : "=r"(r) : "f"(v));
-    return r & 0xFu;          // both halves hold v's code
+    // grid spacing 0.5 below 2, 1 below 4, 2 up to 6: scale to unit spacing, round to the
+    // nearest integer (ties to even, which is the even code), scale back; no branches
+    const float a = fabsf(v);
+    const float up = a < 2.0f ? 2.0f : (a < 4.0f ? 1.0f : 0.5f);
+    const float dn = a < 2.0f ? 0.5f : (a < 4.0f ? 1.0f : 2.0f);
+    const float q = fminf(rintf(a * up) * dn, 6.0f);
+    // the code from q's bits: 2 (exponent - 127) + top mantissa bit + 2 from 1 up, 1 for 0.5
+    const uint32_t bits = __float_as_uint(q);
+    const uint32_t code = q >= 1.0f ? 2u * ((bits >> 23) - 127u) + ((bits >> 22) & 1u) + 2u : (q > 0.0f ? 1u : 0u);
+    nib = code ? (code | (v < 0.0f ? 8u : 0u)) : 0u;
+    return code ? (v < 0.0f ? -q : q) : 0.0f;
+}
+
+// The 32 codes of one piece of a block (lane l holds element l's nibble) as the 16 bytes of
+// its B row segment: lanes 0, 8, 16 and 24 return one 32-bit word each (bytes 0-3, 4-7, 8-11,
+// 12-15; the low nibble of byte i is element 2i), the other lanes garbage: four 32-bit
+// stores per piece instead of sixteen byte stores.
+__device__ __forceinline__ uint32_t piece_word(uint32_t nib)
+{
+    const uint32_t b = nib | (__shfl_down_sync(0xffffffffu, nib, 1) << 4);
+    return b | (__shfl_down_sync(0xffffffffu, b, 2) << 8) | (__shfl_down_sync(0xffffffffu, b, 4) << 16) |
+           (__shfl_down_sync(0xffffffffu, b, 6) << 24);
 }
 
 // NV vectors per B operand (the grouped layout, NV = 4): slot v's piece p is B row
@@ -913,27 +950,31 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
     }
     int my_code = 255;                       // lane p < 16 keeps piece p's scale code
     if (__any_sync(0xffffffffu, !isfinite(r))) {
-#pragma unroll
+#pragma unroll 1
         for (int p = 0; p < kN; p++)
-            if ((lane & 1) == 0)
-                tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] = 0;
+            if ((lane & 7) == 0)
+                *reinterpret_cast<uint32_t *>(tile + (p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) +
+                                              (lane >> 1)) = 0u;
     } else {
         const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r)));
         const int code0 = (int)(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
-#pragma unroll
+        bool live = true;                    // the residual is not yet zero everywhere
+#pragma unroll 1                             // rolled: a small body stays in the instruction cache
         for (int p = 0; p < kN; p++) {
             const int code = max(0, p == 0 ? code0 : code0 + 1 - 3 * p);
-            const float rs = __fmul_rn(r, __int_as_float((254 - code) << 23));   // r / 2^s, exact
-            uint32_t nib = e2m1_code(rs);
-            if ((nib & 7u) == 0u) nib = 0u;                                     // no -0 codes
-            const float q = __half2float(__ushort_as_half((unsigned short)(e2m1x2_to_f16x2(nib) & 0xffffu)));
-            const float sc = code ? __int_as_float(code << 23) : __int_as_float(0x00400000);
-            r = __fmul_rn(__fsub_rn(rs, q), sc);
+            uint32_t nib = 0u;
+            if (live) {
+                const float rs = __fmul_rn(r, __int_as_float((254 - code) << 23));   // r / 2^s, exact
+                const float q = e2m1_rne(rs, nib);                                  // no -0 codes
+                const float sc = code ? __int_as_float(code << 23) : __int_as_float(0x00400000);
+                r = __fmul_rn(__fsub_rn(rs, q), sc);
+            }
             if (lane == p) my_code = code;
-            const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 1);
-            if ((lane & 1) == 0)
-                tile[(p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)] =
-                    (uint8_t)(nib | (hi << 4));
+            const uint32_t w = live ? piece_word(nib) : 0u;
+            live = live && __any_sync(0xffffffffu, r != 0.0f);
+            if ((lane & 7) == 0)
+                *reinterpret_cast<uint32_t *>(tile + (p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) +
+                                              (lane >> 1)) = w;
         }
     }
     if (lane < kN) atom[16 * (16 * (v & 1) + lane) + 4 * (v >> 1) + (j & 3)] = (uint8_t)my_code;
@@ -998,6 +1039,484 @@ __global__ void k_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int
     if (p >= n) return;
     const int nch = inter / kStageK;
     split_block<1>(bq + (size_t)p * nch * kTileB, bs + (size_t)p * nch * kTileSF, act, blk, 0, lane);
+}
+
+// ------------------------------------------------------------ fused decode pass
+// gate/up, the act split and down in ONE launch, for the decode shapes whose items fit
+// one table per CTA (T * topk up to 16 at config 1). Both passes run back to back in every
+// CTA's roles, with no kernel boundary between them:
+//   warp 0 lane 0   weight producer: the ring streams the CTA's gate/up tiles, then its
+//                   down tiles; the down weights do not depend on the gate/up results, so
+//                   they fill the ring while the last gate/up stages finish;
+//   warp 1 lane 0   B producer of the gate/up runs (x's pieces, one bulk copy per run);
+//   warp 4          MMA issuer, as in k_mxfp4_umma;
+//   warps 5-8       epilogue. After their gate/up items they publish the CTA's gate/up rows
+//                   (one release per act chunk touched), then form the B operand of each
+//                   of the CTA's down runs themselves: act = silu(gate) * up over the K
+//                   slices (k_bsplit_swiglu's arithmetic) once every CTA's rows of that act
+//                   chunk are out, split into the 16 E2M1 pieces straight into the run's
+//                   shared-memory B slot; then the down items' epilogue.
+// Cross-CTA dependencies go through counters in the workspace (zeroed by the router of the
+// same layer, before this launch's programmatic wait returns):
+//   cnt[p * nact + c]      gate/up rows of act chunk c of position p published (expected:
+//                          4 epilogue warps x 8 tiles x the K slices);
+//   cnt[2 * npos * nact]   abort word: a CTA whose wait ran out sets it, every waiter then
+//                          gives up at once.
+// A CTA only ever waits for gate/up work, which waits on nothing across CTAs, so progress
+// needs no more co-residency than the scheduler eventually provides; every wait is bounded
+// (k3_wait_cycles). Results are bit-identical to the three-launch form (kind 4).
+struct FusedJob {
+    Job A, B;          // gate/up and down, both in the resident-B geometry (one stage per item)
+    int *cnt;          // counters, 2 * npos * nact + 1 ints
+    int npos;          // positions the counters cover (the launch's npos_max)
+    int nact;          // act chunks per position: inter / 512
+    int arrivals;      // expected gate/up arrivals per (position, act chunk)
+};
+constexpr int kFusedCtr = 96;            // shared per-(position, act chunk) arrival counts
+
+__device__ __forceinline__ int ld_acquire(const int *p)
+{
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_add(int *p, int v)
+{
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+// Barrier of the 4 epilogue warps, bounded: a shared arrival count that every warp's lane 0
+// bumps and then waits to reach 4 x gen (gen = this barrier's ordinal, counted by each warp
+// alike). A hardware named barrier would wait forever for a warp that left on an abort;
+// this one returns false on the abort flag or the time limit.
+__device__ __forceinline__ bool epi_barrier(int *ctr, int gen, volatile int *abort, int lane)
+{
+    int ok = 1;
+    __syncwarp();
+    if (lane == 0) {
+        __threadfence_block();
+        atomicAdd(ctr, 1);
+        const long long t0 = clock64(), lim = k3_wait_cycles;
+        while (*(volatile int *)ctr < 4 * gen) {
+            __nanosleep(32);
+            if (*abort) { ok = 0; break; }
+            if (clock64() - t0 > lim) {
+                k3_raise(K3D_ETIMEOUT, K3_SITE_MXFP4);
+                *abort = 1;
+                ok = 0;
+                break;
+            }
+        }
+        __threadfence_block();
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+
+// Bounded wait for *p >= target (acquire); false when it gave up: this CTA's or another
+// CTA's abort, or the time limit (which raises K3D_ETIMEOUT and sets both abort words).
+__device__ __forceinline__ bool wait_count(const int *p, int target, volatile int *abort, int *gabort)
+{
+    if (ld_acquire(p) >= target) return true;
+    const long long t0 = clock64(), lim = k3_wait_cycles;
+    while (ld_acquire(p) < target) {
+        if (*abort) return false;
+        if (*(volatile int *)gabort) { *abort = 1; return false; }
+        if (clock64() - t0 > lim) {
+            k3_raise(K3D_ETIMEOUT, K3_SITE_MXFP4);
+            *abort = 1;
+            atomicExch(gabort, 1);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// Run identity of an item in the fused table: the pass, its B vector and its K chunk.
+__device__ __forceinline__ bool fused_new_run(const ItemEnt &it, int pass, int key, int chunk)
+{
+    return ((pass << 24) | it.vec) != key || it.s != chunk;
+}
+
+// split_block<1> for the four blocks j0..j0+3 of one 512-element chunk (one scale atom, j0 a
+// multiple of 4) at once: lane l holds element l of each block, and the four blocks' piece
+// chains are independent, so they run side by side. Same bytes as four split_block<1> calls.
+__device__ __forceinline__ void split_block4(uint8_t *bq, uint8_t *bs, const float r_in[4], int j0, int lane)
+{
+    uint8_t *atom = bs + (j0 >> 2) * 512;
+    if (lane < 16) {
+        uint32_t *z = reinterpret_cast<uint32_t *>(atom + 16 * lane + 4);
+        z[0] = 0u; z[1] = 0u; z[2] = 0u;
+    } else {
+        *reinterpret_cast<uint4 *>(atom + 256 + 16 * (lane - 16)) = make_uint4(0, 0, 0, 0);
+    }
+    float r[4];
+    int code0[4], my_code[4];
+    bool fin[4];
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        r[b] = r_in[b];
+        fin[b] = !__any_sync(0xffffffffu, !isfinite(r[b]));
+        const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r[b])));
+        code0[b] = (int)(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
+        my_code[b] = 255;
+    }
+    bool live = true;              // some residual of the four blocks is not yet zero
+    // a rolled loop: unrolled, the body is thousands of instructions that every SM fetches
+    // once per call through the instruction cache, all at the same time
+#pragma unroll 1
+    for (int p = 0; p < kN; p++) {
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const int j = j0 + b;
+            uint32_t nib = 0u;
+            int code = 255;
+            if (fin[b]) code = max(0, p == 0 ? code0[b] : code0[b] + 1 - 3 * p);
+            if (fin[b] && live) {
+                const float rs = __fmul_rn(r[b], __int_as_float((254 - code) << 23));
+                const float q = e2m1_rne(rs, nib);
+                const float sc = code ? __int_as_float(code << 23) : __int_as_float(0x00400000);
+                r[b] = __fmul_rn(__fsub_rn(rs, q), sc);
+            }
+            if (lane == p) my_code[b] = code;
+            const uint32_t w = live ? piece_word(nib) : 0u;
+            if ((lane & 7) == 0)
+                *reinterpret_cast<uint32_t *>(bq + (j >> 3) * 2048 + (p >> 3) * 1024 + (p & 7) * 128 +
+                                              (((j & 7) ^ (p & 7)) << 4) + (lane >> 1)) = w;
+        }
+        // the remaining pieces of a zero residual are zero codes (their scales still follow
+        // the schedule)
+        live = live && __any_sync(0xffffffffu, (fin[0] && r[0] != 0.0f) || (fin[1] && r[1] != 0.0f) ||
+                                                (fin[2] && r[2] != 0.0f) || (fin[3] && r[3] != 0.0f));
+    }
+    if (lane < kN)
+        *reinterpret_cast<uint32_t *>(atom + 16 * lane) = (uint32_t)(my_code[0] & 0xff) |
+            ((uint32_t)(my_code[1] & 0xff) << 8) | ((uint32_t)(my_code[2] & 0xff) << 16) |
+            ((uint32_t)(my_code[3] & 0xff) << 24);
+}
+
+__device__ __forceinline__ void fused_act_split(const FusedJob &F, int p, int c, unsigned char *tile, unsigned char *atoms,
+                                            int q, int lane);
+
+// The B operand of one down run (position p, act chunk c) formed by the 4 epilogue warps
+// into the shared-memory slot at `slot` (pieces, then the scale atoms): each warp waits for
+// the chunk's gate/up rows, then forms 4 of its 16 blocks (act = silu(gate) * up with the K
+// slices summed in order, as act_value; the split of split_block). false when a wait gave up.
+__device__ __forceinline__ bool fused_make_b(const FusedJob &F, int p, int c, unsigned char *tile,
+                                             unsigned char *atoms, int q, int lane, volatile int *abort, int *gabort)
+{
+    const int *ca = F.cnt + (size_t)p * F.nact + c;
+    int okw = 1;
+    if (lane == 0) okw = wait_count(ca, F.arrivals, abort, gabort) ? 1 : 0;
+    okw = __shfl_sync(0xffffffffu, okw, 0);
+    if (!okw) return false;
+    (void)ld_acquire(ca);                   // every lane acquires the gate/up stores
+    fused_act_split(F, p, c, tile, atoms, q, lane);
+    return true;
+}
+
+// act of the warp's 4 blocks of act chunk c of position p, split into `slot` (B pieces, then
+// the scale atoms).
+__device__ __forceinline__ void fused_act_split(const FusedJob &F, int p, int c, unsigned char *tile, unsigned char *atoms,
+                                            int q, int lane)
+{
+    const int inter = F.nact * kStageK, ks = F.A.ks;
+    const size_t ss = F.A.slice_stride;
+    const float *pa = F.A.part + (size_t)p * 2 * inter + (size_t)(c * 16 + q * 4) * 32 + lane;
+    // the four blocks' gate and up partials, all slices of a group of 8 in flight together
+    float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < ks; s0 += 8) {
+        float gv[4][8], uv[4][8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int b = 0; b < 4; b++)
+                if (s0 + i < ks) {
+                    gv[b][i] = __ldcg(pa + (size_t)(s0 + i) * ss + 32 * b);
+                    uv[b][i] = __ldcg(pa + (size_t)(s0 + i) * ss + 32 * b + inter);
+                }
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int b = 0; b < 4; b++)
+                if (s0 + i < ks) {
+                    g[b] += gv[b][i];
+                    u[b] += uv[b][i];
+                }
+    }
+    float act[4];
+#pragma unroll
+    for (int b = 0; b < 4; b++) act[b] = silu_f(g[b]) * u[b];
+    split_block4(tile, atoms, act, q * 4, lane);
+    // a bulk copy brings these bytes into the run's shared-memory slot
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_mxfp4_fused(const __grid_constant__ FusedJob F)
+{
+    using G = Geo<1, 1>;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = saddr(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char *gbase = smem_raw + (base - raw);
+    const uint32_t b_full = base, b_empty = base + 64, b_accf = base + 128;
+    const uint32_t b_acce = b_accf + 8 * kAccBufs, b_drain = b_acce + 8 * kAccBufs;
+    const uint32_t b_bfull = b_drain + 8, b_bempty = b_bfull + 16;
+    volatile int *abort = reinterpret_cast<volatile int *>(gbase + 512);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + 520);
+    int *s_n = reinterpret_cast<int *>(gbase + 528);            // na, nb, first items
+    int *s_ctr = reinterpret_cast<int *>(gbase + 544);          // [kFusedCtr] arrivals
+    int *s_epi = reinterpret_cast<int *>(gbase + 544 + 4 * kFusedCtr);   // epilogue barrier
+    ItemEnt *items = reinterpret_cast<ItemEnt *>(gbase + kOffItems);
+    const uint32_t stage0 = base + kStage0;
+    const uint32_t bslots = base + (uint32_t)G::kBSlots;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int *gabort = F.cnt + 2 * F.npos * F.nact;
+    static_assert(544 + 4 * kFusedCtr + 4 <= kOffItems, "shared header");
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < G::kNStages; s++) { mbar_init(b_full + 8 * s, 1); mbar_init(b_empty + 8 * s, 1); }
+        for (int i = 0; i < kAccBufs; i++) { mbar_init(b_accf + 8 * i, 1); mbar_init(b_acce + 8 * i, 4); }
+        mbar_init(b_drain, 1);
+        for (int i = 0; i < 2; i++) { mbar_init(b_bfull + 8 * i, 1); mbar_init(b_bempty + 8 * i, 1); }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i <= kFusedCtr; i += blockDim.x) s_ctr[i] = 0;   // and s_epi
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(saddr(tmem_slot)), "r"(G::kTmem) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();                      // the work lists and the counters' zeroing come from the router
+
+    if (threadIdx.x == 0) {
+        const int ta = item_count(F.A), tb = item_count(F.B);
+        const int a0 = (int)((long long)blockIdx.x * ta / gridDim.x), a1 = (int)((long long)(blockIdx.x + 1) * ta / gridDim.x);
+        const int b0 = (int)((long long)blockIdx.x * tb / gridDim.x), b1 = (int)((long long)(blockIdx.x + 1) * tb / gridDim.x);
+        s_n[0] = a1 - a0;
+        s_n[1] = b1 - b0;
+        s_n[2] = a0;
+        s_n[3] = b0;
+    }
+    __syncthreads();
+    int na = s_n[0], nb = s_n[1];
+    if (na + nb > kMaxItems || F.npos * F.nact > kFusedCtr) {   // the host sizes launches so that
+        if (threadIdx.x == 0) k3_raise(K3D_EBOUND, K3_SITE_MXFP4);  // this cannot happen
+        na = nb = 0;
+    }
+    for (int i = threadIdx.x; i < na + nb; i += blockDim.x)
+        items[i] = i < na ? decode<1, 1>(F.A, s_n[2] + i) : decode<1, 1>(F.B, s_n[3] + i - na);
+    __syncthreads();
+    pdl_trigger();
+    const int n = na + nb;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ weight producer
+        if (lane == 0) {
+            int g = 0;
+            for (int k = 0; k < n; k++) {
+                const ItemEnt &it = items[k];
+                const int st = g % G::kNStages;
+                if (g >= G::kNStages && !mbar_wait(b_empty + 8 * st, ((g / G::kNStages) - 1) & 1, abort)) break;
+                const uint32_t fb = b_full + 8 * st;
+                if (item_ok(it)) {
+                    mbar_expect_tx(fb, G::kTx);
+                    issue_weights<1, 1>(stage0 + (uint32_t)st * G::kBytes, fb, k < na ? F.A : F.B, it, it.s);
+                } else {
+                    k3_raise(K3D_EINVAL, K3_SITE_MXFP4);
+                    mbar_arrive(fb);
+                }
+                g++;
+            }
+            // no copy may land after the CTA exits: wait for the last stages issued (each
+            // earlier one was consumed before its slot was reused)
+            for (int h = max(0, g - G::kNStages); h < g; h++)
+                mbar_drain(b_full + 8 * (h % G::kNStages), (h / G::kNStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------- B producer, gate/up runs
+        if (lane == 0) {
+            int rb = 0, key = -1, chunk = -1;
+            for (int k = 0; k < na; k++) {
+                const ItemEnt &it = items[k];
+                if (!fused_new_run(it, 0, key, chunk)) continue;
+                const int slot = rb & 1;
+                if (rb >= 2 && !mbar_wait(b_bempty + 8 * slot, ((rb >> 1) - 1) & 1, abort)) break;
+                const uint32_t bb = b_bfull + 8 * slot, dst = bslots + (uint32_t)(slot * G::kBSlot);
+                const size_t vix = (size_t)it.vec * F.A.nch + it.s;
+                mbar_expect_tx(bb, G::kBTile + kTileSF);
+                bulk_g2s(dst, F.A.bq + vix * G::kBTile, G::kBTile, bb);
+                bulk_g2s(dst + G::kBTile, F.A.bs + vix * kTileSF, kTileSF, bb);
+                rb++;
+                key = it.vec;
+                chunk = it.s;
+            }
+            for (int h = max(0, rb - 2); h < rb; h++) mbar_drain(b_bfull + 8 * (h & 1), (h >> 1) & 1);
+        }
+    } else if (warp == 4) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            int g = 0, rb = 0, key = -1, chunk = -1;
+            for (int k = 0; k < n; k++) {
+                const ItemEnt &it = items[k];
+                const int pass = k < na ? 0 : 1;
+                const int buf = k % kAccBufs;
+                if (k >= kAccBufs && !mbar_wait(b_acce + 8 * buf, ((k / kAccBufs) - 1) & 1, abort)) break;
+                tc_fence_after();
+                if (fused_new_run(it, pass, key, chunk)) {
+                    if (rb > 0) tc_commit(b_bempty + 8 * ((rb - 1) & 1));
+                    const int slot = rb & 1;
+                    if (!mbar_wait(b_bfull + 8 * slot, (rb >> 1) & 1, abort)) break;
+                    tc_fence_after();
+                    const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)(slot * 16);
+#pragma unroll
+                    for (int a4 = 0; a4 < 4; a4++)
+                        tc_cp_sf(sfb + 4 * a4, desc_sf(bslots + (uint32_t)(slot * G::kBSlot + G::kBTile + 512 * a4)));
+                    rb++;
+                    key = (pass << 24) | it.vec;
+                    chunk = it.s;
+                }
+                const int slot = (rb - 1) & 1;
+                const uint32_t bs = bslots + (uint32_t)(slot * G::kBSlot);
+                const uint32_t sfb = tmem + G::kSfbCol + (uint32_t)(slot * 16);
+                const uint32_t dcol = tmem + (uint32_t)(buf * G::kCols);
+                const int st = g % G::kNStages;
+                if (!mbar_wait(b_full + 8 * st, (g / G::kNStages) & 1, abort)) break;
+                tc_fence_after();
+                const uint32_t sb = stage0 + (uint32_t)st * G::kBytes;
+                const uint32_t sfa = tmem + G::kSfaCol + (uint32_t)((g & 1) * 16);
+#pragma unroll
+                for (int a4 = 0; a4 < 4; a4++) tc_cp_sf(sfa + 4 * a4, desc_sf(sb + G::kSFA + 512 * a4));
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t kb = (uint32_t)(j >> 2), off = (uint32_t)((j & 3) * 32);
+                    const uint64_t ad = desc_sw128(sb + kb * 16384u + off);
+                    const uint64_t bd = desc_sw128(bs + kb * 2048u + off);
+                    const uint32_t id = (uint32_t)((j & 1) * 2);
+                    const uint32_t atom = (uint32_t)(4 * (j >> 1));
+                    tc_mma(dcol, ad, bd, idesc_mxf4<G::kCols>(id), j > 0 ? 1u : 0u, (sfa + atom) | (id << 30),
+                           (sfb + atom) | (id << 30));
+                }
+                tc_commit(b_empty + 8 * st);
+                g++;
+                tc_commit(b_accf + 8 * buf);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 5) {
+        // ---------------------------------------------------------------- epilogue
+        // a warp reads the tensor-memory lanes of its own quadrant (warp % 4)
+        const int q = warp & 3, m = q * 32 + lane;
+        bool ok = true;
+        // gate/up runs: the global index of the first down run continues from them
+        int ra = 0;
+        {
+            int key = -1, chunk = -1;
+            for (int k = 0; k < na; k++)
+                if (fused_new_run(items[k], 0, key, chunk)) { ra++; key = items[k].vec; chunk = items[k].s; }
+        }
+        int rb = ra, key = -1, chunk = -1, gen = 0;   // down runs begun; epilogue barriers
+        int built = ra;                                // down runs whose B operand is formed
+        for (int k = 0; k <= n && ok; k++) {
+            if (k == na) {
+                // every gate/up row of this CTA is stored: publish them, one release per act
+                // chunk this CTA touched (each thread's stores are made visible by its fence
+                // before the epilogue barrier, and the releases come after it)
+                __threadfence();
+                if (!epi_barrier(s_epi, ++gen, abort, lane)) { ok = false; break; }
+                for (int i = m; i < F.npos * F.nact; i += 128)
+                    if (s_ctr[i]) red_release_add(F.cnt + i, s_ctr[i]);
+            }
+            if (k == n) break;
+            const ItemEnt &it = items[k];
+            const bool up = k < na;
+            if (!up && fused_new_run(it, 1, key, chunk)) {
+                // the B operands of the down runs are formed in their slots one run ahead: the
+                // first run's here, then the next run's while the MMA works on this one (its
+                // slot is free once the MMA has begun this run)
+                bool fail_ = false;
+                for (int r = rb, kk = k; r < rb + 2 && !fail_; r++) {
+                    if (r < built) continue;
+                    // the first item of run r (kk for r == rb; the next key change after it)
+                    if (r > rb) {
+                        int k2 = kk + 1;
+                        while (k2 < n && !fused_new_run(items[k2], 1, (1 << 24) | items[kk].vec, items[kk].s)) k2++;
+                        if (k2 >= n) break;
+                        kk = k2;
+                    }
+                    const ItemEnt &ir = items[kk];
+                    const int slot = r & 1;
+                    if (r >= 2) {
+                        int okw = 1;
+                        if (lane == 0) okw = mbar_wait(b_bempty + 8 * slot, ((r >> 1) - 1) & 1, abort) ? 1 : 0;
+                        if (!__shfl_sync(0xffffffffu, okw, 0)) { fail_ = true; break; }
+                    }
+                    // formed in global memory (the down pass's B operand at this position and
+                    // chunk; every CTA with this run writes the same bytes), then one bulk copy
+                    // into the slot
+                    const size_t vix = (size_t)ir.vec * F.B.nch + ir.s;
+                    unsigned char *gq = const_cast<unsigned char *>(F.B.bq) + vix * kTileB;
+                    unsigned char *gs = const_cast<unsigned char *>(F.B.bs) + vix * kTileSF;
+                    if (!fused_make_b(F, ir.vec, ir.s, gq, gs, q, lane, abort, gabort) ||
+                        !epi_barrier(s_epi, ++gen, abort, lane)) {
+                        fail_ = true;
+                        break;
+                    }
+                    if (m == 0) {
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        const uint32_t bb = b_bfull + 8 * slot, dst = bslots + (uint32_t)(slot * G::kBSlot);
+                        mbar_expect_tx(bb, G::kBTile + kTileSF);
+                        bulk_g2s(dst, gq, G::kBTile, bb);
+                        bulk_g2s(dst + G::kBTile, gs, kTileSF, bb);
+                    }
+                    built = r + 1;
+                }
+                if (fail_) { ok = false; break; }
+                rb++;
+                key = (1 << 24) | it.vec;
+                chunk = it.s;
+            }
+            const Job &J = up ? F.A : F.B;
+            const int row = up ? (m < 64 ? it.tile * 64 + m : (J.out_w >> 1) + it.tile * 64 + (m - 64))
+                               : it.tile * 128 + m;
+            float *dst = J.part + (size_t)it.s * J.slice_stride + (size_t)it.out * J.out_w + row;
+            const int buf = k % kAccBufs;
+            int okw = 1;
+            if (!mbar_wait(b_accf + 8 * buf, (k / kAccBufs) & 1, abort)) okw = 0;
+            if (!__all_sync(0xffffffffu, okw)) { ok = false; break; }
+            tc_fence_after();
+            float v[kN];
+            tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * G::kCols), v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_acce + 8 * buf);
+            float sum = v[15];
+#pragma unroll
+            for (int i = 14; i >= 0; i--) sum += v[i];
+            *dst = sum;
+            if (up && lane == 0) atomicAdd(&s_ctr[it.out * F.nact + it.tile / 8], 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort) atomicExch(gabort, 1);   // other CTAs' waiters give up
+    if (warp == 4 && lane == 0) {
+        tc_commit(b_drain);
+        mbar_drain(b_drain, 0);
+    }
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                     :: "r"(tmem), "r"(G::kTmem) : "memory");
+    }
 }
 
 // ------------------------------------------------------------- grouped items (T > 8)
@@ -1289,6 +1808,55 @@ int umma_launch(int mode, int tiled, const MoeWork &w, const int *idx, const int
         return launch_job<1, 1>(J, (long long)npos_max * J.ntiles * ks, st);
     }
     return launch_job<1, 0>(J, (long long)npos_max * J.ntiles * ks, st);
+}
+
+// Items per CTA of the two passes of the fused launch for npos positions (the table
+// bound), and whether the shapes take it: tiled experts, the resident-B geometry.
+int umma_fused_items(int npos, int hidden, int inter)
+{
+    if (!umma_supported(hidden, inter, GATEUP) || !umma_supported(inter, hidden, DOWN)) return 1 << 30;
+    const long long a = (long long)npos * (inter / 64) * (hidden / kStageK);
+    const long long b = (long long)npos * (hidden / 128) * (inter / kStageK);
+    const long long g = sm_count();
+    return (int)((a + g - 1) / g + (b + g - 1) / g);
+}
+
+size_t umma_fused_cnt_ints(int npos, int inter) { return (size_t)2 * npos * (inter / kStageK) + 1; }
+
+int umma_fused_ok(int npos, int hidden, int inter)
+{
+    return umma_fused_items(npos, hidden, inter) <= kMaxItems && npos * (inter / kStageK) <= kFusedCtr;
+}
+
+// gate/up, act split and down in one launch (k_mxfp4_fused). cnt: umma_fused_cnt_ints
+// ints, zero on entry (the router's grouping zeroes them). Partials and B operands as the
+// three-launch path: part_gu [hidden/512][npos][2 inter] by position, act pieces by
+// position, part_d [inter/512][npos][hidden] by assignment.
+int umma_launch_fused(const MoeWork &w, const int *idx, const int *count, int npos_max, int hidden, int inter,
+                      const uint8_t *bq_x, const uint8_t *bs_x, int vec_div, float *part_gu, size_t sl_gu,
+                      uint8_t *bq_a, uint8_t *bs_a, float *part_d, size_t sl_d, int *cnt, cudaStream_t st)
+{
+    if (!umma_fused_ok(npos_max, hidden, inter)) return fail(K3D_EINVAL, "umma fused: %d positions", npos_max);
+    FusedJob F;
+    K3_TRY(make_job(F.A, GATEUP, 1, w, idx, count, npos_max, hidden, inter, hidden / kStageK, bq_x, bs_x, vec_div,
+                    part_gu, 2 * inter, sl_gu, 0));
+    K3_TRY(make_job(F.B, DOWN, 1, w, idx, count, npos_max, inter, hidden, inter / kStageK, bq_a, bs_a, 1, part_d,
+                    hidden, sl_d, 1));
+    F.cnt = cnt;
+    F.npos = npos_max;
+    F.nact = inter / kStageK;
+    F.arrivals = 4 * (kStageK / 64) * F.A.ks;      // 4 epilogue warps x 8 tiles x K slices
+    static bool init = false;
+    if (!init) {
+        cudaError_t e = cudaFuncSetAttribute(k_mxfp4_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)Geo<1, 1>::kSmem);
+        if (e != cudaSuccess) return fail(K3D_ECUDA, "umma fused smem attribute: %s", cudaGetErrorString(e));
+        init = true;
+    }
+    if (npos_max <= 0) return K3D_OK;
+    launch_pdl(k_mxfp4_fused, dim3(sm_count()), dim3(kThreads), Geo<1, 1>::kSmem, st, F);
+    note_launch();
+    return check_launch("mxfp4 umma fused");
 }
 
 // The grouped pass: items over the groups of G (ng = their device count, at most

@@ -64,6 +64,12 @@ size_t umma_bq_bytes(int K);
 size_t umma_bs_bytes(int K);
 int umma_bsplit(uint8_t *bq, uint8_t *bs, const float *x, int K, int nvec, size_t ld,
                 cudaStream_t st);
+// the fused decode pass (gate/up, act split, down in one launch)
+int umma_fused_ok(int npos, int hidden, int inter);
+size_t umma_fused_cnt_ints(int npos, int inter);
+int umma_launch_fused(const MoeWork &w, const int *idx, const int *count, int npos_max, int hidden, int inter,
+                      const uint8_t *bq_x, const uint8_t *bs_x, int vec_div, float *part_gu, size_t sl_gu,
+                      uint8_t *bq_a, uint8_t *bs_a, float *part_d, size_t sl_d, int *cnt, cudaStream_t st);
 int umma_bsplit_swiglu(uint8_t *bq, uint8_t *bs, const float *part, int ks, size_t slice_stride,
                        int inter, const int *count, int npos, cudaStream_t st);
 int umma_slice_sum(float *y, const float *part, int ks, size_t slice_stride, int n,
@@ -117,6 +123,8 @@ struct RouterGroup {
     int *n_active, *act_expert, *act_off, *assign;
     int lo, hi;
     int done;
+    int *zero = nullptr;     // zeroed by the grouping (the fused expert pass's counters)
+    int nzero = 0;
 };
 int router_bf16(int *idx, float *w, const float *x, const uint16_t *W, const float *bias,
                 int T, int hidden, int n_experts, int topk, int renorm, float routed_scale,

@@ -575,6 +575,8 @@ struct RouterJob {
     // grouping of the assignments by expert (MoE), when n_active is set
     int *n_active, *act_expert, *act_off, *assign;
     int e_lo, e_hi;
+    int *zero;                     // zeroed with the grouping (nzero ints)
+    int nzero;
 };
 
 template <typename WT> struct WChunk;       // 8 weights held in registers
@@ -924,7 +926,7 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
         if (!s_last) return;
     }
     group_assignments(J.idx, J.T * K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
-                      J.assign, gsm);
+                      J.assign, gsm, J.zero, J.nzero);
 }
 
 size_t router_ws_bytes(int T, int n_experts)
@@ -971,6 +973,8 @@ static int router_launch(int *idx, float *w, const float *x, const WT *W, const 
         J.assign = grp ? grp->assign : nullptr;
         J.e_lo = grp ? grp->lo : 0;
         J.e_hi = grp ? grp->hi : n_experts;
+        J.zero = grp ? grp->zero : nullptr;
+        J.nzero = grp ? grp->nzero : 0;
         const size_t smem = fused_smem_bytes<WT>(hidden, n_experts);
         static bool init = false;
         if (!init) { allow_smem_max(k_router_fused<WT>); init = true; }

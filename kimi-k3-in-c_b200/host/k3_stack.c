@@ -134,6 +134,20 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
     m->c = *cfg;
     m->seed = seed;
     m->use_graph = 1;
+    /* Under expert parallelism the shared expert is split over the ranks by its
+     * intermediate rows: rank r computes rows [r SI / N, (r + 1) SI / N) of gate and up and
+     * the same columns of down, and its partial rides the routed experts' combine (SwiGLU
+     * acts row by row, so the partials sum to the whole expert). */
+    const int sh_full = m->c.moe.shared_inter;
+    int sh_lo = 0;
+    {
+        const int nr = k3d_ep_size(), r = k3d_ep_rank();
+        if (nr > 1 && sh_full > 0 && sh_full % (8 * nr) == 0) {
+            m->c.moe.shared_inter = sh_full / nr;
+            m->c.moe.add_shared = 1;
+            sh_lo = r * (sh_full / nr);
+        }
+    }
     const K3dStackCfg *c = &m->c;
     const int E = c->hidden, B = c->batch;
     const size_t P = (size_t)c->kda_heads * c->kda_head_dim;
@@ -277,13 +291,34 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             L->moe.router_w = bf16_param(m, nm, (size_t)s->n_experts * E, 0.02f, &err);
             snprintf(nm, sizeof nm, "layer%d.moe.router_bias", l);
             L->moe.router_bias = f32_uniform(m, nm, s->n_experts, -0.1f, 0.1f, &err);
-            if (s->shared_inter > 0) {
+            if (s->shared_inter > 0 && s->shared_inter == sh_full) {
                 snprintf(nm, sizeof nm, "layer%d.moe.sh_gate", l);
                 L->moe.sh_gate = bf16_param(m, nm, (size_t)s->shared_inter * E, 0.02f, &err);
                 snprintf(nm, sizeof nm, "layer%d.moe.sh_up", l);
                 L->moe.sh_up = bf16_param(m, nm, (size_t)s->shared_inter * E, 0.02f, &err);
                 snprintf(nm, sizeof nm, "layer%d.moe.sh_down", l);
                 L->moe.sh_down = bf16_param(m, nm, (size_t)E * s->shared_inter, 0.02f, &err);
+            } else if (s->shared_inter > 0) {
+                /* this rank's slice of the same seeded matrices a single GPU holds */
+                const size_t SIl = (size_t)s->shared_inter;
+                uint16_t **dst[2] = {(uint16_t **)&L->moe.sh_gate, (uint16_t **)&L->moe.sh_up};
+                const char *nms[2] = {"sh_gate", "sh_up"};
+                for (int k = 0; k < 2 && !err; k++) {
+                    snprintf(nm, sizeof nm, "layer%d.moe.%s", l, nms[k]);
+                    uint16_t *pk = (uint16_t *)dalloc(m, nm, SIl * E * 2);
+                    if (!pk || k3d_fill_bf16_normal_at(pk, SIl * E, next_seed(m), 0.02f, (size_t)sh_lo * E))
+                        err = 1;
+                    *dst[k] = pk;
+                }
+                snprintf(nm, sizeof nm, "layer%d.moe.sh_down", l);
+                uint16_t *pd = (uint16_t *)dalloc(m, nm, (size_t)E * SIl * 2);
+                uint16_t *full = (uint16_t *)k3d_alloc((size_t)E * sh_full * 2);
+                if (!pd || !full || k3d_fill_bf16_normal(full, (size_t)E * sh_full, next_seed(m), 0.02f) ||
+                    k3d_copy2d(pd, SIl * 2, full + sh_lo, (size_t)sh_full * 2, SIl * 2, (size_t)E) ||
+                    k3d_sync())
+                    err = 1;
+                k3d_free(full);
+                L->moe.sh_down = pd;
             }
             const size_t w = k3d_moe_ws_bytes(&c->moe, B);
             if (w > ws) ws = w;
@@ -308,6 +343,8 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             err = 1;
         if (!err && k3d_memset(m->pos, 0, 16)) err = 1;
         if (!err && k3d_sync()) err = 1;
+        /* the peer buffers of the MoE combine (every rank maps every other rank's) */
+        if (!err && k3d_ep_size() > 1 && k3d_ep_peer_init((size_t)B * E)) err = 1;
     }
     if (m->stage_expert) {
         if (k3d_sync()) err = 1;
@@ -383,9 +420,10 @@ static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
             TRY(k3d_swiglu_mlp_bf16(m->h, m->xn, L->dg, L->du, L->dd, E, c->dense_inter, B, 1,
                                     m->mlp_ws));
         } else if (ep) {
+            /* this rank's experts (and shared-expert slice), then the NVLink push combine
+             * that sums every rank's partial into the residual */
             TRY(k3d_moe_swiglu(m->mo, m->xn, &L->moe, &c->moe, B, 0, NULL, NULL, m->ws, m->ws_bytes));
-            TRY(k3d_ep_allreduce_f32(m->mo, (size_t)B * E));
-            TRY(k3d_add_f32(m->h, m->mo, (size_t)B * E));
+            TRY(k3d_ep_combine_add(m->h, m->mo, (size_t)B * E, 1));
         } else {
             TRY(k3d_moe_swiglu(m->h, m->xn, &L->moe, &c->moe, B, 1, NULL, NULL, m->ws, m->ws_bytes));
         }

@@ -148,12 +148,14 @@ _PROTOS = {
     "k3d_last_message": (C.c_char_p, []),
     "k3d_set_abort_on_error": (None, [i32]),
     "k3d_device_error": (i32, [C.POINTER(i32), C.POINTER(i32)]),
+    "k3d_set_wait_limit": (i32, [C.c_longlong]),
     "k3d_alloc": (vp, [sz]),
     "k3d_free": (None, [vp]),
     "k3d_upload": (i32, [vp, vp, sz]),
     "k3d_download": (i32, [vp, vp, sz]),
     "k3d_memset": (i32, [vp, i32, sz]),
     "k3d_copy": (i32, [vp, vp, sz]),
+    "k3d_copy2d": (i32, [vp, C.c_size_t, vp, C.c_size_t, C.c_size_t, C.c_size_t]),
     "k3d_set_weight_cache": (None, [i32]),
     "k3d_forget": (None, [vp]),
     "k3d_forget_all": (None, []),
@@ -226,6 +228,8 @@ _PROTOS = {
     "k3d_ep_rank": (i32, []),
     "k3d_ep_size": (i32, []),
     "k3d_ep_allreduce_f32": (i32, [vp, sz]),
+    "k3d_ep_peer_init": (i32, [C.c_size_t]),
+    "k3d_ep_combine_add": (i32, [vp, vp, C.c_size_t, i32]),
     "k3d_moe_a2a_ws_bytes": (sz, [C.POINTER(K3dMoeShape), i32, i32]),
     "k3d_moe_swiglu_a2a": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, i32, vp,
                                  vp, vp, sz]),

@@ -1,0 +1,118 @@
+"""One rank (one GPU) of the two-GPU tests of the NVLink push combine (test_gpu_ep_combine.py).
+
+run_combine: k3d_ep_combine_add on seeded partials of several lengths, repeated (the
+parity of the receive slots alternates), against the rank-order sum computed on the host;
+every rank must hold the same result.
+run_stack: the reduced-width decode stack under expert parallelism (routed experts split
+by rank, shared expert split by intermediate rows, vocabulary-split LM head, the push
+combine per MoE layer; eager, graph capture, replay), then rank 0 alone steps the same
+seeded model on one GPU with the same tokens: logits within 1e-5 and the same greedy
+tokens."""
+import ctypes
+import datetime
+import os
+
+import numpy as np
+
+
+def _setup(rank, world, port):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    import k3cuda
+    lib = k3cuda.init(rank)
+    idb = np.zeros(128, np.uint8)
+    if rank == 0:
+        k3cuda.check(lib.k3d_ep_unique_id(idb.ctypes.data))
+    t = torch.from_numpy(idb)
+    dist.broadcast(t, 0)
+    idb = t.numpy().copy()
+    k3cuda.check(lib.k3d_ep_init(rank, world, idb.ctypes.data), "ep init")
+    return lib, dist, torch
+
+
+def run_combine(rank, world, port, seed):
+    lib, dist, torch = _setup(rank, world, port)
+    import k3cuda
+    try:
+        nmax = 64 * 7168
+        k3cuda.check(lib.k3d_ep_peer_init(nmax), "peer init")
+        for call, n in enumerate([7168, 7168, 3 * 7168, nmax, 7168, 1000]):
+            parts = [np.random.default_rng(seed * 100 + call * 10 + r).standard_normal(n).astype(np.float32)
+                     for r in range(world)]
+            h0 = np.random.default_rng(seed * 100 + call).standard_normal(n).astype(np.float32)
+            H = k3cuda.DevBuf.from_array(h0, lib)
+            P = k3cuda.DevBuf.from_array(parts[rank], lib)
+            k3cuda.check(lib.k3d_ep_combine_add(H.ptr, P.ptr, n, 1), f"combine {call}")
+            k3cuda.check(lib.k3d_sync(), f"combine {call} sync")
+            got = H.download(np.float32, n)
+            v = parts[0].copy()
+            for r in range(1, world):
+                v = (v + parts[r]).astype(np.float32)
+            want = (h0 + v).astype(np.float32)
+            assert np.array_equal(got, want), (call, float(np.abs(got - want).max()))
+            allg = [torch.zeros(n, dtype=torch.float32) for _ in range(world)]
+            dist.all_gather(allg, torch.from_numpy(got))
+            assert all(np.array_equal(a.numpy(), got) for a in allg), "ranks disagree"
+        k3cuda.check(lib.k3d_ep_finalize())
+    finally:
+        dist.destroy_process_group()
+
+
+def run_stack(rank, world, port, seed, batch):
+    lib, dist, torch = _setup(rank, world, port)
+    import k3cuda
+    from test_gpu_stack import CFG, make_cfg, download
+    try:
+        c = CFG
+        E = c["moe"]["n_experts"]
+
+        def model_cfg(lo, hi, add_shared):
+            sc = make_cfg(c, batch=batch, layout=1)
+            sc.moe.expert_lo, sc.moe.expert_hi, sc.moe.add_shared = lo, hi, add_shared
+            return sc
+
+        def steps(model, toks):
+            out, logs = [], []
+            for step in range(3):            # eager, graph capture, replay
+                nxt = np.zeros(batch, np.int32)
+                k3cuda.check(lib.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
+                logs.append(download(lib, model, "logits", np.float32).reshape(batch, -1).copy())
+                out.append(nxt.copy())
+                toks = nxt.copy()
+            return out, logs
+
+        toks0 = ((np.arange(batch) * 37 + 5) % c["vocab"]).astype(np.int32)
+        lo, hi = rank * E // world, (rank + 1) * E // world
+        model = lib.k3d_model_create(ctypes.byref(model_cfg(lo, hi, 1 if rank == 0 else 0)), seed)
+        assert model, lib.k3d_last_message()
+        k3cuda.check(lib.k3d_model_fill_context(model, 6, 17))
+        toks_ep, logs_ep = steps(model, toks0)
+        lib.k3d_model_destroy(model)           # releases the graph (it holds an NCCL call)
+        k3cuda.check(lib.k3d_sync())
+        for t in toks_ep:
+            allg = [torch.zeros(batch, dtype=torch.int32) for _ in range(world)]
+            dist.all_gather(allg, torch.from_numpy(t))
+            assert all(np.array_equal(a.numpy(), t) for a in allg), "ranks disagree on tokens"
+        k3cuda.check(lib.k3d_ep_finalize())
+        if rank == 0:
+            assert lib.k3d_ep_size() == 1
+            model = lib.k3d_model_create(ctypes.byref(model_cfg(0, E, 1)), seed)
+            assert model, lib.k3d_last_message()
+            k3cuda.check(lib.k3d_model_fill_context(model, 6, 17))
+            toks_1, logs_1 = steps(model, toks0)
+            lib.k3d_model_destroy(model)
+            for s in range(3):
+                a, b = logs_ep[s], logs_1[s]
+                err = float(np.abs(a - b).max() / np.abs(b).max())
+                assert err <= 1e-5, (s, err)
+                for q in range(batch):
+                    top2 = np.sort(b[q])[-2:]
+                    if top2[1] - top2[0] > 1e-4 * np.abs(b[q]).max():
+                        assert toks_ep[s][q] == toks_1[s][q], (s, q)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()

@@ -204,3 +204,27 @@ def test_resident_b_matches_per_stage_b_and_oracle(k3, oracle, T):
     want, oi, _ = oracle.moe_swiglu(x, T, hidden, inter, E, 8, 1, 2.5, W, bias, experts, 256, *sh)
     assert np.array_equal(idx, oi)
     assert max_rel_err(ys[0][0], want) <= 1e-4
+
+
+@pytest.mark.parametrize("T,hidden,inter,E", [(1, 1024, 512, 16), (2, 1024, 512, 16), (1, 7168, 2048, 16)])
+def test_fused_pass_matches_three_launches_and_oracle(k3, oracle, T, hidden, inter, E):
+    """Kind 4: decode-sized work lists (up to 16 assignments) run gate/up, the act split and
+    down as one launch (k_mxfp4_fused) with cross-CTA counters; the result is bit-identical
+    to the three-launch form (kind 0) and matches the oracle; repeated calls agree (the
+    router zeroes the counters every call, so a fresh workspace needs no set-up)."""
+    g, experts, W, bias, sh = small_layer(1400 + T + hidden, hidden=hidden, inter=inter, E=E)
+    mw = k3cuda.MoeWeights(hidden, inter, E, 8, W, bias, shared=sh, experts=experts, tiled=True)
+    x = synth.bf16_to_f32(synth.bf16_normal(g, (T, hidden), 1.0))
+    ys = {}
+    try:
+        for kind in (4, 0, 4):
+            k3cuda.check(k3.k3d_set_expert_kernel(kind))
+            y, idx, _ = run_layer(k3, mw, x, T)
+            ys.setdefault(kind, []).append(y)
+    finally:
+        k3cuda.check(k3.k3d_set_expert_kernel(0))
+    assert np.array_equal(ys[4][0], ys[0][0])
+    assert np.array_equal(ys[4][0], ys[4][1])
+    want, oi, _ = oracle.moe_swiglu(x, T, hidden, inter, E, 8, 1, 2.5, W, bias, experts, 256, *sh)
+    assert np.array_equal(idx, oi)
+    assert max_rel_err(ys[0][0], want) <= 1e-4
