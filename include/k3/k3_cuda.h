@@ -278,6 +278,11 @@ int    k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K
 int    k3d_kda_layer_decode_normed(float *h, const float *norm_w, float eps, const K3dKdaW *w,
                                    const K3dKdaShape *s, int B, float *state, void *ws,
                                    size_t ws_bytes);
+/* Which kernel runs the per-head step of the decode layer: 0 (default) keeps each thread's
+ * state column in registers where head_dim is 32, 64 or 128 and conv_k is 4 (else as 1);
+ * 1 stages the head's state tile in shared memory. Bit-identical; the switch exists to
+ * measure and test each. No reference counterpart. */
+int    k3d_set_kda_head_kernel(int kind);
 
 /* ------------------------------------------------------------------- MLA ---- */
 typedef struct {
@@ -342,6 +347,12 @@ int k3d_lm_head_argmax_shard_normed(int *next, float *logits, const float *x, co
                                     int hidden, int B, void *key_ws);
 /* y[i] += x[i] for i < n (device floats) */
 int k3d_add_f32(float *y, const float *x, size_t n);
+/* Row-wise conversions between bf16 (rows with a pitch, in elements) and packed fp32,
+ * round to nearest even towards bf16, and a transpose of a rows x cols matrix of 16-bit
+ * values (dst is cols x rows). Device pointers. No reference counterpart. */
+int k3d_bf16_rows_to_f32(float *dst, const uint16_t *src, size_t spitch, int rows, int cols);
+int k3d_f32_rows_to_bf16(uint16_t *dst, size_t dpitch, const float *src, int rows, int cols);
+int k3d_transpose_u16(uint16_t *dst, const uint16_t *src, int rows, int cols);
 /* p[i] += delta for i < n (device ints; advances cache positions inside a graph) */
 int k3d_add_i32(int *p, int n, int delta);
 
@@ -435,6 +446,31 @@ int       k3d_model_use_graph(K3dModel *m, int on);
 void     *k3d_model_tensor(K3dModel *m, const char *name, size_t *bytes);
 /* Algorithmic bytes the last step read or wrote in HBM (weights + caches + states). */
 double    k3d_model_last_step_bytes(K3dModel *m);
+
+/* Conversation state in the CPU engine's file format (K3ST version 1, k3_run.c:158-300,
+ * which has no library interface: k3_state_peek/k3_state_save/k3_state_load are static
+ * in the CLI): the configuration fingerprint, the token ids, one KDA state slot per layer,
+ * the MLA caches as expanded keys and values (kv_b times the latent, fp32) and rope slots,
+ * only the occupied positions. The CPU engine can resume from a file saved here and the
+ * reverse. After the CPU engine's payload a save appends the device's own bf16 cache rows
+ * ("K3LT"), which the CPU engine does not read; a load with that trailer restores the
+ * caches bit for bit, one without it recovers each latent from the expanded keys and
+ * values by least squares (within bf16 rounding of the original).
+ *   peek: the header only, so the caller can size seq before loading; has_latent says
+ *         whether the trailer is there.
+ *   save: sequence b of the batch at the model's current position; seq (nseq ids, host)
+ *         are the tokens the caller keeps for it.
+ *   load: into sequence b; refuses (K3D_EINVAL) a file whose fingerprint, layer counts
+ *         or per-layer sizes differ from this model, K3D_EBOUND when it holds more
+ *         positions than ctx_cap or more ids than seq_cap. Sets the model's position to
+ *         the file's (the position is shared by the batch). seq may be NULL. A load that
+ *         fails part-way leaves the caches partly written. */
+typedef struct {
+    int version, n_bound, n_mla, cached, nseq, has_latent;
+} K3dStateInfo;
+int       k3d_state_peek(const char *path, K3dStateInfo *info);
+int       k3d_model_state_save(K3dModel *m, const char *path, const int *seq, int nseq, int b);
+int       k3d_model_state_load(K3dModel *m, const char *path, int *seq, int seq_cap, int b);
 
 #ifdef __cplusplus
 }

@@ -202,6 +202,111 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
     A.heads[bp] = o;
 }
 
+// The same head with the state column in registers: thread j loads column j of the head's
+// state (DT coalesced rows, all issued before the programmatic wait), runs both passes of
+// the step on its registers and stores the column back. No shared-memory tile, no bulk
+// copy, and the two dependent fadd chains (u, then o) are the only serial part: the
+// shared-tile kernel paid a shared-memory round trip per row in each pass with four warps
+// per SM to hide it. Same operations in the same order, so bit-identical to k_kda_head.
+template <int KC, int DT>
+__global__ void __launch_bounds__(DT) k_kda_head_reg(const __grid_constant__ KdaHeadArgs A)
+{
+    static_assert(KC > 0 && DT % 32 == 0 && DT <= 128, "register head: KC > 0, DT in 32..128");
+    constexpr int NW = DT / 32;
+    __shared__ float qs[DT], ks[DT], kbs[DT], as[DT];
+    __shared__ double red[2][NW];
+    const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
+    const int H = A.H, P = H * DT, lane = j & 31, warp = j >> 5;
+    float *S = A.state + (size_t)b * A.state_stride + (size_t)h * DT * DT;
+    float *conv = A.state + (size_t)b * A.state_stride + (size_t)H * DT * DT;
+    const int c = h * DT + j;
+    const size_t bp = (size_t)b * P + c;
+    float *hq = conv + (size_t)c * (KC - 1);
+    float *hk = conv + (size_t)P * (KC - 1) + (size_t)c * (KC - 1);
+    float *hv = conv + (size_t)2 * P * (KC - 1) + (size_t)c * (KC - 1);
+    // this layer's previous step wrote the state and the conv history; no kernel since
+    float s[DT];
+#pragma unroll
+    for (int i = 0; i < DT; i++) s[i] = S[(size_t)i * DT + j];
+    float wq[KC], wk[KC], wv[KC], xq[KC], xk[KC], xv[KC];
+#pragma unroll
+    for (int t = 0; t < KC; t++) {
+        wq[t] = A.q_conv[(size_t)c * KC + t];
+        wk[t] = A.k_conv[(size_t)c * KC + t];
+        wv[t] = A.v_conv[(size_t)c * KC + t];
+    }
+#pragma unroll
+    for (int t = 0; t < KC - 1; t++) { xq[t] = hq[t]; xk[t] = hk[t]; xv[t] = hv[t]; }
+    const float dtb = A.dt_bias[c], alog = A.A_log[h], onw = A.o_norm[j];
+    pdl_wait();
+    pdl_trigger();
+    xq[KC - 1] = A.qp[bp]; xk[KC - 1] = A.kp[bp]; xv[KC - 1] = A.vp[bp];
+    const float gpv = A.gp[bp], zv = A.z[bp], bpv = A.bp[(size_t)b * H + h];
+    float aq = __fmul_rn(wq[KC - 1], xq[KC - 1]);
+    float ak = __fmul_rn(wk[KC - 1], xk[KC - 1]);
+    float av = __fmul_rn(wv[KC - 1], xv[KC - 1]);
+#pragma unroll
+    for (int t = 0; t < KC - 1; t++) {
+        aq = __fadd_rn(aq, __fmul_rn(wq[t], xq[t]));
+        ak = __fadd_rn(ak, __fmul_rn(wk[t], xk[t]));
+        av = __fadd_rn(av, __fmul_rn(wv[t], xv[t]));
+    }
+#pragma unroll
+    for (int t = 0; t < KC - 1; t++) { hq[t] = xq[t + 1]; hk[t] = xk[t + 1]; hv[t] = xv[t + 1]; }
+    float qv = __fmul_rn(aq, sigm(aq));
+    float kv = __fmul_rn(ak, sigm(ak));
+    const float vv = __fmul_rn(av, sigm(av));
+    // both L2 norms in one exchange, each summed as block_sum_dd sums it
+    {
+        const double q2 = warp_sum_d((double)qv * (double)qv), k2 = warp_sum_d((double)kv * (double)kv);
+        if (lane == 0) { red[0][warp] = q2; red[1][warp] = k2; }
+    }
+    __syncthreads();
+    double sq = 0.0, sk = 0.0;
+#pragma unroll
+    for (int i = 0; i < NW; i++) { sq += red[0][i]; sk += red[1][i]; }
+    qv = __fmul_rn(qv, (float)(1.0 / sqrt(sq + (double)1e-6f)));
+    kv = __fmul_rn(kv, (float)(1.0 / sqrt(sk + (double)1e-6f)));
+    qv = __fmul_rn(qv, 1.0f / sqrtf((float)A.D));
+    const float beta = sigm(bpv);
+    const float a = expf(alog);
+    const float gdec = __fmul_rn(A.lb, sigm(__fmul_rn(a, __fadd_rn(zv, dtb))));
+    qs[j] = qv;
+    ks[j] = kv;
+    kbs[j] = __fmul_rn(kv, beta);
+    as[j] = expf(gdec);
+    __syncthreads();
+    float u = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DT; i++) {
+        s[i] = __fmul_rn(s[i], as[i]);
+        const float ki = ks[i];
+        if (ki != 0.0f) u = __fadd_rn(u, __fmul_rn(ki, s[i]));
+    }
+    const float d = __fsub_rn(vv, u);
+    float o = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DT; i++) {
+        float si = s[i];
+        if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(kbs[i], d));
+        const float qi = qs[i];
+        if (qi != 0.0f) o = __fadd_rn(o, __fmul_rn(qi, si));
+        S[(size_t)i * DT + j] = si;
+    }
+    {
+        const double o2 = warp_sum_d((double)o * (double)o);
+        if (lane == 0) red[0][warp] = o2;            // red[0] was last read before the
+    }                                                // barrier above
+    __syncthreads();
+    double so = 0.0;
+#pragma unroll
+    for (int i = 0; i < NW; i++) so += red[0][i];
+    const float inv = (float)(1.0 / sqrt(so / (double)DT + (double)A.eps));
+    o = __fmul_rn(__fmul_rn(onw, o), inv);
+    o = __fmul_rn(o, sigm(gpv));
+    A.heads[bp] = o;
+}
+
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 }  // namespace k3
@@ -225,6 +330,11 @@ size_t k3d_kda_state_floats(const K3dKdaShape *s)
 }
 
 }  // extern "C"
+
+// Which head kernel runs (k3d_set_kda_head_kernel): 0 the register-column kernel where
+// head_dim is 32, 64 or 128 and conv_k is 4, else the shared-tile kernel; 1 always the
+// shared-tile kernel.
+static int g_kda_head_kernel = 0;
 
 // The layer; with ni, xn is the raw residual and the projection GEMV normalises it.
 static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K3dKdaW *w,
@@ -268,7 +378,11 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
         allow_smem_max(k_kda_head<0>);
         init = true;
     }
-    if (s->conv_k == 4) launch_pdl(k_kda_head<4>, dim3(H, B), dim3(D), smem, st, A);
+    const bool reg = g_kda_head_kernel == 0 && s->conv_k == 4;
+    if (reg && D == 128) launch_pdl(k_kda_head_reg<4, 128>, dim3(H, B), dim3(D), 0, st, A);
+    else if (reg && D == 64) launch_pdl(k_kda_head_reg<4, 64>, dim3(H, B), dim3(D), 0, st, A);
+    else if (reg && D == 32) launch_pdl(k_kda_head_reg<4, 32>, dim3(H, B), dim3(D), 0, st, A);
+    else if (s->conv_k == 4) launch_pdl(k_kda_head<4>, dim3(H, B), dim3(D), smem, st, A);
     else launch_pdl(k_kda_head<0>, dim3(H, B), dim3(D), smem, st, A);
     note_launch();
     K3_TRY(check_launch("kda head"));
@@ -280,6 +394,13 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
 }
 
 extern "C" {
+
+int k3d_set_kda_head_kernel(int kind)
+{
+    if (kind < 0 || kind > 1) return fail(K3D_EINVAL, "k3d_set_kda_head_kernel(%d): 0 or 1", kind);
+    g_kda_head_kernel = kind;
+    return K3D_OK;
+}
 
 int k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K3dKdaShape *s,
                          int B, float *state, void *ws, size_t ws_bytes)

@@ -169,28 +169,33 @@ __global__ void __launch_bounds__(256) k_mla_prep(float *ql, float *c, uint16_t 
 __global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, const float2 *rope_tab,
                              const int *pos_p, MlaDims d, int cap)
 {
-    pdl_wait();
-    pdl_trigger();
     __shared__ float qs[256];
     __shared__ float part[8][128 + 4];
     const int h = blockIdx.x, jb = blockIdx.y, b = blockIdx.z;
     const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * 16 + tx;
-    const float *qh = q + ((size_t)b * d.H + h) * d.qh;
-    for (int i = tid; i < d.qh; i += 128) qs[i] = qh[i];
-    __syncthreads();
     const size_t kvd = (size_t)(d.qn + d.vh);
     const uint16_t *wuk = kv_b + (size_t)h * kvd * d.kv_lora + jb * 128 + tx * 8;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const int per = (d.qn + 7) / 8;          // rows of W_uk per thread row (<= 32)
-    for (int g0 = 0; g0 < per; g0 += 16) {
-        // all of this group's 16-byte loads are issued before any arithmetic
-        uint4 wv[16];
+    // all of a group's 16-byte loads are issued before any arithmetic; the first group's
+    // before the programmatic wait (weights)
+    uint4 wv[16];
+    auto load_group = [&](int g0) {
 #pragma unroll
         for (int ii = 0; ii < 16; ii++) {
             // clamped row (always a valid address); out-of-range rows get weight 0 below
             const int i = min(ty * per + min(g0 + ii, per - 1), d.qn - 1);
             wv[ii] = __ldg(reinterpret_cast<const uint4 *>(wuk + (size_t)i * d.kv_lora));
         }
+    };
+    load_group(0);
+    pdl_wait();
+    pdl_trigger();
+    const float *qh = q + ((size_t)b * d.H + h) * d.qh;
+    for (int i = tid; i < d.qh; i += 128) qs[i] = qh[i];
+    __syncthreads();
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int g0 = 0; g0 < per; g0 += 16) {
+        if (g0 > 0) load_group(g0);
 #pragma unroll
         for (int ii = 0; ii < 16; ii++) {
             const int i = min(ty * per + g0 + ii, d.qn - 1);
@@ -383,16 +388,21 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
         for (int j = 0; j < 8; j++) acc8[j][0] = acc8[j][1] = acc8[j][2] = acc8[j][3] = 0.f;
         const uint32_t a_row = cbase + (uint32_t)((warp * 16 + (lane & 15)) * pitch + (lane >> 4) * 8) * 2u;
         const uint32_t b_row = (uint32_t)((((lane >> 4) << 3) + (lane & 7)) * pitch + ((lane >> 3) & 1) * 8) * 2u;
-        for (int ks = 0; ks < ksteps; ks++) {
-            uint32_t a[4], bh[4], bl[4];
-            ldsm4(a, a_row + ks * 32u);
-            ldsm4(bh, qhi_s + b_row + ks * 32u);
-            ldsm4(bl, qlo_s + b_row + ks * 32u);
-            const int o = (ks & 1) * 4;
-            mma_bf16(acc8[o + 0], a, bh[0], bh[1]);
-            mma_bf16(acc8[o + 1], a, bh[2], bh[3]);
-            mma_bf16(acc8[o + 2], a, bl[0], bl[1]);
-            mma_bf16(acc8[o + 3], a, bl[2], bl[3]);
+        // even k steps into acc8[0..3], odd into acc8[4..7]; the pair is unrolled so that
+        // every accumulator index is a constant (a run-time index puts acc8 in local memory)
+        for (int ks = 0; ks < ksteps; ks += 2) {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                if (u == 1 && ks + 1 >= ksteps) break;
+                uint32_t a[4], bh[4], bl[4];
+                ldsm4(a, a_row + (ks + u) * 32u);
+                ldsm4(bh, qhi_s + b_row + (ks + u) * 32u);
+                ldsm4(bl, qlo_s + b_row + (ks + u) * 32u);
+                mma_bf16(acc8[4 * u + 0], a, bh[0], bh[1]);
+                mma_bf16(acc8[4 * u + 1], a, bh[2], bh[3]);
+                mma_bf16(acc8[4 * u + 2], a, bl[0], bl[1]);
+                mma_bf16(acc8[4 * u + 3], a, bl[2], bl[3]);
+            }
         }
         float sc[2][4];
 #pragma unroll
@@ -531,18 +541,35 @@ static size_t mla_attn_smem(int kvw)
 
 // grid (H, vh / 32, B), 256 threads: merge the splits of head h into ctx (each CTA of the
 // head repeats this small step), then 32 rows of o = W_uv ctx, times sigmoid(gate).
-// heads [B][H*vh].
+// heads [B][H*vh]. The W_uv rows are loaded before the programmatic wait (weights), and
+// after it every partial load the merge needs first (m and l of one split per thread, the
+// first kMP ctx partials of the thread's column pair) is issued before any reduction.
+static const int kMP = 12;
 __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *part,
                                                    const uint16_t *kv_b, const float *gate,
                                                    const int *pos_p, MlaDims d, int cap)
 {
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ float cx[];   // [kv_lora]
     __shared__ float wsc[256 + 2 * 256];   // split weights, then partial column sums
     __shared__ float red[8];
     const int h = blockIdx.x, rb = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // 32 rows of W_uv, 4 per warp: every 16-byte load of the warp's rows first (kv_lora <=
+    // 512, so a lane holds at most 2 chunks of each row)
+    const size_t kvd = (size_t)(d.qn + d.vh);
+    const uint16_t *rows = kv_b + ((size_t)h * kvd + d.qn + rb * 32 + warp * 4) * d.kv_lora;
+    const bool vec = (d.kv_lora & 255) == 0;
+    const int nck = d.kv_lora / 256;          // chunks per lane per row: 1 or 2
+    uint4 wv[4][2];
+    if (vec) {
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int k = 0; k < 2; k++)
+                if (k < nck) wv[r][k] = __ldg(reinterpret_cast<const uint4 *>(rows + (size_t)r * d.kv_lora + k * 256 + lane * 8));
+    }
+    pdl_wait();
+    pdl_trigger();
     const int pos = *pos_p;
     if (pos < 0 || pos >= cap) {
         for (int r = tid; r < 32; r += blockDim.x)
@@ -551,23 +578,32 @@ __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *pa
     }
     const float *pp = part + ((size_t)b * d.H + h) * d.nsplit * (d.kv_lora + 2);
     const int stride = d.kv_lora + 2;
-    // the splits that own positions (a split past the end wrote nothing)
+    // the splits that own positions (a split past the end wrote nothing); ns <= 256
     const int n = pos + 1, per = (n + d.nsplit - 1) / d.nsplit;
     const int ns = min(d.nsplit, (n + per - 1) / per);
-    float M = -INFINITY;
-    for (int s = tid; s < ns; s += blockDim.x) M = fmaxf(M, pp[s * stride + d.kv_lora]);
-    M = warp_max(M);
+    const int np2 = d.kv_lora / 2;            // 256 for kv_lora 512
+    const int nsub = blockDim.x / np2;        // 1 (kv_lora 512) .. 4 (kv_lora 128)
+    const int cp = tid % np2, sub = tid / np2;
+    const float ms = tid < ns ? pp[tid * stride + d.kv_lora] : -INFINITY;
+    const float ls = tid < ns ? pp[tid * stride + d.kv_lora + 1] : 0.f;
+    float2 pv[kMP];
+#pragma unroll
+    for (int k = 0; k < kMP; k++) {
+        const int sp = sub + k * nsub;
+        pv[k] = (sub < nsub && sp < ns) ? *reinterpret_cast<const float2 *>(pp + (size_t)sp * stride + 2 * cp)
+                                        : make_float2(0.f, 0.f);
+    }
+    float M = warp_max(ms);
     if (lane == 0) red[warp] = M;
     __syncthreads();
     M = red[0];
     for (int i = 1; i < 8; i++) M = fmaxf(M, red[i]);
     __syncthreads();
     float L = 0.f;
-    for (int s = tid; s < ns; s += blockDim.x) {
-        const float ms = pp[s * stride + d.kv_lora];
+    if (tid < ns) {
         const float w = (ms == -INFINITY) ? 0.f : expf(ms - M);
-        wsc[s] = w;
-        L += w * pp[s * stride + d.kv_lora + 1];
+        wsc[tid] = w;
+        L = w * ls;
     }
     L = warp_sum(L);
     if (lane == 0) red[warp] = L;
@@ -579,13 +615,18 @@ __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *pa
     // splits congruent to t / np2 (mod nsub), then the nsub partial sums are added in a
     // fixed order through shared memory
     {
-        const int np2 = d.kv_lora / 2;            // 256 for kv_lora 512
-        const int nsub = blockDim.x / np2;        // 1 (kv_lora 512) .. 4 (kv_lora 128)
-        const int cp = tid % np2, sub = tid / np2;
         float2 a = make_float2(0.f, 0.f);
         if (sub < nsub) {
+#pragma unroll
+            for (int k = 0; k < kMP; k++) {
+                const int sp = sub + k * nsub;
+                if (sp < ns) {
+                    a.x = fmaf(wsc[sp], pv[k].x, a.x);
+                    a.y = fmaf(wsc[sp], pv[k].y, a.y);
+                }
+            }
 #pragma unroll 8
-            for (int sp = sub; sp < ns; sp += nsub) {
+            for (int sp = sub + kMP * nsub; sp < ns; sp += nsub) {
                 const float2 v = *reinterpret_cast<const float2 *>(pp + (size_t)sp * stride + 2 * cp);
                 a.x = fmaf(wsc[sp], v.x, a.x);
                 a.y = fmaf(wsc[sp], v.y, a.y);
@@ -607,19 +648,8 @@ __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *pa
         }
     }
     __syncthreads();
-    // 32 rows of W_uv, 4 per warp: every 16-byte load of the warp's rows is issued before
-    // any arithmetic (kv_lora <= 512, so a lane holds at most 2 chunks of each row)
-    const size_t kvd = (size_t)(d.qn + d.vh);
-    const uint16_t *rows = kv_b + ((size_t)h * kvd + d.qn + rb * 32 + warp * 4) * d.kv_lora;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if ((d.kv_lora & 255) == 0) {
-        const int nck = d.kv_lora / 256;          // chunks per lane per row: 1 or 2
-        uint4 wv[4][2];
-#pragma unroll
-        for (int r = 0; r < 4; r++)
-#pragma unroll
-            for (int k = 0; k < 2; k++)
-                if (k < nck) wv[r][k] = __ldg(reinterpret_cast<const uint4 *>(rows + (size_t)r * d.kv_lora + k * 256 + lane * 8));
+    if (vec) {
 #pragma unroll
         for (int r = 0; r < 4; r++)
 #pragma unroll

@@ -13,6 +13,8 @@
  * rank allocates only the experts in cfg->moe.[expert_lo, expert_hi) and the step sums
  * the per-rank MoE partials with one NCCL all-reduce per MoE layer.
  */
+#include <math.h>
+#include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -259,6 +261,11 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
                 m->stage_expert = (unsigned char *)k3d_alloc(per);
                 if (!m->stage_expert) { err = 1; free(tab); break; }
             }
+            /* one seed per matrix kind and layer, mixed with the expert index: expert e
+             * holds the same bytes whichever rank fills it, and the seed counter advances
+             * the same way on every rank (the weights after this layer match too) */
+            uint64_t msd[3];
+            for (int j = 0; j < 3; j++) msd[j] = next_seed(m);
             for (int e = s->expert_lo; e < s->expert_hi && !err; e++) {
                 unsigned char *base = L->pool + (size_t)(e - s->expert_lo) * per;
                 unsigned char *src = tiled ? m->stage_expert : base;
@@ -268,7 +275,8 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
                 q.p2 = src + off[4]; q.s2 = src + off[5];
                 for (int j = 0; j < 3; j++)
                     if (k3d_fill_mxfp4(src + off[2 * j], sz[2 * j], src + off[2 * j + 1],
-                                       sz[2 * j + 1], next_seed(m) + (uint64_t)e, 117, 121))
+                                       sz[2 * j + 1], msd[j] ^ ((uint64_t)(e + 1) * 0x9E3779B97F4A7C15ull),
+                                       117, 121))
                         err = 1;
                 if (tiled) {
                     K3ExpertQ t;
@@ -533,4 +541,350 @@ double k3d_model_last_step_bytes(K3dModel *m)
         }
     }
     return bytes;
+}
+
+/* ------------------------------------------------------ conversation state ----
+ * The CPU engine's state file (K3ST version 1, src/cli/k3_run.c:158-300): a header with a
+ * configuration fingerprint, the sequence's token ids, one KDA state slot per layer
+ * (k3_kda_layer's layout; zeros for MLA and dense layers), then per MLA layer the cached
+ * positions of the EXPANDED keys and values (kv_b times the normalised latent, [H][nope +
+ * v] per position, the CPU engine's cache) and per MLA layer the rope slots. The device
+ * keeps the compressed bf16 latent instead, so saving expands it through kv_b on the
+ * tensor-core GEMM, and a trailer after the CPU engine's payload ("K3LT": the cache rows
+ * exactly as the device holds them) lets a device load restore them bit for bit. The CPU
+ * engine reads exactly its payload and never the trailer. A file without the trailer
+ * (written by the CPU engine) is loaded by recovering each position's latent from its
+ * expanded keys and values by least squares: (kv_b^T kv_b) c = kv_b^T kv, the Gram matrix
+ * and the right-hand sides on the GPU, the Cholesky solve in double on the host. */
+#define K3ST_MAGIC "K3ST"
+#define K3ST_VERSION 1
+#define K3LT_MAGIC "K3LT"
+#define K3ST_CHUNK 256                 /* positions per device pass */
+
+typedef struct {
+    char    magic[4];
+    int32_t version;
+    int32_t fp[12];
+    int32_t n_bound, n_mla, cached, nseq;
+    int64_t kper;
+    int64_t kvpp, ropepp;
+} K3StHeader;                          /* the field order and types of the CPU engine's */
+
+typedef struct {
+    char    magic[4];
+    int32_t version, n_mla, cached, kvw;
+} K3LtTrailer;
+
+static void state_fingerprint(const K3dStackCfg *c, int32_t fp[12])
+{
+    fp[0] = c->hidden;         fp[1] = c->n_layers;      fp[2] = c->vocab;
+    fp[3] = c->kda_heads;      fp[4] = c->kda_head_dim;  fp[5] = c->conv_k;
+    fp[6] = c->mla.n_heads;    fp[7] = c->mla.qk_nope;   fp[8] = c->mla.qk_rope;
+    fp[9] = c->mla.v_head;     fp[10] = c->moe.n_experts; fp[11] = c->moe.topk;
+}
+
+static int state_n_mla(const K3dModel *m)
+{
+    int n = 0;
+    for (int l = 0; l < m->c.n_layers; l++) n += m->L[l].is_mla;
+    return n;
+}
+
+static int64_t state_kper(const K3dStackCfg *c)
+{
+    const int64_t P = (int64_t)c->kda_heads * c->kda_head_dim;
+    return P * c->kda_head_dim + 3 * P * (c->conv_k - 1);
+}
+
+static int read_header(FILE *f, K3StHeader *hd)
+{
+    if (fread(hd, 1, sizeof *hd, f) != sizeof *hd || memcmp(hd->magic, K3ST_MAGIC, 4) != 0)
+        return K3D_EINVAL;
+    return hd->version == K3ST_VERSION ? K3D_OK : K3D_EINVAL;
+}
+
+int k3d_state_peek(const char *path, K3dStateInfo *info)
+{
+    if (!path || !info) return K3D_EINVAL;
+    FILE *f = fopen(path, "rb");
+    if (!f) return K3D_EINVAL;
+    K3StHeader hd;
+    int r = read_header(f, &hd);
+    memset(info, 0, sizeof *info);
+    if (!r) {
+        info->version = hd.version;
+        info->n_bound = hd.n_bound;
+        info->n_mla = hd.n_mla;
+        info->cached = hd.cached;
+        info->nseq = hd.nseq;
+        const long tail = (long)sizeof hd + (long)hd.nseq * 4 + (long)(hd.kper * hd.n_bound * 4) +
+                          (long)hd.n_mla * hd.cached * (long)(hd.kvpp + hd.ropepp) * 4;
+        K3LtTrailer tr;
+        info->has_latent = fseek(f, tail, SEEK_SET) == 0 && fread(&tr, 1, sizeof tr, f) == sizeof tr &&
+                           memcmp(tr.magic, K3LT_MAGIC, 4) == 0;
+    }
+    fclose(f);
+    return r;
+}
+
+/* Cholesky factor of the n x n symmetric positive definite G (lower, in place). */
+static int cholesky(double *G, int n)
+{
+    for (int j = 0; j < n; j++) {
+        double d = G[(size_t)j * n + j];
+        for (int k = 0; k < j; k++) d -= G[(size_t)j * n + k] * G[(size_t)j * n + k];
+        if (!(d > 0.0)) return -1;
+        d = sqrt(d);
+        G[(size_t)j * n + j] = d;
+        for (int i = j + 1; i < n; i++) {
+            double v = G[(size_t)i * n + j];
+            for (int k = 0; k < j; k++) v -= G[(size_t)i * n + k] * G[(size_t)j * n + k];
+            G[(size_t)i * n + j] = v / d;
+        }
+    }
+    return 0;
+}
+
+static void chol_solve(const double *Lf, int n, const float *rhs, float *out, double *tmp)
+{
+    for (int i = 0; i < n; i++) {
+        double v = rhs[i];
+        for (int k = 0; k < i; k++) v -= Lf[(size_t)i * n + k] * tmp[k];
+        tmp[i] = v / Lf[(size_t)i * n + i];
+    }
+    for (int i = n - 1; i >= 0; i--) {
+        double v = tmp[i];
+        for (int k = i + 1; k < n; k++) v -= Lf[(size_t)k * n + i] * tmp[k];
+        tmp[i] = v / Lf[(size_t)i * n + i];
+    }
+    for (int i = 0; i < n; i++) out[i] = (float)tmp[i];
+}
+
+int k3d_model_state_save(K3dModel *m, const char *path, const int *seq, int nseq, int b)
+{
+    if (!m || !path || nseq < 0 || (nseq > 0 && !seq) || b < 0 || b >= m->c.batch) return K3D_EINVAL;
+    const K3dStackCfg *c = &m->c;
+    const K3dMlaShape *ms = &c->mla;
+    const int kvw = ms->kv_lora + ms->qk_rope, H = ms->n_heads, kvd = ms->qk_nope + ms->v_head;
+    const int64_t kper = state_kper(c);
+    int pos = 0, r = k3d_sync();
+    if (!r) r = k3d_download(&pos, m->pos, sizeof pos);
+    if (r) return r;
+    if (pos < 0 || pos > c->ctx_cap) return K3D_EBOUND;
+    K3StHeader hd;
+    memset(&hd, 0, sizeof hd);
+    memcpy(hd.magic, K3ST_MAGIC, 4);
+    hd.version = K3ST_VERSION;
+    state_fingerprint(c, hd.fp);
+    hd.n_bound = c->n_layers;
+    hd.n_mla = state_n_mla(m);
+    hd.cached = pos;
+    hd.nseq = nseq;
+    hd.kper = kper;
+    hd.kvpp = (int64_t)H * kvd;
+    hd.ropepp = ms->qk_rope;
+    FILE *f = fopen(path, "wb");
+    if (!f) return K3D_EINVAL;
+    const int CH = K3ST_CHUNK;
+    float *hbuf = (float *)malloc((size_t)(kper > (int64_t)CH * H * kvd ? kper : (int64_t)CH * H * kvd) * 4);
+    float *lat = hd.n_mla ? (float *)k3d_alloc((size_t)CH * ms->kv_lora * 4) : NULL;
+    float *kv = hd.n_mla ? (float *)k3d_alloc((size_t)CH * H * kvd * 4) : NULL;
+    uint16_t *rows = (uint16_t *)malloc((size_t)CH * kvw * 2);
+    if (!hbuf || !rows || (hd.n_mla && (!lat || !kv))) r = K3D_ENOMEM;
+    if (!r && fwrite(&hd, sizeof hd, 1, f) != 1) r = K3D_EINVAL;
+    if (!r && nseq && fwrite(seq, sizeof(int), (size_t)nseq, f) != (size_t)nseq) r = K3D_EINVAL;
+    for (int l = 0; l < c->n_layers && !r; l++) {
+        const K3sLayer *L = &m->L[l];
+        if (!L->is_mla && L->kda_state) {
+            r = k3d_download(hbuf, L->kda_state + (size_t)b * kper, (size_t)kper * 4);
+        } else {
+            memset(hbuf, 0, (size_t)kper * 4);
+        }
+        if (!r && fwrite(hbuf, 4, (size_t)kper, f) != (size_t)kper) r = K3D_EINVAL;
+    }
+    /* expanded keys and values, position-major per MLA layer */
+    for (int l = 0; l < c->n_layers && !r; l++) {
+        const K3sLayer *L = &m->L[l];
+        if (!L->is_mla) continue;
+        const uint16_t *cb = L->cache + (size_t)b * c->ctx_cap * kvw;
+        for (int p0 = 0; p0 < pos && !r; p0 += CH) {
+            const int n = pos - p0 < CH ? pos - p0 : CH;
+            r = k3d_bf16_rows_to_f32(lat, cb + (size_t)p0 * kvw, (size_t)kvw, n, ms->kv_lora);
+            if (!r) r = k3d_gemv_bf16(kv, lat, L->mla.kv_b, ms->kv_lora, H * kvd, n, 0);
+            if (!r) r = k3d_download(hbuf, kv, (size_t)n * H * kvd * 4);
+            if (!r && fwrite(hbuf, 4, (size_t)n * H * kvd, f) != (size_t)n * H * kvd) r = K3D_EINVAL;
+        }
+    }
+    /* rope slots */
+    for (int l = 0; l < c->n_layers && !r; l++) {
+        const K3sLayer *L = &m->L[l];
+        if (!L->is_mla) continue;
+        const uint16_t *cb = L->cache + (size_t)b * c->ctx_cap * kvw;
+        for (int p0 = 0; p0 < pos && !r; p0 += CH) {
+            const int n = pos - p0 < CH ? pos - p0 : CH;
+            r = k3d_bf16_rows_to_f32(lat, cb + (size_t)p0 * kvw + ms->kv_lora, (size_t)kvw, n, ms->qk_rope);
+            if (!r) r = k3d_download(hbuf, lat, (size_t)n * ms->qk_rope * 4);
+            if (!r && fwrite(hbuf, 4, (size_t)n * ms->qk_rope, f) != (size_t)n * ms->qk_rope) r = K3D_EINVAL;
+        }
+    }
+    /* the trailer: the device cache rows themselves */
+    if (!r && hd.n_mla) {
+        K3LtTrailer tr;
+        memcpy(tr.magic, K3LT_MAGIC, 4);
+        tr.version = 1;
+        tr.n_mla = hd.n_mla;
+        tr.cached = pos;
+        tr.kvw = kvw;
+        if (fwrite(&tr, sizeof tr, 1, f) != 1) r = K3D_EINVAL;
+        for (int l = 0; l < c->n_layers && !r; l++) {
+            const K3sLayer *L = &m->L[l];
+            if (!L->is_mla) continue;
+            const uint16_t *cb = L->cache + (size_t)b * c->ctx_cap * kvw;
+            for (int p0 = 0; p0 < pos && !r; p0 += CH) {
+                const int n = pos - p0 < CH ? pos - p0 : CH;
+                r = k3d_download(rows, cb + (size_t)p0 * kvw, (size_t)n * kvw * 2);
+                if (!r && fwrite(rows, 2, (size_t)n * kvw, f) != (size_t)n * kvw) r = K3D_EINVAL;
+            }
+        }
+    }
+    if (fclose(f) != 0 && !r) r = K3D_EINVAL;
+    free(hbuf);
+    free(rows);
+    k3d_free(lat);
+    k3d_free(kv);
+    return r;
+}
+
+/* The latent of every cached position of one MLA layer from its expanded keys and values
+ * at file offset `off` (cached x H*kvd floats), written into the device cache rows. */
+static int load_latent_lsq(K3dModel *m, const K3sLayer *L, uint16_t *cb, FILE *f, long off, int cached)
+{
+    const K3dMlaShape *ms = &m->c.mla;
+    const int kvw = ms->kv_lora + ms->qk_rope, R = ms->n_heads * (ms->qk_nope + ms->v_head);
+    const int n_l = ms->kv_lora, CH = K3ST_CHUNK;
+    int r = 0;
+    uint16_t *kvbT = (uint16_t *)k3d_alloc((size_t)n_l * R * 2);
+    float *xt = (float *)k3d_alloc((size_t)(n_l > CH ? n_l : CH) * R * 4);   /* kv_b^T widened; later kv rows */
+    float *rhs = (float *)k3d_alloc((size_t)(n_l > CH ? n_l : CH) * n_l * 4);
+    double *G = (double *)malloc((size_t)n_l * n_l * sizeof(double));
+    float *hb = (float *)malloc((size_t)(n_l > CH ? n_l : CH) * (R > n_l ? R : n_l) * 4);
+    double *tmp = (double *)malloc((size_t)n_l * sizeof(double));
+    if (!kvbT || !xt || !rhs || !G || !hb || !tmp) r = K3D_ENOMEM;
+    /* Gram matrix kv_b^T kv_b: kv_b^T as the weight matrix, its own rows as the tokens */
+    if (!r) r = k3d_transpose_u16(kvbT, L->mla.kv_b, R, n_l);
+    if (!r) r = k3d_bf16_rows_to_f32(xt, kvbT, (size_t)R, n_l, R);
+    if (!r) r = k3d_gemv_bf16(rhs, xt, kvbT, R, n_l, n_l, 0);
+    if (!r) r = k3d_download(hb, rhs, (size_t)n_l * n_l * 4);
+    if (!r) {
+        for (size_t i = 0; i < (size_t)n_l * n_l; i++) G[i] = hb[i];
+        if (cholesky(G, n_l)) r = K3D_EINVAL;                   /* kv_b without full rank */
+    }
+    if (!r && fseek(f, off, SEEK_SET) != 0) r = K3D_EINVAL;
+    for (int p0 = 0; p0 < cached && !r; p0 += CH) {
+        const int n = cached - p0 < CH ? cached - p0 : CH;
+        if (fread(hb, 4, (size_t)n * R, f) != (size_t)n * R) { r = K3D_EINVAL; break; }
+        r = k3d_upload(xt, hb, (size_t)n * R * 4);
+        if (!r) r = k3d_gemv_bf16(rhs, xt, kvbT, R, n_l, n, 0);
+        if (!r) r = k3d_download(hb, rhs, (size_t)n * n_l * 4);
+        if (r) break;
+        for (int p = 0; p < n; p++) chol_solve(G, n_l, hb + (size_t)p * n_l, hb + (size_t)p * n_l, tmp);
+        r = k3d_upload(rhs, hb, (size_t)n * n_l * 4);
+        if (!r) r = k3d_f32_rows_to_bf16(cb + (size_t)p0 * kvw, (size_t)kvw, rhs, n, n_l);
+    }
+    if (!r) r = k3d_sync();
+    k3d_free(kvbT);
+    k3d_free(xt);
+    k3d_free(rhs);
+    free(G);
+    free(hb);
+    free(tmp);
+    return r;
+}
+
+int k3d_model_state_load(K3dModel *m, const char *path, int *seq, int seq_cap, int b)
+{
+    if (!m || !path || b < 0 || b >= m->c.batch) return K3D_EINVAL;
+    const K3dStackCfg *c = &m->c;
+    const K3dMlaShape *ms = &c->mla;
+    const int kvw = ms->kv_lora + ms->qk_rope, H = ms->n_heads, kvd = ms->qk_nope + ms->v_head;
+    FILE *f = fopen(path, "rb");
+    if (!f) return K3D_EINVAL;
+    K3StHeader hd;
+    int32_t fp[12];
+    state_fingerprint(c, fp);
+    int r = read_header(f, &hd);
+    /* a file from another architecture would decode fluent, wrong text: refused, as the
+     * CPU engine refuses it (k3_run.c:226-240) */
+    if (!r && (memcmp(fp, hd.fp, sizeof fp) != 0 || hd.n_bound != c->n_layers || hd.n_mla != state_n_mla(m) ||
+               hd.kper != state_kper(c) || hd.kvpp != (int64_t)H * kvd || hd.ropepp != ms->qk_rope))
+        r = K3D_EINVAL;
+    if (!r && (hd.cached < 0 || hd.cached > c->ctx_cap)) r = K3D_EBOUND;
+    if (!r && (hd.nseq < 0 || (hd.nseq > 0 && seq && hd.nseq > seq_cap))) r = K3D_EBOUND;
+    if (r) { fclose(f); return r; }
+    const int cached = hd.cached, CH = K3ST_CHUNK;
+    const int64_t kper = hd.kper;
+    const long after_seq = (long)sizeof hd + (long)hd.nseq * 4;
+    const long kv_off = after_seq + (long)(kper * hd.n_bound * 4);
+    const long rope_off = kv_off + (long)hd.n_mla * cached * (long)hd.kvpp * 4;
+    const long tail = rope_off + (long)hd.n_mla * cached * (long)hd.ropepp * 4;
+    if (seq && hd.nseq && fread(seq, sizeof(int), (size_t)hd.nseq, f) != (size_t)hd.nseq) r = K3D_EINVAL;
+    float *hbuf = (float *)malloc((size_t)kper * 4);
+    if (!hbuf) r = K3D_ENOMEM;
+    if (!r && fseek(f, after_seq, SEEK_SET) != 0) r = K3D_EINVAL;
+    for (int l = 0; l < c->n_layers && !r; l++) {
+        K3sLayer *L = &m->L[l];
+        if (fread(hbuf, 4, (size_t)kper, f) != (size_t)kper) { r = K3D_EINVAL; break; }
+        if (!L->is_mla && L->kda_state) r = k3d_upload(L->kda_state + (size_t)b * kper, hbuf, (size_t)kper * 4);
+    }
+    free(hbuf);
+    K3LtTrailer tr;
+    const int exact = !r && cached > 0 && hd.n_mla > 0 && fseek(f, tail, SEEK_SET) == 0 &&
+                      fread(&tr, 1, sizeof tr, f) == sizeof tr && memcmp(tr.magic, K3LT_MAGIC, 4) == 0 &&
+                      tr.version == 1 && tr.n_mla == hd.n_mla && tr.cached == cached && tr.kvw == kvw;
+    if (exact) {
+        /* the trailer holds the device rows themselves */
+        uint16_t *rows = (uint16_t *)malloc((size_t)CH * kvw * 2);
+        if (!rows) r = K3D_ENOMEM;
+        for (int l = 0; l < c->n_layers && !r; l++) {
+            K3sLayer *L = &m->L[l];
+            if (!L->is_mla) continue;
+            uint16_t *cb = L->cache + (size_t)b * c->ctx_cap * kvw;
+            for (int p0 = 0; p0 < cached && !r; p0 += CH) {
+                const int n = cached - p0 < CH ? cached - p0 : CH;
+                if (fread(rows, 2, (size_t)n * kvw, f) != (size_t)n * kvw) { r = K3D_EINVAL; break; }
+                r = k3d_upload(cb + (size_t)p0 * kvw, rows, (size_t)n * kvw * 2);
+            }
+        }
+        free(rows);
+    } else if (!r && cached > 0) {
+        int mi = 0;
+        float *hb = (float *)malloc((size_t)CH * ms->qk_rope * 4);
+        float *dv = (float *)k3d_alloc((size_t)CH * ms->qk_rope * 4);
+        if (!hb || !dv) r = K3D_ENOMEM;
+        for (int l = 0; l < c->n_layers && !r; l++) {
+            K3sLayer *L = &m->L[l];
+            if (!L->is_mla) continue;
+            uint16_t *cb = L->cache + (size_t)b * c->ctx_cap * kvw;
+            r = load_latent_lsq(m, L, cb, f, kv_off + (long)mi * cached * (long)hd.kvpp * 4, cached);
+            if (!r && fseek(f, rope_off + (long)mi * cached * (long)hd.ropepp * 4, SEEK_SET) != 0) r = K3D_EINVAL;
+            for (int p0 = 0; p0 < cached && !r; p0 += CH) {
+                const int n = cached - p0 < CH ? cached - p0 : CH;
+                if (fread(hb, 4, (size_t)n * ms->qk_rope, f) != (size_t)n * ms->qk_rope) { r = K3D_EINVAL; break; }
+                r = k3d_upload(dv, hb, (size_t)n * ms->qk_rope * 4);
+                if (!r) r = k3d_f32_rows_to_bf16(cb + (size_t)p0 * kvw + ms->kv_lora, (size_t)kvw, dv, n,
+                                                 ms->qk_rope);
+                if (!r) r = k3d_sync();
+            }
+            mi++;
+        }
+        free(hb);
+        k3d_free(dv);
+    }
+    fclose(f);
+    if (!r) {
+        int p[4] = {cached, cached, cached, cached};
+        r = k3d_upload(m->pos, p, sizeof p);
+    }
+    if (!r) r = k3d_sync();
+    return r;
 }

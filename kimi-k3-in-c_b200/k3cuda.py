@@ -100,6 +100,11 @@ class K3dKdaW(C.Structure):
                 ("dt_bias", vp), ("o_norm", vp)]
 
 
+class K3dStateInfo(C.Structure):
+    _fields_ = [("version", i32), ("n_bound", i32), ("n_mla", i32), ("cached", i32), ("nseq", i32),
+                ("has_latent", i32)]
+
+
 class K3dStackCfg(C.Structure):
     _fields_ = [("hidden", i32), ("vocab", i32), ("n_layers", i32), ("eps", f32),
                 ("kda_heads", i32), ("kda_head_dim", i32), ("conv_k", i32), ("gate_lb", f32),
@@ -217,6 +222,13 @@ _PROTOS = {
     "k3d_add_i32": (i32, [vp, i32, i32]),
     "k3d_kda_layer_ws_bytes": (sz, [C.POINTER(K3dKdaShape), i32]),
     "k3d_kda_state_floats": (sz, [C.POINTER(K3dKdaShape)]),
+    "k3d_set_kda_head_kernel": (i32, [i32]),
+    "k3d_state_peek": (i32, [C.c_char_p, C.POINTER(K3dStateInfo)]),
+    "k3d_model_state_save": (i32, [vp, C.c_char_p, vp, i32, i32]),
+    "k3d_model_state_load": (i32, [vp, C.c_char_p, vp, i32, i32]),
+    "k3d_bf16_rows_to_f32": (i32, [vp, vp, sz, i32, i32]),
+    "k3d_f32_rows_to_bf16": (i32, [vp, sz, vp, i32, i32]),
+    "k3d_transpose_u16": (i32, [vp, vp, i32, i32]),
     "k3d_kda_layer_decode": (i32, [vp, vp, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32, vp, vp, sz]),
     "k3d_kda_layer_decode_normed": (i32, [vp, vp, f32, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32,
                                           vp, vp, sz]),

@@ -6,8 +6,8 @@ every rank must hold the same result.
 run_stack: the reduced-width decode stack under expert parallelism (routed experts split
 by rank, shared expert split by intermediate rows, vocabulary-split LM head, the push
 combine per MoE layer; eager, graph capture, replay), then rank 0 alone steps the same
-seeded model on one GPU with the same tokens: logits within 1e-5 and the same greedy
-tokens."""
+seeded model on one GPU with the same tokens: logits (the ranks' vocabulary slices put
+together) within 1e-5 and the same greedy tokens."""
 import ctypes
 import datetime
 import os
@@ -75,12 +75,27 @@ def run_stack(rank, world, port, seed, batch):
             sc.moe.expert_lo, sc.moe.expert_hi, sc.moe.add_shared = lo, hi, add_shared
             return sc
 
-        def steps(model, toks):
+        V = c["vocab"]
+
+        def full_logits(raw, nr):
+            """Under expert parallelism each rank's logits buffer holds its vocabulary slice,
+            [batch][vshard] from the start; the slices of all ranks make the whole row."""
+            if nr == 1:
+                return raw.reshape(batch, V).copy()
+            allg = [torch.zeros(raw.size, dtype=torch.float32) for _ in range(nr)]
+            dist.all_gather(allg, torch.from_numpy(raw))
+            parts = []
+            for r in range(nr):
+                v0, v1 = r * V // nr, (r + 1) * V // nr
+                parts.append(allg[r].numpy()[:batch * (v1 - v0)].reshape(batch, v1 - v0))
+            return np.concatenate(parts, axis=1)
+
+        def steps(model, toks, nr):
             out, logs = [], []
             for step in range(3):            # eager, graph capture, replay
                 nxt = np.zeros(batch, np.int32)
                 k3cuda.check(lib.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
-                logs.append(download(lib, model, "logits", np.float32).reshape(batch, -1).copy())
+                logs.append(full_logits(download(lib, model, "logits", np.float32), nr))
                 out.append(nxt.copy())
                 toks = nxt.copy()
             return out, logs
@@ -90,7 +105,7 @@ def run_stack(rank, world, port, seed, batch):
         model = lib.k3d_model_create(ctypes.byref(model_cfg(lo, hi, 1 if rank == 0 else 0)), seed)
         assert model, lib.k3d_last_message()
         k3cuda.check(lib.k3d_model_fill_context(model, 6, 17))
-        toks_ep, logs_ep = steps(model, toks0)
+        toks_ep, logs_ep = steps(model, toks0, world)
         lib.k3d_model_destroy(model)           # releases the graph (it holds an NCCL call)
         k3cuda.check(lib.k3d_sync())
         for t in toks_ep:
@@ -103,7 +118,7 @@ def run_stack(rank, world, port, seed, batch):
             model = lib.k3d_model_create(ctypes.byref(model_cfg(0, E, 1)), seed)
             assert model, lib.k3d_last_message()
             k3cuda.check(lib.k3d_model_fill_context(model, 6, 17))
-            toks_1, logs_1 = steps(model, toks0)
+            toks_1, logs_1 = steps(model, toks0, 1)
             lib.k3d_model_destroy(model)
             for s in range(3):
                 a, b = logs_ep[s], logs_1[s]
