@@ -472,6 +472,39 @@ int       k3d_state_peek(const char *path, K3dStateInfo *info);
 int       k3d_model_state_save(K3dModel *m, const char *path, const int *seq, int nseq, int b);
 int       k3d_model_state_load(K3dModel *m, const char *path, int *seq, int seq_cap, int b);
 
+/* Released-checkpoint loading (the device counterpart of src/io/k3_st.c, the names and
+ * element-count checks of src/model/k3_bind.c:167-241 and the expert checks of
+ * src/io/k3_load.c:46-103). k3d_ckpt_open indexes every *.safetensors file of dir (shards
+ * in file-name order) and validates every header entry (known dtype, span = elements x
+ * element size, inside the file); lookups are O(1). Host only: none of the k3d_ckpt_*
+ * calls touches the GPU. k3d_ckpt_error gives the reason of the last failure. */
+typedef struct K3dCkpt K3dCkpt;
+enum { K3D_DT_U8 = 1, K3D_DT_BF16 = 2, K3D_DT_F16 = 3, K3D_DT_F32 = 4 };
+typedef struct {
+    int     shard, dtype, ndim;
+    int64_t shape[4];
+    int64_t off, nbytes;          /* absolute byte offset within the shard file, size */
+} K3dCkptTensor;
+K3dCkpt    *k3d_ckpt_open(const char *dir);
+void        k3d_ckpt_close(K3dCkpt *ck);
+int         k3d_ckpt_count(const K3dCkpt *ck);
+int         k3d_ckpt_find(const K3dCkpt *ck, const char *name, K3dCkptTensor *out);  /* K3D_EINVAL if absent */
+int64_t     k3d_ckpt_read(const K3dCkpt *ck, int shard, int64_t off, int64_t nbytes, void *buf);
+int         k3d_ckpt_elem_size(int dtype);
+const char *k3d_ckpt_error(void);
+/* Binds the checkpoint's tensors (the released names: language_model.model.layers.L.
+ * self_attn.*, block_sparse_moe.gate / experts.E.w{1,2,3}.weight_{packed,scale} /
+ * shared_experts.*, mlp.* for dense layers, embed_tokens, norm, language_model.lm_head)
+ * to the model's weights and uploads them, replacing the random initialisation. Every
+ * tensor is checked before a byte is read: present, the expected element count for the
+ * model's configuration, bf16 for matrices (fp32 / bf16 / f16 for vectors, widened),
+ * U8 MXFP4 experts with one E8M0 scale per 32 elements and all six tensors in one shard.
+ * An expert whose six tensors form one contiguous run is read with one read. Under expert
+ * parallelism only this rank's experts, LM-head rows and shared-expert slice are read.
+ * Returns K3D_EINVAL (reason in k3d_ckpt_error) without uploading anything when a check
+ * fails. Caches and states are left as they are. */
+int         k3d_model_load_checkpoint(K3dModel *m, const K3dCkpt *ck);
+
 #ifdef __cplusplus
 }
 #endif

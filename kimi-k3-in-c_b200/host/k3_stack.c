@@ -14,6 +14,7 @@
  * the per-rank MoE partials with one NCCL all-reduce per MoE layer.
  */
 #include <math.h>
+#include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -73,6 +74,7 @@ struct K3dModel {
     K3sTensor t[K3S_MAX_TENSORS];
     int nt;
     unsigned char *stage_expert;   /* creation only: checkpoint-layout expert before tiling */
+    int sh_lo, sh_full;            /* this rank's first shared-expert row, and the full count */
 };
 
 static int is_mla_layer(const K3dStackCfg *c, int l)
@@ -99,6 +101,24 @@ static void *dalloc(K3dModel *m, const char *name, size_t bytes)
     return reg(m, name, p, bytes);
 }
 
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+/* One expert's six tensors in the checkpoint layout (gate codes, gate scales, up codes, up
+ * scales, down codes, down scales, each 256-byte aligned; per = the expert's bytes), and the
+ * offsets of the tiled layout ([gate/up codes][gate/up scales][down codes][down scales]),
+ * which fits in the same per. */
+static void expert_layout(const K3dMoeShape *s, int E, size_t sz[6], size_t off[6], size_t *per,
+                          size_t toff[4])
+{
+    const size_t gu = (size_t)s->inter * E / 2, gus = (size_t)s->inter * E / 32;
+    const size_t z[6] = {gu, gus, gu, gus, gu, gus};
+    *per = 0;
+    for (int i = 0; i < 6; i++) { sz[i] = z[i]; off[i] = *per; *per += align256(z[i]); }
+    const size_t tsz[4] = {2 * gu, 2 * gus, gu, gus};
+    size_t tper = 0;
+    for (int i = 0; i < 4; i++) { toff[i] = tper; tper += align256(tsz[i]); }
+}
+
 static uint64_t next_seed(K3dModel *m) { return m->seed * 1000003ull + (++m->counter) * 7919ull; }
 
 static uint16_t *bf16_param(K3dModel *m, const char *name, size_t n, float sd, int *err)
@@ -123,7 +143,6 @@ static float *f32_normal(K3dModel *m, const char *name, size_t n, float sd, int 
     return p;
 }
 
-static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
 {
@@ -150,6 +169,8 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             sh_lo = r * (sh_full / nr);
         }
     }
+    m->sh_lo = sh_lo;
+    m->sh_full = sh_full;
     const K3dStackCfg *c = &m->c;
     const int E = c->hidden, B = c->batch;
     const size_t P = (size_t)c->kda_heads * c->kda_head_dim;
@@ -240,14 +261,8 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             L->dd = bf16_param(m, nm, (size_t)E * c->dense_inter, 0.02f, &err);
         } else {
             const K3dMoeShape *s = &c->moe;
-            const size_t gu = (size_t)s->inter * E / 2, gus = (size_t)s->inter * E / 32;
-            const size_t sz[6] = {gu, gus, gu, gus, gu, gus};
-            size_t off[6], per = 0;
-            for (int i = 0; i < 6; i++) { off[i] = per; per += align256(sz[i]); }
-            /* tiled layout: [gate/up codes][gate/up scales][down codes][down scales] */
-            const size_t tsz[4] = {2 * gu, 2 * gus, gu, gus};
-            size_t toff[4], tper = 0;
-            for (int i = 0; i < 4; i++) { toff[i] = tper; tper += align256(tsz[i]); }
+            size_t sz[6], off[6], per, toff[4];
+            expert_layout(s, E, sz, off, &per, toff);
             const int tiled = s->expert_layout == 1;
             const int nloc = s->expert_hi - s->expert_lo;
             snprintf(nm, sizeof nm, "layer%d.moe.pool", l);
@@ -886,5 +901,341 @@ int k3d_model_state_load(K3dModel *m, const char *path, int *seq, int seq_cap, i
         r = k3d_upload(m->pos, p, sizeof p);
     }
     if (!r) r = k3d_sync();
+    return r;
+}
+
+/* --------------------------------------------------------- checkpoint binding ----
+ * The released checkpoint's names (src/model/k3_bind.c:167-241, src/io/k3_load.c:11)
+ * bound to this stack's weights. All requests are resolved and checked first; only then is
+ * anything read, so a checkpoint that does not fit the configuration leaves the model as
+ * it was. */
+void k3h_ckpt_fail(const char *fmt, ...);
+
+#define CK_PRE "language_model.model."
+enum { CK_MAT = 1, CK_VEC, CK_ROUTER, CK_SH_DOWN };
+
+typedef struct {
+    char name[160];
+    int kind;
+    void *dst;
+    int64_t want, take, row0, rows, cols;   /* CK_MAT: rows [row0, row0 + rows) of cols; CK_SH_DOWN: columns */
+    K3dCkptTensor t;
+} CkReq;
+
+typedef struct {
+    CkReq *r;
+    int n, cap, bad;
+    const K3dCkpt *ck;
+} CkPlan;
+
+static CkReq *ck_add(CkPlan *p, int kind, void *dst, int64_t want, const char *fmt, ...)
+{
+    if (p->n == p->cap) {
+        const int nc = p->cap ? 2 * p->cap : 256;
+        CkReq *r = (CkReq *)realloc(p->r, (size_t)nc * sizeof(CkReq));
+        if (!r) { p->bad++; return NULL; }
+        p->r = r;
+        p->cap = nc;
+    }
+    CkReq *q = &p->r[p->n];
+    memset(q, 0, sizeof *q);
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(q->name, sizeof q->name, fmt, ap);
+    va_end(ap);
+    q->kind = kind;
+    q->dst = dst;
+    q->want = want;
+    q->take = want;
+    if (k3d_ckpt_find(p->ck, q->name, &q->t)) {
+        if (!p->bad) k3h_ckpt_fail("missing tensor %s", q->name);
+        p->bad++;
+        return NULL;
+    }
+    int64_t numel = 1;
+    for (int i = 0; i < q->t.ndim; i++) numel *= q->t.shape[i];
+    const int dt = q->t.dtype;
+    const char *why = NULL;
+    if (want >= 0 && numel != want) why = "element count";
+    else if ((kind == CK_MAT || kind == CK_SH_DOWN) && dt != K3D_DT_BF16) why = "dtype (matrices must be BF16)";
+    else if (kind == CK_VEC && dt != K3D_DT_F32 && dt != K3D_DT_BF16 && dt != K3D_DT_F16) why = "dtype";
+    else if (kind == CK_ROUTER && dt != K3D_DT_F32 && dt != K3D_DT_BF16) why = "dtype";
+    if (why) {
+        if (!p->bad)
+            k3h_ckpt_fail("%s: %s does not fit the model (%lld elements, dtype %d; expected %lld)", q->name, why,
+                          (long long)numel, dt, (long long)want);
+        p->bad++;
+        return NULL;
+    }
+    p->n++;
+    return q;
+}
+
+static float half_to_f32(uint16_t h)
+{
+    const uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 31u, m = h & 1023u;
+    uint32_t u;
+    if (e == 31) u = s | 0x7f800000u | (m << 13);
+    else if (e) u = s | ((e + 112u) << 23) | (m << 13);
+    else if (!m) u = s;
+    else {                                   /* subnormal: normalise */
+        int k = 0;
+        uint32_t mm = m;
+        while (!(mm & 1024u)) { mm <<= 1; k++; }
+        u = s | ((uint32_t)(113 - k) << 23) | ((mm & 1023u) << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+#define CK_HOST (64u << 20)
+
+static int ck_copy_bytes(const K3dCkpt *ck, const K3dCkptTensor *t, int64_t off, int64_t bytes, void *dst,
+                         unsigned char *hb, const char *name)
+{
+    for (int64_t d = 0; d < bytes;) {
+        const int64_t n = bytes - d < (int64_t)CK_HOST ? bytes - d : (int64_t)CK_HOST;
+        if (k3d_ckpt_read(ck, t->shard, t->off + off + d, n, hb) != n) {
+            k3h_ckpt_fail("short read of %s", name);
+            return K3D_EINVAL;
+        }
+        const int r = k3d_upload((char *)dst + d, hb, (size_t)n);
+        if (r) return r;
+        d += n;
+    }
+    return K3D_OK;
+}
+
+static int ck_load_req(const K3dCkpt *ck, const CkReq *q, unsigned char *hb)
+{
+    const int es = k3d_ckpt_elem_size(q->t.dtype);
+    if (q->kind == CK_MAT) {
+        if (q->rows) return ck_copy_bytes(ck, &q->t, q->row0 * q->cols * 2, q->rows * q->cols * 2, q->dst, hb, q->name);
+        return ck_copy_bytes(ck, &q->t, 0, q->t.nbytes, q->dst, hb, q->name);
+    }
+    if (q->kind == CK_SH_DOWN) {
+        /* columns [row0, row0 + cols) of each of the `rows` rows of a [rows][take] matrix */
+        const int64_t rowb = q->cols * 2;
+        unsigned char *out = hb;
+        if (q->rows * rowb > (int64_t)CK_HOST) { k3h_ckpt_fail("%s too large", q->name); return K3D_EINVAL; }
+        for (int64_t r = 0; r < q->rows; r++)
+            if (k3d_ckpt_read(ck, q->t.shard, q->t.off + (r * q->take + q->row0) * 2, rowb, out + r * rowb) != rowb) {
+                k3h_ckpt_fail("short read of %s", q->name);
+                return K3D_EINVAL;
+            }
+        return k3d_upload(q->dst, out, (size_t)(q->rows * rowb));
+    }
+    /* vectors widened to fp32 (a prefix of `take` elements), the router as bf16 */
+    const int64_t n = q->kind == CK_VEC ? q->take : q->want;
+    if (n * 4 > (int64_t)CK_HOST || n * es > (int64_t)CK_HOST / 2) {
+        k3h_ckpt_fail("%s too large", q->name);
+        return K3D_EINVAL;
+    }
+    unsigned char *raw = hb + CK_HOST / 2;
+    if (k3d_ckpt_read(ck, q->t.shard, q->t.off, n * es, raw) != n * es) {
+        k3h_ckpt_fail("short read of %s", q->name);
+        return K3D_EINVAL;
+    }
+    if (q->kind == CK_ROUTER) {
+        if (q->t.dtype == K3D_DT_BF16) return k3d_upload(q->dst, raw, (size_t)n * 2);
+        uint16_t *o = (uint16_t *)hb;
+        for (int64_t i = 0; i < n; i++) {
+            uint32_t u;
+            memcpy(&u, raw + 4 * i, 4);
+            if (u & 0xffffu) {
+                k3h_ckpt_fail("%s: fp32 router weights that bf16 does not hold exactly", q->name);
+                return K3D_EINVAL;
+            }
+            o[i] = (uint16_t)(u >> 16);
+        }
+        return k3d_upload(q->dst, o, (size_t)n * 2);
+    }
+    float *o = (float *)hb;
+    for (int64_t i = 0; i < n; i++) {
+        if (q->t.dtype == K3D_DT_F32) memcpy(&o[i], raw + 4 * i, 4);
+        else {
+            uint16_t h;
+            memcpy(&h, raw + 2 * i, 2);
+            if (q->t.dtype == K3D_DT_BF16) {
+                const uint32_t u = (uint32_t)h << 16;
+                memcpy(&o[i], &u, 4);
+            } else {
+                o[i] = half_to_f32(h);
+            }
+        }
+    }
+    return k3d_upload(q->dst, o, (size_t)n * 4);
+}
+
+typedef struct {
+    int layer, e;
+    K3dCkptTensor t[6];                      /* w1 packed, w1 scale, w3 packed, w3 scale, w2 packed, w2 scale */
+} CkExpert;
+
+int k3d_model_load_checkpoint(K3dModel *m, const K3dCkpt *ck)
+{
+    if (!m || !ck) return K3D_EINVAL;
+    const K3dStackCfg *c = &m->c;
+    const int64_t E = c->hidden, P = (int64_t)c->kda_heads * c->kda_head_dim, D = c->kda_head_dim;
+    CkPlan p = {NULL, 0, 0, 0, ck};
+    CkReq *q;
+    q = ck_add(&p, CK_MAT, m->embed, (int64_t)c->vocab * E, CK_PRE "embed_tokens.weight");
+    q = ck_add(&p, CK_VEC, m->final_norm, E, CK_PRE "norm.weight");
+    q = ck_add(&p, CK_MAT, m->lm_head, (int64_t)c->vocab * E, "language_model.lm_head.weight");
+    if (q) { q->row0 = m->v0; q->rows = m->vshard; q->cols = E; }
+    CkExpert *ex = NULL;
+    int nex = 0, capex = 0;
+    for (int l = 0; l < c->n_layers; l++) {
+        K3sLayer *L = &m->L[l];
+        ck_add(&p, CK_VEC, L->in_norm, E, CK_PRE "layers.%d.input_layernorm.weight", l);
+        ck_add(&p, CK_VEC, L->post_norm, E, CK_PRE "layers.%d.post_attention_layernorm.weight", l);
+        if (L->is_mla) {
+            const K3dMlaShape *s = &c->mla;
+            const int64_t qh = s->qk_nope + s->qk_rope, kvw = s->kv_lora + s->qk_rope;
+            ck_add(&p, CK_MAT, (void *)L->mla.q_a, (int64_t)s->q_lora * E, CK_PRE "layers.%d.self_attn.q_a_proj.weight", l);
+            ck_add(&p, CK_VEC, (void *)L->mla.q_a_norm, s->q_lora, CK_PRE "layers.%d.self_attn.q_a_layernorm.weight", l);
+            ck_add(&p, CK_MAT, (void *)L->mla.q_b, (int64_t)s->n_heads * qh * s->q_lora, CK_PRE "layers.%d.self_attn.q_b_proj.weight", l);
+            ck_add(&p, CK_MAT, (void *)L->mla.kv_a, kvw * E, CK_PRE "layers.%d.self_attn.kv_a_proj_with_mqa.weight", l);
+            ck_add(&p, CK_VEC, (void *)L->mla.kv_a_norm, s->kv_lora, CK_PRE "layers.%d.self_attn.kv_a_layernorm.weight", l);
+            ck_add(&p, CK_MAT, (void *)L->mla.kv_b, (int64_t)s->n_heads * (s->qk_nope + s->v_head) * s->kv_lora,
+                   CK_PRE "layers.%d.self_attn.kv_b_proj.weight", l);
+            ck_add(&p, CK_MAT, (void *)L->mla.o, E * s->n_heads * s->v_head, CK_PRE "layers.%d.self_attn.o_proj.weight", l);
+            if (s->out_gate)
+                ck_add(&p, CK_MAT, (void *)L->mla.g, (int64_t)s->n_heads * s->v_head * E, CK_PRE "layers.%d.self_attn.g_proj.weight", l);
+        } else {
+            const char *mats[4] = {"q", "k", "v", "g"};
+            const uint16_t *dm[4] = {L->kda.q, L->kda.k, L->kda.v, L->kda.g};
+            for (int i = 0; i < 4; i++)
+                ck_add(&p, CK_MAT, (void *)dm[i], P * E, CK_PRE "layers.%d.self_attn.%s_proj.weight", l, mats[i]);
+            ck_add(&p, CK_MAT, (void *)L->kda.o, E * P, CK_PRE "layers.%d.self_attn.o_proj.weight", l);
+            const char *cv[3] = {"q", "k", "v"};
+            const float *dc[3] = {L->kda.q_conv, L->kda.k_conv, L->kda.v_conv};
+            for (int i = 0; i < 3; i++)
+                ck_add(&p, CK_VEC, (void *)dc[i], P * c->conv_k, CK_PRE "layers.%d.self_attn.%s_conv1d.weight", l, cv[i]);
+            ck_add(&p, CK_MAT, (void *)L->kda.f_a, D * E, CK_PRE "layers.%d.self_attn.f_a_proj.weight", l);
+            ck_add(&p, CK_MAT, (void *)L->kda.f_b, P * D, CK_PRE "layers.%d.self_attn.f_b_proj.weight", l);
+            ck_add(&p, CK_MAT, (void *)L->kda.b, (int64_t)c->kda_heads * E, CK_PRE "layers.%d.self_attn.b_proj.weight", l);
+            /* per head: the checkpoint ships head_dim values, the first kda_heads are the heads'
+             * (k3_bind.c:218-222) */
+            q = ck_add(&p, CK_VEC, (void *)L->kda.A_log, D, CK_PRE "layers.%d.self_attn.A_log", l);
+            if (q) {
+                q->take = c->kda_heads;
+                if (q->take > q->want) { k3h_ckpt_fail("%s: fewer values than heads", q->name); p.bad++; }
+            }
+            ck_add(&p, CK_VEC, (void *)L->kda.dt_bias, P, CK_PRE "layers.%d.self_attn.dt_bias", l);
+            ck_add(&p, CK_VEC, (void *)L->kda.o_norm, D, CK_PRE "layers.%d.self_attn.o_norm.weight", l);
+        }
+        if (L->is_dense) {
+            ck_add(&p, CK_MAT, L->dg, (int64_t)c->dense_inter * E, CK_PRE "layers.%d.mlp.gate_proj.weight", l);
+            ck_add(&p, CK_MAT, L->du, (int64_t)c->dense_inter * E, CK_PRE "layers.%d.mlp.up_proj.weight", l);
+            ck_add(&p, CK_MAT, L->dd, E * c->dense_inter, CK_PRE "layers.%d.mlp.down_proj.weight", l);
+            continue;
+        }
+        const K3dMoeShape *s = &c->moe;
+        ck_add(&p, CK_ROUTER, (void *)L->moe.router_w, (int64_t)s->n_experts * E, CK_PRE "layers.%d.block_sparse_moe.gate.weight", l);
+        ck_add(&p, CK_VEC, (void *)L->moe.router_bias, s->n_experts,
+               CK_PRE "layers.%d.block_sparse_moe.gate.e_score_correction_bias", l);
+        if (s->shared_inter > 0) {
+            const int64_t SI = m->sh_full, SIl = s->shared_inter;
+            const char *gu[2] = {"gate", "up"};
+            const uint16_t *dg[2] = {L->moe.sh_gate, L->moe.sh_up};
+            for (int i = 0; i < 2; i++) {
+                q = ck_add(&p, CK_MAT, (void *)dg[i], SI * E, CK_PRE "layers.%d.block_sparse_moe.shared_experts.%s_proj.weight", l, gu[i]);
+                if (q) { q->row0 = m->sh_lo; q->rows = SIl; q->cols = E; }
+            }
+            q = ck_add(&p, CK_SH_DOWN, (void *)L->moe.sh_down, E * SI, CK_PRE "layers.%d.block_sparse_moe.shared_experts.down_proj.weight", l);
+            if (q) { q->row0 = m->sh_lo; q->rows = E; q->cols = SIl; q->take = SI; }
+        }
+        /* routed experts: the six U8 tensors, shapes from the configuration, one E8M0 scale
+         * per 32 elements, one shard (k3_load.c:16-66) */
+        for (int e = s->expert_lo; e < s->expert_hi && !p.bad; e++) {
+            if (nex == capex) {
+                capex = capex ? 2 * capex : 512;
+                CkExpert *x2 = (CkExpert *)realloc(ex, (size_t)capex * sizeof(CkExpert));
+                if (!x2) { p.bad++; break; }
+                ex = x2;
+            }
+            CkExpert *x = &ex[nex];
+            x->layer = l;
+            x->e = e;
+            const char *wn[3] = {"w1", "w3", "w2"};
+            const int64_t rows[3] = {s->inter, s->inter, E}, in[3] = {E, E, s->inter};
+            for (int i = 0; i < 3 && !p.bad; i++) {
+                char nm[192];
+                for (int k = 0; k < 2; k++) {
+                    snprintf(nm, sizeof nm, CK_PRE "layers.%d.block_sparse_moe.experts.%d.%s.%s", l, e, wn[i],
+                             k ? "weight_scale" : "weight_packed");
+                    K3dCkptTensor *t = &x->t[2 * i + k];
+                    if (k3d_ckpt_find(ck, nm, t)) { k3h_ckpt_fail("missing tensor %s", nm); p.bad++; break; }
+                    const int64_t cols = k ? in[i] / 32 : in[i] / 2;
+                    if (t->dtype != K3D_DT_U8 || t->ndim != 2 || t->shape[0] != rows[i] || t->shape[1] != cols) {
+                        k3h_ckpt_fail("%s: expected U8 [%lld][%lld] (one scale per 32 elements)", nm,
+                                      (long long)rows[i], (long long)cols);
+                        p.bad++;
+                        break;
+                    }
+                    if (t->shard != x->t[0].shard) {
+                        k3h_ckpt_fail("layer %d expert %d spans shards", l, e);
+                        p.bad++;
+                        break;
+                    }
+                }
+            }
+            nex++;
+        }
+    }
+    int r = p.bad ? K3D_EINVAL : K3D_OK;
+    unsigned char *hb = r ? NULL : (unsigned char *)malloc(CK_HOST);
+    if (!r && !hb) r = K3D_ENOMEM;
+    for (int i = 0; i < p.n && !r; i++) r = ck_load_req(ck, &p.r[i], hb);
+    /* experts: one read when the six tensors tile one run, else six; staged in the
+     * checkpoint layout, then tiled where the model keeps tiled experts */
+    size_t sz[6], off[6], per, toff[4];
+    expert_layout(&c->moe, (int)E, sz, off, &per, toff);
+    unsigned char *stage = (!r && nex) ? (unsigned char *)k3d_alloc(per) : NULL;
+    unsigned char *hx = (!r && nex) ? (unsigned char *)malloc(per + 6 * 256) : NULL;
+    if (!r && nex && (!stage || !hx)) r = K3D_ENOMEM;
+    for (int i = 0; i < nex && !r; i++) {
+        const CkExpert *x = &ex[i];
+        const K3sLayer *L = &m->L[x->layer];
+        const K3dMoeShape *s = &c->moe;
+        int64_t lo = x->t[0].off, hi = 0, own = 0;
+        for (int k = 0; k < 6; k++) {
+            if (x->t[k].off < lo) lo = x->t[k].off;
+            if (x->t[k].off + x->t[k].nbytes > hi) hi = x->t[k].off + x->t[k].nbytes;
+            own += x->t[k].nbytes;
+        }
+        if (hi - lo == own && own <= (int64_t)per) {
+            if (k3d_ckpt_read(ck, x->t[0].shard, lo, own, hx) != own) r = K3D_EINVAL;
+            for (int k = 0; k < 6 && !r; k++)
+                r = k3d_upload(stage + off[k], hx + (x->t[k].off - lo), (size_t)x->t[k].nbytes);
+        } else {
+            for (int k = 0; k < 6 && !r; k++) {
+                if (k3d_ckpt_read(ck, x->t[k].shard, x->t[k].off, x->t[k].nbytes, hx) != x->t[k].nbytes) r = K3D_EINVAL;
+                if (!r) r = k3d_upload(stage + off[k], hx, (size_t)x->t[k].nbytes);
+            }
+        }
+        if (r) { if (r == K3D_EINVAL) k3h_ckpt_fail("short read of layer %d expert %d", x->layer, x->e); break; }
+        unsigned char *base = L->pool + (size_t)(x->e - s->expert_lo) * per;
+        if (s->expert_layout == 1) {
+            K3ExpertQ src, dst;
+            src.p1 = stage + off[0]; src.s1 = stage + off[1];
+            src.p3 = stage + off[2]; src.s3 = stage + off[3];
+            src.p2 = stage + off[4]; src.s2 = stage + off[5];
+            dst.p1 = base + toff[0]; dst.s1 = base + toff[1];
+            dst.p3 = NULL; dst.s3 = NULL;
+            dst.p2 = base + toff[2]; dst.s2 = base + toff[3];
+            r = k3d_expert_pretile(&dst, &src, (int)E, s->inter);
+        } else {
+            r = k3d_copy(base, stage, per);
+        }
+        if (!r) r = k3d_sync();
+    }
+    k3d_free(stage);
+    free(hx);
+    free(hb);
+    free(ex);
+    free(p.r);
     return r;
 }

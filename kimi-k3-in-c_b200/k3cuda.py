@@ -105,6 +105,11 @@ class K3dStateInfo(C.Structure):
                 ("has_latent", i32)]
 
 
+class K3dCkptTensor(C.Structure):
+    _fields_ = [("shard", i32), ("dtype", i32), ("ndim", i32), ("shape", C.c_int64 * 4),
+                ("off", C.c_int64), ("nbytes", C.c_int64)]
+
+
 class K3dStackCfg(C.Structure):
     _fields_ = [("hidden", i32), ("vocab", i32), ("n_layers", i32), ("eps", f32),
                 ("kda_heads", i32), ("kda_head_dim", i32), ("conv_k", i32), ("gate_lb", f32),
@@ -224,6 +229,14 @@ _PROTOS = {
     "k3d_kda_state_floats": (sz, [C.POINTER(K3dKdaShape)]),
     "k3d_set_kda_head_kernel": (i32, [i32]),
     "k3d_state_peek": (i32, [C.c_char_p, C.POINTER(K3dStateInfo)]),
+    "k3d_ckpt_open": (vp, [C.c_char_p]),
+    "k3d_ckpt_close": (None, [vp]),
+    "k3d_ckpt_count": (i32, [vp]),
+    "k3d_ckpt_find": (i32, [vp, C.c_char_p, C.POINTER(K3dCkptTensor)]),
+    "k3d_ckpt_read": (C.c_int64, [vp, i32, C.c_int64, C.c_int64, vp]),
+    "k3d_ckpt_elem_size": (i32, [i32]),
+    "k3d_ckpt_error": (C.c_char_p, []),
+    "k3d_model_load_checkpoint": (i32, [vp, vp]),
     "k3d_model_state_save": (i32, [vp, C.c_char_p, vp, i32, i32]),
     "k3d_model_state_load": (i32, [vp, C.c_char_p, vp, i32, i32]),
     "k3d_bf16_rows_to_f32": (i32, [vp, vp, sz, i32, i32]),
