@@ -163,12 +163,73 @@ __global__ void __launch_bounds__(256) k_mla_prep(float *ql, float *c, uint16_t 
     }
 }
 
-// grid (H, kv_lora / 128, B), block (16, 8): q_lat[j] = sum_i W_uk[h][i][j] q_nope[i] for a
-// 128-wide block of j, 8 j per thread (16-byte loads), the 8 thread rows splitting i;
-// then RoPE(q_rope_h). Output qa [B][H][kvw].
-__global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, const float2 *rope_tab,
-                             const int *pos_p, MlaDims d, int cap)
+// The latent half of k_mla_prep for one sequence, by 128 threads: RMSNorm of the latent
+// part of c (sum of squares in double), RoPE of the rope part at pos, the bf16 cache entry
+// at pos. Thread t owns latent elements t + 128 i.
+__device__ __forceinline__ void mla_latent_prep(float *c, uint16_t *cache, const float2 *rope_tab,
+                                                const float *kv_a_norm, const int *pos_p,
+                                                const MlaDims &d, int cap, int b, int tid)
 {
+    __shared__ double red[4];
+    __shared__ float crope[256];
+    const int pos = *pos_p;
+    const bool pos_ok = pos >= 0 && pos < cap;
+    if (!pos_ok) {
+        if (tid == 0) k3_raise(K3D_EBOUND, K3_SITE_MLA);
+        return;
+    }
+    float *cb = c + (size_t)b * d.kvw;
+    float cv[6], cw[6];
+#pragma unroll
+    for (int i = 0; i < 6; i++) {
+        const int k = tid + 128 * i;
+        cv[i] = k < d.kvw ? cb[k] : 0.f;
+        cw[i] = k < d.kv_lora ? kv_a_norm[k] : 0.f;
+    }
+    float2 rp = make_float2(1.f, 0.f);
+    if (d.theta > 0.f && tid < d.qr / 2) rp = rope_tab[(size_t)pos * (d.qr / 2) + tid];
+    double sl = 0.0;
+#pragma unroll
+    for (int i = 0; i < 6; i++)
+        if (tid + 128 * i < d.kv_lora) sl = fma((double)cv[i], (double)cv[i], sl);
+    sl = warp_sum_d(sl);
+    if ((tid & 31) == 0) red[tid >> 5] = sl;
+    __syncthreads();
+    sl = (red[0] + red[1]) + (red[2] + red[3]);
+    const float inv_c = (float)(1.0 / sqrt(sl / (double)d.kv_lora + (double)d.eps));
+    uint16_t *dst = cache + ((size_t)b * cap + pos) * d.kvw;
+#pragma unroll
+    for (int i = 0; i < 6; i++) {
+        const int k = tid + 128 * i;
+        if (k < d.kv_lora) dst[k] = f32_to_bf16_bits(__fmul_rn(__fmul_rn(cw[i], cv[i]), inv_c));
+        else if (k < d.kvw) crope[k - d.kv_lora] = cv[i];
+    }
+    __syncthreads();
+    if (tid < d.qr / 2) {
+        if (d.theta > 0.f) rope_apply(crope, tid, rp.x, rp.y);
+        const int k = d.kv_lora + 2 * tid;
+        dst[k] = f32_to_bf16_bits(crope[2 * tid]);
+        dst[k + 1] = f32_to_bf16_bits(crope[2 * tid + 1]);
+    }
+}
+
+// grid (H, kv_lora / 128 [+ 1], B), block (16, 8): q_lat[j] = sum_i W_uk[h][i][j] q_nope[i]
+// for a 128-wide block of j, 8 j per thread (16-byte loads), the 8 thread rows splitting i;
+// then RoPE(q_rope_h). Output qa [B][H][kvw]. With latent (decode of up to four tokens,
+// where q_b normalises its input itself and k_mla_prep is not launched) the extra row of
+// CTAs y = kv_lora / 128 does the latent half of k_mla_prep (CTA x = 0 of each sequence).
+__global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, const float2 *rope_tab,
+                             const int *pos_p, MlaDims d, int cap, float *c, uint16_t *cache,
+                             const float *kv_a_norm, int latent)
+{
+    if (latent && (int)blockIdx.y == d.kv_lora / 128) {
+        pdl_wait();
+        pdl_trigger();
+        if (blockIdx.x == 0)
+            mla_latent_prep(c, cache, rope_tab, kv_a_norm, pos_p, d, cap, blockIdx.z,
+                            threadIdx.y * 16 + threadIdx.x);
+        return;
+    }
     __shared__ float qs[256];
     __shared__ float part[8][128 + 4];
     const int h = blockIdx.x, jb = blockIdx.y, b = blockIdx.z;
@@ -782,12 +843,24 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
         rope_tab = rope_table(d.theta, d.qr, cap, st);
         if (!rope_tab) return k3d_status();
     }
-    launch_pdl(k_mla_prep, dim3(B), dim3(256), 0, st, L.ql, L.c, cache, rope_tab, w->q_a_norm, w->kv_a_norm, pos, d, cap);
-    note_launch();
-    K3_TRY(check_launch("mla prep"));
-    K3_TRY(gemv_bf16(L.q, L.ql, w->q_b, s->q_lora, d.H * d.qh, B, 0, st));
-    launch_pdl(k_mla_absorb, dim3(d.H, d.kv_lora / 128, B), dim3(16, 8), 0, st, L.qa, L.q, w->kv_b, rope_tab,
-                                                                       pos, d, cap);
+    // Up to four tokens: q_b takes the raw q_lora activation and applies q_a_norm as it loads
+    // it, and the latent half of k_mla_prep rides in the absorb launch; larger batches run
+    // k_mla_prep first (their q_b is the tensor-core GEMM).
+    const bool fused_prep = B <= 4;
+    if (fused_prep) {
+        const NormIn qn{w->q_a_norm, d.eps};
+        const uint16_t *Wq[1] = {w->q_b};
+        float *Yq[1] = {L.q};
+        const int rq[1] = {d.H * d.qh};
+        K3_TRY(gemv_bf16_multi(1, Wq, Yq, rq, L.ql, s->q_lora, B, st, &qn));
+    } else {
+        launch_pdl(k_mla_prep, dim3(B), dim3(256), 0, st, L.ql, L.c, cache, rope_tab, w->q_a_norm, w->kv_a_norm, pos, d, cap);
+        note_launch();
+        K3_TRY(check_launch("mla prep"));
+        K3_TRY(gemv_bf16(L.q, L.ql, w->q_b, s->q_lora, d.H * d.qh, B, 0, st));
+    }
+    launch_pdl(k_mla_absorb, dim3(d.H, d.kv_lora / 128 + (fused_prep ? 1 : 0), B), dim3(16, 8), 0, st, L.qa, L.q,
+               w->kv_b, rope_tab, pos, d, cap, L.c, cache, w->kv_a_norm, fused_prep ? 1 : 0);
     note_launch();
     K3_TRY(check_launch("mla absorb"));
     {

@@ -46,10 +46,12 @@ __device__ __forceinline__ int work_assign(const MoeWork &w, int p)
 // 2 * n_experts ints. idx is read through L2 (it may have been written by other CTAs of
 // the same grid).
 // zero/nzero: a region zeroed on the way (the fused expert pass's counters).
+// idx_local: idx is this CTA's shared-memory copy (read with plain loads), not global
 __device__ __forceinline__ void group_assignments(const int *idx, int TK, int n_experts, int lo,
                                                   int hi, int *n_active, int *act_expert,
                                                   int *act_off, int *assign, int *sm,
-                                                  int *zero = nullptr, int nzero = 0)
+                                                  int *zero = nullptr, int nzero = 0,
+                                                  bool idx_local = false)
 {
     for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
     int *cnt = sm;                 // [n_experts]
@@ -57,7 +59,7 @@ __device__ __forceinline__ void group_assignments(const int *idx, int TK, int n_
     for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int a = threadIdx.x; a < TK; a += blockDim.x) {
-        const int e = __ldcg(idx + a);
+        const int e = idx_local ? idx[a] : __ldcg(idx + a);
         if (e >= lo && e < hi && e < n_experts && e >= 0) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
@@ -84,7 +86,7 @@ __device__ __forceinline__ void group_assignments(const int *idx, int TK, int n_
     }
     __syncthreads();
     for (int a = threadIdx.x; a < TK; a += blockDim.x) {
-        const int e = __ldcg(idx + a);
+        const int e = idx_local ? idx[a] : __ldcg(idx + a);
         if (e >= lo && e < hi && e < n_experts && e >= 0) {
             const int p = atomicAdd(&cur[e], 1);
             assign[p] = a;

@@ -663,6 +663,7 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
     __shared__ int s_last, s_nneed;
     __shared__ int s_need[kNeedMax];
     __shared__ int s_isel[K3_MAX_TOPK];
+    __shared__ int s_idx[K3_MAX_TOPK];
     __shared__ float s_m;
     const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
     const int t = blockIdx.y;
@@ -768,12 +769,14 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
             J.lo[tE + e] = lo;
             J.hi[tE + e] = hi;
             J.score[tE + e] = sc;
-            // one arrival per expert; the release publishes this thread's stores, and the
-            // thread that completes the count acquires everyone's
-            if (atom_add_acq_rel(&g_router_ctr[t], 1u) == (unsigned)E - 1) {
-                g_router_ctr[t] = 0;
-                s_last = 1;
-            }
+            __threadfence();
+        }
+        __syncthreads();
+        // one arrival per CTA (both writers fenced their stores before the barrier); the
+        // CTA that completes the count acquires every other CTA's stores
+        if (threadIdx.x == 0 && atom_add_acq_rel(&g_router_ctr[t], 1u) == gridDim.x - 1) {
+            g_router_ctr[t] = 0;
+            s_last = 1;
         }
         __syncthreads();
         if (!s_last) return;
@@ -905,10 +908,12 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
         }
         if (lane < K) {
             J.idx[(size_t)t * K + lane] = b0 >= 0 ? b0 : 0;
+            s_idx[lane] = b0 >= 0 ? b0 : 0;
             J.wts[(size_t)t * K + lane] = __fmul_rn(w0, J.routed_scale);
         }
         if (lane + 32 < K) {
             J.idx[(size_t)t * K + lane + 32] = b1 >= 0 ? b1 : 0;
+            s_idx[lane + 32] = b1 >= 0 ? b1 : 0;
             J.wts[(size_t)t * K + lane + 32] = __fmul_rn(w1, J.routed_scale);
         }
         if (J.T > 1) __threadfence();
@@ -925,8 +930,14 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
         __syncthreads();
         if (!s_last) return;
     }
-    group_assignments(J.idx, J.T * K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
-                      J.assign, gsm, J.zero, J.nzero);
+    // one token: its selection is in this CTA's shared memory; more: every token's last CTA
+    // published its row of idx (fenced) before the count
+    if (J.T == 1)
+        group_assignments(s_idx, K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
+                          J.assign, gsm, J.zero, J.nzero, true);
+    else
+        group_assignments(J.idx, J.T * K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
+                          J.assign, gsm, J.zero, J.nzero);
 }
 
 size_t router_ws_bytes(int T, int n_experts)
