@@ -192,7 +192,20 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
         float si = St[i * D + j];
         if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(__fmul_rn(ks[i], beta), d));
         if (qs[i] != 0.0f) o = __fadd_rn(o, __fmul_rn(qs[i], si));
-        S[(size_t)i * D + j] = si;
+        St[i * D + j] = si;
+    }
+    // the tile goes back in one coalesced pass after the loop (a global store inside it,
+    // through a generic pointer, would order every later shared-memory read after it)
+    __syncthreads();
+    {
+        float4 *S4 = reinterpret_cast<float4 *>(S);
+        const float4 *T4 = reinterpret_cast<const float4 *>(St);
+        if (bulk_ok) {
+#pragma unroll 8
+            for (int f = j; f < D * D / 4; f += blockDim.x) S4[f] = T4[f];
+        } else {
+            for (int f = j; f < D * D; f += blockDim.x) S[f] = St[f];
+        }
     }
     // head RMSNorm, then the output gate
     const double so = block_sum_dd((double)o * (double)o, red, nw);
@@ -291,8 +304,12 @@ __global__ void __launch_bounds__(DT) k_kda_head_reg(const __grid_constant__ Kda
         if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(kbs[i], d));
         const float qi = qs[i];
         if (qi != 0.0f) o = __fadd_rn(o, __fmul_rn(qi, si));
-        S[(size_t)i * DT + j] = si;
+        s[i] = si;
     }
+    // the column goes back after the loop: a store through a generic pointer between the
+    // loop's shared-memory reads would order every later read after it
+#pragma unroll
+    for (int i = 0; i < DT; i++) S[(size_t)i * DT + j] = s[i];
     {
         const double o2 = warp_sum_d((double)o * (double)o);
         if (lane == 0) red[0][warp] = o2;            // red[0] was last read before the
@@ -305,6 +322,182 @@ __global__ void __launch_bounds__(DT) k_kda_head_reg(const __grid_constant__ Kda
     o = __fmul_rn(__fmul_rn(onw, o), inv);
     o = __fmul_rn(o, sigm(gpv));
     A.heads[bp] = o;
+}
+
+// The same head split over a cluster of DT / 32 one-warp CTAs: CTA r of the cluster owns
+// value columns [32 r, 32 r + 32) (lane = column), so a head's 64 KB state tile streams
+// through DT / 32 SMs instead of one (at batch 1, 256 CTAs on 148 SMs instead of 64). Every
+// CTA computes the conv, L2 norms, gates and decays of all DT key channels (lane l holds
+// channels l + 32 g), which are cheap; the head RMSNorm's sum of o^2 is combined across the
+// cluster through distributed shared memory. Each sum keeps the order of k_kda_head (a
+// warp's butterfly over 32 consecutive channels, then the 32-channel groups in order), so
+// the result is bit-identical to it. The q and k conv histories are written by CTA 0 of
+// the cluster only (every CTA computes the same values); each CTA writes its own v
+// channels.
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ double ld_dsmem_f64(const double *local, uint32_t rank)
+{
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+    uint32_t ra;
+    double v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+template <int KC, int DT>
+__global__ void __launch_bounds__(32) k_kda_head_cl(const __grid_constant__ KdaHeadArgs A)
+{
+    static_assert(KC > 0 && DT % 32 == 0 && DT <= 128, "cluster head: KC > 0, DT in 32..128");
+    constexpr int NG = DT / 32;                      // channel groups = CTAs per head
+    __shared__ float qs[DT], ks[DT], kbs[DT], as[DT];
+    __shared__ double s_o2;
+    const int l = threadIdx.x;
+    const int cr = (int)cluster_rank();
+    const int h = blockIdx.x / NG, b = blockIdx.y;
+    const int H = A.H, P = H * DT;
+    const int j = cr * 32 + l;                       // this lane's value column
+    float *S = A.state + (size_t)b * A.state_stride + (size_t)h * DT * DT;
+    float *conv = A.state + (size_t)b * A.state_stride + (size_t)H * DT * DT;
+    const size_t rowb = (size_t)b * P + (size_t)h * DT;
+    float s[DT];
+#pragma unroll
+    for (int i = 0; i < DT; i++) s[i] = S[(size_t)i * DT + j];
+    // key channels c_g = h * DT + l + 32 g: q and k conv taps and histories, the decay inputs
+    float wq[NG][KC], wk[NG][KC], xq[NG][KC], xk[NG][KC], dtb[NG];
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+        const int c = h * DT + l + 32 * g;
+#pragma unroll
+        for (int t = 0; t < KC; t++) {
+            wq[g][t] = A.q_conv[(size_t)c * KC + t];
+            wk[g][t] = A.k_conv[(size_t)c * KC + t];
+        }
+#pragma unroll
+        for (int t = 0; t < KC - 1; t++) {
+            xq[g][t] = conv[(size_t)c * (KC - 1) + t];
+            xk[g][t] = conv[(size_t)P * (KC - 1) + (size_t)c * (KC - 1) + t];
+        }
+        dtb[g] = A.dt_bias[c];
+    }
+    // value channel j
+    const int cj = h * DT + j;
+    float wv[KC], xv[KC];
+    float *hv = conv + (size_t)2 * P * (KC - 1) + (size_t)cj * (KC - 1);
+#pragma unroll
+    for (int t = 0; t < KC; t++) wv[t] = A.v_conv[(size_t)cj * KC + t];
+#pragma unroll
+    for (int t = 0; t < KC - 1; t++) xv[t] = hv[t];
+    const float alog = A.A_log[h], onw = A.o_norm[j];
+    pdl_wait();
+    pdl_trigger();
+    float zv[NG];
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+        xq[g][KC - 1] = A.qp[rowb + l + 32 * g];
+        xk[g][KC - 1] = A.kp[rowb + l + 32 * g];
+        zv[g] = A.z[rowb + l + 32 * g];
+    }
+    xv[KC - 1] = A.vp[rowb + j];
+    const float gpv = A.gp[rowb + j], bpv = A.bp[(size_t)b * H + h];
+    // ShortConv + SiLU in the CPU's order (k3_ops.c:875-878)
+    float qv[NG], kv[NG];
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+        float aq = __fmul_rn(wq[g][KC - 1], xq[g][KC - 1]);
+        float ak = __fmul_rn(wk[g][KC - 1], xk[g][KC - 1]);
+#pragma unroll
+        for (int t = 0; t < KC - 1; t++) {
+            aq = __fadd_rn(aq, __fmul_rn(wq[g][t], xq[g][t]));
+            ak = __fadd_rn(ak, __fmul_rn(wk[g][t], xk[g][t]));
+        }
+        qv[g] = __fmul_rn(aq, sigm(aq));
+        kv[g] = __fmul_rn(ak, sigm(ak));
+    }
+    float av = __fmul_rn(wv[KC - 1], xv[KC - 1]);
+#pragma unroll
+    for (int t = 0; t < KC - 1; t++) av = __fadd_rn(av, __fmul_rn(wv[t], xv[t]));
+    const float vv = __fmul_rn(av, sigm(av));
+#pragma unroll
+    for (int t = 0; t < KC - 1; t++) hv[t] = xv[t + 1];
+    // L2 norms: warp sums per 32-channel group, the groups added in order (block_sum_dd's)
+    double sq = 0.0, sk = 0.0;
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+        sq += warp_sum_d((double)qv[g] * (double)qv[g]);
+        sk += warp_sum_d((double)kv[g] * (double)kv[g]);
+    }
+    const float iq = (float)(1.0 / sqrt(sq + (double)1e-6f)), ik = (float)(1.0 / sqrt(sk + (double)1e-6f));
+    const float qscale = 1.0f / sqrtf((float)A.D);
+    const float beta = sigm(bpv);
+    const float a = expf(alog);
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+        const int i = l + 32 * g;
+        const float qn = __fmul_rn(__fmul_rn(qv[g], iq), qscale);
+        const float kn = __fmul_rn(kv[g], ik);
+        qs[i] = qn;
+        ks[i] = kn;
+        kbs[i] = __fmul_rn(kn, beta);
+        as[i] = expf(__fmul_rn(A.lb, sigm(__fmul_rn(a, __fadd_rn(zv[g], dtb[g])))));
+    }
+    __syncwarp();
+    float u = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DT; i++) {
+        s[i] = __fmul_rn(s[i], as[i]);
+        const float ki = ks[i];
+        if (ki != 0.0f) u = __fadd_rn(u, __fmul_rn(ki, s[i]));
+    }
+    const float d = __fsub_rn(vv, u);
+    float o = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DT; i++) {
+        float si = s[i];
+        if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(kbs[i], d));
+        const float qi = qs[i];
+        if (qi != 0.0f) o = __fadd_rn(o, __fmul_rn(qi, si));
+        s[i] = si;
+    }
+    // the column goes back after the loop: a store through a generic pointer between the
+    // loop's shared-memory reads would order every later read after it
+#pragma unroll
+    for (int i = 0; i < DT; i++) S[(size_t)i * DT + j] = s[i];
+    // head RMSNorm: this CTA's 32 columns are one group; the cluster's groups in order
+    const double o2 = warp_sum_d((double)o * (double)o);
+    if (l == 0) s_o2 = o2;
+    cluster_sync_all();
+    // every CTA of the cluster has read the q and k histories by now
+    if (cr == 0) {
+#pragma unroll
+        for (int g = 0; g < NG; g++) {
+            const int c = h * DT + l + 32 * g;
+#pragma unroll
+            for (int t = 0; t < KC - 1; t++) {
+                conv[(size_t)c * (KC - 1) + t] = xq[g][t + 1];
+                conv[(size_t)P * (KC - 1) + (size_t)c * (KC - 1) + t] = xk[g][t + 1];
+            }
+        }
+    }
+    double so = 0.0;
+#pragma unroll
+    for (int g = 0; g < NG; g++) so += ld_dsmem_f64(&s_o2, (uint32_t)g);
+    cluster_sync_all();                              // every CTA has read every s_o2
+    const float inv = (float)(1.0 / sqrt(so / (double)DT + (double)A.eps));
+    o = __fmul_rn(__fmul_rn(onw, o), inv);
+    o = __fmul_rn(o, sigm(gpv));
+    A.heads[rowb + j] = o;
 }
 
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
@@ -331,9 +524,10 @@ size_t k3d_kda_state_floats(const K3dKdaShape *s)
 
 }  // extern "C"
 
-// Which head kernel runs (k3d_set_kda_head_kernel): 0 the register-column kernel where
-// head_dim is 32, 64 or 128 and conv_k is 4, else the shared-tile kernel; 1 always the
-// shared-tile kernel.
+// Which head kernel runs (k3d_set_kda_head_kernel): 0 the cluster kernel (head_dim / 32
+// one-warp CTAs per head) where head_dim is 32, 64 or 128 and conv_k is 4, else the
+// shared-tile kernel; 1 always the shared-tile kernel; 2 the register-column kernel (one
+// CTA per head) where it applies.
 static int g_kda_head_kernel = 0;
 
 // The layer; with ni, xn is the raw residual and the projection GEMV normalises it.
@@ -378,8 +572,12 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
         allow_smem_max(k_kda_head<0>);
         init = true;
     }
-    const bool reg = g_kda_head_kernel == 0 && s->conv_k == 4;
-    if (reg && D == 128) launch_pdl(k_kda_head_reg<4, 128>, dim3(H, B), dim3(D), 0, st, A);
+    const bool cl = g_kda_head_kernel == 0 && s->conv_k == 4;
+    const bool reg = g_kda_head_kernel == 2 && s->conv_k == 4;
+    if (cl && D == 128) launch_pdl_cluster(k_kda_head_cl<4, 128>, dim3(H * 4, B), dim3(32), 0, st, 4, A);
+    else if (cl && D == 64) launch_pdl_cluster(k_kda_head_cl<4, 64>, dim3(H * 2, B), dim3(32), 0, st, 2, A);
+    else if (cl && D == 32) launch_pdl_cluster(k_kda_head_cl<4, 32>, dim3(H, B), dim3(32), 0, st, 1, A);
+    else if (reg && D == 128) launch_pdl(k_kda_head_reg<4, 128>, dim3(H, B), dim3(D), 0, st, A);
     else if (reg && D == 64) launch_pdl(k_kda_head_reg<4, 64>, dim3(H, B), dim3(D), 0, st, A);
     else if (reg && D == 32) launch_pdl(k_kda_head_reg<4, 32>, dim3(H, B), dim3(D), 0, st, A);
     else if (s->conv_k == 4) launch_pdl(k_kda_head<4>, dim3(H, B), dim3(D), smem, st, A);
@@ -397,7 +595,7 @@ extern "C" {
 
 int k3d_set_kda_head_kernel(int kind)
 {
-    if (kind < 0 || kind > 1) return fail(K3D_EINVAL, "k3d_set_kda_head_kernel(%d): 0 or 1", kind);
+    if (kind < 0 || kind > 2) return fail(K3D_EINVAL, "k3d_set_kda_head_kernel(%d): 0 to 2", kind);
     g_kda_head_kernel = kind;
     return K3D_OK;
 }

@@ -366,12 +366,18 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
                                                      const uint16_t *cache, const int *pos_p,
                                                      MlaDims d, int cap)
 {
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     const int split = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
+    // The position and the cache rows below it are read before the programmatic wait:
+    // nothing in the kernels just before writes them (the position changes between steps,
+    // row pos is written by the latent prep of this call, and every kernel before the one
+    // still running has completed).
     const int pos = *pos_p;
-    if (pos < 0 || pos >= cap) return;          // k_mla_prep has raised K3D_EBOUND
+    if (pos < 0 || pos >= cap) {                // the latent prep has raised K3D_EBOUND
+        pdl_wait();
+        pdl_trigger();
+        return;
+    }
     const int kvw = d.kvw;
     const int pitch = kvw + 8;                  // bf16 per smem row: 16 B pad, no conflicts
     const int hgn = min(kAHG, d.H - hg * kAHG);
@@ -393,7 +399,11 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
     const int s0 = split * per, s1 = min(n, s0 + per);
     const uint16_t *cb = cache + (size_t)b * cap * kvw;
     const uint32_t ct_s = (uint32_t)__cvta_generic_to_shared(Ct);
-    if (s0 < s1) mla_stage_tile(ct_s, cb, s0, s1, kvw, pitch);
+    const bool early = s0 < s1 && min(s0 + kATP, s1) <= pos;     // tile 0 lies below row pos
+    if (early) mla_stage_tile(ct_s, cb, s0, s1, kvw, pitch);
+    pdl_wait();
+    pdl_trigger();
+    if (s0 < s1 && !early) mla_stage_tile(ct_s, cb, s0, s1, kvw, pitch);
 
     // Q hi/lo for this CTA's heads (rows >= hgn zero): float4 loads, unrolled so that
     // many are in flight at once
