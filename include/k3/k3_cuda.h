@@ -278,12 +278,13 @@ int    k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K
 int    k3d_kda_layer_decode_normed(float *h, const float *norm_w, float eps, const K3dKdaW *w,
                                    const K3dKdaShape *s, int B, float *state, void *ws,
                                    size_t ws_bytes);
-/* Which kernel runs the per-head step of the decode layer: 0 (default) splits each head's
- * value columns over a cluster of head_dim / 32 one-warp CTAs, state columns in registers,
- * where head_dim is 32, 64 or 128 and conv_k is 4 (else as 1); 1 stages the head's state
- * tile in shared memory, one CTA per head; 2 keeps the state columns in registers, one
- * CTA per head. Bit-identical; the switch exists to measure and test each. No reference
- * counterpart. */
+/* Which kernel runs the per-head step of the decode layer: 0 (default) chooses 2 for up to
+ * four sequences and 1 above; 1 stages the head's state tile in shared memory, one CTA per
+ * head; 2 keeps each thread's state column in registers, one CTA per head; 3 splits each
+ * head's value columns over a cluster of head_dim / 32 one-warp CTAs (registers, the head
+ * norm's sum through distributed shared memory). 2 and 3 apply where head_dim is 32, 64 or
+ * 128 and conv_k is 4 (else 1 runs). Bit-identical; the switch exists to measure and test
+ * each. No reference counterpart. */
 int    k3d_set_kda_head_kernel(int kind);
 
 /* ------------------------------------------------------------------- MLA ---- */

@@ -192,20 +192,7 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
         float si = St[i * D + j];
         if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(__fmul_rn(ks[i], beta), d));
         if (qs[i] != 0.0f) o = __fadd_rn(o, __fmul_rn(qs[i], si));
-        St[i * D + j] = si;
-    }
-    // the tile goes back in one coalesced pass after the loop (a global store inside it,
-    // through a generic pointer, would order every later shared-memory read after it)
-    __syncthreads();
-    {
-        float4 *S4 = reinterpret_cast<float4 *>(S);
-        const float4 *T4 = reinterpret_cast<const float4 *>(St);
-        if (bulk_ok) {
-#pragma unroll 8
-            for (int f = j; f < D * D / 4; f += blockDim.x) S4[f] = T4[f];
-        } else {
-            for (int f = j; f < D * D; f += blockDim.x) S[f] = St[f];
-        }
+        S[(size_t)i * D + j] = si;
     }
     // head RMSNorm, then the output gate
     const double so = block_sum_dd((double)o * (double)o, red, nw);
@@ -524,10 +511,10 @@ size_t k3d_kda_state_floats(const K3dKdaShape *s)
 
 }  // extern "C"
 
-// Which head kernel runs (k3d_set_kda_head_kernel): 0 the cluster kernel (head_dim / 32
-// one-warp CTAs per head) where head_dim is 32, 64 or 128 and conv_k is 4, else the
-// shared-tile kernel; 1 always the shared-tile kernel; 2 the register-column kernel (one
-// CTA per head) where it applies.
+// Which head kernel runs (k3d_set_kda_head_kernel): 0 chooses (the register-column kernel
+// for up to four sequences, else the shared-tile kernel); 1 the shared-tile kernel; 2 the
+// register-column kernel (one CTA per head); 3 the cluster kernel (head_dim / 32 one-warp
+// CTAs per head). 2 and 3 apply where head_dim is 32, 64 or 128 and conv_k is 4 (else 1).
 static int g_kda_head_kernel = 0;
 
 // The layer; with ni, xn is the raw residual and the projection GEMV normalises it.
@@ -572,8 +559,12 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
         allow_smem_max(k_kda_head<0>);
         init = true;
     }
-    const bool cl = g_kda_head_kernel == 0 && s->conv_k == 4;
-    const bool reg = g_kda_head_kernel == 2 && s->conv_k == 4;
+    // default: the register-column kernel for up to four sequences (64 to 256 CTAs), the
+    // shared-tile kernel above (the register kernel's 186 registers per thread cost it
+    // occupancy when there are thousands of CTAs)
+    const int kind = g_kda_head_kernel == 0 ? (B <= 4 ? 2 : 1) : g_kda_head_kernel;
+    const bool cl = kind == 3 && s->conv_k == 4;
+    const bool reg = kind == 2 && s->conv_k == 4;
     if (cl && D == 128) launch_pdl_cluster(k_kda_head_cl<4, 128>, dim3(H * 4, B), dim3(32), 0, st, 4, A);
     else if (cl && D == 64) launch_pdl_cluster(k_kda_head_cl<4, 64>, dim3(H * 2, B), dim3(32), 0, st, 2, A);
     else if (cl && D == 32) launch_pdl_cluster(k_kda_head_cl<4, 32>, dim3(H, B), dim3(32), 0, st, 1, A);
@@ -595,7 +586,7 @@ extern "C" {
 
 int k3d_set_kda_head_kernel(int kind)
 {
-    if (kind < 0 || kind > 2) return fail(K3D_EINVAL, "k3d_set_kda_head_kernel(%d): 0 to 2", kind);
+    if (kind < 0 || kind > 3) return fail(K3D_EINVAL, "k3d_set_kda_head_kernel(%d): 0 to 3", kind);
     g_kda_head_kernel = kind;
     return K3D_OK;
 }

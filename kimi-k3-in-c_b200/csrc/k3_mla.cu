@@ -272,13 +272,21 @@ __global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, co
 #pragma unroll
     for (int k = 0; k < 8; k++) part[ty][tx * 8 + k] = acc[k];
     __syncthreads();
-    float *out = qa + ((size_t)b * d.H + h) * d.kvw;
+    // q_lat as the attention's bf16 operand pair: hi = bf16(v), lo = bf16(v - hi)
+    uint16_t *qhi = reinterpret_cast<uint16_t *>(qa);
+    uint16_t *ohi = qhi + ((size_t)b * d.H + h) * d.kvw;
+    uint16_t *olo = ohi + (size_t)gridDim.z * d.H * d.kvw;
+    auto put = [&](int k, float v) {
+        const uint16_t hb = f32_to_bf16_bits(v);
+        ohi[k] = hb;
+        olo[k] = f32_to_bf16_bits(v - bf16_to_f32(hb));
+    };
     {
         const int j = tid;   // 0..127
         float v = 0.f;
 #pragma unroll
         for (int r = 0; r < 8; r++) v += part[r][j];
-        out[jb * 128 + j] = v;
+        put(jb * 128 + j, v);
     }
     if (jb == 0) {
         const int pos = *pos_p;
@@ -288,7 +296,7 @@ __global__ void k_mla_absorb(float *qa, const float *q, const uint16_t *kv_b, co
             for (int i = tid; i < d.qr / 2; i += 128) rope_apply(qs + d.qn, i, rt[i].x, rt[i].y);
             __syncthreads();
         }
-        for (int i = tid; i < d.qr; i += 128) out[d.kv_lora + i] = qs[d.qn + i];
+        for (int i = tid; i < d.qr; i += 128) put(d.kv_lora + i, qs[d.qn + i]);
     }
 }
 
@@ -405,28 +413,23 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
     pdl_trigger();
     if (s0 < s1 && !early) mla_stage_tile(ct_s, cb, s0, s1, kvw, pitch);
 
-    // Q hi/lo for this CTA's heads (rows >= hgn zero): float4 loads, unrolled so that
-    // many are in flight at once
+    // Q as the bf16 hi/lo pair the absorb kernel wrote, rows of this CTA's heads (rows >=
+    // hgn zero-filled): 16-byte cp.async chunks, all in flight at once (one group)
     {
-        const int q4 = kvw / 4;
-#pragma unroll 6
-        for (int i = tid; i < kAHG * q4; i += 128) {
-            const int hh = i / q4, k = 4 * (i % q4);
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (hh < hgn)
-                v = __ldg(reinterpret_cast<const float4 *>(qa + ((size_t)b * d.H + hg * kAHG + hh) * kvw + k));
-            const float vv[4] = {v.x, v.y, v.z, v.w};
-            uint32_t hi[2], lo[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const uint16_t h0 = f32_to_bf16_bits(vv[2 * u]), h1 = f32_to_bf16_bits(vv[2 * u + 1]);
-                hi[u] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                lo[u] = (uint32_t)f32_to_bf16_bits(vv[2 * u] - bf16_to_f32(h0)) |
-                        ((uint32_t)f32_to_bf16_bits(vv[2 * u + 1] - bf16_to_f32(h1)) << 16);
-            }
-            *reinterpret_cast<uint2 *>(Qhi + hh * pitch + k) = make_uint2(hi[0], hi[1]);
-            *reinterpret_cast<uint2 *>(Qlo + hh * pitch + k) = make_uint2(lo[0], lo[1]);
+        const uint16_t *qh0 = reinterpret_cast<const uint16_t *>(qa);
+        const uint16_t *ql0 = qh0 + (size_t)gridDim.z * d.H * kvw;
+        const int cpr = kvw / 8;                           // 16-byte chunks per row
+        const uint32_t qhi_d = (uint32_t)__cvta_generic_to_shared(Qhi);
+        const uint32_t qlo_d = (uint32_t)__cvta_generic_to_shared(Qlo);
+        for (int i = tid; i < kAHG * cpr; i += 128) {
+            const int hh = i / cpr, c = i % cpr;
+            const bool ok = hh < hgn;
+            const size_t row = ((size_t)b * d.H + hg * kAHG + (ok ? hh : 0)) * kvw + (size_t)c * 8;
+            const uint32_t off = (uint32_t)(hh * pitch + c * 8) * 2u;
+            cp16(qhi_d + off, qh0 + row, ok ? 16u : 0u);
+            cp16(qlo_d + off, ql0 + row, ok ? 16u : 0u);
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     }
     if (tid < kAHG) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
 
@@ -581,6 +584,7 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
         }
         __syncthreads();     // the buffer and P are reused by the next tile
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");   // a split without positions staged Q only
     // ---- partial outputs of this split
     const int jb = warp * (NT * 8);
     const size_t stride = (size_t)d.kv_lora + 2;
@@ -591,9 +595,8 @@ __global__ void __launch_bounds__(128) k_mla_attn_tc(float *part, const float *q
             float *dst = part + (((size_t)b * d.H + hg * kAHG + h) * d.nsplit + split) * stride;
 #pragma unroll
             for (int i = 0; i < NT; i++) {
-                const int j = jb + 8 * i + 2 * t4;
-                dst[j] = acc[i][2 * rr];
-                dst[j + 1] = acc[i][2 * rr + 1];
+                const int j = jb + 8 * i + 2 * t4;     // even; rows start 8-byte aligned
+                *reinterpret_cast<float2 *>(dst + j) = make_float2(acc[i][2 * rr], acc[i][2 * rr + 1]);
             }
         }
     }
@@ -615,29 +618,33 @@ static size_t mla_attn_smem(int kvw)
 // heads [B][H*vh]. The W_uv rows are loaded before the programmatic wait (weights), and
 // after it every partial load the merge needs first (m and l of one split per thread, the
 // first kMP ctx partials of the thread's column pair) is issued before any reduction.
-static const int kMP = 12;
-__global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *part,
+static const int kMP = 40;
+__global__ void __launch_bounds__(256, 2) k_mla_merge(float *heads, const float *part,
                                                    const uint16_t *kv_b, const float *gate,
                                                    const int *pos_p, MlaDims d, int cap)
 {
-    extern __shared__ float cx[];   // [kv_lora]
+    extern __shared__ __align__(16) float cx[];   // [kv_lora], then W_uv rows [32][kv_lora] bf16
     __shared__ float wsc[256 + 2 * 256];   // split weights, then partial column sums
     __shared__ float red[8];
     const int h = blockIdx.x, rb = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // 32 rows of W_uv, 4 per warp: every 16-byte load of the warp's rows first (kv_lora <=
-    // 512, so a lane holds at most 2 chunks of each row)
+    // this CTA's 32 rows of W_uv into shared memory (16-byte cp.async chunks, issued before
+    // the programmatic wait: weights), 4 rows per warp later
     const size_t kvd = (size_t)(d.qn + d.vh);
-    const uint16_t *rows = kv_b + ((size_t)h * kvd + d.qn + rb * 32 + warp * 4) * d.kv_lora;
-    const bool vec = (d.kv_lora & 255) == 0;
-    const int nck = d.kv_lora / 256;          // chunks per lane per row: 1 or 2
-    uint4 wv[4][2];
-    if (vec) {
+    const uint16_t *rows0 = kv_b + ((size_t)h * kvd + d.qn + rb * 32) * d.kv_lora;
+    uint16_t *wsm = reinterpret_cast<uint16_t *>(cx + d.kv_lora);
+    {
+        const uint32_t w_d = (uint32_t)__cvta_generic_to_shared(wsm);
+        const int nchunk = 32 * d.kv_lora / 8;
+        for (int i = tid; i < nchunk; i += blockDim.x) cp16(w_d + 16u * i, rows0 + (size_t)i * 8, 16u);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    // the output gate of this warp's rows (written by the projection GEMV, long before)
+    float gv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (gate && lane == 0) {
 #pragma unroll
         for (int r = 0; r < 4; r++)
-#pragma unroll
-            for (int k = 0; k < 2; k++)
-                if (k < nck) wv[r][k] = __ldg(reinterpret_cast<const uint4 *>(rows + (size_t)r * d.kv_lora + k * 256 + lane * 8));
+            gv[r] = gate[(size_t)b * d.H * d.vh + (size_t)h * d.vh + rb * 32 + warp * 4 + r];
     }
     pdl_wait();
     pdl_trigger();
@@ -645,6 +652,7 @@ __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *pa
     if (pos < 0 || pos >= cap) {
         for (int r = tid; r < 32; r += blockDim.x)
             heads[(size_t)b * d.H * d.vh + (size_t)h * d.vh + rb * 32 + r] = 0.f;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
         return;
     }
     const float *pp = part + ((size_t)b * d.H + h) * d.nsplit * (d.kv_lora + 2);
@@ -718,34 +726,29 @@ __global__ void __launch_bounds__(256) k_mla_merge(float *heads, const float *pa
             }
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
+    // 4 rows per warp, lane l takes 8-element chunks l, l + 32, ... of each row
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (vec) {
+    const uint16_t *wr = wsm + (size_t)warp * 4 * d.kv_lora;
+    for (int j0 = lane * 8; j0 < d.kv_lora; j0 += 256) {
 #pragma unroll
-        for (int r = 0; r < 4; r++)
+        for (int r = 0; r < 4; r++) {
+            const uint4 wv = *reinterpret_cast<const uint4 *>(wr + (size_t)r * d.kv_lora + j0);
+            const uint32_t u[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int k = 0; k < 2; k++) {
-                if (k >= nck) continue;
-                const int j0 = k * 256 + lane * 8;
-                const uint32_t u[4] = {wv[r][k].x, wv[r][k].y, wv[r][k].z, wv[r][k].w};
-#pragma unroll
-                for (int m = 0; m < 4; m++) {
-                    acc[r] = fmaf(__uint_as_float(u[m] << 16), cx[j0 + 2 * m], acc[r]);
-                    acc[r] = fmaf(__uint_as_float(u[m] & 0xffff0000u), cx[j0 + 2 * m + 1], acc[r]);
-                }
+            for (int m = 0; m < 4; m++) {
+                acc[r] = fmaf(__uint_as_float(u[m] << 16), cx[j0 + 2 * m], acc[r]);
+                acc[r] = fmaf(__uint_as_float(u[m] & 0xffff0000u), cx[j0 + 2 * m + 1], acc[r]);
             }
-    } else {
-#pragma unroll
-        for (int r = 0; r < 4; r++)
-            for (int j = lane; j < d.kv_lora; j += 32)
-                acc[r] = fmaf(bf16_to_f32(rows[(size_t)r * d.kv_lora + j]), cx[j], acc[r]);
+        }
     }
 #pragma unroll
     for (int r = 0; r < 4; r++) {
         const float v = warp_sum(acc[r]);
         if (lane == 0) {
             const size_t o = (size_t)b * d.H * d.vh + (size_t)h * d.vh + rb * 32 + warp * 4 + r;
-            heads[o] = gate ? v * (1.0f / (1.0f + expf(-gate[o]))) : v;
+            heads[o] = gate ? v * (1.0f / (1.0f + expf(-gv[r]))) : v;
         }
     }
 }
@@ -893,7 +896,7 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
         note_launch();
         K3_TRY(check_launch("mla attn"));
     }
-    launch_pdl(k_mla_merge, dim3(d.H, d.vh / 32, B), dim3(256), (size_t)d.kv_lora * 4, st, 
+    launch_pdl(k_mla_merge, dim3(d.H, d.vh / 32, B), dim3(256), (size_t)d.kv_lora * 4 + 32 * (size_t)d.kv_lora * 2, st, 
         L.heads, L.part, w->kv_b, s->out_gate ? L.gate : nullptr, pos, d, cap);
     note_launch();
     K3_TRY(check_launch("mla merge"));

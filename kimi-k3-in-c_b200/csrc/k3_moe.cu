@@ -127,17 +127,26 @@ __global__ void __launch_bounds__(256, 2) k_moe_down(float *contrib, const float
 }
 
 // ---- ordered combine ------------------------------------------------------------------
+// early: the routing (idx, wts, pos_of) and the residual were written on this stream at
+// least two kernels back (the expert passes ran in between), so they are read before the
+// programmatic wait. The shared expert's output is read after it: it comes from the side
+// stream, and a captured graph turns that join into a programmatic edge too, which lets
+// this kernel start before the side stream's last kernel has finished.
 __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t slice_stride,
                               const int *idx, const float *wts, const float *sh_out, int hidden,
-                              int K, int lo, int hi, int accumulate, const int *pos_of)
+                              int K, int lo, int hi, int accumulate, const int *pos_of, int early)
 {
-    pdl_wait();
-    pdl_trigger();
     const int t = blockIdx.y;
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= hidden) return;
+    if (!early) {
+        pdl_wait();
+        pdl_trigger();
+    }
+    if (r >= hidden) {
+        if (early) { pdl_wait(); pdl_trigger(); }
+        return;
+    }
     float *o = out + (size_t)t * hidden + r;
-    const float sh = sh_out ? sh_out[(size_t)t * hidden + r] : 0.0f;
     const float prev = accumulate ? *o : 0.0f;
     float acc = 0.0f;
     // top-k slots in groups of 8: the group's expert ids, weights and contributions are all
@@ -157,8 +166,13 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
             const bool local = e[k] >= lo && e[k] < hi;
             const int row = !pos_of ? a : (local ? __ldcg(pos_of + a) : 0);
             c[k] = contrib + (size_t)row * hidden + r;
-            v[k] = c[k][0];
         }
+        if (early && j0 == 0) {
+            pdl_wait();
+            pdl_trigger();
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = c[k][0];
         for (int s0 = 1; s0 < ks; s0 += 4) {
             float t4[4][8];
 #pragma unroll
@@ -180,7 +194,7 @@ __global__ void k_moe_combine(float *out, const float *contrib, int ks, size_t s
             acc = __fadd_rn(acc, __fmul_rn(w[k], v[k]));
         }
     }
-    if (sh_out) acc = __fadd_rn(acc, sh);
+    if (sh_out) acc = __fadd_rn(acc, sh_out[(size_t)t * hidden + r]);   // after the wait (K >= 1)
     *o = accumulate ? __fadd_rn(prev, acc) : acc;
 }
 
@@ -990,7 +1004,8 @@ int k3d_moe_swiglu(float *out, const float *x, const K3dMoeW *w, const K3dMoeSha
         return fail(K3D_ECUDA, "moe: join from the side stream");
     dim3 grid((s->hidden + 255) / 256, T);
     launch_pdl(k_moe_combine, dim3(grid), dim3(256), 0, st, out, O.contrib, O.ks, O.slice, I, Wt, shared ? L.sh_out : nullptr,
-                                        s->hidden, K, s->expert_lo, s->expert_hi, accumulate, O.pos_of);
+                                        s->hidden, K, s->expert_lo, s->expert_hi, accumulate, O.pos_of,
+                                        umax > 0 ? 1 : 0);
     note_launch();
     K3_TRY(check_launch("moe combine"));
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;

@@ -23,6 +23,7 @@
 //   which that classical bound needed about once per 800 experts, becomes rare.
 //   The sigmoid uses k3_expf (glibc's expf restated, bit-identical), and all float
 //   operations use explicit round-to-nearest intrinsics so nothing is contracted.
+#include "k3_bulk.cuh"
 #include "k3_common.cuh"
 #include "k3_expf.h"
 #include "k3_moe.cuh"
@@ -583,6 +584,7 @@ template <typename WT> struct WChunk;       // 8 weights held in registers
 template <> struct WChunk<uint16_t> {
     uint4 v;
     __device__ __forceinline__ void load(const uint16_t *row, int c) { v = ldg_nc_v4(row + 8 * (size_t)c); }
+    __device__ __forceinline__ void load_s(const uint16_t *row, int c) { v = *reinterpret_cast<const uint4 *>(row + 8 * (size_t)c); }
     __device__ __forceinline__ void get(float w[8]) const
     {
         const uint32_t u[4] = {v.x, v.y, v.z, v.w};
@@ -599,6 +601,11 @@ template <> struct WChunk<float> {
     {
         a = ldg_nc_v4(row + 8 * (size_t)c);
         b = ldg_nc_v4(row + 8 * (size_t)c + 4);
+    }
+    __device__ __forceinline__ void load_s(const float *row, int c)
+    {
+        a = *reinterpret_cast<const uint4 *>(row + 8 * (size_t)c);
+        b = *reinterpret_cast<const uint4 *>(row + 8 * (size_t)c + 4);
     }
     __device__ __forceinline__ void get(float w[8]) const
     {
@@ -646,11 +653,15 @@ __device__ __forceinline__ float sigmoid_k(float v)
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, k3_expf(-v)));
 }
 
+// Dynamic shared memory: phase 1 holds the CTA's two weight rows and x (bulk copies);
+// phase 2 (the last CTA only, after phase 1) reuses it for the keys and the exact path.
 template <typename WT>
 __host__ __device__ inline size_t fused_smem_bytes(int hidden, int n_experts)
 {
-    return (size_t)128 * seg_xpitch(hidden) + (size_t)128 * seg_wpitch<WT>(hidden) +
-           (size_t)n_experts * (3 * sizeof(float) + 2 * sizeof(int) + 1) + 16;
+    const size_t p2 = (size_t)128 * seg_xpitch(hidden) + (size_t)128 * seg_wpitch<WT>(hidden) +
+                      (size_t)n_experts * (3 * sizeof(float) + 2 * sizeof(int) + 1) + 16;
+    const size_t p1 = (size_t)2 * hidden * sizeof(WT) + (size_t)hidden * sizeof(float);
+    return p1 > p2 ? p1 : p2;
 }
 
 template <typename WT>
@@ -684,34 +695,50 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
         const int nj = hidden >> 10;                     // chunks per lane
         const int cbase = q * (hidden >> 5) + lane;
         const bool act0 = e0 < E, act1 = e0 + 1 < E;
-        const WT *row0 = W + (size_t)e0 * hidden;
-        const WT *row1 = W + (size_t)(e0 + 1) * hidden;
-        double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
-        float a[2] = {0.0f, 0.0f};
-        WChunk<WT> wv[2][8];
-        // the first batch of weights before waiting for the kernel that writes x (weights
-        // never depend on it), so their latency overlaps that kernel's tail
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            if (j < nj) {
-                const int c = cbase + 32 * j;
-                if (act0) wv[0][j].load(row0, c);
-                if (act1) wv[1][j].load(row1, c);
-            }
+        const int nrows = act1 ? 2 : 1;
+        // the CTA's weight rows (adjacent: one copy) and x arrive by bulk copies into
+        // shared memory, the rows before the programmatic wait (weights never depend on
+        // the kernel before), x after it
+        __shared__ __align__(8) unsigned long long p1_bar[2];
+        __shared__ int p1_abort;
+        WT *wsm = reinterpret_cast<WT *>(rsm);
+        float *xsm = reinterpret_cast<float *>(rsm + (size_t)2 * hidden * sizeof(WT));
+        const uint32_t b_w = bulk::saddr(&p1_bar[0]), b_x = bulk::saddr(&p1_bar[1]);
+        if (threadIdx.x == 0) {
+            bulk::mbar_init(b_w, 1);
+            bulk::mbar_init(b_x, 1);
+            p1_abort = 0;
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            const uint32_t wbytes = (uint32_t)((size_t)nrows * hidden * sizeof(WT));
+            bulk::mbar_expect_tx(b_w, wbytes);
+            bulk::g2s(bulk::saddr(wsm), W + (size_t)e0 * hidden, wbytes, b_w);
         }
         pdl_wait();
         pdl_trigger();
+        if (threadIdx.x == 0) {
+            bulk::mbar_expect_tx(b_x, (uint32_t)(hidden * sizeof(float)));
+            bulk::g2s(bulk::saddr(xsm), xt, (uint32_t)(hidden * sizeof(float)), b_x);
+        }
+        __syncthreads();                                  // the barriers are initialised
+        // bounded waits: on a time-out the error flag is raised and the (stale) contents are
+        // used, so that the completion count still finishes and resets
+        bulk::mbar_wait(b_w, 0, &p1_abort, K3_SITE_ROUTER, 1);
+        bulk::mbar_wait(b_x, 0, &p1_abort, K3_SITE_ROUTER, 2);
+        const WT *row0 = wsm;
+        const WT *row1 = wsm + hidden;
+        double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
+        float a[2] = {0.0f, 0.0f};
+        WChunk<WT> wv[2][8];
         for (int j0 = 0; j0 < nj; j0 += 8) {
             float4 xv[8][2];
-            // every load of the batch is issued before any arithmetic
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 if (j0 + j < nj) {
                     const int c = cbase + 32 * (j0 + j);
-                    xv[j][0] = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c);
-                    xv[j][1] = __ldg(reinterpret_cast<const float4 *>(xt) + 2 * c + 1);
-                    if (j0 > 0 && act0) wv[0][j].load(row0, c);
-                    if (j0 > 0 && act1) wv[1][j].load(row1, c);
+                    xv[j][0] = reinterpret_cast<const float4 *>(xsm)[2 * c];
+                    xv[j][1] = reinterpret_cast<const float4 *>(xsm)[2 * c + 1];
+                    if (act0) wv[0][j].load_s(row0, c);
+                    if (act1) wv[1][j].load_s(row1, c);
                 }
             }
 #pragma unroll
@@ -769,11 +796,12 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
             J.lo[tE + e] = lo;
             J.hi[tE + e] = hi;
             J.score[tE + e] = sc;
-            __threadfence();
         }
         __syncthreads();
-        // one arrival per CTA (both writers fenced their stores before the barrier); the
-        // CTA that completes the count acquires every other CTA's stores
+        // one arrival per CTA: after the barrier, thread 0's gpu-scope fence (cumulative over
+        // the stores the barrier ordered before it) publishes both writers' stores, then the
+        // count; the CTA that completes it acquires every other CTA's stores
+        if (threadIdx.x == 0) __threadfence();
         if (threadIdx.x == 0 && atom_add_acq_rel(&g_router_ctr[t], 1u) == gridDim.x - 1) {
             g_router_ctr[t] = 0;
             s_last = 1;

@@ -1,7 +1,8 @@
 """The KDA decode layer (k3d_kda_layer_decode: projections, per-head step, output
-projection) on random bf16 weights: the cluster head kernel (default), the register-column
-kernel (k3d_set_kda_head_kernel(2)) and the shared-tile kernel (1) bit for bit, output and
-state, over two steps (the conv history shifts); and against the oracle's k3_kda_layer."""
+projection) on random bf16 weights: the default choice, the shared-tile head kernel
+(k3d_set_kda_head_kernel(1)), the register-column kernel (2) and the cluster kernel (3) bit
+for bit, output and state, over two steps (the conv history shifts); and against the
+oracle's k3_kda_layer."""
 import ctypes
 
 import numpy as np
@@ -64,7 +65,7 @@ def test_register_head_matches_shared_tile_head(k3, H, D, B, hidden):
     h0 = g.standard_normal((B, hidden)).astype(np.float32)
     res = {}
     try:
-        for kind in (1, 2, 0):
+        for kind in (1, 2, 3, 0):
             k3cuda.check(k3.k3d_set_kda_head_kernel(kind))
             h, st = h0.copy(), state0.copy()
             for x in xs:
@@ -72,7 +73,7 @@ def test_register_head_matches_shared_tile_head(k3, H, D, B, hidden):
             res[kind] = (h, st)
     finally:
         k3cuda.check(k3.k3d_set_kda_head_kernel(0))
-    for kind in (0, 2):
+    for kind in (0, 2, 3):
         assert np.array_equal(res[kind][1], res[1][1]), kind
         assert np.array_equal(res[kind][0], res[1][0]), kind
     assert not np.array_equal(res[0][1], state0)
