@@ -560,7 +560,7 @@ def bench_moe_a2a(args, rank, world):
     lib.k3d_host_free(hy)
     B = T * world
     return {
-        "metric": METRIC, "value": B * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "metric": METRIC, "value": (B * world if mode_a else B) * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
@@ -716,7 +716,7 @@ def bench_kda_prefill(args, rank, world):
 
 
 # ----------------------------------------------------------------- stack (config 4) ----
-def stack_cfg(world, rank, batch, cap, layout=1):
+def stack_cfg(world, rank, batch, cap, layout=1, ep_tokens=0):
     import k3cuda
     sc = k3cuda.K3dStackCfg()
     sc.hidden, sc.vocab, sc.n_layers, sc.eps = HIDDEN, 163840, 8, 1e-6
@@ -729,16 +729,31 @@ def stack_cfg(world, rank, batch, cap, layout=1):
     for i in range(16):
         sc.mla_layers[i] = (3, 7)[i] if i < 2 else -1
     sc.batch, sc.ctx_cap = batch, cap
+    sc.ep_tokens = ep_tokens
     return sc
 
 
 def stack_config(args, world):
     """The workload description both arms print (the reference arm times the same model)."""
+    mode_a = stack_mode_a(args, world)
     return {"workload": "config4 8-layer K3 stack decode", "batch": args.batch,
             "context": args.context, "hidden": HIDDEN,
             "layers": "KDA x6 + MLA x2 (one-based 4, 8); layer 0 dense 18432, layers 1-7 MoE "
-                      "384x top-8 + shared", "vocab": 163840, "parallelism": f"ep{world}",
+                      "384x top-8 + shared", "vocab": 163840,
+            "parallelism": f"ep{world}" + (f" mode A: {args.batch // world} sequences per rank, "
+                                           "device-planned all-to-all" if mode_a else ""),
             "l2": "per-step weight stream of GBs >> 126 MB L2 (no flush needed)"}
+
+
+def stack_mode_a(args, world):
+    """Mode A (each rank its own share of the batch, all-to-all MoE) for a batch split over
+    several ranks; Mode R (the batch replicated, experts split, NVLink push combine)
+    otherwise or when asked."""
+    if args.ep_mode == "r" or world == 1:
+        return False
+    if args.batch % world:
+        raise SystemExit(f"--batch {args.batch} does not split over {world} ranks")
+    return args.ep_mode == "a" or args.batch > 1
 
 
 def bench_stack(args, rank, world):
@@ -749,7 +764,9 @@ def bench_stack(args, rank, world):
     cap = ctx + args.steps * 2 + args.warmup * 2 + 16
     # the tcgen05 kernel streams experts stored in the tiled layout; the other two
     # kernels read the checkpoint layout
-    cfg = stack_cfg(world, rank, args.batch, cap, 1 if args.expert_kernel in (0, 3, 4) else 0)
+    mode_a = stack_mode_a(args, world)
+    B = args.batch // world if mode_a else args.batch      # this rank's sequences
+    cfg = stack_cfg(world, rank, B, cap, 1 if args.expert_kernel in (0, 3, 4) else 0, 1 if mode_a else 0)
     t0 = time.time()
     model = lib.k3d_model_create(C.byref(cfg), 2024)
     if not model:
@@ -757,7 +774,6 @@ def bench_stack(args, rank, world):
     k3cuda.check(lib.k3d_model_fill_context(model, ctx, 77))
     k3cuda.check(lib.k3d_sync())
     init_s = time.time() - t0
-    B = args.batch
     ids = k3cuda.DevBuf(B * 4, lib)
     nxt = k3cuda.DevBuf(B * 4, lib)
     k3cuda.check(lib.k3d_fill_i32_uniform(ids.ptr, B, 5, 0, 163839))
@@ -814,7 +830,7 @@ def bench_stack(args, rank, world):
     if uniq <= 0:
         uniq = TOPK * B
     alg_exp = uniq * EXPERT_BYTES + TOPK * B * (INTER * 8 + HIDDEN * 4) + HIDDEN * 4 * B
-    if world > 1:
+    if world > 1 and not mode_a:
         alg_exp /= world
     achieved = alg_exp / (exp_ms * 1e-3) / 1e9
     # end to end through the public API with host buffers: token ids in from host memory,
@@ -851,7 +867,8 @@ def bench_stack(args, rank, world):
                           "achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm},
         "sections_ms": sections,
-        "e2e": {"value": B * e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+        "e2e": {"value": (B * world if mode_a else B) * e2e_steps / e2e_s, "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B, "steps": e2e_steps,
                 "tokens_fnv1a": fnv1a(gen), "first_tokens": gen[:8, 0].tolist()},
         "gpu_launches": int(round(launches_per_step * args.steps)),
@@ -921,6 +938,10 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=8192,
                     help="kda_prefill workload: tokens per step (config 3: 8192)")
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ep-mode", choices=("auto", "r", "a"), default="auto",
+                    help="stack under expert parallelism: r = the batch replicated on every rank "
+                         "(push combine), a = the batch split over the ranks (device-planned "
+                         "all-to-all); auto = a when the batch is above 1")
     ap.add_argument("--tokens", type=int, default=1,
                     help="moe workload: tokens per step (config 1 lists T = 1, 8, 64, 512)")
     ap.add_argument("--context", type=int, default=4096)

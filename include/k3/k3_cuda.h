@@ -398,6 +398,14 @@ size_t k3d_moe_a2a_ws_bytes(const K3dMoeShape *s, int t_max, int nranks);
 int    k3d_moe_swiglu_a2a(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s,
                           int T, int t_max, int accumulate, int *idx, float *wts,
                           void *ws, size_t ws_bytes);
+/* Mode A planned on the device, for graph capture: the same rows, experts and top-k
+ * combine (bit-identical results), but every rank passes the same T (its own tokens),
+ * the dispatch plan is computed by a kernel, and each exchange moves fixed regions of
+ * T * topk rows per pair of ranks (grouped NCCL send/recv of fixed sizes), so nothing is
+ * read back to the host. More NVLink traffic than k3d_moe_swiglu_a2a (the full region
+ * whatever the routing); the workspace is k3d_moe_a2a_ws_bytes(s, T, nranks). */
+int    k3d_moe_swiglu_a2a_dev(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s,
+                              int T, int accumulate, int *idx, float *wts, void *ws, size_t ws_bytes);
 /* The Mode A dispatch plan, on HOST arrays (no device work): for assignments idx[TK]
  * (expert ids), cnt[r] rows go to rank r (expert e on rank e / (n_experts / nranks)),
  * rank r's rows start at row off[r] of the send buffer, each rank's rows in assignment
@@ -423,6 +431,14 @@ typedef struct {
      * tensor-core GEMM) and cache */
     int   batch;
     int   ctx_cap;
+    /* Under expert parallelism: 0 (Mode R) every rank steps the same batch (attention and
+     * router replicated, the MoE partials summed by the NVLink push combine, the shared
+     * expert and the LM head split over the ranks); 1 (Mode A) every rank steps its OWN
+     * batch of `batch` sequences (rank r holds the global sequences [r batch, (r + 1)
+     * batch)) with the whole shared expert and LM head, and each MoE layer exchanges rows
+     * with k3d_moe_swiglu_a2a_dev, so the step stays one CUDA graph. Every rank passes the
+     * same batch. Ignored on one rank except that Mode A's MoE path is taken. */
+    int   ep_tokens;
 } K3dStackCfg;
 
 typedef struct K3dModel K3dModel;

@@ -646,14 +646,91 @@ __global__ void k_a2a_combine(float *out, const float *back, const int *pos, con
     *o = accumulate ? __fadd_rn(*o, acc) : acc;
 }
 
+// Device-planned dispatch (k3d_moe_swiglu_a2a_dev): send row (r, p) = x[a / K] for the
+// p-th assignment a (in assignment order) whose expert rank r owns, in rank r's region of
+// cap = t_max * topk rows; meta[r][0] = that region's row count, meta[r][1 + p] = the
+// expert id; pos[a] = r * cap + p. CTA a counts the earlier assignments bound for its rank
+// itself (TK <= a few thousand), CTA 0 also writes every region's count. grid TK, 256
+// threads.
+__global__ void k_a2a_pack_dev(float *send, int *meta, int *pos, const float *x, const int *idx, int TK,
+                               int K, int hidden, int per, int nranks, int cap)
+{
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int s_cnt[8 * 32];
+    const int a = blockIdx.x, tid = threadIdx.x;
+    const int e = idx[a];
+    const bool ok = e >= 0 && e < per * nranks;
+    const int r = ok ? e / per : 0;
+    int c = 0;
+    for (int b = tid; b < a; b += blockDim.x) {
+        const int eb = idx[b];
+        c += (eb >= 0 && eb < per * nranks ? eb / per : 0) == r;
+    }
+    c = __reduce_add_sync(0xffffffffu, c);
+    if ((tid & 31) == 0) s_cnt[tid >> 5] = c;
+    if (a == 0)
+        for (int q = tid; q < nranks; q += blockDim.x) s_cnt[32 + q] = 0;
+    __syncthreads();
+    int p = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) p += s_cnt[w];
+    if (a == 0) {
+        for (int b = tid; b < TK; b += blockDim.x) {
+            const int eb = idx[b];
+            atomicAdd(&s_cnt[32 + (eb >= 0 && eb < per * nranks ? eb / per : 0)], 1);
+        }
+        __syncthreads();
+        for (int q = tid; q < nranks; q += blockDim.x) meta[(size_t)q * (cap + 1)] = s_cnt[32 + q];
+    }
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(a / K) * hidden);
+    float4 *dst = reinterpret_cast<float4 *>(send + ((size_t)r * cap + p) * hidden);
+    for (int i = tid; i < hidden / 4; i += blockDim.x) dst[i] = src[i];
+    if (tid == 0) {
+        meta[(size_t)r * (cap + 1) + 1 + p] = ok ? e : -1;
+        pos[a] = r * cap + p;
+    }
+}
+
+// Received rows: ids[s * cap + p] = the expert id of row p from rank s, or -1 past that
+// rank's count (skipped by the grouping). grid ceil(nranks * cap / 256), 256 threads.
+__global__ void k_a2a_mask_dev(int *ids, const int *meta, int nranks, int cap)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int a = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a >= nranks * cap) return;
+    const int s = a / cap, p = a % cap;
+    const int *m = meta + (size_t)s * (cap + 1);
+    ids[a] = p < m[0] ? m[1 + p] : -1;
+}
+
+// dst[a] = src[pos_of[a]] for the rows with an expert id (ids[a] >= 0); zero rows for the
+// others (their pos_of is not written). grid = rows, 256 threads.
+__global__ void k_gather_rows_masked(float *dst, const float *src, const int *pos_of, const int *ids, int hidden)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int a = blockIdx.x;
+    float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)a * hidden);
+    if (__ldcg(ids + a) < 0) {
+        for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) d4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
+    const float4 *s4 = reinterpret_cast<const float4 *>(src + (size_t)__ldcg(pos_of + a) * hidden);
+    for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
+}
+
 // Workspace of k3d_moe_swiglu_a2a: at most t_max tokens on any rank, so a rank receives at
-// most nranks * t_max * topk rows.
+// most nranks * t_max * topk rows. The device-planned form uses fixed regions of cap =
+// t_max * topk rows per rank in its send, receive and return buffers.
 struct A2aWs {
     int *idx; float *wts; void *router; float *sh_act, *sh_out;
     int *pos, *cnt_s, *cnt_r;
     float *sendbuf, *recvbuf, *back;
     int *send_ids, *recv_ids;
     int *n_active, *act_expert, *act_off, *assign;
+    float *send_dev, *back_dev;
+    int *meta_s, *meta_r;
     ExpertBufs eb;
     size_t total;
 };
@@ -682,6 +759,10 @@ static A2aWs a2a_ws_layout(const K3dMoeShape *s, int t_max, int nranks, void *ba
     L.act_expert = (int *)take((size_t)s->n_experts * sizeof(int));
     L.act_off = (int *)take(((size_t)s->n_experts + 1) * sizeof(int));
     L.assign = (int *)take(R * sizeof(int));
+    L.send_dev = (float *)take(R * s->hidden * sizeof(float));
+    L.back_dev = (float *)take(R * s->hidden * sizeof(float));
+    L.meta_s = (int *)take((size_t)nranks * (TK + 1) * sizeof(int));
+    L.meta_r = (int *)take((size_t)nranks * (TK + 1) * sizeof(int));
     expert_bufs_layout(L.eb, s, R, R, take);
     L.total = off;
     return L;
@@ -1031,3 +1112,115 @@ int k3d_moe_last_unique(void)
 }
 
 }  // extern "C"
+
+// Mode A planned on the device: the same rows and arithmetic as k3d_moe_swiglu_a2a, but the
+// dispatch plan (which rank, which row) is computed by k_a2a_pack_dev and every exchange
+// moves fixed regions of cap = T * topk rows per pair, whatever the routing, so no size
+// reaches the host and the whole layer can be captured into a CUDA graph. The price is
+// traffic: each pair exchanges cap rows both ways instead of the rows routed to it.
+extern "C" int k3d_moe_swiglu_a2a_dev(float *out, const float *x, const K3dMoeW *w, const K3dMoeShape *s,
+                                      int T, int accumulate, int *idx, float *wts, void *ws, size_t ws_bytes)
+{
+    K3_TRY(ensure_ctx());
+    K3_TRY(check_shape(s, T));
+    const int G = k3d_ep_size(), rank = k3d_ep_rank();
+    if (!out || !x || !w || !ws || !w->router_w || !w->experts)
+        return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a_dev null pointer");
+    if (s->n_experts % G) return fail(K3D_EINVAL, "moe a2a: %d experts over %d ranks", s->n_experts, G);
+    const int per = s->n_experts / G;
+    if (s->expert_lo != rank * per || s->expert_hi != (rank + 1) * per)
+        return fail(K3D_EINVAL, "moe a2a: rank %d owns experts [%d, %d), not [%d, %d)", rank, rank * per,
+                    (rank + 1) * per, s->expert_lo, s->expert_hi);
+    if (s->shared_inter > 0 && s->add_shared && (!w->sh_gate || !w->sh_up || !w->sh_down))
+        return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a_dev shared expert weights missing");
+    if (ws_bytes < k3d_moe_a2a_ws_bytes(s, T, G)) return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a_dev workspace too small");
+    if (((uintptr_t)x | (uintptr_t)ws) & 15u) return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a_dev alignment");
+    if (s->hidden % 4) return fail(K3D_EINVAL, "k3d_moe_swiglu_a2a_dev: hidden %% 4");
+    cudaStream_t st = stream();
+    A2aWs L = a2a_ws_layout(s, T, G, ws);
+    const int K = s->topk, TK = T * K, cap = TK, R = G * cap;
+    int *I = idx ? idx : L.idx;
+    float *Wt = wts ? wts : L.wts;
+
+    const bool shared = s->shared_inter > 0 && s->add_shared;
+    cudaStream_t sst = (!profiling() && side_stream()) ? side_stream() : st;
+    if (shared) {
+        if (sst != st && (cudaEventRecord(side_event(0), st) != cudaSuccess ||
+                          cudaStreamWaitEvent(sst, side_event(0), 0) != cudaSuccess))
+            return fail(K3D_ECUDA, "moe a2a: fork to the side stream");
+        prof_begin("moe.shared");
+        K3_TRY(gemv_bf16_swiglu(L.sh_act, x, w->sh_gate, w->sh_up, s->hidden, s->shared_inter, T, sst));
+        K3_TRY(gemv_bf16(L.sh_out, L.sh_act, w->sh_down, s->shared_inter, s->hidden, T, 0, sst));
+        prof_end("moe.shared");
+        if (sst != st && cudaEventRecord(side_event(1), sst) != cudaSuccess)
+            return fail(K3D_ECUDA, "moe a2a: side stream join event");
+    }
+    prof_begin("moe.router");
+    K3_TRY(router_bf16(I, Wt, x, w->router_w, w->router_bias, T, s->hidden, s->n_experts, K, s->renorm,
+                       s->routed_scale, L.router, st));
+    prof_end("moe.router");
+
+    prof_begin("ep.dispatch");
+    launch_pdl(k_a2a_pack_dev, dim3(TK), dim3(256), 0, st, L.send_dev, L.meta_s, L.pos, x, (const int *)I, TK, K,
+               s->hidden, per, G, cap);
+    note_launch();
+    K3_TRY(check_launch("moe a2a pack"));
+    const size_t rowb = (size_t)s->hidden * sizeof(float), metab = (size_t)(cap + 1) * sizeof(int);
+    std::vector<size_t> rb(G, (size_t)cap * rowb), ro(G), mb(G, metab), mo(G);
+    for (int r = 0; r < G; r++) { ro[r] = (size_t)r * cap * rowb; mo[r] = (size_t)r * metab; }
+    K3_TRY(ep_exchange(L.meta_s, mb.data(), mo.data(), L.meta_r, mb.data(), mo.data(), st));
+    K3_TRY(ep_exchange(L.send_dev, rb.data(), ro.data(), L.recvbuf, rb.data(), ro.data(), st));
+    launch_pdl(k_a2a_mask_dev, dim3((R + 255) / 256), dim3(256), 0, st, L.recv_ids, (const int *)L.meta_r, G, cap);
+    note_launch();
+    K3_TRY(check_launch("moe a2a mask"));
+    prof_end("ep.dispatch");
+
+    // this rank's experts over the rows it may have received: one assignment per row, the
+    // rows past a sender's count carry id -1 and stay out of the work list
+    const size_t smem = 2 * (size_t)s->n_experts * sizeof(int);
+    launch_pdl(k_moe_prep, dim3(1), dim3(1024), smem, st, (const int *)L.recv_ids, R, s->n_experts, s->expert_lo,
+               s->expert_hi, L.n_active, L.act_expert, L.act_off, L.assign, L.eb.fcnt, L.eb.fcnt_n);
+    note_launch();
+    K3_TRY(check_launch("moe a2a prep"));
+    MoeWork mw{};
+    mw.table = w->experts;
+    mw.n_active = L.n_active;
+    mw.act_expert = L.act_expert;
+    mw.act_off = L.act_off;
+    mw.assign = L.assign;
+    mw.K = 1;
+    mw.n_experts = s->n_experts;
+    ExpertOut O{L.eb.contrib, 1, 0};
+    const int umax = std::min(R, per);
+    prof_begin("moe.experts");
+    K3_TRY(run_experts(mw, L.recv_ids, L.n_active + 1, umax, L.recvbuf, R, R, s->hidden, s->inter,
+                       s->expert_layout, L.eb, O, st));
+    prof_end("moe.experts");
+    const float *ybuf = O.contrib;
+    if (O.pos_of) {
+        const float *src = O.contrib;
+        if (O.ks > 1) {
+            K3_TRY(umma_slice_sum(L.eb.contrib, O.contrib, O.ks, O.slice, (int)((size_t)R * s->hidden), st));
+            src = L.eb.contrib;
+        }
+        launch_pdl(k_gather_rows_masked, dim3((unsigned)R), dim3(256), 0, st, L.recvbuf, src, O.pos_of,
+                   (const int *)L.recv_ids, s->hidden);
+        note_launch();
+        K3_TRY(check_launch("moe a2a gather"));
+        ybuf = L.recvbuf;
+    } else if (O.ks > 1) {
+        K3_TRY(umma_slice_sum(L.eb.contrib, O.contrib, O.ks, O.slice, (int)((size_t)R * s->hidden), st));
+        ybuf = L.eb.contrib;
+    }
+    // results back: the region of rows received from rank r returns to rank r
+    prof_begin("ep.combine");
+    K3_TRY(ep_exchange(ybuf, rb.data(), ro.data(), L.back_dev, rb.data(), ro.data(), st));
+    prof_end("ep.combine");
+    if (shared && sst != st && cudaStreamWaitEvent(st, side_event(1), 0) != cudaSuccess)
+        return fail(K3D_ECUDA, "moe a2a: join from the side stream");
+    dim3 grid((s->hidden + 255) / 256, T);
+    launch_pdl(k_a2a_combine, dim3(grid), dim3(256), 0, st, out, (const float *)L.back_dev, (const int *)L.pos,
+               (const float *)Wt, shared ? (const float *)L.sh_out : nullptr, s->hidden, K, accumulate);
+    note_launch();
+    return check_launch("moe a2a combine");
+}

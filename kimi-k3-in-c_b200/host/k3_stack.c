@@ -163,7 +163,10 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
     int sh_lo = 0;
     {
         const int nr = k3d_ep_size(), r = k3d_ep_rank();
-        if (nr > 1 && sh_full > 0 && sh_full % (8 * nr) == 0) {
+        if (m->c.ep_tokens) {
+            /* Mode A: every rank's own tokens through the whole shared expert */
+            m->c.moe.add_shared = 1;
+        } else if (nr > 1 && sh_full > 0 && sh_full % (8 * nr) == 0) {
             m->c.moe.shared_inter = sh_full / nr;
             m->c.moe.add_shared = 1;
             sh_lo = r * (sh_full / nr);
@@ -183,7 +186,7 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
     {
         /* under EP each rank holds one slice of the LM head: the same rows of the same
          * seeded matrix a single GPU holds, so the argmax over the slices is the same */
-        const int nr = k3d_ep_size(), r = k3d_ep_rank();
+        const int nr = c->ep_tokens ? 1 : k3d_ep_size(), r = c->ep_tokens ? 0 : k3d_ep_rank();
         m->v0 = (int)((long long)r * c->vocab / nr);
         m->vshard = (int)((long long)(r + 1) * c->vocab / nr) - m->v0;
         const uint64_t sd = next_seed(m);
@@ -343,7 +346,8 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
                 k3d_free(full);
                 L->moe.sh_down = pd;
             }
-            const size_t w = k3d_moe_ws_bytes(&c->moe, B);
+            const size_t w = c->ep_tokens ? k3d_moe_a2a_ws_bytes(&c->moe, B, k3d_ep_size())
+                                          : k3d_moe_ws_bytes(&c->moe, B);
             if (w > ws) ws = w;
         }
     }
@@ -367,7 +371,7 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
         if (!err && k3d_memset(m->pos, 0, 16)) err = 1;
         if (!err && k3d_sync()) err = 1;
         /* the peer buffers of the MoE combine (every rank maps every other rank's) */
-        if (!err && k3d_ep_size() > 1 && k3d_ep_peer_init((size_t)B * E)) err = 1;
+        if (!err && k3d_ep_size() > 1 && !c->ep_tokens && k3d_ep_peer_init((size_t)B * E)) err = 1;
     }
     if (m->stage_expert) {
         if (k3d_sync()) err = 1;
@@ -396,22 +400,25 @@ int k3d_model_fill_context(K3dModel *m, int len, uint64_t seed)
     if (!m || len < 0 || len >= m->c.ctx_cap) return K3D_EINVAL;
     const K3dStackCfg *c = &m->c;
     const int B = c->batch;
+    /* the seeds follow the global sequence index: under Mode A rank r's sequences are the
+     * batch's [r B, (r + 1) B), filled as one GPU holding the whole batch fills them */
+    const int g0 = c->ep_tokens ? k3d_ep_rank() * B : 0;
     for (int l = 0; l < c->n_layers; l++) {
         K3sLayer *L = &m->L[l];
         if (L->is_mla) {
             const int kvw = c->mla.kv_lora + c->mla.qk_rope;
             for (int b = 0; b < B && len > 0; b++) {
                 int r = k3d_fill_bf16_normal(L->cache + (size_t)b * c->ctx_cap * kvw,
-                                             (size_t)len * kvw, seed * 131 + l * 17 + b, 1.0f);
+                                             (size_t)len * kvw, seed * 131 + l * 17 + (g0 + b), 1.0f);
                 if (r) return r;
             }
         } else {
             const size_t sf = k3d_kda_state_floats(&L->kshape);
             const size_t ns = (size_t)L->kshape.heads * L->kshape.head_dim * L->kshape.head_dim;
             for (int b = 0; b < B; b++) {
-                int r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf, ns, seed * 137 + l * 19 + b, 0.01f);
+                int r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf, ns, seed * 137 + l * 19 + (g0 + b), 0.01f);
                 if (!r) r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf + ns, sf - ns,
-                                                seed * 139 + l * 23 + b, 1.0f);
+                                                seed * 139 + l * 23 + (g0 + b), 1.0f);
                 if (r) return r;
             }
         }
@@ -442,6 +449,11 @@ static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
         if (L->is_dense) {
             TRY(k3d_swiglu_mlp_bf16(m->h, m->xn, L->dg, L->du, L->dd, E, c->dense_inter, B, 1,
                                     m->mlp_ws));
+        } else if (c->ep_tokens) {
+            /* Mode A: this rank's tokens' rows to their experts' ranks and back, planned on
+             * the device (fixed-size exchanges), the top-k sum and the shared expert added
+             * into the residual */
+            TRY(k3d_moe_swiglu_a2a_dev(m->h, m->xn, &L->moe, &c->moe, B, 1, NULL, NULL, m->ws, m->ws_bytes));
         } else if (ep) {
             /* this rank's experts (and shared-expert slice), then the NVLink push combine
              * that sums every rank's partial into the residual */

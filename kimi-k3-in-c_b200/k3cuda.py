@@ -115,7 +115,7 @@ class K3dStackCfg(C.Structure):
                 ("kda_heads", i32), ("kda_head_dim", i32), ("conv_k", i32), ("gate_lb", f32),
                 ("mla", K3dMlaShape), ("moe", K3dMoeShape), ("first_dense", i32),
                 ("dense_inter", i32), ("mla_layers", i32 * 16), ("batch", i32),
-                ("ctx_cap", i32)]
+                ("ctx_cap", i32), ("ep_tokens", i32)]
 
 
 # name -> (restype, argtypes)
@@ -256,6 +256,7 @@ _PROTOS = {
     "k3d_ep_peer_init": (i32, [C.c_size_t]),
     "k3d_ep_combine_add": (i32, [vp, vp, C.c_size_t, i32]),
     "k3d_moe_a2a_ws_bytes": (sz, [C.POINTER(K3dMoeShape), i32, i32]),
+    "k3d_moe_swiglu_a2a_dev": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, vp, vp, vp, sz]),
     "k3d_moe_swiglu_a2a": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, i32, vp,
                                  vp, vp, sz]),
     "k3d_a2a_plan": (i32, [vp, i32, i32, i32, vp, vp, vp]),
@@ -466,6 +467,11 @@ class MoeWeights:
         """Mode A: this rank's own T tokens, experts dispatched to their ranks."""
         return self.lib.k3d_moe_swiglu_a2a(out, x, C.byref(self.w), C.byref(self.shape), T, t_max,
                                            accumulate, idx, wts, ws, ws_bytes)
+
+    def run_a2a_dev(self, out, x, T, ws, ws_bytes, accumulate=0, idx=None, wts=None):
+        """Mode A planned on the device (graph-capturable): every rank passes the same T."""
+        return self.lib.k3d_moe_swiglu_a2a_dev(out, x, C.byref(self.w), C.byref(self.shape), T, accumulate,
+                                               idx, wts, ws, ws_bytes)
 
 
 def a2a_plan(idx, n_experts, nranks, lib=None):

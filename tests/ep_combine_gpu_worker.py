@@ -131,3 +131,65 @@ def run_stack(rank, world, port, seed, batch):
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+def run_stack_mode_a(rank, world, port, seed, batch):
+    """Mode A: the batch split over the ranks (rank r steps the global sequences
+    [r b, (r + 1) b), b = batch / world, with its own caches), experts split, every MoE layer
+    through the device-planned all-to-all; eager, captured, replayed. Rank 0 then steps the
+    whole batch on one GPU: the ranks' logits put together within 1e-5 and the same tokens."""
+    lib, dist, torch = _setup(rank, world, port)
+    import k3cuda
+    from test_gpu_stack import CFG, make_cfg, download
+    try:
+        c = CFG
+        E, V = c["moe"]["n_experts"], c["vocab"]
+        b = batch // world
+
+        def steps(model, toks, nb):
+            out, logs = [], []
+            for step in range(3):
+                nxt = np.zeros(nb, np.int32)
+                k3cuda.check(lib.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
+                logs.append(download(lib, model, "logits", np.float32)[:nb * V].reshape(nb, V).copy())
+                out.append(nxt.copy())
+                toks = nxt.copy()
+            return out, logs
+
+        toks_all = ((np.arange(batch) * 37 + 5) % V).astype(np.int32)
+        sc = make_cfg(c, batch=b, layout=1)
+        sc.moe.expert_lo, sc.moe.expert_hi = rank * E // world, (rank + 1) * E // world
+        sc.ep_tokens = 1
+        model = lib.k3d_model_create(ctypes.byref(sc), seed)
+        assert model, lib.k3d_last_message()
+        k3cuda.check(lib.k3d_model_fill_context(model, 6, 17))
+        toks_ep, logs_ep = steps(model, toks_all[rank * b:(rank + 1) * b].copy(), b)
+        lib.k3d_model_destroy(model)           # releases the graph (it holds NCCL calls)
+        k3cuda.check(lib.k3d_sync())
+        gathered = []
+        for s in range(3):
+            tl = [torch.zeros(b, dtype=torch.int32) for _ in range(world)]
+            dist.all_gather(tl, torch.from_numpy(toks_ep[s]))
+            ll = [torch.zeros(b * V, dtype=torch.float32) for _ in range(world)]
+            dist.all_gather(ll, torch.from_numpy(logs_ep[s].reshape(-1)))
+            gathered.append((np.concatenate([t.numpy() for t in tl]),
+                             np.concatenate([x.numpy().reshape(b, V) for x in ll])))
+        k3cuda.check(lib.k3d_ep_finalize())
+        if rank == 0:
+            sc1 = make_cfg(c, batch=batch, layout=1)
+            model = lib.k3d_model_create(ctypes.byref(sc1), seed)
+            assert model, lib.k3d_last_message()
+            k3cuda.check(lib.k3d_model_fill_context(model, 6, 17))
+            toks_1, logs_1 = steps(model, toks_all.copy(), batch)
+            lib.k3d_model_destroy(model)
+            for s in range(3):
+                t_ep, l_ep = gathered[s]
+                err = float(np.abs(l_ep - logs_1[s]).max() / np.abs(logs_1[s]).max())
+                assert err <= 1e-5, (s, err)
+                for q in range(batch):
+                    top2 = np.sort(logs_1[s][q])[-2:]
+                    if top2[1] - top2[0] > 1e-4 * np.abs(logs_1[s][q]).max():
+                        assert t_ep[q] == toks_1[s][q], (s, q)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()

@@ -1,5 +1,5 @@
 """Expert parallelism's MoE combine over NVLink peer memory (k3d_ep_combine_add) and the
-decode stack under expert parallelism, on two GPUs (one process per GPU, gloo for the
+decode stack under expert parallelism (Mode R, and Mode A with the batch split), on two GPUs (one process per GPU, gloo for the
 test's own bookkeeping, CUDA IPC for the peer buffers). On one GPU, the combine is the
 plain residual add."""
 import multiprocessing as mp
@@ -52,3 +52,10 @@ def test_push_combine_two_gpus_equals_rank_order_sum():
 def test_stack_two_gpus_matches_one_gpu(batch):
     import ep_combine_gpu_worker
     _run_two(ep_combine_gpu_worker.run_stack, 99, batch)
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("batch", [12, 64])
+def test_stack_mode_a_two_gpus_matches_one_gpu(batch):
+    import ep_combine_gpu_worker
+    _run_two(ep_combine_gpu_worker.run_stack_mode_a, 99, batch)

@@ -270,3 +270,33 @@ def test_stack_batch_decode_matches_oracle_per_sequence(k3, oracle, B):
             toks = nxt.copy()
     finally:
         k3.k3d_model_destroy(model)
+
+
+@pytest.mark.parametrize("B", [6, 64])
+def test_stack_mode_a_one_rank_matches_mode_r(k3, B):
+    """Mode A (ep_tokens = 1: every MoE layer through k3d_moe_swiglu_a2a_dev, the dispatch
+    planned on the device) on one rank steps like the replicated path: the same logits and
+    tokens, eager, captured and replayed."""
+    c = CFG
+    models = []
+    try:
+        for ep_tokens in (0, 1):
+            sc = make_cfg(c, batch=B, layout=1)
+            sc.ep_tokens = ep_tokens
+            m = k3.k3d_model_create(ctypes.byref(sc), 4321)
+            assert m, k3.k3d_last_message()
+            models.append(m)
+            k3cuda.check(k3.k3d_model_fill_context(m, 7, 55))
+        toks = ((np.arange(B) * 37 + 5) % c["vocab"]).astype(np.int32)
+        for step in range(3):              # eager, capture, replay
+            outs = []
+            for m in models:
+                nxt = np.zeros(B, np.int32)
+                k3cuda.check(k3.k3d_model_step_host(m, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
+                outs.append((nxt, download(k3, m, "logits", np.float32).copy()))
+            assert np.array_equal(outs[0][1], outs[1][1]), step
+            assert np.array_equal(outs[0][0], outs[1][0]), step
+            toks = outs[0][0].copy()
+    finally:
+        for m in models:
+            k3.k3d_model_destroy(m)
