@@ -123,6 +123,9 @@ int k3d_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float stddev);
 int k3d_fill_bf16_normal_at(uint16_t *dst, size_t n, uint64_t seed, float sd, size_t offset);
 int k3d_fill_f32_normal(float *dst, size_t n, uint64_t seed, float stddev);
 int k3d_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi);
+/* Slices of the same seeded streams: elements [offset, offset + n) of the fill above. */
+int k3d_fill_f32_normal_at(float *dst, size_t n, uint64_t seed, float sd, size_t offset);
+int k3d_fill_f32_uniform_at(float *dst, size_t n, uint64_t seed, float lo, float hi, size_t offset);
 /* E2M1 codes uniform over all 16 values; E8M0 bytes uniform in [s_lo, s_hi]. */
 int k3d_fill_mxfp4(unsigned char *packed, size_t packed_bytes,
                    unsigned char *scales, size_t scale_bytes,
@@ -278,6 +281,12 @@ int    k3d_kda_layer_decode(float *h, const float *xn, const K3dKdaW *w, const K
 int    k3d_kda_layer_decode_normed(float *h, const float *norm_w, float eps, const K3dKdaW *w,
                                    const K3dKdaShape *s, int B, float *state, void *ws,
                                    size_t ws_bytes);
+/* The same, with the layer's output written (accumulate = 0) or added (1) to out instead
+ * of the residual h it reads: a tensor-parallel rank's partial (its heads' share of the
+ * output projection), summed over the ranks afterwards. */
+int    k3d_kda_layer_decode_normed_out(float *out, const float *h, const float *norm_w, float eps,
+                                       const K3dKdaW *w, const K3dKdaShape *s, int B, float *state,
+                                       void *ws, size_t ws_bytes, int accumulate);
 /* Which kernel runs the per-head step of the decode layer: 0 (default) chooses 2 for up to
  * four sequences and 1 above; 1 stages the head's state tile in shared memory, one CTA per
  * head; 2 keeps each thread's state column in registers, one CTA per head; 3 splits each

@@ -35,18 +35,18 @@ __global__ void k_fill_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, float
         dst[i] = f32_to_bf16_bits(normal_at(seed, offset + i, sd));
 }
 
-__global__ void k_fill_f32_normal(float *dst, size_t n, uint64_t seed, float sd)
+__global__ void k_fill_f32_normal(float *dst, size_t n, uint64_t seed, float sd, size_t offset)
 {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
-        dst[i] = normal_at(seed, i, sd);
+        dst[i] = normal_at(seed, offset + i, sd);
 }
 
-__global__ void k_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi)
+__global__ void k_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi, size_t offset)
 {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
-        const uint64_t h = hash_at(seed, i);
+        const uint64_t h = hash_at(seed, offset + i);
         const float u = (float)(h >> 40) * (1.0f / 16777216.0f);   // [0, 1)
         dst[i] = lo + (hi - lo) * u;
     }
@@ -117,24 +117,34 @@ int k3d_fill_bf16_normal_at(uint16_t *dst, size_t n, uint64_t seed, float sd, si
     return check_launch("fill bf16 at");
 }
 
-int k3d_fill_f32_normal(float *dst, size_t n, uint64_t seed, float sd)
+int k3d_fill_f32_normal_at(float *dst, size_t n, uint64_t seed, float sd, size_t offset)
 {
     K3_TRY(ensure_ctx());
     if (!dst) return fail(K3D_EINVAL, "fill null pointer");
     if (!n) return K3D_OK;
-    k_fill_f32_normal<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, sd);
+    k_fill_f32_normal<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, sd, offset);
     note_launch();
     return check_launch("fill f32");
 }
 
-int k3d_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi)
+int k3d_fill_f32_normal(float *dst, size_t n, uint64_t seed, float sd)
+{
+    return k3d_fill_f32_normal_at(dst, n, seed, sd, 0);
+}
+
+int k3d_fill_f32_uniform_at(float *dst, size_t n, uint64_t seed, float lo, float hi, size_t offset)
 {
     K3_TRY(ensure_ctx());
     if (!dst) return fail(K3D_EINVAL, "fill null pointer");
     if (!n) return K3D_OK;
-    k_fill_f32_uniform<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, lo, hi);
+    k_fill_f32_uniform<<<grid_n(n), 256, 0, stream()>>>(dst, n, seed, lo, hi, offset);
     note_launch();
     return check_launch("fill uniform");
+}
+
+int k3d_fill_f32_uniform(float *dst, size_t n, uint64_t seed, float lo, float hi)
+{
+    return k3d_fill_f32_uniform_at(dst, n, seed, lo, hi, 0);
 }
 
 int k3d_fill_i32_uniform(int *dst, size_t n, uint64_t seed, int lo, int hi)

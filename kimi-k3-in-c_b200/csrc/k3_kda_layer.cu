@@ -519,7 +519,8 @@ static int g_kda_head_kernel = 0;
 
 // The layer; with ni, xn is the raw residual and the projection GEMV normalises it.
 static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K3dKdaW *w,
-                            const K3dKdaShape *s, int B, float *state, void *ws, size_t ws_bytes)
+                            const K3dKdaShape *s, int B, float *state, void *ws, size_t ws_bytes,
+                            int accumulate = 1)
 {
     K3_TRY(ensure_ctx());
     if (!h || !xn || !w || !s || !state || !ws) return fail(K3D_EINVAL, "kda layer null pointer");
@@ -577,7 +578,7 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
     K3_TRY(check_launch("kda head"));
     prof_end("kda.core");
     prof_begin("kda.proj_out");
-    K3_TRY(gemv_bf16(h, heads, w->o, P, s->hidden, B, 1, st));
+    K3_TRY(gemv_bf16(h, heads, w->o, P, s->hidden, B, accumulate, st));
     prof_end("kda.proj_out");
     return K3D_OK;
 }
@@ -604,6 +605,15 @@ int k3d_kda_layer_decode_normed(float *h, const float *norm_w, float eps, const 
     if (!norm_w) return fail(K3D_EINVAL, "kda layer: null norm weights");
     const NormIn ni{norm_w, eps};
     return kda_layer_decode(h, h, &ni, w, s, B, state, ws, ws_bytes);
+}
+
+int k3d_kda_layer_decode_normed_out(float *out, const float *h, const float *norm_w, float eps,
+                                    const K3dKdaW *w, const K3dKdaShape *s, int B, float *state,
+                                    void *ws, size_t ws_bytes, int accumulate)
+{
+    if (!norm_w || !out) return fail(K3D_EINVAL, "kda layer: null norm weights or output");
+    const NormIn ni{norm_w, eps};
+    return kda_layer_decode(out, h, &ni, w, s, B, state, ws, ws_bytes, accumulate ? 1 : 0);
 }
 
 }  // extern "C"

@@ -75,6 +75,12 @@ struct K3dModel {
     int nt;
     unsigned char *stage_expert;   /* creation only: checkpoint-layout expert before tiling */
     int sh_lo, sh_full;            /* this rank's first shared-expert row, and the full count */
+    /* tensor parallelism of the trunk under Mode R: a rank holds heads [h0, h0 + nh) of
+     * every KDA (and MLA) layer and rows [i0, i0 + ni) of the dense MLP, and its partial
+     * output is summed over the ranks by the push combine */
+    int tp_kda, tp_mla, tp_dense;
+    int kda_h0, mla_h0, dense_i0, dense_ni;
+    K3dMlaShape mla_loc;           /* the MLA shape this rank runs (its heads) */
 };
 
 static int is_mla_layer(const K3dStackCfg *c, int l)
@@ -136,13 +142,41 @@ static float *f32_uniform(K3dModel *m, const char *name, size_t n, float lo, flo
     return p;
 }
 
-static float *f32_normal(K3dModel *m, const char *name, size_t n, float sd, int *err)
+
+
+/* Slices of seeded parameters: exactly the bytes a single GPU's tensor holds there. */
+static uint16_t *bf16_rows(K3dModel *m, const char *name, size_t cols, size_t r0, size_t nr, float sd, int *err)
 {
-    float *p = (float *)dalloc(m, name, n * 4);
-    if (!p || k3d_fill_f32_normal(p, n, next_seed(m), sd)) { *err = 1; return NULL; }
+    uint16_t *p = (uint16_t *)dalloc(m, name, nr * cols * 2);
+    if (!p || k3d_fill_bf16_normal_at(p, nr * cols, next_seed(m), sd, r0 * cols)) { *err = 1; return NULL; }
     return p;
 }
 
+static uint16_t *bf16_cols(K3dModel *m, const char *name, size_t rows, size_t cols, size_t c0, size_t nc, float sd,
+                           int *err)
+{
+    uint16_t *p = (uint16_t *)dalloc(m, name, rows * nc * 2);
+    uint16_t *full = (uint16_t *)k3d_alloc(rows * cols * 2);
+    if (!p || !full || k3d_fill_bf16_normal(full, rows * cols, next_seed(m), sd) ||
+        k3d_copy2d(p, nc * 2, full + c0, cols * 2, nc * 2, rows) || k3d_sync())
+        *err = 1;
+    k3d_free(full);
+    return p;
+}
+
+static float *f32_normal_slice(K3dModel *m, const char *name, size_t i0, size_t n, float sd, int *err)
+{
+    float *p = (float *)dalloc(m, name, n * 4);
+    if (!p || k3d_fill_f32_normal_at(p, n, next_seed(m), sd, i0)) { *err = 1; return NULL; }
+    return p;
+}
+
+static float *f32_uniform_slice(K3dModel *m, const char *name, size_t i0, size_t n, float lo, float hi, int *err)
+{
+    float *p = (float *)dalloc(m, name, n * 4);
+    if (!p || k3d_fill_f32_uniform_at(p, n, next_seed(m), lo, hi, i0)) { *err = 1; return NULL; }
+    return p;
+}
 
 K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
 {
@@ -174,6 +208,20 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
     }
     m->sh_lo = sh_lo;
     m->sh_full = sh_full;
+    {
+        const int nr = k3d_ep_size(), r = k3d_ep_rank();
+        const int tp = nr > 1 && !m->c.ep_tokens;
+        const K3dMlaShape *ms = &m->c.mla;
+        m->tp_kda = tp && m->c.kda_heads % nr == 0;
+        m->tp_mla = tp && ms->n_heads % nr == 0 && (ms->n_heads / nr) % 8 == 0;
+        m->tp_dense = tp && m->c.dense_inter % (64 * nr) == 0;
+        m->kda_h0 = m->tp_kda ? r * (m->c.kda_heads / nr) : 0;
+        m->mla_h0 = m->tp_mla ? r * (ms->n_heads / nr) : 0;
+        m->dense_ni = m->tp_dense ? m->c.dense_inter / nr : m->c.dense_inter;
+        m->dense_i0 = m->tp_dense ? r * m->dense_ni : 0;
+        m->mla_loc = *ms;
+        if (m->tp_mla) m->mla_loc.n_heads = ms->n_heads / nr;
+    }
     const K3dStackCfg *c = &m->c;
     const int E = c->hidden, B = c->batch;
     const size_t P = (size_t)c->kda_heads * c->kda_head_dim;
@@ -211,12 +259,23 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             const int kvd = s->qk_nope + s->v_head;
 #define MLA_W(field, rows, cols) do { snprintf(nm, sizeof nm, "layer%d.mla." #field, l); \
             L->mla.field = bf16_param(m, nm, (size_t)(rows) * (cols), 0.02f, &err); } while (0)
+            /* under tensor parallelism: this rank's heads' rows of q_b, kv_b and g and
+             * columns of o; q_a, kv_a and the latent cache are replicated */
+            const size_t hl = (size_t)m->mla_loc.n_heads, h0 = (size_t)m->mla_h0;
             MLA_W(q_a, s->q_lora, E);
-            MLA_W(q_b, (size_t)s->n_heads * qh, s->q_lora);
+            snprintf(nm, sizeof nm, "layer%d.mla.q_b", l);
+            L->mla.q_b = bf16_rows(m, nm, s->q_lora, h0 * qh, hl * qh, 0.02f, &err);
             MLA_W(kv_a, kvw, E);
-            MLA_W(kv_b, (size_t)s->n_heads * kvd, s->kv_lora);
-            MLA_W(o, E, (size_t)s->n_heads * s->v_head);
-            if (s->out_gate) MLA_W(g, (size_t)s->n_heads * s->v_head, E);
+            snprintf(nm, sizeof nm, "layer%d.mla.kv_b", l);
+            L->mla.kv_b = bf16_rows(m, nm, s->kv_lora, h0 * kvd, hl * kvd, 0.02f, &err);
+            snprintf(nm, sizeof nm, "layer%d.mla.o", l);
+            L->mla.o = m->tp_mla ? bf16_cols(m, nm, E, (size_t)s->n_heads * s->v_head, h0 * s->v_head,
+                                              hl * s->v_head, 0.02f, &err)
+                                 : bf16_param(m, nm, (size_t)E * s->n_heads * s->v_head, 0.02f, &err);
+            if (s->out_gate) {
+                snprintf(nm, sizeof nm, "layer%d.mla.g", l);
+                L->mla.g = bf16_rows(m, nm, E, h0 * s->v_head, hl * s->v_head, 0.02f, &err);
+            }
 #undef MLA_W
             snprintf(nm, sizeof nm, "layer%d.mla.q_a_norm", l);
             L->mla.q_a_norm = f32_uniform(m, nm, s->q_lora, 0.9f, 1.1f, &err);
@@ -225,27 +284,35 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             snprintf(nm, sizeof nm, "layer%d.mla.cache", l);
             L->cache = (uint16_t *)dalloc(m, nm, (size_t)B * c->ctx_cap * kvw * 2);
             if (!L->cache || k3d_memset(L->cache, 0, (size_t)B * c->ctx_cap * kvw * 2)) err = 1;
-            const size_t w = k3d_mla_ws_bytes(&c->mla, B, c->ctx_cap);
+            const size_t w = k3d_mla_ws_bytes(&m->mla_loc, B, c->ctx_cap);
             if (w > ws) ws = w;
         } else {
+            /* under tensor parallelism this rank's heads [h0, h0 + hl): their rows of q, k, v,
+             * g, b and f_b, their columns of o, their channels' conv taps, decays and state */
+            const size_t hl = m->tp_kda ? (size_t)H / k3d_ep_size() : (size_t)H, h0 = (size_t)m->kda_h0;
+            const size_t Pl = hl * D, c0 = h0 * D;
             K3dKdaShape *ks = &L->kshape;
-            ks->hidden = E; ks->heads = H; ks->head_dim = D; ks->conv_k = c->conv_k;
+            ks->hidden = E; ks->heads = (int)hl; ks->head_dim = D; ks->conv_k = c->conv_k;
             ks->gate_lb = c->gate_lb; ks->eps = c->eps;
-#define KDA_W(field, rows, cols) do { snprintf(nm, sizeof nm, "layer%d.kda." #field, l); \
-            L->kda.field = bf16_param(m, nm, (size_t)(rows) * (cols), 0.02f, &err); } while (0)
-            KDA_W(q, P, E); KDA_W(k, P, E); KDA_W(v, P, E); KDA_W(g, P, E);
-            KDA_W(b, H, E); KDA_W(f_a, D, E); KDA_W(f_b, P, D); KDA_W(o, E, P);
-#undef KDA_W
+#define KDA_ROWS(field, cols, r0, nrow) do { snprintf(nm, sizeof nm, "layer%d.kda." #field, l); \
+            L->kda.field = bf16_rows(m, nm, (cols), (r0), (nrow), 0.02f, &err); } while (0)
+            KDA_ROWS(q, E, c0, Pl); KDA_ROWS(k, E, c0, Pl); KDA_ROWS(v, E, c0, Pl); KDA_ROWS(g, E, c0, Pl);
+            KDA_ROWS(b, E, h0, hl); KDA_ROWS(f_a, E, 0, (size_t)D); KDA_ROWS(f_b, (size_t)D, c0, Pl);
+#undef KDA_ROWS
+            snprintf(nm, sizeof nm, "layer%d.kda.o", l);
+            L->kda.o = m->tp_kda ? bf16_cols(m, nm, E, P, c0, Pl, 0.02f, &err)
+                                 : bf16_param(m, nm, (size_t)E * P, 0.02f, &err);
+            const size_t K4 = (size_t)c->conv_k;
             snprintf(nm, sizeof nm, "layer%d.kda.q_conv", l);
-            L->kda.q_conv = f32_normal(m, nm, P * c->conv_k, 0.5f, &err);
+            L->kda.q_conv = f32_normal_slice(m, nm, c0 * K4, Pl * K4, 0.5f, &err);
             snprintf(nm, sizeof nm, "layer%d.kda.k_conv", l);
-            L->kda.k_conv = f32_normal(m, nm, P * c->conv_k, 0.5f, &err);
+            L->kda.k_conv = f32_normal_slice(m, nm, c0 * K4, Pl * K4, 0.5f, &err);
             snprintf(nm, sizeof nm, "layer%d.kda.v_conv", l);
-            L->kda.v_conv = f32_normal(m, nm, P * c->conv_k, 0.5f, &err);
+            L->kda.v_conv = f32_normal_slice(m, nm, c0 * K4, Pl * K4, 0.5f, &err);
             snprintf(nm, sizeof nm, "layer%d.kda.A_log", l);
-            L->kda.A_log = f32_uniform(m, nm, H, 0.0f, 1.5f, &err);
+            L->kda.A_log = f32_uniform_slice(m, nm, h0, hl, 0.0f, 1.5f, &err);
             snprintf(nm, sizeof nm, "layer%d.kda.dt_bias", l);
-            L->kda.dt_bias = f32_normal(m, nm, P, 0.5f, &err);
+            L->kda.dt_bias = f32_normal_slice(m, nm, c0, Pl, 0.5f, &err);
             snprintf(nm, sizeof nm, "layer%d.kda.o_norm", l);
             L->kda.o_norm = f32_uniform(m, nm, D, 0.9f, 1.1f, &err);
             const size_t sf = k3d_kda_state_floats(ks);
@@ -256,12 +323,16 @@ K3dModel *k3d_model_create(const K3dStackCfg *cfg, uint64_t seed)
             if (w > ws) ws = w;
         }
         if (L->is_dense) {
+            /* under tensor parallelism rows [i0, i0 + ni) of gate and up, the same columns
+             * of down */
+            const size_t ni = (size_t)m->dense_ni, i0 = (size_t)m->dense_i0;
             snprintf(nm, sizeof nm, "layer%d.dense.gate", l);
-            L->dg = bf16_param(m, nm, (size_t)c->dense_inter * E, 0.02f, &err);
+            L->dg = bf16_rows(m, nm, E, i0, ni, 0.02f, &err);
             snprintf(nm, sizeof nm, "layer%d.dense.up", l);
-            L->du = bf16_param(m, nm, (size_t)c->dense_inter * E, 0.02f, &err);
+            L->du = bf16_rows(m, nm, E, i0, ni, 0.02f, &err);
             snprintf(nm, sizeof nm, "layer%d.dense.down", l);
-            L->dd = bf16_param(m, nm, (size_t)E * c->dense_inter, 0.02f, &err);
+            L->dd = m->tp_dense ? bf16_cols(m, nm, E, (size_t)c->dense_inter, i0, ni, 0.02f, &err)
+                                : bf16_param(m, nm, (size_t)E * c->dense_inter, 0.02f, &err);
         } else {
             const K3dMoeShape *s = &c->moe;
             size_t sz[6], off[6], per, toff[4];
@@ -413,12 +484,18 @@ int k3d_model_fill_context(K3dModel *m, int len, uint64_t seed)
                 if (r) return r;
             }
         } else {
+            /* this rank's heads' slice of the state a single GPU holds: the state matrices
+             * [H][D][D] of heads [h0, h0 + hl) and the q, k, v conv histories of their
+             * channels, from the same seeded streams */
             const size_t sf = k3d_kda_state_floats(&L->kshape);
-            const size_t ns = (size_t)L->kshape.heads * L->kshape.head_dim * L->kshape.head_dim;
+            const size_t D = (size_t)L->kshape.head_dim, hl = (size_t)L->kshape.heads, h0 = (size_t)m->kda_h0;
+            const size_t ns = hl * D * D, Pl = hl * D, P = (size_t)c->kda_heads * D, hk = (size_t)c->conv_k - 1;
             for (int b = 0; b < B; b++) {
-                int r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf, ns, seed * 137 + l * 19 + (g0 + b), 0.01f);
-                if (!r) r = k3d_fill_f32_normal(L->kda_state + (size_t)b * sf + ns, sf - ns,
-                                                seed * 139 + l * 23 + (g0 + b), 1.0f);
+                float *st = L->kda_state + (size_t)b * sf;
+                int r = k3d_fill_f32_normal_at(st, ns, seed * 137 + l * 19 + (g0 + b), 0.01f, h0 * D * D);
+                for (int j = 0; j < 3 && !r; j++)
+                    r = k3d_fill_f32_normal_at(st + ns + (size_t)j * Pl * hk, Pl * hk, seed * 139 + l * 23 + (g0 + b),
+                                               1.0f, (size_t)j * P * hk + h0 * D * hk);
                 if (r) return r;
             }
         }
@@ -438,15 +515,29 @@ static int step_eager(K3dModel *m, const int *ids, int *next, float *logits)
     TRY(k3d_embed_bf16(m->h, ids, m->embed, B, E, c->vocab));
     for (int l = 0; l < c->n_layers; l++) {
         K3sLayer *L = &m->L[l];
-        /* the layer applies its input RMSNorm itself (inside its projection GEMV) */
-        if (L->is_mla)
-            TRY(k3d_mla_decode_normed(m->h, m->h, L->in_norm, c->eps, &L->mla, &c->mla, B, L->cache,
+        /* the layer applies its input RMSNorm itself (inside its projection GEMV); under
+         * tensor parallelism it writes this rank's heads' partial, which the push combine
+         * sums into the residual */
+        if (L->is_mla && m->tp_mla) {
+            TRY(k3d_mla_decode_normed(m->mo, m->h, L->in_norm, c->eps, &L->mla, &m->mla_loc, B, L->cache,
+                                      c->ctx_cap, m->pos, 0, m->ws, m->ws_bytes));
+            TRY(k3d_ep_combine_add(m->h, m->mo, (size_t)B * E, 1));
+        } else if (L->is_mla) {
+            TRY(k3d_mla_decode_normed(m->h, m->h, L->in_norm, c->eps, &L->mla, &m->mla_loc, B, L->cache,
                                       c->ctx_cap, m->pos, 1, m->ws, m->ws_bytes));
-        else
+        } else if (m->tp_kda) {
+            TRY(k3d_kda_layer_decode_normed_out(m->mo, m->h, L->in_norm, c->eps, &L->kda, &L->kshape, B,
+                                                L->kda_state, m->ws, m->ws_bytes, 0));
+            TRY(k3d_ep_combine_add(m->h, m->mo, (size_t)B * E, 1));
+        } else {
             TRY(k3d_kda_layer_decode_normed(m->h, L->in_norm, c->eps, &L->kda, &L->kshape, B,
                                             L->kda_state, m->ws, m->ws_bytes));
+        }
         TRY(k3d_rmsnorm(m->xn, m->h, L->post_norm, E, B, c->eps));
-        if (L->is_dense) {
+        if (L->is_dense && m->tp_dense) {
+            TRY(k3d_swiglu_mlp_bf16(m->mo, m->xn, L->dg, L->du, L->dd, E, m->dense_ni, B, 0, m->mlp_ws));
+            TRY(k3d_ep_combine_add(m->h, m->mo, (size_t)B * E, 1));
+        } else if (L->is_dense) {
             TRY(k3d_swiglu_mlp_bf16(m->h, m->xn, L->dg, L->du, L->dd, E, c->dense_inter, B, 1,
                                     m->mlp_ws));
         } else if (c->ep_tokens) {
@@ -546,7 +637,7 @@ double k3d_model_last_step_bytes(K3dModel *m)
         const K3sLayer *L = &m->L[l];
         bytes += 2.0 * E * 4;                                /* norms */
         if (L->is_mla) {
-            const K3dMlaShape *s = &c->mla;
+            const K3dMlaShape *s = &m->mla_loc;                 /* this rank's heads */
             const double qh = s->qk_nope + s->qk_rope, kvw = s->kv_lora + s->qk_rope;
             bytes += 2.0 * (s->q_lora * E + s->n_heads * qh * s->q_lora + kvw * E +
                             s->n_heads * (double)(s->qk_nope + s->v_head) * s->kv_lora +
@@ -554,12 +645,12 @@ double k3d_model_last_step_bytes(K3dModel *m)
                             (s->out_gate ? s->n_heads * (double)s->v_head * E : 0.0));
             bytes += B * 2.0 * kvw * pos;                    /* cache read (pos positions) */
         } else {
-            const double P = (double)c->kda_heads * c->kda_head_dim, D = c->kda_head_dim;
-            bytes += 2.0 * (4 * P * E + c->kda_heads * E + D * E + P * D + E * P);
+            const double P = (double)L->kshape.heads * c->kda_head_dim, D = c->kda_head_dim;
+            bytes += 2.0 * (4 * P * E + L->kshape.heads * E + D * E + P * D + E * P);
             bytes += B * 2.0 * 4.0 * k3d_kda_state_floats(&L->kshape);   /* read + write */
         }
         if (L->is_dense) {
-            bytes += 2.0 * 3.0 * c->dense_inter * E;
+            bytes += 2.0 * 3.0 * m->dense_ni * E;
         } else {
             const K3dMoeShape *s = &c->moe;
             const double per = 3.0 * (s->inter * E / 2.0 + s->inter * E / 32.0);
@@ -690,6 +781,7 @@ static void chol_solve(const double *Lf, int n, const float *rhs, float *out, do
 int k3d_model_state_save(K3dModel *m, const char *path, const int *seq, int nseq, int b)
 {
     if (!m || !path || nseq < 0 || (nseq > 0 && !seq) || b < 0 || b >= m->c.batch) return K3D_EINVAL;
+    if (m->tp_kda || m->tp_mla) return K3D_EINVAL;     /* a rank holds only its heads' state */
     const K3dStackCfg *c = &m->c;
     const K3dMlaShape *ms = &c->mla;
     const int kvw = ms->kv_lora + ms->qk_rope, H = ms->n_heads, kvd = ms->qk_nope + ms->v_head;
@@ -831,6 +923,7 @@ static int load_latent_lsq(K3dModel *m, const K3sLayer *L, uint16_t *cb, FILE *f
 int k3d_model_state_load(K3dModel *m, const char *path, int *seq, int seq_cap, int b)
 {
     if (!m || !path || b < 0 || b >= m->c.batch) return K3D_EINVAL;
+    if (m->tp_kda || m->tp_mla) return K3D_EINVAL;     /* a rank holds only its heads' state */
     const K3dStackCfg *c = &m->c;
     const K3dMlaShape *ms = &c->mla;
     const int kvw = ms->kv_lora + ms->qk_rope, H = ms->n_heads, kvd = ms->qk_nope + ms->v_head;
@@ -1088,6 +1181,10 @@ typedef struct {
 int k3d_model_load_checkpoint(K3dModel *m, const K3dCkpt *ck)
 {
     if (!m || !ck) return K3D_EINVAL;
+    if (m->tp_kda || m->tp_mla || m->tp_dense) {
+        k3h_ckpt_fail("checkpoint loading under tensor parallelism is not built (a rank holds head slices)");
+        return K3D_EINVAL;
+    }
     const K3dStackCfg *c = &m->c;
     const int64_t E = c->hidden, P = (int64_t)c->kda_heads * c->kda_head_dim, D = c->kda_head_dim;
     CkPlan p = {NULL, 0, 0, 0, ck};

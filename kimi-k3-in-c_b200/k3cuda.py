@@ -228,6 +228,8 @@ _PROTOS = {
     "k3d_kda_layer_ws_bytes": (sz, [C.POINTER(K3dKdaShape), i32]),
     "k3d_kda_state_floats": (sz, [C.POINTER(K3dKdaShape)]),
     "k3d_set_kda_head_kernel": (i32, [i32]),
+    "k3d_fill_f32_normal_at": (i32, [vp, sz, C.c_uint64, f32, sz]),
+    "k3d_fill_f32_uniform_at": (i32, [vp, sz, C.c_uint64, f32, f32, sz]),
     "k3d_state_peek": (i32, [C.c_char_p, C.POINTER(K3dStateInfo)]),
     "k3d_ckpt_open": (vp, [C.c_char_p]),
     "k3d_ckpt_close": (None, [vp]),
@@ -242,6 +244,8 @@ _PROTOS = {
     "k3d_bf16_rows_to_f32": (i32, [vp, vp, sz, i32, i32]),
     "k3d_f32_rows_to_bf16": (i32, [vp, sz, vp, i32, i32]),
     "k3d_transpose_u16": (i32, [vp, vp, i32, i32]),
+    "k3d_kda_layer_decode_normed_out": (i32, [vp, vp, vp, f32, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32,
+                                              vp, vp, sz, i32]),
     "k3d_kda_layer_decode": (i32, [vp, vp, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32, vp, vp, sz]),
     "k3d_kda_layer_decode_normed": (i32, [vp, vp, f32, C.POINTER(K3dKdaW), C.POINTER(K3dKdaShape), i32,
                                           vp, vp, sz]),
