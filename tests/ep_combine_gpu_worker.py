@@ -4,8 +4,9 @@ run_combine: k3d_ep_combine_add on seeded partials of several lengths, repeated 
 parity of the receive slots alternates), against the rank-order sum computed on the host;
 every rank must hold the same result.
 run_stack: the reduced-width decode stack under expert parallelism (routed experts split
-by rank, shared expert split by intermediate rows, vocabulary-split LM head, the push
-combine per MoE layer; eager, graph capture, replay), then rank 0 alone steps the same
+by rank, shared expert split by intermediate rows, the KDA heads, MLA heads (when they
+split into multiples of 8) and dense rows split by rank, vocabulary-split LM head, the push
+combine after every attention layer, dense MLP and MoE layer; eager, graph capture, replay), then rank 0 alone steps the same
 seeded model on one GPU with the same tokens: logits (the ranks' vocabulary slices put
 together) within 1e-5 and the same greedy tokens."""
 import ctypes
@@ -62,12 +63,14 @@ def run_combine(rank, world, port, seed):
         dist.destroy_process_group()
 
 
-def run_stack(rank, world, port, seed, batch):
+def run_stack(rank, world, port, seed, batch, mla_heads=None):
     lib, dist, torch = _setup(rank, world, port)
     import k3cuda
     from test_gpu_stack import CFG, make_cfg, download
     try:
         c = CFG
+        if mla_heads:      # 16 heads split over 2 ranks: the MLA layers run tensor-parallel too
+            c = dict(CFG, mla=dict(CFG["mla"], H=mla_heads))
         E = c["moe"]["n_experts"]
 
         def model_cfg(lo, hi, add_shared):

@@ -48,10 +48,10 @@ def test_push_combine_two_gpus_equals_rank_order_sum():
 
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("batch", [1, 6])
-def test_stack_two_gpus_matches_one_gpu(batch):
+@pytest.mark.parametrize("batch,mla_heads", [(1, None), (6, None), (1, 16)])
+def test_stack_two_gpus_matches_one_gpu(batch, mla_heads):
     import ep_combine_gpu_worker
-    _run_two(ep_combine_gpu_worker.run_stack, 99, batch)
+    _run_two(ep_combine_gpu_worker.run_stack, 99, batch, mla_heads)
 
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
