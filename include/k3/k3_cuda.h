@@ -390,6 +390,10 @@ int k3d_ep_peer_init(size_t max_floats);
  * library stream and capturable in a CUDA graph. Without k3d_ep_peer_init (or for vectors
  * longer than it was sized for) it runs ncclAllReduce and an add instead. */
 int k3d_ep_combine_add(float *h, const float *partial, size_t n, int accumulate);
+/* The push combine's protocol: 0 (default) every element as one 8-byte word carrying its
+ * own call tag (no fence, no flag round trip), 1 the data, a system fence and a release
+ * flag per slice. Same bits; every rank must choose the same. */
+int k3d_set_ep_combine(int kind);
 
 /* Mode A expert parallelism: all-to-all dispatch and combine for data-parallel tokens (a
  * batch split over the ranks, e.g. B = 64). Every rank passes ITS OWN tokens x[T][hidden]

@@ -182,6 +182,77 @@ int k3d_ep_init(int rank, int nranks, const unsigned char id[128])
     return K3D_OK;
 }
 
+// The same sum in one pass per element (the default): every element travels as one 8-byte
+// word, its float bits in the low half and the slice's call count in the high half, stored
+// to slot (parity, me) of every rank with one single-copy-atomic store; the receiver polls
+// each source's word until its tag shows this call, so a word carries its own arrival flag
+// and there is no fence, no separate flag store and no barrier. Same sum order (rank 0
+// first) and the same per-slice counts as k_ep_push_sum, hence the same bits.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(256) k_ep_push_sum_ll(float *h, const float *part, int n, const __grid_constant__ EpPeers P,
+                                                        int me, int nr, unsigned *epoch, size_t max_n, int accumulate)
+{
+    __shared__ unsigned s_e;
+    pdl_wait();
+    pdl_trigger();
+    const int i = blockIdx.x;
+    const int per = ((n + (int)gridDim.x - 1) / (int)gridDim.x + 3) & ~3;
+    const int s0 = min(n, i * per), s1 = min(n, s0 + per);
+    if (threadIdx.x == 0) s_e = epoch[i] + 1u;
+    __syncthreads();
+    const unsigned e = s_e;
+    const size_t par = e & 1u;
+    for (int j = s0 + (int)threadIdx.x; j < s1; j += blockDim.x) {
+        const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(part[j]);
+        for (int r = 0; r < nr; r++) {
+            unsigned long long *dst = reinterpret_cast<unsigned long long *>(P.data[r]) + (par * kEpMaxRanks + (size_t)me) * max_n;
+            st_relaxed_sys_u64(dst + j, w);
+        }
+    }
+    const unsigned long long *src = reinterpret_cast<const unsigned long long *>(P.data[me]) + par * kEpMaxRanks * max_n;
+    const long long lim = k3_wait_cycles;
+    bool timed_out = false;
+    for (int j = s0 + (int)threadIdx.x; j < s1; j += blockDim.x) {
+        float v = 0.0f;
+        for (int r = 0; r < nr; r++) {
+            const unsigned long long *q = src + (size_t)r * max_n + j;
+            unsigned long long w = ld_relaxed_sys_u64(q);
+            if ((unsigned)(w >> 32) != e && !timed_out) {
+                const long long t0 = clock64();
+                do {
+                    __nanosleep(32);
+                    w = ld_relaxed_sys_u64(q);
+                    if (clock64() - t0 > lim) {
+                        k3_raise_at(K3D_ETIMEOUT, K3_SITE_EP, r, i, (int)e);
+                        timed_out = true;
+                        break;
+                    }
+                } while ((unsigned)(w >> 32) != e);
+            }
+            const float x = __uint_as_float((unsigned)w);
+            v = r == 0 ? x : v + x;
+        }
+        h[j] = accumulate ? h[j] + v : v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) epoch[i] = e;
+}
+
+// which combine kernel k3d_ep_combine_add launches: 0 one tagged word per element, 1 data
+// then a release flag per slice
+static int g_ep_combine_kind = 0;
+
 int k3d_ep_peer_init(size_t max_floats)
 {
     K3_TRY(ensure_ctx());
@@ -191,7 +262,9 @@ int k3d_ep_peer_init(size_t max_floats)
     if (g_pb.local && g_pb.max_n >= max_floats) return K3D_OK;
     if (g_pb.local) return fail(K3D_EINVAL, "k3d_ep_peer_init: already set up for %zu floats", g_pb.max_n);
     const size_t max_n = (max_floats + 63) & ~(size_t)63;
-    const size_t bytes = kEpFlagBytes + 2 * (size_t)kEpMaxRanks * max_n * sizeof(float);
+    // data: [2 parities][kEpMaxRanks sources][max_n] 8-byte words (the flag protocol uses the
+    // first half of the region as floats with the same indexing)
+    const size_t bytes = kEpFlagBytes + 2 * (size_t)kEpMaxRanks * max_n * sizeof(unsigned long long);
     cudaStream_t st = stream();
     if (cudaMalloc(&g_pb.local, bytes) != cudaSuccess || cudaMalloc(&g_pb.epoch, kEpSlices * sizeof(unsigned)) != cudaSuccess) {
         cudaGetLastError();
@@ -256,8 +329,12 @@ int k3d_ep_combine_add(float *h, const float *partial, size_t n, int accumulate)
         P.flags[r] = r < g_size ? (unsigned *)g_pb.peer[r] : nullptr;
     }
     prof_begin("ep.combine");
-    launch_pdl(k_ep_push_sum, dim3(kEpSlices), dim3(256), 0, st, h, partial, (int)n, P, g_rank, g_size,
-               g_pb.epoch, g_pb.max_n, accumulate);
+    if (g_ep_combine_kind == 0)
+        launch_pdl(k_ep_push_sum_ll, dim3(kEpSlices), dim3(256), 0, st, h, partial, (int)n, P, g_rank, g_size,
+                   g_pb.epoch, g_pb.max_n, accumulate);
+    else
+        launch_pdl(k_ep_push_sum, dim3(kEpSlices), dim3(256), 0, st, h, partial, (int)n, P, g_rank, g_size,
+                   g_pb.epoch, g_pb.max_n, accumulate);
     note_launch();
     prof_end("ep.combine");
     return check_launch("ep push combine");
@@ -278,6 +355,13 @@ int k3d_ep_finalize(void)
     g_comm = nullptr;
     g_rank = 0;
     g_size = 1;
+    return K3D_OK;
+}
+
+int k3d_set_ep_combine(int kind)
+{
+    if (kind < 0 || kind > 1) return fail(K3D_EINVAL, "k3d_set_ep_combine(%d): 0 or 1", kind);
+    g_ep_combine_kind = kind;
     return K3D_OK;
 }
 

@@ -258,6 +258,7 @@ _PROTOS = {
     "k3d_ep_size": (i32, []),
     "k3d_ep_allreduce_f32": (i32, [vp, sz]),
     "k3d_ep_peer_init": (i32, [C.c_size_t]),
+    "k3d_set_ep_combine": (i32, [i32]),
     "k3d_ep_combine_add": (i32, [vp, vp, C.c_size_t, i32]),
     "k3d_moe_a2a_ws_bytes": (sz, [C.POINTER(K3dMoeShape), i32, i32]),
     "k3d_moe_swiglu_a2a_dev": (i32, [vp, vp, C.POINTER(K3dMoeW), C.POINTER(K3dMoeShape), i32, i32, vp, vp, vp, sz]),

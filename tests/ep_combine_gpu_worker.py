@@ -1,8 +1,8 @@
 """One rank (one GPU) of the two-GPU tests of the NVLink push combine (test_gpu_ep_combine.py).
 
 run_combine: k3d_ep_combine_add on seeded partials of several lengths, repeated (the
-parity of the receive slots alternates), against the rank-order sum computed on the host;
-every rank must hold the same result.
+parity of the receive slots alternates), with both protocols (k3d_set_ep_combine), against
+the rank-order sum computed on the host; every rank must hold the same result.
 run_stack: the reduced-width decode stack under expert parallelism (routed experts split
 by rank, shared expert split by intermediate rows, the KDA heads, MLA heads (when they
 split into multiples of 8) and dense rows split by rank, vocabulary-split LM head, the push
@@ -41,7 +41,12 @@ def run_combine(rank, world, port, seed):
     try:
         nmax = 64 * 7168
         k3cuda.check(lib.k3d_ep_peer_init(nmax), "peer init")
-        for call, n in enumerate([7168, 7168, 3 * 7168, nmax, 7168, 1000]):
+        sizes = [7168, 7168, 3 * 7168, nmax, 7168, 1000]
+        # the tagged-word protocol, then the flag protocol, then back (both keep the
+        # per-slice call counts in step)
+        kinds = [0] * len(sizes) + [1] * len(sizes) + [0] * 3
+        for call, (kind, n) in enumerate(zip(kinds, sizes * 2 + sizes[:3])):
+            k3cuda.check(lib.k3d_set_ep_combine(kind))
             parts = [np.random.default_rng(seed * 100 + call * 10 + r).standard_normal(n).astype(np.float32)
                      for r in range(world)]
             h0 = np.random.default_rng(seed * 100 + call).standard_normal(n).astype(np.float32)
