@@ -560,7 +560,7 @@ def bench_moe_a2a(args, rank, world):
     lib.k3d_host_free(hy)
     B = T * world
     return {
-        "metric": METRIC, "value": (B * world if mode_a else B) * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "metric": METRIC, "value": B * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
@@ -751,9 +751,11 @@ def stack_mode_a(args, world):
     otherwise or when asked."""
     if args.ep_mode == "r" or world == 1:
         return False
+    if args.ep_mode == "auto" and args.batch == 1:
+        return False
     if args.batch % world:
         raise SystemExit(f"--batch {args.batch} does not split over {world} ranks")
-    return args.ep_mode == "a" or args.batch > 1
+    return True
 
 
 def bench_stack(args, rank, world):
@@ -853,7 +855,7 @@ def bench_stack(args, rank, world):
     lib.k3d_model_destroy(model)
     ms = tot_ms / args.steps
     res = {
-        "metric": METRIC, "value": B * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
+        "metric": METRIC, "value": (B * world if mode_a else B) * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic random-init weights (bf16 ~N(0,0.02), MXFP4 experts E8M0 117..121); "

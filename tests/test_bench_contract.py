@@ -50,3 +50,22 @@ def test_reference_arm_threads_ignore_launcher_omp_setting():
     aff = len(os.sched_getaffinity(0))
     want = max(1, min(aff, psutil.cpu_count(logical=False) or aff))
     assert d["cpu_baseline"]["cores"] == want
+
+
+def test_stack_mode_selection():
+    """--gpus N at batch 1 (the driver's scaling run) keeps Mode R; a batch that splits
+    over the ranks takes Mode A under --ep-mode auto; one that does not is refused."""
+    import argparse
+    sys.path.insert(0, REPO)
+    import bench
+
+    def args(batch, mode="auto"):
+        return argparse.Namespace(batch=batch, ep_mode=mode)
+
+    assert not bench.stack_mode_a(args(1), 8)
+    assert not bench.stack_mode_a(args(64), 1)
+    assert bench.stack_mode_a(args(64), 2)
+    assert not bench.stack_mode_a(args(64, "r"), 2)
+    assert bench.stack_mode_a(args(8, "a"), 8)
+    with pytest.raises(SystemExit):
+        bench.stack_mode_a(args(3), 2)
