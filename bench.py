@@ -68,21 +68,30 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs. Rank 0
+    alone samples, every GPU of the job in one nvidia-smi process at 100 ms: each query
+    takes the driver's locks, and eight processes polling at a high rate slowed the
+    launches of the region they were measuring."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu):
-        self.gpu = gpu
+    def __init__(self, gpu=None):
+        rank, world, _ = dist_env()
+        self.active = rank == 0
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        local = list(range(world)) if world > 1 else [int(os.environ.get("LOCAL_RANK", 0)) if gpu is None else gpu]
+        self.gpus = [vis[i] if i < len(vis) else str(i) for i in local]
         self.rows = []
         self.proc = None
 
     def start(self):
+        if not self.active:
+            return
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                ["nvidia-smi", "-i", ",".join(self.gpus), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -97,9 +106,11 @@ class ClockSampler:
             self.rows.append([c.strip() for c in line.split(",")])
 
     def stop(self):
+        if not self.active:
+            return None
         t0 = time.time()
         n0 = len(self.rows)
-        while self.proc and len(self.rows) < n0 + 2 and time.time() - t0 < 2.0:
+        while self.proc and len(self.rows) < n0 + 2 * len(self.gpus) and time.time() - t0 < 2.0:
             time.sleep(0.02)                                     # a sample after the region
         if self.proc:
             self.proc.terminate()
@@ -118,7 +129,7 @@ class ClockSampler:
                         reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "gpus": len(self.gpus)}
 
 
 def load_traffic(name):
@@ -763,7 +774,10 @@ def bench_stack(args, rank, world):
     lib = k3cuda.init(0)
     k3cuda.check(lib.k3d_set_expert_kernel(args.expert_kernel))
     ctx = args.context
-    cap = ctx + args.steps * 2 + args.warmup * 2 + 16
+    n_prof = max(3, min(args.steps, 10))
+    e2e_steps = max(args.steps, 200)
+    # the timed and profiled steps, then (from a refilled context) the end-to-end ones
+    cap = ctx + max(args.warmup + args.steps + n_prof, 3 + e2e_steps) + 16
     # the tcgen05 kernel streams experts stored in the tiled layout; the other two
     # kernels read the checkpoint layout
     mode_a = stack_mode_a(args, world)
@@ -809,7 +823,6 @@ def bench_stack(args, rank, world):
     lib.k3d_prof_reset()
     lib.k3d_prof_enable(1)
     lib.k3d_launch_count_reset()
-    n_prof = max(3, min(args.steps, 10))
     for i in range(n_prof):
         k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "profiled step")
     k3cuda.check(lib.k3d_sync())
@@ -837,13 +850,17 @@ def bench_stack(args, rank, world):
     achieved = alg_exp / (exp_ms * 1e-3) / 1e9
     # end to end through the public API with host buffers: token ids in from host memory,
     # next ids out to host memory, every step (greedy decoding); a few untimed steps first,
-    # then at least 200 timed steps so that host jitter averages out
-    hid = np.zeros(B, np.int32)
+    # then at least 200 timed steps so that host jitter averages out. The context is filled
+    # again and sequence b starts from token (37 b + 5) mod vocab (b the global sequence
+    # index), so the generated tokens, and their hash, do not depend on how many steps ran
+    # before or on how many ranks share the job.
+    k3cuda.check(lib.k3d_model_fill_context(model, ctx, 77))
+    g0 = rank * B if mode_a else 0
+    hid = ((np.arange(g0, g0 + B) * 37 + 5) % 163840).astype(np.int32)
     hnx = np.zeros(B, np.int32)
     for i in range(3):
         k3cuda.check(lib.k3d_model_step_host(model, hid.ctypes.data, hnx.ctypes.data), "e2e warm-up")
         hid[:] = hnx
-    e2e_steps = max(args.steps, 200)
     gen = np.zeros((e2e_steps, B), np.int32)
     barrier()
     t0 = time.perf_counter()
@@ -852,7 +869,10 @@ def bench_stack(args, rank, world):
         hid[:] = hnx
         gen[i] = hnx
     e2e_s = reduce_max(time.perf_counter() - t0)
+    k3cuda.check(lib.k3d_sync(), "after the e2e steps")      # device errors of the steps
     lib.k3d_model_destroy(model)
+    if mode_a:
+        gen = gather_cols(gen)                                # every rank's sequences
     ms = tot_ms / args.steps
     res = {
         "metric": METRIC, "value": (B * world if mode_a else B) * args.steps / (tot_ms * 1e-3), "unit": "tok/s",
@@ -888,6 +908,18 @@ def barrier():
     if _PG is not None:
         import torch.distributed as dist
         dist.barrier()
+
+
+def gather_cols(a):
+    """The ranks' [steps][B] arrays side by side, in rank order (a copy on one rank)."""
+    if _PG is None:
+        return a
+    import torch
+    import torch.distributed as dist
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t)
+    return np.concatenate([p.numpy() for p in parts], axis=1)
 
 
 def reduce_max(v):

@@ -202,18 +202,47 @@ __global__ void __launch_bounds__(128) k_kda_head(KdaHeadArgs A)
     A.heads[bp] = o;
 }
 
+// Column j of the step from the state still in memory, with the CPU's skips of zero keys
+// and queries (k_kda_head's loops): the register kernel's fallback when its dot products
+// came out non-finite. Writes the column back and returns o.
+template <int DT>
+__device__ __forceinline__ float kda_column_exact(float *S, int j, const float *as, const float *ks,
+                                               const float *kbs, const float *qs, float vv)
+{
+    float u = 0.0f;
+    for (int i = 0; i < DT; i++) {
+        const float si = __fmul_rn(S[(size_t)i * DT + j], as[i]);
+        if (ks[i] != 0.0f) u = __fadd_rn(u, __fmul_rn(ks[i], si));
+    }
+    const float d = __fsub_rn(vv, u);
+    float o = 0.0f;
+    for (int i = 0; i < DT; i++) {
+        float si = __fmul_rn(S[(size_t)i * DT + j], as[i]);
+        if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(kbs[i], d));
+        if (qs[i] != 0.0f) o = __fadd_rn(o, __fmul_rn(qs[i], si));
+        S[(size_t)i * DT + j] = si;
+    }
+    return o;
+}
+
 // The same head with the state column in registers: thread j loads column j of the head's
 // state (DT coalesced rows, all issued before the programmatic wait), runs both passes of
 // the step on its registers and stores the column back. No shared-memory tile, no bulk
 // copy, and the two dependent fadd chains (u, then o) are the only serial part: the
 // shared-tile kernel paid a shared-memory round trip per row in each pass with four warps
 // per SM to hide it. Same operations in the same order, so bit-identical to k_kda_head.
+// The per-row operands come four rows at a time (16-byte shared loads), and the two dot
+// products add every row's product without the zero test: u and o start at +0 and a sum
+// in round-to-nearest is -0 only when both terms are, so adding the +-0 product of a zero
+// key or query changes nothing while the state is finite; a non-finite u or o (the only
+// way a skipped product could have mattered) recomputes the column with the skips
+// (kda_column_exact). The state update keeps its test.
 template <int KC, int DT>
 __global__ void __launch_bounds__(DT) k_kda_head_reg(const __grid_constant__ KdaHeadArgs A)
 {
     static_assert(KC > 0 && DT % 32 == 0 && DT <= 128, "register head: KC > 0, DT in 32..128");
     constexpr int NW = DT / 32;
-    __shared__ float qs[DT], ks[DT], kbs[DT], as[DT];
+    __shared__ __align__(16) float qs[DT], ks[DT], kbs[DT], as[DT];
     __shared__ double red[2][NW];
     const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
     const int H = A.H, P = H * DT, lane = j & 31, warp = j >> 5;
@@ -278,25 +307,41 @@ __global__ void __launch_bounds__(DT) k_kda_head_reg(const __grid_constant__ Kda
     __syncthreads();
     float u = 0.0f;
 #pragma unroll
-    for (int i = 0; i < DT; i++) {
-        s[i] = __fmul_rn(s[i], as[i]);
-        const float ki = ks[i];
-        if (ki != 0.0f) u = __fadd_rn(u, __fmul_rn(ki, s[i]));
+    for (int i4 = 0; i4 < DT / 4; i4++) {
+        const float4 a4 = reinterpret_cast<const float4 *>(as)[i4];
+        const float4 k4 = reinterpret_cast<const float4 *>(ks)[i4];
+        const float ar[4] = {a4.x, a4.y, a4.z, a4.w}, kr[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            s[4 * i4 + t] = __fmul_rn(s[4 * i4 + t], ar[t]);
+            u = __fadd_rn(u, __fmul_rn(kr[t], s[4 * i4 + t]));
+        }
     }
     const float d = __fsub_rn(vv, u);
     float o = 0.0f;
 #pragma unroll
-    for (int i = 0; i < DT; i++) {
-        float si = s[i];
-        if (ks[i] != 0.0f) si = __fadd_rn(si, __fmul_rn(kbs[i], d));
-        const float qi = qs[i];
-        if (qi != 0.0f) o = __fadd_rn(o, __fmul_rn(qi, si));
-        s[i] = si;
+    for (int i4 = 0; i4 < DT / 4; i4++) {
+        const float4 k4 = reinterpret_cast<const float4 *>(ks)[i4];
+        const float4 b4 = reinterpret_cast<const float4 *>(kbs)[i4];
+        const float4 q4 = reinterpret_cast<const float4 *>(qs)[i4];
+        const float kr[4] = {k4.x, k4.y, k4.z, k4.w}, br[4] = {b4.x, b4.y, b4.z, b4.w};
+        const float qr[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            float si = s[4 * i4 + t];
+            if (kr[t] != 0.0f) si = __fadd_rn(si, __fmul_rn(br[t], d));
+            o = __fadd_rn(o, __fmul_rn(qr[t], si));
+            s[4 * i4 + t] = si;
+        }
     }
     // the column goes back after the loop: a store through a generic pointer between the
     // loop's shared-memory reads would order every later read after it
+    if (isfinite(u) && isfinite(o)) {
 #pragma unroll
-    for (int i = 0; i < DT; i++) S[(size_t)i * DT + j] = s[i];
+        for (int i = 0; i < DT; i++) S[(size_t)i * DT + j] = s[i];
+    } else {
+        o = kda_column_exact<DT>(S, j, as, ks, kbs, qs, vv);
+    }
     {
         const double o2 = warp_sum_d((double)o * (double)o);
         if (lane == 0) red[0][warp] = o2;            // red[0] was last read before the

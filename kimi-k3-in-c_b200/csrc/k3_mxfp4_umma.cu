@@ -926,6 +926,20 @@ __device__ __forceinline__ uint32_t piece_word(uint32_t nib)
            (__shfl_down_sync(0xffffffffu, b, 6) << 24);
 }
 
+// Piece p of one element's split: the E2M1 code (nibble) of the residual r at the
+// schedule's scale, r replaced by what remains; lane p records the scale code.
+__device__ __forceinline__ uint32_t split_piece(float &r, int code0, int p, int lane, int &my_code)
+{
+    const int code = max(0, p == 0 ? code0 : code0 + 1 - 3 * p);
+    uint32_t nib;
+    const float rs = __fmul_rn(r, __int_as_float((254 - code) << 23));   // r / 2^s, exact
+    const float q = e2m1_rne(rs, nib);                                  // no -0 codes
+    const float sc = code ? __int_as_float(code << 23) : __int_as_float(0x00400000);
+    r = __fmul_rn(__fsub_rn(rs, q), sc);
+    if (lane == p) my_code = code;
+    return nib;
+}
+
 // NV vectors per B operand (the grouped layout, NV = 4): slot v's piece p is B row
 // m = 16 v + p, at row m of each K block's (16 NV) x 128-byte SWIZZLE_128B image, and its
 // scale at byte 16 (m % 32) + 4 (m / 32) + (block % 4) of the block's atom.
@@ -958,20 +972,17 @@ __device__ __forceinline__ void split_block(uint8_t *bq, uint8_t *bs, float r, i
     } else {
         const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r)));
         const int code0 = (int)(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
-        bool live = true;                    // the residual is not yet zero everywhere
-#pragma unroll 1                             // rolled: a small body stays in the instruction cache
+        // the lane's 16 codes first, a chain of plain arithmetic with no warp operation in
+        // it (a zero residual gives zero codes from there on, as the schedule wants), kept
+        // as nibbles; then the 16 row words, whose shuffles are independent of one another
+        uint32_t nlo = 0u, nhi = 0u;
+#pragma unroll 4
+        for (int p = 0; p < 8; p++) nlo |= split_piece(r, code0, p, lane, my_code) << (4 * p);
+#pragma unroll 4
+        for (int p = 8; p < kN; p++) nhi |= split_piece(r, code0, p, lane, my_code) << (4 * (p - 8));
+#pragma unroll
         for (int p = 0; p < kN; p++) {
-            const int code = max(0, p == 0 ? code0 : code0 + 1 - 3 * p);
-            uint32_t nib = 0u;
-            if (live) {
-                const float rs = __fmul_rn(r, __int_as_float((254 - code) << 23));   // r / 2^s, exact
-                const float q = e2m1_rne(rs, nib);                                  // no -0 codes
-                const float sc = code ? __int_as_float(code << 23) : __int_as_float(0x00400000);
-                r = __fmul_rn(__fsub_rn(rs, q), sc);
-            }
-            if (lane == p) my_code = code;
-            const uint32_t w = live ? piece_word(nib) : 0u;
-            live = live && __any_sync(0xffffffffu, r != 0.0f);
+            const uint32_t w = piece_word(((p < 8 ? nlo : nhi) >> (4 * (p & 7))) & 15u);
             if ((lane & 7) == 0)
                 *reinterpret_cast<uint32_t *>(tile + (p >> 3) * 1024 + (p & 7) * 128 + (((j & 7) ^ (p & 7)) << 4) +
                                               (lane >> 1)) = w;

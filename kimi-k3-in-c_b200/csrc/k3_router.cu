@@ -675,6 +675,8 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
     __shared__ int s_need[kNeedMax];
     __shared__ int s_isel[K3_MAX_TOPK];
     __shared__ int s_idx[K3_MAX_TOPK];
+    __shared__ uint32_t s_qc[4][8];          // quarter top-k (K <= 8): codes, experts
+    __shared__ int s_qi[4][8];
     __shared__ float s_m;
     const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
     const int t = blockIdx.y;
@@ -845,7 +847,65 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
     const int K = J.topk;
     bool x_staged = false;
     for (int iter = 0; iter <= E; iter++) {
-        if (q == 0) {
+        if (K <= 8) {
+            // top-k by repeated strict-greater max over the keys, lowest index on ties
+            // (k3_ops.c:459-466), in two steps: warp q selects the top K of experts
+            // [128 q, 128 q + 128) (lane l holds 128 q + l + 32 k, k < 4) by the rounds of
+            // the single-warp scan below, then warp 0 selects the top K of the 4 K
+            // candidates (one a lane) the same way. Every expert of the overall top K is in
+            // its quarter's top K (fewer than K keys, in the order (key desc, index asc),
+            // precede it there too), so the selection and its order are the same.
+            uint32_t c[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int e = 128 * q + lane + 32 * k;
+                c[k] = e < E ? order_code(key[e]) : 0u;
+            }
+            uint32_t bc = max(max(c[0], c[1]), max(c[2], c[3]));
+            for (int j = 0; j < K; j++) {
+                const uint32_t m = __reduce_max_sync(0xffffffffu, bc);
+                int best = -1;
+                if (m != 0u) {
+                    uint32_t mask = 0u;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) mask |= (c[k] == m ? 1u : 0u) << k;
+                    const uint32_t cand = mask ? (uint32_t)(128 * q + lane + 32 * (__ffs(mask) - 1)) : 0xffffffffu;
+                    best = (int)__reduce_min_sync(0xffffffffu, cand);
+                }
+                if (best >= 0 && (best & 31) == lane) {
+                    const int kb = (best - 128 * q) >> 5;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) c[k] = (k == kb) ? 0u : c[k];
+                    bc = max(max(c[0], c[1]), max(c[2], c[3]));
+                }
+                if (lane == 0) {
+                    s_qc[q][j] = best >= 0 ? m : 0u;
+                    s_qi[q][j] = best;
+                }
+            }
+            __syncthreads();
+            if (q == 0) {
+                uint32_t cc = 0u;
+                int ci = -1;
+                if (lane < 4 * K) {
+                    cc = s_qc[lane / K][lane % K];
+                    ci = s_qi[lane / K][lane % K];
+                }
+                for (int j = 0; j < K; j++) {
+                    const uint32_t m = __reduce_max_sync(0xffffffffu, cc);
+                    int best = -1;
+                    if (m != 0u)
+                        best = (int)__reduce_min_sync(0xffffffffu, cc == m ? (uint32_t)ci : 0xffffffffu);
+                    if (best >= 0 && cc == m && ci == best) cc = 0u;
+                    if (lane == 0) s_isel[j] = best;
+                }
+                if (lane == 0) {
+                    const int b = s_isel[K - 1];
+                    s_m = b >= 0 ? key[b] : -INFINITY;
+                    s_nneed = 0;
+                }
+            }
+        } else if (q == 0) {
             // top-k by repeated strict-greater max over the keys, lowest index on ties
             // (k3_ops.c:459-466): per round one redux for the largest key and one for the
             // lowest index holding it; lane l holds experts l + 32k, its lowest k holding
@@ -925,12 +985,22 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
         float inv = 1.0f;
         if (rn) {
             double sum = 0.0;
-            for (int j = 0; j < K; j++) {
-                const float wj = __shfl_sync(0xffffffffu, j < 32 ? w0 : w1, j & 31);
-                sum = __dadd_rn(sum, (double)wj);
+            if (K <= 8) {
+                // the shuffles first (independent of the sum), then the sum in slot order
+                float wv[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) wv[j] = __shfl_sync(0xffffffffu, w0, j);
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (j < K) sum = __dadd_rn(sum, (double)wv[j]);
+            } else {
+                for (int j = 0; j < K; j++) {
+                    const float wj = __shfl_sync(0xffffffffu, j < 32 ? w0 : w1, j & 31);
+                    sum = __dadd_rn(sum, (double)wj);
+                }
             }
-            if (lane == 0) inv = (float)__ddiv_rn(1.0, __dadd_rn(sum, 1e-20));
-            inv = __shfl_sync(0xffffffffu, inv, 0);
+            // every lane holds the same sum: each forms the reciprocal itself
+            inv = (float)__ddiv_rn(1.0, __dadd_rn(sum, 1e-20));
             w0 = __fmul_rn(w0, inv);
             w1 = __fmul_rn(w1, inv);
         }
@@ -960,6 +1030,43 @@ __global__ void __launch_bounds__(128) k_router_fused(RouterJob J)
     }
     // one token: its selection is in this CTA's shared memory; more: every token's last CTA
     // published its row of idx (fenced) before the count
+    if (J.T == 1 && K <= 32) {
+        // one token's K distinct experts: warp 0 writes what group_assignments writes (active
+        // experts in increasing id order, one assignment each, act_off[u] = u, assign[u] the
+        // slot of the u-th expert) from each slot's rank among the slots, without the count
+        // and scan passes; a token holding an expert twice (only when fewer than K experts
+        // were selectable) takes the general grouping below
+        __shared__ int s_dup;
+        for (int i = threadIdx.x; i < J.nzero; i += blockDim.x) J.zero[i] = 0;
+        if (q == 0) {
+            const int e = lane < K ? s_idx[lane] : -1;
+            const bool in = lane < K && e >= J.e_lo && e < J.e_hi && e >= 0 && e < E;
+            const unsigned inm = __ballot_sync(0xffffffffu, in);
+            const unsigned same = __match_any_sync(0xffffffffu, in ? e : -1 - lane);
+            const bool dup = __any_sync(0xffffffffu, in && __popc(same) > 1);
+            if (!dup) {
+                int rank = 0;
+                for (int j = 0; j < K; j++) {
+                    const int ej = __shfl_sync(0xffffffffu, e, j);
+                    rank += ((inm >> j) & 1u) && ej < e;
+                }
+                if (in) {
+                    J.act_expert[rank] = e;
+                    J.act_off[rank] = rank;
+                    J.assign[rank] = lane;
+                }
+                if (lane == 0) {
+                    const int n = __popc(inm);
+                    J.n_active[0] = n;
+                    J.n_active[1] = n;
+                    J.act_off[n] = n;
+                }
+            }
+            if (lane == 0) s_dup = dup;
+        }
+        __syncthreads();
+        if (!s_dup) return;
+    }
     if (J.T == 1)
         group_assignments(s_idx, K, E, J.e_lo, J.e_hi, J.n_active, J.act_expert, J.act_off,
                           J.assign, gsm, J.zero, J.nzero, true);

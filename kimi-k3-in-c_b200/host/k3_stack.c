@@ -69,6 +69,7 @@ struct K3dModel {
     int *g_next;
     float *g_logits;
     int use_graph, warmed;
+    int hpos;                      /* positions the caches hold (the host's copy of pos) */
     uint64_t seed, counter;
     double step_bytes;
     K3sTensor t[K3S_MAX_TENSORS];
@@ -501,6 +502,7 @@ int k3d_model_fill_context(K3dModel *m, int len, uint64_t seed)
         }
     }
     int p[4] = {len, len, len, len};
+    m->hpos = len;
     return k3d_upload(m->pos, p, sizeof p);
 }
 
@@ -575,11 +577,15 @@ int k3d_model_use_graph(K3dModel *m, int on)
 int k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits)
 {
     if (!m || !ids || !next_ids) return K3D_EINVAL;
+    /* a step writes cache position hpos: refused once the caches are full (the kernels
+     * would only raise a device error and skip the attention) */
+    if (m->hpos >= m->c.ctx_cap) return K3D_EBOUND;
     if (!m->use_graph || !m->warmed) {
         /* the first step runs eagerly: it initialises every kernel's attributes and
          * lazily created buffers before anything is captured */
         int r = step_eager(m, ids, next_ids, logits);
         if (!r) m->warmed = 1;
+        if (!r) m->hpos++;
         return r;
     }
     if (!m->graph || m->g_ids != ids || m->g_next != next_ids || m->g_logits != logits) {
@@ -595,7 +601,9 @@ int k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits
         m->g_next = next_ids;
         m->g_logits = logits;
     }
-    return k3d_graph_launch(m->graph);
+    const int r = k3d_graph_launch(m->graph);
+    if (!r) m->hpos++;
+    return r;
 }
 
 int k3d_model_step_host(K3dModel *m, const int *ids_host, int *next_host)
@@ -1004,6 +1012,7 @@ int k3d_model_state_load(K3dModel *m, const char *path, int *seq, int seq_cap, i
     if (!r) {
         int p[4] = {cached, cached, cached, cached};
         r = k3d_upload(m->pos, p, sizeof p);
+        if (!r) m->hpos = cached;
     }
     if (!r) r = k3d_sync();
     return r;

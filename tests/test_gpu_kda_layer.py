@@ -93,3 +93,40 @@ def test_layer_matches_oracle(k3, oracle):
         want = orc_mod.kda_layer(oracle, x, w, hidden, H, D, K, -5.0, 1e-6, st_o)
         assert max_rel_err(hg, want) <= 1e-4, step
         assert max_rel_err(state, st_o) <= 1e-4, step
+
+
+def test_zero_keys_and_non_finite_state_agree_across_head_kernels(k3):
+    """Keys and queries that are exactly zero (their conv weights zero) and infinite state
+    entries: the register kernel's branch-free dot products must still agree bit for bit
+    with the kernels that skip zero keys and queries. Head 0 has an infinite state entry in
+    a row whose key and query are zero (finite output: the skipped products are 0 * inf),
+    head 1 one in a row whose key alone is zero (its output is not finite)."""
+    hidden, H, D, K, B = 1024, 8, 128, 4, 1
+    w = make_layer(404, hidden, H, D, K)
+    for h in range(H):
+        for i in (3, 77):
+            w["k_conv"][h * D + i] = 0.0
+        for i in (5, 77):
+            w["q_conv"][h * D + i] = 0.0
+    L = DevLayer(k3, w, hidden, H, D, K, B)
+    g = synth.rng(405)
+    state0 = (g.standard_normal((B, L.state_floats)) * 0.3).astype(np.float32)
+    state0[0, 0 * D * D + 77 * D + 5] = np.inf
+    state0[0, 1 * D * D + 3 * D + 9] = -np.inf
+    xs = [(g.standard_normal((B, hidden))).astype(np.float32) for _ in range(2)]
+    h0 = g.standard_normal((B, hidden)).astype(np.float32)
+    res = {}
+    try:
+        for kind in (1, 2, 3, 0):
+            k3cuda.check(k3.k3d_set_kda_head_kernel(kind))
+            h, st = h0.copy(), state0.copy()
+            for x in xs:
+                h, st = L.run(h, x, st)
+            res[kind] = (h, st)
+    finally:
+        k3cuda.check(k3.k3d_set_kda_head_kernel(0))
+    for kind in (0, 2, 3):
+        assert np.array_equal(res[kind][1].view(np.uint32), res[1][1].view(np.uint32)), kind
+        assert np.array_equal(res[kind][0].view(np.uint32), res[1][0].view(np.uint32)), kind
+    st = res[1][1][0]
+    assert np.isinf(st[77 * D + 5])                    # skipped row: the entry stays infinite

@@ -300,3 +300,31 @@ def test_stack_mode_a_one_rank_matches_mode_r(k3, B):
     finally:
         for m in models:
             k3.k3d_model_destroy(m)
+
+
+def test_step_past_the_cache_is_refused(k3):
+    """A step needs a free cache position: with the cache full the host step is refused with
+    K3D_EBOUND before anything launches (eager and graph-captured steps alike), no device
+    error is left behind, and refilling the context makes the model step again."""
+    c = CFG
+    model = k3.k3d_model_create(ctypes.byref(make_cfg(c, batch=1, cap=8, layout=1)), 99)
+    assert model, k3.k3d_last_message()
+    try:
+        k3cuda.check(k3.k3d_model_fill_context(model, 5, 3))
+        toks = np.array([11], np.int32)
+        for step in range(3):          # eager, capture, replay: positions 5, 6, 7
+            nxt = np.zeros(1, np.int32)
+            k3cuda.check(k3.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data), f"step {step}")
+            toks = nxt.copy()
+        assert int(download(k3, model, "pos", np.int32)[0]) == 8
+        nxt = np.zeros(1, np.int32)
+        assert k3.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data) == k3cuda.K3D_EBOUND
+        k3cuda.check(k3.k3d_sync())
+        code, site = ctypes.c_int(), ctypes.c_int()
+        k3cuda.check(k3.k3d_device_error(ctypes.byref(code), ctypes.byref(site)))
+        assert code.value == 0
+        assert int(download(k3, model, "pos", np.int32)[0]) == 8
+        k3cuda.check(k3.k3d_model_fill_context(model, 5, 3))
+        k3cuda.check(k3.k3d_model_step_host(model, toks.ctypes.data, nxt.ctypes.data))
+    finally:
+        k3.k3d_model_destroy(model)
