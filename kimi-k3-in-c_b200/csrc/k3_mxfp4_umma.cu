@@ -671,8 +671,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_mxfp4_umma(Job J)
             if (threadIdx.x == 0) {
                 int pre = 0;
                 if (prefetch) {
-                    // early launch: the first stages' weights before the programmatic wait
-                    pre = min(G::kNStages, nr);
+                    // early launch: the first stages' weights before the programmatic wait,
+                    // three of the six: when every CTA has six 34 KB stages in flight (30 MB)
+                    // as the wait returns, the B operand requested then lands only as they
+                    // drain, about 4.5 us later (a plain-load copy of B waits as long); with
+                    // three, B comes sooner and the stream starts earlier (down pass 23.0 ->
+                    // 21.6 us in the stack; two and four measured slower than three)
+                    pre = min(3, nr);
                     for (int h = 0; h < pre; h++) {
                         const ItemEnt &it = items[h];
                         if (!item_ok(it)) continue;
