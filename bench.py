@@ -68,20 +68,19 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the timed region runs. Rank 0
-    alone samples, every GPU of the job in one nvidia-smi process at 100 ms: each query
-    takes the driver's locks, and eight processes polling at a high rate slowed the
-    launches of the region they were measuring."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms by rank 0 on its own
+    GPU. Under several ranks any query during the timed steps stalls the push combines
+    (the caller then samples a second pass of the same steps instead)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu=None):
-        rank, world, _ = dist_env()
+        rank, world, local = dist_env()
         self.active = rank == 0
         vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-        local = list(range(world)) if world > 1 else [int(os.environ.get("LOCAL_RANK", 0)) if gpu is None else gpu]
-        self.gpus = [vis[i] if i < len(vis) else str(i) for i in local]
+        me = local if gpu is None else gpu
+        self.gpus = [vis[me] if me < len(vis) else str(me)]
         self.rows = []
         self.proc = None
 
@@ -777,7 +776,9 @@ def bench_stack(args, rank, world):
     n_prof = max(3, min(args.steps, 10))
     e2e_steps = max(args.steps, 200)
     # the timed and profiled steps, then (from a refilled context) the end-to-end ones
-    cap = ctx + max(args.warmup + args.steps + n_prof, 3 + e2e_steps) + 16
+    # the timed steps (twice under several ranks: see the clocks below) and the profiled
+    # steps, then (from a refilled context) the end-to-end ones
+    cap = ctx + max(args.warmup + 2 * args.steps + n_prof, 3 + e2e_steps) + 16
     # the tcgen05 kernel streams experts stored in the tiled layout; the other two
     # kernels read the checkpoint layout
     mode_a = stack_mode_a(args, world)
@@ -801,20 +802,37 @@ def bench_stack(args, rank, world):
         k3cuda.check(lib.k3d_copy(ids.ptr, nxt.ptr, B * 4))
     k3cuda.check(lib.k3d_sync())
     barrier()
-    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0)))
-    clocks.start()
-    lib.k3d_launch_count_reset()
-    # one event pair around the K steps on the library stream, no host synchronisation
-    # inside the region: the host enqueues graph replays back to back
-    lib.k3d_event_record(ev[0])
-    for i in range(args.steps):
-        k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "step")
-        k3cuda.check(lib.k3d_copy(ids.ptr, nxt.ptr, B * 4))   # greedy: next token in
-    lib.k3d_event_record(ev[1])
-    k3cuda.check(lib.k3d_sync())
-    clk = clocks.stop()
-    barrier()
-    tot_ms = reduce_max(lib.k3d_event_elapsed_ms(ev[0], ev[1]))
+    def timed_steps(sample):
+        """K steps between one event pair on the library stream, no host synchronisation
+        inside the region (the host enqueues graph replays back to back); the device time
+        as the max over ranks, and the clocks when sampled."""
+        clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", 0)))
+        if sample:
+            clocks.start()
+        lib.k3d_launch_count_reset()
+        lib.k3d_event_record(ev[0])
+        for i in range(args.steps):
+            k3cuda.check(lib.k3d_model_step_dev(model, ids.ptr, nxt.ptr, logits_p), "step")
+            k3cuda.check(lib.k3d_copy(ids.ptr, nxt.ptr, B * 4))   # greedy: next token in
+        lib.k3d_event_record(ev[1])
+        k3cuda.check(lib.k3d_sync())
+        clk = clocks.stop() if sample else None
+        barrier()
+        return reduce_max(lib.k3d_event_elapsed_ms(ev[0], ev[1])), clk
+
+    # One GPU: the clocks are sampled during the timed steps. Several: an nvidia-smi query
+    # during the steps stalls the ranks' push combines (two B200, 50 steps: 775 tok/s
+    # unsampled, 667 with an NVML clock and throttle-reason poll, 175-475 with nvidia-smi),
+    # so the K timed steps run unsampled and the same K steps run again right after,
+    # sampled by rank 0; the line reports that pass's rate beside its clocks.
+    if world == 1:
+        tot_ms, clk = timed_steps(True)
+    else:
+        tot_ms, _ = timed_steps(False)
+        s_ms, clk = timed_steps(True)
+        if clk is not None:
+            clk["window"] = "the same K steps run again right after the timed ones, sampled"
+            clk["window_tok_s"] = (B * world if mode_a else B) * args.steps / (s_ms * 1e-3)
     step_bytes = lib.k3d_model_last_step_bytes(model)
     hbm, peak_kind = measured_peaks()
     # per-kernel device times from an eager pass with the section timers on (graph
