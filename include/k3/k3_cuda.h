@@ -467,7 +467,9 @@ int       k3d_model_fill_context(K3dModel *m, int len, uint64_t seed);
 /* One decode step for the batch: ids (device [B]) in, next ids (device [B], argmax of
  * the logits) out, logits (device [B][vocab]) optional. Captures into a graph. Under EP
  * (k3d_ep_init with more than one rank) each rank holds a slice of the LM head and logits
- * receives that slice, [B][rows of the slice]; next is the argmax over all of them. */
+ * receives that slice, [B][rows of the slice]; next is the argmax over all of them.
+ * A step writes the next cache position: with the caches full (ctx_cap positions since
+ * the last fill or state load) it returns K3D_EBOUND and launches nothing. */
 int       k3d_model_step_dev(K3dModel *m, const int *ids, int *next_ids, float *logits);
 /* The same through host buffers: copies ids in, runs the step, copies next ids out. */
 int       k3d_model_step_host(K3dModel *m, const int *ids_host, int *next_host);
