@@ -40,6 +40,16 @@ int device_flag_status();
 void allow_dyn_smem(const void *func);
 template <typename F> inline void allow_smem_max(F *f) { allow_dyn_smem((const void *)f); }
 
+// The current device's bit in a one-time set-up mask: a kernel attribute such as its
+// dynamic shared memory limit is set per device, so launchers keep one bit per device
+// (`static unsigned long long init`; device ids below 64) instead of one flag per process.
+inline unsigned long long dev_bit()
+{
+    int d = 0;
+    cudaGetDevice(&d);
+    return 1ull << (d & 63);
+}
+
 // Programmatic dependent launch: kernels of the decode path are launched with
 // launch_pdl, so that a kernel's launch and prologue overlap the end of the kernel before
 // it in the stream. Such a kernel must execute pdl_wait() before its first access to

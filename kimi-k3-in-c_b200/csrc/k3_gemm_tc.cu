@@ -449,11 +449,11 @@ static int gemm_pass(int nmat, const uint16_t *const *W, float *const *Y, const 
     r.swiglu = swiglu;
     r.accumulate = accumulate;
     const size_t smem = 1024 + kHeader + (size_t)stages * stage_bytes;
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) != cudaSuccess)
             return fail(K3D_ECUDA, "gemm smem attribute");
-        init = true;
+        init |= dev_bit();
     }
     const long long units = (long long)nch * N * 8;
     launch_pdl(k_split_hilo, dim3((unsigned)((units + 255) / 256)), dim3(256), 0, st, ws, x, in, T, Tp, nch);

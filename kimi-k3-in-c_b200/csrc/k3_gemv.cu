@@ -363,11 +363,11 @@ int gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int 
         }
         return check_launch("gemv bf16 generic");
     }
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         allow_smem(k_gemv_bf16<2, 7, 1>);
         allow_smem(k_gemv_bf16<2, 7, 4>);
-        init = true;
+        init |= dev_bit();
     }
     for (int t0 = 0; t0 < T; t0 += 4) {
         const int nt = min(4, T - t0);
@@ -397,8 +397,8 @@ int gemv_bf16_swiglu(float *act, const float *x, const uint16_t *Wg, const uint1
     }
     if ((in % 8) != 0 || !al16(Wg) || !al16(Wu) || (size_t)in * 4 * 4 > 200 * 1024)
         return fail(K3D_EINVAL, "swiglu gemv needs in %% 8 == 0 and aligned rows (in=%d)", in);
-    static bool init = false;
-    if (!init) { allow_smem(k_gemv_bf16_swiglu<7>); init = true; }
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) { allow_smem(k_gemv_bf16_swiglu<7>); init |= dev_bit(); }
     for (int t0 = 0; t0 < T; t0 += 4) {
         const int nt = min(4, T - t0);
         const size_t smem = (size_t)nt * in * sizeof(float);
@@ -448,8 +448,8 @@ int gemv_bf16_multi(int nseg, const uint16_t *const *W, float *const *y, const i
     }
     if ((in % 8) != 0 || (size_t)in * 4 * T > 200 * 1024)
         return fail(K3D_EINVAL, "multi-segment GEMV: in=%d", in);
-    static bool init = false;
-    if (!init) { allow_smem(k_gemv_bf16_multi<2, 7>); init = true; }
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) { allow_smem(k_gemv_bf16_multi<2, 7>); init |= dev_bit(); }
     launch_pdl(k_gemv_bf16_multi<2, 7>, dim3(grid_for(S.start[nseg], 16)), dim3(256), (size_t)T * in * 4, s, S, x, in, T);
     note_launch();
     return check_launch("gemv bf16 multi");
@@ -478,8 +478,8 @@ int lm_head_keys(float *y, unsigned long long *key, const float *x, const uint16
         note_launch();
         return check_launch("lm head rows argmax");
     }
-    static bool init = false;
-    if (!init) { allow_smem(k_gemv_bf16_argmax<2, 7>); init = true; }
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) { allow_smem(k_gemv_bf16_argmax<2, 7>); init |= dev_bit(); }
     K3_TRY(cudaMemsetAsync(key, 0, (size_t)T * sizeof(unsigned long long), s) == cudaSuccess
                ? K3D_OK : fail(K3D_ECUDA, "argmax key reset"));
     if (g_gemv_stream && s == stream() && gemv_stream_argmax(y, key, x, W, in, out, T, s, ni))
@@ -531,8 +531,8 @@ int gemv_f32(float *y, const float *x, const float *W, int in, int out, cudaStre
         note_launch();
         return check_launch("gemv f32 generic");
     }
-    static bool init = false;
-    if (!init) { allow_smem(k_gemv_f32<2, 4>); init = true; }
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) { allow_smem(k_gemv_f32<2, 4>); init |= dev_bit(); }
     k_gemv_f32<2, 4><<<grid_for(out, 16), 256, (size_t)in * sizeof(float), s>>>(y, x, W, in, out);
     note_launch();
     return check_launch("gemv f32");

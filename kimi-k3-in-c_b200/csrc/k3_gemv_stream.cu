@@ -333,8 +333,8 @@ static int stream_launch(Args &A, cudaStream_t st)
     const int grid = std::max(1, std::min(sm_count(), U));
 #define K3_STREAM_LAUNCH(NT)                                                              \
     do {                                                                                  \
-        static bool init = false;                                                         \
-        if (!init) { allow_smem_max(k_gemv_stream<MODE, NT>); init = true; }              \
+        static unsigned long long init = 0;   /* one bit per device */                        \
+        if (!(init & dev_bit())) { allow_smem_max(k_gemv_stream<MODE, NT>); init |= dev_bit(); } \
         launch_pdl(k_gemv_stream<MODE, NT>, dim3(grid), dim3(kThreads), smem, st, A);     \
     } while (0)
     switch (A.T) {

@@ -116,11 +116,11 @@ static bool kda_fits(int dk, int dv)
 
 static void kda_attrs()
 {
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         allow_smem_max(k_kda_decode);
         allow_smem_max(k_kda_seq);
-        init = true;
+        init |= dev_bit();
     }
 }
 
@@ -753,14 +753,14 @@ int kda_chunked(float *S, float *o, const float *q, const float *k, const float 
                                 "dv %d (32..128, multiple of 32)", dk, dv);
     if (((uintptr_t)S | (uintptr_t)o | (uintptr_t)q | (uintptr_t)k | (uintptr_t)alpha) & 15u)
         return fail(K3D_EINVAL, "k3d_kda_prefill chunk=64: S, o, q, k and alpha must be 16-byte aligned");
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         allow_smem_max(k_kda_chunk_prep);
         allow_smem_max(k_kda_chunk_scan<128, 64>);
         allow_smem_max(k_kda_chunk_scan<0, 64>);
         allow_smem_max(k_kda_chunk_scan<128, 32>);
         allow_smem_max(k_kda_chunk_scan<0, 32>);
-        init = true;
+        init |= dev_bit();
     }
     const Rec R = rec(dk, dv);
     const int nch = (T + C - 1) / C;

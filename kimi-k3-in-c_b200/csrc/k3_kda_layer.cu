@@ -599,11 +599,11 @@ static int kda_layer_decode(float *h, const float *xn, const NormIn *ni, const K
     A.H = H; A.D = D; A.K = s->conv_k; A.lb = s->gate_lb; A.eps = s->eps;
     A.state_stride = k3d_kda_state_floats(s);
     const size_t smem = ((size_t)D * D + 3 * (size_t)D) * 4;
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         allow_smem_max(k_kda_head<4>);
         allow_smem_max(k_kda_head<0>);
-        init = true;
+        init |= dev_bit();
     }
     // default: the register-column kernel for up to four sequences (64 to 256 CTAs), the
     // shared-tile kernel above (the register kernel's 186 registers per thread cost it

@@ -877,13 +877,13 @@ int mla_decode(float *out, const float *x, const K3dMlaW *w, const K3dMlaShape *
     note_launch();
     K3_TRY(check_launch("mla absorb"));
     {
-        static bool init = false;
-        if (!init) {
+        static unsigned long long init = 0;   // one bit per device
+        if (!(init & dev_bit())) {
             allow_smem_max(k_mla_attn_tc<4>);
             allow_smem_max(k_mla_attn_tc<8>);
             allow_smem_max(k_mla_attn_tc<12>);
             allow_smem_max(k_mla_attn_tc<16>);
-            init = true;
+            init |= dev_bit();
         }
         const size_t smem = mla_attn_smem(d.kvw);
         const dim3 grid(d.nsplit, (d.H + kAHG - 1) / kAHG, B);

@@ -458,12 +458,12 @@ int mxfp4_mma_launch(int mode, const MoeWork &w, int umax, int in, int rows, con
     if (S < 2) return fail(K3D_EINVAL, "mxfp4 mma: stage of %d bytes does not fit", J.stage_bytes);
     J.stages = S;
     const size_t smem = (size_t)head + (size_t)S * J.stage_bytes;
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         allow_smem_max(k_mxfp4_mma<14>);
         allow_smem_max(k_mxfp4_mma<16>);
         allow_smem_max(k_mxfp4_mma<0>);
-        init = true;
+        init |= dev_bit();
     }
     int grid = sm_count();
     if (grid > J.n_items) grid = J.n_items;

@@ -1796,12 +1796,12 @@ static int make_job(Job &J, int mode, int tiled, const MoeWork &w, const int *id
 template <int NV, int RES>
 static int launch_job(const Job &J, long long items, cudaStream_t st)
 {
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         cudaError_t e = cudaFuncSetAttribute(k_mxfp4_umma<NV, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)Geo<NV, RES>::kSmem);
         if (e != cudaSuccess) return fail(K3D_ECUDA, "umma smem attribute: %s", cudaGetErrorString(e));
-        init = true;
+        init |= dev_bit();
     }
     if (items <= 0) return K3D_OK;
     const int grid = (int)(items < sm_count() ? items : sm_count());
@@ -1862,12 +1862,12 @@ int umma_launch_fused(const MoeWork &w, const int *idx, const int *count, int np
     F.npos = npos_max;
     F.nact = inter / kStageK;
     F.arrivals = 4 * (kStageK / 64) * F.A.ks;      // 4 epilogue warps x 8 tiles x K slices
-    static bool init = false;
-    if (!init) {
+    static unsigned long long init = 0;   // one bit per device
+    if (!(init & dev_bit())) {
         cudaError_t e = cudaFuncSetAttribute(k_mxfp4_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)Geo<1, 1>::kSmem);
         if (e != cudaSuccess) return fail(K3D_ECUDA, "umma fused smem attribute: %s", cudaGetErrorString(e));
-        init = true;
+        init |= dev_bit();
     }
     if (npos_max <= 0) return K3D_OK;
     launch_pdl(k_mxfp4_fused, dim3(sm_count()), dim3(kThreads), Geo<1, 1>::kSmem, st, F);

@@ -1122,8 +1122,8 @@ static int router_launch(int *idx, float *w, const float *x, const WT *W, const 
         J.zero = grp ? grp->zero : nullptr;
         J.nzero = grp ? grp->nzero : 0;
         const size_t smem = fused_smem_bytes<WT>(hidden, n_experts);
-        static bool init = false;
-        if (!init) { allow_smem_max(k_router_fused<WT>); init = true; }
+        static unsigned long long init = 0;   // one bit per device
+        if (!(init & dev_bit())) { allow_smem_max(k_router_fused<WT>); init |= dev_bit(); }
         dim3 grid((n_experts + 1) / 2, T);
         launch_pdl(k_router_fused<WT>, dim3(grid), dim3(128), smem, s, J);
         note_launch();
