@@ -393,8 +393,17 @@ int k3d_init(int device)
         return fail(K3D_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a",
                     device, p.major, p.minor);
     }
+    // the library's stream at the device's highest priority, the side stream (shared
+    // expert, x split) at the default, lowest one: where both have CTAs waiting, the block
+    // scheduler starts the router and routed experts first (graphs keep the priorities:
+    // k3d_graph_end instantiates with node priorities). Stack 534.2 -> 541.8 tok/s.
     cudaStream_t s;
-    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+    int prio_lo = 0, prio_hi = 0;
+    if (cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi) != cudaSuccess) {
+        cudaGetLastError();
+        prio_hi = 0;
+    }
+    if (cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, prio_hi) != cudaSuccess)
         return fail(K3D_ECUDA, "stream creation");
     g.device = device;
     g.stream = s;
@@ -625,7 +634,8 @@ void *k3d_graph_end(void)
         return nullptr;
     }
     cudaGraphExec_t ex = nullptr;
-    if (cudaGraphInstantiate(&ex, graph, 0) != cudaSuccess) {
+    // node priorities: each captured kernel keeps its stream's priority (see k3d_init)
+    if (cudaGraphInstantiate(&ex, graph, cudaGraphInstantiateFlagUseNodePriority) != cudaSuccess) {
         cudaGetLastError();
         cudaGraphDestroy(graph);
         fail(K3D_ECUDA, "graph instantiate");
