@@ -99,6 +99,11 @@ float  k3d_event_elapsed_ms(void *start, void *stop);
 void   k3d_event_destroy(void *ev);
 int    k3d_graph_begin(void);
 void  *k3d_graph_end(void);
+/* Whether graphs made by k3d_graph_end keep each captured kernel's stream priority
+ * (default 1: the library's stream runs above the side stream's shared expert, which
+ * helps batch-1 decode; the decode stack turns it off above four sequences, where it
+ * measured 2% slower). No counterpart in the reference. */
+int    k3d_set_graph_priorities(int on);
 int    k3d_graph_launch(void *graph_exec);
 void   k3d_graph_destroy(void *graph_exec);
 /* Section timers. When enabled, the library records CUDA events on its stream around its

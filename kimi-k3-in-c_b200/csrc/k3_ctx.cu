@@ -28,6 +28,7 @@ struct Ctx {
     int device = -1;
     cudaStream_t stream = nullptr;
     bool own_stream = false;
+    bool graph_prio = true;        // k3d_graph_end keeps the nodes' stream priorities
     int sms = 0;
     int status = 0;
     char msg[512] = {0};
@@ -614,6 +615,12 @@ float k3d_event_elapsed_ms(void *a, void *b)
 
 void k3d_event_destroy(void *ev) { if (ev) cudaEventDestroy((cudaEvent_t)ev); }
 
+int k3d_set_graph_priorities(int on)
+{
+    g.graph_prio = on != 0;
+    return K3D_OK;
+}
+
 int k3d_graph_begin(void)
 {
     K3_TRY(ensure_ctx());
@@ -634,8 +641,10 @@ void *k3d_graph_end(void)
         return nullptr;
     }
     cudaGraphExec_t ex = nullptr;
-    // node priorities: each captured kernel keeps its stream's priority (see k3d_init)
-    if (cudaGraphInstantiate(&ex, graph, cudaGraphInstantiateFlagUseNodePriority) != cudaSuccess) {
+    // node priorities: each captured kernel keeps its stream's priority (see k3d_init);
+    // without them every node runs at the priority of the stream the graph is launched on
+    const unsigned long long flags = g.graph_prio ? cudaGraphInstantiateFlagUseNodePriority : 0;
+    if (cudaGraphInstantiate(&ex, graph, flags) != cudaSuccess) {
         cudaGetLastError();
         cudaGraphDestroy(graph);
         fail(K3D_ECUDA, "graph instantiate");

@@ -179,6 +179,7 @@ _PROTOS = {
     "k3d_event_destroy": (None, [vp]),
     "k3d_graph_begin": (i32, []),
     "k3d_graph_end": (vp, []),
+    "k3d_set_graph_priorities": (i32, [i32]),
     "k3d_graph_launch": (i32, [vp]),
     "k3d_graph_destroy": (None, [vp]),
     "k3d_host_alloc": (vp, [sz]),
